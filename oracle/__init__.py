@@ -1,0 +1,227 @@
+"""CPU oracle for spindle's quantized matvec path — TEST INFRASTRUCTURE ONLY.
+
+Thin numpy/ctypes front end over oracle/_build/libsg_oracle.so, a C restatement
+of the reference Rust kernels (WiseHax/spindle 1.1.0: quant_q8k.rs, quant.rs,
+quant_multi.rs, q4k_gemv.rs, worker_pool.rs) with bit-identical fp32 results.
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs may use it,
+and only as the checker / the timed reference — never as the product path.
+
+Parity anchoring: the reference ships no golden vectors; the oracle is checked
+against all of its own tests' known-answer comparators (tests/test_oracle.py).
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import build as _build
+
+F32, F16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 2, 3, 6, 7, 8, 12, 13, 14, 30
+QK = 256
+
+_lib = None
+
+
+class Mat(C.Structure):
+    """`Mat` of quant.rs:914-935: dtype, byte offset, cols, rows."""
+    _fields_ = [("dtype", C.c_int32), ("_pad", C.c_uint32), ("offset", C.c_uint64),
+                ("cols", C.c_uint64), ("rows", C.c_uint64)]
+
+    def __init__(self, dtype, cols, rows, offset=0):
+        super().__init__(dtype, 0, offset, cols, rows)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = _build.build()
+        L = C.CDLL(path)
+        P, S, U64, I32 = C.c_void_p, C.c_size_t, C.c_uint64, C.c_int32
+        sig = {
+            "or_rng_next": (U64, [C.POINTER(U64)]),
+            "or_rng_f": (C.c_float, [C.POINTER(U64), C.c_float, C.c_float]),
+            "or_rng_fill_f32": (None, [C.POINTER(U64), C.c_float, C.c_float, P, S]),
+            "or_f16_trunc": (C.c_uint16, [C.c_float]),
+            "or_f16_trunc_flush": (C.c_uint16, [C.c_float]),
+            "or_random_matrix": (C.c_int, [I32, S, S, C.POINTER(U64), P]),
+            "or_random_row": (C.c_int, [I32, S, C.POINTER(U64), P]),
+            "or_row_bytes": (C.c_int64, [I32, U64]),
+            "or_f16_to_f32": (C.c_float, [C.c_uint16]),
+            "or_dequant_row": (C.c_int, [I32, P, S, P]),
+            "or_q8k_quantize": (None, [P, S, P, P, P]),
+            "or_matmul_rows": (C.c_int, [P, C.POINTER(Mat), S, P, P, P, P, S, S]),
+            "or_block_sums": (C.c_int, [P, C.POINTER(Mat), P, S, S, P]),
+            "or_matvec_rows": (C.c_int, [P, C.POINTER(Mat), P, P, S, S]),
+            "or_matmul_rows_multi": (C.c_int, [P, C.POINTER(Mat), S, P, P, S, S]),
+            "or_pool_create": (C.c_int, [C.c_int]),
+            "or_pool_destroy": (None, []),
+            "or_pool_threads": (C.c_int, []),
+            "or_pool_matvec_multi": (C.c_int, [P, C.POINTER(Mat), S, P, P]),
+            "or_cpu_has_avx2": (C.c_int, []),
+            "or_quantize_q4k": (None, [P, S, P]),
+            "or_quantize_q6k": (None, [P, S, P]),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(L, name)
+            f.restype, f.argtypes = res, args
+        if not L.or_cpu_has_avx2():
+            raise RuntimeError("oracle needs a CPU with AVX2, FMA and F16C")
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class Rng:
+    """The tests' xorshift64 generator (quant_q8k.rs:302-313)."""
+
+    def __init__(self, seed):
+        self.s = C.c_uint64(seed)
+
+    def next(self):
+        return lib().or_rng_next(C.byref(self.s))
+
+    def f(self, lo, hi):
+        return lib().or_rng_f(C.byref(self.s), lo, hi)
+
+    def fill(self, lo, hi, n):
+        out = np.empty(n, np.float32)
+        lib().or_rng_fill_f32(C.byref(self.s), lo, hi, _p(out), n)
+        return out
+
+
+def row_bytes(dtype, cols):
+    r = lib().or_row_bytes(dtype, cols)
+    if r < 0:
+        raise ValueError("unsupported dtype %d / width %d" % (dtype, cols))
+    return r
+
+
+def random_matrix(dtype, cols, rows, rng):
+    """quant_q8k.rs:323-336 (+ Q8_0 / F32 from quant_multi.rs:301-322)."""
+    out = np.empty(row_bytes(dtype, cols) * rows, np.uint8)
+    if lib().or_random_matrix(dtype, cols, rows, C.byref(rng.s), _p(out)):
+        raise ValueError("random_matrix: unsupported dtype %d" % dtype)
+    return out
+
+
+def random_row(dtype, cols, rng):
+    """quant.rs:1693-1723."""
+    out = np.empty(row_bytes(dtype, cols), np.uint8)
+    if lib().or_random_row(dtype, cols, C.byref(rng.s), _p(out)):
+        raise ValueError("random_row: unsupported dtype %d" % dtype)
+    return out
+
+
+def dequant_row(dtype, row, cols):
+    row = np.ascontiguousarray(row, np.uint8)
+    out = np.empty(cols, np.float32)
+    if lib().or_dequant_row(dtype, _p(row), cols, _p(out)):
+        raise ValueError("dequant_row: unsupported dtype %d" % dtype)
+    return out
+
+
+class Q8K:
+    """One quantized activation vector (quant_q8k.rs:61-65)."""
+
+    def __init__(self, d, qs, bsums):
+        self.d, self.qs, self.bsums = d, qs, bsums
+
+    def dequant(self):
+        return (self.d.repeat(QK) * self.qs.astype(np.float32)).astype(np.float32)
+
+
+def quantize(x):
+    x = np.ascontiguousarray(x, np.float32)
+    n = x.size
+    if n % QK:
+        raise ValueError("length must be a multiple of 256")
+    d = np.empty(n // QK, np.float32)
+    qs = np.empty(n, np.int8)
+    bs = np.empty(n // 16, np.int16)
+    lib().or_q8k_quantize(_p(x), n, _p(d), _p(qs), _p(bs))
+    return Q8K(d, qs, bs)
+
+
+def _ptrs(arrs):
+    return (C.c_void_p * len(arrs))(*[a.ctypes.data for a in arrs])
+
+
+def matmul_rows(w, mat, qs, outs, r0, r1):
+    """quant_q8k::matmul_rows: rows r0..r1 of outs[b] = W * qs[b]."""
+    w = np.ascontiguousarray(w, np.uint8)
+    rc = lib().or_matmul_rows(_p(w), C.byref(mat), len(qs), _ptrs([q.d for q in qs]),
+                              _ptrs([q.qs for q in qs]), _ptrs([q.bsums for q in qs]),
+                              _ptrs(outs), r0, r1)
+    if rc:
+        raise ValueError("matmul_rows: unsupported matrix")
+
+
+def gemv_int(w, mat, qs):
+    """All rows for a list of Q8K vectors -> float32 [n_vec, rows]."""
+    out = np.full((len(qs), mat.rows), np.nan, np.float32)
+    matmul_rows(w, mat, qs, [out[b] for b in range(len(qs))], 0, mat.rows)
+    return out
+
+
+def block_sums(w, mat, q, r0, r1):
+    """int32 [r1-r0, nb, 8] lane sums of quant_q8k.rs:235-242 for one vector."""
+    w = np.ascontiguousarray(w, np.uint8)
+    nb = mat.cols // QK
+    out = np.empty((r1 - r0, nb, 8), np.int32)
+    if lib().or_block_sums(_p(w), C.byref(mat), _p(q.qs), r0, r1, _p(out)):
+        raise ValueError("block_sums: unsupported matrix")
+    return out
+
+
+def matvec_rows(w, mat, x, r0, n_rows):
+    """quant::matvec_rows_avx2 (float kernels)."""
+    w = np.ascontiguousarray(w, np.uint8)
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(n_rows, np.float32)
+    if lib().or_matvec_rows(_p(w), C.byref(mat), _p(x), _p(out), r0, n_rows):
+        raise ValueError("matvec_rows: unsupported dtype %d" % mat.dtype)
+    return out
+
+
+def matmul_rows_multi(w, mat, xs, r0, r1):
+    """quant_multi::matmul_rows_avx2 -> float32 [n_vec, rows] (rows outside r0..r1 NaN)."""
+    w = np.ascontiguousarray(w, np.uint8)
+    xs = [np.ascontiguousarray(x, np.float32) for x in xs]
+    out = np.full((len(xs), mat.rows), np.nan, np.float32)
+    rc = lib().or_matmul_rows_multi(_p(w), C.byref(mat), len(xs), _ptrs(xs),
+                                    _ptrs([out[b] for b in range(len(xs))]), r0, r1)
+    if rc:
+        raise ValueError("matmul_rows_multi: unsupported dtype %d" % mat.dtype)
+    return out
+
+
+def pool_create(n_threads):
+    return lib().or_pool_create(n_threads)
+
+
+def pool_destroy():
+    lib().or_pool_destroy()
+
+
+def pool_matvec_multi(w, mat, xs, out):
+    """matvec / matvec_multi on the worker pool; xs [n_vec, cols] -> out [n_vec, rows]."""
+    rc = lib().or_pool_matvec_multi(_p(w), C.byref(mat), xs.shape[0], _p(xs), _p(out))
+    if rc:
+        raise RuntimeError("pool_matvec_multi failed (%d)" % rc)
+
+
+def quantize_weights(dtype, w):
+    """The build's f32 -> Q4_K / Q6_K quantizer (kquant.c); w is [rows, cols]."""
+    w = np.ascontiguousarray(w, np.float32)
+    rows, cols = w.shape
+    out = np.empty(row_bytes(dtype, cols) * rows, np.uint8)
+    if dtype == Q4_K:
+        lib().or_quantize_q4k(_p(w), w.size, _p(out))
+    elif dtype == Q6_K:
+        lib().or_quantize_q6k(_p(w), w.size, _p(out))
+    else:
+        raise ValueError("quantize_weights: dtype %d" % dtype)
+    return out

@@ -1,0 +1,105 @@
+/*
+ * sg_oracle.h — CPU restatement of spindle's quantized matvec path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the checker the CUDA path is
+ * compared against (tests/, __graft_entry__.smoke()) and the CPU baseline that
+ * bench.py times.  The product (spindle_b200/) never links or calls it.
+ *
+ * Every function restates one piece of the reference Rust crate (WiseHax/spindle
+ * 1.1.0, src/...) with the same arithmetic in the same order, so that its fp32
+ * results are bit-identical to the reference's AVX2 code:
+ *   - the x86 AVX2/FMA/F16C operations are the same instructions the reference's
+ *     `std::arch` intrinsics lower to;
+ *   - the file is compiled with -ffp-contract=off (rustc never fuses a*b+c; gcc
+ *     would), so every FMA here is an explicit one.
+ *
+ * Parity anchoring: the reference ships no golden vectors or fixture files.  The
+ * oracle is checked against every known-answer comparator its tests hold for
+ * this path (tests/test_oracle.py ports them: quant_q8k.rs:343-442,
+ * quant.rs:1728-1771, quant_multi.rs:372-417), using the same seeded generators.
+ */
+#ifndef SG_ORACLE_H
+#define SG_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* GGML type ids, gguf_loader.rs:25-65. */
+enum {
+    OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q4_1 = 3, OR_Q5_0 = 6, OR_Q5_1 = 7,
+    OR_Q8_0 = 8, OR_Q4_K = 12, OR_Q5_K = 13, OR_Q6_K = 14, OR_BF16 = 30
+};
+
+/* quant.rs:914-935 `Mat`. */
+typedef struct {
+    int32_t dtype;
+    uint32_t _pad;
+    uint64_t offset;
+    uint64_t cols;
+    uint64_t rows;
+} or_mat;
+
+/* ---- test-input generators (quant_q8k.rs:302-336, quant.rs:1666-1723) ---- */
+uint64_t or_rng_next(uint64_t *state);
+float or_rng_f(uint64_t *state, float lo, float hi);
+void or_rng_fill_f32(uint64_t *state, float lo, float hi, float *out, size_t n);
+uint16_t or_f16_trunc(float v);        /* quant_q8k.rs:315-321 */
+uint16_t or_f16_trunc_flush(float v);  /* quant.rs:1680-1690 */
+/* quant_q8k.rs:323-336 (Q4_K, Q6_K) and quant_multi.rs:301-322 (Q8_0, F32). */
+int or_random_matrix(int32_t dtype, size_t cols, size_t rows, uint64_t *rng, uint8_t *out);
+/* quant.rs:1693-1723 (every format of the float test). */
+int or_random_row(int32_t dtype, size_t cols, uint64_t *rng, uint8_t *out);
+
+/* ---- formats (quant.rs:877-899, :1527-1660, q4k_gemv.rs:75-85) ---- */
+int64_t or_row_bytes(int32_t dtype, uint64_t cols);
+float or_f16_to_f32(uint16_t h);
+void or_unpack_q4k_scales(const uint8_t sc12[12], uint8_t sc[8], uint8_t mn[8]);
+int or_dequant_row(int32_t dtype, const uint8_t *row, size_t cols, float *out);
+
+/* ---- the build's own f32 -> K-quant weight quantizer (kquant.c) ---- */
+void or_quantize_q4k(const float *x, size_t n, uint8_t *out);
+void or_quantize_q6k(const float *x, size_t n, uint8_t *out);
+
+/* ---- integer path (quant_q8k.rs) ---- */
+/* Q8K::quantize, quant_q8k.rs:73-121.  n % 256 == 0. */
+void or_q8k_quantize(const float *x, size_t n, float *d, int8_t *qs, int16_t *bsums);
+/* matmul_rows, quant_q8k.rs:255-295.  Vector b: xd[b] (n/256 floats),
+ * xs[b] (n int8), xb[b] (n/16 int16); row r of vector b -> outs[b][r]. */
+int or_matmul_rows(const uint8_t *base, const or_mat *m, size_t n_vec,
+                   const float *const *xd, const int8_t *const *xs,
+                   const int16_t *const *xb, float *const *outs,
+                   size_t r0, size_t r1);
+/* The int32 lane sums of rows<B,T> (quant_q8k.rs:235-242) for one vector:
+ * out[(r - r0) * nb * 8 + i * 8 + l] = lane l of `sumi` for block i of row r. */
+int or_block_sums(const uint8_t *base, const or_mat *m, const int8_t *xs,
+                  size_t r0, size_t r1, int32_t *out);
+
+/* ---- float path (quant.rs:939-1094, quant_multi.rs:232-273) ---- */
+/* matvec_rows_avx2: rows r0..r0+n_rows of W*x -> out[0..n_rows]. */
+int or_matvec_rows(const uint8_t *base, const or_mat *m, const float *x,
+                   float *out, size_t r0, size_t n_rows);
+/* quant_multi::matmul_rows_avx2: rows r0..r1 of W*xs[b] -> outs[b][r]. */
+int or_matmul_rows_multi(const uint8_t *base, const or_mat *m, size_t n_vec,
+                         const float *const *xs, float *const *outs,
+                         size_t r0, size_t r1);
+
+/* ---- worker pool (worker_pool.rs:38-139, smollm_chat.rs:309-349) ---- */
+/* matvec / matvec_multi on the integer kernels with the reference's row split
+ * [R*t/T, R*(t+1)/T) over n_threads persistent spinning workers.  xs is
+ * n_vec x cols (row-major), outs is n_vec x rows.  Quantizes inside. */
+int or_pool_create(int n_threads);
+void or_pool_destroy(void);
+int or_pool_threads(void);
+int or_pool_matvec_multi(const uint8_t *base, const or_mat *m, size_t n_vec,
+                         const float *xs, float *outs);
+
+int or_cpu_has_avx2(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
