@@ -1,0 +1,423 @@
+#!/usr/bin/env python
+"""Headline benchmark: K-quant GEMV HBM GB/s on B200 (BASELINE.json metric and
+Q4_K and Q6_K weights x Q8_K activations at 4096x4096,
+14336x4096, 4096x14336 and the 151936x1024 Q6_K LM head).
+
+One step = the hot path of `matvec` (smollm_chat.rs:309-318) over every matrix
+of the sweep: Q8_K-quantize that step's activation, then the integer GEMV
+(quant_q8k::matmul_rows).  N(0, 0.02) weights quantized by the library's own
+quantizer, N(0, 1) activations, all seeded; synthetic data.  The 7 matrices
+hold 314 MB, more than the 126 MB L2, so every matrix is evicted before it is
+read again.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--nvec B] [--impl reference]
+
+N > 1 (under torchrun): weak scaling.  Every rank owns a full-size row shard
+of its own (seeded by rank); rows are independent, so the data path has no
+collective.  value = all ranks' bytes / max-over-ranks time.
+--impl reference: the reference's CPU algorithm (the oracle's C restatement
+of the AVX2 kernels with its worker pool) on all host cores, same metric.
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+Q4_K, Q6_K = 12, 14
+SHAPES = [(Q4_K, 4096, 4096), (Q6_K, 4096, 4096), (Q4_K, 14336, 4096), (Q6_K, 14336, 4096),
+          (Q4_K, 4096, 14336), (Q6_K, 4096, 14336), (Q6_K, 151936, 1024)]
+BLK = {Q4_K: 144, Q6_K: 210}
+NAME = {Q4_K: "Q4_K", Q6_K: "Q6_K"}
+METRIC = "K-quant GEMV HBM GB/s (Q4_K/Q6_K x Q8_K sweep)"
+
+
+def alg_bytes(dt, rows, cols, n):
+    """Algorithmic bytes of one GEMV: weights + Q8_K activations + fp32 out."""
+    return rows * (cols // 256) * BLK[dt] + n * (cols + 4 * cols // 256 + 2 * cols // 16) + n * rows * 4
+
+
+def step_bytes(n):
+    return sum(alg_bytes(dt, r, c, n) for dt, r, c in SHAPES)
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x1: "gpu_idle", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, index, period=0.01):
+        self.index, self.period = index, period
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+            return self
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        names = sorted(n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle")
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples),
+                "source": "NVML, 10 ms period, during the timed region"}
+
+
+def rank_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def cpu_sample(shapes_host, nvec, budget_s, threads):
+    """Times the oracle's pooled matvec (the reference's CPU algorithm) on
+    full sweeps until budget_s is spent (at least one sweep after warm-up)."""
+    import numpy as np
+    import oracle as O
+    O.pool_create(threads)
+    try:
+        g = np.random.default_rng(7)
+        xs = [g.standard_normal((nvec, c), dtype=np.float32) for _, _, c in SHAPES]
+        outs = [np.empty((nvec, r), np.float32) for _, r, _ in SHAPES]
+        mats = [O.Mat(dt, c, r) for dt, r, c in SHAPES]
+
+        def sweep(frac=1.0):
+            for k, (dt, r, c) in enumerate(SHAPES):
+                m = mats[k] if frac >= 1.0 else O.Mat(dt, c, max(1, int(r * frac)))
+                O.pool_matvec_multi(shapes_host[k], m, xs[k], outs[k])
+
+        sweep()  # warm-up
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            sweep()
+            n += 1
+            if time.perf_counter() - t0 >= budget_s:
+                break
+        dt = (time.perf_counter() - t0) / n
+    finally:
+        O.pool_destroy()
+    return dt, n
+
+
+def host_weights(rank):
+    """The sweep's weights as host bytes, made the same way as on the GPU."""
+    import numpy as np
+    import oracle as O
+    g = np.random.default_rng(1000 + rank)
+    out = []
+    for dt, r, c in SHAPES:
+        w = (g.standard_normal((r, c), dtype=np.float32) * np.float32(0.02))
+        out.append(O.quantize_weights(dt, w))
+    return out
+
+
+def run_reference(args):
+    rank, world, _ = rank_env()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    wh = host_weights(0)
+    # Size each step so that warm-up + steps stay within about two minutes.
+    probe, _ = cpu_sample(wh, args.nvec, 0.0, threads)
+    total = args.steps + args.warmup
+    frac = min(1.0, 120.0 / max(total * probe, 1e-9))
+    import numpy as np
+    import oracle as O
+    O.pool_create(threads)
+    try:
+        g = np.random.default_rng(7)
+        xs = [g.standard_normal((args.nvec, c), dtype=np.float32) for _, _, c in SHAPES]
+        outs = [np.empty((args.nvec, r), np.float32) for _, r, _ in SHAPES]
+        mats = [O.Mat(dt, c, max(1, int(r * frac))) for dt, r, c in SHAPES]
+        bytes_step = sum(alg_bytes(dt, m.rows, c, args.nvec) for (dt, _, c), m in zip(SHAPES, mats))
+        for _ in range(args.warmup):
+            for k in range(len(SHAPES)):
+                O.pool_matvec_multi(wh[k], mats[k], xs[k], outs[k])
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            for k in range(len(SHAPES)):
+                O.pool_matvec_multi(wh[k], mats[k], xs[k], outs[k])
+        el = time.perf_counter() - t0
+    finally:
+        O.pool_destroy()
+    value = bytes_step * args.steps / el / 1e9
+    sample = "each step: rows [0, %.4g x rows) of every sweep matrix" % frac if frac < 1 else "each step: the full sweep"
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int32 + fp32",
+            "data": "synthetic", "config": config_block(args, 1),
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": sample + "; oracle = C restatement of quant_q8k.rs with the worker pool"},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_block(args, world):
+    return {"workload": "gemv_sweep_n%d" % args.nvec, "layout": getattr(args, "layout", "tiled"),
+            "shapes": ["%s %dx%d" % (NAME[dt], r, c) for dt, r, c in SHAPES],
+            "n_vec": args.nvec, "global_batch": args.nvec * world, "parallelism": "row-shard x%d (weak)" % world,
+            "l2": "314 MB of weights per step > 126 MB L2: each matrix is evicted before its next read",
+            "weights": "N(0,0.02) seeded, own Q4_K/Q6_K quantizer", "activations": "N(0,1) seeded"}
+
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    import spindle_b200 as sg
+    from spindle_b200 import _lib
+
+    rank, world, local = rank_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    lib = sg.lib()
+    nvec = args.nvec
+
+    # ---- resident inputs: weights, activations, Q8_K buffers, outputs ------
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    W, WG, X, XQ, OUT, M = [], [], [], [], [], []
+    for dt, r, c in SHAPES:
+        wf = torch.randn(r, c, device=dev, generator=gen) * 0.02
+        wq = sg.quantize_weights(dt, wf)
+        del wf
+        WG.append(wq)
+        if args.layout == "tiled":
+            t, m = sg.repack_tiled16(dt, wq, r, c)
+            W.append(t)
+            M.append(m)
+        else:
+            W.append(wq)
+            M.append(sg.Mat(dt, c, r))
+        X.append(torch.randn(nvec, c, device=dev, generator=gen))
+        XQ.append([sg.Q8K(c, dev) for _ in range(nvec)])
+        OUT.append(torch.empty(nvec, r, device=dev))
+    torch.cuda.synchronize()
+
+    def gemv(k):
+        sg.matmul_rows(W[k], M[k], XQ[k], [OUT[k][b] for b in range(nvec)], 0, M[k].rows)
+
+    def step():
+        for k in range(len(SHAPES)):
+            sg.quantize_into(X[k], XQ[k])
+            gemv(k)
+
+    # Warm-up outside capture (plans, function attributes), then capture.
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        step()
+        torch.cuda.synchronize()
+        g_step = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_step, stream=stream):
+            step()
+        g_gemv = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_gemv, stream=stream):
+            for k in range(len(SHAPES)):
+                gemv(k)
+    launches_per_step = 2 * len(SHAPES)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            g_step.replay()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(stream)
+            for _ in range(args.steps):
+                g_step.replay()
+            e1.record(stream)
+            e1.synchronize()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+        if args.profile:
+            if rank == 0:
+                print(json.dumps({"profile": True, "shapes": [list(s) for s in SHAPES], "ms_per_step": ms}))
+            return None, WG
+
+        # Roofline of the dominant kernel: the 7 GEMV launches alone, replayed.
+        reps = max(args.warmup, min(args.steps, 2000))
+        for _ in range(args.warmup):
+            g_gemv.replay()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(reps):
+            g_gemv.replay()
+        f1.record(stream)
+        f1.synchronize()
+        gemv_ms = f0.elapsed_time(f1) / reps  # 7 launches
+
+        # Per-shape GEMV time: one launch, timed right after the whole sweep
+        # has streamed 314 MB through L2, so the matrix is read from HBM.
+        per_shape = []
+        for k, (dt, r, c) in enumerate(SHAPES):
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g1 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g1, stream=stream):
+                gemv(k)
+            tot = 0.0
+            n_rep = 20
+            for _ in range(n_rep):
+                g_gemv.replay()           # evicts matrix k from L2 (314 MB streamed)
+                a0.record(stream)
+                g1.replay()
+                a1.record(stream)
+                a1.synchronize()
+                tot += a0.elapsed_time(a1)
+            us = tot / n_rep * 1e3
+            per_shape.append({"shape": "%s %dx%d" % (NAME[dt], r, c), "us": round(us, 2),
+                              "GB_s": round(alg_bytes(dt, r, c, nvec) / (us * 1e-6) / 1e9, 1)})
+
+        # ---- e2e through the C ABI with host buffers -----------------------
+        h_x = [torch.empty(nvec, c, dtype=torch.float32).pin_memory() for _, _, c in SHAPES]
+        h_o = [torch.empty(nvec, r, dtype=torch.float32).pin_memory() for _, r, _ in SHAPES]
+        for k in range(len(SHAPES)):
+            h_x[k].copy_(X[k].cpu())
+        sp = C.c_void_p(stream.cuda_stream)
+
+        def e2e_step():
+            for k in range(len(SHAPES)):
+                _lib.check(lib.sg_memcpy_h2d(C.c_void_p(X[k].data_ptr()), C.c_void_p(h_x[k].data_ptr()),
+                                             h_x[k].numel() * 4, sp), "h2d")
+                sg.quantize_into(X[k], XQ[k])
+                gemv(k)
+                _lib.check(lib.sg_memcpy_d2h(C.c_void_p(h_o[k].data_ptr()), C.c_void_p(OUT[k].data_ptr()),
+                                             h_o[k].numel() * 4, sp), "d2h")
+
+        e2e_step()
+        torch.cuda.synchronize()
+        g_e2e = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_e2e, stream=stream):
+            e2e_step()
+        for _ in range(args.warmup):
+            g_e2e.replay()
+        barrier()
+        reps_e2e = max(3, min(args.steps, 2000))
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(stream)
+        for _ in range(reps_e2e):
+            g_e2e.replay()
+        b1.record(stream)
+        b1.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(b0.elapsed_time(b1)) / reps_e2e
+    sg.device_status()
+
+    bytes_rank = step_bytes(nvec)
+    value = bytes_rank * world / (ms * 1e-3) / 1e9
+    gemv_bytes = bytes_rank
+    achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
+    peak, peak_src = None, "MEASURED_PEAKS.json hbm_gbs"
+    try:
+        peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"]
+    except Exception:
+        peak, peak_src = 6650.0, "fallback 6.65 TB/s"
+    h2d = sum(t.numel() * 4 for t in h_x)
+    d2h = sum(t.numel() * 4 for t in h_o)
+    line = None
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "int8 x int4/int6 -> int32, fp32 epilogue", "data": "synthetic",
+                "config": config_block(args, world),
+                "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
+                             "kernel": "gemv_q8k_kernel", "how": "algorithmic bytes of the 7 GEMV launches / "
+                             "their replayed duration (CUDA events on the launch stream)"},
+                "per_shape": per_shape,
+                "e2e": {"value": round(bytes_rank * world / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "how": "sg_memcpy_h2d of the fp32 activations from pinned host, quantize, GEMV, "
+                               "sg_memcpy_d2h of the fp32 outputs, every step"},
+                "gpu_launches": launches_per_step * args.steps,
+                "clocks": clk.summary()}
+    if world > 1:
+        dist.barrier()
+        del g_step, g_gemv, g_e2e
+        dist.destroy_process_group()
+    return line, WG
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--nvec", type=int, default=1)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layout", default="tiled", choices=["tiled", "gguf"],
+                    help="weight layout on the device: TILED16 (repacked at upload) or GGUF rows")
+    ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU-baseline work (rank 0, N=1)")
+    ap.add_argument("--shape", type=int, default=None, help="profiling: run only this sweep entry")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling: only the timed step loop (no e2e, per-shape or CPU legs)")
+    args = ap.parse_args()
+    if args.warmup < 3 and not args.profile:
+        args.warmup = 3
+    if args.shape is not None:
+        SHAPES[:] = [SHAPES[args.shape]]
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    line, W = run_gpu(args)
+    rank, world, _ = rank_env()
+    if args.profile:
+        return
+    if rank == 0 and line is not None:
+        if world == 1 and args.cpu_budget > 0:
+            wh = [w.cpu().numpy() for w in W]
+            threads = os.cpu_count() or 1
+            sweep_s, n = cpu_sample(wh, args.nvec, args.cpu_budget, threads)
+            cpu_v = step_bytes(args.nvec) / sweep_s / 1e9
+            line["cpu_baseline"] = {"value": round(cpu_v, 2), "unit": "GB/s", "cores": threads, "kind": "port",
+                                    "sample": "%d full sweeps (same 7 matrices, same bytes) through the oracle's "
+                                              "pooled matvec, %.1f s" % (n, sweep_s * n)}
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,157 @@
+/*
+ * spindle_gpu.h — C ABI of spindle-b200, the B200 (sm_100a) implementation of
+ * spindle's quantized matvec path.
+ *
+ * The reference (WiseHax/spindle 1.1.0, Rust) has no plugin system: its drop-in
+ * boundary is the crate-internal kernel API that the engine calls.  Each entry
+ * point below replaces one of those functions; the comment names it by
+ * file:line under the reference's src/.  A Rust binding is shown in
+ * INTEGRATION.md.
+ *
+ * Conventions
+ *   - Every function returns sg_status (0 = SG_OK) and never aborts the process.
+ *   - Pointers named d_* are device pointers (cudaMalloc'd, or from sg_alloc);
+ *     pointers named h_* are host pointers.  All memory is caller-owned unless
+ *     an sg_* function allocated it.
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream).  Calls are
+ *     asynchronous with respect to the host unless stated otherwise.
+ *   - Weight tensors keep the GGUF byte layout verbatim: row r starts at
+ *     d_base + m->offset + r * row_bytes(dtype, cols), and the tensor start
+ *     must be 16-byte aligned (GGUF aligns tensors to 32 bytes).
+ */
+#ifndef SPINDLE_GPU_H
+#define SPINDLE_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define SG_API __attribute__((visibility("default")))
+#else
+#define SG_API
+#endif
+
+typedef int32_t sg_status;
+#define SG_OK 0
+#define SG_ERR_INVALID 1   /* null pointer, bad count or range */
+#define SG_ERR_DTYPE 2     /* format not on this path (the reference panics, quant.rs:1092) */
+#define SG_ERR_SHAPE 3     /* cols not a multiple of the block, or above SG_MAX_COLS */
+#define SG_ERR_ALIGN 4     /* tensor start not 16-byte aligned */
+#define SG_ERR_CUDA 5      /* a CUDA runtime call failed; see sg_last_error_string() */
+#define SG_ERR_NCCL 6
+#define SG_ERR_TIMEOUT 7   /* a bounded device-side wait gave up */
+#define SG_ERR_NOMEM 8
+
+/* GGML type ids (gguf_loader.rs:25-65). */
+#define SG_F32 0
+#define SG_F16 1
+#define SG_Q8_0 8
+#define SG_Q4_K 12
+#define SG_Q6_K 14
+
+/* Weight layouts (sg_mat.layout).  GGUF: the file's rows, verbatim.
+ * TILED16: the same bytes permuted once at upload by sg_repack_tiled16 so that
+ * the GEMV streams aligned 16-row tiles (see sg_repack_tiled16). */
+#define SG_LAYOUT_GGUF 0
+#define SG_LAYOUT_TILED16 1
+
+/* Widest row the integer kernels take (256 super-blocks). */
+#define SG_MAX_COLS 65536
+
+/* A weight matrix inside a device buffer: quant.rs:914-935 `Mat`. */
+typedef struct sg_mat {
+    int32_t dtype;
+    uint32_t layout; /* SG_LAYOUT_GGUF (0) or SG_LAYOUT_TILED16 */
+    uint64_t offset; /* bytes from the base pointer to row 0 */
+    uint64_t cols;
+    uint64_t rows;
+} sg_mat;
+
+/* One Q8_K activation vector in device memory: quant_q8k.rs:61-65 `Q8K`.
+ * d: n/256 floats, qs: n int8, bsums: n/16 int16. */
+typedef struct sg_q8k {
+    float *d;
+    int8_t *qs;
+    int16_t *bsums;
+    uint64_t n;
+} sg_q8k;
+
+/* ---- status, formats, device memory ------------------------------------ */
+
+SG_API const char *sg_status_string(sg_status s);
+/* Text of the last CUDA error seen by this thread's calls. */
+SG_API const char *sg_last_error_string(void);
+/* quant.rs:1527-1542 `row_bytes`: SG_ERR_DTYPE / SG_ERR_SHAPE when undefined. */
+SG_API sg_status sg_row_bytes(int32_t dtype, uint64_t cols, uint64_t *out);
+/* quant_q8k.rs:55-57 `supports`: 1 when m runs on the integer kernels. */
+SG_API int32_t sg_supports(const sg_mat *m);
+/* quant_q8k.rs:22-24 `set_enabled` (the --float-kernels switch), process-wide. */
+SG_API void sg_set_int_kernels(int32_t on);
+SG_API int32_t sg_int_kernels_enabled(void);
+/* Bytes of one Q8_K vector of n values (d + qs + bsums), and carving of a
+ * 16-byte aligned buffer of that size into an sg_q8k. */
+SG_API uint64_t sg_q8k_bytes(uint64_t n);
+SG_API sg_status sg_q8k_view(void *d_buf, uint64_t n, sg_q8k *out);
+
+/* Device memory helpers for callers without a CUDA binding.  sg_upload pads
+ * the allocation to 256 bytes so that 16-byte bulk copies never leave it. */
+SG_API sg_status sg_alloc(uint64_t bytes, void **d_out);
+SG_API sg_status sg_free(void *d_ptr);
+SG_API sg_status sg_upload(const void *h_src, uint64_t bytes, void **d_out);
+SG_API sg_status sg_memcpy_h2d(void *d_dst, const void *h_src, uint64_t bytes, void *stream);
+SG_API sg_status sg_memcpy_d2h(void *h_dst, const void *d_src, uint64_t bytes, void *stream);
+SG_API sg_status sg_stream_sync(void *stream);
+/* Reads and clears the device-side status word that bounded waits set. */
+SG_API sg_status sg_device_status(void);
+
+/* ---- integer path: quant_q8k.rs ------------------------------------------ */
+
+/* Q8K::quantize (quant_q8k.rs:73-121) of n_vec vectors: vector b is read from
+ * d_x + b*ldx and written to outs[b] (outs is a host array).  n % 256 == 0.
+ * Bit-identical to the reference, including non-finite and all-zero blocks. */
+SG_API sg_status sg_q8k_quantize(const float *d_x, uint64_t n, uint64_t n_vec, uint64_t ldx,
+                          const sg_q8k *outs, void *stream);
+
+/* quant_q8k::matmul_rows (quant_q8k.rs:255-295): rows r0..r1 of
+ * outs[b] = W * xq[b] for b < n_vec; row r of vector b goes to outs[b][r]
+ * (outs[b] points at the START of a full output).  xq and outs are host arrays
+ * of device descriptors / pointers.  dtype Q4_K or Q6_K, cols % 256 == 0,
+ * cols <= SG_MAX_COLS, either layout.  Bit-identical fp32 results to the
+ * reference for any n_vec and any row split. */
+SG_API sg_status sg_matmul_rows(const uint8_t *d_base, const sg_mat *m, const sg_q8k *xq,
+                         float *const *outs, uint64_t n_vec, uint64_t r0, uint64_t r1,
+                         void *stream);
+
+/* TILED16 layout (no reference counterpart; the reference reads the mmap'd
+ * GGUF rows).  Rows are grouped in tiles of 16; tile t stores super-block
+ * column i of its 16 rows as aligned planes: Q4_K qs[16][128] then
+ * head[16][16] (d, dmin, scales); Q6_K qlqh[16][192], scales[16][16], d[16][2].
+ * The last tile is zero-padded.  Only bytes move: results are bit-identical
+ * to the GGUF layout.  sg_tiled16_bytes gives the buffer size;
+ * sg_repack_tiled16 / sg_unpack_tiled16 convert between the two layouts
+ * (device buffers, no overlap). */
+SG_API sg_status sg_tiled16_bytes(int32_t dtype, uint64_t rows, uint64_t cols, uint64_t *out);
+SG_API sg_status sg_repack_tiled16(int32_t dtype, const uint8_t *d_gguf, uint64_t rows, uint64_t cols,
+                                   uint8_t *d_tiled, void *stream);
+SG_API sg_status sg_unpack_tiled16(int32_t dtype, const uint8_t *d_tiled, uint64_t rows, uint64_t cols,
+                                   uint8_t *d_gguf, void *stream);
+
+/* The int32 lane sums of rows<B,T> (quant_q8k.rs:235-242) for one vector, as
+ * the kernel computes them: d_out[(r-r0)*nb*8 + i*8 + l] = lane l of block i
+ * of row r.  Exists to check per-super-block sums bit for bit.  GGUF layout only. */
+SG_API sg_status sg_block_sums(const uint8_t *d_base, const sg_mat *m, const sg_q8k *xq,
+                        int32_t *d_out, uint64_t r0, uint64_t r1, void *stream);
+
+/* ---- weight quantizer (no reference counterpart: its tests use random bytes)
+ * f32 [rows, cols] -> Q4_K or Q6_K rows, deterministic; cols % 256 == 0. */
+SG_API sg_status sg_quantize_weights(int32_t dtype, const float *d_w, uint64_t rows, uint64_t cols,
+                              uint8_t *d_out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,179 @@
+"""spindle-b200: spindle's quantized matvec path on B200 (sm_100a).
+
+Host-side mirror of the reference's kernel API (WiseHax/spindle 1.1.0, src/):
+  Mat                      quant.rs:914-935
+  row_bytes                quant.rs:1527-1542
+  supports / set_enabled   quant_q8k.rs:22-57
+  Q8K, Q8K.quantize        quant_q8k.rs:61-81
+  matmul_rows              quant_q8k.rs:255-295
+Every call goes through the C ABI of include/spindle_gpu.h (libspindle_b200.so);
+torch tensors are only the device-memory plumbing.  There is no CPU path: a
+missing library or a failed call raises.
+"""
+import ctypes as C
+
+import torch
+
+from . import _lib
+from ._lib import SgError, SgMat, SgQ8K
+
+F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
+GGUF, TILED16 = 0, 1  # weight layouts (sg_mat.layout)
+QK = 256
+DTYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
+
+
+def lib():
+    return _lib.load()
+
+
+def _stream(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+class Mat:
+    """A weight matrix inside a device byte buffer (quant.rs:914-935 `Mat`)."""
+
+    def __init__(self, dtype, cols, rows, offset=0, layout=GGUF):
+        self.dtype, self.cols, self.rows, self.offset, self.layout = dtype, cols, rows, offset, layout
+
+    def c(self):
+        return SgMat(self.dtype, self.layout, self.offset, self.cols, self.rows)
+
+    def expert(self, e):
+        """View of expert e of a 3D tensor (quant.rs:929-934)."""
+        return Mat(self.dtype, self.cols, self.rows, self.offset + e * self.rows * row_bytes(self.dtype, self.cols))
+
+
+def row_bytes(dtype, cols):
+    out = C.c_uint64()
+    _lib.check(lib().sg_row_bytes(dtype, cols, C.byref(out)), "row_bytes")
+    return out.value
+
+
+def supports(m):
+    return bool(lib().sg_supports(C.byref(m.c())))
+
+
+def set_enabled(on):
+    """The --float-kernels switch (quant_q8k.rs:22-24)."""
+    lib().sg_set_int_kernels(1 if on else 0)
+
+
+def enabled():
+    return bool(lib().sg_int_kernels_enabled())
+
+
+class Q8K:
+    """One Q8_K activation vector in device memory (quant_q8k.rs:61-65),
+    carved from one 16-byte aligned buffer."""
+
+    def __init__(self, n, device=None):
+        if n % QK:
+            raise ValueError("Q8K length must be a multiple of 256")
+        self.n = n
+        nbytes = lib().sg_q8k_bytes(n)
+        self.buf = torch.empty(nbytes, dtype=torch.uint8, device=device or "cuda")
+        self.desc = SgQ8K()
+        _lib.check(lib().sg_q8k_view(C.c_void_p(self.buf.data_ptr()), n, C.byref(self.desc)), "q8k_view")
+        nb = n // QK
+        self.d = self.buf[:nb * 4].view(torch.float32)
+        off_qs = self.desc.qs - self.desc.d
+        off_bs = self.desc.bsums - self.desc.d
+        self.qs = self.buf[off_qs:off_qs + n].view(torch.int8)
+        self.bsums = self.buf[off_bs:off_bs + nb * 32].view(torch.int16)
+
+    def quantize(self, x, stream=None):
+        """Q8K::quantize (quant_q8k.rs:73-81) of a float32 CUDA vector."""
+        quantize_into(x.reshape(1, -1), [self], stream)
+        return self
+
+
+def quantize_into(xs, outs, stream=None):
+    """Quantizes the rows of xs [n_vec, n] (float32, CUDA) into outs (Q8K list)."""
+    if xs.dtype != torch.float32 or not xs.is_cuda:
+        raise TypeError("expected a float32 CUDA tensor")
+    if xs.stride(-1) != 1:
+        raise ValueError("rows must be contiguous")
+    n_vec, n = xs.shape
+    descs = (SgQ8K * n_vec)(*[q.desc for q in outs])
+    _lib.check(lib().sg_q8k_quantize(C.c_void_p(xs.data_ptr()), n, n_vec, xs.stride(0), descs, _stream(stream)),
+               "q8k_quantize")
+
+
+def quantize(xs, stream=None):
+    """Float32 CUDA [n] or [n_vec, n] -> Q8K (or list of Q8K)."""
+    single = xs.dim() == 1
+    xs2 = xs.reshape(1, -1) if single else xs
+    outs = [Q8K(xs2.shape[1], xs2.device) for _ in range(xs2.shape[0])]
+    quantize_into(xs2, outs, stream)
+    return outs[0] if single else outs
+
+
+def matmul_rows(base, m, xq, outs, r0, r1, stream=None):
+    """quant_q8k::matmul_rows (quant_q8k.rs:255-295): rows r0..r1 of
+    outs[b] = W * xq[b].  base: uint8 CUDA tensor holding the GGUF bytes;
+    outs[b]: float32 CUDA tensors of m.rows entries (row r -> outs[b][r])."""
+    n = len(xq)
+    if len(outs) != n:
+        raise ValueError("one output per vector")
+    for o in outs:
+        if o.dtype != torch.float32 or o.numel() < m.rows:
+            raise ValueError("each output must be float32 with m.rows entries")
+    descs = (SgQ8K * n)(*[q.desc for q in xq])
+    ptrs = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
+    _lib.check(lib().sg_matmul_rows(C.c_void_p(base.data_ptr()), C.byref(m.c()), descs, ptrs, n, r0, r1,
+                                    _stream(stream)), "matmul_rows")
+
+
+def gemv(base, m, xq, stream=None):
+    """All rows for a list of Q8K vectors -> float32 CUDA [n_vec, rows]."""
+    out = torch.empty((len(xq), m.rows), dtype=torch.float32, device=base.device)
+    matmul_rows(base, m, xq, [out[b] for b in range(len(xq))], 0, m.rows, stream)
+    return out
+
+
+def block_sums(base, m, q, r0, r1, stream=None):
+    """int32 [r1-r0, nb, 8] lane sums of quant_q8k.rs:235-242, as the kernel computes them."""
+    out = torch.empty((r1 - r0, m.cols // QK, 8), dtype=torch.int32, device=base.device)
+    _lib.check(lib().sg_block_sums(C.c_void_p(base.data_ptr()), C.byref(m.c()), C.byref(q.desc),
+                                   C.c_void_p(out.data_ptr()), r0, r1, _stream(stream)), "block_sums")
+    return out
+
+
+def quantize_weights(dtype, w, stream=None):
+    """f32 [rows, cols] CUDA -> uint8 CUDA bytes of Q4_K / Q6_K rows (own quantizer)."""
+    w = w.contiguous()
+    rows, cols = w.shape
+    out = torch.empty(rows * row_bytes(dtype, cols), dtype=torch.uint8, device=w.device)
+    _lib.check(lib().sg_quantize_weights(dtype, C.c_void_p(w.data_ptr()), rows, cols, C.c_void_p(out.data_ptr()),
+                                         _stream(stream)), "quantize_weights")
+    return out
+
+
+def tiled16_bytes(dtype, rows, cols):
+    out = C.c_uint64()
+    _lib.check(lib().sg_tiled16_bytes(dtype, rows, cols, C.byref(out)), "tiled16_bytes")
+    return out.value
+
+
+def repack_tiled16(dtype, w, rows, cols, stream=None):
+    """GGUF-row bytes (uint8 CUDA) -> TILED16 bytes; returns (buffer, Mat)."""
+    out = torch.empty(tiled16_bytes(dtype, rows, cols), dtype=torch.uint8, device=w.device)
+    _lib.check(lib().sg_repack_tiled16(dtype, C.c_void_p(w.data_ptr()), rows, cols, C.c_void_p(out.data_ptr()),
+                                       _stream(stream)), "repack_tiled16")
+    return out, Mat(dtype, cols, rows, layout=TILED16)
+
+
+def unpack_tiled16(dtype, t, rows, cols, stream=None):
+    """TILED16 bytes -> GGUF-row bytes (uint8 CUDA)."""
+    out = torch.empty(rows * row_bytes(dtype, cols), dtype=torch.uint8, device=t.device)
+    _lib.check(lib().sg_unpack_tiled16(dtype, C.c_void_p(t.data_ptr()), rows, cols, C.c_void_p(out.data_ptr()),
+                                       _stream(stream)), "unpack_tiled16")
+    return out
+
+
+def device_status():
+    """Raises SgError if a bounded device wait gave up since the last check."""
+    _lib.check(lib().sg_device_status(), "device status")

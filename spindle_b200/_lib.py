@@ -1,0 +1,93 @@
+"""ctypes binding of libspindle_b200.so (the C ABI of include/spindle_gpu.h).
+
+There is no CPU fallback: if the library is missing and cannot be built, or a
+call fails, an exception is raised.
+"""
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libspindle_b200.so")
+
+OK = 0
+STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported dtype", 3: "unsupported shape",
+          4: "misaligned device pointer", 5: "CUDA error", 6: "NCCL error", 7: "device wait timed out",
+          8: "out of memory"}
+
+
+class SgError(RuntimeError):
+    def __init__(self, status, what, detail=""):
+        self.status = status
+        msg = "%s: %s" % (what, STATUS.get(status, "status %d" % status))
+        super().__init__(msg + (" (%s)" % detail if detail else ""))
+
+
+class SgMat(C.Structure):
+    _fields_ = [("dtype", C.c_int32), ("layout", C.c_uint32), ("offset", C.c_uint64),
+                ("cols", C.c_uint64), ("rows", C.c_uint64)]
+
+
+class SgQ8K(C.Structure):
+    _fields_ = [("d", C.c_void_p), ("qs", C.c_void_p), ("bsums", C.c_void_p), ("n", C.c_uint64)]
+
+
+P, U64, I32 = C.c_void_p, C.c_uint64, C.c_int32
+
+# name -> (restype, argtypes); every function the header declares.
+SIGNATURES = {
+    "sg_status_string": (C.c_char_p, [I32]),
+    "sg_last_error_string": (C.c_char_p, []),
+    "sg_row_bytes": (I32, [I32, U64, C.POINTER(U64)]),
+    "sg_supports": (I32, [C.POINTER(SgMat)]),
+    "sg_set_int_kernels": (None, [I32]),
+    "sg_int_kernels_enabled": (I32, []),
+    "sg_q8k_bytes": (U64, [U64]),
+    "sg_q8k_view": (I32, [P, U64, C.POINTER(SgQ8K)]),
+    "sg_alloc": (I32, [U64, C.POINTER(P)]),
+    "sg_free": (I32, [P]),
+    "sg_upload": (I32, [P, U64, C.POINTER(P)]),
+    "sg_memcpy_h2d": (I32, [P, P, U64, P]),
+    "sg_memcpy_d2h": (I32, [P, P, U64, P]),
+    "sg_stream_sync": (I32, [P]),
+    "sg_device_status": (I32, []),
+    "sg_q8k_quantize": (I32, [P, U64, U64, U64, C.POINTER(SgQ8K), P]),
+    "sg_matmul_rows": (I32, [P, C.POINTER(SgMat), C.POINTER(SgQ8K), C.POINTER(P), U64, U64, U64, P]),
+    "sg_block_sums": (I32, [P, C.POINTER(SgMat), C.POINTER(SgQ8K), P, U64, U64, P]),
+    "sg_quantize_weights": (I32, [I32, P, U64, U64, P, P]),
+    "sg_tiled16_bytes": (I32, [I32, U64, U64, C.POINTER(U64)]),
+    "sg_repack_tiled16": (I32, [I32, P, U64, U64, P, P]),
+    "sg_unpack_tiled16": (I32, [I32, P, U64, U64, P, P]),
+}
+
+_lib = None
+
+
+def load(build_if_missing=True):
+    """Loads the library, building it first when it is missing or stale and
+    nvcc is available (the GPU box ships the prebuilt .so)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    try:
+        from . import build as _build
+        if os.path.exists(_build.NVCC) and build_if_missing:
+            _build.build()
+    except Exception:
+        if not os.path.exists(LIB_PATH):
+            raise
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError("libspindle_b200.so is missing; run spindle_b200/build.py")
+    lib = C.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        f = getattr(lib, name)
+        f.restype, f.argtypes = res, args
+    _lib = lib
+    return lib
+
+
+def check(status, what):
+    if status != OK:
+        detail = ""
+        if status == 5 and _lib is not None:
+            detail = _lib.sg_last_error_string().decode(errors="replace")
+        raise SgError(status, what, detail)

@@ -1,0 +1,570 @@
+// api.cu — the C ABI of include/spindle_gpu.h: argument checks, launch plans
+// and kernel dispatch.  Host code only; kernels live in the other .cu files.
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "gemv_q8k.cuh"
+#include "gemv_tiled.cuh"
+#include "kernels.cuh"
+
+using namespace sg;
+
+namespace {
+
+thread_local char g_err[256] = "";
+
+sg_status cuda_fail(cudaError_t e, const char *what) {
+    snprintf(g_err, sizeof g_err, "%s: %s", what, cudaGetErrorString(e));
+    return SG_ERR_CUDA;
+}
+
+#define CK(call)                                       \
+    do {                                               \
+        cudaError_t e_ = (call);                       \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+    } while (0)
+
+std::atomic<int> g_int_enabled{0};  // 0 = undecided, 1 = on, 2 = off
+
+struct DevInfo {
+    int sms = 0;
+    bool attrs_set = false;
+};
+DevInfo g_dev[64];
+std::mutex g_mu;
+
+sg_status dev_info(DevInfo **out) {
+    int d;
+    CK(cudaGetDevice(&d));
+    if (d < 0 || d >= 64) return SG_ERR_INVALID;
+    DevInfo &di = g_dev[d];
+    if (!di.sms) {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!di.sms) CK(cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, d));
+    }
+    *out = &di;
+    return SG_OK;
+}
+
+inline uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+inline bool aligned(const void *p, uintptr_t a) { return ((uintptr_t)p & (a - 1)) == 0; }
+
+// ---- GEMV kernel table -----------------------------------------------------
+
+typedef void (*gemv_fn)(const GemvArgs);
+
+template <int DT, bool DBG>
+gemv_fn pick(int nv, int cpt) {
+    switch (cpt) {
+    case 1:
+        switch (nv) {
+        case 1: return gemv_q8k_kernel<DT, 1, 1, DBG>;
+        case 2: return gemv_q8k_kernel<DT, 2, 1, DBG>;
+        case 3: return gemv_q8k_kernel<DT, 3, 1, DBG>;
+        case 4: return gemv_q8k_kernel<DT, 4, 1, DBG>;
+        case 5: return gemv_q8k_kernel<DT, 5, 1, DBG>;
+        case 6: return gemv_q8k_kernel<DT, 6, 1, DBG>;
+        case 7: return gemv_q8k_kernel<DT, 7, 1, DBG>;
+        default: return gemv_q8k_kernel<DT, 8, 1, DBG>;
+        }
+    case 2:
+        switch (nv) {
+        case 1: return gemv_q8k_kernel<DT, 1, 2, DBG>;
+        case 2: return gemv_q8k_kernel<DT, 2, 2, DBG>;
+        case 3: return gemv_q8k_kernel<DT, 3, 2, DBG>;
+        default: return gemv_q8k_kernel<DT, 4, 2, DBG>;
+        }
+    case 4: return nv == 1 ? gemv_q8k_kernel<DT, 1, 4, DBG> : gemv_q8k_kernel<DT, 2, 4, DBG>;
+    default: return gemv_q8k_kernel<DT, 1, 8, DBG>;
+    }
+}
+
+gemv_fn pick_gemv(int dt, bool dbg, int nv, int cpt) {
+    if (dt == DT_Q4K) return dbg ? pick<DT_Q4K, true>(nv, cpt) : pick<DT_Q4K, false>(nv, cpt);
+    return dbg ? pick<DT_Q6K, true>(nv, cpt) : pick<DT_Q6K, false>(nv, cpt);
+}
+
+struct Plan {
+    int cpt, nv;
+    uint32_t R, ntiles, stage_bytes, nstages, sum_stride, grid;
+    size_t smem;
+    gemv_fn fn;
+};
+
+constexpr size_t SMEM_PER_CTA = 110 * 1024;  // two CTAs per SM
+constexpr uint32_t STAGE_TARGET = 24 * 1024;
+constexpr uint32_t SCRATCH_MAX = 48 * 1024;
+
+sg_status make_plan_uncached(DevInfo *di, int dt, uint32_t nb, uint32_t nrows, uint32_t nvec, bool dbg, Plan *p) {
+    sg_status st;
+    const uint32_t ncol = nb * 8, bb = dt == DT_Q4K ? 144 : 210, rb = nb * bb;
+    int cpt = 1;
+    while (ncol > (uint32_t)GEMV_THREADS * cpt) cpt *= 2;
+    if (cpt > 8) return SG_ERR_SHAPE;
+    const uint32_t nv = nvec < (uint32_t)(8 / cpt) ? nvec : (uint32_t)(8 / cpt);
+    const uint32_t P = cpt == 1 ? GEMV_THREADS / ncol : 1;
+    const uint32_t stride = 8 * (nb | 1u);
+    uint32_t R = STAGE_TARGET / rb;
+    R = R < P ? P : R / P * P;
+    while (R > P && gemv_scratch_bytes(R, nv, nb, stride) > SCRATCH_MAX) R -= P;
+    // Small matrices: split finer so that every SM gets work.
+    const uint32_t want_tiles = (uint32_t)di->sms * 2;
+    if ((nrows + R - 1) / R < want_tiles) {
+        uint32_t r = (nrows + want_tiles - 1) / want_tiles;
+        r = (r + P - 1) / P * P;
+        if (r < R) R = r;
+    }
+    if (R == 0) R = 1;
+    uint32_t stage = (uint32_t)align_up((uint64_t)R * rb + 48, 128);
+    uint32_t nst = 4;
+    size_t smem = 128 + (size_t)nst * stage + gemv_scratch_bytes(R, nv, nb, stride);
+    while (smem > SMEM_PER_CTA && nst > 2) {
+        nst--;
+        smem = 128 + (size_t)nst * stage + gemv_scratch_bytes(R, nv, nb, stride);
+    }
+    if (smem > 220 * 1024) return SG_ERR_SHAPE;
+    p->cpt = cpt;
+    p->nv = (int)nv;
+    p->R = R;
+    p->ntiles = (nrows + R - 1) / R;
+    p->stage_bytes = stage;
+    p->nstages = nst;
+    p->sum_stride = stride;
+    p->smem = smem;
+    p->fn = pick_gemv(dt, dbg, (int)nv, cpt);
+    CK(cudaFuncSetAttribute((const void *)p->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    int occ = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, (const void *)p->fn, GEMV_THREADS, smem));
+    if (occ < 1) occ = 1;
+    const uint32_t cap = (uint32_t)(di->sms * occ);
+    p->grid = p->ntiles < cap ? p->ntiles : cap;
+    (void)st;
+    return SG_OK;
+}
+
+// Plans are cached per device and shape: a launch then costs one hash lookup.
+struct PlanKey {
+    int dev, dt;
+    uint32_t nb, nrows, nvec;
+    bool dbg;
+    bool operator==(const PlanKey &o) const {
+        return dev == o.dev && dt == o.dt && nb == o.nb && nrows == o.nrows && nvec == o.nvec && dbg == o.dbg;
+    }
+};
+struct PlanHash {
+    size_t operator()(const PlanKey &k) const {
+        uint64_t h = (uint64_t)k.dev * 0x9E3779B97F4A7C15ull ^ (uint64_t)k.dt << 1 ^ (uint64_t)k.dbg;
+        h = h * 1099511628211ull ^ k.nb;
+        h = h * 1099511628211ull ^ k.nrows;
+        h = h * 1099511628211ull ^ k.nvec;
+        return (size_t)h;
+    }
+};
+std::unordered_map<PlanKey, Plan, PlanHash> g_plans;
+
+sg_status make_plan(int dt, uint32_t nb, uint32_t nrows, uint32_t nvec, bool dbg, Plan *p) {
+    int dev;
+    CK(cudaGetDevice(&dev));
+    const PlanKey key{dev, dt, nb, nrows, nvec, dbg};
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_plans.find(key);
+        if (it != g_plans.end()) {
+            *p = it->second;
+            return SG_OK;
+        }
+    }
+    DevInfo *di;
+    sg_status st = dev_info(&di);
+    if (st) return st;
+    if ((st = make_plan_uncached(di, dt, nb, nrows, nvec, dbg, p))) return st;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_plans.size() > 4096) g_plans.clear();
+    g_plans.emplace(key, *p);
+    return SG_OK;
+}
+
+sg_status check_mat(const uint8_t *d_base, const sg_mat *m, uint64_t r0, uint64_t r1, int *dt) {
+    if (!d_base || !m) return SG_ERR_INVALID;
+    if (m->dtype != SG_Q4_K && m->dtype != SG_Q6_K) return SG_ERR_DTYPE;
+    if (m->cols == 0 || m->cols % 256 || m->cols > SG_MAX_COLS) return SG_ERR_SHAPE;
+    if (r0 > r1 || r1 > m->rows || m->rows > 0xFFFFFFFFull) return SG_ERR_INVALID;
+    if (m->layout != SG_LAYOUT_GGUF && m->layout != SG_LAYOUT_TILED16) return SG_ERR_INVALID;
+    if (!aligned(d_base + m->offset, 16)) return SG_ERR_ALIGN;
+    *dt = m->dtype == SG_Q4_K ? DT_Q4K : DT_Q6K;
+    return SG_OK;
+}
+
+sg_status check_q8k(const sg_q8k &q, uint64_t n) {
+    if (!q.d || !q.qs || !q.bsums || q.n != n) return SG_ERR_INVALID;
+    if (!aligned(q.d, 4) || !aligned(q.qs, 16) || !aligned(q.bsums, 4)) return SG_ERR_ALIGN;
+    return SG_OK;
+}
+
+// ---- TILED16 GEMV ------------------------------------------------------------
+
+typedef void (*tgemv_fn)(const TGemvArgs);
+
+tgemv_fn pick_tiled(int dt, int nv) {
+    if (dt == DT_Q4K)
+        return nv == 1 ? gemv_tiled_kernel<0, 1> : nv == 2 ? gemv_tiled_kernel<0, 2>
+               : nv <= 4 ? gemv_tiled_kernel<0, 4> : gemv_tiled_kernel<0, 8>;
+    return nv == 1 ? gemv_tiled_kernel<1, 1> : nv == 2 ? gemv_tiled_kernel<1, 2>
+           : nv <= 4 ? gemv_tiled_kernel<1, 4> : gemv_tiled_kernel<1, 8>;
+}
+
+int env_int(const char *name, int dflt) {
+    const char *e = getenv(name);
+    return e && *e ? atoi(e) : dflt;
+}
+
+struct TPlan {
+    tgemv_fn fn;
+    uint32_t bc, nstages, stage_bytes, grid;
+    size_t smem;
+};
+
+std::unordered_map<uint64_t, TPlan> g_tplans;
+
+sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, TPlan *p) {
+    int dev;
+    CK(cudaGetDevice(&dev));
+    const uint64_t key = ((uint64_t)dev << 56) ^ ((uint64_t)dt << 52) ^ ((uint64_t)nv << 44) ^
+                         ((uint64_t)nb << 32) ^ ntiles;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_tplans.find(key);
+        if (it != g_tplans.end()) {
+            *p = it->second;
+            return SG_OK;
+        }
+    }
+    DevInfo *di;
+    sg_status st = dev_info(&di);
+    if (st) return st;
+    const uint32_t cb = tiled_col_bytes(dt == DT_Q4K ? 0 : 1);
+    p->bc = (uint32_t)env_int("SG_TILED_BC", 1);
+    if (p->bc < 1) p->bc = 1;
+    if (p->bc > nb) p->bc = nb;
+    p->nstages = (uint32_t)env_int("SG_TILED_STAGES", 6);
+    if (p->nstages < 2) p->nstages = 2;
+    if (p->nstages > 8) p->nstages = 8;
+    p->stage_bytes = p->bc * cb;
+    p->smem = 256 + (size_t)TGEMV_WARPS * p->nstages * p->stage_bytes;
+    while (p->smem > 200 * 1024 && p->nstages > 2) {
+        p->nstages--;
+        p->smem = 256 + (size_t)TGEMV_WARPS * p->nstages * p->stage_bytes;
+    }
+    p->fn = pick_tiled(dt, nv);
+    CK(cudaFuncSetAttribute((const void *)p->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    int occ = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, (const void *)p->fn, TGEMV_WARPS * 32, p->smem));
+    if (occ < 1) occ = 1;
+    const uint32_t need = (ntiles + TGEMV_WARPS - 1) / TGEMV_WARPS, cap = (uint32_t)(di->sms * occ);
+    p->grid = need < cap ? need : cap;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_tplans.size() > 4096) g_tplans.clear();
+    g_tplans.emplace(key, *p);
+    return SG_OK;
+}
+
+sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, float *const *outs, uint64_t n_vec,
+                       uint64_t r0, uint64_t r1, cudaStream_t stream) {
+    const uint32_t t0 = (uint32_t)(r0 / TILE_ROWS), t1 = (uint32_t)((r1 + TILE_ROWS - 1) / TILE_ROWS);
+    for (uint64_t g = 0; g < n_vec; g += TGEMV_MAXV) {
+        const int nv = (int)(n_vec - g < TGEMV_MAXV ? n_vec - g : TGEMV_MAXV);
+        TPlan p;
+        sg_status st = tiled_plan(dt, nb, t1 - t0, nv, &p);
+        if (st) return st;
+        TGemvArgs a;
+        memset(&a, 0, sizeof a);
+        a.w = w;
+        a.nb = nb;
+        a.t0 = t0;
+        a.ntiles = t1 - t0;
+        a.r0 = (uint32_t)r0;
+        a.r1 = (uint32_t)r1;
+        a.bc = p.bc;
+        a.nstages = p.nstages;
+        a.stage_bytes = p.stage_bytes;
+        a.nvec = (uint32_t)nv;
+        for (int v = 0; v < nv; v++) {
+            a.xd[v] = xq[g + v].d;
+            a.xs[v] = xq[g + v].qs;
+            a.xb[v] = xq[g + v].bsums;
+            a.out[v] = outs[g + v];
+        }
+        p.fn<<<p.grid, TGEMV_WARPS * 32, p.smem, stream>>>(a);
+        CK(cudaGetLastError());
+    }
+    return SG_OK;
+}
+
+sg_status launch_gemv(const uint8_t *d_base, const sg_mat *m, const sg_q8k *xq, float *const *outs,
+                      uint64_t n_vec, uint64_t r0, uint64_t r1, int32_t *dbg, cudaStream_t stream) {
+    int dt;
+    sg_status st = check_mat(d_base, m, r0, r1, &dt);
+    if (st) return st;
+    if (r1 == r0 || n_vec == 0) return SG_OK;
+    if (!xq || !outs) return SG_ERR_INVALID;
+    for (uint64_t b = 0; b < n_vec; b++) {
+        if ((st = check_q8k(xq[b], m->cols))) return st;
+        if (!outs[b] || !aligned(outs[b], 4)) return SG_ERR_INVALID;
+    }
+    const uint32_t nb = (uint32_t)(m->cols / 256), bb = dt == DT_Q4K ? 144 : 210;
+    const uint64_t rb = (uint64_t)nb * bb;
+    if (m->layout == SG_LAYOUT_TILED16) {
+        if (dbg) return SG_ERR_INVALID;
+        return launch_tiled(d_base + m->offset, dt, nb, xq, outs, n_vec, r0, r1, stream);
+    }
+    for (uint64_t g = 0; g < n_vec; g += GEMV_MAXV) {
+        const uint32_t nv = (uint32_t)(n_vec - g < GEMV_MAXV ? n_vec - g : GEMV_MAXV);
+        Plan p;
+        if ((st = make_plan(dt, nb, (uint32_t)(r1 - r0), nv, dbg != nullptr, &p))) return st;
+        GemvArgs a;
+        memset(&a, 0, sizeof a);
+        a.w = d_base + m->offset;
+        a.tma_limit = (m->rows * rb) & ~15ull;
+        a.nb = nb;
+        a.rb = (uint32_t)rb;
+        a.r0 = (uint32_t)r0;
+        a.nrows = (uint32_t)(r1 - r0);
+        a.R = p.R;
+        a.ntiles = p.ntiles;
+        a.stage_bytes = p.stage_bytes;
+        a.nstages = p.nstages;
+        a.sum_stride = p.sum_stride;
+        a.nvec = nv;
+        for (uint32_t v = 0; v < nv; v++) {
+            a.xd[v] = xq[g + v].d;
+            a.xs[v] = xq[g + v].qs;
+            a.xb[v] = xq[g + v].bsums;
+            a.out[v] = outs[g + v];
+        }
+        a.dbg_sums = dbg;
+        p.fn<<<p.grid, GEMV_THREADS, p.smem, stream>>>(a);
+        CK(cudaGetLastError());
+    }
+    return SG_OK;
+}
+
+}  // namespace
+
+// ---- C ABI -----------------------------------------------------------------
+
+extern "C" {
+
+const char *sg_status_string(sg_status s) {
+    switch (s) {
+    case SG_OK: return "ok";
+    case SG_ERR_INVALID: return "invalid argument";
+    case SG_ERR_DTYPE: return "unsupported dtype";
+    case SG_ERR_SHAPE: return "unsupported shape";
+    case SG_ERR_ALIGN: return "misaligned device pointer";
+    case SG_ERR_CUDA: return "CUDA error";
+    case SG_ERR_NCCL: return "NCCL error";
+    case SG_ERR_TIMEOUT: return "device wait timed out";
+    case SG_ERR_NOMEM: return "out of memory";
+    default: return "unknown status";
+    }
+}
+
+const char *sg_last_error_string(void) { return g_err; }
+
+sg_status sg_row_bytes(int32_t dtype, uint64_t cols, uint64_t *out) {
+    if (!out) return SG_ERR_INVALID;
+    uint64_t blk, bytes;
+    switch (dtype) {
+    case SG_F32: blk = 1; bytes = 4; break;
+    case SG_F16: blk = 1; bytes = 2; break;
+    case SG_Q8_0: blk = 32; bytes = 34; break;
+    case SG_Q4_K: blk = 256; bytes = 144; break;
+    case SG_Q6_K: blk = 256; bytes = 210; break;
+    default: return SG_ERR_DTYPE;
+    }
+    if (cols % blk) return SG_ERR_SHAPE;
+    *out = cols / blk * bytes;
+    return SG_OK;
+}
+
+int32_t sg_int_kernels_enabled(void) {
+    int v = g_int_enabled.load(std::memory_order_relaxed);
+    if (v == 0) {
+        const char *e = getenv("SPINDLE_FLOAT_KERNELS");  // quant_q8k.rs:46
+        v = (!e || !*e || strcmp(e, "0") == 0) ? 1 : 2;
+        g_int_enabled.store(v, std::memory_order_relaxed);
+    }
+    return v == 1;
+}
+
+void sg_set_int_kernels(int32_t on) { g_int_enabled.store(on ? 1 : 2, std::memory_order_relaxed); }
+
+int32_t sg_supports(const sg_mat *m) {
+    return m && sg_int_kernels_enabled() && (m->dtype == SG_Q4_K || m->dtype == SG_Q6_K) && m->cols > 0 &&
+           m->cols % 256 == 0;
+}
+
+uint64_t sg_q8k_bytes(uint64_t n) {
+    const uint64_t nb = n / 256;
+    return align_up(nb * 4, 16) + align_up(n, 16) + align_up(nb * 32, 16);
+}
+
+sg_status sg_q8k_view(void *d_buf, uint64_t n, sg_q8k *out) {
+    if (!d_buf || !out || n % 256) return SG_ERR_INVALID;
+    if (!aligned(d_buf, 16)) return SG_ERR_ALIGN;
+    const uint64_t nb = n / 256;
+    uint8_t *p = (uint8_t *)d_buf;
+    out->d = (float *)p;
+    out->qs = (int8_t *)(p + align_up(nb * 4, 16));
+    out->bsums = (int16_t *)(p + align_up(nb * 4, 16) + align_up(n, 16));
+    out->n = n;
+    return SG_OK;
+}
+
+sg_status sg_alloc(uint64_t bytes, void **d_out) {
+    if (!d_out) return SG_ERR_INVALID;
+    cudaError_t e = cudaMalloc(d_out, align_up(bytes ? bytes : 1, 256));
+    if (e == cudaErrorMemoryAllocation) return SG_ERR_NOMEM;
+    CK(e);
+    return SG_OK;
+}
+
+sg_status sg_free(void *d_ptr) {
+    CK(cudaFree(d_ptr));
+    return SG_OK;
+}
+
+sg_status sg_upload(const void *h_src, uint64_t bytes, void **d_out) {
+    if (!h_src || !d_out) return SG_ERR_INVALID;
+    sg_status st = sg_alloc(bytes, d_out);
+    if (st) return st;
+    CK(cudaMemcpy(*d_out, h_src, bytes, cudaMemcpyHostToDevice));
+    return SG_OK;
+}
+
+sg_status sg_memcpy_h2d(void *d_dst, const void *h_src, uint64_t bytes, void *stream) {
+    CK(cudaMemcpyAsync(d_dst, h_src, bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream));
+    return SG_OK;
+}
+
+sg_status sg_memcpy_d2h(void *h_dst, const void *d_src, uint64_t bytes, void *stream) {
+    CK(cudaMemcpyAsync(h_dst, d_src, bytes, cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+    return SG_OK;
+}
+
+sg_status sg_stream_sync(void *stream) {
+    CK(cudaStreamSynchronize((cudaStream_t)stream));
+    return SG_OK;
+}
+
+sg_status sg_device_status(void) {
+    unsigned v = 0, zero = 0;
+    CK(cudaMemcpyFromSymbol(&v, g_dev_status, sizeof v));
+    if (v) CK(cudaMemcpyToSymbol(g_dev_status, &zero, sizeof zero));
+    return v == DEV_OK ? SG_OK : SG_ERR_TIMEOUT;
+}
+
+sg_status sg_matmul_rows(const uint8_t *d_base, const sg_mat *m, const sg_q8k *xq, float *const *outs,
+                         uint64_t n_vec, uint64_t r0, uint64_t r1, void *stream) {
+    return launch_gemv(d_base, m, xq, outs, n_vec, r0, r1, nullptr, (cudaStream_t)stream);
+}
+
+sg_status sg_block_sums(const uint8_t *d_base, const sg_mat *m, const sg_q8k *xq, int32_t *d_out, uint64_t r0,
+                        uint64_t r1, void *stream) {
+    if (!d_out || !xq) return SG_ERR_INVALID;
+    if (!aligned(d_out, 4)) return SG_ERR_ALIGN;
+    // The kernel also writes the fp32 outputs; park them in the export buffer's
+    // slack is not possible, so use a scratch row buffer the caller cannot see.
+    float *tmp = nullptr;
+    CK(cudaMallocAsync((void **)&tmp, (r1 > r0 ? r1 : 1) * sizeof(float), (cudaStream_t)stream));
+    float *outs[1] = {tmp - r0};
+    sg_status st = launch_gemv(d_base, m, xq, outs, 1, r0, r1, d_out, (cudaStream_t)stream);
+    cudaError_t e = cudaFreeAsync(tmp, (cudaStream_t)stream);
+    if (st) return st;
+    CK(e);
+    return SG_OK;
+}
+
+sg_status sg_q8k_quantize(const float *d_x, uint64_t n, uint64_t n_vec, uint64_t ldx, const sg_q8k *outs,
+                          void *stream) {
+    if (n_vec == 0) return SG_OK;
+    if (!d_x || !outs || n == 0 || n % 256 || (n_vec > 1 && ldx < n)) return SG_ERR_INVALID;
+    if (!aligned(d_x, 16) || (n_vec > 1 && ldx % 4)) return SG_ERR_ALIGN;
+    for (uint64_t b = 0; b < n_vec; b++) {
+        sg_status st = check_q8k(outs[b], n);
+        if (st) return st;
+        if (!aligned(outs[b].qs, 8)) return SG_ERR_ALIGN;
+    }
+    const uint64_t nb = n / 256;
+    for (uint64_t g = 0; g < n_vec; g += Q8K_MAXV) {
+        Q8kArgs a;
+        memset(&a, 0, sizeof a);
+        const uint32_t nv = (uint32_t)(n_vec - g < Q8K_MAXV ? n_vec - g : Q8K_MAXV);
+        a.x = d_x + g * ldx;
+        a.ldx = ldx;
+        a.nb = (uint32_t)nb;
+        a.nvec = nv;
+        for (uint32_t v = 0; v < nv; v++) a.outs[v] = outs[g + v];
+        const uint64_t warps = nb * nv;
+        q8k_quantize_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, (cudaStream_t)stream>>>(a);
+        CK(cudaGetLastError());
+    }
+    return SG_OK;
+}
+
+sg_status sg_quantize_weights(int32_t dtype, const float *d_w, uint64_t rows, uint64_t cols, uint8_t *d_out,
+                              void *stream) {
+    if (!d_w || !d_out) return SG_ERR_INVALID;
+    if (dtype != SG_Q4_K && dtype != SG_Q6_K) return SG_ERR_DTYPE;
+    if (cols == 0 || cols % 256) return SG_ERR_SHAPE;
+    const uint64_t nblocks = rows * (cols / 256);
+    if (!nblocks) return SG_OK;
+    const unsigned grid = (unsigned)((nblocks + 127) / 128);
+    if (dtype == SG_Q4_K)
+        quantize_q4k_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(d_w, nblocks, d_out);
+    else
+        quantize_q6k_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(d_w, nblocks, d_out);
+    CK(cudaGetLastError());
+    return SG_OK;
+}
+
+sg_status sg_tiled16_bytes(int32_t dtype, uint64_t rows, uint64_t cols, uint64_t *out) {
+    if (!out) return SG_ERR_INVALID;
+    if (dtype != SG_Q4_K && dtype != SG_Q6_K) return SG_ERR_DTYPE;
+    if (cols == 0 || cols % 256) return SG_ERR_SHAPE;
+    const uint64_t tiles = (rows + TILE_ROWS - 1) / TILE_ROWS;
+    *out = tiles * (cols / 256) * tiled_col_bytes(dtype == SG_Q4_K ? 0 : 1);
+    return SG_OK;
+}
+
+static sg_status repack(int32_t dtype, const uint8_t *src, uint64_t rows, uint64_t cols, uint8_t *dst, int inverse,
+                        void *stream) {
+    uint64_t bytes;
+    sg_status st = sg_tiled16_bytes(dtype, rows, cols, &bytes);
+    if (st) return st;
+    if (!src || !dst) return SG_ERR_INVALID;
+    if (!inverse) CK(cudaMemsetAsync(dst, 0, bytes, (cudaStream_t)stream));  // zero padding rows
+    const uint64_t n = rows * (cols / 256);
+    if (n) {
+        repack_tiled16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+            dtype == SG_Q4_K ? 0 : 1, src, rows, (uint32_t)(cols / 256), dst, inverse);
+        CK(cudaGetLastError());
+    }
+    return SG_OK;
+}
+
+sg_status sg_repack_tiled16(int32_t dtype, const uint8_t *d_gguf, uint64_t rows, uint64_t cols, uint8_t *d_tiled,
+                            void *stream) {
+    return repack(dtype, d_gguf, rows, cols, d_tiled, 0, stream);
+}
+
+sg_status sg_unpack_tiled16(int32_t dtype, const uint8_t *d_tiled, uint64_t rows, uint64_t cols, uint8_t *d_gguf,
+                            void *stream) {
+    return repack(dtype, d_tiled, rows, cols, d_gguf, 1, stream);
+}
+
+}  // extern "C"
