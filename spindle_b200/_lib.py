@@ -7,7 +7,7 @@ import ctypes as C
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libspindle_b200.so")
+LIB_PATH = os.environ.get("SG_LIB_PATH") or os.path.join(HERE, "libspindle_b200.so")
 
 OK = 0
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported dtype", 3: "unsupported shape",
@@ -70,7 +70,7 @@ def load(build_if_missing=True):
         return _lib
     try:
         from . import build as _build
-        if os.path.exists(_build.NVCC) and build_if_missing:
+        if os.path.exists(_build.NVCC) and build_if_missing and not os.environ.get("SG_LIB_PATH"):
             _build.build()
     except Exception:
         if not os.path.exists(LIB_PATH):

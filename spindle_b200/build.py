@@ -20,12 +20,12 @@ FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC,-fv
          "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]
 
 
-def sources():
-    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+def sources(csrc=CSRC):
+    return sorted(glob.glob(os.path.join(csrc, "*.cu")))
 
 
-def headers():
-    return sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h")))
+def headers(csrc=CSRC):
+    return sorted(glob.glob(os.path.join(csrc, "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 
 def _newer(target, deps):
@@ -35,12 +35,13 @@ def _newer(target, deps):
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force=False, verbose=False, jobs=8):
-    os.makedirs(OBJ, exist_ok=True)
-    hdrs = headers() + [os.path.abspath(__file__)]
+def build(force=False, verbose=False, jobs=8, csrc=CSRC, lib=LIB, obj_dir=OBJ):
+    """Compiles csrc/*.cu into lib (defaults: this package's sources and .so)."""
+    os.makedirs(obj_dir, exist_ok=True)
+    hdrs = headers(csrc) + [os.path.abspath(__file__)]
     objs, procs = [], []
-    for src in sources():
-        obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
+    for src in sources(csrc):
+        obj = os.path.join(obj_dir, os.path.basename(src)[:-3] + ".o")
         objs.append(obj)
         if force or _newer(obj, [src] + hdrs):
             cmd = [NVCC, *ARCH, *FLAGS, "-c", src, "-o", obj]
@@ -55,12 +56,21 @@ def build(force=False, verbose=False, jobs=8):
     for s, p in procs:
         if p.wait():
             raise RuntimeError("nvcc failed on " + s)
-    if force or _newer(LIB, objs):
-        tmp = LIB + ".tmp.%d" % os.getpid()
+    if force or _newer(lib, objs):
+        tmp = lib + ".tmp.%d" % os.getpid()
         subprocess.run([NVCC, *ARCH, "-shared", "-rdc=true", "-cudart", "static", "-o", tmp, *objs], check=True)
-        os.replace(tmp, LIB)
-    return LIB
+        os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-v", action="store_true")
+    ap.add_argument("--src", default=CSRC, help="directory of .cu sources")
+    ap.add_argument("--out", default=LIB, help="shared library to write")
+    args = ap.parse_args()
+    od = OBJ if args.src == CSRC else os.path.join(os.path.dirname(os.path.abspath(args.out)), "obj")
+    print(build(force=args.force, verbose=args.v, csrc=os.path.abspath(args.src), lib=os.path.abspath(args.out),
+                obj_dir=od))

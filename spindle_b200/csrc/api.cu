@@ -205,9 +205,30 @@ sg_status check_q8k(const sg_q8k &q, uint64_t n) {
     return SG_OK;
 }
 
+// Launch with programmatic stream serialization: the kernel may start while
+// the previous kernel in the stream finishes; it waits for it (griddepcontrol)
+// before reading anything that kernel wrote.
+template <typename Args>
+cudaError_t launch_pdl(const void *fn, uint32_t grid, uint32_t block, size_t smem, cudaStream_t stream, Args *args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *params[] = {args};
+    return cudaLaunchKernelExC(&cfg, fn, params);
+}
+
 // ---- TILED16 GEMV ------------------------------------------------------------
 
 typedef void (*tgemv_fn)(const TGemvArgs);
+
+uint32_t tiled_nv_inst(int nv) { return nv <= 1 ? 1u : nv == 2 ? 2u : nv <= 4 ? 4u : 8u; }
 
 tgemv_fn pick_tiled(int dt, int nv) {
     if (dt == DT_Q4K)
@@ -224,12 +245,15 @@ int env_int(const char *name, int dflt) {
 
 struct TPlan {
     tgemv_fn fn;
-    uint32_t bc, nstages, stage_bytes, grid;
+    uint32_t S, bc, nstages, stage_bytes, slot_blocks, grid;
     size_t smem;
 };
 
 std::unordered_map<uint64_t, TPlan> g_tplans;
 
+// Launch shape of the tiled GEMV: S warps per tile so that the whole GPU has
+// work (small row counts split each tile's super-blocks over more warps),
+// a 3-stage ring per warp, CTAs of TGEMV_WARPS warps.
 sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, TPlan *p) {
     int dev;
     CK(cudaGetDevice(&dev));
@@ -247,24 +271,47 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, TPlan *p) {
     sg_status st = dev_info(&di);
     if (st) return st;
     const uint32_t cb = tiled_col_bytes(dt == DT_Q4K ? 0 : 1);
-    p->bc = (uint32_t)env_int("SG_TILED_BC", 1);
-    if (p->bc < 1) p->bc = 1;
-    if (p->bc > nb) p->bc = nb;
-    p->nstages = (uint32_t)env_int("SG_TILED_STAGES", 6);
-    if (p->nstages < 2) p->nstages = 2;
-    if (p->nstages > 8) p->nstages = 8;
-    p->stage_bytes = p->bc * cb;
-    p->smem = 256 + (size_t)TGEMV_WARPS * p->nstages * p->stage_bytes;
-    while (p->smem > 200 * 1024 && p->nstages > 2) {
-        p->nstages--;
-        p->smem = 256 + (size_t)TGEMV_WARPS * p->nstages * p->stage_bytes;
+    // the kernel is instantiated for 1, 2, 4 or 8 vectors; its chain scratch is
+    // laid out for that count, so size shared memory for it too
+    const uint32_t nv_inst = tiled_nv_inst(nv);
+    const uint32_t warp_slots = (uint32_t)di->sms * TGEMV_WARPS;
+    uint32_t S = 1;
+    const int forced = env_int("SG_TILED_S", 0);
+    if (forced == 1 || forced == 2 || forced == 4 || forced == 8)
+        S = (uint32_t)forced;
+    else
+        while (S < 8 && S * 2 <= nb && (uint64_t)ntiles * S < warp_slots) S *= 2;
+    uint32_t ns = (uint32_t)env_int("SG_TILED_STAGES", 2), bc = (uint32_t)env_int("SG_TILED_BC", 2);
+    if (ns < 2) ns = 2;
+    if (ns > 8) ns = 8;
+    if (bc < 1) bc = 1;
+    // Fit the CTA in shared memory: fewer stages, then smaller stages, then
+    // fewer warps per tile (less chain scratch).
+    const size_t budget = 220 * 1024;
+    for (;;) {
+        p->S = S;
+        p->slot_blocks = (nb + S - 1) / S;
+        p->bc = bc < p->slot_blocks ? bc : p->slot_blocks;
+        p->nstages = ns;
+        p->stage_bytes = p->bc * cb;
+        p->smem = tiled_smem_bytes(S, ns, p->stage_bytes, p->slot_blocks, nv_inst, nb);
+        if (p->smem <= budget) break;
+        if (ns > 2)
+            ns--;
+        else if (bc > 1)
+            bc--;
+        else if (S > 1)
+            S /= 2;
+        else
+            return SG_ERR_SHAPE;
     }
     p->fn = pick_tiled(dt, nv);
     CK(cudaFuncSetAttribute((const void *)p->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
     int occ = 0;
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, (const void *)p->fn, TGEMV_WARPS * 32, p->smem));
     if (occ < 1) occ = 1;
-    const uint32_t need = (ntiles + TGEMV_WARPS - 1) / TGEMV_WARPS, cap = (uint32_t)(di->sms * occ);
+    const uint32_t groups = TGEMV_WARPS / p->S;
+    const uint32_t need = (ntiles + groups - 1) / groups, cap = (uint32_t)(di->sms * occ);
     p->grid = need < cap ? need : cap;
     std::lock_guard<std::mutex> lk(g_mu);
     if (g_tplans.size() > 4096) g_tplans.clear();
@@ -275,10 +322,12 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, TPlan *p) {
 sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, float *const *outs, uint64_t n_vec,
                        uint64_t r0, uint64_t r1, cudaStream_t stream) {
     const uint32_t t0 = (uint32_t)(r0 / TILE_ROWS), t1 = (uint32_t)((r1 + TILE_ROWS - 1) / TILE_ROWS);
-    for (uint64_t g = 0; g < n_vec; g += TGEMV_MAXV) {
-        const int nv = (int)(n_vec - g < TGEMV_MAXV ? n_vec - g : TGEMV_MAXV);
+    for (uint64_t g = 0; g < n_vec;) {
+        // as many vectors per launch as the shared-memory plan can stage
+        int nv = (int)(n_vec - g < TGEMV_MAXV ? n_vec - g : TGEMV_MAXV);
         TPlan p;
-        sg_status st = tiled_plan(dt, nb, t1 - t0, nv, &p);
+        sg_status st;
+        while ((st = tiled_plan(dt, nb, t1 - t0, nv, &p)) == SG_ERR_SHAPE && nv > 1) nv = nv > 4 ? 4 : nv / 2;
         if (st) return st;
         TGemvArgs a;
         memset(&a, 0, sizeof a);
@@ -288,9 +337,11 @@ sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, 
         a.ntiles = t1 - t0;
         a.r0 = (uint32_t)r0;
         a.r1 = (uint32_t)r1;
+        a.S = p.S;
         a.bc = p.bc;
         a.nstages = p.nstages;
         a.stage_bytes = p.stage_bytes;
+        a.slot_blocks = p.slot_blocks;
         a.nvec = (uint32_t)nv;
         for (int v = 0; v < nv; v++) {
             a.xd[v] = xq[g + v].d;
@@ -298,8 +349,8 @@ sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, 
             a.xb[v] = xq[g + v].bsums;
             a.out[v] = outs[g + v];
         }
-        p.fn<<<p.grid, TGEMV_WARPS * 32, p.smem, stream>>>(a);
-        CK(cudaGetLastError());
+        CK(launch_pdl((const void *)p.fn, p.grid, TGEMV_WARPS * 32, p.smem, stream, &a));
+        g += (uint64_t)nv;
     }
     return SG_OK;
 }
@@ -465,7 +516,7 @@ sg_status sg_device_status(void) {
     unsigned v = 0, zero = 0;
     CK(cudaMemcpyFromSymbol(&v, g_dev_status, sizeof v));
     if (v) CK(cudaMemcpyToSymbol(g_dev_status, &zero, sizeof zero));
-    return v == DEV_OK ? SG_OK : SG_ERR_TIMEOUT;
+    return v == DEV_OK ? SG_OK : v == DEV_BAD_LAUNCH ? SG_ERR_INVALID : SG_ERR_TIMEOUT;
 }
 
 sg_status sg_matmul_rows(const uint8_t *d_base, const sg_mat *m, const sg_q8k *xq, float *const *outs,
@@ -510,8 +561,8 @@ sg_status sg_q8k_quantize(const float *d_x, uint64_t n, uint64_t n_vec, uint64_t
         a.nvec = nv;
         for (uint32_t v = 0; v < nv; v++) a.outs[v] = outs[g + v];
         const uint64_t warps = nb * nv;
-        q8k_quantize_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, (cudaStream_t)stream>>>(a);
-        CK(cudaGetLastError());
+        CK(launch_pdl((const void *)q8k_quantize_kernel, (uint32_t)((warps + 7) / 8), 256, 0, (cudaStream_t)stream,
+                      &a));
     }
     return SG_OK;
 }

@@ -5,17 +5,23 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/spindle_gpu.h"
+#include "spindle_gpu.h"
 
 namespace sg {
 
 // Device-side status word: bounded waits record where they gave up instead of
 // hanging or trapping; the host reads it with sg_device_status().
-enum : unsigned { DEV_OK = 0, DEV_TIMEOUT_TMA = 1 };
+enum : unsigned { DEV_OK = 0, DEV_TIMEOUT_TMA = 1, DEV_BAD_LAUNCH = 2 };
 extern __device__ unsigned g_dev_status;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint32_t dynamic_smem_size() {
+    uint32_t v;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(v));
+    return v;
 }
 
 __device__ __forceinline__ float half_at(const uint8_t *p) {

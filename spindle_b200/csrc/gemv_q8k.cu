@@ -35,6 +35,10 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_q8k_kernel(const __grid_con
     const uint32_t nb = a.nb, rb = a.rb, R = a.R, ncol = nb * 8u;
     int32_t *s_corr = s_sum + R * NV * a.sum_stride;
 
+    if (128u + a.nstages * a.stage_bytes + gemv_scratch_bytes(R, NV, nb, a.sum_stride) > dynamic_smem_size()) {
+        if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+        return;
+    }
     const uint32_t tid = threadIdx.x;
     const unsigned gmask = 0xFFu << (tid & 24u);
 

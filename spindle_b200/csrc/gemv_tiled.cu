@@ -8,52 +8,227 @@ namespace {
 constexpr uint32_t M4 = 0x0F0F0F0Fu, B45 = 0x30303030u;
 
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
-__device__ __forceinline__ uint4 ldg128(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
 __device__ __forceinline__ uint32_t w4(const uint4 &v, int m) { return m == 0 ? v.x : m == 1 ? v.y : m == 2 ? v.z : v.w; }
 __device__ __forceinline__ int sbyte(uint32_t w, int b) { return (int)(int8_t)(w >> (8 * b)); }
 __device__ __forceinline__ int ubyte(uint32_t w, int b) { return (int)((w >> (8 * b)) & 0xFFu); }
-__device__ __forceinline__ int lo16(uint32_t w) { return (int)(int16_t)(w & 0xFFFFu); }
-__device__ __forceinline__ int hi16(uint32_t w) { return (int)(int16_t)(w >> 16); }
 __device__ __forceinline__ float h2f_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
 __device__ __forceinline__ float h2f_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+
+// float(s), exact.  Q4_K lane sums satisfy |s| < 2^22, so 1.5*2^23 + s is an
+// exact float whose bits are 0x4B400000 + s; subtracting 1.5*2^23 is exact
+// too (two ALU/FMA ops instead of a conversion).  Q6_K sums can reach 2^25 and
+// use the rounding conversion.
+template <int DT>
+__device__ __forceinline__ float lane_f(int s) {
+    if constexpr (DT == 0) return __fsub_rn(__int_as_float(0x4B400000 + s), 12582912.0f);
+    return __int2float_rn(s);
+}
+
+// TILED16 stores each row's quant bytes in 16-byte chunks permuted by row so
+// that the 8 rows an LDS.128 phase reads fall in 8 different bank groups:
+//   Q4_K qs (8 chunks/row):    chunk c at c ^ (r & 7)
+//   Q6_K qlqh (12 chunks/row): chunk c at (c & ~3) | ((c ^ (r >> 1)) & 3)
+__host__ __device__ __forceinline__ uint32_t q4k_chunk(uint32_t c, uint32_t r) { return c ^ (r & 7u); }
+__host__ __device__ __forceinline__ uint32_t q6k_chunk(uint32_t c, uint32_t r) {
+    return (c & ~3u) | ((c ^ (r >> 1)) & 3u);
+}
+
+// Programmatic dependent launch: wait for the grids this one depends on
+// (no-op when launched without the attribute), and let dependents launch.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 }  // namespace
 
+namespace {
+
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void named_arrive(uint32_t id, uint32_t n) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// One super-block of one 16-row tile for lanes 4g..4g+3 of row r: the exact
+// int32 lane sums s, d*xd (cd) and the correction term (ct) per vector.
+template <int NV>
+__device__ __forceinline__ void block_q4k(const uint8_t *col, uint32_t g, uint32_t r, uint32_t i,
+                                          const TGemvArgs &a, const uint8_t *act, uint32_t act_stride,
+                                          int (&s)[NV][4], float (&cd)[NV], float (&ct)[NV]) {
+    const uint4 hd = lds128(col + 2048 + 16 * r);
+    const float d = h2f_lo(hd.x), dmin = h2f_hi(hd.x);
+    const uint32_t sclo = hd.y & 0x3F3F3F3Fu, schi = (hd.w & M4) | ((hd.y >> 2) & B45);
+    const uint32_t mnw = g ? (((hd.w >> 4) & M4) | ((hd.z >> 2) & B45)) : (hd.z & 0x3F3F3F3Fu);
+    const int sc[8] = {ubyte(sclo, 0), ubyte(sclo, 1), ubyte(sclo, 2), ubyte(sclo, 3),
+                       ubyte(schi, 0), ubyte(schi, 1), ubyte(schi, 2), ubyte(schi, 3)};
+    uint32_t lo[4][4], hi[4][4];
+#pragma unroll
+    for (int cc = 0; cc < 4; cc++) {
+        const uint4 qv = lds128(col + 128 * r + 16 * q4k_chunk(2 * cc + g, r));
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            lo[cc][m] = w4(qv, m) & M4;
+            hi[cc][m] = (w4(qv, m) >> 4) & M4;
+        }
+    }
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        if (v >= (int)a.nvec) break;
+        const uint8_t *av = act + v * act_stride;
+        const uint8_t *y = av + 256u * i + 16u * g;
+        uint4 Y[8];
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) Y[kk] = lds128(y + 32 * kk);
+        const uint4 B = lds128(av + 256u * a.nb + 32u * i + 16u * g);
+        const float xd = *reinterpret_cast<const float *>(av + 288u * a.nb + 4u * i);
+#pragma unroll
+        for (int m = 0; m < 4; m++) s[v][m] = 0;
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++)
+#pragma unroll
+            for (int m = 0; m < 4; m++) {
+                s[v][m] += sc[2 * cc] * __dp4a((int)lo[cc][m], (int)w4(Y[2 * cc], m), 0);
+                s[v][m] += sc[2 * cc + 1] * __dp4a((int)hi[cc][m], (int)w4(Y[2 * cc + 1], m), 0);
+            }
+        cd[v] = __fmul_rn(d, xd);
+        // mins: sum over sub-blocks j = 4g..4g+3 of mn_j * (bsums[2j] + bsums[2j+1]),
+        // one dp2a per pair with mn_j in both low bytes
+        int sp = 0;
+#pragma unroll
+        for (int m = 0; m < 4; m++) sp = __dp2a_lo((int)w4(B, m), (int)__byte_perm(mnw, 0, 0x11 * m), sp);
+        sp += __shfl_xor_sync(0xffffffffu, sp, 16);
+        ct[v] = __fmul_rn(__fmul_rn(dmin, xd), __int2float_rn(sp));
+    }
+}
+
+template <int NV>
+__device__ __forceinline__ void block_q6k(const uint8_t *col, uint32_t g, uint32_t r, uint32_t i,
+                                          const TGemvArgs &a, const uint8_t *act, uint32_t act_stride,
+                                          int (&s)[NV][4], float (&cd)[NV], float (&ct)[NV]) {
+    const uint8_t *qrow = col + 192 * r;
+    uint32_t w[8][4];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const uint4 L0 = lds128(qrow + 16 * q6k_chunk(4 * h + g, r));
+        const uint4 L1 = lds128(qrow + 16 * q6k_chunk(4 * h + 2 + g, r));
+        const uint4 H = lds128(qrow + 16 * q6k_chunk(8 + 2 * h + g, r));
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            const uint32_t l0 = w4(L0, m), l1 = w4(L1, m), hh = w4(H, m);
+            w[4 * h + 0][m] = (l0 & M4) | ((hh << 4) & B45);
+            w[4 * h + 1][m] = (l1 & M4) | ((hh << 2) & B45);
+            w[4 * h + 2][m] = ((l0 >> 4) & M4) | (hh & B45);
+            w[4 * h + 3][m] = ((l1 >> 4) & M4) | ((hh >> 2) & B45);
+        }
+    }
+    const uint4 SC = lds128(col + 3072 + 16 * r);
+    const float d = __half2float(*reinterpret_cast<const __half *>(col + 3328 + 2 * r));
+    // chunk 4h+k of lanes 4g..4g+3 uses scale 8h + 2k + g
+    int scv[8];
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) scv[4 * h + kk] = sbyte(w4(SC, 2 * h + (kk >> 1)), 2 * (kk & 1) + (int)g);
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        if (v >= (int)a.nvec) break;
+        const uint8_t *av = act + v * act_stride;
+        const uint8_t *y = av + 256u * i + 16u * g;
+        uint4 Y[8];
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) Y[kk] = lds128(y + 32 * kk);
+        const uint4 B = lds128(av + 256u * a.nb + 32u * i + 16u * g);
+        const float xd = *reinterpret_cast<const float *>(av + 288u * a.nb + 4u * i);
+#pragma unroll
+        for (int m = 0; m < 4; m++) s[v][m] = 0;
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++)
+#pragma unroll
+            for (int m = 0; m < 4; m++) s[v][m] += scv[kk] * __dp4a((int)w[kk][m], (int)w4(Y[kk], m), 0);
+        cd[v] = __fmul_rn(d, xd);
+        // offset: sum over groups 8g..8g+7 of sc * bsums, one dp2a per pair
+        const uint32_t sw0 = g ? SC.z : SC.x, sw1 = g ? SC.w : SC.y;
+        int sp = __dp2a_lo((int)B.x, (int)sw0, 0);
+        sp = __dp2a_hi((int)B.y, (int)sw0, sp);
+        sp = __dp2a_lo((int)B.z, (int)sw1, sp);
+        sp = __dp2a_hi((int)B.w, (int)sw1, sp);
+        sp += __shfl_xor_sync(0xffffffffu, sp, 16);
+        ct[v] = __fmul_rn(cd[v], __int2float_rn(32 * sp));
+    }
+}
+
+}  // namespace
+
 template <int DT, int NV>
-__global__ void __launch_bounds__(TGEMV_WARPS * 32) gemv_tiled_kernel(const __grid_constant__ TGemvArgs a) {
+__global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const __grid_constant__ TGemvArgs a) {
     constexpr uint32_t CB = tiled_col_bytes(DT);
     extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * a.nstages;
-    uint8_t *ring = smem + 256 + warp * a.nstages * a.stage_bytes;
-    const uint32_t g = lane >> 4, r = lane & 15u;
-    const uint32_t nchunks = (a.nb + a.bc - 1) / a.bc;
-    const uint32_t gw = blockIdx.x * TGEMV_WARPS + warp, W = gridDim.x * TGEMV_WARPS;
-    const uint32_t my_tiles = gw < a.ntiles ? (a.ntiles - gw + W - 1) / W : 0u;
-    const uint32_t nitems = my_tiles * nchunks;
-    const uint64_t tile_bytes = (uint64_t)a.nb * CB;
-
-    auto issue = [&](uint32_t k) {
-        const uint32_t tt = a.t0 + gw + (k / nchunks) * W, c = k % nchunks;
-        const uint32_t ncols = min(a.bc, a.nb - c * a.bc);
-        uint64_t *bar = &bars[k % a.nstages];
-        mbar_arrive_expect_tx(bar, ncols * CB);
-        bulk_g2s(ring + (k % a.nstages) * a.stage_bytes, a.w + tt * tile_bytes + (uint64_t)c * a.bc * CB,
-                 ncols * CB, bar);
-    };
-    if (lane == 0) {
-        for (uint32_t s = 0; s < a.nstages; s++) mbar_init(&bars[s], 1);
-        fence_mbar_init();
+    // A launch whose shared memory cannot hold this layout records an error
+    // and does nothing (uniform exit, before any barrier).
+    if (tiled_smem_bytes(a.S, a.nstages, a.stage_bytes, a.slot_blocks, NV, a.nb) > dynamic_smem_size() ||
+        a.bc == 0 || a.stage_bytes < a.bc * CB || a.S == 0 || TGEMV_WARPS % a.S ||
+        a.nstages * TGEMV_WARPS * 8 > TGEMV_BAR_BYTES) {
+        if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+        return;
     }
-    __syncwarp();
-    if (lane == 0)
-        for (uint32_t k = 0; k < nitems && k < a.nstages; k++) issue(k);
+    // Let the next kernel in the stream launch as soon as SMs free up: it only
+    // prefetches its own weights before waiting for this grid to finish.
+    grid_launch_dependents();
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t g = lane >> 4, r = lane & 15u;
+    const uint32_t S = a.S, group = warp / S, slot = warp % S, G = TGEMV_WARPS / S;
+    const uint32_t astride = act_bytes(a.nb);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * a.nstages;
+    uint8_t *act = smem + TGEMV_BAR_BYTES;
+    uint8_t *rings = act + NV * astride;
+    uint8_t *ring = rings + warp * a.nstages * a.stage_bytes;
+    const uint32_t worker_floats = a.slot_blocks * NV * CHAIN_FLOATS;
+    float *gscratch = reinterpret_cast<float *>(rings + TGEMV_WARPS * a.nstages * a.stage_bytes) +
+                      group * (S - 1) * worker_floats;
+    const uint32_t b_lo = a.nb * slot / S, nblk = a.nb * (slot + 1) / S - b_lo;
+    const uint32_t bc = a.bc, nchunk = (nblk + bc - 1) / bc;  // stages per tile for this slot
+    const uint32_t gid = blockIdx.x * G + group, GW = gridDim.x * G;
+    const uint32_t my_tiles = gid < a.ntiles ? (a.ntiles - gid + GW - 1) / GW : 0u;
+    const uint32_t nitems = my_tiles * nchunk;
+    const uint64_t tile_bytes = (uint64_t)a.nb * CB;
+    const uint32_t bar_full = 1 + group, bar_free = 1 + G + group, nbar = 32 * S;
 
+    // item k = chunk k % nchunk (bc super-blocks) of this group's tile k / nchunk
+    auto issue = [&](uint32_t k) {
+        const uint32_t tt = a.t0 + gid + (k / nchunk) * GW, c = k % nchunk;
+        const uint32_t nbytes = min(bc, nblk - c * bc) * CB;
+        uint64_t *bar = &bars[k % a.nstages];
+        mbar_arrive_expect_tx(bar, nbytes);
+        bulk_g2s(ring + (k % a.nstages) * a.stage_bytes, a.w + tt * tile_bytes + (uint64_t)(b_lo + c * bc) * CB,
+                 nbytes, bar);
+    };
+    // Weights do not depend on the previous kernel: start streaming them first.
+    if (lane == 0) {
+        for (uint32_t st = 0; st < a.nstages; st++) mbar_init(&bars[st], 1);
+        fence_mbar_init();
+        for (uint32_t k = 0; k < nitems && k < a.nstages; k++) issue(k);
+    }
+    // The activations do: wait for the grid that wrote them, then stage them.
+    grid_dependency_wait();
+    const uint32_t nb = a.nb;
+    for (uint32_t v = 0; v < a.nvec; v++) {
+        uint8_t *av = act + v * astride;
+        const uint4 *qs = reinterpret_cast<const uint4 *>(a.xs[v]);
+        for (uint32_t j = threadIdx.x; j < nb * 16; j += blockDim.x) reinterpret_cast<uint4 *>(av)[j] = qs[j];
+        const uint32_t *bs = reinterpret_cast<const uint32_t *>(a.xb[v]);
+        for (uint32_t j = threadIdx.x; j < nb * 8; j += blockDim.x)
+            reinterpret_cast<uint32_t *>(av + 256 * nb)[j] = bs[j];
+        for (uint32_t j = threadIdx.x; j < nb; j += blockDim.x)
+            reinterpret_cast<float *>(av + 288 * nb)[j] = a.xd[v][j];
+    }
+    __syncthreads();
+
+    bool failed = false;
     uint32_t k = 0;
     for (uint32_t ti = 0; ti < my_tiles; ti++) {
-        const uint32_t tt = a.t0 + gw + ti * W;
+        const uint32_t tt = a.t0 + gid + ti * GW;
         float acc[NV][4], corr[NV];
 #pragma unroll
         for (int v = 0; v < NV; v++) {
@@ -61,138 +236,96 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32) gemv_tiled_kernel(const __gr
 #pragma unroll
             for (int m = 0; m < 4; m++) acc[v][m] = 0.0f;
         }
-        for (uint32_t c = 0; c < nchunks; c++, k++) {
+        float *mine = gscratch + (slot ? (slot - 1) * worker_floats : 0u);
+        if (slot > 0 && ti > 0) named_sync(bar_free, nbar);  // slot 0 has read the previous tile
+        for (uint32_t c = 0; c < nchunk; c++, k++) {
             const uint32_t st = k % a.nstages;
-            const bool ok = mbar_wait_bounded(&bars[st], (k / a.nstages) & 1u, WAIT_LIMIT_NS);
-            if (__any_sync(0xffffffffu, !ok)) {
-                if (lane == 0) {
-                    atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_TMA);
-                    for (uint32_t q = k; q < nitems && q < k + a.nstages; q++)
-                        mbar_wait_bounded(&bars[q % a.nstages], (q / a.nstages) & 1u, WAIT_LIMIT_NS);
+            if (!failed) {
+                const bool ok = mbar_wait_bounded(&bars[st], (k / a.nstages) & 1u, WAIT_LIMIT_NS);
+                if (__any_sync(0xffffffffu, !ok)) {
+                    // Record the timeout, let copies in flight land (bounded), stop
+                    // issuing; keep the barrier protocol so the CTA still exits.
+                    if (lane == 0) {
+                        atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_TMA);
+                        for (uint32_t p = k; p < nitems && p < k + a.nstages; p++)
+                            mbar_wait_bounded(&bars[p % a.nstages], (p / a.nstages) & 1u, WAIT_LIMIT_NS);
+                    }
+                    failed = true;
+                    __syncwarp();
                 }
-                __syncwarp();
-                return;
             }
-            const uint8_t *stage = ring + st * a.stage_bytes;
-            const uint32_t ncols = min(a.bc, a.nb - c * a.bc);
-            for (uint32_t q = 0; q < ncols; q++) {
-                const uint32_t i = c * a.bc + q;
-                const uint8_t *col = stage + q * CB;
-                if constexpr (DT == 0) {
-                    // ---- Q4_K: head = d, dmin, 12 scale bytes; qs row = 128 B
-                    const uint4 hd = lds128(col + 2048 + 16 * r);
-                    const float d = h2f_lo(hd.x), dmin = h2f_hi(hd.x);
-                    const uint32_t sclo = hd.y & 0x3F3F3F3Fu, schi = (hd.w & M4) | ((hd.y >> 2) & B45);
-                    const uint32_t mnw = g ? (((hd.w >> 4) & M4) | ((hd.z >> 2) & B45)) : (hd.z & 0x3F3F3F3Fu);
-                    const int sc[8] = {ubyte(sclo, 0), ubyte(sclo, 1), ubyte(sclo, 2), ubyte(sclo, 3),
-                                       ubyte(schi, 0), ubyte(schi, 1), ubyte(schi, 2), ubyte(schi, 3)};
-                    uint32_t lo[4][4], hi[4][4];
+            const uint32_t ncols = min(bc, nblk - c * bc);
+            for (uint32_t qq = 0; qq < ncols; qq++) {
+                const uint32_t q = c * bc + qq, i = b_lo + q;
+                const uint8_t *col = ring + st * a.stage_bytes + qq * CB;
+                int s[NV][4];
+                float cd[NV], ct[NV];
+                if constexpr (DT == 0)
+                    block_q4k<NV>(col, g, r, i, a, act, astride, s, cd, ct);
+                else
+                    block_q6k<NV>(col, g, r, i, a, act, astride, s, cd, ct);
 #pragma unroll
-                    for (int cc = 0; cc < 4; cc++) {
-                        const uint4 qv = lds128(col + 128 * r + 32 * cc + 16 * g);
+                for (int v = 0; v < NV; v++) {
+                    if (v >= (int)a.nvec) break;
+                    if (slot == 0) {
 #pragma unroll
-                        for (int m = 0; m < 4; m++) {
-                            lo[cc][m] = w4(qv, m) & M4;
-                            hi[cc][m] = (w4(qv, m) >> 4) & M4;
+                        for (int m = 0; m < 4; m++) acc[v][m] = __fmaf_rn(cd[v], lane_f<DT>(s[v][m]), acc[v][m]);
+                        corr[v] = __fadd_rn(corr[v], ct[v]);
+                    } else {
+                        float *e = mine + (q * NV + v) * CHAIN_FLOATS;
+                        *reinterpret_cast<float4 *>(e + 64 * g + 4 * r) =
+                            make_float4(lane_f<DT>(s[v][0]), lane_f<DT>(s[v][1]), lane_f<DT>(s[v][2]),
+                                        lane_f<DT>(s[v][3]));
+                        if (g == 0) {
+                            e[128 + r] = cd[v];
+                            e[144 + r] = ct[v];
                         }
-                    }
-#pragma unroll
-                    for (int v = 0; v < NV; v++) {
-                        if (v >= (int)a.nvec) break;
-                        const int8_t *y = a.xs[v] + 256u * i + 16u * g;
-                        uint4 Y[8];
-#pragma unroll
-                        for (int kk = 0; kk < 8; kk++) Y[kk] = ldg128(y + 32 * kk);
-                        const uint4 B = ldg128(a.xb[v] + 16u * i + 8u * g);
-                        const float xd = __ldg(a.xd[v] + i);
-                        int s[4] = {0, 0, 0, 0};
-#pragma unroll
-                        for (int cc = 0; cc < 4; cc++)
-#pragma unroll
-                            for (int m = 0; m < 4; m++) {
-                                s[m] += sc[2 * cc] * __dp4a((int)lo[cc][m], (int)w4(Y[2 * cc], m), 0);
-                                s[m] += sc[2 * cc + 1] * __dp4a((int)hi[cc][m], (int)w4(Y[2 * cc + 1], m), 0);
-                            }
-                        const float cd = __fmul_rn(d, xd);
-#pragma unroll
-                        for (int m = 0; m < 4; m++) acc[v][m] = __fmaf_rn(cd, __int2float_rn(s[m]), acc[v][m]);
-                        int sp = 0;
-#pragma unroll
-                        for (int m = 0; m < 4; m++) sp += ubyte(mnw, m) * (lo16(w4(B, m)) + hi16(w4(B, m)));
-                        sp += __shfl_xor_sync(0xffffffffu, sp, 16);
-                        corr[v] = __fadd_rn(corr[v], __fmul_rn(__fmul_rn(dmin, xd), __int2float_rn(sp)));
-                    }
-                } else {
-                    // ---- Q6_K: qlqh row = ql[128] qh[64]; scales row = 16 B; d = 2 B
-                    const uint8_t *qrow = col + 192 * r;
-                    uint32_t w[8][4];
-#pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        const uint4 L0 = lds128(qrow + 64 * h + 16 * g);
-                        const uint4 L1 = lds128(qrow + 64 * h + 32 + 16 * g);
-                        const uint4 H = lds128(qrow + 128 + 32 * h + 16 * g);
-#pragma unroll
-                        for (int m = 0; m < 4; m++) {
-                            const uint32_t l0 = w4(L0, m), l1 = w4(L1, m), hh = w4(H, m);
-                            w[4 * h + 0][m] = (l0 & M4) | ((hh << 4) & B45);
-                            w[4 * h + 1][m] = (l1 & M4) | ((hh << 2) & B45);
-                            w[4 * h + 2][m] = ((l0 >> 4) & M4) | (hh & B45);
-                            w[4 * h + 3][m] = ((l1 >> 4) & M4) | ((hh >> 2) & B45);
-                        }
-                    }
-                    const uint4 SC = lds128(col + 3072 + 16 * r);
-                    const float d = __half2float(*reinterpret_cast<const __half *>(col + 3328 + 2 * r));
-                    // chunk 4h+k of lanes 4g..4g+3 uses scale 8h + 2k + g
-                    int scv[8];
-#pragma unroll
-                    for (int h = 0; h < 2; h++)
-#pragma unroll
-                        for (int kk = 0; kk < 4; kk++)
-                            scv[4 * h + kk] = sbyte(w4(SC, 2 * h + (kk >> 1)), 2 * (kk & 1) + (int)g);
-#pragma unroll
-                    for (int v = 0; v < NV; v++) {
-                        if (v >= (int)a.nvec) break;
-                        const int8_t *y = a.xs[v] + 256u * i + 16u * g;
-                        uint4 Y[8];
-#pragma unroll
-                        for (int kk = 0; kk < 8; kk++) Y[kk] = ldg128(y + 32 * kk);
-                        const uint4 Ba = ldg128(a.xb[v] + 16u * i), Bb = ldg128(a.xb[v] + 16u * i + 8u);
-                        const float xd = __ldg(a.xd[v] + i);
-                        int s[4] = {0, 0, 0, 0};
-#pragma unroll
-                        for (int kk = 0; kk < 8; kk++)
-#pragma unroll
-                            for (int m = 0; m < 4; m++) s[m] += scv[kk] * __dp4a((int)w[kk][m], (int)w4(Y[kk], m), 0);
-                        const float cd = __fmul_rn(d, xd);
-#pragma unroll
-                        for (int m = 0; m < 4; m++) acc[v][m] = __fmaf_rn(cd, __int2float_rn(s[m]), acc[v][m]);
-                        // groups of parity g: sum_j sc[2j+g] * bsums[2j+g]
-                        int sp = 0;
-#pragma unroll
-                        for (int j = 0; j < 8; j++) {
-                            const uint32_t bw = j < 4 ? w4(Ba, j) : w4(Bb, j - 4);
-                            sp += scv[j] * (g ? hi16(bw) : lo16(bw));
-                        }
-                        sp += __shfl_xor_sync(0xffffffffu, sp, 16);
-                        corr[v] = __fadd_rn(corr[v], __fmul_rn(cd, __int2float_rn(32 * sp)));
                     }
                 }
             }
             __syncwarp();
-            if (lane == 0 && k + a.nstages < nitems) {
+            if (lane == 0 && !failed && k + a.nstages < nitems) {
                 fence_proxy_async();
                 issue(k + a.nstages);
             }
         }
-        // 8-lane tree ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)), then minus the correction.
-        const uint32_t row = tt * TILE_ROWS + r;
+        if (S > 1) {
+            if (slot > 0) {
+                named_arrive(bar_full, nbar);
+            } else {
+                named_sync(bar_full, nbar);
+                // continue the chain over the other slots' blocks, in block order
+                for (uint32_t ws = 1; ws < S; ws++) {
+                    const float *src = gscratch + (ws - 1) * worker_floats;
+                    const uint32_t n_ws = a.nb * (ws + 1) / S - a.nb * ws / S;
+                    for (uint32_t q = 0; q < n_ws; q++)
 #pragma unroll
-        for (int v = 0; v < NV; v++) {
-            float x[4];
+                        for (int v = 0; v < NV; v++) {
+                            if (v >= (int)a.nvec) break;
+                            const float *e = src + (q * NV + v) * CHAIN_FLOATS;
+                            const float4 f = *reinterpret_cast<const float4 *>(e + 64 * g + 4 * r);
+                            const float c = e[128 + r];
+                            acc[v][0] = __fmaf_rn(c, f.x, acc[v][0]);
+                            acc[v][1] = __fmaf_rn(c, f.y, acc[v][1]);
+                            acc[v][2] = __fmaf_rn(c, f.z, acc[v][2]);
+                            acc[v][3] = __fmaf_rn(c, f.w, acc[v][3]);
+                            corr[v] = __fadd_rn(corr[v], e[144 + r]);
+                        }
+                }
+                if (ti + 1 < my_tiles) named_arrive(bar_free, nbar);
+            }
+        }
+        if (slot == 0) {
+            // 8-lane tree ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)), then minus the correction.
+            const uint32_t row = tt * TILE_ROWS + r;
 #pragma unroll
-            for (int m = 0; m < 4; m++) x[m] = __fadd_rn(acc[v][m], __shfl_down_sync(0xffffffffu, acc[v][m], 16));
-            if (g == 0 && v < (int)a.nvec && row >= a.r0 && row < a.r1)
-                a.out[v][row] = __fsub_rn(__fadd_rn(__fadd_rn(x[0], x[2]), __fadd_rn(x[1], x[3])), corr[v]);
+            for (int v = 0; v < NV; v++) {
+                float x[4];
+#pragma unroll
+                for (int m = 0; m < 4; m++) x[m] = __fadd_rn(acc[v][m], __shfl_down_sync(0xffffffffu, acc[v][m], 16));
+                if (g == 0 && v < (int)a.nvec && row >= a.r0 && row < a.r1)
+                    a.out[v][row] = __fsub_rn(__fadd_rn(__fadd_rn(x[0], x[2]), __fadd_rn(x[1], x[3])), corr[v]);
+            }
         }
     }
 }
@@ -216,18 +349,17 @@ __global__ void repack_tiled16_kernel(int dt, const uint8_t *src, uint64_t rows,
     const uint32_t bb = dt == 0 ? 144u : 210u, cb = tiled_col_bytes(dt);
     const uint64_t g_off = (row * nb + i) * bb;
     const uint64_t t_off = (row / TILE_ROWS) * (uint64_t)nb * cb + (uint64_t)i * cb;
-    // (offset in the GGUF block, offset in the tile column, length)
-    uint32_t seg[3][3];
-    int nseg;
+    // (offset in the GGUF block, offset in the tile column, length); the quant
+    // bytes move in 16-byte chunks to their swizzled slots
+    uint32_t seg[16][3];
+    int nseg = 0;
     if (dt == 0) {
-        seg[0][0] = 0, seg[0][1] = 2048 + 16 * r, seg[0][2] = 16;
-        seg[1][0] = 16, seg[1][1] = 128 * r, seg[1][2] = 128;
-        nseg = 2;
+        seg[nseg][0] = 0, seg[nseg][1] = 2048 + 16 * r, seg[nseg++][2] = 16;
+        for (uint32_t c = 0; c < 8; c++) seg[nseg][0] = 16 + 16 * c, seg[nseg][1] = 128 * r + 16 * q4k_chunk(c, r), seg[nseg++][2] = 16;
     } else {
-        seg[0][0] = 0, seg[0][1] = 192 * r, seg[0][2] = 192;
-        seg[1][0] = 192, seg[1][1] = 3072 + 16 * r, seg[1][2] = 16;
-        seg[2][0] = 208, seg[2][1] = 3328 + 2 * r, seg[2][2] = 2;
-        nseg = 3;
+        for (uint32_t c = 0; c < 12; c++) seg[nseg][0] = 16 * c, seg[nseg][1] = 192 * r + 16 * q6k_chunk(c, r), seg[nseg++][2] = 16;
+        seg[nseg][0] = 192, seg[nseg][1] = 3072 + 16 * r, seg[nseg++][2] = 16;
+        seg[nseg][0] = 208, seg[nseg][1] = 3328 + 2 * r, seg[nseg++][2] = 2;
     }
     for (int sgi = 0; sgi < nseg; sgi++)
         for (uint32_t b = 0; b < seg[sgi][2]; b++) {

@@ -26,6 +26,11 @@ __device__ __forceinline__ int8_t cvt_pack(float v) {
 }  // namespace
 
 __global__ void __launch_bounds__(256) q8k_quantize_kernel(const __grid_constant__ Q8kArgs a) {
+    // Programmatic dependent launch: let the next kernel (the GEMV that reads
+    // this output) launch now, so its weight prefetch overlaps this kernel and
+    // the one before it; then wait for the kernel that wrote x.
+    asm volatile("griddepcontrol.launch_dependents;" :::);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31u;
     if (warp >= a.nb * a.nvec) return;
     const uint32_t vec = warp / a.nb, b = warp % a.nb;
