@@ -228,11 +228,14 @@ def run_gpu(args):
     torch.cuda.synchronize()
 
     def gemv(k):
-        sg.matmul_rows(W[k], M[k], XQ[k], [OUT[k][b] for b in range(nvec)], 0, M[k].rows)
+        if args.layout == "tiled":
+            sg.matvec(W[k], M[k], X[k], OUT[k])  # Q8_K quantization fused into the GEMV kernel
+        else:
+            sg.quantize_into(X[k], XQ[k])
+            sg.matmul_rows(W[k], M[k], XQ[k], [OUT[k][b] for b in range(nvec)], 0, M[k].rows)
 
     def step():
         for k in range(len(SHAPES)):
-            sg.quantize_into(X[k], XQ[k])
             gemv(k)
 
     # Warm-up outside capture (plans, function attributes), then capture.
@@ -247,7 +250,7 @@ def run_gpu(args):
         with torch.cuda.graph(g_gemv, stream=stream):
             for k in range(len(SHAPES)):
                 gemv(k)
-    launches_per_step = 2 * len(SHAPES)
+    launches_per_step = (1 if args.layout == "tiled" else 2) * len(SHAPES)
 
     def barrier():
         if world > 1:
@@ -323,7 +326,6 @@ def run_gpu(args):
             for k in range(len(SHAPES)):
                 _lib.check(lib.sg_memcpy_h2d(C.c_void_p(X[k].data_ptr()), C.c_void_p(h_x[k].data_ptr()),
                                              h_x[k].numel() * 4, sp), "h2d")
-                sg.quantize_into(X[k], XQ[k])
                 gemv(k)
                 _lib.check(lib.sg_memcpy_d2h(C.c_void_p(h_o[k].data_ptr()), C.c_void_p(OUT[k].data_ptr()),
                                              h_o[k].numel() * 4, sp), "d2h")
@@ -366,13 +368,14 @@ def run_gpu(args):
                 "config": config_block(args, world),
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
-                             "kernel": "gemv_q8k_kernel", "how": "algorithmic bytes of the 7 GEMV launches / "
-                             "their replayed duration (CUDA events on the launch stream)"},
+                             "kernel": "gemv_tiled_kernel" if args.layout == "tiled" else "gemv_q8k_kernel",
+                             "how": "algorithmic bytes of the 7 GEMV launches / their replayed duration "
+                                    "(CUDA events on the launch stream)"},
                 "per_shape": per_shape,
                 "e2e": {"value": round(bytes_rank * world / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                        "how": "sg_memcpy_h2d of the fp32 activations from pinned host, quantize, GEMV, "
-                               "sg_memcpy_d2h of the fp32 outputs, every step"},
+                        "how": "sg_memcpy_h2d of the fp32 activations from pinned host, sg_matvec "
+                               "(quantize + GEMV), sg_memcpy_d2h of the fp32 outputs, every step"},
                 "gpu_launches": launches_per_step * args.steps,
                 "clocks": clk.summary()}
     if world > 1:

@@ -140,6 +140,15 @@ SG_API sg_status sg_repack_tiled16(int32_t dtype, const uint8_t *d_gguf, uint64_
 SG_API sg_status sg_unpack_tiled16(int32_t dtype, const uint8_t *d_tiled, uint64_t rows, uint64_t cols,
                                    uint8_t *d_gguf, void *stream);
 
+/* matvec / matvec_multi on the integer path (smollm_chat.rs:309-318 and
+ * :447-512): out_b = W * x_b for b < n_vec, rows r0..r1, where x_b = d_x +
+ * b*ldx holds cols fp32 values (16-byte aligned) and row r of out_b is
+ * d_out[b*ldo + r].  The Q8_K quantization of x_b runs inside the GEMV kernel
+ * (no scratch memory, one launch); the bits equal sg_q8k_quantize followed by
+ * sg_matmul_rows.  TILED16 weights only (SG_ERR_INVALID for GGUF rows). */
+SG_API sg_status sg_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
+                           uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, void *stream);
+
 /* The int32 lane sums of rows<B,T> (quant_q8k.rs:235-242) for one vector, as
  * the kernel computes them: d_out[(r-r0)*nb*8 + i*8 + l] = lane l of block i
  * of row r.  Exists to check per-super-block sums bit for bit.  GGUF layout only. */

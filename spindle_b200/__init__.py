@@ -127,6 +127,24 @@ def matmul_rows(base, m, xq, outs, r0, r1, stream=None):
                                     _stream(stream)), "matmul_rows")
 
 
+def matvec(base, m, xs, out=None, r0=0, r1=None, stream=None):
+    """matvec / matvec_multi (smollm_chat.rs:309, :447) on the integer path:
+    fp32 CUDA xs [n_vec, cols] (or [cols]) -> out [n_vec, rows]; the Q8_K
+    quantization runs inside the GEMV kernel.  TILED16 weights."""
+    single = xs.dim() == 1
+    xs2 = xs.reshape(1, -1) if single else xs
+    if xs2.dtype != torch.float32 or xs2.stride(-1) != 1:
+        raise ValueError("xs must be float32 with contiguous rows")
+    r1 = m.rows if r1 is None else r1
+    if out is None:
+        out = torch.empty((xs2.shape[0], m.rows), dtype=torch.float32, device=xs2.device)
+    out2 = out.reshape(1, -1) if out.dim() == 1 else out
+    _lib.check(lib().sg_matvec(C.c_void_p(base.data_ptr()), C.byref(m.c()), C.c_void_p(xs2.data_ptr()),
+                               xs2.stride(0), C.c_void_p(out2.data_ptr()), out2.stride(0), xs2.shape[0], r0, r1,
+                               _stream(stream)), "matvec")
+    return out
+
+
 def gemv(base, m, xq, stream=None):
     """All rows for a list of Q8K vectors -> float32 CUDA [n_vec, rows]."""
     out = torch.empty((len(xq), m.rows), dtype=torch.float32, device=base.device)

@@ -230,12 +230,15 @@ typedef void (*tgemv_fn)(const TGemvArgs);
 
 uint32_t tiled_nv_inst(int nv) { return nv <= 1 ? 1u : nv == 2 ? 2u : nv <= 4 ? 4u : 8u; }
 
-tgemv_fn pick_tiled(int dt, int nv) {
-    if (dt == DT_Q4K)
-        return nv == 1 ? gemv_tiled_kernel<0, 1> : nv == 2 ? gemv_tiled_kernel<0, 2>
-               : nv <= 4 ? gemv_tiled_kernel<0, 4> : gemv_tiled_kernel<0, 8>;
-    return nv == 1 ? gemv_tiled_kernel<1, 1> : nv == 2 ? gemv_tiled_kernel<1, 2>
-           : nv <= 4 ? gemv_tiled_kernel<1, 4> : gemv_tiled_kernel<1, 8>;
+template <int DT, bool QX>
+tgemv_fn pick_tiled_t(int nv) {
+    return nv == 1 ? gemv_tiled_kernel<DT, 1, QX> : nv == 2 ? gemv_tiled_kernel<DT, 2, QX>
+           : nv <= 4 ? gemv_tiled_kernel<DT, 4, QX> : gemv_tiled_kernel<DT, 8, QX>;
+}
+
+tgemv_fn pick_tiled(int dt, int nv, bool qx) {
+    if (dt == DT_Q4K) return qx ? pick_tiled_t<0, true>(nv) : pick_tiled_t<0, false>(nv);
+    return qx ? pick_tiled_t<1, true>(nv) : pick_tiled_t<1, false>(nv);
 }
 
 int env_int(const char *name, int dflt) {
@@ -245,7 +248,7 @@ int env_int(const char *name, int dflt) {
 
 struct TPlan {
     tgemv_fn fn;
-    uint32_t S, bc, nstages, stage_bytes, slot_blocks, grid;
+    uint32_t S, bc, nstages, stage_bytes, slot_blocks, grid, warps;
     size_t smem;
 };
 
@@ -253,11 +256,11 @@ std::unordered_map<uint64_t, TPlan> g_tplans;
 
 // Launch shape of the tiled GEMV: S warps per tile so that the whole GPU has
 // work (small row counts split each tile's super-blocks over more warps),
-// a 3-stage ring per warp, CTAs of TGEMV_WARPS warps.
-sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, TPlan *p) {
+// a 2-stage ring per warp, CTAs of 8 or 16 warps.
+sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, bool qx, TPlan *p) {
     int dev;
     CK(cudaGetDevice(&dev));
-    const uint64_t key = ((uint64_t)dev << 56) ^ ((uint64_t)dt << 52) ^ ((uint64_t)nv << 44) ^
+    const uint64_t key = ((uint64_t)dev << 56) ^ ((uint64_t)qx << 55) ^ ((uint64_t)dt << 52) ^ ((uint64_t)nv << 44) ^
                          ((uint64_t)nb << 32) ^ ntiles;
     {
         std::lock_guard<std::mutex> lk(g_mu);
@@ -274,27 +277,46 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, TPlan *p) {
     // the kernel is instantiated for 1, 2, 4 or 8 vectors; its chain scratch is
     // laid out for that count, so size shared memory for it too
     const uint32_t nv_inst = tiled_nv_inst(nv);
-    const uint32_t warp_slots = (uint32_t)di->sms * TGEMV_WARPS;
+    // CTA width: 16 warps (one CTA per SM) or 8 warps (two per SM, so that the
+    // next kernel of a chain can become resident and prefetch its weights
+    // while this one drains)
+    const uint32_t warps = env_int("SG_TILED_WARPS", 16) == 8 ? 8u : 16u;
+    const uint32_t warp_slots = (uint32_t)di->sms * 16u;
+    // S warps per tile: the critical warp (slot 0 of the busiest group) does
+    // ceil(ntiles / groups) tiles, each of ceil(nb / S) full super-blocks plus
+    // the cheap chain steps over the other slots' blocks.  Pick the S with the
+    // shortest such path.
     uint32_t S = 1;
     const int forced = env_int("SG_TILED_S", 0);
-    if (forced == 1 || forced == 2 || forced == 4 || forced == 8)
+    if ((forced == 1 || forced == 2 || forced == 4 || forced == 8 || forced == 16) && (uint32_t)forced <= warps) {
         S = (uint32_t)forced;
-    else
-        while (S < 8 && S * 2 <= nb && (uint64_t)ntiles * S < warp_slots) S *= 2;
+    } else {
+        double best = 1e30;
+        for (uint32_t s = 1; s <= warps && s <= nb; s *= 2) {
+            const uint64_t groups = warp_slots / s;
+            const uint64_t tiles = (ntiles + groups - 1) / groups;
+            const double per_tile = (double)((nb + s - 1) / s) + 0.06 * (double)(nb - nb / s) + (s > 1 ? 0.5 : 0.0);
+            const double cost = (double)tiles * per_tile;
+            if (cost < best * 0.98) {
+                best = cost;
+                S = s;
+            }
+        }
+    }
     uint32_t ns = (uint32_t)env_int("SG_TILED_STAGES", 2), bc = (uint32_t)env_int("SG_TILED_BC", 2);
     if (ns < 2) ns = 2;
     if (ns > 8) ns = 8;
     if (bc < 1) bc = 1;
     // Fit the CTA in shared memory: fewer stages, then smaller stages, then
     // fewer warps per tile (less chain scratch).
-    const size_t budget = 220 * 1024;
+    const size_t budget = warps == 16 ? 220 * 1024 : 110 * 1024;
     for (;;) {
         p->S = S;
         p->slot_blocks = (nb + S - 1) / S;
         p->bc = bc < p->slot_blocks ? bc : p->slot_blocks;
         p->nstages = ns;
         p->stage_bytes = p->bc * cb;
-        p->smem = tiled_smem_bytes(S, ns, p->stage_bytes, p->slot_blocks, nv_inst, nb);
+        p->smem = tiled_smem_bytes(warps, S, ns, p->stage_bytes, p->slot_blocks, nv_inst, nb);
         if (p->smem <= budget) break;
         if (ns > 2)
             ns--;
@@ -305,12 +327,13 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, TPlan *p) {
         else
             return SG_ERR_SHAPE;
     }
-    p->fn = pick_tiled(dt, nv);
+    p->fn = pick_tiled(dt, nv, qx);
     CK(cudaFuncSetAttribute((const void *)p->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
     int occ = 0;
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, (const void *)p->fn, TGEMV_WARPS * 32, p->smem));
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, (const void *)p->fn, warps * 32, p->smem));
     if (occ < 1) occ = 1;
-    const uint32_t groups = TGEMV_WARPS / p->S;
+    p->warps = warps;
+    const uint32_t groups = warps / p->S;
     const uint32_t need = (ntiles + groups - 1) / groups, cap = (uint32_t)(di->sms * occ);
     p->grid = need < cap ? need : cap;
     std::lock_guard<std::mutex> lk(g_mu);
@@ -319,15 +342,17 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, TPlan *p) {
     return SG_OK;
 }
 
-sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, float *const *outs, uint64_t n_vec,
-                       uint64_t r0, uint64_t r1, cudaStream_t stream) {
+// One of xq (Q8_K inputs) or x (fp32 inputs, vector b at x + b*ldx) is given.
+sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, const float *x, uint64_t ldx,
+                       float *const *outs, uint64_t n_vec, uint64_t r0, uint64_t r1, cudaStream_t stream) {
     const uint32_t t0 = (uint32_t)(r0 / TILE_ROWS), t1 = (uint32_t)((r1 + TILE_ROWS - 1) / TILE_ROWS);
+    const bool qx = x != nullptr;
     for (uint64_t g = 0; g < n_vec;) {
         // as many vectors per launch as the shared-memory plan can stage
         int nv = (int)(n_vec - g < TGEMV_MAXV ? n_vec - g : TGEMV_MAXV);
         TPlan p;
         sg_status st;
-        while ((st = tiled_plan(dt, nb, t1 - t0, nv, &p)) == SG_ERR_SHAPE && nv > 1) nv = nv > 4 ? 4 : nv / 2;
+        while ((st = tiled_plan(dt, nb, t1 - t0, nv, qx, &p)) == SG_ERR_SHAPE && nv > 1) nv = nv > 4 ? 4 : nv / 2;
         if (st) return st;
         TGemvArgs a;
         memset(&a, 0, sizeof a);
@@ -344,12 +369,16 @@ sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, 
         a.slot_blocks = p.slot_blocks;
         a.nvec = (uint32_t)nv;
         for (int v = 0; v < nv; v++) {
-            a.xd[v] = xq[g + v].d;
-            a.xs[v] = xq[g + v].qs;
-            a.xb[v] = xq[g + v].bsums;
+            if (qx) {
+                a.x[v] = x + (g + v) * ldx;
+            } else {
+                a.xd[v] = xq[g + v].d;
+                a.xs[v] = xq[g + v].qs;
+                a.xb[v] = xq[g + v].bsums;
+            }
             a.out[v] = outs[g + v];
         }
-        CK(launch_pdl((const void *)p.fn, p.grid, TGEMV_WARPS * 32, p.smem, stream, &a));
+        CK(launch_pdl((const void *)p.fn, p.grid, p.warps * 32, p.smem, stream, &a));
         g += (uint64_t)nv;
     }
     return SG_OK;
@@ -370,7 +399,7 @@ sg_status launch_gemv(const uint8_t *d_base, const sg_mat *m, const sg_q8k *xq, 
     const uint64_t rb = (uint64_t)nb * bb;
     if (m->layout == SG_LAYOUT_TILED16) {
         if (dbg) return SG_ERR_INVALID;
-        return launch_tiled(d_base + m->offset, dt, nb, xq, outs, n_vec, r0, r1, stream);
+        return launch_tiled(d_base + m->offset, dt, nb, xq, nullptr, 0, outs, n_vec, r0, r1, stream);
     }
     for (uint64_t g = 0; g < n_vec; g += GEMV_MAXV) {
         const uint32_t nv = (uint32_t)(n_vec - g < GEMV_MAXV ? n_vec - g : GEMV_MAXV);
@@ -616,6 +645,26 @@ sg_status sg_repack_tiled16(int32_t dtype, const uint8_t *d_gguf, uint64_t rows,
 sg_status sg_unpack_tiled16(int32_t dtype, const uint8_t *d_tiled, uint64_t rows, uint64_t cols, uint8_t *d_gguf,
                             void *stream) {
     return repack(dtype, d_tiled, rows, cols, d_gguf, 1, stream);
+}
+
+sg_status sg_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
+                    uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, void *stream) {
+    int dt;
+    sg_status st = check_mat(d_base, m, r0, r1, &dt);
+    if (st) return st;
+    if (m->layout != SG_LAYOUT_TILED16) return SG_ERR_INVALID;
+    if (r1 == r0 || n_vec == 0) return SG_OK;
+    if (!d_x || !d_out || (n_vec > 1 && (ldx < m->cols || ldo < m->rows))) return SG_ERR_INVALID;
+    if (!aligned(d_x, 16) || (n_vec > 1 && ldx % 4) || !aligned(d_out, 4)) return SG_ERR_ALIGN;
+    float *outs[TGEMV_MAXV];
+    for (uint64_t g = 0; g < n_vec; g += TGEMV_MAXV) {
+        const uint64_t nv = n_vec - g < TGEMV_MAXV ? n_vec - g : TGEMV_MAXV;
+        for (uint64_t v = 0; v < nv; v++) outs[v] = d_out + (g + v) * ldo;
+        st = launch_tiled(d_base + m->offset, dt, (uint32_t)(m->cols / 256), nullptr, d_x + g * ldx, ldx, outs, nv, r0,
+                          r1, (cudaStream_t)stream);
+        if (st) return st;
+    }
+    return SG_OK;
 }
 
 }  // extern "C"

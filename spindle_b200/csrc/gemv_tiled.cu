@@ -1,5 +1,6 @@
 // gemv_tiled.cu — kernels over the TILED16 layout (see gemv_tiled.cuh).
 #include "gemv_tiled.cuh"
+#include "q8k_block.cuh"
 
 namespace sg {
 
@@ -161,15 +162,16 @@ __device__ __forceinline__ void block_q6k(const uint8_t *col, uint32_t g, uint32
 
 }  // namespace
 
-template <int DT, int NV>
+template <int DT, int NV, bool QX>
 __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const __grid_constant__ TGemvArgs a) {
     constexpr uint32_t CB = tiled_col_bytes(DT);
     extern __shared__ __align__(128) uint8_t smem[];
     // A launch whose shared memory cannot hold this layout records an error
     // and does nothing (uniform exit, before any barrier).
-    if (tiled_smem_bytes(a.S, a.nstages, a.stage_bytes, a.slot_blocks, NV, a.nb) > dynamic_smem_size() ||
-        a.bc == 0 || a.stage_bytes < a.bc * CB || a.S == 0 || TGEMV_WARPS % a.S ||
-        a.nstages * TGEMV_WARPS * 8 > TGEMV_BAR_BYTES) {
+    const uint32_t nwarps = blockDim.x >> 5;
+    if (tiled_smem_bytes(nwarps, a.S, a.nstages, a.stage_bytes, a.slot_blocks, NV, a.nb) > dynamic_smem_size() ||
+        a.bc == 0 || a.stage_bytes < a.bc * CB || a.S == 0 || nwarps % a.S || (blockDim.x & 31) ||
+        a.nstages * nwarps * 8 > TGEMV_BAR_BYTES) {
         if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
         return;
     }
@@ -178,14 +180,14 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     grid_launch_dependents();
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t g = lane >> 4, r = lane & 15u;
-    const uint32_t S = a.S, group = warp / S, slot = warp % S, G = TGEMV_WARPS / S;
+    const uint32_t S = a.S, group = warp / S, slot = warp % S, G = nwarps / S;
     const uint32_t astride = act_bytes(a.nb);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * a.nstages;
     uint8_t *act = smem + TGEMV_BAR_BYTES;
     uint8_t *rings = act + NV * astride;
     uint8_t *ring = rings + warp * a.nstages * a.stage_bytes;
     const uint32_t worker_floats = a.slot_blocks * NV * CHAIN_FLOATS;
-    float *gscratch = reinterpret_cast<float *>(rings + TGEMV_WARPS * a.nstages * a.stage_bytes) +
+    float *gscratch = reinterpret_cast<float *>(rings + nwarps * a.nstages * a.stage_bytes) +
                       group * (S - 1) * worker_floats;
     const uint32_t b_lo = a.nb * slot / S, nblk = a.nb * (slot + 1) / S - b_lo;
     const uint32_t bc = a.bc, nchunk = (nblk + bc - 1) / bc;  // stages per tile for this slot
@@ -213,15 +215,26 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     // The activations do: wait for the grid that wrote them, then stage them.
     grid_dependency_wait();
     const uint32_t nb = a.nb;
-    for (uint32_t v = 0; v < a.nvec; v++) {
-        uint8_t *av = act + v * astride;
-        const uint4 *qs = reinterpret_cast<const uint4 *>(a.xs[v]);
-        for (uint32_t j = threadIdx.x; j < nb * 16; j += blockDim.x) reinterpret_cast<uint4 *>(av)[j] = qs[j];
-        const uint32_t *bs = reinterpret_cast<const uint32_t *>(a.xb[v]);
-        for (uint32_t j = threadIdx.x; j < nb * 8; j += blockDim.x)
-            reinterpret_cast<uint32_t *>(av + 256 * nb)[j] = bs[j];
-        for (uint32_t j = threadIdx.x; j < nb; j += blockDim.x)
-            reinterpret_cast<float *>(av + 288 * nb)[j] = a.xd[v][j];
+    if constexpr (QX) {
+        // one warp per (vector, 256-block): the exact Q8_K quantization
+        for (uint32_t wb = warp; wb < a.nvec * nb; wb += nwarps) {
+            const uint32_t v = wb / nb, b = wb % nb;
+            uint8_t *av = act + v * astride;
+            q8k_block(a.x[v] + 256u * b, reinterpret_cast<int8_t *>(av + 256u * b),
+                      reinterpret_cast<int16_t *>(av + 256u * nb + 32u * b),
+                      reinterpret_cast<float *>(av + 288u * nb + 4u * b), lane);
+        }
+    } else {
+        for (uint32_t v = 0; v < a.nvec; v++) {
+            uint8_t *av = act + v * astride;
+            const uint4 *qs = reinterpret_cast<const uint4 *>(a.xs[v]);
+            for (uint32_t j = threadIdx.x; j < nb * 16; j += blockDim.x) reinterpret_cast<uint4 *>(av)[j] = qs[j];
+            const uint32_t *bs = reinterpret_cast<const uint32_t *>(a.xb[v]);
+            for (uint32_t j = threadIdx.x; j < nb * 8; j += blockDim.x)
+                reinterpret_cast<uint32_t *>(av + 256 * nb)[j] = bs[j];
+            for (uint32_t j = threadIdx.x; j < nb; j += blockDim.x)
+                reinterpret_cast<float *>(av + 288 * nb)[j] = a.xd[v][j];
+        }
     }
     __syncthreads();
 
@@ -330,11 +343,10 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     }
 }
 
-#define SG_TINST(DT)                                                                                         \
-    template __global__ void gemv_tiled_kernel<DT, 1>(const __grid_constant__ TGemvArgs);                   \
-    template __global__ void gemv_tiled_kernel<DT, 2>(const __grid_constant__ TGemvArgs);                   \
-    template __global__ void gemv_tiled_kernel<DT, 4>(const __grid_constant__ TGemvArgs);                   \
-    template __global__ void gemv_tiled_kernel<DT, 8>(const __grid_constant__ TGemvArgs);
+#define SG_TINST1(DT, NV)                                                                         \
+    template __global__ void gemv_tiled_kernel<DT, NV, false>(const __grid_constant__ TGemvArgs); \
+    template __global__ void gemv_tiled_kernel<DT, NV, true>(const __grid_constant__ TGemvArgs);
+#define SG_TINST(DT) SG_TINST1(DT, 1) SG_TINST1(DT, 2) SG_TINST1(DT, 4) SG_TINST1(DT, 8)
 SG_TINST(0)
 SG_TINST(1)
 

@@ -27,7 +27,7 @@
 
 namespace sg {
 
-constexpr int TGEMV_WARPS = 16;        // warps per CTA (one CTA per SM)
+constexpr int TGEMV_WARPS = 16;        // most warps per CTA (launches use 8 or 16)
 constexpr int TGEMV_MAXV = 8;          // vectors per launch
 constexpr uint32_t TILE_ROWS = 16;
 constexpr uint32_t CHAIN_FLOATS = 160; // per (block, vector): 16 rows x (8 lane floats + d*xd + corr term)
@@ -49,21 +49,27 @@ struct TGemvArgs {
     uint32_t stage_bytes;
     uint32_t slot_blocks; // max super-blocks of one slot (chain scratch sizing)
     uint32_t nvec;
+    const float *x[TGEMV_MAXV];   // fp32 inputs, when the kernel quantizes them itself (QX)
     const float *xd[TGEMV_MAXV];
     const int8_t *xs[TGEMV_MAXV];
     const int16_t *xb[TGEMV_MAXV];
     float *out[TGEMV_MAXV];
 };
 
-// Dynamic shared memory of one CTA: barriers | activations | rings | chain scratch.
-__host__ __device__ inline uint32_t tiled_smem_bytes(uint32_t S, uint32_t nstages, uint32_t stage_bytes,
-                                                     uint32_t slot_blocks, uint32_t nv, uint32_t nb) {
-    const uint32_t groups = TGEMV_WARPS / S;
-    return TGEMV_BAR_BYTES + nv * act_bytes(nb) + TGEMV_WARPS * nstages * stage_bytes +
+// Dynamic shared memory of one CTA of `warps` warps:
+// barriers | activations | rings | chain scratch.
+__host__ __device__ inline uint32_t tiled_smem_bytes(uint32_t warps, uint32_t S, uint32_t nstages,
+                                                     uint32_t stage_bytes, uint32_t slot_blocks, uint32_t nv,
+                                                     uint32_t nb) {
+    const uint32_t groups = warps / S;
+    return TGEMV_BAR_BYTES + nv * act_bytes(nb) + warps * nstages * stage_bytes +
            groups * (S - 1) * slot_blocks * nv * CHAIN_FLOATS * 4u;
 }
 
-template <int DT, int NV>
+// QX = true: the inputs are fp32 (a.x) and every CTA quantizes them to Q8_K
+// in shared memory (the reference's matvec = Q8K::quantize + matmul_rows, in
+// one kernel).  QX = false: the inputs are Q8_K vectors (a.xd, a.xs, a.xb).
+template <int DT, int NV, bool QX>
 __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const __grid_constant__ TGemvArgs a);
 
 __global__ void repack_tiled16_kernel(int dt, const uint8_t *src, uint64_t rows, uint32_t nb, uint8_t *dst,

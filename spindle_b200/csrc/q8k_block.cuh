@@ -1,0 +1,63 @@
+// q8k_block.cuh — one warp quantizes one 256-value block to Q8_K exactly as
+// Q8K::quantize / quantize_avx2 (quant_q8k.rs:73-121) does, bit for bit,
+// including NaN/Inf and all-zero blocks.
+//
+// amax: the reference keeps 8 running MAXPS lanes (lane j sees x[j], x[j+8],
+// ...; MAXPS returns its second operand when either is NaN), then folds
+// hi->lo, 2->0, 1->0; lanes 0..7 replay exactly that.  Each value becomes
+// cvtps_epi32(x * (127/amax)) saturated to int8 by two packs: round to
+// nearest even, and NaN or |v| >= 2^31 give INT32_MIN, i.e. -128.
+// d = amax/127 and 127/amax are correctly rounded divisions.
+#pragma once
+
+#include "common.cuh"
+
+namespace sg {
+
+__device__ __forceinline__ float maxps(float a, float b) { return a > b ? a : b; }
+
+__device__ __forceinline__ int8_t cvt_pack_i8(float v) {
+    if (isnan(v) || fabsf(v) >= 2147483648.0f) return -128;
+    const int q = __float2int_rn(v);
+    return (int8_t)(q > 127 ? 127 : (q < -128 ? -128 : q));
+}
+
+// xb: 256 floats (16-byte aligned, global or shared); qs: 256 int8 (8-byte
+// aligned); bsums: 16 int16; d: one float.  All 32 lanes of the warp call it.
+__device__ __forceinline__ void q8k_block(const float *xb, int8_t *qs, int16_t *bsums, float *d, uint32_t lane) {
+    float lm = 0.0f;
+    if (lane < 8)
+        for (int m = 0; m < 32; m++) lm = maxps(lm, fabsf(xb[8 * m + lane]));
+    const float v4 = maxps(lm, __shfl_down_sync(0xffffffffu, lm, 4));
+    const float v2 = maxps(v4, __shfl_down_sync(0xffffffffu, v4, 2));
+    const float amax = __shfl_sync(0xffffffffu, maxps(v2, __shfl_down_sync(0xffffffffu, v2, 1)), 0);
+
+    int8_t q[8];
+    if (!(amax > 0.0f) || isinf(amax)) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) q[k] = 0;
+        if (lane == 0) *d = 0.0f;
+    } else {
+        const float inv = __fdiv_rn(127.0f, amax);
+        if (lane == 0) *d = __fdiv_rn(amax, 127.0f);
+        const float4 p0 = reinterpret_cast<const float4 *>(xb)[2 * lane];
+        const float4 p1 = reinterpret_cast<const float4 *>(xb)[2 * lane + 1];
+        const float xv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+        for (int k = 0; k < 8; k++) q[k] = cvt_pack_i8(__fmul_rn(xv[k], inv));
+    }
+    uint32_t w0 = 0, w1 = 0;
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        w0 |= (uint32_t)(uint8_t)q[k] << (8 * k);
+        w1 |= (uint32_t)(uint8_t)q[k + 4] << (8 * k);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) s += q[k];
+    reinterpret_cast<uint2 *>(qs)[lane] = make_uint2(w0, w1);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);  // a group of 16 values = lanes 2g, 2g+1
+    if ((lane & 1u) == 0) bsums[lane / 2] = (int16_t)s;
+}
+
+}  // namespace sg

@@ -82,3 +82,35 @@ def test_tiled_baseline_shapes(dev, dt, rows, cols):
         want = O.gemv_int(w_host, O.Mat(dt, cols, rows), [O.quantize(x) for x in xs_host[:nvec]])
         assert np.array_equal(bits(got), bits(want)), nvec
     sg.device_status()
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
+def test_matvec_fused_quantize_bitexact(dev, dt):
+    # sg_matvec quantizes inside the GEMV kernel; the bits must equal the
+    # oracle's Q8K::quantize + matmul_rows, including non-finite inputs.
+    for n, rows, nvec in [(256, 37, 1), (1024, 301, 3), (4096, 45, 8), (14336, 19, 2), (2048, 64, 11)]:
+        rng = O.Rng(n + rows)
+        w = O.random_matrix(dt, n, rows, rng)
+        xs = np.stack([rng.fill(-2.0, 2.0, n) for _ in range(nvec)])
+        xs[0, 5] = np.nan
+        if n >= 512:
+            xs[-1, 256:512] = 0.0
+            xs[-1, 300] = np.inf if nvec > 1 else 0.0
+        want = O.gemv_int(w, O.Mat(dt, n, rows), [O.quantize(x) for x in xs])
+        t, m = sg.repack_tiled16(dt, to_dev(w, dev), rows, n)
+        xd = torch.zeros(nvec, n + 64, device=dev)   # padded rows: ldx > cols
+        xd[:, :n] = to_dev(xs, dev)
+        got = sg.matvec(t, m, xd[:, :n])
+        assert np.array_equal(bits(got), bits(want)), (n, rows, nvec)
+        # a row range
+        out = torch.full((nvec, rows), float("nan"), device=dev)
+        sg.matvec(t, m, xd[:, :n], out, 3, rows - 2)
+        o = out.cpu().numpy()
+        assert np.array_equal(bits(o[:, 3:rows - 2]), bits(want[:, 3:rows - 2]))
+        assert np.isnan(o[:, :3]).all() and np.isnan(o[:, rows - 2:]).all()
+
+
+def test_matvec_rejects_gguf_layout(dev):
+    w = torch.zeros(144 * 4, dtype=torch.uint8, device=dev)
+    with pytest.raises(sg.SgError):
+        sg.matvec(w, sg.Mat(sg.Q4_K, 1024, 1), torch.zeros(1024, device=dev))
