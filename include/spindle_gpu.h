@@ -149,6 +149,16 @@ SG_API sg_status sg_unpack_tiled16(int32_t dtype, const uint8_t *d_tiled, uint64
 SG_API sg_status sg_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
                            uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, void *stream);
 
+/* The same matvec for either layout with the Q8_K images in caller-owned
+ * scratch (the reference keeps them in thread-local scratch, quant_q8k.rs:
+ * 123-142): quantizes x_b into d_scratch (>= sg_matvec_scratch_bytes(cols,
+ * n_vec) bytes, 16-byte aligned), then runs sg_matmul_rows on it.  Same bits
+ * as sg_matvec. */
+SG_API uint64_t sg_matvec_scratch_bytes(uint64_t cols, uint64_t n_vec);
+SG_API sg_status sg_matvec_scratch(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx,
+                                   float *d_out, uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1,
+                                   void *d_scratch, uint64_t scratch_bytes, void *stream);
+
 /* The int32 lane sums of rows<B,T> (quant_q8k.rs:235-242) for one vector, as
  * the kernel computes them: d_out[(r-r0)*nb*8 + i*8 + l] = lane l of block i
  * of row r.  Exists to check per-super-block sums bit for bit.  GGUF layout only. */

@@ -145,6 +145,27 @@ def matvec(base, m, xs, out=None, r0=0, r1=None, stream=None):
     return out
 
 
+def matvec_scratch(base, m, xs, out=None, r0=0, r1=None, scratch=None, stream=None):
+    """matvec for either layout, Q8_K images in caller scratch (a uint8 CUDA
+    tensor of at least sg_matvec_scratch_bytes bytes; allocated if None)."""
+    single = xs.dim() == 1
+    xs2 = xs.reshape(1, -1) if single else xs
+    if xs2.dtype != torch.float32 or xs2.stride(-1) != 1:
+        raise ValueError("xs must be float32 with contiguous rows")
+    r1 = m.rows if r1 is None else r1
+    if out is None:
+        out = torch.empty((xs2.shape[0], m.rows), dtype=torch.float32, device=xs2.device)
+    out2 = out.reshape(1, -1) if out.dim() == 1 else out
+    need = lib().sg_matvec_scratch_bytes(m.cols, xs2.shape[0])
+    if scratch is None:
+        scratch = torch.empty(need, dtype=torch.uint8, device=xs2.device)
+    _lib.check(lib().sg_matvec_scratch(C.c_void_p(base.data_ptr()), C.byref(m.c()), C.c_void_p(xs2.data_ptr()),
+                                       xs2.stride(0), C.c_void_p(out2.data_ptr()), out2.stride(0), xs2.shape[0], r0,
+                                       r1, C.c_void_p(scratch.data_ptr()), scratch.numel(), _stream(stream)),
+               "matvec_scratch")
+    return out
+
+
 def gemv(base, m, xq, stream=None):
     """All rows for a list of Q8K vectors -> float32 CUDA [n_vec, rows]."""
     out = torch.empty((len(xq), m.rows), dtype=torch.float32, device=base.device)

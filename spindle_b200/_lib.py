@@ -53,6 +53,8 @@ SIGNATURES = {
     "sg_q8k_quantize": (I32, [P, U64, U64, U64, C.POINTER(SgQ8K), P]),
     "sg_matmul_rows": (I32, [P, C.POINTER(SgMat), C.POINTER(SgQ8K), C.POINTER(P), U64, U64, U64, P]),
     "sg_matvec": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
+    "sg_matvec_scratch_bytes": (U64, [U64, U64]),
+    "sg_matvec_scratch": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P, U64, P]),
     "sg_block_sums": (I32, [P, C.POINTER(SgMat), C.POINTER(SgQ8K), P, U64, U64, P]),
     "sg_quantize_weights": (I32, [I32, P, U64, U64, P, P]),
     "sg_tiled16_bytes": (I32, [I32, U64, U64, C.POINTER(U64)]),

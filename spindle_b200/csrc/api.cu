@@ -334,8 +334,10 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, bool qx, TPla
     if (occ < 1) occ = 1;
     p->warps = warps;
     const uint32_t groups = warps / p->S;
+    // every SM pulls its share of the weights: launch a full wave even when
+    // some groups get no tile (tiles go to CTAs round-robin)
     const uint32_t need = (ntiles + groups - 1) / groups, cap = (uint32_t)(di->sms * occ);
-    p->grid = need < cap ? need : cap;
+    p->grid = need < (uint32_t)di->sms ? (ntiles < (uint32_t)di->sms ? ntiles : (uint32_t)di->sms) : (need < cap ? need : cap);
     std::lock_guard<std::mutex> lk(g_mu);
     if (g_tplans.size() > 4096) g_tplans.clear();
     g_tplans.emplace(key, *p);
@@ -663,6 +665,33 @@ sg_status sg_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x, ui
         st = launch_tiled(d_base + m->offset, dt, (uint32_t)(m->cols / 256), nullptr, d_x + g * ldx, ldx, outs, nv, r0,
                           r1, (cudaStream_t)stream);
         if (st) return st;
+    }
+    return SG_OK;
+}
+
+uint64_t sg_matvec_scratch_bytes(uint64_t cols, uint64_t n_vec) { return n_vec * sg_q8k_bytes(cols); }
+
+sg_status sg_matvec_scratch(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
+                            uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, void *d_scratch,
+                            uint64_t scratch_bytes, void *stream) {
+    int dt;
+    sg_status st = check_mat(d_base, m, r0, r1, &dt);
+    if (st) return st;
+    if (r1 == r0 || n_vec == 0) return SG_OK;
+    if (!d_x || !d_out || !d_scratch || (n_vec > 1 && (ldx < m->cols || ldo < m->rows))) return SG_ERR_INVALID;
+    if (scratch_bytes < sg_matvec_scratch_bytes(m->cols, n_vec)) return SG_ERR_INVALID;
+    if (!aligned(d_scratch, 16)) return SG_ERR_ALIGN;
+    const uint64_t qb = sg_q8k_bytes(m->cols);
+    for (uint64_t g = 0; g < n_vec; g += Q8K_MAXV) {
+        const uint64_t nv = n_vec - g < Q8K_MAXV ? n_vec - g : Q8K_MAXV;
+        sg_q8k q[Q8K_MAXV];
+        float *outs[Q8K_MAXV];
+        for (uint64_t v = 0; v < nv; v++) {
+            if ((st = sg_q8k_view((uint8_t *)d_scratch + (g + v) * qb, m->cols, &q[v]))) return st;
+            outs[v] = d_out + (g + v) * ldo;
+        }
+        if ((st = sg_q8k_quantize(d_x + g * ldx, m->cols, nv, ldx, q, stream))) return st;
+        if ((st = launch_gemv(d_base, m, q, outs, nv, r0, r1, nullptr, (cudaStream_t)stream))) return st;
     }
     return SG_OK;
 }

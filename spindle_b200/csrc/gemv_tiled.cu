@@ -191,7 +191,8 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                       group * (S - 1) * worker_floats;
     const uint32_t b_lo = a.nb * slot / S, nblk = a.nb * (slot + 1) / S - b_lo;
     const uint32_t bc = a.bc, nchunk = (nblk + bc - 1) / bc;  // stages per tile for this slot
-    const uint32_t gid = blockIdx.x * G + group, GW = gridDim.x * G;
+    // groups are numbered CTA-minor so that consecutive tiles land on different SMs
+    const uint32_t gid = group * gridDim.x + blockIdx.x, GW = gridDim.x * G;
     const uint32_t my_tiles = gid < a.ntiles ? (a.ntiles - gid + GW - 1) / GW : 0u;
     const uint32_t nitems = my_tiles * nchunk;
     const uint64_t tile_bytes = (uint64_t)a.nb * CB;

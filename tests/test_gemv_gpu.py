@@ -220,3 +220,22 @@ def test_bad_arguments_raise(dev):
     with pytest.raises(sg.SgError):
         sg.matmul_rows(w, sg.Mat(sg.Q4_K, 1024, 1), [q], [out], 0, 2)  # r1 > rows
     sg.device_status()
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
+def test_matvec_scratch_both_layouts(dev, dt):
+    # Quantize into caller scratch + integer GEMV, GGUF rows and TILED16.
+    for n, rows, nvec in [(768, 37, 1), (4096, 45, 5), (14336, 20, 2)]:
+        rng = O.Rng(3 * n + rows)
+        w = O.random_matrix(dt, n, rows, rng)
+        xs = np.stack([rng.fill(-2.0, 2.0, n) for _ in range(nvec)])
+        want = O.gemv_int(w, O.Mat(dt, n, rows), [O.quantize(x) for x in xs])
+        wd = to_dev(w, dev)
+        xd = to_dev(xs, dev)
+        got = sg.matvec_scratch(wd, sg.Mat(dt, n, rows), xd)
+        assert np.array_equal(bits(got), bits(want))
+        t, m = sg.repack_tiled16(dt, wd, rows, n)
+        assert np.array_equal(bits(sg.matvec_scratch(t, m, xd)), bits(want))
+        small = torch.empty(16, dtype=torch.uint8, device=dev)
+        with pytest.raises(sg.SgError):
+            sg.matvec_scratch(wd, sg.Mat(dt, n, rows), xd, scratch=small)
