@@ -45,6 +45,7 @@ typedef int32_t sg_status;
 #define SG_ERR_NCCL 6
 #define SG_ERR_TIMEOUT 7   /* a bounded device-side wait gave up */
 #define SG_ERR_NOMEM 8
+#define SG_ERR_NOALLOC_LIMIT 9 /* request larger than the static scratch of sg_matvec_static */
 
 /* GGML type ids (gguf_loader.rs:25-65). */
 #define SG_F32 0
@@ -158,6 +159,20 @@ SG_API uint64_t sg_matvec_scratch_bytes(uint64_t cols, uint64_t n_vec);
 SG_API sg_status sg_matvec_scratch(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx,
                                    float *d_out, uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1,
                                    void *d_scratch, uint64_t scratch_bytes, void *stream);
+
+/* sg_matvec_scratch for callers that cannot allocate device memory (hosts
+ * without their own CUDA allocator, or paths where a cudaMalloc would stall
+ * the device).  No counterpart in the reference, whose scratch is ordinary
+ * thread-local heap memory.  The Q8_K scratch is a static device array of
+ * SG_NOALLOC_SCRATCH_BYTES bytes inside the library: requests needing more
+ * (sg_matvec_scratch_bytes(cols, n_vec)) return SG_ERR_NOALLOC_LIMIT; it
+ * allocates nothing.  The first call on a device looks the array up (make it
+ * before any stream capture); all calls share the array, so calls that
+ * overlap on the GPU race and must be serialized by the caller. */
+#define SG_NOALLOC_SCRATCH_BYTES 262144
+SG_API sg_status sg_matvec_static(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx,
+                                  float *d_out, uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1,
+                                  void *stream);
 
 /* The int32 lane sums of rows<B,T> (quant_q8k.rs:235-242) for one vector, as
  * the kernel computes them: d_out[(r-r0)*nb*8 + i*8 + l] = lane l of block i

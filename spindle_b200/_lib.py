@@ -12,7 +12,7 @@ LIB_PATH = os.environ.get("SG_LIB_PATH") or os.path.join(HERE, "libspindle_b200.
 OK = 0
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported dtype", 3: "unsupported shape",
           4: "misaligned device pointer", 5: "CUDA error", 6: "NCCL error", 7: "device wait timed out",
-          8: "out of memory"}
+          8: "out of memory", 9: "request above the static scratch limit"}
 
 
 class SgError(RuntimeError):
@@ -55,6 +55,7 @@ SIGNATURES = {
     "sg_matvec": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
     "sg_matvec_scratch_bytes": (U64, [U64, U64]),
     "sg_matvec_scratch": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P, U64, P]),
+    "sg_matvec_static": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
     "sg_block_sums": (I32, [P, C.POINTER(SgMat), C.POINTER(SgQ8K), P, U64, U64, P]),
     "sg_quantize_weights": (I32, [I32, P, U64, U64, P, P]),
     "sg_tiled16_bytes": (I32, [I32, U64, U64, C.POINTER(U64)]),

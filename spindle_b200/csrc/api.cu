@@ -451,6 +451,7 @@ const char *sg_status_string(sg_status s) {
     case SG_ERR_NCCL: return "NCCL error";
     case SG_ERR_TIMEOUT: return "device wait timed out";
     case SG_ERR_NOMEM: return "out of memory";
+    case SG_ERR_NOALLOC_LIMIT: return "request above the static scratch limit";
     default: return "unknown status";
     }
 }
