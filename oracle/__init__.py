@@ -225,3 +225,66 @@ def quantize_weights(dtype, w):
     else:
         raise ValueError("quantize_weights: dtype %d" % dtype)
     return out
+
+
+class Moe(C.Structure):
+    """`Moe` of smollm_chat.rs:152-169 (without residency): router and expert-0 views."""
+    _fields_ = [("router", Mat), ("gate", Mat), ("up", Mat), ("down", Mat), ("n_expert", C.c_uint32),
+                ("n_used", C.c_uint32), ("norm", C.c_int32), ("moe_prune", C.c_float), ("has_shared", C.c_int32),
+                ("has_shared_gate", C.c_int32), ("sh_gate", Mat), ("sh_up", Mat), ("sh_down", Mat),
+                ("shared_gate_offset", C.c_uint64)]
+
+
+def _moe_sigs():
+    L = lib()
+    if not hasattr(L, "_moe_ready"):
+        P, S = C.c_void_p, C.c_size_t
+        L.or_moe_forward.restype = C.c_int
+        L.or_moe_forward.argtypes = [P, C.POINTER(Moe), P, P, C.c_int, P, P, C.POINTER(C.c_uint32)]
+        L.or_moe_route.restype = C.c_int
+        L.or_moe_route.argtypes = [P, C.POINTER(Moe), P, P, P, P, C.POINTER(C.c_uint32)]
+        L.or_ffns_fused.restype = C.c_int
+        L.or_ffns_fused.argtypes = [P, P, P, P, P, S, P, P, C.c_int]
+        L._moe_ready = True
+    return L
+
+
+def moe_forward(buf, moe, x, int_on=True):
+    """moe_forward (smollm_chat.rs:1178-1392): returns (out, chosen experts, weights)."""
+    L = _moe_sigs()
+    buf = np.ascontiguousarray(buf, np.uint8)
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(moe.down.rows, np.float32)
+    chosen = np.empty(moe.n_used, np.int32)
+    ws = np.empty(moe.n_used, np.float32)
+    n = C.c_uint32()
+    if L.or_moe_forward(_p(buf), C.byref(moe), _p(x), _p(out), int(int_on), _p(chosen), _p(ws), C.byref(n)):
+        raise RuntimeError("moe_forward failed")
+    return out, chosen[:n.value].copy(), ws[:n.value].copy()
+
+
+def moe_route(buf, moe, x):
+    """Router + softmax + top-k + prune: (probs, chosen, weights)."""
+    L = _moe_sigs()
+    buf = np.ascontiguousarray(buf, np.uint8)
+    x = np.ascontiguousarray(x, np.float32)
+    probs = np.empty(moe.n_expert, np.float32)
+    chosen = np.empty(moe.n_used, np.int32)
+    ws = np.empty(moe.n_used, np.float32)
+    n = C.c_uint32()
+    if L.or_moe_route(_p(buf), C.byref(moe), _p(x), _p(probs), _p(chosen), _p(ws), C.byref(n)):
+        raise RuntimeError("moe_route failed")
+    return probs, chosen[:n.value].copy(), ws[:n.value].copy()
+
+
+def ffns_fused(buf, gates, ups, downs, weights, x, out, int_on=True):
+    """ffns_fused (smollm_chat.rs:382-442): out += sum_e w_e * FFN_e(x), in order."""
+    L = _moe_sigs()
+    k = len(gates)
+    arr = lambda ms: (Mat * k)(*ms)
+    w = np.ascontiguousarray(weights, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    if L.or_ffns_fused(_p(np.ascontiguousarray(buf, np.uint8)), arr(gates), arr(ups), arr(downs), _p(w), k, _p(x),
+                       _p(out), int(int_on)):
+        raise RuntimeError("ffns_fused failed")
+    return out

@@ -87,6 +87,26 @@ int or_matmul_rows_multi(const uint8_t *base, const or_mat *m, size_t n_vec,
                          const float *const *xs, float *const *outs,
                          size_t r0, size_t r1);
 
+/* ---- FFN / MoE layer (smollm_chat.rs:382-442, :1178-1392) ---- */
+typedef struct {
+    or_mat router;           /* F32, rows = n_expert, cols = dim */
+    or_mat gate, up, down;   /* expert 0; expert e starts e * rows * row_bytes later */
+    uint32_t n_expert, n_used;
+    int32_t norm;
+    float moe_prune;
+    int32_t has_shared, has_shared_gate;
+    or_mat sh_gate, sh_up, sh_down;
+    uint64_t shared_gate_offset; /* F32[dim] */
+} or_moe;
+int or_ffns_fused(const uint8_t *base, const or_mat *gate, const or_mat *up, const or_mat *down,
+                  const float *weights, size_t k, const float *x, float *out, int int_on);
+/* Router, softmax, top-k and prune: probs[n_expert], then the chosen experts
+ * in order with their weights. */
+int or_moe_route(const uint8_t *base, const or_moe *m, const float *x, float *probs, int32_t *chosen,
+                 float *weights, uint32_t *n_chosen);
+int or_moe_forward(const uint8_t *base, const or_moe *m, const float *x, float *out, int int_on,
+                   int32_t *chosen_out, float *weights_out, uint32_t *n_chosen_out);
+
 /* ---- worker pool (worker_pool.rs:38-139, smollm_chat.rs:309-349) ---- */
 /* matvec / matvec_multi on the integer kernels with the reference's row split
  * [R*t/T, R*(t+1)/T) over n_threads persistent spinning workers.  xs is
