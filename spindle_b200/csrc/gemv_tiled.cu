@@ -1,166 +1,9 @@
 // gemv_tiled.cu — kernels over the TILED16 layout (see gemv_tiled.cuh).
-#include "gemv_tiled.cuh"
 #include "q8k_block.cuh"
+#include "tiled_block.cuh"
 
 namespace sg {
-
-namespace {
-
-constexpr uint32_t M4 = 0x0F0F0F0Fu, B45 = 0x30303030u;
-
-__device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
-__device__ __forceinline__ uint32_t w4(const uint4 &v, int m) { return m == 0 ? v.x : m == 1 ? v.y : m == 2 ? v.z : v.w; }
-__device__ __forceinline__ int sbyte(uint32_t w, int b) { return (int)(int8_t)(w >> (8 * b)); }
-__device__ __forceinline__ int ubyte(uint32_t w, int b) { return (int)((w >> (8 * b)) & 0xFFu); }
-__device__ __forceinline__ float h2f_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
-__device__ __forceinline__ float h2f_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
-
-// float(s), exact.  Q4_K lane sums satisfy |s| < 2^22, so 1.5*2^23 + s is an
-// exact float whose bits are 0x4B400000 + s; subtracting 1.5*2^23 is exact
-// too (two ALU/FMA ops instead of a conversion).  Q6_K sums can reach 2^25 and
-// use the rounding conversion.
-template <int DT>
-__device__ __forceinline__ float lane_f(int s) {
-    if constexpr (DT == 0) return __fsub_rn(__int_as_float(0x4B400000 + s), 12582912.0f);
-    return __int2float_rn(s);
-}
-
-// TILED16 stores each row's quant bytes in 16-byte chunks permuted by row so
-// that the 8 rows an LDS.128 phase reads fall in 8 different bank groups:
-//   Q4_K qs (8 chunks/row):    chunk c at c ^ (r & 7)
-//   Q6_K qlqh (12 chunks/row): chunk c at (c & ~3) | ((c ^ (r >> 1)) & 3)
-__host__ __device__ __forceinline__ uint32_t q4k_chunk(uint32_t c, uint32_t r) { return c ^ (r & 7u); }
-__host__ __device__ __forceinline__ uint32_t q6k_chunk(uint32_t c, uint32_t r) {
-    return (c & ~3u) | ((c ^ (r >> 1)) & 3u);
-}
-
-// Programmatic dependent launch: wait for the grids this one depends on
-// (no-op when launched without the attribute), and let dependents launch.
-__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
-
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-}  // namespace
-
-namespace {
-
-__device__ __forceinline__ void named_sync(uint32_t id, uint32_t n) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-__device__ __forceinline__ void named_arrive(uint32_t id, uint32_t n) {
-    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-
-// One super-block of one 16-row tile for lanes 4g..4g+3 of row r: the exact
-// int32 lane sums s, d*xd (cd) and the correction term (ct) per vector.
-template <int NV>
-__device__ __forceinline__ void block_q4k(const uint8_t *col, uint32_t g, uint32_t r, uint32_t i,
-                                          const TGemvArgs &a, const uint8_t *act, uint32_t act_stride,
-                                          int (&s)[NV][4], float (&cd)[NV], float (&ct)[NV]) {
-    const uint4 hd = lds128(col + 2048 + 16 * r);
-    const float d = h2f_lo(hd.x), dmin = h2f_hi(hd.x);
-    const uint32_t sclo = hd.y & 0x3F3F3F3Fu, schi = (hd.w & M4) | ((hd.y >> 2) & B45);
-    const uint32_t mnw = g ? (((hd.w >> 4) & M4) | ((hd.z >> 2) & B45)) : (hd.z & 0x3F3F3F3Fu);
-    const int sc[8] = {ubyte(sclo, 0), ubyte(sclo, 1), ubyte(sclo, 2), ubyte(sclo, 3),
-                       ubyte(schi, 0), ubyte(schi, 1), ubyte(schi, 2), ubyte(schi, 3)};
-    uint32_t lo[4][4], hi[4][4];
-#pragma unroll
-    for (int cc = 0; cc < 4; cc++) {
-        const uint4 qv = lds128(col + 128 * r + 16 * q4k_chunk(2 * cc + g, r));
-#pragma unroll
-        for (int m = 0; m < 4; m++) {
-            lo[cc][m] = w4(qv, m) & M4;
-            hi[cc][m] = (w4(qv, m) >> 4) & M4;
-        }
-    }
-#pragma unroll
-    for (int v = 0; v < NV; v++) {
-        if (v >= (int)a.nvec) break;
-        const uint8_t *av = act + v * act_stride;
-        const uint8_t *y = av + 256u * i + 16u * g;
-        uint4 Y[8];
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) Y[kk] = lds128(y + 32 * kk);
-        const uint4 B = lds128(av + 256u * a.nb + 32u * i + 16u * g);
-        const float xd = *reinterpret_cast<const float *>(av + 288u * a.nb + 4u * i);
-#pragma unroll
-        for (int m = 0; m < 4; m++) s[v][m] = 0;
-#pragma unroll
-        for (int cc = 0; cc < 4; cc++)
-#pragma unroll
-            for (int m = 0; m < 4; m++) {
-                s[v][m] += sc[2 * cc] * __dp4a((int)lo[cc][m], (int)w4(Y[2 * cc], m), 0);
-                s[v][m] += sc[2 * cc + 1] * __dp4a((int)hi[cc][m], (int)w4(Y[2 * cc + 1], m), 0);
-            }
-        cd[v] = __fmul_rn(d, xd);
-        // mins: sum over sub-blocks j = 4g..4g+3 of mn_j * (bsums[2j] + bsums[2j+1]),
-        // one dp2a per pair with mn_j in both low bytes
-        int sp = 0;
-#pragma unroll
-        for (int m = 0; m < 4; m++) sp = __dp2a_lo((int)w4(B, m), (int)__byte_perm(mnw, 0, 0x11 * m), sp);
-        sp += __shfl_xor_sync(0xffffffffu, sp, 16);
-        ct[v] = __fmul_rn(__fmul_rn(dmin, xd), __int2float_rn(sp));
-    }
-}
-
-template <int NV>
-__device__ __forceinline__ void block_q6k(const uint8_t *col, uint32_t g, uint32_t r, uint32_t i,
-                                          const TGemvArgs &a, const uint8_t *act, uint32_t act_stride,
-                                          int (&s)[NV][4], float (&cd)[NV], float (&ct)[NV]) {
-    const uint8_t *qrow = col + 192 * r;
-    uint32_t w[8][4];
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const uint4 L0 = lds128(qrow + 16 * q6k_chunk(4 * h + g, r));
-        const uint4 L1 = lds128(qrow + 16 * q6k_chunk(4 * h + 2 + g, r));
-        const uint4 H = lds128(qrow + 16 * q6k_chunk(8 + 2 * h + g, r));
-#pragma unroll
-        for (int m = 0; m < 4; m++) {
-            const uint32_t l0 = w4(L0, m), l1 = w4(L1, m), hh = w4(H, m);
-            w[4 * h + 0][m] = (l0 & M4) | ((hh << 4) & B45);
-            w[4 * h + 1][m] = (l1 & M4) | ((hh << 2) & B45);
-            w[4 * h + 2][m] = ((l0 >> 4) & M4) | (hh & B45);
-            w[4 * h + 3][m] = ((l1 >> 4) & M4) | ((hh >> 2) & B45);
-        }
-    }
-    const uint4 SC = lds128(col + 3072 + 16 * r);
-    const float d = __half2float(*reinterpret_cast<const __half *>(col + 3328 + 2 * r));
-    // chunk 4h+k of lanes 4g..4g+3 uses scale 8h + 2k + g
-    int scv[8];
-#pragma unroll
-    for (int h = 0; h < 2; h++)
-#pragma unroll
-        for (int kk = 0; kk < 4; kk++) scv[4 * h + kk] = sbyte(w4(SC, 2 * h + (kk >> 1)), 2 * (kk & 1) + (int)g);
-#pragma unroll
-    for (int v = 0; v < NV; v++) {
-        if (v >= (int)a.nvec) break;
-        const uint8_t *av = act + v * act_stride;
-        const uint8_t *y = av + 256u * i + 16u * g;
-        uint4 Y[8];
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) Y[kk] = lds128(y + 32 * kk);
-        const uint4 B = lds128(av + 256u * a.nb + 32u * i + 16u * g);
-        const float xd = *reinterpret_cast<const float *>(av + 288u * a.nb + 4u * i);
-#pragma unroll
-        for (int m = 0; m < 4; m++) s[v][m] = 0;
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++)
-#pragma unroll
-            for (int m = 0; m < 4; m++) s[v][m] += scv[kk] * __dp4a((int)w[kk][m], (int)w4(Y[kk], m), 0);
-        cd[v] = __fmul_rn(d, xd);
-        // offset: sum over groups 8g..8g+7 of sc * bsums, one dp2a per pair
-        const uint32_t sw0 = g ? SC.z : SC.x, sw1 = g ? SC.w : SC.y;
-        int sp = __dp2a_lo((int)B.x, (int)sw0, 0);
-        sp = __dp2a_hi((int)B.y, (int)sw0, sp);
-        sp = __dp2a_lo((int)B.z, (int)sw1, sp);
-        sp = __dp2a_hi((int)B.w, (int)sw1, sp);
-        sp += __shfl_xor_sync(0xffffffffu, sp, 16);
-        ct[v] = __fmul_rn(cd[v], __int2float_rn(32 * sp));
-    }
-}
-
-}  // namespace
+using namespace tiled;
 
 template <int DT, int NV, bool QX>
 __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const __grid_constant__ TGemvArgs a) {
@@ -275,9 +118,9 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                 int s[NV][4];
                 float cd[NV], ct[NV];
                 if constexpr (DT == 0)
-                    block_q4k<NV>(col, g, r, i, a, act, astride, s, cd, ct);
+                    block_q4k<NV>(col, g, r, i, a.nvec, a.nb, act, astride, s, cd, ct);
                 else
-                    block_q6k<NV>(col, g, r, i, a, act, astride, s, cd, ct);
+                    block_q6k<NV>(col, g, r, i, a.nvec, a.nb, act, astride, s, cd, ct);
 #pragma unroll
                 for (int v = 0; v < NV; v++) {
                     if (v >= (int)a.nvec) break;
