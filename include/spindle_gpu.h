@@ -180,6 +180,67 @@ SG_API sg_status sg_matvec_static(const uint8_t *d_base, const sg_mat *m, const 
 SG_API sg_status sg_block_sums(const uint8_t *d_base, const sg_mat *m, const sg_q8k *xq,
                         int32_t *d_out, uint64_t r0, uint64_t r1, void *stream);
 
+/* ---- MoE layer (smollm_chat.rs:1178-1382, moe_forward with the fused expert
+ * FFNs of ffns_fused, :382-442) ------------------------------------------------
+ *
+ * One token through a top-k MoE feed-forward layer, with the expert choice kept
+ * on the device (no host round trip between router and experts):
+ *   logits = router x (F32 rows, the float path's lane order);
+ *   p = softmax(logits); top n_used by p (descending; equal p: lower index
+ *   first); pruned by moe_prune; weight_i = norm ? p_i / sum(kept p) : p_i;
+ *   out = sum_i weight_i * down_i(silu(gate_i x) * up_i x), in router order,
+ *   plus the shared expert (times sigmoid(shared_gate . x) when given).
+ * The expert matrices run on the integer path: x and each h are quantized to
+ * Q8_K exactly as the reference does (dim and n_ff multiples of 256). */
+#define SG_MOE_MAX_USED 16
+
+/* The router's choice (device memory, written by sg_moe_forward). */
+typedef struct {
+    uint32_t n;                       /* experts kept after pruning */
+    uint32_t pad_[3];
+    int32_t id[SG_MOE_MAX_USED];      /* router order */
+    float weight[SG_MOE_MAX_USED];
+} sg_moe_choice;
+
+/* Device weights of one MoE layer (struct Moe, smollm_chat.rs:152-167).
+ * Expert e's gate and up (n_ff rows each, dim cols) are stacked as one TILED16
+ * matrix [gate_e; up_e] at gate_up + e * gate_up_stride; its down (dim rows,
+ * n_ff cols) is TILED16 at down + e * down_stride.  sg_moe_pack_gate_up and
+ * sg_moe_pack_down build both from the GGUF expert tensors; the strides are
+ * sg_tiled16_bytes(dtype, 2 * n_ff, dim) and sg_tiled16_bytes(dtype, dim, n_ff). */
+typedef struct {
+    const float *router;              /* F32 [n_expert][dim] (ffn_gate_inp) */
+    const uint8_t *gate_up;
+    const uint8_t *down;
+    int32_t gate_up_dtype, down_dtype;    /* SG_Q4_K or SG_Q6_K */
+    uint64_t gate_up_stride, down_stride;
+    uint64_t dim, n_ff, n_expert, n_used;
+    int32_t norm;                     /* expert_norm */
+    float moe_prune;                  /* 0 = off; (0,1) = keep mass 1-prune; >= 1 = keep that many */
+    /* Shared expert (Qwen2-MoE): NULL shared_gate_up = none. */
+    const uint8_t *shared_gate_up;    /* TILED16 [gate; up], 2 * shared_n_ff rows */
+    const uint8_t *shared_down;       /* TILED16, dim rows x shared_n_ff cols */
+    int32_t shared_gate_up_dtype, shared_down_dtype;
+    uint64_t shared_n_ff;
+    const float *shared_gate;         /* F32 [dim] (ffn_gate_inp_shexp) or NULL */
+} sg_moe;
+
+/* Repack the GGUF expert tensors ffn_gate_exps and ffn_up_exps ([n_expert]
+ * matrices of n_ff x dim, same dtype) into the stacked TILED16 form above. */
+SG_API sg_status sg_moe_pack_gate_up(int32_t dtype, const uint8_t *d_gate_exps, const uint8_t *d_up_exps,
+                                     uint64_t n_expert, uint64_t n_ff, uint64_t dim, uint8_t *d_out, void *stream);
+/* Repack ffn_down_exps ([n_expert] matrices of dim x n_ff) into TILED16 per expert. */
+SG_API sg_status sg_moe_pack_down(int32_t dtype, const uint8_t *d_down_exps, uint64_t n_expert, uint64_t dim,
+                                  uint64_t n_ff, uint8_t *d_out, void *stream);
+/* Device scratch that sg_moe_forward needs for this layer (0 for an invalid m). */
+SG_API uint64_t sg_moe_scratch_bytes(const sg_moe *m);
+/* out[dim] = moe_forward(x[dim]) (smollm_chat.rs:1178).  d_scratch: at least
+ * sg_moe_scratch_bytes(m) bytes, 256-byte aligned, not shared with a call that
+ * may overlap on the GPU.  d_choice and d_probs (float[n_expert], the softmax
+ * probabilities) are optional outputs.  Four kernel launches, no host sync. */
+SG_API sg_status sg_moe_forward(const sg_moe *m, const float *d_x, float *d_out, void *d_scratch,
+                                uint64_t scratch_bytes, sg_moe_choice *d_choice, float *d_probs, void *stream);
+
 /* ---- weight quantizer (no reference counterpart: its tests use random bytes)
  * f32 [rows, cols] -> Q4_K or Q6_K rows, deterministic; cols % 256 == 0. */
 SG_API sg_status sg_quantize_weights(int32_t dtype, const float *d_w, uint64_t rows, uint64_t cols,

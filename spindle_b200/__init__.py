@@ -216,3 +216,93 @@ def unpack_tiled16(dtype, t, rows, cols, stream=None):
 def device_status():
     """Raises SgError if a bounded device wait gave up since the last check."""
     _lib.check(lib().sg_device_status(), "device status")
+
+
+# ---- MoE layer (smollm_chat.rs:1178-1382 moe_forward, with ffns_fused :382-442)
+
+MOE_MAX_USED = _lib.MOE_MAX_USED
+
+
+class Moe:
+    """Device weights of one MoE layer (smollm_chat.rs:152-167 `Moe`).
+
+    Built by `Moe.pack` from the GGUF expert tensors (uint8 CUDA buffers of
+    GGUF rows: ffn_gate_exps / ffn_up_exps [n_expert][n_ff][dim], ffn_down_exps
+    [n_expert][dim][n_ff]) and the F32 router [n_expert][dim].  The tensors the
+    layer holds stay referenced by this object for as long as it lives."""
+
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+    @classmethod
+    def pack(cls, router, gate_exps, up_exps, down_exps, gate_up_dtype, down_dtype, n_expert, n_used, dim, n_ff,
+             norm=True, moe_prune=0.0, shared=None, shared_gate=None, stream=None):
+        """shared: optional (gate, up, down, gate_up_dtype, down_dtype, n_ff) of GGUF
+        rows (one expert); shared_gate: optional F32 [dim] CUDA tensor."""
+        dev = router.device
+        gu_stride = tiled16_bytes(gate_up_dtype, 2 * n_ff, dim)
+        dn_stride = tiled16_bytes(down_dtype, dim, n_ff)
+        gu = torch.empty(gu_stride * n_expert, dtype=torch.uint8, device=dev)
+        dn = torch.empty(dn_stride * n_expert, dtype=torch.uint8, device=dev)
+        s = _stream(stream)
+        _lib.check(lib().sg_moe_pack_gate_up(gate_up_dtype, C.c_void_p(gate_exps.data_ptr()),
+                                             C.c_void_p(up_exps.data_ptr()), n_expert, n_ff, dim,
+                                             C.c_void_p(gu.data_ptr()), s), "moe_pack_gate_up")
+        _lib.check(lib().sg_moe_pack_down(down_dtype, C.c_void_p(down_exps.data_ptr()), n_expert, dim, n_ff,
+                                          C.c_void_p(dn.data_ptr()), s), "moe_pack_down")
+        m = cls(router=router.contiguous(), gate_up=gu, down=dn, gate_up_dtype=gate_up_dtype,
+                down_dtype=down_dtype, gate_up_stride=gu_stride, down_stride=dn_stride, dim=dim, n_ff=n_ff,
+                n_expert=n_expert, n_used=n_used, norm=bool(norm), moe_prune=float(moe_prune),
+                shared_gate_up=None, shared_down=None, shared_gate_up_dtype=0, shared_down_dtype=0,
+                shared_n_ff=0, shared_gate=None)
+        if shared is not None:
+            sg_, su, sd, sgu_dt, sd_dt, sh_ff = shared
+            sgu = torch.empty(tiled16_bytes(sgu_dt, 2 * sh_ff, dim), dtype=torch.uint8, device=dev)
+            sdn = torch.empty(tiled16_bytes(sd_dt, dim, sh_ff), dtype=torch.uint8, device=dev)
+            _lib.check(lib().sg_moe_pack_gate_up(sgu_dt, C.c_void_p(sg_.data_ptr()), C.c_void_p(su.data_ptr()), 1,
+                                                 sh_ff, dim, C.c_void_p(sgu.data_ptr()), s), "moe_pack_gate_up")
+            _lib.check(lib().sg_moe_pack_down(sd_dt, C.c_void_p(sd.data_ptr()), 1, dim, sh_ff,
+                                              C.c_void_p(sdn.data_ptr()), s), "moe_pack_down")
+            m.shared_gate_up, m.shared_down = sgu, sdn
+            m.shared_gate_up_dtype, m.shared_down_dtype, m.shared_n_ff = sgu_dt, sd_dt, sh_ff
+            m.shared_gate = None if shared_gate is None else shared_gate.contiguous()
+        return m
+
+    def c(self):
+        ptr = lambda t: None if t is None else t.data_ptr()
+        return _lib.SgMoe(ptr(self.router), ptr(self.gate_up), ptr(self.down), self.gate_up_dtype, self.down_dtype,
+                          self.gate_up_stride, self.down_stride, self.dim, self.n_ff, self.n_expert, self.n_used,
+                          int(self.norm), self.moe_prune, ptr(self.shared_gate_up), ptr(self.shared_down),
+                          self.shared_gate_up_dtype, self.shared_down_dtype, self.shared_n_ff,
+                          ptr(self.shared_gate))
+
+    def scratch_bytes(self):
+        n = lib().sg_moe_scratch_bytes(C.byref(self.c()))
+        if not n:
+            raise SgError(1, "moe_scratch_bytes")
+        return n
+
+
+def moe_forward(m, x, out=None, scratch=None, choice=None, probs=None, stream=None):
+    """out[dim] = moe_forward(x[dim]) (smollm_chat.rs:1178).  choice: optional
+    int32 CUDA tensor of 36 words receiving sg_moe_choice (n, pad, id[16],
+    weight bits[16]); probs: optional float32 [n_expert] for the softmax."""
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise ValueError("x must be contiguous float32")
+    if out is None:
+        out = torch.empty(m.dim, dtype=torch.float32, device=x.device)
+    if scratch is None:
+        scratch = torch.empty(m.scratch_bytes(), dtype=torch.uint8, device=x.device)
+    ptr = lambda t: None if t is None else C.c_void_p(t.data_ptr())
+    _lib.check(lib().sg_moe_forward(C.byref(m.c()), ptr(x), ptr(out), ptr(scratch), scratch.numel(), ptr(choice),
+                                    ptr(probs), _stream(stream)), "moe_forward")
+    return out
+
+
+def decode_choice(choice):
+    """(ids, weights) of the kept experts from a choice tensor filled by moe_forward."""
+    c = choice.cpu()
+    n = int(c[0])
+    ids = [int(v) for v in c[4:4 + n]]
+    w = c[4 + MOE_MAX_USED:4 + MOE_MAX_USED + n].view(torch.float32).tolist()
+    return ids, w

@@ -31,6 +31,25 @@ class SgQ8K(C.Structure):
     _fields_ = [("d", C.c_void_p), ("qs", C.c_void_p), ("bsums", C.c_void_p), ("n", C.c_uint64)]
 
 
+MOE_MAX_USED = 16
+
+
+class SgMoeChoice(C.Structure):
+    _fields_ = [("n", C.c_uint32), ("pad_", C.c_uint32 * 3), ("id", C.c_int32 * MOE_MAX_USED),
+                ("weight", C.c_float * MOE_MAX_USED)]
+
+
+class SgMoe(C.Structure):
+    _fields_ = [("router", C.c_void_p), ("gate_up", C.c_void_p), ("down", C.c_void_p),
+                ("gate_up_dtype", C.c_int32), ("down_dtype", C.c_int32),
+                ("gate_up_stride", C.c_uint64), ("down_stride", C.c_uint64),
+                ("dim", C.c_uint64), ("n_ff", C.c_uint64), ("n_expert", C.c_uint64), ("n_used", C.c_uint64),
+                ("norm", C.c_int32), ("moe_prune", C.c_float),
+                ("shared_gate_up", C.c_void_p), ("shared_down", C.c_void_p),
+                ("shared_gate_up_dtype", C.c_int32), ("shared_down_dtype", C.c_int32),
+                ("shared_n_ff", C.c_uint64), ("shared_gate", C.c_void_p)]
+
+
 P, U64, I32 = C.c_void_p, C.c_uint64, C.c_int32
 
 # name -> (restype, argtypes); every function the header declares.
@@ -61,6 +80,10 @@ SIGNATURES = {
     "sg_tiled16_bytes": (I32, [I32, U64, U64, C.POINTER(U64)]),
     "sg_repack_tiled16": (I32, [I32, P, U64, U64, P, P]),
     "sg_unpack_tiled16": (I32, [I32, P, U64, U64, P, P]),
+    "sg_moe_pack_gate_up": (I32, [I32, P, P, U64, U64, U64, P, P]),
+    "sg_moe_pack_down": (I32, [I32, P, U64, U64, U64, P, P]),
+    "sg_moe_scratch_bytes": (U64, [C.POINTER(SgMoe)]),
+    "sg_moe_forward": (I32, [C.POINTER(SgMoe), P, P, P, U64, P, P, P]),
 }
 
 _lib = None

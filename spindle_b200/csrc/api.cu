@@ -10,6 +10,7 @@
 #include "gemv_q8k.cuh"
 #include "gemv_tiled.cuh"
 #include "kernels.cuh"
+#include "moe.cuh"
 
 using namespace sg;
 
@@ -230,15 +231,27 @@ typedef void (*tgemv_fn)(const TGemvArgs);
 
 uint32_t tiled_nv_inst(int nv) { return nv <= 1 ? 1u : nv == 2 ? 2u : nv <= 4 ? 4u : 8u; }
 
-template <int DT, bool QX>
+template <int DT, int MODE>
 tgemv_fn pick_tiled_t(int nv) {
-    return nv == 1 ? gemv_tiled_kernel<DT, 1, QX> : nv == 2 ? gemv_tiled_kernel<DT, 2, QX>
-           : nv <= 4 ? gemv_tiled_kernel<DT, 4, QX> : gemv_tiled_kernel<DT, 8, QX>;
+    return nv == 1 ? gemv_tiled_kernel<DT, 1, MODE> : nv == 2 ? gemv_tiled_kernel<DT, 2, MODE>
+           : nv <= 4 ? gemv_tiled_kernel<DT, 4, MODE> : gemv_tiled_kernel<DT, 8, MODE>;
 }
 
-tgemv_fn pick_tiled(int dt, int nv, bool qx) {
-    if (dt == DT_Q4K) return qx ? pick_tiled_t<0, true>(nv) : pick_tiled_t<0, false>(nv);
-    return qx ? pick_tiled_t<1, true>(nv) : pick_tiled_t<1, false>(nv);
+tgemv_fn pick_tiled(int dt, int nv, int mode) {
+    if (dt == DT_Q4K) {
+        switch (mode) {
+        case IN_MOE_X: return gemv_tiled_kernel<0, 1, IN_MOE_X>;
+        case IN_MOE_H: return gemv_tiled_kernel<0, 1, IN_MOE_H>;
+        case IN_F32: return pick_tiled_t<0, IN_F32>(nv);
+        default: return pick_tiled_t<0, IN_Q8K>(nv);
+        }
+    }
+    switch (mode) {
+    case IN_MOE_X: return gemv_tiled_kernel<1, 1, IN_MOE_X>;
+    case IN_MOE_H: return gemv_tiled_kernel<1, 1, IN_MOE_H>;
+    case IN_F32: return pick_tiled_t<1, IN_F32>(nv);
+    default: return pick_tiled_t<1, IN_Q8K>(nv);
+    }
 }
 
 int env_int(const char *name, int dflt) {
@@ -257,11 +270,13 @@ std::unordered_map<uint64_t, TPlan> g_tplans;
 // Launch shape of the tiled GEMV: S warps per tile so that the whole GPU has
 // work (small row counts split each tile's super-blocks over more warps),
 // a 2-stage ring per warp, CTAs of 8 or 16 warps.
-sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, bool qx, TPlan *p) {
+// mode: IN_Q8K, IN_F32, IN_MOE_X or IN_MOE_H; max_slots: the MoE slots the
+// launch is sized for (ntiles counts all of them), 0 otherwise.
+sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uint32_t max_slots, TPlan *p) {
     int dev;
     CK(cudaGetDevice(&dev));
-    const uint64_t key = ((uint64_t)dev << 56) ^ ((uint64_t)qx << 55) ^ ((uint64_t)dt << 52) ^ ((uint64_t)nv << 44) ^
-                         ((uint64_t)nb << 32) ^ ntiles;
+    const uint64_t key = ((uint64_t)dev << 56) ^ ((uint64_t)mode << 53) ^ ((uint64_t)dt << 52) ^
+                         ((uint64_t)max_slots << 48) ^ ((uint64_t)nv << 44) ^ ((uint64_t)nb << 32) ^ ntiles;
     {
         std::lock_guard<std::mutex> lk(g_mu);
         auto it = g_tplans.find(key);
@@ -306,6 +321,8 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, bool qx, TPla
     uint32_t ns = (uint32_t)env_int("SG_TILED_STAGES", 2), bc = (uint32_t)env_int("SG_TILED_BC", 2);
     if (ns < 2) ns = 2;
     if (ns > 8) ns = 8;
+    // the MoE modes keep the router's choice at the top of the barrier area
+    if (mode >= IN_MOE_X && ns * warps * 8 > MOE_SEL_OFF) ns = MOE_SEL_OFF / (warps * 8);
     if (bc < 1) bc = 1;
     // Fit the CTA in shared memory: fewer stages, then smaller stages, then
     // fewer warps per tile (less chain scratch).
@@ -316,7 +333,8 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, bool qx, TPla
         p->bc = bc < p->slot_blocks ? bc : p->slot_blocks;
         p->nstages = ns;
         p->stage_bytes = p->bc * cb;
-        p->smem = tiled_smem_bytes(warps, S, ns, p->stage_bytes, p->slot_blocks, nv_inst, nb);
+        p->smem = tiled_smem_bytes(warps, S, ns, p->stage_bytes, p->slot_blocks, nv_inst, nb,
+                                   tiled_nact(mode, nv_inst, max_slots), tiled_extra(mode, warps));
         if (p->smem <= budget) break;
         if (ns > 2)
             ns--;
@@ -327,7 +345,7 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, bool qx, TPla
         else
             return SG_ERR_SHAPE;
     }
-    p->fn = pick_tiled(dt, nv, qx);
+    p->fn = pick_tiled(dt, nv, mode);
     CK(cudaFuncSetAttribute((const void *)p->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
     int occ = 0;
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, (const void *)p->fn, warps * 32, p->smem));
@@ -354,7 +372,8 @@ sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, 
         int nv = (int)(n_vec - g < TGEMV_MAXV ? n_vec - g : TGEMV_MAXV);
         TPlan p;
         sg_status st;
-        while ((st = tiled_plan(dt, nb, t1 - t0, nv, qx, &p)) == SG_ERR_SHAPE && nv > 1) nv = nv > 4 ? 4 : nv / 2;
+        while ((st = tiled_plan(dt, nb, t1 - t0, nv, qx ? IN_F32 : IN_Q8K, 0, &p)) == SG_ERR_SHAPE && nv > 1)
+            nv = nv > 4 ? 4 : nv / 2;
         if (st) return st;
         TGemvArgs a;
         memset(&a, 0, sizeof a);
@@ -431,6 +450,161 @@ sg_status launch_gemv(const uint8_t *d_base, const sg_mat *m, const sg_q8k *xq, 
         p.fn<<<p.grid, GEMV_THREADS, p.smem, stream>>>(a);
         CK(cudaGetLastError());
     }
+    return SG_OK;
+}
+
+// ---- MoE layer ---------------------------------------------------------------
+
+inline bool kquant(int32_t dt) { return dt == SG_Q4_K || dt == SG_Q6_K; }
+inline bool cols_ok(uint64_t c) { return c && c % 256 == 0 && c <= SG_MAX_COLS; }
+
+uint64_t tiled_bytes(int32_t dt, uint64_t rows, uint64_t cols) {
+    uint64_t b = 0;
+    return sg_tiled16_bytes(dt, rows, cols, &b) == SG_OK ? b : 0;
+}
+
+sg_status check_moe(const sg_moe *m) {
+    if (!m || !m->router || !m->gate_up || !m->down) return SG_ERR_INVALID;
+    if (!kquant(m->gate_up_dtype) || !kquant(m->down_dtype)) return SG_ERR_DTYPE;
+    if (!cols_ok(m->dim) || !cols_ok(m->n_ff)) return SG_ERR_SHAPE;
+    if (m->n_expert == 0 || m->n_expert > ROUTER_MAX_EXPERTS || m->n_used == 0 || m->n_used > m->n_expert)
+        return SG_ERR_INVALID;
+    if (m->n_used > SG_MOE_MAX_USED) return SG_ERR_SHAPE;
+    if (m->gate_up_stride < tiled_bytes(m->gate_up_dtype, 2 * m->n_ff, m->dim) ||
+        m->down_stride < tiled_bytes(m->down_dtype, m->dim, m->n_ff))
+        return SG_ERR_INVALID;
+    if (!aligned(m->router, 16) || !aligned(m->gate_up, 16) || !aligned(m->down, 16) || m->gate_up_stride % 16 ||
+        m->down_stride % 16)
+        return SG_ERR_ALIGN;
+    if (m->shared_gate_up) {
+        if (!m->shared_down) return SG_ERR_INVALID;
+        if (!kquant(m->shared_gate_up_dtype) || !kquant(m->shared_down_dtype)) return SG_ERR_DTYPE;
+        if (!cols_ok(m->shared_n_ff)) return SG_ERR_SHAPE;
+        if (!aligned(m->shared_gate_up, 16) || !aligned(m->shared_down, 16) || !aligned(m->shared_gate, 16))
+            return SG_ERR_ALIGN;
+    }
+    return SG_OK;
+}
+
+// Scratch of sg_moe_forward, each piece 256-byte aligned.
+struct MoeScratch {
+    uint64_t sel, shsel, scale, gu, y, gush, ysh, total;
+};
+
+MoeScratch moe_scratch(const sg_moe *m) {
+    MoeScratch L;
+    uint64_t off = 0;
+    auto take = [&](uint64_t bytes) {
+        const uint64_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const bool sh = m->shared_gate_up != nullptr;
+    L.sel = take(sizeof(sg_moe_choice));
+    L.shsel = take(sizeof(sg_moe_choice));
+    L.scale = take(4);
+    L.gu = take(m->n_used * 2 * m->n_ff * 4);
+    L.y = take(m->n_used * m->dim * 4);
+    L.gush = take(sh ? 2 * m->shared_n_ff * 4 : 0);
+    L.ysh = take(sh ? m->dim * 4 : 0);
+    L.total = off;
+    return L;
+}
+
+// One grouped launch of the tiled GEMV over the chosen experts (IN_MOE_X or IN_MOE_H).
+sg_status launch_moe_group(int32_t dtype, int mode, const uint8_t *w, uint64_t mat_stride, uint64_t rows,
+                           uint64_t cols, uint32_t max_slots, uint32_t n_expert, const sg_moe_choice *sel,
+                           const float *x, const float *gu, uint64_t gu_stride, uint64_t n_ff, float *out,
+                           uint64_t out_stride, cudaStream_t stream) {
+    const int dt = dtype == SG_Q4_K ? DT_Q4K : DT_Q6K;
+    const uint32_t nb = (uint32_t)(cols / 256), tiles = (uint32_t)((rows + TILE_ROWS - 1) / TILE_ROWS);
+    TPlan p;
+    sg_status st = tiled_plan(dt, nb, max_slots * tiles, 1, mode, max_slots, &p);
+    if (st) return st;
+    TGemvArgs a;
+    memset(&a, 0, sizeof a);
+    a.w = w;
+    a.nb = nb;
+    a.ntiles = max_slots * tiles;
+    a.r1 = (uint32_t)rows;
+    a.S = p.S;
+    a.bc = p.bc;
+    a.nstages = p.nstages;
+    a.stage_bytes = p.stage_bytes;
+    a.slot_blocks = p.slot_blocks;
+    a.nvec = 1;
+    a.x[0] = x;
+    a.out[0] = out;
+    a.sel = sel;
+    a.mat_stride = mat_stride;
+    a.out_stride = out_stride;
+    a.tiles_per_mat = tiles;
+    a.max_slots = max_slots;
+    a.n_expert = n_expert;
+    a.n_ff = (uint32_t)n_ff;
+    a.gu = gu;
+    a.gu_stride = gu_stride;
+    CK(launch_pdl((const void *)p.fn, p.grid, p.warps * 32, p.smem, stream, &a));
+    return SG_OK;
+}
+
+sg_status launch_router(const sg_moe *m, const float *x, sg_moe_choice *sel, sg_moe_choice *shsel, float *scale,
+                        float *probs, cudaStream_t stream) {
+    static std::atomic<uint64_t> attr_done{0};  // bit d: the smem attribute is set on device d
+    int dev;
+    CK(cudaGetDevice(&dev));
+    if (!(attr_done.load() >> dev & 1)) {
+        CK(cudaFuncSetAttribute((const void *)moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                227 * 1024));
+        attr_done.fetch_or(1ull << dev);
+    }
+    RouterArgs a;
+    memset(&a, 0, sizeof a);
+    a.w = m->router;
+    a.x = x;
+    a.dim = (uint32_t)m->dim;
+    a.n_expert = (uint32_t)m->n_expert;
+    a.n_used = (uint32_t)m->n_used;
+    a.rows_per_cta = (a.n_expert + ROUTER_CLUSTER - 1) / ROUTER_CLUSTER;
+    // as many rows per ring stage as 200 KB of shared memory hold (at most 16)
+    uint32_t rc = a.rows_per_cta < 16 ? a.rows_per_cta : 16;
+    while (rc > 1 && router_smem_bytes(a.dim, rc, a.rows_per_cta, a.n_expert) > 200 * 1024) rc--;
+    const uint32_t smem = router_smem_bytes(a.dim, rc, a.rows_per_cta, a.n_expert);
+    if (smem > 227 * 1024) return SG_ERR_SHAPE;
+    a.rc = rc;
+    a.norm = m->norm;
+    a.prune = m->moe_prune;
+    a.probs = probs;
+    a.sel = sel;
+    a.shared_sel = m->shared_gate_up ? shsel : nullptr;
+    a.shared_gate = m->shared_gate_up ? m->shared_gate : nullptr;
+    a.shared_scale = m->shared_gate_up ? scale : nullptr;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ROUTER_CLUSTER);
+    cfg.blockDim = dim3(ROUTER_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = ROUTER_CLUSTER;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    void *params[] = {&a};
+    CK(cudaLaunchKernelExC(&cfg, (const void *)moe_router_kernel, params));
+    return SG_OK;
+}
+
+sg_status pack_experts(int32_t dtype, const uint8_t *src, uint64_t n_expert, uint64_t rows, uint64_t cols,
+                       uint64_t dst_rows, uint64_t off, uint8_t *dst, cudaStream_t stream) {
+    const uint64_t n = n_expert * rows * (cols / 256);
+    if (!n) return SG_OK;
+    repack_tiled16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+        dtype == SG_Q4_K ? 0 : 1, src, n_expert * rows, (uint32_t)(cols / 256), dst, 0, rows, dst_rows, off);
+    CK(cudaGetLastError());
     return SG_OK;
 }
 
@@ -634,7 +808,7 @@ static sg_status repack(int32_t dtype, const uint8_t *src, uint64_t rows, uint64
     const uint64_t n = rows * (cols / 256);
     if (n) {
         repack_tiled16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-            dtype == SG_Q4_K ? 0 : 1, src, rows, (uint32_t)(cols / 256), dst, inverse);
+            dtype == SG_Q4_K ? 0 : 1, src, rows, (uint32_t)(cols / 256), dst, inverse, rows, 0, 0);
         CK(cudaGetLastError());
     }
     return SG_OK;
@@ -694,6 +868,76 @@ sg_status sg_matvec_scratch(const uint8_t *d_base, const sg_mat *m, const float 
         if ((st = sg_q8k_quantize(d_x + g * ldx, m->cols, nv, ldx, q, stream))) return st;
         if ((st = launch_gemv(d_base, m, q, outs, nv, r0, r1, nullptr, (cudaStream_t)stream))) return st;
     }
+    return SG_OK;
+}
+
+sg_status sg_moe_pack_gate_up(int32_t dtype, const uint8_t *d_gate_exps, const uint8_t *d_up_exps,
+                              uint64_t n_expert, uint64_t n_ff, uint64_t dim, uint8_t *d_out, void *stream) {
+    if (!d_gate_exps || !d_up_exps || !d_out || !n_expert || !n_ff) return SG_ERR_INVALID;
+    if (!kquant(dtype)) return SG_ERR_DTYPE;
+    if (!cols_ok(dim)) return SG_ERR_SHAPE;
+    const uint64_t stride = tiled_bytes(dtype, 2 * n_ff, dim), drows = align_up(2 * n_ff, TILE_ROWS);
+    CK(cudaMemsetAsync(d_out, 0, stride * n_expert, (cudaStream_t)stream));  // zero padding rows
+    sg_status st = pack_experts(dtype, d_gate_exps, n_expert, n_ff, dim, drows, 0, d_out, (cudaStream_t)stream);
+    if (st) return st;
+    return pack_experts(dtype, d_up_exps, n_expert, n_ff, dim, drows, n_ff, d_out, (cudaStream_t)stream);
+}
+
+sg_status sg_moe_pack_down(int32_t dtype, const uint8_t *d_down_exps, uint64_t n_expert, uint64_t dim,
+                           uint64_t n_ff, uint8_t *d_out, void *stream) {
+    if (!d_down_exps || !d_out || !n_expert || !dim) return SG_ERR_INVALID;
+    if (!kquant(dtype)) return SG_ERR_DTYPE;
+    if (!cols_ok(n_ff)) return SG_ERR_SHAPE;
+    const uint64_t stride = tiled_bytes(dtype, dim, n_ff);
+    CK(cudaMemsetAsync(d_out, 0, stride * n_expert, (cudaStream_t)stream));
+    return pack_experts(dtype, d_down_exps, n_expert, dim, n_ff, align_up(dim, TILE_ROWS), 0, d_out,
+                        (cudaStream_t)stream);
+}
+
+uint64_t sg_moe_scratch_bytes(const sg_moe *m) { return check_moe(m) ? 0 : moe_scratch(m).total; }
+
+sg_status sg_moe_forward(const sg_moe *m, const float *d_x, float *d_out, void *d_scratch, uint64_t scratch_bytes,
+                         sg_moe_choice *d_choice, float *d_probs, void *stream) {
+    sg_status st = check_moe(m);
+    if (st) return st;
+    if (!d_x || !d_out || !d_scratch) return SG_ERR_INVALID;
+    if (!aligned(d_x, 16) || !aligned(d_out, 4) || !aligned(d_scratch, 256) || !aligned(d_choice, 16) ||
+        !aligned(d_probs, 4))
+        return SG_ERR_ALIGN;
+    const MoeScratch L = moe_scratch(m);
+    if (scratch_bytes < L.total) return SG_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t *sc = (uint8_t *)d_scratch;
+    sg_moe_choice *sel = d_choice ? d_choice : (sg_moe_choice *)(sc + L.sel);
+    sg_moe_choice *shsel = (sg_moe_choice *)(sc + L.shsel);
+    float *scale = (float *)(sc + L.scale), *gu = (float *)(sc + L.gu), *y = (float *)(sc + L.y);
+    float *gush = (float *)(sc + L.gush), *ysh = (float *)(sc + L.ysh);
+    const bool sh = m->shared_gate_up != nullptr;
+    const uint32_t k = (uint32_t)m->n_used, ne = (uint32_t)m->n_expert;
+    // Order matters for the dependent launches: every grouped GEMV starts
+    // after the router has completed (see gemv_tiled_kernel's MoE prologue).
+    if ((st = launch_router(m, d_x, sel, shsel, scale, d_probs, s))) return st;
+    if (sh && (st = launch_moe_group(m->shared_gate_up_dtype, IN_MOE_X, m->shared_gate_up, 0, 2 * m->shared_n_ff,
+                                     m->dim, 1, 1, shsel, d_x, nullptr, 0, 0, gush, 0, s)))
+        return st;
+    if ((st = launch_moe_group(m->gate_up_dtype, IN_MOE_X, m->gate_up, m->gate_up_stride, 2 * m->n_ff, m->dim, k,
+                               ne, sel, d_x, nullptr, 0, 0, gu, 2 * m->n_ff, s)))
+        return st;
+    if ((st = launch_moe_group(m->down_dtype, IN_MOE_H, m->down, m->down_stride, m->dim, m->n_ff, k, ne, sel,
+                               nullptr, gu, 2 * m->n_ff, m->n_ff, y, m->dim, s)))
+        return st;
+    if (sh && (st = launch_moe_group(m->shared_down_dtype, IN_MOE_H, m->shared_down, 0, m->dim, m->shared_n_ff, 1, 1,
+                                     shsel, nullptr, gush, 2 * m->shared_n_ff, m->shared_n_ff, ysh, 0, s)))
+        return st;
+    CombineArgs c;
+    c.sel = sel;
+    c.y = y;
+    c.ysh = sh ? ysh : nullptr;
+    c.shared_scale = scale;
+    c.out = d_out;
+    c.dim = (uint32_t)m->dim;
+    c.max_slots = k;
+    CK(launch_pdl((const void *)moe_combine_kernel, (uint32_t)((m->dim + 255) / 256), 256, 0, s, &c));
     return SG_OK;
 }
 

@@ -5,38 +5,66 @@
 namespace sg {
 using namespace tiled;
 
-template <int DT, int NV, bool QX>
+template <int DT, int NV, int MODE>
 __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const __grid_constant__ TGemvArgs a) {
     constexpr uint32_t CB = tiled_col_bytes(DT);
+    constexpr bool MOE = MODE == IN_MOE_X || MODE == IN_MOE_H;
     extern __shared__ __align__(128) uint8_t smem[];
     // A launch whose shared memory cannot hold this layout records an error
     // and does nothing (uniform exit, before any barrier).
     const uint32_t nwarps = blockDim.x >> 5;
-    if (tiled_smem_bytes(nwarps, a.S, a.nstages, a.stage_bytes, a.slot_blocks, NV, a.nb) > dynamic_smem_size() ||
+    if (tiled_smem_bytes(nwarps, a.S, a.nstages, a.stage_bytes, a.slot_blocks, NV, a.nb,
+                         tiled_nact(MODE, NV, a.max_slots), tiled_extra(MODE, nwarps)) > dynamic_smem_size() ||
         a.bc == 0 || a.stage_bytes < a.bc * CB || a.S == 0 || nwarps % a.S || (blockDim.x & 31) ||
-        a.nstages * nwarps * 8 > TGEMV_BAR_BYTES) {
+        a.nstages * nwarps * 8 > (MOE ? MOE_SEL_OFF : TGEMV_BAR_BYTES) ||
+        (MOE && (a.max_slots > MOE_MAXK || a.tiles_per_mat == 0))) {
         if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
         return;
     }
-    // Let the next kernel in the stream launch as soon as SMs free up: it only
-    // prefetches its own weights before waiting for this grid to finish.
-    grid_launch_dependents();
+    uint32_t ntiles = a.ntiles;
+    const int32_t *sids = reinterpret_cast<const int32_t *>(smem + MOE_SEL_OFF + 64);
+    if constexpr (MOE) {
+        // The expert choice is the router's.  IN_MOE_X runs right after the
+        // router: wait for it.  IN_MOE_H runs after IN_MOE_X, which lets it
+        // launch only once every CTA of IN_MOE_X has waited for the router, so
+        // the choice is already in memory: read it past L1 without waiting,
+        // and prefetch the chosen experts' weights before waiting for h.
+        if constexpr (MODE == IN_MOE_X) grid_dependency_wait();
+        grid_launch_dependents();
+        if (threadIdx.x < 32) {
+            uint32_t *sm = reinterpret_cast<uint32_t *>(smem + MOE_SEL_OFF);
+            const uint32_t n = min(__ldcg(&a.sel->n), a.max_slots);
+            const int32_t id = threadIdx.x < n ? __ldcg(&a.sel->id[threadIdx.x]) : 0;
+            const bool bad = __any_sync(0xffffffffu, threadIdx.x < n && (id < 0 || (uint32_t)id >= a.n_expert));
+            if (threadIdx.x < MOE_MAXK) sm[16 + threadIdx.x] = (uint32_t)id;
+            if (threadIdx.x == 0) {
+                sm[0] = bad ? 0u : n;
+                if (bad) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+            }
+        }
+        __syncthreads();
+        ntiles = *reinterpret_cast<const uint32_t *>(smem + MOE_SEL_OFF) * a.tiles_per_mat;
+    } else {
+        // Let the next kernel in the stream launch as soon as SMs free up: it
+        // only prefetches its own weights before waiting for this grid to finish.
+        grid_launch_dependents();
+    }
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t g = lane >> 4, r = lane & 15u;
     const uint32_t S = a.S, group = warp / S, slot = warp % S, G = nwarps / S;
     const uint32_t astride = act_bytes(a.nb);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * a.nstages;
     uint8_t *act = smem + TGEMV_BAR_BYTES;
-    uint8_t *rings = act + NV * astride;
+    uint8_t *rings = act + tiled_nact(MODE, NV, a.max_slots) * astride;
     uint8_t *ring = rings + warp * a.nstages * a.stage_bytes;
     const uint32_t worker_floats = a.slot_blocks * NV * CHAIN_FLOATS;
-    float *gscratch = reinterpret_cast<float *>(rings + nwarps * a.nstages * a.stage_bytes) +
-                      group * (S - 1) * worker_floats;
+    float *gscratch0 = reinterpret_cast<float *>(rings + nwarps * a.nstages * a.stage_bytes);
+    float *gscratch = gscratch0 + group * (S - 1) * worker_floats;
     const uint32_t b_lo = a.nb * slot / S, nblk = a.nb * (slot + 1) / S - b_lo;
     const uint32_t bc = a.bc, nchunk = (nblk + bc - 1) / bc;  // stages per tile for this slot
     // groups are numbered CTA-minor so that consecutive tiles land on different SMs
     const uint32_t gid = group * gridDim.x + blockIdx.x, GW = gridDim.x * G;
-    const uint32_t my_tiles = gid < a.ntiles ? (a.ntiles - gid + GW - 1) / GW : 0u;
+    const uint32_t my_tiles = gid < ntiles ? (ntiles - gid + GW - 1) / GW : 0u;
     const uint32_t nitems = my_tiles * nchunk;
     const uint64_t tile_bytes = (uint64_t)a.nb * CB;
     const uint32_t bar_full = 1 + group, bar_free = 1 + G + group, nbar = 32 * S;
@@ -45,10 +73,16 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     auto issue = [&](uint32_t k) {
         const uint32_t tt = a.t0 + gid + (k / nchunk) * GW, c = k % nchunk;
         const uint32_t nbytes = min(bc, nblk - c * bc) * CB;
+        const uint8_t *tile;
+        if constexpr (MOE) {
+            const uint32_t s = tt / a.tiles_per_mat;
+            tile = a.w + (uint64_t)sids[s] * a.mat_stride + (uint64_t)(tt - s * a.tiles_per_mat) * tile_bytes;
+        } else {
+            tile = a.w + tt * tile_bytes;
+        }
         uint64_t *bar = &bars[k % a.nstages];
         mbar_arrive_expect_tx(bar, nbytes);
-        bulk_g2s(ring + (k % a.nstages) * a.stage_bytes, a.w + tt * tile_bytes + (uint64_t)(b_lo + c * bc) * CB,
-                 nbytes, bar);
+        bulk_g2s(ring + (k % a.nstages) * a.stage_bytes, tile + (uint64_t)(b_lo + c * bc) * CB, nbytes, bar);
     };
     // Weights do not depend on the previous kernel: start streaming them first.
     if (lane == 0) {
@@ -59,7 +93,28 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     // The activations do: wait for the grid that wrote them, then stage them.
     grid_dependency_wait();
     const uint32_t nb = a.nb;
-    if constexpr (QX) {
+    if constexpr (MODE == IN_MOE_H) {
+        // one warp per (slot, 256-block): h = silu(g) * up into a per-warp fp32
+        // block, then the exact Q8_K quantization of it
+        float *hb = gscratch0 + G * (S - 1) * worker_floats + warp * 256u;
+        const uint32_t nsel = ntiles / a.tiles_per_mat;
+        for (uint32_t wb = warp; wb < nsel * nb; wb += nwarps) {
+            const uint32_t s = wb / nb, b = wb % nb;
+            const float *gp = a.gu + s * a.gu_stride + 256u * b + 8u * lane;
+            const float4 g0 = *reinterpret_cast<const float4 *>(gp), g1 = *reinterpret_cast<const float4 *>(gp + 4);
+            const float4 u0 = *reinterpret_cast<const float4 *>(gp + a.n_ff);
+            const float4 u1 = *reinterpret_cast<const float4 *>(gp + a.n_ff + 4);
+            reinterpret_cast<float4 *>(hb)[2 * lane] =
+                make_float4(silu_mul(g0.x, u0.x), silu_mul(g0.y, u0.y), silu_mul(g0.z, u0.z), silu_mul(g0.w, u0.w));
+            reinterpret_cast<float4 *>(hb)[2 * lane + 1] =
+                make_float4(silu_mul(g1.x, u1.x), silu_mul(g1.y, u1.y), silu_mul(g1.z, u1.z), silu_mul(g1.w, u1.w));
+            __syncwarp();
+            uint8_t *av = act + s * astride;
+            q8k_block(hb, reinterpret_cast<int8_t *>(av + 256u * b), reinterpret_cast<int16_t *>(av + 256u * nb + 32u * b),
+                      reinterpret_cast<float *>(av + 288u * nb + 4u * b), lane);
+            __syncwarp();
+        }
+    } else if constexpr (MODE == IN_F32 || MODE == IN_MOE_X) {
         // one warp per (vector, 256-block): the exact Q8_K quantization
         for (uint32_t wb = warp; wb < a.nvec * nb; wb += nwarps) {
             const uint32_t v = wb / nb, b = wb % nb;
@@ -86,6 +141,13 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     uint32_t k = 0;
     for (uint32_t ti = 0; ti < my_tiles; ti++) {
         const uint32_t tt = a.t0 + gid + ti * GW;
+        // MoE: slot ms of the choice, tile mt of its matrix
+        uint32_t ms = 0, mt = tt;
+        if constexpr (MOE) {
+            ms = tt / a.tiles_per_mat;
+            mt = tt - ms * a.tiles_per_mat;
+        }
+        const uint8_t *tact = MODE == IN_MOE_H ? act + ms * astride : act;
         float acc[NV][4], corr[NV];
 #pragma unroll
         for (int v = 0; v < NV; v++) {
@@ -118,9 +180,9 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                 int s[NV][4];
                 float cd[NV], ct[NV];
                 if constexpr (DT == 0)
-                    block_q4k<NV>(col, g, r, i, a.nvec, a.nb, act, astride, s, cd, ct);
+                    block_q4k<NV>(col, g, r, i, a.nvec, a.nb, tact, astride, s, cd, ct);
                 else
-                    block_q6k<NV>(col, g, r, i, a.nvec, a.nb, act, astride, s, cd, ct);
+                    block_q6k<NV>(col, g, r, i, a.nvec, a.nb, tact, astride, s, cd, ct);
 #pragma unroll
                 for (int v = 0; v < NV; v++) {
                     if (v >= (int)a.nvec) break;
@@ -174,37 +236,41 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
         }
         if (slot == 0) {
             // 8-lane tree ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)), then minus the correction.
-            const uint32_t row = tt * TILE_ROWS + r;
+            const uint32_t row = mt * TILE_ROWS + r;
 #pragma unroll
             for (int v = 0; v < NV; v++) {
                 float x[4];
 #pragma unroll
                 for (int m = 0; m < 4; m++) x[m] = __fadd_rn(acc[v][m], __shfl_down_sync(0xffffffffu, acc[v][m], 16));
+                float *dst = MOE ? a.out[0] + ms * a.out_stride : a.out[v];
                 if (g == 0 && v < (int)a.nvec && row >= a.r0 && row < a.r1)
-                    a.out[v][row] = __fsub_rn(__fadd_rn(__fadd_rn(x[0], x[2]), __fadd_rn(x[1], x[3])), corr[v]);
+                    dst[row] = __fsub_rn(__fadd_rn(__fadd_rn(x[0], x[2]), __fadd_rn(x[1], x[3])), corr[v]);
             }
         }
     }
 }
 
-#define SG_TINST1(DT, NV)                                                                         \
-    template __global__ void gemv_tiled_kernel<DT, NV, false>(const __grid_constant__ TGemvArgs); \
-    template __global__ void gemv_tiled_kernel<DT, NV, true>(const __grid_constant__ TGemvArgs);
-#define SG_TINST(DT) SG_TINST1(DT, 1) SG_TINST1(DT, 2) SG_TINST1(DT, 4) SG_TINST1(DT, 8)
+#define SG_TINST1(DT, NV)                                                                          \
+    template __global__ void gemv_tiled_kernel<DT, NV, IN_Q8K>(const __grid_constant__ TGemvArgs); \
+    template __global__ void gemv_tiled_kernel<DT, NV, IN_F32>(const __grid_constant__ TGemvArgs);
+#define SG_TINST(DT)                                                                                        \
+    SG_TINST1(DT, 1) SG_TINST1(DT, 2) SG_TINST1(DT, 4) SG_TINST1(DT, 8)                                     \
+    template __global__ void gemv_tiled_kernel<DT, 1, IN_MOE_X>(const __grid_constant__ TGemvArgs); \
+    template __global__ void gemv_tiled_kernel<DT, 1, IN_MOE_H>(const __grid_constant__ TGemvArgs);
 SG_TINST(0)
 SG_TINST(1)
 
 // GGUF rows <-> TILED16 (inverse = 1: src is TILED16, dst GGUF rows).
 // One thread per (row, super-block); padding rows of dst are left as they are.
 __global__ void repack_tiled16_kernel(int dt, const uint8_t *src, uint64_t rows, uint32_t nb, uint8_t *dst,
-                                      int inverse) {
+                                      int inverse, uint64_t rpg, uint64_t dgr, uint64_t off) {
     const uint64_t id = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (id >= rows * nb) return;
-    const uint64_t row = id / nb;
-    const uint32_t i = (uint32_t)(id % nb), r = (uint32_t)(row % TILE_ROWS);
+    const uint64_t row = id / nb, trow = (row / rpg) * dgr + off + row % rpg;
+    const uint32_t i = (uint32_t)(id % nb), r = (uint32_t)(trow % TILE_ROWS);
     const uint32_t bb = dt == 0 ? 144u : 210u, cb = tiled_col_bytes(dt);
     const uint64_t g_off = (row * nb + i) * bb;
-    const uint64_t t_off = (row / TILE_ROWS) * (uint64_t)nb * cb + (uint64_t)i * cb;
+    const uint64_t t_off = (trow / TILE_ROWS) * (uint64_t)nb * cb + (uint64_t)i * cb;
     // (offset in the GGUF block, offset in the tile column, length); the quant
     // bytes move in 16-byte chunks to their swizzled slots
     uint32_t seg[16][3];

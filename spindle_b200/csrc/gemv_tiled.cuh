@@ -38,6 +38,19 @@ __host__ __device__ constexpr uint32_t tiled_col_bytes(int dt) { return dt == 0 
 // Shared-memory image of one Q8_K vector: qs[cols] | bsums[nb*16] | d[nb] (16-aligned).
 __host__ __device__ inline uint32_t act_bytes(uint32_t nb) { return nb * 256u + nb * 32u + ((nb * 4u + 15u) & ~15u); }
 
+// What the kernel reads as its vectors, and where its tiles come from.
+//   IN_Q8K:   Q8_K vectors (xd, xs, xb).
+//   IN_F32:   fp32 vectors x, quantized to Q8_K by every CTA in shared memory
+//             (the reference's matvec = Q8K::quantize + matmul_rows in one kernel).
+//   IN_MOE_X: grouped over the experts the router chose (sel): launch tile tt is
+//             tile tt % tiles_per_mat of expert sel->id[tt / tiles_per_mat], whose
+//             matrix is at w + id * mat_stride; one fp32 vector x[0], quantized
+//             as in IN_F32; slot s's rows go to out[0] + s * out_stride.
+//   IN_MOE_H: grouped like IN_MOE_X; slot s's vector is h = silu(g) * up (g at
+//             gu + s * gu_stride, up n_ff floats after it), quantized per CTA.
+constexpr int IN_Q8K = 0, IN_F32 = 1, IN_MOE_X = 2, IN_MOE_H = 3;
+constexpr uint32_t MOE_MAXK = SG_MOE_MAX_USED;
+
 struct TGemvArgs {
     const uint8_t *w;     // TILED16 buffer (16-byte aligned)
     uint32_t nb;          // super-blocks per row
@@ -54,25 +67,45 @@ struct TGemvArgs {
     const int8_t *xs[TGEMV_MAXV];
     const int16_t *xb[TGEMV_MAXV];
     float *out[TGEMV_MAXV];
+    // IN_MOE_X / IN_MOE_H only
+    const sg_moe_choice *sel;
+    uint64_t mat_stride;
+    uint64_t out_stride;
+    uint32_t tiles_per_mat;
+    uint32_t max_slots;   // slots the launch was sized for (n_used)
+    uint32_t n_expert;
+    uint32_t n_ff;        // IN_MOE_H
+    const float *gu;      // IN_MOE_H
+    uint64_t gu_stride;   // IN_MOE_H, floats
 };
 
+// In the MoE modes the router's choice is copied into the top of the barrier
+// area: n at MOE_SEL_OFF, ids after it.
+constexpr uint32_t MOE_SEL_OFF = TGEMV_BAR_BYTES - 128;
+
+// Activation images staged per CTA, and per-warp fp32 staging for h (IN_MOE_H).
+__host__ __device__ inline uint32_t tiled_nact(int mode, uint32_t nv, uint32_t max_slots) {
+    return mode == IN_MOE_H ? max_slots : nv;
+}
+__host__ __device__ inline uint32_t tiled_extra(int mode, uint32_t warps) { return mode == IN_MOE_H ? warps * 1024u : 0u; }
+
 // Dynamic shared memory of one CTA of `warps` warps:
-// barriers | activations | rings | chain scratch.
+// barriers | activations (nact images) | rings | chain scratch | extra.
 __host__ __device__ inline uint32_t tiled_smem_bytes(uint32_t warps, uint32_t S, uint32_t nstages,
                                                      uint32_t stage_bytes, uint32_t slot_blocks, uint32_t nv,
-                                                     uint32_t nb) {
+                                                     uint32_t nb, uint32_t nact, uint32_t extra) {
     const uint32_t groups = warps / S;
-    return TGEMV_BAR_BYTES + nv * act_bytes(nb) + warps * nstages * stage_bytes +
-           groups * (S - 1) * slot_blocks * nv * CHAIN_FLOATS * 4u;
+    return TGEMV_BAR_BYTES + nact * act_bytes(nb) + warps * nstages * stage_bytes +
+           groups * (S - 1) * slot_blocks * nv * CHAIN_FLOATS * 4u + extra;
 }
 
-// QX = true: the inputs are fp32 (a.x) and every CTA quantizes them to Q8_K
-// in shared memory (the reference's matvec = Q8K::quantize + matmul_rows, in
-// one kernel).  QX = false: the inputs are Q8_K vectors (a.xd, a.xs, a.xb).
-template <int DT, int NV, bool QX>
+template <int DT, int NV, int MODE>
 __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const __grid_constant__ TGemvArgs a);
 
+// GGUF row `row` is row (row / rpg) * dgr + off + row % rpg of the TILED16
+// buffer (plain matrices: rpg = rows, dgr = off = 0; stacked expert tensors:
+// rpg = rows per expert, dgr = padded rows per stacked expert).
 __global__ void repack_tiled16_kernel(int dt, const uint8_t *src, uint64_t rows, uint32_t nb, uint8_t *dst,
-                                      int inverse);
+                                      int inverse, uint64_t rpg, uint64_t dgr, uint64_t off);
 
 }  // namespace sg
