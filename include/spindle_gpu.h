@@ -203,11 +203,14 @@ typedef struct {
 } sg_moe_choice;
 
 /* Device weights of one MoE layer (struct Moe, smollm_chat.rs:152-167).
- * Expert e's gate and up (n_ff rows each, dim cols) are stacked as one TILED16
- * matrix [gate_e; up_e] at gate_up + e * gate_up_stride; its down (dim rows,
- * n_ff cols) is TILED16 at down + e * down_stride.  sg_moe_pack_gate_up and
- * sg_moe_pack_down build both from the GGUF expert tensors; the strides are
- * sg_tiled16_bytes(dtype, 2 * n_ff, dim) and sg_tiled16_bytes(dtype, dim, n_ff). */
+ * Expert e's gate and up (n_ff rows each, dim cols) are one TILED16 matrix of
+ * 2 * n_ff rows at gate_up + e * gate_up_stride, interleaved in groups of 8:
+ * rows 16q..16q+7 are gate rows 8q..8q+7 and rows 16q+8..16q+15 the up rows
+ * 8q..8q+7, so that each 16-row tile yields 8 outputs of silu(gate) * up.  Its
+ * down (dim rows, n_ff cols) is TILED16 at down + e * down_stride.
+ * sg_moe_pack_gate_up and sg_moe_pack_down build both from the GGUF expert
+ * tensors; the strides are sg_tiled16_bytes(dtype, 2 * n_ff, dim) and
+ * sg_tiled16_bytes(dtype, dim, n_ff). */
 typedef struct {
     const float *router;              /* F32 [n_expert][dim] (ffn_gate_inp) */
     const uint8_t *gate_up;
@@ -218,7 +221,7 @@ typedef struct {
     int32_t norm;                     /* expert_norm */
     float moe_prune;                  /* 0 = off; (0,1) = keep mass 1-prune; >= 1 = keep that many */
     /* Shared expert (Qwen2-MoE): NULL shared_gate_up = none. */
-    const uint8_t *shared_gate_up;    /* TILED16 [gate; up], 2 * shared_n_ff rows */
+    const uint8_t *shared_gate_up;    /* TILED16 gate/up, interleaved as above, 2 * shared_n_ff rows */
     const uint8_t *shared_down;       /* TILED16, dim rows x shared_n_ff cols */
     int32_t shared_gate_up_dtype, shared_down_dtype;
     uint64_t shared_n_ff;
@@ -226,7 +229,8 @@ typedef struct {
 } sg_moe;
 
 /* Repack the GGUF expert tensors ffn_gate_exps and ffn_up_exps ([n_expert]
- * matrices of n_ff x dim, same dtype) into the stacked TILED16 form above. */
+ * matrices of n_ff x dim, same dtype; n_ff a multiple of 8) into the
+ * interleaved TILED16 form above. */
 SG_API sg_status sg_moe_pack_gate_up(int32_t dtype, const uint8_t *d_gate_exps, const uint8_t *d_up_exps,
                                      uint64_t n_expert, uint64_t n_ff, uint64_t dim, uint8_t *d_out, void *stream);
 /* Repack ffn_down_exps ([n_expert] matrices of dim x n_ff) into TILED16 per expert. */

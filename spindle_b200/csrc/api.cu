@@ -261,7 +261,7 @@ int env_int(const char *name, int dflt) {
 
 struct TPlan {
     tgemv_fn fn;
-    uint32_t S, bc, nstages, stage_bytes, slot_blocks, grid, warps;
+    uint32_t S, bc, nstages, stage_bytes, slot_blocks, grid, warps, nact;
     size_t smem;
 };
 
@@ -322,8 +322,19 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
     if (ns < 2) ns = 2;
     if (ns > 8) ns = 8;
     // the MoE modes keep the router's choice at the top of the barrier area
-    if (mode >= IN_MOE_X && ns * warps * 8 > MOE_SEL_OFF) ns = MOE_SEL_OFF / (warps * 8);
+    if (mode >= IN_MOE_X && ns * warps * 8 > MOE_QX_BAR_OFF) ns = MOE_QX_BAR_OFF / (warps * 8);
     if (bc < 1) bc = 1;
+    // MoE: one CTA per SM, each on a contiguous range of tiles; IN_MOE_H stages
+    // h for every slot its range touches (at most this many).
+    uint32_t moe_nact = 0, moe_grid = 0;
+    if (mode >= IN_MOE_X) {
+        moe_grid = ntiles < (uint32_t)di->sms ? ntiles : (uint32_t)di->sms;
+        if (moe_grid == 0) moe_grid = 1;
+        const uint32_t tpm = max_slots ? ntiles / max_slots : 1, tpc = (ntiles + moe_grid - 1) / moe_grid;
+        moe_nact = tpm ? (tpc + tpm - 2) / tpm + 1 : 1;
+        if (moe_nact > max_slots) moe_nact = max_slots;
+        if (moe_nact == 0) moe_nact = 1;
+    }
     // Fit the CTA in shared memory: fewer stages, then smaller stages, then
     // fewer warps per tile (less chain scratch).
     const size_t budget = warps == 16 ? 220 * 1024 : 110 * 1024;
@@ -334,7 +345,7 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
         p->nstages = ns;
         p->stage_bytes = p->bc * cb;
         p->smem = tiled_smem_bytes(warps, S, ns, p->stage_bytes, p->slot_blocks, nv_inst, nb,
-                                   tiled_nact(mode, nv_inst, max_slots), tiled_extra(mode, warps));
+                                   tiled_nact(mode, nv_inst, moe_nact));
         if (p->smem <= budget) break;
         if (ns > 2)
             ns--;
@@ -356,6 +367,8 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
     // some groups get no tile (tiles go to CTAs round-robin)
     const uint32_t need = (ntiles + groups - 1) / groups, cap = (uint32_t)(di->sms * occ);
     p->grid = need < (uint32_t)di->sms ? (ntiles < (uint32_t)di->sms ? ntiles : (uint32_t)di->sms) : (need < cap ? need : cap);
+    p->nact = moe_nact;
+    if (mode >= IN_MOE_X) p->grid = moe_grid;
     std::lock_guard<std::mutex> lk(g_mu);
     if (g_tplans.size() > 4096) g_tplans.clear();
     g_tplans.emplace(key, *p);
@@ -488,7 +501,7 @@ sg_status check_moe(const sg_moe *m) {
 
 // Scratch of sg_moe_forward, each piece 256-byte aligned.
 struct MoeScratch {
-    uint64_t sel, shsel, scale, gu, y, gush, ysh, total;
+    uint64_t sel, shsel, scale, logits, qx, h, y, hsh, ysh, total;
 };
 
 MoeScratch moe_scratch(const sg_moe *m) {
@@ -503,24 +516,38 @@ MoeScratch moe_scratch(const sg_moe *m) {
     L.sel = take(sizeof(sg_moe_choice));
     L.shsel = take(sizeof(sg_moe_choice));
     L.scale = take(4);
-    L.gu = take(m->n_used * 2 * m->n_ff * 4);
+    L.logits = take(m->n_expert * 4);
+    L.qx = take(act_bytes((uint32_t)(m->dim / 256)));
+    L.h = take(m->n_used * m->n_ff * 4);
     L.y = take(m->n_used * m->dim * 4);
-    L.gush = take(sh ? 2 * m->shared_n_ff * 4 : 0);
+    L.hsh = take(sh ? m->shared_n_ff * 4 : 0);
     L.ysh = take(sh ? m->dim * 4 : 0);
     L.total = off;
     return L;
 }
 
+// The expert choice of a grouped launch: made from the router's logits in the
+// kernel (IN_MOE_X with logits), or read from `sel`.
+struct MoeRoute {
+    const float *logits;
+    sg_moe_choice *sel_out;
+    float *probs;
+    uint32_t n_used;
+    int32_t norm;
+    float prune;
+};
+
 // One grouped launch of the tiled GEMV over the chosen experts (IN_MOE_X or IN_MOE_H).
 sg_status launch_moe_group(int32_t dtype, int mode, const uint8_t *w, uint64_t mat_stride, uint64_t rows,
                            uint64_t cols, uint32_t max_slots, uint32_t n_expert, const sg_moe_choice *sel,
-                           const float *x, const float *gu, uint64_t gu_stride, uint64_t n_ff, float *out,
-                           uint64_t out_stride, cudaStream_t stream) {
+                           const MoeRoute *route, const float *x, const uint8_t *qx, const float *h,
+                           uint64_t h_stride, float *out, uint64_t out_stride, cudaStream_t stream) {
     const int dt = dtype == SG_Q4_K ? DT_Q4K : DT_Q6K;
     const uint32_t nb = (uint32_t)(cols / 256), tiles = (uint32_t)((rows + TILE_ROWS - 1) / TILE_ROWS);
     TPlan p;
     sg_status st = tiled_plan(dt, nb, max_slots * tiles, 1, mode, max_slots, &p);
     if (st) return st;
+    if (route && moe_select_bytes(n_expert) > p.warps * p.nstages * p.stage_bytes) return SG_ERR_SHAPE;
     TGemvArgs a;
     memset(&a, 0, sizeof a);
     a.w = w;
@@ -534,22 +561,34 @@ sg_status launch_moe_group(int32_t dtype, int mode, const uint8_t *w, uint64_t m
     a.slot_blocks = p.slot_blocks;
     a.nvec = 1;
     a.x[0] = x;
+    a.qx_image = qx;
+    a.swiglu = mode == IN_MOE_X;  // the packed gate/up tiles interleave 8 gate and 8 up rows
     a.out[0] = out;
     a.sel = sel;
+    if (route) {
+        a.logits = route->logits;
+        a.sel_out = route->sel_out;
+        a.probs = route->probs;
+        a.n_used = route->n_used;
+        a.norm = route->norm;
+        a.prune = route->prune;
+    }
+    a.nact = p.nact;
     a.mat_stride = mat_stride;
     a.out_stride = out_stride;
     a.tiles_per_mat = tiles;
     a.max_slots = max_slots;
     a.n_expert = n_expert;
-    a.n_ff = (uint32_t)n_ff;
-    a.gu = gu;
-    a.gu_stride = gu_stride;
+    a.gu = h;
+    a.gu_stride = h_stride;
     CK(launch_pdl((const void *)p.fn, p.grid, p.warps * 32, p.smem, stream, &a));
     return SG_OK;
 }
 
-sg_status launch_router(const sg_moe *m, const float *x, sg_moe_choice *sel, sg_moe_choice *shsel, float *scale,
-                        float *probs, cudaStream_t stream) {
+// Router logits over the whole GPU (a few rows per CTA), plus one CTA for the
+// shared expert's gate and one-slot choice when the layer has a shared expert.
+sg_status launch_router(const sg_moe *m, const float *x, float *logits, uint8_t *qx, sg_moe_choice *shsel, float *scale,
+                        cudaStream_t stream) {
     static std::atomic<uint64_t> attr_done{0};  // bit d: the smem attribute is set on device d
     int dev;
     CK(cudaGetDevice(&dev));
@@ -558,43 +597,31 @@ sg_status launch_router(const sg_moe *m, const float *x, sg_moe_choice *sel, sg_
                                 227 * 1024));
         attr_done.fetch_or(1ull << dev);
     }
+    DevInfo *di;
+    sg_status st = dev_info(&di);
+    if (st) return st;
     RouterArgs a;
     memset(&a, 0, sizeof a);
     a.w = m->router;
     a.x = x;
     a.dim = (uint32_t)m->dim;
     a.n_expert = (uint32_t)m->n_expert;
-    a.n_used = (uint32_t)m->n_used;
-    a.rows_per_cta = (a.n_expert + ROUTER_CLUSTER - 1) / ROUTER_CLUSTER;
-    // as many rows per ring stage as 200 KB of shared memory hold (at most 16)
-    uint32_t rc = a.rows_per_cta < 16 ? a.rows_per_cta : 16;
-    while (rc > 1 && router_smem_bytes(a.dim, rc, a.rows_per_cta, a.n_expert) > 200 * 1024) rc--;
-    const uint32_t smem = router_smem_bytes(a.dim, rc, a.rows_per_cta, a.n_expert);
+    // about one CTA per SM; fewer rows per CTA when they do not fit in 200 KB
+    uint32_t rpc = (a.n_expert + di->sms - 1) / di->sms;
+    if (rpc > ROUTER_MAX_ROWS) rpc = ROUTER_MAX_ROWS;
+    while (rpc > 1 && router_smem_bytes(a.dim, rpc) > 200 * 1024) rpc--;
+    const uint32_t smem = router_smem_bytes(a.dim, rpc);
     if (smem > 227 * 1024) return SG_ERR_SHAPE;
-    a.rc = rc;
-    a.norm = m->norm;
-    a.prune = m->moe_prune;
-    a.probs = probs;
-    a.sel = sel;
-    a.shared_sel = m->shared_gate_up ? shsel : nullptr;
-    a.shared_gate = m->shared_gate_up ? m->shared_gate : nullptr;
-    a.shared_scale = m->shared_gate_up ? scale : nullptr;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(ROUTER_CLUSTER);
-    cfg.blockDim = dim3(ROUTER_THREADS);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = ROUTER_CLUSTER;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    void *params[] = {&a};
-    CK(cudaLaunchKernelExC(&cfg, (const void *)moe_router_kernel, params));
+    a.rows_per_cta = rpc;
+    a.row_ctas = (a.n_expert + rpc - 1) / rpc;
+    a.logits = logits;
+    a.qx = qx;
+    const bool sh = m->shared_gate_up != nullptr;
+    a.shared_sel = sh ? shsel : nullptr;
+    a.shared_gate = sh ? m->shared_gate : nullptr;
+    a.shared_scale = sh ? scale : nullptr;
+    const uint32_t threads = (8 * rpc + 31) / 32 * 32;
+    CK(launch_pdl((const void *)moe_router_kernel, a.row_ctas + (sh ? 1 : 0), threads, smem, stream, &a));
     return SG_OK;
 }
 
@@ -876,11 +903,12 @@ sg_status sg_moe_pack_gate_up(int32_t dtype, const uint8_t *d_gate_exps, const u
     if (!d_gate_exps || !d_up_exps || !d_out || !n_expert || !n_ff) return SG_ERR_INVALID;
     if (!kquant(dtype)) return SG_ERR_DTYPE;
     if (!cols_ok(dim)) return SG_ERR_SHAPE;
-    const uint64_t stride = tiled_bytes(dtype, 2 * n_ff, dim), drows = align_up(2 * n_ff, TILE_ROWS);
-    CK(cudaMemsetAsync(d_out, 0, stride * n_expert, (cudaStream_t)stream));  // zero padding rows
-    sg_status st = pack_experts(dtype, d_gate_exps, n_expert, n_ff, dim, drows, 0, d_out, (cudaStream_t)stream);
+    if (n_ff % 8) return SG_ERR_SHAPE;
+    // gate row i of an expert -> packed row 16 * (i / 8) + i % 8, up row i ->
+    // the same + 8 (every row of every tile is written: no padding)
+    sg_status st = pack_experts(dtype, d_gate_exps, n_expert * n_ff / 8, 8, dim, 16, 0, d_out, (cudaStream_t)stream);
     if (st) return st;
-    return pack_experts(dtype, d_up_exps, n_expert, n_ff, dim, drows, n_ff, d_out, (cudaStream_t)stream);
+    return pack_experts(dtype, d_up_exps, n_expert * n_ff / 8, 8, dim, 16, 8, d_out, (cudaStream_t)stream);
 }
 
 sg_status sg_moe_pack_down(int32_t dtype, const uint8_t *d_down_exps, uint64_t n_expert, uint64_t dim,
@@ -910,24 +938,28 @@ sg_status sg_moe_forward(const sg_moe *m, const float *d_x, float *d_out, void *
     uint8_t *sc = (uint8_t *)d_scratch;
     sg_moe_choice *sel = d_choice ? d_choice : (sg_moe_choice *)(sc + L.sel);
     sg_moe_choice *shsel = (sg_moe_choice *)(sc + L.shsel);
-    float *scale = (float *)(sc + L.scale), *gu = (float *)(sc + L.gu), *y = (float *)(sc + L.y);
-    float *gush = (float *)(sc + L.gush), *ysh = (float *)(sc + L.ysh);
+    float *scale = (float *)(sc + L.scale), *y = (float *)(sc + L.y);
+    float *logits = (float *)(sc + L.logits), *h = (float *)(sc + L.h);
+    float *hsh = (float *)(sc + L.hsh), *ysh = (float *)(sc + L.ysh);
+    uint8_t *qx = sc + L.qx;
     const bool sh = m->shared_gate_up != nullptr;
     const uint32_t k = (uint32_t)m->n_used, ne = (uint32_t)m->n_expert;
-    // Order matters for the dependent launches: every grouped GEMV starts
-    // after the router has completed (see gemv_tiled_kernel's MoE prologue).
-    if ((st = launch_router(m, d_x, sel, shsel, scale, d_probs, s))) return st;
+    // Each kernel waits for the one before it (programmatic dependent launch):
+    // router -> [shared gate/up] -> gate/up (makes the choice, publishes it in
+    // sel) -> down -> [shared down] -> combine.
+    if ((st = launch_router(m, d_x, logits, qx, shsel, scale, s))) return st;
     if (sh && (st = launch_moe_group(m->shared_gate_up_dtype, IN_MOE_X, m->shared_gate_up, 0, 2 * m->shared_n_ff,
-                                     m->dim, 1, 1, shsel, d_x, nullptr, 0, 0, gush, 0, s)))
+                                     m->dim, 1, 1, shsel, nullptr, d_x, qx, nullptr, 0, hsh, 0, s)))
         return st;
+    const MoeRoute route = {logits, sel, d_probs, k, m->norm, m->moe_prune};
     if ((st = launch_moe_group(m->gate_up_dtype, IN_MOE_X, m->gate_up, m->gate_up_stride, 2 * m->n_ff, m->dim, k,
-                               ne, sel, d_x, nullptr, 0, 0, gu, 2 * m->n_ff, s)))
+                               ne, sel, &route, d_x, qx, nullptr, 0, h, m->n_ff, s)))
         return st;
     if ((st = launch_moe_group(m->down_dtype, IN_MOE_H, m->down, m->down_stride, m->dim, m->n_ff, k, ne, sel,
-                               nullptr, gu, 2 * m->n_ff, m->n_ff, y, m->dim, s)))
+                               nullptr, nullptr, nullptr, h, m->n_ff, y, m->dim, s)))
         return st;
     if (sh && (st = launch_moe_group(m->shared_down_dtype, IN_MOE_H, m->shared_down, 0, m->dim, m->shared_n_ff, 1, 1,
-                                     shsel, nullptr, gush, 2 * m->shared_n_ff, m->shared_n_ff, ysh, 0, s)))
+                                     shsel, nullptr, nullptr, nullptr, hsh, m->shared_n_ff, ysh, 0, s)))
         return st;
     CombineArgs c;
     c.sel = sel;

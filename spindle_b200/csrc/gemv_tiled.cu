@@ -1,6 +1,7 @@
 // gemv_tiled.cu — kernels over the TILED16 layout (see gemv_tiled.cuh).
 #include "q8k_block.cuh"
 #include "tiled_block.cuh"
+#include "moe_select.cuh"
 
 namespace sg {
 using namespace tiled;
@@ -13,41 +14,19 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     // A launch whose shared memory cannot hold this layout records an error
     // and does nothing (uniform exit, before any barrier).
     const uint32_t nwarps = blockDim.x >> 5;
-    if (tiled_smem_bytes(nwarps, a.S, a.nstages, a.stage_bytes, a.slot_blocks, NV, a.nb,
-                         tiled_nact(MODE, NV, a.max_slots), tiled_extra(MODE, nwarps)) > dynamic_smem_size() ||
+    const uint32_t nact = tiled_nact(MODE, NV, a.nact);
+    if (tiled_smem_bytes(nwarps, a.S, a.nstages, a.stage_bytes, a.slot_blocks, NV, a.nb, nact) >
+            dynamic_smem_size() ||
         a.bc == 0 || a.stage_bytes < a.bc * CB || a.S == 0 || nwarps % a.S || (blockDim.x & 31) ||
-        a.nstages * nwarps * 8 > (MOE ? MOE_SEL_OFF : TGEMV_BAR_BYTES) ||
-        (MOE && (a.max_slots > MOE_MAXK || a.tiles_per_mat == 0))) {
+        a.nstages * nwarps * 8 > (MOE ? MOE_QX_BAR_OFF : TGEMV_BAR_BYTES) ||
+        (MOE && a.swiglu && (MODE != IN_MOE_X || a.nvec != 1)) ||
+        (MOE && (a.max_slots > MOE_MAXK || a.tiles_per_mat == 0 || nact == 0 ||
+                 (uint64_t)a.ntiles * gridDim.x >= (1ull << 32) || a.ntiles < a.max_slots * a.tiles_per_mat)) ||
+        (MODE == IN_MOE_X && a.logits &&
+         (a.n_expert == 0 || a.n_used == 0 || a.n_used > a.n_expert || a.n_used > MOE_MAXK ||
+          moe_select_bytes(a.n_expert) > nwarps * a.nstages * a.stage_bytes))) {
         if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
         return;
-    }
-    uint32_t ntiles = a.ntiles;
-    const int32_t *sids = reinterpret_cast<const int32_t *>(smem + MOE_SEL_OFF + 64);
-    if constexpr (MOE) {
-        // The expert choice is the router's.  IN_MOE_X runs right after the
-        // router: wait for it.  IN_MOE_H runs after IN_MOE_X, which lets it
-        // launch only once every CTA of IN_MOE_X has waited for the router, so
-        // the choice is already in memory: read it past L1 without waiting,
-        // and prefetch the chosen experts' weights before waiting for h.
-        if constexpr (MODE == IN_MOE_X) grid_dependency_wait();
-        grid_launch_dependents();
-        if (threadIdx.x < 32) {
-            uint32_t *sm = reinterpret_cast<uint32_t *>(smem + MOE_SEL_OFF);
-            const uint32_t n = min(__ldcg(&a.sel->n), a.max_slots);
-            const int32_t id = threadIdx.x < n ? __ldcg(&a.sel->id[threadIdx.x]) : 0;
-            const bool bad = __any_sync(0xffffffffu, threadIdx.x < n && (id < 0 || (uint32_t)id >= a.n_expert));
-            if (threadIdx.x < MOE_MAXK) sm[16 + threadIdx.x] = (uint32_t)id;
-            if (threadIdx.x == 0) {
-                sm[0] = bad ? 0u : n;
-                if (bad) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
-            }
-        }
-        __syncthreads();
-        ntiles = *reinterpret_cast<const uint32_t *>(smem + MOE_SEL_OFF) * a.tiles_per_mat;
-    } else {
-        // Let the next kernel in the stream launch as soon as SMs free up: it
-        // only prefetches its own weights before waiting for this grid to finish.
-        grid_launch_dependents();
     }
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t g = lane >> 4, r = lane & 15u;
@@ -55,63 +34,169 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     const uint32_t astride = act_bytes(a.nb);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * a.nstages;
     uint8_t *act = smem + TGEMV_BAR_BYTES;
-    uint8_t *rings = act + tiled_nact(MODE, NV, a.max_slots) * astride;
+    uint8_t *rings = act + nact * astride;
     uint8_t *ring = rings + warp * a.nstages * a.stage_bytes;
     const uint32_t worker_floats = a.slot_blocks * NV * CHAIN_FLOATS;
-    float *gscratch0 = reinterpret_cast<float *>(rings + nwarps * a.nstages * a.stage_bytes);
-    float *gscratch = gscratch0 + group * (S - 1) * worker_floats;
+    float *gscratch = reinterpret_cast<float *>(rings + nwarps * a.nstages * a.stage_bytes) +
+                      group * (S - 1) * worker_floats;
+
+    uint32_t ntiles = a.ntiles;
+    uint32_t *msel = reinterpret_cast<uint32_t *>(smem + MOE_SEL_OFF);  // [0]: n, [16..32): ids
+    const int32_t *sids = reinterpret_cast<const int32_t *>(msel + 16);
+    if constexpr (MOE) {
+        // The choice comes from the grids before this one: wait for them.
+        grid_dependency_wait();
+        grid_launch_dependents();
+        if (MODE == IN_MOE_X && a.qx_image && threadIdx.x == 0) {
+            // x's Q8_K image, ready-made by the router, lands while the choice is made
+            uint64_t *qbar = reinterpret_cast<uint64_t *>(smem + MOE_QX_BAR_OFF);
+            mbar_init(qbar, 1);
+            fence_mbar_init();
+            mbar_arrive_expect_tx(qbar, act_bytes(a.nb));
+            bulk_g2s(act, a.qx_image, act_bytes(a.nb), qbar);
+        }
+        if (MODE == IN_MOE_X && a.logits) {
+            // every CTA makes the router's choice itself (identical results);
+            // the rings are free until the first weight copy is issued
+            float *P = reinterpret_cast<float *>(rings);
+            int32_t *K = reinterpret_cast<int32_t *>(P + ((a.n_expert + 3u) & ~3u));
+            float *red = reinterpret_cast<float *>(K + ((a.n_expert + 3u) & ~3u));
+            moe::Choice *ch = reinterpret_cast<moe::Choice *>(red + 64);
+            float *probs = blockIdx.x == 0 ? a.probs : nullptr;
+            if (a.n_expert <= 256) {
+                // one warp, experts in registers
+                if (warp == 0) {
+                    if (a.n_expert <= 64)
+                        moe::select_warp<2>(a.logits, a.n_expert, a.n_used, a.norm, a.prune, ch, probs, P, lane);
+                    else if (a.n_expert <= 128)
+                        moe::select_warp<4>(a.logits, a.n_expert, a.n_used, a.norm, a.prune, ch, probs, P, lane);
+                    else
+                        moe::select_warp<8>(a.logits, a.n_expert, a.n_used, a.norm, a.prune, ch, probs, P, lane);
+                }
+                __syncthreads();
+            } else {
+                moe::select(a.logits, a.n_expert, a.n_used, a.norm, a.prune, P, K, red, ch, probs);
+            }
+            if (threadIdx.x < MOE_MAXK) {
+                msel[16 + threadIdx.x] = (uint32_t)ch->id[threadIdx.x];
+                if (blockIdx.x == 0) {
+                    a.sel_out->id[threadIdx.x] = ch->id[threadIdx.x];
+                    a.sel_out->weight[threadIdx.x] = ch->w[threadIdx.x];
+                }
+            }
+            if (threadIdx.x == 0) {
+                msel[0] = min(ch->n, a.max_slots);
+                if (blockIdx.x == 0) {
+                    a.sel_out->pad_[0] = a.sel_out->pad_[1] = a.sel_out->pad_[2] = 0;
+                    a.sel_out->n = ch->n;
+                }
+            }
+            fence_proxy_async();  // generic writes to the rings before the copies into them
+        } else if (threadIdx.x < 32) {
+            const uint32_t n = min(__ldcg(&a.sel->n), a.max_slots);
+            const int32_t id = threadIdx.x < n ? __ldcg(&a.sel->id[threadIdx.x]) : 0;
+            const bool bad = __any_sync(0xffffffffu, threadIdx.x < n && (id < 0 || (uint32_t)id >= a.n_expert));
+            if (threadIdx.x < MOE_MAXK) msel[16 + threadIdx.x] = (uint32_t)id;
+            if (threadIdx.x == 0) {
+                msel[0] = bad ? 0u : n;
+                if (bad) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+            }
+        }
+        __syncthreads();
+        ntiles = msel[0] * a.tiles_per_mat;
+    } else {
+        // Let the next kernel in the stream launch as soon as SMs free up: it
+        // only prefetches its own weights before waiting for this grid to finish.
+        grid_launch_dependents();
+    }
     const uint32_t b_lo = a.nb * slot / S, nblk = a.nb * (slot + 1) / S - b_lo;
     const uint32_t bc = a.bc, nchunk = (nblk + bc - 1) / bc;  // stages per tile for this slot
-    // groups are numbered CTA-minor so that consecutive tiles land on different SMs
-    const uint32_t gid = group * gridDim.x + blockIdx.x, GW = gridDim.x * G;
-    const uint32_t my_tiles = gid < ntiles ? (ntiles - gid + GW - 1) / GW : 0u;
+    // This group's tiles: first, first + step, ... (my_tiles of them).  GEMV:
+    // groups are numbered CTA-minor so that consecutive tiles land on different
+    // SMs.  MoE: each CTA takes a contiguous range, so that it needs the
+    // activations of one or two slots only (slots s_lo..s_hi).
+    uint32_t first, step, my_tiles, s_lo = 0, s_hi = 0;
+    if constexpr (MOE) {
+        // 32-bit products: the entry check bounds ntiles * gridDim.x below 2^32
+        const uint32_t lo = ntiles * blockIdx.x / gridDim.x, hi = ntiles * (blockIdx.x + 1) / gridDim.x;
+        first = lo + group;
+        step = G;
+        my_tiles = first < hi ? (hi - first + G - 1) / G : 0u;
+        if (lo < hi) {
+            s_lo = lo / a.tiles_per_mat;
+            s_hi = (hi - 1) / a.tiles_per_mat;
+        }
+        if (MODE == IN_MOE_H && lo < hi && s_hi - s_lo + 1 > nact) {  // the host sized nact for this
+            if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+            my_tiles = 0;
+            s_hi = s_lo;
+        }
+    } else {
+        const uint32_t gid = group * gridDim.x + blockIdx.x;
+        first = a.t0 + gid;
+        step = gridDim.x * G;
+        my_tiles = gid < ntiles ? (ntiles - gid + step - 1) / step : 0u;
+    }
     const uint32_t nitems = my_tiles * nchunk;
     const uint64_t tile_bytes = (uint64_t)a.nb * CB;
     const uint32_t bar_full = 1 + group, bar_free = 1 + G + group, nbar = 32 * S;
 
-    // item k = chunk k % nchunk (bc super-blocks) of this group's tile k / nchunk
-    auto issue = [&](uint32_t k) {
-        const uint32_t tt = a.t0 + gid + (k / nchunk) * GW, c = k % nchunk;
-        const uint32_t nbytes = min(bc, nblk - c * bc) * CB;
-        const uint8_t *tile;
+    // Item k = chunk k % nchunk (bc super-blocks) of this group's tile k / nchunk.
+    // Lane 0 issues the items in order; (ic, itt, itile, ist) follow the next
+    // one so that no issue divides.
+    auto tile_ptr = [&](uint32_t tt) -> const uint8_t * {
         if constexpr (MOE) {
             const uint32_t s = tt / a.tiles_per_mat;
-            tile = a.w + (uint64_t)sids[s] * a.mat_stride + (uint64_t)(tt - s * a.tiles_per_mat) * tile_bytes;
+            return a.w + (uint64_t)sids[s] * a.mat_stride + (uint64_t)(tt - s * a.tiles_per_mat) * tile_bytes;
         } else {
-            tile = a.w + tt * tile_bytes;
+            return a.w + tt * tile_bytes;
         }
-        uint64_t *bar = &bars[k % a.nstages];
-        mbar_arrive_expect_tx(bar, nbytes);
-        bulk_g2s(ring + (k % a.nstages) * a.stage_bytes, tile + (uint64_t)(b_lo + c * bc) * CB, nbytes, bar);
     };
-    // Weights do not depend on the previous kernel: start streaming them first.
+    uint32_t ic = 0, itt = first, ist = 0, iss = 0;
+    const uint8_t *itile = nullptr;
+    auto issue_next = [&]() {
+        if (ic == 0) itile = tile_ptr(itt);
+        const uint32_t nbytes = min(bc, nblk - ic * bc) * CB;
+        uint64_t *bar = &bars[ist];
+        mbar_arrive_expect_tx(bar, nbytes);
+        bulk_g2s(ring + ist * a.stage_bytes, itile + (uint64_t)(b_lo + ic * bc) * CB, nbytes, bar);
+        iss++;
+        if (++ist == a.nstages) ist = 0;
+        if (++ic == nchunk) {
+            ic = 0;
+            itt += step;
+        }
+    };
+    // GEMV: weights do not depend on the previous kernel, so they stream first.
     if (lane == 0) {
         for (uint32_t st = 0; st < a.nstages; st++) mbar_init(&bars[st], 1);
         fence_mbar_init();
-        for (uint32_t k = 0; k < nitems && k < a.nstages; k++) issue(k);
+        while (iss < nitems && iss < a.nstages) issue_next();
     }
     // The activations do: wait for the grid that wrote them, then stage them.
     grid_dependency_wait();
     const uint32_t nb = a.nb;
+    bool failed = false;
     if constexpr (MODE == IN_MOE_H) {
-        // one warp per (slot, 256-block): h = silu(g) * up into a per-warp fp32
-        // block, then the exact Q8_K quantization of it
-        float *hb = gscratch0 + G * (S - 1) * worker_floats + warp * 256u;
-        const uint32_t nsel = ntiles / a.tiles_per_mat;
-        for (uint32_t wb = warp; wb < nsel * nb; wb += nwarps) {
-            const uint32_t s = wb / nb, b = wb % nb;
-            const float *gp = a.gu + s * a.gu_stride + 256u * b + 8u * lane;
-            const float4 g0 = *reinterpret_cast<const float4 *>(gp), g1 = *reinterpret_cast<const float4 *>(gp + 4);
-            const float4 u0 = *reinterpret_cast<const float4 *>(gp + a.n_ff);
-            const float4 u1 = *reinterpret_cast<const float4 *>(gp + a.n_ff + 4);
-            reinterpret_cast<float4 *>(hb)[2 * lane] =
-                make_float4(silu_mul(g0.x, u0.x), silu_mul(g0.y, u0.y), silu_mul(g0.z, u0.z), silu_mul(g0.w, u0.w));
-            reinterpret_cast<float4 *>(hb)[2 * lane + 1] =
-                make_float4(silu_mul(g1.x, u1.x), silu_mul(g1.y, u1.y), silu_mul(g1.z, u1.z), silu_mul(g1.w, u1.w));
-            __syncwarp();
-            uint8_t *av = act + s * astride;
-            q8k_block(hb, reinterpret_cast<int8_t *>(av + 256u * b), reinterpret_cast<int16_t *>(av + 256u * nb + 32u * b),
+        // one warp per (slot, 256-block) of this CTA's slots: the exact Q8_K
+        // quantization of h
+        for (uint32_t wb = warp; wb < (s_hi - s_lo + 1) * nb; wb += nwarps) {
+            const uint32_t s = s_lo + wb / nb, b = wb % nb;
+            uint8_t *av = act + (wb / nb) * astride;
+            q8k_block(a.gu + s * a.gu_stride + 256u * b, reinterpret_cast<int8_t *>(av + 256u * b),
+                      reinterpret_cast<int16_t *>(av + 256u * nb + 32u * b),
                       reinterpret_cast<float *>(av + 288u * nb + 4u * b), lane);
+        }
+    } else if (MODE == IN_MOE_X && a.qx_image) {
+        if (!mbar_wait_bounded(reinterpret_cast<uint64_t *>(smem + MOE_QX_BAR_OFF), 0, WAIT_LIMIT_NS)) {
+            // record it, let this warp's weight copies land (bounded), issue no
+            // more; the tile loop keeps its barrier protocol so the CTA exits
+            if (lane == 0) {
+                atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_TMA);
+                for (uint32_t p = 0; p < nitems && p < a.nstages; p++)
+                    mbar_wait_bounded(&bars[p], 0, WAIT_LIMIT_NS);
+            }
+            failed = true;
             __syncwarp();
         }
     } else if constexpr (MODE == IN_F32 || MODE == IN_MOE_X) {
@@ -137,17 +222,16 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     }
     __syncthreads();
 
-    bool failed = false;
     uint32_t k = 0;
     for (uint32_t ti = 0; ti < my_tiles; ti++) {
-        const uint32_t tt = a.t0 + gid + ti * GW;
+        const uint32_t tt = first + ti * step;
         // MoE: slot ms of the choice, tile mt of its matrix
         uint32_t ms = 0, mt = tt;
         if constexpr (MOE) {
             ms = tt / a.tiles_per_mat;
             mt = tt - ms * a.tiles_per_mat;
         }
-        const uint8_t *tact = MODE == IN_MOE_H ? act + ms * astride : act;
+        const uint8_t *tact = MODE == IN_MOE_H ? act + (ms - s_lo) * astride : act;
         float acc[NV][4], corr[NV];
 #pragma unroll
         for (int v = 0; v < NV; v++) {
@@ -205,7 +289,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
             __syncwarp();
             if (lane == 0 && !failed && k + a.nstages < nitems) {
                 fence_proxy_async();
-                issue(k + a.nstages);
+                issue_next();  // item k + nstages, into the stage just consumed
             }
         }
         if (S > 1) {
@@ -242,9 +326,17 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                 float x[4];
 #pragma unroll
                 for (int m = 0; m < 4; m++) x[m] = __fadd_rn(acc[v][m], __shfl_down_sync(0xffffffffu, acc[v][m], 16));
+                const float yv = __fsub_rn(__fadd_rn(__fadd_rn(x[0], x[2]), __fadd_rn(x[1], x[3])), corr[v]);
                 float *dst = MOE ? a.out[0] + ms * a.out_stride : a.out[v];
-                if (g == 0 && v < (int)a.nvec && row >= a.r0 && row < a.r1)
-                    dst[row] = __fsub_rn(__fadd_rn(__fadd_rn(x[0], x[2]), __fadd_rn(x[1], x[3])), corr[v]);
+                if (MODE == IN_MOE_X && a.swiglu) {
+                    // rows r < 8 are gate rows, rows r + 8 the up rows of the
+                    // same outputs: h = silu(gate) * up (smollm_chat.rs:357-359)
+                    const float up = __shfl_down_sync(0xffffffffu, yv, 8);
+                    const uint32_t j = mt * 8 + r;
+                    if (g == 0 && r < 8 && 2 * j < a.r1) dst[j] = silu_mul(yv, up);
+                } else if (g == 0 && v < (int)a.nvec && row >= a.r0 && row < a.r1) {
+                    dst[row] = yv;
+                }
             }
         }
     }

@@ -42,12 +42,22 @@ __host__ __device__ inline uint32_t act_bytes(uint32_t nb) { return nb * 256u + 
 //   IN_Q8K:   Q8_K vectors (xd, xs, xb).
 //   IN_F32:   fp32 vectors x, quantized to Q8_K by every CTA in shared memory
 //             (the reference's matvec = Q8K::quantize + matmul_rows in one kernel).
-//   IN_MOE_X: grouped over the experts the router chose (sel): launch tile tt is
-//             tile tt % tiles_per_mat of expert sel->id[tt / tiles_per_mat], whose
-//             matrix is at w + id * mat_stride; one fp32 vector x[0], quantized
-//             as in IN_F32; slot s's rows go to out[0] + s * out_stride.
-//   IN_MOE_H: grouped like IN_MOE_X; slot s's vector is h = silu(g) * up (g at
-//             gu + s * gu_stride, up n_ff floats after it), quantized per CTA.
+//   IN_MOE_X: grouped over the chosen experts: launch tile tt is tile
+//             tt % tiles_per_mat of expert id[tt / tiles_per_mat] (slot s =
+//             tt / tiles_per_mat), whose matrix is at w + id * mat_stride; one
+//             fp32 vector x[0], quantized as in IN_F32; slot s's rows go to
+//             out[0] + s * out_stride.  With `logits`, every CTA makes the
+//             choice itself from the router's logits (softmax, top-k, prune,
+//             weights) and CTA 0 publishes it in sel_out; without, it runs `sel`.
+//             With qx_image, x arrives already quantized (an act_bytes(nb)
+//             shared-memory image made by the router) in one bulk copy.
+//             With swiglu, each tile holds 8 gate rows then the 8 up rows of
+//             the same outputs, and the kernel writes h = silu(gate) * up
+//             (8 outputs per tile) instead of the 16 rows.
+//   IN_MOE_H: grouped like IN_MOE_X over `sel`; slot s's vector is the fp32
+//             h at gu + s * gu_stride, quantized by each CTA for the slots its
+//             tiles belong to.
+// In the MoE modes each CTA takes a contiguous range of the launch's tiles.
 constexpr int IN_Q8K = 0, IN_F32 = 1, IN_MOE_X = 2, IN_MOE_H = 3;
 constexpr uint32_t MOE_MAXK = SG_MOE_MAX_USED;
 
@@ -68,7 +78,16 @@ struct TGemvArgs {
     const int16_t *xb[TGEMV_MAXV];
     float *out[TGEMV_MAXV];
     // IN_MOE_X / IN_MOE_H only
-    const sg_moe_choice *sel;
+    const sg_moe_choice *sel;   // the choice to run (IN_MOE_H; IN_MOE_X without logits)
+    sg_moe_choice *sel_out;     // IN_MOE_X with logits: CTA 0 writes the choice here
+    const float *logits;        // IN_MOE_X: router logits [n_expert], or null
+    float *probs;               // optional: CTA 0 writes the softmax here
+    uint32_t n_used;            // top-k
+    int32_t norm;
+    float prune;
+    uint32_t nact;              // IN_MOE_H: activation images per CTA
+    uint32_t swiglu;            // IN_MOE_X: interleaved gate/up tiles, h out
+    const uint8_t *qx_image;    // IN_MOE_X: Q8_K image of x, or null
     uint64_t mat_stride;
     uint64_t out_stride;
     uint32_t tiles_per_mat;
@@ -79,24 +98,29 @@ struct TGemvArgs {
     uint64_t gu_stride;   // IN_MOE_H, floats
 };
 
-// In the MoE modes the router's choice is copied into the top of the barrier
-// area: n at MOE_SEL_OFF, ids after it.
+// In the MoE modes the choice is kept at the top of the barrier area: n at
+// MOE_SEL_OFF, ids 64 bytes after it; the barrier of the x image copy sits
+// just below (MOE_QX_BAR_OFF), and the rings' barriers below that.
 constexpr uint32_t MOE_SEL_OFF = TGEMV_BAR_BYTES - 128;
+constexpr uint32_t MOE_QX_BAR_OFF = MOE_SEL_OFF - 8;
 
-// Activation images staged per CTA, and per-warp fp32 staging for h (IN_MOE_H).
-__host__ __device__ inline uint32_t tiled_nact(int mode, uint32_t nv, uint32_t max_slots) {
-    return mode == IN_MOE_H ? max_slots : nv;
+// Shared memory the in-kernel expert choice borrows from the rings (before
+// any weight copy is issued): probabilities, sort keys and a little scratch.
+__host__ __device__ inline uint32_t moe_select_bytes(uint32_t n_expert) { return 2u * ((n_expert * 4u + 15u) & ~15u) + 512u; }
+
+// Activation images staged per CTA.
+__host__ __device__ inline uint32_t tiled_nact(int mode, uint32_t nv, uint32_t nact) {
+    return mode == IN_MOE_H ? nact : mode == IN_MOE_X ? 1u : nv;
 }
-__host__ __device__ inline uint32_t tiled_extra(int mode, uint32_t warps) { return mode == IN_MOE_H ? warps * 1024u : 0u; }
 
 // Dynamic shared memory of one CTA of `warps` warps:
-// barriers | activations (nact images) | rings | chain scratch | extra.
+// barriers | activations (nact images) | rings | chain scratch.
 __host__ __device__ inline uint32_t tiled_smem_bytes(uint32_t warps, uint32_t S, uint32_t nstages,
                                                      uint32_t stage_bytes, uint32_t slot_blocks, uint32_t nv,
-                                                     uint32_t nb, uint32_t nact, uint32_t extra) {
+                                                     uint32_t nb, uint32_t nact) {
     const uint32_t groups = warps / S;
     return TGEMV_BAR_BYTES + nact * act_bytes(nb) + warps * nstages * stage_bytes +
-           groups * (S - 1) * slot_blocks * nv * CHAIN_FLOATS * 4u + extra;
+           groups * (S - 1) * slot_blocks * nv * CHAIN_FLOATS * 4u;
 }
 
 template <int DT, int NV, int MODE>

@@ -1,13 +1,13 @@
 // moe.cuh — the top-k MoE layer of spindle (moe_forward, smollm_chat.rs:1178-1382,
 // with the fused expert FFNs of ffns_fused, :382-442) as a chain of kernels
 // on one stream, the expert choice staying on the device:
-//   1. moe_router_kernel: one cluster of ROUTER_CLUSTER CTAs.  Each CTA computes
-//      the logits of its share of the router rows (F32 GEMV with the lane order
-//      of dot_f32_2rows_avx2, quant.rs:1461-1483), the cluster syncs, and CTA 0
-//      gathers all logits through distributed shared memory and runs softmax,
-//      top-k, prune and the mixing weights (smollm_chat.rs:1199-1240).
-//   2. gemv_tiled_kernel<., 1, IN_MOE_X>: gate and up of every chosen expert.
-//   3. gemv_tiled_kernel<., 1, IN_MOE_H>: down of every chosen expert.
+//   1. moe_router_kernel: the router logits (F32 GEMV with the lane order of
+//      dot_f32_2rows_avx2, quant.rs:1461-1483), a few rows per CTA over the
+//      whole GPU; one more CTA computes the shared expert's gate.
+//   2. gemv_tiled_kernel<., 1, IN_MOE_X>: every CTA makes the choice from the
+//      logits (softmax, top-k, prune, weights: smollm_chat.rs:1199-1240), CTA 0
+//      publishes it, and the gate and up rows of the chosen experts run.
+//   3. gemv_tiled_kernel<., 1, IN_MOE_H>: down rows of the chosen experts.
 //   (2 and 3 again for the shared expert, with a one-slot choice.)
 //   4. moe_combine_kernel: out[r] = sum over the choice, in router order, of
 //      w_i * y_i[r] (smollm_chat.rs:431-438), plus g * shared[r] (:1370-1382).
@@ -17,37 +17,29 @@
 
 namespace sg {
 
-constexpr uint32_t ROUTER_CLUSTER = 8;   // CTAs of the router (one cluster)
-constexpr uint32_t ROUTER_THREADS = 128; // 16 rows at a time, 8 threads (AVX lanes) per row
 constexpr uint32_t ROUTER_MAX_EXPERTS = 4096;
 constexpr uint32_t ROUTER_ROW_PAD = 32;  // bytes between staged rows (spreads rows over banks)
+constexpr uint32_t ROUTER_MAX_ROWS = 16; // rows per CTA (8 threads each)
 
 struct RouterArgs {
-    const float *w;        // F32 [n_expert][dim]
-    const float *x;        // [dim]
-    uint32_t dim, n_expert, n_used;
-    uint32_t rows_per_cta; // ceil(n_expert / ROUTER_CLUSTER)
-    uint32_t rc;           // rows per ring stage (<= 16)
-    int32_t norm;
-    float prune;
-    float *probs;          // optional: softmax probabilities [n_expert]
-    sg_moe_choice *sel;
-    sg_moe_choice *shared_sel;  // optional: written as {1, id 0, weight 1}
-    const float *shared_gate;   // optional F32 [dim]
+    const float *w;             // F32 [n_expert][dim]
+    const float *x;             // [dim]
+    uint32_t dim, n_expert;
+    uint32_t rows_per_cta;      // CTA b < row_ctas computes rows [b * rows_per_cta, ...)
+    uint32_t row_ctas;
+    float *logits;              // [n_expert]
+    uint8_t *qx;                // optional: Q8_K image of x (act_bytes(dim / 256) bytes)
+    // shared expert (CTA row_ctas, when shared_scale is set)
+    sg_moe_choice *shared_sel;  // written as {1, id 0, weight 1}
+    const float *shared_gate;   // F32 [dim] or null
     float *shared_scale;        // sigmoid(shared_gate . x), or 1 without a gate
 };
 
-// bars (64) | x (dim floats) | shared gate (dim floats) | ring: 2 stages of rc rows | logits
+// bars (64) | x (dim floats) | rows (rows_per_cta, padded) ; the gate CTA puts
+// the gate vector where the rows go.
 __host__ __device__ inline uint32_t router_row_stride(uint32_t dim) { return dim * 4u + ROUTER_ROW_PAD; }
-__host__ __device__ inline uint32_t router_ring_bytes(uint32_t dim, uint32_t rc, uint32_t n_expert) {
-    const uint32_t ring = 2u * rc * router_row_stride(dim);
-    // CTA 0 reuses the ring for the softmax (probabilities and sort keys)
-    const uint32_t sel_area = n_expert * 8u + 256u;
-    return ring > sel_area ? ring : sel_area;
-}
-__host__ __device__ inline uint32_t router_smem_bytes(uint32_t dim, uint32_t rc, uint32_t rows_per_cta,
-                                                      uint32_t n_expert) {
-    return 64u + 2u * dim * 4u + router_ring_bytes(dim, rc, n_expert) + ((rows_per_cta * 4u + 15u) & ~15u);
+__host__ __device__ inline uint32_t router_smem_bytes(uint32_t dim, uint32_t rows_per_cta) {
+    return 64u + dim * 4u + (rows_per_cta ? rows_per_cta : 1u) * router_row_stride(dim);
 }
 
 struct CombineArgs {

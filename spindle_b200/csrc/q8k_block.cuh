@@ -4,7 +4,9 @@
 //
 // amax: the reference keeps 8 running MAXPS lanes (lane j sees x[j], x[j+8],
 // ...; MAXPS returns its second operand when either is NaN), then folds
-// hi->lo, 2->0, 1->0; lanes 0..7 replay exactly that.  Each value becomes
+// hi->lo, 2->0, 1->0.  Without a NaN in the block that is the plain maximum,
+// whatever the order; a NaN makes a lane keep only what follows its last NaN,
+// so that (rare) case replays the lane folds in order.  Each value becomes
 // cvtps_epi32(x * (127/amax)) saturated to int8 by two packs: round to
 // nearest even, and NaN or |v| >= 2^31 give INT32_MIN, i.e. -128.
 // d = amax/127 and 127/amax are correctly rounded divisions.
@@ -22,16 +24,41 @@ __device__ __forceinline__ int8_t cvt_pack_i8(float v) {
     return (int8_t)(q > 127 ? 127 : (q < -128 ? -128 : q));
 }
 
-// xb: 256 floats (16-byte aligned, global or shared); qs: 256 int8 (8-byte
-// aligned); bsums: 16 int16; d: one float.  All 32 lanes of the warp call it.
-__device__ __forceinline__ void q8k_block(const float *xb, int8_t *qs, int16_t *bsums, float *d, uint32_t lane) {
+// The block's amax; lane t holds x[8t .. 8t+7] in xv (so xv[j] is element t
+// of AVX lane j).  Returned to every lane.
+__device__ __forceinline__ float q8k_amax(const float (&xv)[8], uint32_t lane) {
+    bool nan = false;
+#pragma unroll
+    for (int k = 0; k < 8; k++) nan |= isnan(xv[k]);
+    if (!__any_sync(0xffffffffu, nan)) {
+        float m = fabsf(xv[0]);
+#pragma unroll
+        for (int k = 1; k < 8; k++) m = fmaxf(m, fabsf(xv[k]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        return m;
+    }
+    // in-order replay: lane j < 8 folds x[j], x[j+8], ..., fetched from lane m
     float lm = 0.0f;
-    if (lane < 8)
-        for (int m = 0; m < 32; m++) lm = maxps(lm, fabsf(xb[8 * m + lane]));
+    for (int m = 0; m < 32; m++) {
+        float v = 0.0f;
+#pragma unroll
+        for (int jj = 0; jj < 8; jj++) {
+            const float t = __shfl_sync(0xffffffffu, xv[jj], m);
+            if (jj == (int)(lane & 7u)) v = t;
+        }
+        lm = maxps(lm, fabsf(v));
+    }
     const float v4 = maxps(lm, __shfl_down_sync(0xffffffffu, lm, 4));
     const float v2 = maxps(v4, __shfl_down_sync(0xffffffffu, v4, 2));
-    const float amax = __shfl_sync(0xffffffffu, maxps(v2, __shfl_down_sync(0xffffffffu, v2, 1)), 0);
+    return __shfl_sync(0xffffffffu, maxps(v2, __shfl_down_sync(0xffffffffu, v2, 1)), 0);
+}
 
+// Values in registers (lane t: x[8t .. 8t+7]); qs: 256 int8 (8-byte aligned);
+// bsums: 16 int16; d: one float.  All 32 lanes of the warp call it.
+__device__ __forceinline__ void q8k_block_regs(const float (&xv)[8], int8_t *qs, int16_t *bsums, float *d,
+                                               uint32_t lane) {
+    const float amax = q8k_amax(xv, lane);
     int8_t q[8];
     if (!(amax > 0.0f) || isinf(amax)) {
 #pragma unroll
@@ -40,9 +67,6 @@ __device__ __forceinline__ void q8k_block(const float *xb, int8_t *qs, int16_t *
     } else {
         const float inv = __fdiv_rn(127.0f, amax);
         if (lane == 0) *d = __fdiv_rn(amax, 127.0f);
-        const float4 p0 = reinterpret_cast<const float4 *>(xb)[2 * lane];
-        const float4 p1 = reinterpret_cast<const float4 *>(xb)[2 * lane + 1];
-        const float xv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
         for (int k = 0; k < 8; k++) q[k] = cvt_pack_i8(__fmul_rn(xv[k], inv));
     }
@@ -58,6 +82,14 @@ __device__ __forceinline__ void q8k_block(const float *xb, int8_t *qs, int16_t *
     reinterpret_cast<uint2 *>(qs)[lane] = make_uint2(w0, w1);
     s += __shfl_xor_sync(0xffffffffu, s, 1);  // a group of 16 values = lanes 2g, 2g+1
     if ((lane & 1u) == 0) bsums[lane / 2] = (int16_t)s;
+}
+
+// xb: 256 floats (16-byte aligned, global or shared), read once.
+__device__ __forceinline__ void q8k_block(const float *xb, int8_t *qs, int16_t *bsums, float *d, uint32_t lane) {
+    const float4 p0 = reinterpret_cast<const float4 *>(xb)[2 * lane];
+    const float4 p1 = reinterpret_cast<const float4 *>(xb)[2 * lane + 1];
+    const float xv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+    q8k_block_regs(xv, qs, bsums, d, lane);
 }
 
 }  // namespace sg

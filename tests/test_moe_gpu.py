@@ -118,6 +118,9 @@ def compare(L, x, dev, norm=True, prune=0.0):
     (1024, 512, 8, 2, O.Q4_K, O.Q4_K),    # Mixtral-like top-2 of 8
     (768, 1024, 64, 6, O.Q6_K, O.Q6_K),
     (256, 256, 4, 1, O.Q6_K, O.Q4_K),
+    (256, 256, 100, 8, O.Q4_K, O.Q6_K),   # expert count not a multiple of 32
+    (256, 256, 200, 16, O.Q4_K, O.Q6_K),  # most experts a token may use
+    (256, 256, 300, 4, O.Q4_K, O.Q6_K),   # above 256 experts: the block-wide choice
 ])
 def test_moe_matches_oracle(dev, dim, ff, n_exp, k, gu, dn):
     L = make_layer(dim + ff + n_exp, dim, ff, n_exp, k, gu, dn)
@@ -153,9 +156,10 @@ def test_moe_shared_expert(dev, gate):
 
 
 def test_moe_pack_matches_stacked_repack(dev):
-    # expert e of the packed gate/up buffer == TILED16 of [gate_e; up_e] (GGUF rows stacked)
-    # and expert e of the packed down buffer == TILED16 of down_e
-    dim, ff, n_exp = 512, 40, 3   # ff not a multiple of 16: tiles straddle gate and up
+    # expert e of the packed gate/up buffer == TILED16 of gate_e and up_e
+    # interleaved in groups of 8 rows (GGUF rows), and expert e of the packed
+    # down buffer == TILED16 of down_e
+    dim, ff, n_exp = 512, 40, 3
     rng = O.Rng(8)
     g = O.random_matrix(O.Q4_K, dim, ff * n_exp, rng)
     u = O.random_matrix(O.Q4_K, dim, ff * n_exp, rng)
@@ -167,7 +171,9 @@ def test_moe_pack_matches_stacked_repack(dev):
                                                n_exp, ff, dim, C.c_void_p(packed.data_ptr()), None), "pack")
     rb = O.row_bytes(O.Q4_K, dim)
     for e in range(n_exp):
-        stacked = np.concatenate([g[e * ff * rb:(e + 1) * ff * rb], u[e * ff * rb:(e + 1) * ff * rb]])
+        ge = g[e * ff * rb:(e + 1) * ff * rb].reshape(ff // 8, 8 * rb)
+        ue = u[e * ff * rb:(e + 1) * ff * rb].reshape(ff // 8, 8 * rb)
+        stacked = np.concatenate([ge, ue], axis=1).reshape(-1)
         want, _ = sg.repack_tiled16(O.Q4_K, t(stacked), 2 * ff, dim)
         assert torch.equal(packed[e * stride:(e + 1) * stride], want), e
     rows, n_ff = 24, 512          # down: 24 rows (padding inside each expert), 512 cols
