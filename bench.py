@@ -385,6 +385,248 @@ def run_gpu(args):
     return line, WG
 
 
+# ---- MoE layer workload (--workload moe) -------------------------------------
+# One step = one token through MOE_LAYERS distinct MoE layers of the
+# Qwen3-30B-A3B shape (128 experts, top 8, hidden 2048,
+# FFN 768, Q4_K gate/up, Q6_K down, F32 router with logits about N(0,1)),
+# each layer moe_forward (smollm_chat.rs:1178): router, softmax/top-k, the
+# chosen experts' SwiGLU FFNs, the weighted sum.  8 layers hold 3.1 GB of
+# experts, so the 24.5 MB a token reads per layer is not left in L2 by the
+# step before.
+
+MOE = dict(dim=2048, n_ff=768, n_expert=128, n_used=8, gu=Q4_K, dn=Q6_K)
+MOE_LAYERS = 8
+MOE_METRIC = "MoE layer decode: chosen-expert weight GB/s (Qwen3-30B-A3B layer, top-8 of 128)"
+
+
+def moe_layer_bytes(n_chosen):
+    """Algorithmic bytes of one token through one layer: F32 router, the chosen
+    experts' gate/up/down rows, the input and the output."""
+    d, f, ne = MOE["dim"], MOE["n_ff"], MOE["n_expert"]
+    per_expert = 2 * f * (d // 256) * BLK[MOE["gu"]] + d * (f // 256) * BLK[MOE["dn"]]
+    return ne * d * 4 + n_chosen * per_expert + 2 * d * 4
+
+
+def moe_host_layers(n_layers, seed=2000):
+    """Host weights of the MoE layers (numpy), seeded: router N(0, 1/dim) so
+    that logits of an N(0,1) input are about N(0,1); experts N(0, 0.02)."""
+    import numpy as np
+    import oracle as O
+    d, f, ne = MOE["dim"], MOE["n_ff"], MOE["n_expert"]
+    g = np.random.default_rng(seed)
+    layers = []
+    for _ in range(n_layers):
+        router = (g.standard_normal((ne, d), dtype=np.float32) / np.float32(np.sqrt(d))).astype(np.float32)
+        gate = O.quantize_weights(MOE["gu"], g.standard_normal((ne * f, d), dtype=np.float32) * np.float32(0.02))
+        up = O.quantize_weights(MOE["gu"], g.standard_normal((ne * f, d), dtype=np.float32) * np.float32(0.02))
+        down = O.quantize_weights(MOE["dn"], g.standard_normal((ne * d, f), dtype=np.float32) * np.float32(0.02))
+        layers.append((router, gate, up, down))
+    return layers
+
+
+def moe_oracle(layer):
+    import numpy as np
+    import oracle as O
+    router, gate, up, down = layer
+    d, f, ne = MOE["dim"], MOE["n_ff"], MOE["n_expert"]
+    parts = [np.ascontiguousarray(router, np.float32).reshape(-1).view(np.uint8), gate, up, down]
+    off = np.cumsum([0] + [p.nbytes for p in parts])
+    moe = O.Moe(router=O.Mat(O.F32, d, ne, 0), gate=O.Mat(MOE["gu"], d, f, int(off[1])),
+                up=O.Mat(MOE["gu"], d, f, int(off[2])), down=O.Mat(MOE["dn"], f, d, int(off[3])), n_expert=ne,
+                n_used=MOE["n_used"], norm=1, moe_prune=0.0)
+    return np.concatenate(parts), moe
+
+
+def moe_cpu_sample(layers_host, budget_s):
+    """Times the oracle's moe_forward (one thread) token-layers for budget_s."""
+    import numpy as np
+    import oracle as O
+    bufs = [moe_oracle(l) for l in layers_host]
+    g = np.random.default_rng(11)
+    xs = [g.standard_normal(MOE["dim"], dtype=np.float32) for _ in range(16)]
+    O.moe_forward(bufs[0][0], bufs[0][1], xs[0])  # warm-up
+    t0, n, nbytes = time.perf_counter(), 0, 0
+    while True:
+        raw, moe = bufs[n % len(bufs)]
+        _, chosen, _ = O.moe_forward(raw, moe, xs[n % len(xs)])
+        nbytes += moe_layer_bytes(len(chosen))
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    el = time.perf_counter() - t0
+    return el / n, nbytes / el / 1e9, n
+
+
+def moe_config(world):
+    return {"workload": "moe_layer_decode_qwen3_30b_a3b", "layers_per_step": MOE_LAYERS,
+            "dim": MOE["dim"], "n_ff": MOE["n_ff"], "n_expert": MOE["n_expert"], "top_k": MOE["n_used"],
+            "gate_up": NAME[MOE["gu"]], "down": NAME[MOE["dn"]], "router": "F32", "moe_prune": 0.0,
+            "global_batch": world, "parallelism": "replicas x%d (weak)" % world,
+            "l2": "8 layers x 391 MB of experts > 126 MB L2: a layer's experts are evicted before its next step",
+            "weights": "router N(0,1/dim), experts N(0,0.02) seeded, own Q4_K/Q6_K quantizer",
+            "activations": "N(0,1) seeded, a different token per layer and step"}
+
+
+def run_reference_moe(args):
+    rank, world, _ = rank_env()
+    if rank != 0:
+        return
+    layers = moe_host_layers(1)
+    per_layer, gbs, n = moe_cpu_sample(layers, 2.0)
+    # each step: MOE_LAYERS token-layers; whole run within about two minutes
+    total = (args.steps + args.warmup) * MOE_LAYERS * per_layer
+    steps = args.steps if total <= 120 else max(1, int(120 / (MOE_LAYERS * per_layer)) - args.warmup)
+    per_layer, gbs, n = moe_cpu_sample(layers, per_layer * MOE_LAYERS * (steps + args.warmup))
+    line = {"impl": "reference", "metric": MOE_METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(per_layer * MOE_LAYERS * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8/int32 + fp32", "data": "synthetic", "config": moe_config(1),
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                             "sample": "%d token-layers through the oracle's moe_forward (C restatement of "
+                                       "smollm_chat.rs moe_forward/ffns_fused), one thread" % n},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_gpu_moe(args):
+    import torch
+    import torch.distributed as dist
+
+    import spindle_b200 as sg
+    from spindle_b200 import _lib
+
+    rank, world, local = rank_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    lib = sg.lib()
+    d, f, ne, k = MOE["dim"], MOE["n_ff"], MOE["n_expert"], MOE["n_used"]
+    gen = torch.Generator(device=dev).manual_seed(3000 + rank)
+    layers, host0 = [], None
+    for li in range(MOE_LAYERS):
+        router = torch.randn(ne, d, device=dev, generator=gen) / d ** 0.5
+        gq = sg.quantize_weights(MOE["gu"], torch.randn(ne * f, d, device=dev, generator=gen) * 0.02)
+        uq = sg.quantize_weights(MOE["gu"], torch.randn(ne * f, d, device=dev, generator=gen) * 0.02)
+        dq = sg.quantize_weights(MOE["dn"], torch.randn(ne * d, f, device=dev, generator=gen) * 0.02)
+        layers.append(sg.Moe.pack(router, gq, uq, dq, MOE["gu"], MOE["dn"], ne, k, d, f))
+        if li == 0:  # GGUF bytes of layer 0 for the CPU baseline
+            host0 = (router.cpu().numpy(), gq.cpu().numpy(), uq.cpu().numpy(), dq.cpu().numpy())
+        del gq, uq, dq
+    torch.cuda.synchronize()
+    nx = 64  # distinct tokens, so that the chosen experts change from step to step
+    X = torch.randn(nx, MOE_LAYERS, d, device=dev, generator=gen)
+    OUT = torch.empty(MOE_LAYERS, d, device=dev)
+    CH = torch.zeros(MOE_LAYERS, 36, dtype=torch.int32, device=dev)
+    scratch = [torch.empty(l.scratch_bytes(), dtype=torch.uint8, device=dev) for l in layers]
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(t):
+        for l in range(MOE_LAYERS):
+            sg.moe_forward(layers[l], X[t % nx, l], OUT[l], scratch[l], choice=CH[l], stream=stream)
+
+    with torch.cuda.stream(stream):
+        step(0)
+        torch.cuda.synchronize()
+        graphs = []
+        for t in range(nx):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step(t)
+            graphs.append(g)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            graphs[i % nx].replay()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(stream)
+            for i in range(args.steps):
+                graphs[i % nx].replay()
+            e1.record(stream)
+            e1.synchronize()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+        # bytes: the experts each layer actually chose (all n_used: no pruning)
+        n_ch = [int(c) for c in CH[:, 0].cpu()]
+        bytes_step = sum(moe_layer_bytes(n) for n in n_ch)
+
+        # e2e: host x -> device, moe_forward, device out -> host, per layer
+        h_x = torch.empty(nx, MOE_LAYERS, d, dtype=torch.float32).pin_memory()
+        h_x.copy_(X.cpu())
+        h_o = torch.empty(MOE_LAYERS, d, dtype=torch.float32).pin_memory()
+        sp = C.c_void_p(stream.cuda_stream)
+
+        def e2e_step(t):
+            for l in range(MOE_LAYERS):
+                _lib.check(lib.sg_memcpy_h2d(C.c_void_p(X[t % nx, l].data_ptr()), C.c_void_p(h_x[t % nx, l].data_ptr()),
+                                             d * 4, sp), "h2d")
+                sg.moe_forward(layers[l], X[t % nx, l], OUT[l], scratch[l], choice=CH[l], stream=stream)
+                _lib.check(lib.sg_memcpy_d2h(C.c_void_p(h_o[l].data_ptr()), C.c_void_p(OUT[l].data_ptr()), d * 4, sp),
+                           "d2h")
+
+        e2e_step(0)
+        torch.cuda.synchronize()
+        g_e2e = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_e2e, stream=stream):
+            e2e_step(1)
+        for _ in range(args.warmup):
+            g_e2e.replay()
+        barrier()
+        reps = max(3, min(args.steps, 2000))
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(stream)
+        for _ in range(reps):
+            g_e2e.replay()
+        b1.record(stream)
+        b1.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(b0.elapsed_time(b1)) / reps
+    sg.device_status()
+    value = bytes_step * world / (ms * 1e-3) / 1e9
+    peak, peak_src = None, "MEASURED_PEAKS.json hbm_gbs"
+    try:
+        peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"]
+    except Exception:
+        peak, peak_src = 6650.0, "fallback 6.65 TB/s"
+    line = None
+    if rank == 0:
+        achieved = bytes_step / (ms * 1e-3) / 1e9
+        line = {"metric": MOE_METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms, 5), "us_per_token_layer": round(ms * 1e3 / MOE_LAYERS, 2),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "int8 x int4/int6 -> int32, fp32 router/softmax/epilogue", "data": "synthetic",
+                "config": moe_config(world),
+                "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
+                             "kernel": "the 4-kernel MoE chain (router, gate/up, down, combine)",
+                             "how": "algorithmic bytes of the chosen experts + router per step / step time"},
+                "e2e": {"value": round(bytes_step * world / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                        "h2d_bytes_per_step": MOE_LAYERS * d * 4, "d2h_bytes_per_step": MOE_LAYERS * d * 4,
+                        "how": "per layer: sg_memcpy_h2d of x from pinned host, sg_moe_forward, sg_memcpy_d2h of out"},
+                "gpu_launches": 4 * MOE_LAYERS * args.steps,
+                "clocks": clk.summary()}
+    if world > 1:
+        dist.barrier()
+        del graphs, g_e2e
+        dist.destroy_process_group()
+    return line, host0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -398,9 +640,28 @@ def main():
     ap.add_argument("--shape", type=int, default=None, help="profiling: run only this sweep entry")
     ap.add_argument("--profile", action="store_true",
                     help="profiling: only the timed step loop (no e2e, per-shape or CPU legs)")
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "moe"],
+                    help="gemv: the headline K-quant GEMV sweep; moe: the Qwen3-30B-A3B MoE layer")
     args = ap.parse_args()
     if args.warmup < 3 and not args.profile:
         args.warmup = 3
+    if args.workload == "moe":
+        if args.steps == 20000:
+            args.steps = 2000  # one step is 8 token-layers
+        if args.impl == "reference":
+            run_reference_moe(args)
+            return
+        line, host0 = run_gpu_moe(args)
+        rank, world, _ = rank_env()
+        if rank == 0 and line is not None:
+            if world == 1 and args.cpu_budget > 0:
+                per_layer, gbs, n = moe_cpu_sample([host0], args.cpu_budget)
+                line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                                        "sample": "%d token-layers through the oracle's moe_forward (same layer "
+                                                  "shape, host-quantized weights), one thread, %.1f s"
+                                                  % (n, per_layer * n)}
+            print(json.dumps(line), flush=True)
+        return
     if args.shape is not None:
         SHAPES[:] = [SHAPES[args.shape]]
     if args.impl == "reference":
