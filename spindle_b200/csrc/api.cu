@@ -397,6 +397,12 @@ sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, 
         a.r0 = (uint32_t)r0;
         a.r1 = (uint32_t)r1;
         a.S = p.S;
+        a.s_log2 = ilog2u(p.S);
+        {
+            const uint32_t step = p.grid * (p.warps >> a.s_log2);  // tile groups in the grid
+            a.tiles_q = a.ntiles / step;
+            a.tiles_r = a.ntiles % step;
+        }
         a.bc = p.bc;
         a.nstages = p.nstages;
         a.stage_bytes = p.stage_bytes;
@@ -555,6 +561,7 @@ sg_status launch_moe_group(int32_t dtype, int mode, const uint8_t *w, uint64_t m
     a.ntiles = max_slots * tiles;
     a.r1 = (uint32_t)rows;
     a.S = p.S;
+    a.s_log2 = ilog2u(p.S);
     a.bc = p.bc;
     a.nstages = p.nstages;
     a.stage_bytes = p.stage_bytes;

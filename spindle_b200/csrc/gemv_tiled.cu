@@ -17,7 +17,8 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     const uint32_t nact = tiled_nact(MODE, NV, a.nact);
     if (tiled_smem_bytes(nwarps, a.S, a.nstages, a.stage_bytes, a.slot_blocks, NV, a.nb, nact) >
             dynamic_smem_size() ||
-        a.bc == 0 || a.stage_bytes < a.bc * CB || a.S == 0 || nwarps % a.S || (blockDim.x & 31) ||
+        a.bc == 0 || a.stage_bytes < a.bc * CB || a.S == 0 || a.S != (1u << a.s_log2) || a.S > nwarps ||
+        (nwarps & (a.S - 1)) || (blockDim.x & 31) ||
         a.nstages * nwarps * 8 > (MOE ? MOE_QX_BAR_OFF : TGEMV_BAR_BYTES) ||
         (MOE && a.swiglu && (MODE != IN_MOE_X || a.nvec != 1)) ||
         (MOE && (a.max_slots > MOE_MAXK || a.tiles_per_mat == 0 || nact == 0 ||
@@ -30,7 +31,9 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     }
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t g = lane >> 4, r = lane & 15u;
-    const uint32_t S = a.S, group = warp / S, slot = warp % S, G = nwarps / S;
+    // S is a power of two: shifts and masks instead of divisions (a runtime
+    // division costs some twenty instructions, paid by every warp)
+    const uint32_t S = a.S, SL = a.s_log2, group = warp >> SL, slot = warp & (S - 1u), G = nwarps >> SL;
     const uint32_t astride = act_bytes(a.nb);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * a.nstages;
     uint8_t *act = smem + TGEMV_BAR_BYTES;
@@ -109,7 +112,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
         // only prefetches its own weights before waiting for this grid to finish.
         grid_launch_dependents();
     }
-    const uint32_t b_lo = a.nb * slot / S, nblk = a.nb * (slot + 1) / S - b_lo;
+    const uint32_t b_lo = (a.nb * slot) >> SL, nblk = ((a.nb * (slot + 1)) >> SL) - b_lo;
     const uint32_t bc = a.bc, nchunk = (nblk + bc - 1) / bc;  // stages per tile for this slot
     // This group's tiles: first, first + step, ... (my_tiles of them).  GEMV:
     // groups are numbered CTA-minor so that consecutive tiles land on different
@@ -135,7 +138,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
         const uint32_t gid = group * gridDim.x + blockIdx.x;
         first = a.t0 + gid;
         step = gridDim.x * G;
-        my_tiles = gid < ntiles ? (ntiles - gid + step - 1) / step : 0u;
+        my_tiles = a.tiles_q + (gid < a.tiles_r ? 1u : 0u);  // ceil((ntiles - gid) / step), host-divided
     }
     const uint32_t nitems = my_tiles * nchunk;
     const uint64_t tile_bytes = (uint64_t)a.nb * CB;
@@ -200,13 +203,33 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
             __syncwarp();
         }
     } else if constexpr (MODE == IN_F32 || MODE == IN_MOE_X) {
-        // one warp per (vector, 256-block): the exact Q8_K quantization
-        for (uint32_t wb = warp; wb < a.nvec * nb; wb += nwarps) {
-            const uint32_t v = wb / nb, b = wb % nb;
+        // one warp per (vector, 256-block): the exact Q8_K quantization.  A
+        // warp loads up to QB of its blocks at once, so that the whole of x is
+        // in flight in one round instead of one L2 round trip per block.
+        constexpr int QB = 2;
+        for (uint32_t v = 0; v < a.nvec; v++) {
             uint8_t *av = act + v * astride;
-            q8k_block(a.x[v] + 256u * b, reinterpret_cast<int8_t *>(av + 256u * b),
-                      reinterpret_cast<int16_t *>(av + 256u * nb + 32u * b),
-                      reinterpret_cast<float *>(av + 288u * nb + 4u * b), lane);
+            for (uint32_t b0 = warp; b0 < nb; b0 += nwarps * QB) {
+                float xv[QB][8];
+#pragma unroll
+                for (int j = 0; j < QB; j++) {
+                    const uint32_t b = b0 + j * nwarps;
+                    if (b < nb) {
+                        const float4 *xp = reinterpret_cast<const float4 *>(a.x[v] + 256u * b) + 2 * lane;
+                        const float4 p0 = xp[0], p1 = xp[1];
+                        xv[j][0] = p0.x, xv[j][1] = p0.y, xv[j][2] = p0.z, xv[j][3] = p0.w;
+                        xv[j][4] = p1.x, xv[j][5] = p1.y, xv[j][6] = p1.z, xv[j][7] = p1.w;
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < QB; j++) {
+                    const uint32_t b = b0 + j * nwarps;
+                    if (b < nb)
+                        q8k_block_regs(xv[j], reinterpret_cast<int8_t *>(av + 256u * b),
+                                       reinterpret_cast<int16_t *>(av + 256u * nb + 32u * b),
+                                       reinterpret_cast<float *>(av + 288u * nb + 4u * b), lane);
+                }
+            }
         }
     } else {
         for (uint32_t v = 0; v < a.nvec; v++) {
@@ -222,7 +245,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     }
     __syncthreads();
 
-    uint32_t k = 0;
+    uint32_t k = 0, kst = 0, kph = 0;  // item k's ring stage and mbarrier phase
     for (uint32_t ti = 0; ti < my_tiles; ti++) {
         const uint32_t tt = first + ti * step;
         // MoE: slot ms of the choice, tile mt of its matrix
@@ -242,9 +265,13 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
         float *mine = gscratch + (slot ? (slot - 1) * worker_floats : 0u);
         if (slot > 0 && ti > 0) named_sync(bar_free, nbar);  // slot 0 has read the previous tile
         for (uint32_t c = 0; c < nchunk; c++, k++) {
-            const uint32_t st = k % a.nstages;
+            const uint32_t st = kst, ph = kph;  // = k % nstages, (k / nstages) & 1
+            if (++kst == a.nstages) {
+                kst = 0;
+                kph ^= 1u;
+            }
             if (!failed) {
-                const bool ok = mbar_wait_bounded(&bars[st], (k / a.nstages) & 1u, WAIT_LIMIT_NS);
+                const bool ok = mbar_wait_bounded(&bars[st], ph, WAIT_LIMIT_NS);
                 if (__any_sync(0xffffffffu, !ok)) {
                     // Record the timeout, let copies in flight land (bounded), stop
                     // issuing; keep the barrier protocol so the CTA still exits.
@@ -300,7 +327,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                 // continue the chain over the other slots' blocks, in block order
                 for (uint32_t ws = 1; ws < S; ws++) {
                     const float *src = gscratch + (ws - 1) * worker_floats;
-                    const uint32_t n_ws = a.nb * (ws + 1) / S - a.nb * ws / S;
+                    const uint32_t n_ws = ((a.nb * (ws + 1)) >> SL) - ((a.nb * ws) >> SL);
                     for (uint32_t q = 0; q < n_ws; q++)
 #pragma unroll
                         for (int v = 0; v < NV; v++) {

@@ -66,7 +66,9 @@ struct TGemvArgs {
     uint32_t nb;          // super-blocks per row
     uint32_t t0, ntiles;  // tiles t0 .. t0 + ntiles
     uint32_t r0, r1;      // rows written (others of the tiles are skipped)
-    uint32_t S;           // warps per tile (1, 2, 4 or 8)
+    uint32_t S;           // warps per tile (1, 2, 4, 8 or 16)
+    uint32_t s_log2;      // log2(S)
+    uint32_t tiles_q, tiles_r;  // GEMV: ntiles = tiles_q * (gridDim.x * warps / S) + tiles_r
     uint32_t bc;          // super-blocks per stage
     uint32_t nstages;
     uint32_t stage_bytes;
@@ -115,10 +117,19 @@ __host__ __device__ inline uint32_t tiled_nact(int mode, uint32_t nv, uint32_t n
 
 // Dynamic shared memory of one CTA of `warps` warps:
 // barriers | activations (nact images) | rings | chain scratch.
+__host__ __device__ inline uint32_t ilog2u(uint32_t v) {
+#ifdef __CUDA_ARCH__
+    return 31u - (uint32_t)__clz(v);
+#else
+    return 31u - (uint32_t)__builtin_clz(v);
+#endif
+}
+
+// (S a power of two, as the kernel requires)
 __host__ __device__ inline uint32_t tiled_smem_bytes(uint32_t warps, uint32_t S, uint32_t nstages,
                                                      uint32_t stage_bytes, uint32_t slot_blocks, uint32_t nv,
                                                      uint32_t nb, uint32_t nact) {
-    const uint32_t groups = warps / S;
+    const uint32_t groups = S ? warps >> ilog2u(S) : 0u;
     return TGEMV_BAR_BYTES + nact * act_bytes(nb) + warps * nstages * stage_bytes +
            groups * (S - 1) * slot_blocks * nv * CHAIN_FLOATS * 4u;
 }
