@@ -245,6 +245,56 @@ SG_API uint64_t sg_moe_scratch_bytes(const sg_moe *m);
 SG_API sg_status sg_moe_forward(const sg_moe *m, const float *d_x, float *d_out, void *d_scratch,
                                 uint64_t scratch_bytes, sg_moe_choice *d_choice, float *d_probs, void *stream);
 
+/* ---- Decoder step (forward_slice, smollm_chat.rs:3371-3552, with greedy
+ * sampling, :3565-3602 and :3661-3671) -----------------------------------------
+ *
+ * One token through every layer: embedding, then per layer RMSNorm, Q/K/V,
+ * per-head Q/K norm, RoPE, the f16 KV cache, grouped-query attention, output
+ * projection and residual, RMSNorm, dense SwiGLU FFN or MoE layer and residual;
+ * then the output norm, the LM head and the greedy token.  The token and its
+ * position are device state (int32 state[2] = {token, pos}); the step writes
+ * the greedy token into state[0] and advances state[1], so a captured step can
+ * be replayed token after token.  Matrices are TILED16; the GEMVs and expert
+ * passes are the reference's bits, the rest matches within tolerance (see
+ * spindle_b200/csrc/decode.cuh). */
+typedef struct {
+    const float *attn_norm, *ffn_norm;      /* F32 [dim] */
+    const float *q_norm, *k_norm;           /* F32 [head_dim] (Qwen3 per-head norms), or NULL */
+    const uint8_t *wq, *wk, *wv, *wo;       /* TILED16 */
+    int32_t wq_dtype, wk_dtype, wv_dtype, wo_dtype;
+    int32_t is_moe;
+    sg_moe moe;                             /* when is_moe */
+    const uint8_t *ffn_gate_up, *ffn_down;  /* dense FFN: one expert as sg_moe_pack_gate_up / _down pack it */
+    int32_t ffn_gate_up_dtype, ffn_down_dtype;
+    uint64_t n_ff;
+} sg_layer;
+
+typedef struct {
+    uint32_t dim, n_heads, n_kv_heads, head_dim, n_layers, vocab, max_seq;
+    int32_t rope_neox;                      /* NEOX pairs (i, i + head_dim/2), else (2i, 2i+1) */
+    float rope_theta, rms_eps, residual_scale, embedding_scale;
+    float attn_scale;                       /* 0: 1/sqrt(head_dim) */
+    const uint8_t *embed;                   /* GGUF rows [vocab][dim]: F32, F16, Q4_K or Q6_K */
+    int32_t embed_dtype;
+    const uint8_t *lm_head;                 /* TILED16 [vocab][dim] */
+    int32_t lm_head_dtype;
+    const float *output_norm;               /* F32 [dim] */
+    const sg_layer *layers;                 /* host array of n_layers */
+} sg_model;
+
+/* Device scratch of sg_forward (0 for an invalid model), and the f16 K and V
+ * caches ([n_layers][max_seq][n_kv_heads * head_dim] each). */
+SG_API uint64_t sg_model_scratch_bytes(const sg_model *m);
+SG_API uint64_t sg_model_kv_bytes(const sg_model *m);
+/* Fills the scratch's constant part (RoPE frequencies from the host's powf);
+ * once per model and scratch, before sg_forward. */
+SG_API sg_status sg_model_prepare(const sg_model *m, void *d_scratch, uint64_t scratch_bytes, void *stream);
+/* One decoder step on the device state {token, pos}.  d_hidden (optional):
+ * the output-normed hidden state [dim]; d_logits (optional): [vocab];
+ * d_token (optional): the greedy token also as int64. */
+SG_API sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_scratch, uint64_t scratch_bytes,
+                            float *d_hidden, float *d_logits, int64_t *d_token, void *stream);
+
 /* ---- weight quantizer (no reference counterpart: its tests use random bytes)
  * f32 [rows, cols] -> Q4_K or Q6_K rows, deterministic; cols % 256 == 0. */
 SG_API sg_status sg_quantize_weights(int32_t dtype, const float *d_w, uint64_t rows, uint64_t cols,

@@ -288,3 +288,87 @@ def ffns_fused(buf, gates, ups, downs, weights, x, out, int_on=True):
                        _p(out), int(int_on)):
         raise RuntimeError("ffns_fused failed")
     return out
+
+
+# ---- decoder forward pass (smollm_chat.rs:3371-3552) ----
+
+NO_NORM = 0xFFFFFFFFFFFFFFFF
+
+
+class Layer(C.Structure):
+    """One decoder layer: norm offsets, attention matrices, dense FFN or MoE."""
+    _fields_ = [("attn_norm", C.c_uint64), ("ffn_norm", C.c_uint64), ("q_norm", C.c_uint64),
+                ("k_norm", C.c_uint64), ("wq", Mat), ("wk", Mat), ("wv", Mat), ("wo", Mat),
+                ("is_moe", C.c_int32), ("moe", Moe), ("gate", Mat), ("up", Mat), ("down", Mat)]
+
+
+class Model(C.Structure):
+    _fields_ = [("dim", C.c_uint32), ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32),
+                ("head_dim", C.c_uint32), ("n_layers", C.c_uint32), ("vocab", C.c_uint32),
+                ("max_seq", C.c_uint32), ("rope_neox", C.c_int32), ("rope_theta", C.c_float),
+                ("rms_eps", C.c_float), ("residual_scale", C.c_float), ("embedding_scale", C.c_float),
+                ("attn_scale", C.c_float), ("embed", Mat), ("lm_head", Mat), ("output_norm", C.c_uint64),
+                ("layers", C.POINTER(Layer))]
+
+
+def _fwd_sigs():
+    L = lib()
+    if not hasattr(L, "_fwd_ready"):
+        P = C.c_void_p
+        L.or_forward.restype = C.c_int
+        L.or_forward.argtypes = [P, C.POINTER(Model), P, P, C.c_int64, P, C.c_uint32, C.c_int, P, P]
+        L.or_argmax.restype = C.c_int64
+        L.or_argmax.argtypes = [P, C.c_size_t]
+        L.or_rmsnorm.restype = None
+        L.or_rmsnorm.argtypes = [P, P, P, C.c_size_t, C.c_float]
+        L.or_rope_freqs.restype = None
+        L.or_rope_freqs.argtypes = [C.c_float, C.c_uint32, P]
+        L._fwd_ready = True
+    return L
+
+
+class Decoder:
+    """A model (weights in one byte buffer, GGUF-like offsets) with its own f16 KV cache."""
+
+    def __init__(self, buf, model, layers):
+        self.buf = np.ascontiguousarray(buf, np.uint8)
+        self.layers = (Layer * len(layers))(*layers)
+        model.layers = self.layers
+        self.model = model
+        kv = model.n_layers * model.max_seq * model.n_kv_heads * model.head_dim
+        self.kcache = np.zeros(kv, np.uint16)
+        self.vcache = np.zeros(kv, np.uint16)
+
+    def forward(self, token, pos, int_on=True, logits=True):
+        """One token (id, or an fp32 hidden vector) at pos: (output-normed hidden, logits or None)."""
+        L = _fwd_sigs()
+        m = self.model
+        hidden = np.empty(m.dim, np.float32)
+        out = np.empty(m.vocab, np.float32) if logits else None
+        tok, xin = (int(token), None) if np.isscalar(token) else (-1, np.ascontiguousarray(token, np.float32))
+        rc = L.or_forward(_p(self.buf), C.byref(m), _p(self.kcache), _p(self.vcache), tok,
+                          None if xin is None else _p(xin), pos, int(int_on), _p(hidden),
+                          None if out is None else _p(out))
+        if rc:
+            raise RuntimeError("or_forward failed (%d)" % rc)
+        return hidden, out
+
+
+def argmax(logits):
+    """Greedy token: largest under f32::total_cmp, the last one on ties."""
+    a = np.ascontiguousarray(logits, np.float32)
+    return int(_fwd_sigs().or_argmax(_p(a), a.size))
+
+
+def rmsnorm(x, w, eps):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    _fwd_sigs().or_rmsnorm(_p(x), _p(w), _p(out), x.size, eps)
+    return out
+
+
+def rope_freqs(theta, head_dim):
+    out = np.empty(head_dim // 2, np.float32)
+    _fwd_sigs().or_rope_freqs(theta, head_dim, _p(out))
+    return out

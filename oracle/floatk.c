@@ -380,3 +380,7 @@ int or_matmul_rows_multi(const uint8_t *base, const or_mat *m, size_t n_vec, con
     }
     return 0;
 }
+
+/* dot_f16_row_avx2 (quant.rs:1412-1425) for the attention scores: f16 K row
+ * times the fp32 query, as the forward pass calls it (smollm_chat.rs:3475). */
+float or_dot_f16_row(const uint8_t *row, const float *x, size_t n) { return dot_f16(row, x, n); }

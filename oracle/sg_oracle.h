@@ -119,6 +119,40 @@ int or_pool_matvec_multi(const uint8_t *base, const or_mat *m, size_t n_vec,
 
 int or_cpu_has_avx2(void);
 
+/* ---- decoder forward pass (smollm_chat.rs:3371-3552 forward_slice,
+ * :569-584 rmsnorm, :1397-1420 Rope, :3565-3602 greedy sampling) ---- */
+float or_dot_f16_row(const uint8_t *row, const float *x, size_t n);
+typedef struct {
+    uint64_t attn_norm, ffn_norm;   /* F32[dim] offsets */
+    uint64_t q_norm, k_norm;        /* F32[head_dim] offsets, or UINT64_MAX when absent */
+    or_mat wq, wk, wv, wo;
+    int32_t is_moe;
+    or_moe moe;                     /* is_moe */
+    or_mat gate, up, down;          /* dense SwiGLU FFN */
+} or_layer;
+typedef struct {
+    uint32_t dim, n_heads, n_kv_heads, head_dim, n_layers, vocab, max_seq;
+    int32_t rope_neox;
+    float rope_theta, rms_eps, residual_scale, embedding_scale;
+    float attn_scale;               /* 0: 1/sqrt(head_dim) */
+    or_mat embed, lm_head;
+    uint64_t output_norm;           /* F32[dim] */
+    const or_layer *layers;         /* n_layers */
+} or_model;
+/* rmsnorm: out[i] = (x[i] * inv) * w[i], inv = 1 / sqrt(sum of squares / n + eps). */
+void or_rmsnorm(const float *x, const float *w, float *out, size_t n, float eps);
+/* Rope inverse frequencies 1 / theta^(2i / head_dim), i < head_dim / 2. */
+void or_rope_freqs(float theta, uint32_t head_dim, float *inv_freq);
+/* One token at position pos through every layer: the KV caches (f16,
+ * [n_layers][max_seq][n_kv_heads * head_dim]) get this position's K and V;
+ * hidden_out (optional) = the output-normed hidden state, logits_out
+ * (optional) = the LM head on it.  int_on selects the integer kernels. */
+int or_forward(const uint8_t *base, const or_model *m, uint16_t *kcache, uint16_t *vcache, int64_t token,
+               const float *in_hidden, uint32_t pos, int int_on, float *hidden_out, float *logits_out);
+/* Greedy choice: the index of the largest logit under f32::total_cmp, the
+ * last one on ties (Iterator::max_by). */
+int64_t or_argmax(const float *logits, size_t n);
+
 #ifdef __cplusplus
 }
 #endif

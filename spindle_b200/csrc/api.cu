@@ -6,11 +6,14 @@
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
+#include <vector>
+#include <cmath>
 
 #include "gemv_q8k.cuh"
 #include "gemv_tiled.cuh"
 #include "kernels.cuh"
 #include "moe.cuh"
+#include "decode.cuh"
 
 using namespace sg;
 
@@ -322,7 +325,8 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
     if (ns < 2) ns = 2;
     if (ns > 8) ns = 8;
     // the MoE modes keep the router's choice at the top of the barrier area
-    if (mode >= IN_MOE_X && ns * warps * 8 > MOE_QX_BAR_OFF) ns = MOE_QX_BAR_OFF / (warps * 8);
+    // the barriers stay below the ones the MoE modes and image copies keep at the top
+    if (ns * warps * 8 > MOE_QX_BAR_OFF) ns = MOE_QX_BAR_OFF / (warps * 8);
     if (bc < 1) bc = 1;
     // MoE: one CTA per SM, each on a contiguous range of tiles; IN_MOE_H stages
     // h for every slot its range touches (at most this many).
@@ -376,8 +380,12 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
 }
 
 // One of xq (Q8_K inputs) or x (fp32 inputs, vector b at x + b*ldx) is given.
+// With image (one vector): x is the Q8_K shared-memory image made by the
+// kernel before (act_bytes(nb) bytes), copied in by one bulk copy.
 sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, const float *x, uint64_t ldx,
-                       float *const *outs, uint64_t n_vec, uint64_t r0, uint64_t r1, cudaStream_t stream) {
+                       float *const *outs, uint64_t n_vec, uint64_t r0, uint64_t r1, cudaStream_t stream,
+                       const uint8_t *image = nullptr) {
+    if (image && n_vec != 1) return SG_ERR_INVALID;
     const uint32_t t0 = (uint32_t)(r0 / TILE_ROWS), t1 = (uint32_t)((r1 + TILE_ROWS - 1) / TILE_ROWS);
     const bool qx = x != nullptr;
     for (uint64_t g = 0; g < n_vec;) {
@@ -408,10 +416,11 @@ sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, 
         a.stage_bytes = p.stage_bytes;
         a.slot_blocks = p.slot_blocks;
         a.nvec = (uint32_t)nv;
+        a.qx_image = image;
         for (int v = 0; v < nv; v++) {
             if (qx) {
                 a.x[v] = x + (g + v) * ldx;
-            } else {
+            } else if (!image) {
                 a.xd[v] = xq[g + v].d;
                 a.xs[v] = xq[g + v].qs;
                 a.xb[v] = xq[g + v].bsums;
@@ -977,6 +986,205 @@ sg_status sg_moe_forward(const sg_moe *m, const float *d_x, float *d_out, void *
     c.dim = (uint32_t)m->dim;
     c.max_slots = k;
     CK(launch_pdl((const void *)moe_combine_kernel, (uint32_t)((m->dim + 255) / 256), 256, 0, s, &c));
+    return SG_OK;
+}
+
+}  // extern "C"
+
+// ---- decoder step (forward_slice) ------------------------------------------
+
+namespace {
+
+bool kq(int32_t dt) { return dt == SG_Q4_K || dt == SG_Q6_K; }
+
+sg_status check_model(const sg_model *m) {
+    if (!m || !m->embed || !m->lm_head || !m->output_norm || !m->layers) return SG_ERR_INVALID;
+    if (!m->n_heads || !m->n_kv_heads || m->n_heads % m->n_kv_heads || !m->n_layers || !m->vocab || !m->max_seq)
+        return SG_ERR_INVALID;
+    if (m->dim % 256 || m->dim == 0 || m->dim > 8192 || m->head_dim % 64 || m->head_dim == 0 || m->head_dim > 256 ||
+        (m->n_heads * m->head_dim) % 256 || attn_smem_bytes(m->head_dim, m->max_seq) > 227 * 1024)
+        return SG_ERR_SHAPE;
+    if (m->embed_dtype != SG_F32 && m->embed_dtype != SG_F16 && !kq(m->embed_dtype)) return SG_ERR_DTYPE;
+    if (!kq(m->lm_head_dtype)) return SG_ERR_DTYPE;
+    for (uint32_t l = 0; l < m->n_layers; l++) {
+        const sg_layer &y = m->layers[l];
+        if (!y.attn_norm || !y.ffn_norm || !y.wq || !y.wk || !y.wv || !y.wo) return SG_ERR_INVALID;
+        if (!kq(y.wq_dtype) || !kq(y.wk_dtype) || !kq(y.wv_dtype) || !kq(y.wo_dtype)) return SG_ERR_DTYPE;
+        if (y.is_moe) {
+            sg_status st = check_moe(&y.moe);
+            if (st) return st;
+            if (y.moe.dim != m->dim) return SG_ERR_SHAPE;
+        } else {
+            if (!y.ffn_gate_up || !y.ffn_down) return SG_ERR_INVALID;
+            if (!kq(y.ffn_gate_up_dtype) || !kq(y.ffn_down_dtype)) return SG_ERR_DTYPE;
+            if (!cols_ok(y.n_ff)) return SG_ERR_SHAPE;
+        }
+    }
+    return SG_OK;
+}
+
+struct ModelScratch {
+    uint64_t x, xn, qx, q, k, v, att, proj, logits, h, freqs, sel1, moe, moe_bytes, total;
+};
+
+ModelScratch model_scratch(const sg_model *m) {
+    ModelScratch L;
+    uint64_t off = 0;
+    auto take = [&](uint64_t bytes) {
+        const uint64_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const uint64_t q_dim = (uint64_t)m->n_heads * m->head_dim, kv_dim = (uint64_t)m->n_kv_heads * m->head_dim;
+    uint64_t n_ff = 0, moe = 0;
+    for (uint32_t l = 0; l < m->n_layers; l++) {
+        const sg_layer &y = m->layers[l];
+        if (y.is_moe) {
+            const uint64_t b = moe_scratch(&y.moe).total;
+            moe = b > moe ? b : moe;
+        } else if (y.n_ff > n_ff) {
+            n_ff = y.n_ff;
+        }
+    }
+    L.x = take(m->dim * 4);
+    L.xn = take(m->dim * 4);
+    L.qx = take(act_bytes(m->dim / 256));
+    L.q = take(q_dim * 4);
+    L.k = take(kv_dim * 4);
+    L.v = take(kv_dim * 4);
+    L.att = take(q_dim * 4);
+    L.proj = take(m->dim * 4);
+    L.logits = take((uint64_t)m->vocab * 4);
+    L.h = take(n_ff * 4);
+    L.freqs = take(m->head_dim / 2 * 4);
+    L.sel1 = take(sizeof(sg_moe_choice));
+    L.moe = take(moe);
+    L.moe_bytes = moe;
+    L.total = off;
+    return L;
+}
+
+sg_status launch_norm(float *x, const float *add, float rs, const float *w, float eps, uint32_t n, float *xn,
+                      uint8_t *qx, cudaStream_t s) {
+    NormArgs a = {x, add, rs, w, eps, n, xn, qx};
+    CK(launch_pdl((const void *)rmsnorm_kernel, 1, NORM_THREADS, n * 4, s, &a));
+    return SG_OK;
+}
+
+sg_status gemv_image(const uint8_t *w, int32_t dtype, uint64_t rows, uint64_t cols, const uint8_t *image, float *out,
+                     cudaStream_t s) {
+    float *outs[1] = {out};
+    return launch_tiled(w, dtype == SG_Q4_K ? DT_Q4K : DT_Q6K, (uint32_t)(cols / 256), nullptr, nullptr, 0, outs, 1,
+                        0, rows, s, image);
+}
+
+}  // namespace
+
+extern "C" {
+
+uint64_t sg_model_scratch_bytes(const sg_model *m) { return check_model(m) ? 0 : model_scratch(m).total; }
+
+uint64_t sg_model_kv_bytes(const sg_model *m) {
+    if (check_model(m)) return 0;
+    return 2ull * m->n_layers * m->max_seq * m->n_kv_heads * m->head_dim * 2;
+}
+
+sg_status sg_model_prepare(const sg_model *m, void *d_scratch, uint64_t scratch_bytes, void *stream) {
+    sg_status st = check_model(m);
+    if (st) return st;
+    const ModelScratch L = model_scratch(m);
+    if (!d_scratch || scratch_bytes < L.total) return SG_ERR_INVALID;
+    if (!aligned(d_scratch, 256)) return SG_ERR_ALIGN;
+    // Rope::new (smollm_chat.rs:1403-1406): 1 / theta^(2i / head_dim), the host's powf
+    std::vector<float> f(m->head_dim / 2);
+    for (uint32_t i = 0; i < m->head_dim / 2; i++) {
+        const float e = (2.0f * (float)i) / (float)m->head_dim;
+        f[i] = 1.0f / powf(m->rope_theta, e);
+    }
+    sg_moe_choice one;
+    memset(&one, 0, sizeof one);
+    one.n = 1;
+    one.weight[0] = 1.0f;
+    uint8_t *sc = (uint8_t *)d_scratch;
+    CK(cudaMemcpyAsync(sc + L.freqs, f.data(), f.size() * 4, cudaMemcpyHostToDevice, (cudaStream_t)stream));
+    CK(cudaMemcpyAsync(sc + L.sel1, &one, sizeof one, cudaMemcpyHostToDevice, (cudaStream_t)stream));
+    CK(cudaStreamSynchronize((cudaStream_t)stream));  // the host sources go out of scope
+    return SG_OK;
+}
+
+sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_scratch, uint64_t scratch_bytes,
+                     float *d_hidden, float *d_logits, int64_t *d_token, void *stream) {
+    sg_status st = check_model(m);
+    if (st) return st;
+    if (!d_state || !d_kv || !d_scratch) return SG_ERR_INVALID;
+    if (!aligned(d_scratch, 256) || !aligned(d_kv, 16) || !aligned(d_state, 4) || !aligned(d_hidden, 4) ||
+        !aligned(d_logits, 4) || !aligned(d_token, 8))
+        return SG_ERR_ALIGN;
+    const ModelScratch L = model_scratch(m);
+    if (scratch_bytes < L.total) return SG_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t *sc = (uint8_t *)d_scratch;
+    float *x = (float *)(sc + L.x), *xn = (float *)(sc + L.xn), *q = (float *)(sc + L.q), *k = (float *)(sc + L.k);
+    float *v = (float *)(sc + L.v), *att = (float *)(sc + L.att), *proj = (float *)(sc + L.proj);
+    float *logits = d_logits ? d_logits : (float *)(sc + L.logits), *h = (float *)(sc + L.h);
+    const float *freqs = (const float *)(sc + L.freqs);
+    const sg_moe_choice *sel1 = (const sg_moe_choice *)(sc + L.sel1);
+    uint8_t *qx = sc + L.qx;
+    const uint32_t dim = m->dim, hd = m->head_dim, q_dim = m->n_heads * hd, kv_dim = m->n_kv_heads * hd;
+    const uint64_t cache = (uint64_t)m->max_seq * kv_dim;  // f16 elements per layer
+    uint16_t *kc = (uint16_t *)d_kv, *vc = kc + (uint64_t)m->n_layers * cache;
+    const float scale = m->attn_scale != 0.0f ? m->attn_scale : 1.0f / sqrtf((float)hd);
+    static std::atomic<uint64_t> attr_done{0};
+    int dev;
+    CK(cudaGetDevice(&dev));
+    if (!(attr_done.load() >> dev & 1)) {
+        CK(cudaFuncSetAttribute((const void *)attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                227 * 1024));
+        attr_done.fetch_or(1ull << dev);
+    }
+
+    EmbedArgs ea = {m->embed, m->embed_dtype, dim, m->vocab, m->embedding_scale, d_state, x};
+    CK(launch_pdl((const void *)embed_kernel, (dim + 255) / 256, 256, 0, s, &ea));
+    for (uint32_t l = 0; l < m->n_layers; l++) {
+        const sg_layer &y = m->layers[l];
+        // attention: norm (+ the previous layer's FFN residual), Q/K/V, head norms, RoPE, KV, attention
+        if ((st = launch_norm(x, l ? proj : nullptr, m->residual_scale, y.attn_norm, m->rms_eps, dim, xn, qx, s)))
+            return st;
+        if ((st = gemv_image(y.wq, y.wq_dtype, q_dim, dim, qx, q, s)) ||
+            (st = gemv_image(y.wk, y.wk_dtype, kv_dim, dim, qx, k, s)) ||
+            (st = gemv_image(y.wv, y.wv_dtype, kv_dim, dim, qx, v, s)))
+            return st;
+        RopeArgs ra = {q, k, v, y.q_norm, y.k_norm, m->rms_eps, freqs, hd, m->n_heads, m->n_kv_heads,
+                       m->rope_neox, d_state, kc + l * cache, vc + l * cache, m->max_seq};
+        CK(launch_pdl((const void *)rope_kv_kernel, m->n_heads + m->n_kv_heads, 32, 0, s, &ra));
+        AttnArgs aa = {q, kc + l * cache, vc + l * cache, m->n_heads, m->n_kv_heads, hd, m->max_seq, scale,
+                       d_state, att};
+        CK(launch_pdl((const void *)attention_kernel, m->n_heads, ATTN_THREADS, attn_smem_bytes(hd, m->max_seq), s,
+                      &aa));
+        {
+            float *outs[1] = {proj};
+            if ((st = launch_tiled(y.wo, y.wo_dtype == SG_Q4_K ? DT_Q4K : DT_Q6K, q_dim / 256, nullptr, att, q_dim,
+                                   outs, 1, 0, dim, s)))
+                return st;
+        }
+        // feed-forward: norm (+ attention residual), then the dense SwiGLU or the MoE layer
+        if ((st = launch_norm(x, proj, m->residual_scale, y.ffn_norm, m->rms_eps, dim, xn, qx, s))) return st;
+        if (y.is_moe) {
+            if ((st = sg_moe_forward(&y.moe, xn, proj, sc + L.moe, L.moe_bytes, nullptr, nullptr, stream))) return st;
+        } else {
+            if ((st = launch_moe_group(y.ffn_gate_up_dtype, IN_MOE_X, y.ffn_gate_up, 0, 2 * y.n_ff, dim, 1, 1, sel1,
+                                       nullptr, xn, qx, nullptr, 0, h, 0, s)) ||
+                (st = launch_moe_group(y.ffn_down_dtype, IN_MOE_H, y.ffn_down, 0, dim, y.n_ff, 1, 1, sel1, nullptr,
+                                       nullptr, nullptr, h, 0, proj, 0, s)))
+                return st;
+        }
+    }
+    // output norm (+ the last FFN residual), LM head, greedy token
+    if ((st = launch_norm(x, proj, m->residual_scale, m->output_norm, m->rms_eps, dim, xn, qx, s))) return st;
+    if (d_hidden) CK(cudaMemcpyAsync(d_hidden, xn, dim * 4, cudaMemcpyDeviceToDevice, s));
+    if ((st = gemv_image(m->lm_head, m->lm_head_dtype, m->vocab, dim, qx, logits, s))) return st;
+    ArgmaxArgs ga = {logits, m->vocab, d_state, d_token};
+    CK(launch_pdl((const void *)argmax_kernel, 1, ARGMAX_THREADS, 0, s, &ga));
     return SG_OK;
 }
 

@@ -1,0 +1,91 @@
+// decode.cuh — the kernels of one decoder step besides the GEMVs and the MoE
+// layer (forward_slice, smollm_chat.rs:3371-3552), one token at a time.  The
+// token and its position live in device memory (state[0], state[1]) so that a
+// whole step can be captured once and replayed: the argmax kernel writes the
+// next token and advances the position.
+//
+// Parity with the reference's step is within tolerance, not bit for bit: the
+// GEMVs and the MoE expert passes are exact, but the RMSNorm sums of squares
+// and the attention softmax run in parallel orders here (the reference adds
+// them one element at a time), and sin/cos/exp are correctly rounded rather
+// than glibc's.  The reference test suite holds no golden vectors for the
+// forward pass; the oracle's restatement is the checker.
+#pragma once
+
+#include "common.cuh"
+
+namespace sg {
+
+constexpr uint32_t NORM_THREADS = 1024;
+constexpr uint32_t ATTN_THREADS = 256;
+constexpr uint32_t ARGMAX_THREADS = 1024;
+
+// x = dequant_row(embed[token]) * scale (dequant_row, quant.rs:1527-1660).
+struct EmbedArgs {
+    const uint8_t *embed;   // GGUF rows [vocab][dim]
+    int32_t dtype;          // SG_F32, SG_F16, SG_Q4_K or SG_Q6_K
+    uint32_t dim, vocab;
+    float scale;
+    const int32_t *state;   // state[0] = token
+    float *x;
+};
+
+// x += rs * add (when add); xn = (x * inv) * w with inv = 1 / sqrt(mean(x^2) + eps);
+// qx (when set) = Q8_K image of xn in the GEMV's shared-memory layout.
+struct NormArgs {
+    float *x;
+    const float *add;
+    float rs;
+    const float *w;
+    float eps;
+    uint32_t n;
+    float *xn;
+    uint8_t *qx;
+};
+
+// Per-head RMSNorm of q and k (when weights are given), RoPE on both, and the
+// K and V rows of this position into the f16 caches (round to nearest even).
+struct RopeArgs {
+    float *q;
+    const float *k, *v;
+    const float *qn_w, *kn_w;   // [head_dim] or null
+    float eps;
+    const float *inv_freq;      // [head_dim / 2], from the host (glibc powf)
+    uint32_t head_dim, n_heads, n_kv;
+    int32_t neox;
+    const int32_t *state;       // state[1] = pos
+    uint16_t *kc, *vc;          // this layer's caches: [max_seq][n_kv * head_dim]
+    uint32_t max_seq;
+};
+
+// Grouped-query attention of one token over positions 0..pos.
+struct AttnArgs {
+    const float *q;
+    const uint16_t *kc, *vc;
+    uint32_t n_heads, n_kv, head_dim, max_seq;
+    float scale;
+    const int32_t *state;
+    float *out;
+};
+
+// The greedy token (f32::total_cmp, last maximum on ties), written as the next
+// step's token; the position advances.
+struct ArgmaxArgs {
+    const float *logits;
+    uint32_t n;
+    int32_t *state;
+    int64_t *out;               // optional: the token, also kept here
+};
+
+// q | scores, then p | alpha | 1/l
+__host__ __device__ inline uint32_t attn_smem_bytes(uint32_t head_dim, uint32_t max_seq) {
+    return (head_dim + 2u * max_seq + 4u) * 4u;
+}
+
+__global__ void embed_kernel(const __grid_constant__ EmbedArgs a);
+__global__ void rmsnorm_kernel(const __grid_constant__ NormArgs a);
+__global__ void rope_kv_kernel(const __grid_constant__ RopeArgs a);
+__global__ void attention_kernel(const __grid_constant__ AttnArgs a);
+__global__ void argmax_kernel(const __grid_constant__ ArgmaxArgs a);
+
+}  // namespace sg

@@ -19,7 +19,8 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
             dynamic_smem_size() ||
         a.bc == 0 || a.stage_bytes < a.bc * CB || a.S == 0 || a.S != (1u << a.s_log2) || a.S > nwarps ||
         (nwarps & (a.S - 1)) || (blockDim.x & 31) ||
-        a.nstages * nwarps * 8 > (MOE ? MOE_QX_BAR_OFF : TGEMV_BAR_BYTES) ||
+        a.nstages * nwarps * 8 > ((MOE || a.qx_image) ? MOE_QX_BAR_OFF : TGEMV_BAR_BYTES) ||
+        (MODE == IN_Q8K && a.qx_image && a.nvec != 1) ||
         (MOE && a.swiglu && (MODE != IN_MOE_X || a.nvec != 1)) ||
         (MOE && (a.max_slots > MOE_MAXK || a.tiles_per_mat == 0 || nact == 0 ||
                  (uint64_t)a.ntiles * gridDim.x >= (1ull << 32) || a.ntiles < a.max_slots * a.tiles_per_mat)) ||
@@ -231,6 +232,22 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                 }
             }
         }
+    } else if (a.qx_image) {
+        // one Q8_K vector as a ready image (made by the kernel before): one bulk copy
+        if (threadIdx.x == 0) {
+            uint64_t *qbar = reinterpret_cast<uint64_t *>(smem + MOE_QX_BAR_OFF);
+            mbar_init(qbar, 1);
+            fence_mbar_init();
+            mbar_arrive_expect_tx(qbar, act_bytes(nb));
+            bulk_g2s(act, a.qx_image, act_bytes(nb), qbar);
+            if (!mbar_wait_bounded(qbar, 0, WAIT_LIMIT_NS)) {
+                atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_TMA);
+                failed = true;
+            }
+        }
+        failed = __syncthreads_or(failed);
+        if (failed && lane == 0)  // let this warp's weight copies land (bounded) before the tiles are skipped
+            for (uint32_t p = 0; p < nitems && p < a.nstages; p++) mbar_wait_bounded(&bars[p], 0, WAIT_LIMIT_NS);
     } else {
         for (uint32_t v = 0; v < a.nvec; v++) {
             uint8_t *av = act + v * astride;

@@ -1,0 +1,216 @@
+"""Decoder step on the GPU (forward_slice, smollm_chat.rs:3371-3552, greedy
+sampling :3661-3671) through the C ABI: sg_model_*, sg_forward.
+
+A model is a dict of weights named like the GGUF tensors of one architecture
+(Qwen3 / Qwen3-MoE): `embed` [vocab][dim] and `head` [vocab][dim] (K-quant or
+F32/F16 GGUF rows), `out_norm` [dim]; per layer i `l{i}.attn_norm`,
+`l{i}.ffn_norm`, optional `l{i}.q_norm` / `l{i}.k_norm` [head_dim], `l{i}.wq`
+[q_dim][dim], `l{i}.wk` / `l{i}.wv` [kv_dim][dim], `l{i}.wo` [dim][q_dim], and
+either the dense FFN `l{i}.gate` / `l{i}.up` [n_ff][dim], `l{i}.down`
+[dim][n_ff] or the MoE `l{i}.router` F32 [n_expert][dim], `l{i}.gate_exps`,
+`l{i}.up_exps` [n_expert * n_ff][dim], `l{i}.down_exps` [n_expert * dim][n_ff].
+"""
+import ctypes as C
+
+import torch
+
+from . import _lib, lib, _stream, repack_tiled16, tiled16_bytes, Q4_K, Q6_K, F32, F16
+from . import quantize_weights as _quantize_weights
+from ._lib import SgError, SgMoe
+
+
+class SgLayer(C.Structure):
+    _fields_ = [("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p), ("q_norm", C.c_void_p), ("k_norm", C.c_void_p),
+                ("wq", C.c_void_p), ("wk", C.c_void_p), ("wv", C.c_void_p), ("wo", C.c_void_p),
+                ("wq_dtype", C.c_int32), ("wk_dtype", C.c_int32), ("wv_dtype", C.c_int32), ("wo_dtype", C.c_int32),
+                ("is_moe", C.c_int32), ("moe", SgMoe), ("ffn_gate_up", C.c_void_p), ("ffn_down", C.c_void_p),
+                ("ffn_gate_up_dtype", C.c_int32), ("ffn_down_dtype", C.c_int32), ("n_ff", C.c_uint64)]
+
+
+class SgModel(C.Structure):
+    _fields_ = [("dim", C.c_uint32), ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32), ("head_dim", C.c_uint32),
+                ("n_layers", C.c_uint32), ("vocab", C.c_uint32), ("max_seq", C.c_uint32), ("rope_neox", C.c_int32),
+                ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("residual_scale", C.c_float),
+                ("embedding_scale", C.c_float), ("attn_scale", C.c_float), ("embed", C.c_void_p),
+                ("embed_dtype", C.c_int32), ("lm_head", C.c_void_p), ("lm_head_dtype", C.c_int32),
+                ("output_norm", C.c_void_p), ("layers", C.POINTER(SgLayer))]
+
+
+def _sigs():
+    L = lib()
+    if not hasattr(L, "_dec_ready"):
+        P = C.c_void_p
+        L.sg_model_scratch_bytes.restype = C.c_uint64
+        L.sg_model_scratch_bytes.argtypes = [C.POINTER(SgModel)]
+        L.sg_model_kv_bytes.restype = C.c_uint64
+        L.sg_model_kv_bytes.argtypes = [C.POINTER(SgModel)]
+        L.sg_model_prepare.restype = C.c_int32
+        L.sg_model_prepare.argtypes = [C.POINTER(SgModel), P, C.c_uint64, P]
+        L.sg_forward.restype = C.c_int32
+        L.sg_forward.argtypes = [C.POINTER(SgModel), P, P, P, C.c_uint64, P, P, P, P]
+        L._dec_ready = True
+    return L
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+class Decoder:
+    """Device weights, KV cache, scratch and the {token, pos} state of one model."""
+
+    def __init__(self, cfg, weights, dtypes, device):
+        """weights: name -> CUDA tensor (uint8 GGUF rows for matrices, float32
+        vectors); dtypes: name -> GGML dtype of each matrix."""
+        self.cfg, self.dev = dict(cfg), device
+        c = self.cfg
+        self.keep = []  # every device buffer the model points at
+        dim, hd = c["dim"], c["head_dim"]
+        q_dim, kv_dim = c["n_heads"] * hd, c["n_kv_heads"] * hd
+
+        def tiled(name, rows, cols):
+            t, _ = repack_tiled16(dtypes[name], weights[name], rows, cols)
+            self.keep.append(t)
+            return t.data_ptr()
+
+        def vec(name):
+            t = weights.get(name)
+            if t is None:
+                return None
+            t = t.contiguous()
+            self.keep.append(t)
+            return t.data_ptr()
+
+        layers = []
+        moe = c.get("moe")
+        for i in range(c["n_layers"]):
+            p = "l%d." % i
+            y = SgLayer()
+            y.attn_norm, y.ffn_norm = vec(p + "attn_norm"), vec(p + "ffn_norm")
+            y.q_norm, y.k_norm = vec(p + "q_norm"), vec(p + "k_norm")
+            y.wq, y.wq_dtype = tiled(p + "wq", q_dim, dim), dtypes[p + "wq"]
+            y.wk, y.wk_dtype = tiled(p + "wk", kv_dim, dim), dtypes[p + "wk"]
+            y.wv, y.wv_dtype = tiled(p + "wv", kv_dim, dim), dtypes[p + "wv"]
+            y.wo, y.wo_dtype = tiled(p + "wo", dim, q_dim), dtypes[p + "wo"]
+            if moe:
+                from . import Moe
+                m = Moe.pack(weights[p + "router"].float(), weights[p + "gate_exps"], weights[p + "up_exps"],
+                             weights[p + "down_exps"], dtypes[p + "gate_exps"], dtypes[p + "down_exps"],
+                             moe["n_expert"], moe["n_used"], dim, moe["n_ff"], norm=moe.get("norm", True),
+                             moe_prune=moe.get("prune", 0.0))
+                self.keep.append(m)
+                y.is_moe, y.moe = 1, m.c()
+            else:
+                from . import Moe
+                f = c["n_ff"]
+                one = Moe.pack(torch.zeros(1, dim, device=device), weights[p + "gate"], weights[p + "up"],
+                               weights[p + "down"], dtypes[p + "gate"], dtypes[p + "down"], 1, 1, dim, f)
+                self.keep.append(one)
+                y.is_moe = 0
+                y.ffn_gate_up, y.ffn_down = one.gate_up.data_ptr(), one.down.data_ptr()
+                y.ffn_gate_up_dtype, y.ffn_down_dtype, y.n_ff = dtypes[p + "gate"], dtypes[p + "down"], f
+            layers.append(y)
+        self.layers = (SgLayer * len(layers))(*layers)
+        m = SgModel()
+        m.dim, m.n_heads, m.n_kv_heads, m.head_dim = dim, c["n_heads"], c["n_kv_heads"], hd
+        m.n_layers, m.vocab, m.max_seq = c["n_layers"], c["vocab"], c["max_seq"]
+        m.rope_neox, m.rope_theta, m.rms_eps = int(c.get("rope_neox", True)), c["rope_theta"], c["rms_eps"]
+        m.residual_scale, m.embedding_scale = c.get("residual_scale", 1.0), c.get("embedding_scale", 1.0)
+        m.attn_scale = c.get("attn_scale", 0.0)
+        emb = weights["embed"].contiguous()
+        self.keep.append(emb)
+        m.embed, m.embed_dtype = emb.data_ptr(), dtypes["embed"]
+        m.lm_head, m.lm_head_dtype = tiled("head", c["vocab"], dim), dtypes["head"]
+        m.output_norm = vec("out_norm")
+        m.layers = self.layers
+        self.model = m
+        L = _sigs()
+        nbytes = L.sg_model_scratch_bytes(C.byref(m))
+        if not nbytes:
+            raise SgError(1, "sg_model_scratch_bytes (invalid model)")
+        self.scratch = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        self.kv = torch.zeros(L.sg_model_kv_bytes(C.byref(m)), dtype=torch.uint8, device=device)
+        self.state = torch.zeros(2, dtype=torch.int32, device=device)
+        self.logits = torch.empty(c["vocab"], dtype=torch.float32, device=device)
+        self.hidden = torch.empty(dim, dtype=torch.float32, device=device)
+        self.token = torch.zeros(1, dtype=torch.int64, device=device)
+        _lib.check(L.sg_model_prepare(C.byref(m), C.c_void_p(self.scratch.data_ptr()), self.scratch.numel(),
+                                      _stream()), "sg_model_prepare")
+
+    def set_state(self, token, pos, stream=None):
+        self.state.copy_(torch.tensor([token, pos], dtype=torch.int32), non_blocking=False)
+
+    def step(self, stream=None, hidden=True, logits=True):
+        """One decoder step on the device state; the state then holds the greedy
+        token and the next position."""
+        L = _sigs()
+        _lib.check(L.sg_forward(C.byref(self.model), C.c_void_p(self.state.data_ptr()), C.c_void_p(self.kv.data_ptr()),
+                                C.c_void_p(self.scratch.data_ptr()), self.scratch.numel(),
+                                C.c_void_p(self.hidden.data_ptr()) if hidden else None,
+                                C.c_void_p(self.logits.data_ptr()) if logits else None,
+                                C.c_void_p(self.token.data_ptr()), _stream(stream)), "sg_forward")
+
+    def generate(self, prompt, n_new):
+        """Greedy decode: feed the prompt, then n_new tokens; returns the new tokens."""
+        out = []
+        for i, t in enumerate(prompt):
+            self.set_state(t, i)
+            self.step(hidden=False, logits=False)
+        for _ in range(n_new):
+            out.append(int(self.token.item()))
+            self.step(hidden=False, logits=False)
+        return out
+
+
+def random_weights(cfg, dtypes, device, seed=0):
+    """Random-init weights of the architecture in cfg, made on the GPU with the
+    library's quantizer (N(0, 0.02) matrices, router N(0, 1/dim), norms 1)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    c = cfg
+    dim, hd = c["dim"], c["head_dim"]
+    q_dim, kv_dim = c["n_heads"] * hd, c["n_kv_heads"] * hd
+
+    def mat(name, rows, cols):
+        w = torch.randn(rows, cols, device=device, generator=g) * 0.02
+        return _quantize_weights(dtypes[name], w)
+
+    W = {"embed": mat("embed", c["vocab"], dim), "head": mat("head", c["vocab"], dim),
+         "out_norm": torch.ones(dim, device=device)}
+    for i in range(c["n_layers"]):
+        p = "l%d." % i
+        W[p + "attn_norm"] = torch.ones(dim, device=device)
+        W[p + "ffn_norm"] = torch.ones(dim, device=device)
+        if c.get("qk_norm", True):
+            W[p + "q_norm"] = torch.ones(hd, device=device)
+            W[p + "k_norm"] = torch.ones(hd, device=device)
+        W[p + "wq"] = mat(p + "wq", q_dim, dim)
+        W[p + "wk"] = mat(p + "wk", kv_dim, dim)
+        W[p + "wv"] = mat(p + "wv", kv_dim, dim)
+        W[p + "wo"] = mat(p + "wo", dim, q_dim)
+        moe = c.get("moe")
+        if moe:
+            ne, f = moe["n_expert"], moe["n_ff"]
+            W[p + "router"] = torch.randn(ne, dim, device=device, generator=g) / dim ** 0.5
+            W[p + "gate_exps"] = mat(p + "gate_exps", ne * f, dim)
+            W[p + "up_exps"] = mat(p + "up_exps", ne * f, dim)
+            W[p + "down_exps"] = mat(p + "down_exps", ne * dim, f)
+        else:
+            f = c["n_ff"]
+            W[p + "gate"] = mat(p + "gate", f, dim)
+            W[p + "up"] = mat(p + "up", f, dim)
+            W[p + "down"] = mat(p + "down", dim, f)
+    return W
+
+
+def qwen3_dtypes(cfg, attn_v=Q6_K, down=Q6_K, head=Q6_K, embed=Q6_K, other=Q4_K):
+    """The Q4_K_M mix of the BASELINE configs: Q6_K for attn_v, ffn_down and
+    the embedding/head, Q4_K elsewhere."""
+    d = {"embed": embed, "head": head}
+    for i in range(cfg["n_layers"]):
+        p = "l%d." % i
+        d.update({p + "wq": other, p + "wk": other, p + "wv": attn_v, p + "wo": other})
+        if cfg.get("moe"):
+            d.update({p + "gate_exps": other, p + "up_exps": other, p + "down_exps": down})
+        else:
+            d.update({p + "gate": other, p + "up": other, p + "down": down})
+    return d
