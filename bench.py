@@ -627,6 +627,203 @@ def run_gpu_moe(args):
     return line, host0
 
 
+# ---- decode workload (--workload decode) -------------------------------------
+# BASELINE configs[3] (Qwen3-30B-A3B, 48 layers, hidden 2048, 32/4 heads of
+# 128, 128 experts top 8 with FFN 768, vocab 151936) and configs[2]
+# (Qwen3-0.6B dense): random-init Q4_K_M mix (Q6_K attn_v, down and head),
+# a 64-token random prompt fed one token at a time, then greedy decode steps.
+# One step = one token through forward_slice + LM head + argmax, replayed from
+# one captured graph (the token and position are device state).
+
+DECODE_MODELS = {
+    "qwen3_30b_a3b": dict(dim=2048, n_heads=32, n_kv_heads=4, head_dim=128, n_layers=48, vocab=151936,
+                          rope_theta=1e6, rms_eps=1e-6, rope_neox=True,
+                          moe=dict(n_expert=128, n_used=8, n_ff=768, norm=True)),
+    "qwen3_0_6b": dict(dim=1024, n_heads=16, n_kv_heads=8, head_dim=128, n_layers=28, vocab=151936,
+                       rope_theta=1e6, rms_eps=1e-6, rope_neox=True, n_ff=3072),
+}
+PROMPT = 64
+
+
+def decode_bytes(cfg, n_chosen_per_layer=None):
+    """Algorithmic bytes of one token: every weight the step reads (attention,
+    router and the chosen experts, or the dense FFN, per layer; the LM head;
+    one embedding row), plus the KV cache rows it reads are left out (they are
+    small next to the weights at these lengths)."""
+    d, hd = cfg["dim"], cfg["head_dim"]
+    q, kv = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    blk = lambda dt, rows, cols: rows * (cols // 256) * BLK[dt]
+    attn = blk(Q4_K, q, d) + blk(Q4_K, kv, d) + blk(Q6_K, kv, d) + blk(Q4_K, d, q)
+    if cfg.get("moe"):
+        m = cfg["moe"]
+        expert = 2 * blk(Q4_K, m["n_ff"], d) + blk(Q6_K, d, m["n_ff"])
+        ffn = m["n_expert"] * d * 4 + m["n_used"] * expert
+    else:
+        ffn = 2 * blk(Q4_K, cfg["n_ff"], d) + blk(Q6_K, d, cfg["n_ff"])
+    return cfg["n_layers"] * (attn + ffn + 2 * d * 4) + blk(Q6_K, cfg["vocab"], d) + blk(Q4_K, 1, d) + d * 4
+
+
+def decode_config(name, cfg, world):
+    return {"workload": "decode_%s" % name, "model": name, "layers": cfg["n_layers"], "dim": cfg["dim"],
+            "heads": "%d/%d x %d" % (cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"]),
+            "ffn": ("%d experts top %d, FFN %d" % (cfg["moe"]["n_expert"], cfg["moe"]["n_used"], cfg["moe"]["n_ff"])
+                    if cfg.get("moe") else "dense FFN %d" % cfg["n_ff"]),
+            "vocab": cfg["vocab"], "quant": "Q4_K_M mix: Q4_K, Q6_K attn_v / ffn_down / head, Q4_K embedding",
+            "prompt": PROMPT, "global_batch": world, "seq_len": PROMPT, "parallelism": "replicas x%d (weak)" % world,
+            "weights": "random-init N(0,0.02), router N(0,1/dim), norms 1, seeded",
+            "l2": "2.0 GB (30B) / 0.4 GB (0.6B) of weights per token > 126 MB L2"}
+
+
+def run_gpu_decode(args):
+    import torch
+    import torch.distributed as dist
+
+    import spindle_b200 as sg
+    from spindle_b200 import _lib
+    from spindle_b200.decoder import Decoder, qwen3_dtypes, random_weights
+
+    rank, world, local = rank_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    name = args.model
+    cfg = dict(DECODE_MODELS[name], max_seq=PROMPT + args.warmup + args.steps + 8)
+    dtypes = qwen3_dtypes(cfg, embed=Q4_K)
+    W = random_weights(cfg, dtypes, dev, seed=5000 + rank)
+    host = None
+    if rank == 0 and world == 1 and args.cpu_budget > 0:
+        # two layers' GGUF bytes plus embedding and head, for the CPU baseline
+        keep = ["embed", "head", "out_norm"] + [k for k in W if k.startswith("l0.") or k.startswith("l1.")]
+        host = {k: W[k].cpu().numpy() for k in keep}
+    dec = Decoder(cfg, W, dtypes, dev)
+    del W
+    torch.cuda.synchronize()
+    g = torch.Generator().manual_seed(77 + rank)
+    prompt = torch.randint(0, cfg["vocab"], (PROMPT,), generator=g).tolist()
+    for i, t in enumerate(prompt):
+        dec.set_state(t, i)
+        dec.step(hidden=False, logits=False)
+    torch.cuda.synchronize()
+    lib = sg.lib()
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            dec.step(stream=s, hidden=False, logits=False)
+        for _ in range(args.warmup):
+            graph.replay()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(s)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(s)
+            e1.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        pos_after = int(dec.state[1].item())
+        # e2e: the host feeds each token (pinned h2d) and reads the greedy token
+        # back (d2h) every step, then continues from it
+        h_state = torch.zeros(2, dtype=torch.int32).pin_memory()
+        h_tok = torch.zeros(1, dtype=torch.int64).pin_memory()
+        sp = C.c_void_p(s.cuda_stream)
+        n_e2e = min(16, cfg["max_seq"] - pos_after - 1)
+        h_state[0], h_state[1] = int(dec.state[0].item()), pos_after
+        torch.cuda.synchronize()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(s)
+        for _ in range(n_e2e):
+            _lib.check(lib.sg_memcpy_h2d(C.c_void_p(dec.state.data_ptr()), C.c_void_p(h_state.data_ptr()), 8, sp), "h2d")
+            graph.replay()
+            _lib.check(lib.sg_memcpy_d2h(C.c_void_p(h_tok.data_ptr()), C.c_void_p(dec.token.data_ptr()), 8, sp), "d2h")
+            s.synchronize()
+            h_state[0], h_state[1] = int(h_tok[0]), int(h_state[1]) + 1
+        b1.record(s)
+        b1.synchronize()
+        e2e_ms = b0.elapsed_time(b1) / max(n_e2e, 1)
+    sg.device_status()
+    bytes_tok = decode_bytes(cfg)
+    value = world * 1e3 / ms
+    peak, peak_src = 6650.0, "fallback 6.65 TB/s"
+    try:
+        peak, peak_src = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"], "MEASURED_PEAKS.json hbm_gbs"
+    except Exception:
+        pass
+    launches = 1 + cfg["n_layers"] * (8 + (4 if cfg.get("moe") else 2)) + 3
+    line = None
+    if rank == 0:
+        achieved = bytes_tok / (ms * 1e-3) / 1e9
+        line = {"metric": "decode tokens/s, %s (random-init, Q4_K_M mix), greedy" % name, "value": round(value, 2),
+                "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "int8 x int4/int6 -> int32 GEMVs, fp32 norms/attention/router, f16 KV", "data": "synthetic",
+                "config": decode_config(name, cfg, world),
+                "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
+                             "kernel": "the whole decode step (%d launches)" % launches,
+                             "how": "algorithmic weight bytes per token (%.3f GB) x tokens/s" % (bytes_tok / 1e9)},
+                "e2e": {"value": round(1e3 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
+                        "how": "per token: sg_memcpy_h2d of {token, pos} from pinned host, the step, sg_memcpy_d2h "
+                               "of the greedy token, host sync (%d tokens)" % n_e2e},
+                "gpu_launches": launches * args.steps,
+                "clocks": clk.summary()}
+    if world > 1:
+        dist.barrier()
+        del graph
+        dist.destroy_process_group()
+    return line, host, cfg, dtypes
+
+
+def decode_cpu_sample(cfg, dtypes, host, budget_s):
+    """Per-token time of the oracle's forward_slice (one thread), measured on a
+    two-layer model made of the real model's first two layers, embedding and
+    head, and scaled: 2-layer time minus the head's, times layers / 2, plus the
+    head's."""
+    import numpy as np
+    import oracle as O
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import decoder_util as U
+    c2 = dict(cfg, n_layers=2, max_seq=64)
+    d2 = {k: v for k, v in dtypes.items() if not k.startswith("l") or k.split(".")[0] in ("l0", "l1")}
+    D = U.oracle_decoder(c2, d2, host)
+    hd_buf = np.ascontiguousarray(host["head"])
+    head = O.Mat(dtypes["head"], cfg["dim"], cfg["vocab"], 0)
+    xq = np.random.default_rng(3).standard_normal(cfg["dim"], dtype=np.float32)
+    # the head's share: its integer matvec (Q8_K quantize + rows) on one thread
+    O.pool_create(1)
+    try:
+        logits = np.empty((1, cfg["vocab"]), np.float32)
+        t0 = time.perf_counter()
+        n_h = 0
+        while True:
+            O.pool_matvec_multi(hd_buf, head, xq.reshape(1, -1), logits)
+            n_h += 1
+            if time.perf_counter() - t0 > 0.2 * budget_s:
+                break
+        t_head = (time.perf_counter() - t0) / n_h
+    finally:
+        O.pool_destroy()
+    t0 = time.perf_counter()
+    n = 0
+    while n < c2["max_seq"]:
+        D.forward(n % 1000, n)
+        n += 1
+        if time.perf_counter() - t0 > 0.8 * budget_s:
+            break
+    t2 = (time.perf_counter() - t0) / n
+    per_tok = (t2 - t_head) * cfg["n_layers"] / 2 + t_head
+    return per_tok, n
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -640,11 +837,33 @@ def main():
     ap.add_argument("--shape", type=int, default=None, help="profiling: run only this sweep entry")
     ap.add_argument("--profile", action="store_true",
                     help="profiling: only the timed step loop (no e2e, per-shape or CPU legs)")
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "moe"],
-                    help="gemv: the headline K-quant GEMV sweep; moe: the Qwen3-30B-A3B MoE layer")
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "moe", "decode"],
+                    help="gemv: the headline K-quant GEMV sweep; moe: the Qwen3-30B-A3B MoE layer; "
+                         "decode: greedy decode of a whole random-init model")
+    ap.add_argument("--model", default="qwen3_30b_a3b", choices=sorted(DECODE_MODELS),
+                    help="decode workload: the model architecture")
     args = ap.parse_args()
     if args.warmup < 3 and not args.profile:
         args.warmup = 3
+    if args.workload == "decode":
+        if args.steps == 20000:
+            args.steps = 128  # the BASELINE workload's 128 greedy tokens
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "decode reference arm: use the cpu_baseline of the "
+                              "GPU line (the oracle forward on two real layers, scaled)"}), flush=True)
+            return
+        line, host, cfg, dtypes = run_gpu_decode(args)
+        rank, world, _ = rank_env()
+        if rank == 0 and line is not None:
+            if host is not None:
+                per_tok, n = decode_cpu_sample(cfg, dtypes, host, args.cpu_budget)
+                line["cpu_baseline"] = {"value": round(1.0 / per_tok, 3), "unit": "tok/s", "cores": 1, "kind": "port",
+                                        "sample": "the oracle's forward_slice (one thread) on the model's first 2 "
+                                                  "layers + embedding + head, %d tokens; per-token time = "
+                                                  "(2-layer time - head time) x %d / 2 + head time"
+                                                  % (n, cfg["n_layers"])}
+            print(json.dumps(line), flush=True)
+        return
     if args.workload == "moe":
         if args.steps == 20000:
             args.steps = 2000  # one step is 8 token-layers
