@@ -47,6 +47,21 @@ def step_bytes(n):
     return sum(alg_bytes(dt, r, c, n) for dt, r, c in SHAPES)
 
 
+def profiled_traffic(args):
+    """DRAM bytes (read + write) of one sweep step's GEMV launches, from the
+    committed ncu launch list of this workload (N = 1 vector, tiled layout,
+    all seven matrices); None for any other configuration."""
+    if args.nvec != 1 or getattr(args, "layout", "tiled") != "tiled" or args.shape is not None:
+        return None
+    import re
+    try:
+        text = open(os.path.join(ROOT, "profiles", "bench_launch_list.md")).read()
+        m = re.search(r"^\| step \| \| [\d.]+ \| ([\d.]+) \|", text, re.M)
+        return int(float(m.group(1)) * 1e6) if m else None
+    except OSError:
+        return None
+
+
 class ClockSampler:
     """Samples SM clock and throttle reasons through NVML while running."""
 
@@ -367,10 +382,12 @@ def run_gpu(args):
                 "vs_baseline": None, "dtype": "int8 x int4/int6 -> int32, fp32 epilogue", "data": "synthetic",
                 "config": config_block(args, world),
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                             "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
+                             "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args),
+                             "algorithmic_bytes": gemv_bytes, "peak_source": peak_src,
                              "kernel": "gemv_tiled_kernel" if args.layout == "tiled" else "gemv_q8k_kernel",
                              "how": "algorithmic bytes of the 7 GEMV launches / their replayed duration "
-                                    "(CUDA events on the launch stream)"},
+                                    "(CUDA events on the launch stream); traffic = DRAM read + write "
+                                    "of the same 7 launches from the committed ncu launch list"},
                 "per_shape": per_shape,
                 "e2e": {"value": round(bytes_rank * world / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
