@@ -323,6 +323,8 @@ def _fwd_sigs():
         L.or_rmsnorm.argtypes = [P, P, P, C.c_size_t, C.c_float]
         L.or_rope_freqs.restype = None
         L.or_rope_freqs.argtypes = [C.c_float, C.c_uint32, P]
+        L.or_rope_rotate.restype = None
+        L.or_rope_rotate.argtypes = [P, C.c_size_t, C.c_uint32, P, C.c_int32, C.c_float]
         L._fwd_ready = True
     return L
 
@@ -372,3 +374,11 @@ def rope_freqs(theta, head_dim):
     out = np.empty(head_dim // 2, np.float32)
     _fwd_sigs().or_rope_freqs(theta, head_dim, _p(out))
     return out
+
+
+def rope_rotate(v, head_dim, inv_freq, neox, pos):
+    """Rope::rotate (smollm_chat.rs:1409-1419) on a copy of v."""
+    v = np.array(v, np.float32, copy=True)
+    f = np.ascontiguousarray(inv_freq, np.float32)
+    _fwd_sigs().or_rope_rotate(_p(v), v.size, head_dim, _p(f), int(neox), pos)
+    return v

@@ -5,7 +5,7 @@
  * or_rmsnorm     rmsnorm              smollm_chat.rs:569-575
  * (heads)        rmsnorm_heads        smollm_chat.rs:578-584
  * or_rope_freqs  Rope::new            smollm_chat.rs:1403-1406
- * (rotate)       Rope::rotate         smollm_chat.rs:1408-1419
+ * or_rope_rotate Rope::rotate         smollm_chat.rs:1408-1419
  * (matvec)       matvec               smollm_chat.rs:309-349 (integer path when supported)
  * or_forward     forward_slice        smollm_chat.rs:3371-3552 (one token; no bias tensors,
  *                                     no layer streaming or expert cache)
@@ -49,7 +49,7 @@ void or_rope_freqs(float theta, uint32_t head_dim, float *inv_freq)
     }
 }
 
-static void rope_rotate(float *v, size_t len, uint32_t head_dim, const float *inv_freq, int neox, float pos)
+void or_rope_rotate(float *v, size_t len, uint32_t head_dim, const float *inv_freq, int neox, float pos)
 {
     uint32_t half = head_dim / 2;
     for (size_t h0 = 0; h0 < len; h0 += head_dim) {
@@ -172,8 +172,8 @@ int or_forward(const uint8_t *base, const or_model *m, uint16_t *kcache, uint16_
                 or_rmsnorm(k + h, (const float *)(base + ly->k_norm), tmp, hd, m->rms_eps);
                 memcpy(k + h, tmp, hd * 4);
             }
-        rope_rotate(q, q_dim, m->head_dim, freqs, m->rope_neox, (float)pos);
-        rope_rotate(k, kv_dim, m->head_dim, freqs, m->rope_neox, (float)pos);
+        or_rope_rotate(q, q_dim, m->head_dim, freqs, m->rope_neox, (float)pos);
+        or_rope_rotate(k, kv_dim, m->head_dim, freqs, m->rope_neox, (float)pos);
         size_t kv_off = ((size_t)l * m->max_seq + pos) * kv_dim;
         to_f16(k, kcache + kv_off, kv_dim);
         to_f16(v, vcache + kv_off, kv_dim);

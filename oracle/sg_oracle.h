@@ -143,6 +143,8 @@ typedef struct {
 void or_rmsnorm(const float *x, const float *w, float *out, size_t n, float eps);
 /* Rope inverse frequencies 1 / theta^(2i / head_dim), i < head_dim / 2. */
 void or_rope_freqs(float theta, uint32_t head_dim, float *inv_freq);
+/* Rope::rotate: every head of v (len values) rotated to position pos. */
+void or_rope_rotate(float *v, size_t len, uint32_t head_dim, const float *inv_freq, int neox, float pos);
 /* One token at position pos through every layer: the KV caches (f16,
  * [n_layers][max_seq][n_kv_heads * head_dim]) get this position's K and V;
  * hidden_out (optional) = the output-normed hidden state, logits_out

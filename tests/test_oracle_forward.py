@@ -153,3 +153,31 @@ def test_forward_int_path_close_to_float_path():
         _, li = a.forward(t, pos, int_on=True)
         _, lf = b.forward(t, pos, int_on=False)
         assert np.abs(li - lf).max() <= 0.05 * np.abs(lf).max()
+
+
+def _rope_textbook(v, head_dim, pos, theta, neox):
+    # rope_reference (smollm_chat.rs:4853-4865): theta^(-2i/hd) per pair
+    out = v.copy()
+    half = head_dim // 2
+    for h in range(v.size // head_dim):
+        for i in range(half):
+            ang = np.float32(pos) * np.float32(theta) ** np.float32(-(2.0 * i) / head_dim)
+            a, b = (h * head_dim + i, h * head_dim + i + half) if neox else (h * head_dim + 2 * i, h * head_dim + 2 * i + 1)
+            c, s = np.float32(math.cos(ang)), np.float32(math.sin(ang))
+            out[a] = v[a] * c - v[b] * s
+            out[b] = v[a] * s + v[b] * c
+    return out
+
+
+@pytest.mark.parametrize("neox", [False, True])
+def test_rope_matches_reference_and_composes(neox):
+    # rope_matches_reference_and_composes (smollm_chat.rs:4867-4886)
+    hd = 64
+    v = np.array([((i * 37 % 101) / 50.0) - 1.0 for i in range(3 * hd)], np.float32)
+    f = O.rope_freqs(100000.0, hd)
+    a = O.rope_rotate(v, hd, f, neox, 17.0)
+    assert np.abs(a - _rope_textbook(v, hd, 17.0, 100000.0, neox)).max() < 1e-4
+    # the KV-cache shift: rotate(p) then rotate(-d) == rotate(p - d)
+    a = O.rope_rotate(a, hd, f, neox, -5.0)
+    b = O.rope_rotate(v, hd, f, neox, 12.0)
+    assert np.abs(a - b).max() < 1e-4
