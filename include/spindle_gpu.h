@@ -150,6 +150,26 @@ SG_API sg_status sg_unpack_tiled16(int32_t dtype, const uint8_t *d_tiled, uint64
 SG_API sg_status sg_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
                            uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, void *stream);
 
+/* The float path (quant.rs:939-1094 matvec_rows_avx2; quant_multi.rs:232-273
+ * matmul_rows_avx2), for formats or switches that keep a matrix off the integer
+ * kernels: out_b[r] = d_out[b*ldo + r] for r in r0..r1, x_b = d_x + b*ldx (cols
+ * fp32).  GGUF rows only, base + offset 16-byte aligned for Q4_K, 4 for F32,
+ * 2 otherwise.  Formats: SG_F32, SG_F16 (any cols), SG_Q8_0 (cols % 32),
+ * SG_Q4_K and SG_Q6_K (cols % 256), cols <= SG_MAX_COLS.
+ * sg_matvec_rows_float runs every vector through matvec_rows_avx2 (the
+ * single-vector algorithm; also what matvec_multi does for F32 matrices,
+ * smollm_chat.rs:455-463).  sg_matmul_rows_float is matmul_rows_avx2: for
+ * n_vec > 1 and a format with a shared-decode kernel (F32 cols % 8, Q8_0,
+ * Q4_K, Q6_K) the rows_multi algorithm, whose bits differ from the
+ * single-vector ones exactly as in the reference.  Both are bit-identical to
+ * the reference (NaN payloads aside). */
+SG_API sg_status sg_matvec_rows_float(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx,
+                                      float *d_out, uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1,
+                                      void *stream);
+SG_API sg_status sg_matmul_rows_float(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx,
+                                      float *d_out, uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1,
+                                      void *stream);
+
 /* The same matvec for either layout with the Q8_K images in caller-owned
  * scratch (the reference keeps them in thread-local scratch, quant_q8k.rs:
  * 123-142): quantizes x_b into d_scratch (>= sg_matvec_scratch_bytes(cols,

@@ -6,6 +6,8 @@ Host-side mirror of the reference's kernel API (WiseHax/spindle 1.1.0, src/):
   supports / set_enabled   quant_q8k.rs:22-57
   Q8K, Q8K.quantize        quant_q8k.rs:61-81
   matmul_rows              quant_q8k.rs:255-295
+  matvec_rows_float        quant.rs:939-1094 (float path, one vector at a time)
+  matmul_rows_float        quant_multi.rs:232-273 (float path, shared decode)
 Every call goes through the C ABI of include/spindle_gpu.h (libspindle_b200.so);
 torch tensors are only the device-memory plumbing.  There is no CPU path: a
 missing library or a failed call raises.
@@ -164,6 +166,33 @@ def matvec_scratch(base, m, xs, out=None, r0=0, r1=None, scratch=None, stream=No
                                        r1, C.c_void_p(scratch.data_ptr()), scratch.numel(), _stream(stream)),
                "matvec_scratch")
     return out
+
+
+def _float_call(fn, what, base, m, xs, out, r0, r1, stream):
+    single = xs.dim() == 1
+    xs2 = xs.reshape(1, -1) if single else xs
+    if xs2.dtype != torch.float32 or xs2.stride(-1) != 1:
+        raise ValueError("xs must be float32 with contiguous rows")
+    r1 = m.rows if r1 is None else r1
+    if out is None:
+        out = torch.full((xs2.shape[0], m.rows), float("nan"), dtype=torch.float32, device=xs2.device)
+    out2 = out.reshape(1, -1) if out.dim() == 1 else out
+    _lib.check(fn(C.c_void_p(base.data_ptr()), C.byref(m.c()), C.c_void_p(xs2.data_ptr()), xs2.stride(0),
+                  C.c_void_p(out2.data_ptr()), out2.stride(0), xs2.shape[0], r0, r1, _stream(stream)), what)
+    return out
+
+
+def matvec_rows_float(base, m, xs, out=None, r0=0, r1=None, stream=None):
+    """quant::matvec_rows_avx2 (quant.rs:939-1094) for every vector: fp32 CUDA
+    xs [n_vec, cols] (or [cols]) -> out [n_vec, rows] (rows outside r0..r1
+    untouched).  GGUF rows of F32, F16, Q8_0, Q4_K or Q6_K."""
+    return _float_call(lib().sg_matvec_rows_float, "matvec_rows_float", base, m, xs, out, r0, r1, stream)
+
+
+def matmul_rows_float(base, m, xs, out=None, r0=0, r1=None, stream=None):
+    """quant_multi::matmul_rows_avx2 (quant_multi.rs:232-273): the shared-decode
+    rows_multi kernels for several vectors, matvec_rows for one."""
+    return _float_call(lib().sg_matmul_rows_float, "matmul_rows_float", base, m, xs, out, r0, r1, stream)
 
 
 def gemv(base, m, xq, stream=None):

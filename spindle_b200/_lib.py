@@ -72,6 +72,8 @@ SIGNATURES = {
     "sg_q8k_quantize": (I32, [P, U64, U64, U64, C.POINTER(SgQ8K), P]),
     "sg_matmul_rows": (I32, [P, C.POINTER(SgMat), C.POINTER(SgQ8K), C.POINTER(P), U64, U64, U64, P]),
     "sg_matvec": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
+    "sg_matvec_rows_float": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
+    "sg_matmul_rows_float": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
     "sg_matvec_scratch_bytes": (U64, [U64, U64]),
     "sg_matvec_scratch": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P, U64, P]),
     "sg_matvec_static": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),

@@ -14,6 +14,7 @@
 #include "kernels.cuh"
 #include "moe.cuh"
 #include "decode.cuh"
+#include "gemv_float.cuh"
 
 using namespace sg;
 
@@ -651,6 +652,83 @@ sg_status pack_experts(int32_t dtype, const uint8_t *src, uint64_t n_expert, uin
     return SG_OK;
 }
 
+// ---- float path --------------------------------------------------------------
+
+typedef void (*fgemv_fn)(const FGemvArgs);
+
+template <int DT, bool M>
+fgemv_fn pick_float_t(uint64_t nv) {
+    return nv == 1 ? gemv_float_kernel<DT, 1, M> : nv == 2 ? gemv_float_kernel<DT, 2, M>
+           : nv <= 4 ? gemv_float_kernel<DT, 4, M> : gemv_float_kernel<DT, 8, M>;
+}
+
+fgemv_fn pick_float(int32_t dt, bool multi, uint64_t nv) {
+    switch (dt) {
+    case SG_F32: return multi ? pick_float_t<FDT_F32, true>(nv) : pick_float_t<FDT_F32, false>(nv);
+    case SG_F16: return pick_float_t<FDT_F16, false>(nv);
+    case SG_Q8_0: return multi ? pick_float_t<FDT_Q8_0, true>(nv) : pick_float_t<FDT_Q8_0, false>(nv);
+    case SG_Q4_K: return multi ? pick_float_t<FDT_Q4_K, true>(nv) : pick_float_t<FDT_Q4_K, false>(nv);
+    default: return multi ? pick_float_t<FDT_Q6_K, true>(nv) : pick_float_t<FDT_Q6_K, false>(nv);
+    }
+}
+
+// has_multi_kernel (quant_multi.rs:220-227)
+bool float_has_multi(int32_t dt, uint64_t n) {
+    switch (dt) {
+    case SG_Q4_K: case SG_Q6_K: return n % 256 == 0;
+    case SG_Q8_0: return n % 32 == 0;
+    case SG_F32: return n % 8 == 0;
+    default: return false;
+    }
+}
+
+// matvec_rows_avx2 per vector (allow_multi false) or matmul_rows_avx2
+// (quant_multi.rs:232-273: rows_multi for several vectors when the format has
+// a shared-decode kernel).
+sg_status float_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
+                       uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, bool allow_multi, cudaStream_t stream) {
+    if (!d_base || !m) return SG_ERR_INVALID;
+    const int32_t dt = m->dtype;
+    if (dt != SG_F32 && dt != SG_F16 && dt != SG_Q8_0 && dt != SG_Q4_K && dt != SG_Q6_K) return SG_ERR_DTYPE;
+    uint64_t rb;
+    sg_status st = sg_row_bytes(dt, m->cols, &rb);
+    if (st) return st;
+    if (m->cols == 0 || m->cols > SG_MAX_COLS) return SG_ERR_SHAPE;
+    if (m->layout != SG_LAYOUT_GGUF) return SG_ERR_INVALID;
+    if (r0 > r1 || r1 > m->rows || m->rows > 0xFFFFFFFFull) return SG_ERR_INVALID;
+    if (r1 == r0 || n_vec == 0) return SG_OK;
+    if (!d_x || !d_out || (n_vec > 1 && (ldx < m->cols || ldo < m->rows))) return SG_ERR_INVALID;
+    const uint8_t *w = d_base + m->offset;
+    const uint64_t walign = dt == SG_Q4_K ? 16 : dt == SG_F32 ? 4 : 2;
+    if (!aligned(w, walign) || !aligned(d_x, 4) || !aligned(d_out, 4)) return SG_ERR_ALIGN;
+    const bool multi = allow_multi && n_vec > 1 && float_has_multi(dt, m->cols);
+    uint64_t group = FGEMV_MAXV;
+    if (dt == SG_Q4_K && !multi) {  // the per-vector sub-block sums live in 48 KB of shared memory
+        const uint64_t per = fgemv_smem_bytes(FDT_Q4_K, false, 1, (uint32_t)m->cols);
+        if (per > 48 * 1024) return SG_ERR_SHAPE;
+        group = 48 * 1024 / per < group ? 48 * 1024 / per : group;
+    }
+    for (uint64_t g = 0; g < n_vec; g += group) {
+        const uint64_t nv = n_vec - g < group ? n_vec - g : group;
+        FGemvArgs a;
+        memset(&a, 0, sizeof a);
+        a.w = w;
+        a.row_bytes = rb;
+        a.n = (uint32_t)m->cols;
+        a.r0 = (uint32_t)r0;
+        a.r1 = (uint32_t)r1;
+        a.nvec = (uint32_t)nv;
+        a.x = d_x + g * ldx;
+        a.ldx = ldx;
+        a.out = d_out + g * ldo;
+        a.ldo = ldo;
+        const uint32_t grid = (uint32_t)((r1 - r0 + FGEMV_ROWS - 1) / FGEMV_ROWS);
+        const uint32_t smem = fgemv_smem_bytes(dt, multi, (uint32_t)nv, (uint32_t)m->cols);
+        CK(launch_pdl((const void *)pick_float(dt, multi, nv), grid, FGEMV_THREADS, smem, stream, &a));
+    }
+    return SG_OK;
+}
+
 }  // namespace
 
 // ---- C ABI -----------------------------------------------------------------
@@ -885,6 +963,16 @@ sg_status sg_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x, ui
         if (st) return st;
     }
     return SG_OK;
+}
+
+sg_status sg_matvec_rows_float(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
+                               uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, void *stream) {
+    return float_matvec(d_base, m, d_x, ldx, d_out, ldo, n_vec, r0, r1, false, (cudaStream_t)stream);
+}
+
+sg_status sg_matmul_rows_float(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
+                               uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, void *stream) {
+    return float_matvec(d_base, m, d_x, ldx, d_out, ldo, n_vec, r0, r1, true, (cudaStream_t)stream);
 }
 
 uint64_t sg_matvec_scratch_bytes(uint64_t cols, uint64_t n_vec) { return n_vec * sg_q8k_bytes(cols); }

@@ -42,6 +42,13 @@ def make():
         xv = rng.fill(-1.0, 1.0, n)
         out[name + "_w"], out[name + "_x"] = w, xv
         out[name + "_out"] = O.matvec_rows(w, O.Mat(dt, n, rows), xv, 0, rows)
+    for name, dt in [("mf32", O.F32), ("mq8_0", O.Q8_0), ("mq4k", O.Q4_K), ("mq6k", O.Q6_K)]:
+        rng = O.Rng(0x9E3779B97F4A7C15)
+        n, rows, nvec = 512, 7, 5
+        w = O.random_matrix(dt, n, rows, rng)
+        xs = np.stack([rng.fill(-1.0, 1.0, n) for _ in range(nvec)])
+        out[name + "_w"], out[name + "_x"] = w, xs
+        out[name + "_out"] = O.matmul_rows_multi(w, O.Mat(dt, n, rows), list(xs), 0, rows)
     g = np.random.default_rng(5)
     wf = (g.standard_normal((16, 512)) * 0.02).astype(np.float32)
     out["wq_f32"] = wf

@@ -32,6 +32,13 @@ def test_float_matvec_fixtures():
         assert same(O.matvec_rows(w, O.Mat(dt, xv.size, want.size), xv, 0, want.size), want)
 
 
+def test_float_multi_fixtures():
+    for name, dt in [("mf32", O.F32), ("mq8_0", O.Q8_0), ("mq4k", O.Q4_K), ("mq6k", O.Q6_K)]:
+        w, xs, want = G[name + "_w"], G[name + "_x"], G[name + "_out"]
+        m = O.Mat(dt, xs.shape[1], want.shape[1])
+        assert same(O.matmul_rows_multi(w, m, list(xs), 0, m.rows), want)
+
+
 def test_weight_quantizer_fixtures():
     assert same(O.quantize_weights(O.Q4_K, G["wq_f32"]), G["wq_q4k"])
     assert same(O.quantize_weights(O.Q6_K, G["wq_f32"]), G["wq_q6k"])
