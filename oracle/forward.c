@@ -12,8 +12,9 @@
  * or_argmax      sample_from_logits   smollm_chat.rs:3661-3671 at temperature 0
  *
  * Scalar float code keeps the Rust expression order with one rounding per
- * operation (-ffp-contract=off); sinf/cosf/powf/expf/sqrtf are glibc's, as
- * Rust's f32 methods call them on Linux.
+ * operation (-ffp-contract=off); powf/sqrtf are glibc's and sin/cos/exp
+ * glibc's sinf/cosf/expf, as Rust's f32 methods call them on Linux (or the
+ * correctly rounded values, see libm.c).
  */
 #include <immintrin.h>
 #include <math.h>
@@ -56,7 +57,7 @@ void or_rope_rotate(float *v, size_t len, uint32_t head_dim, const float *inv_fr
         float *head = v + h0;
         for (uint32_t i = 0; i < half; i++) {
             float ang = pos * inv_freq[i];
-            float s = sinf(ang), c = cosf(ang);
+            float s = or_sinf(ang), c = or_cosf(ang);
             uint32_t a = neox ? i : 2 * i, b = neox ? i + half : 2 * i + 1;
             float x0 = head[a], x1 = head[b];
             float t0 = x0 * c, t1 = x1 * s;
@@ -113,8 +114,8 @@ AVX static void attn_head(const uint16_t *kc, const uint16_t *vc, size_t stride,
         float dot = or_dot_f16_row((const uint8_t *)k, q, head_dim);
         float score = dot * scale;
         float m_new = rmax(m_prev, score);
-        float alpha = expf(m_prev - m_new);
-        float p = expf(score - m_new);
+        float alpha = or_expf(m_prev - m_new);
+        float p = or_expf(score - m_new);
         float la = l_prev * alpha;
         l_prev = la + p;
         m_prev = m_new;

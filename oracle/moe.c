@@ -7,7 +7,8 @@
  *                                   top-k, prune), :1333-1351 (fused experts),
  *                                   :1367-1382 (shared expert)
  * Scalar float code follows the Rust expressions left to right with separate
- * roundings (-ffp-contract=off); exp is glibc expf, as Rust's f32::exp on Linux.
+ * roundings (-ffp-contract=off); exp is glibc expf, as Rust's f32::exp on Linux
+ * (or the correctly rounded value, see libm.c).
  */
 #include <math.h>
 #include <stdlib.h>
@@ -18,7 +19,7 @@
 /* silu, smollm_chat.rs:586-588: x / (1 + exp(-x)). */
 static float silu(float x)
 {
-    float e = expf(-x);
+    float e = or_expf(-x);
     float den = 1.0f + e;
     return x / den;
 }
@@ -142,7 +143,7 @@ int or_moe_route(const uint8_t *base, const or_moe *m, const float *x, float *pr
     if (rc) return rc;
     float mx = -INFINITY;
     for (size_t e = 0; e < ne; e++) mx = rmax(mx, probs[e]);
-    for (size_t e = 0; e < ne; e++) { float d = probs[e] - mx; probs[e] = expf(d); }
+    for (size_t e = 0; e < ne; e++) { float d = probs[e] - mx; probs[e] = or_expf(d); }
     float sum = 0.0f;
     for (size_t e = 0; e < ne; e++) sum += probs[e];
     for (size_t e = 0; e < ne; e++) probs[e] /= sum;
@@ -215,7 +216,7 @@ int or_moe_forward(const uint8_t *base, const or_moe *m, const float *x, float *
             const float *w = (const float *)(base + m->shared_gate_offset);
             float z = 0.0f;
             for (size_t c = 0; c < m->gate.cols; c++) { float p = w[c] * x[c]; z += p; }
-            float e = expf(-z);
+            float e = or_expf(-z);
             float den = 1.0f + e;
             gsc = 1.0f / den;
         }

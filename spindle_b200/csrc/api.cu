@@ -1112,7 +1112,7 @@ sg_status check_model(const sg_model *m) {
 }
 
 struct ModelScratch {
-    uint64_t x, xn, qx, q, k, v, att, proj, logits, h, freqs, sel1, moe, moe_bytes, total;
+    uint64_t x, xn, qx, q, k, v, att, proj, logits, h, freqs, sel1, amax, moe, moe_bytes, total;
 };
 
 ModelScratch model_scratch(const sg_model *m) {
@@ -1137,8 +1137,8 @@ ModelScratch model_scratch(const sg_model *m) {
     L.x = take(m->dim * 4);
     L.xn = take(m->dim * 4);
     L.qx = take(act_bytes(m->dim / 256));
-    L.q = take(q_dim * 4);
-    L.k = take(kv_dim * 4);
+    L.q = take((q_dim + kv_dim) * 4);  // q then k: one GEMV fills both when wk follows wq
+    L.k = L.q + q_dim * 4;
     L.v = take(kv_dim * 4);
     L.att = take(q_dim * 4);
     L.proj = take(m->dim * 4);
@@ -1146,6 +1146,7 @@ ModelScratch model_scratch(const sg_model *m) {
     L.h = take(n_ff * 4);
     L.freqs = take(m->head_dim / 2 * 4);
     L.sel1 = take(sizeof(sg_moe_choice));
+    L.amax = take(ARGMAX_CTAS * 8 + 8);  // the argmax's partial maxima, then its ticket count
     L.moe = take(moe);
     L.moe_bytes = moe;
     L.total = off;
@@ -1196,6 +1197,7 @@ sg_status sg_model_prepare(const sg_model *m, void *d_scratch, uint64_t scratch_
     uint8_t *sc = (uint8_t *)d_scratch;
     CK(cudaMemcpyAsync(sc + L.freqs, f.data(), f.size() * 4, cudaMemcpyHostToDevice, (cudaStream_t)stream));
     CK(cudaMemcpyAsync(sc + L.sel1, &one, sizeof one, cudaMemcpyHostToDevice, (cudaStream_t)stream));
+    CK(cudaMemsetAsync(sc + L.amax + ARGMAX_CTAS * 8, 0, 8, (cudaStream_t)stream));
     CK(cudaStreamSynchronize((cudaStream_t)stream));  // the host sources go out of scope
     return SG_OK;
 }
@@ -1226,10 +1228,13 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
     int dev;
     CK(cudaGetDevice(&dev));
     if (!(attr_done.load() >> dev & 1)) {
-        CK(cudaFuncSetAttribute((const void *)attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                227 * 1024));
+        for (const void *fn : {(const void *)attention_kernel<64>, (const void *)attention_kernel<128>,
+                               (const void *)attention_kernel<256>})
+            CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         attr_done.fetch_or(1ull << dev);
     }
+    const void *attn_fn = hd == 64 ? (const void *)attention_kernel<64>
+                          : hd == 128 ? (const void *)attention_kernel<128> : (const void *)attention_kernel<256>;
 
     EmbedArgs ea = {m->embed, m->embed_dtype, dim, m->vocab, m->embedding_scale, d_state, x};
     CK(launch_pdl((const void *)embed_kernel, (dim + 255) / 256, 256, 0, s, &ea));
@@ -1238,17 +1243,20 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
         // attention: norm (+ the previous layer's FFN residual), Q/K/V, head norms, RoPE, KV, attention
         if ((st = launch_norm(x, l ? proj : nullptr, m->residual_scale, y.attn_norm, m->rms_eps, dim, xn, qx, s)))
             return st;
-        if ((st = gemv_image(y.wq, y.wq_dtype, q_dim, dim, qx, q, s)) ||
-            (st = gemv_image(y.wk, y.wk_dtype, kv_dim, dim, qx, k, s)) ||
-            (st = gemv_image(y.wv, y.wv_dtype, kv_dim, dim, qx, v, s)))
+        // wk stored right after wq in the same format: one launch computes q and k (k follows q in scratch)
+        uint64_t wq_bytes = 0;
+        const bool qk_one = y.wk_dtype == y.wq_dtype && !sg_tiled16_bytes(y.wq_dtype, q_dim, dim, &wq_bytes) &&
+                            y.wk == y.wq + wq_bytes;
+        if (qk_one) {
+            if ((st = gemv_image(y.wq, y.wq_dtype, q_dim + kv_dim, dim, qx, q, s))) return st;
+        } else if ((st = gemv_image(y.wq, y.wq_dtype, q_dim, dim, qx, q, s)) ||
+                   (st = gemv_image(y.wk, y.wk_dtype, kv_dim, dim, qx, k, s))) {
             return st;
-        RopeArgs ra = {q, k, v, y.q_norm, y.k_norm, m->rms_eps, freqs, hd, m->n_heads, m->n_kv_heads,
-                       m->rope_neox, d_state, kc + l * cache, vc + l * cache, m->max_seq};
-        CK(launch_pdl((const void *)rope_kv_kernel, m->n_heads + m->n_kv_heads, 32, 0, s, &ra));
-        AttnArgs aa = {q, kc + l * cache, vc + l * cache, m->n_heads, m->n_kv_heads, hd, m->max_seq, scale,
-                       d_state, att};
-        CK(launch_pdl((const void *)attention_kernel, m->n_heads, ATTN_THREADS, attn_smem_bytes(hd, m->max_seq), s,
-                      &aa));
+        }
+        if ((st = gemv_image(y.wv, y.wv_dtype, kv_dim, dim, qx, v, s))) return st;
+        AttnArgs aa = {q, k, v, y.q_norm, y.k_norm, m->rms_eps, freqs, hd, m->n_heads, m->n_kv_heads, m->max_seq,
+                       m->rope_neox, scale, d_state, kc + l * cache, vc + l * cache, att};
+        CK(launch_pdl(attn_fn, m->n_heads, attn_threads(hd), attn_smem_bytes(hd, m->max_seq), s, &aa));
         {
             float *outs[1] = {proj};
             if ((st = launch_tiled(y.wo, y.wo_dtype == SG_Q4_K ? DT_Q4K : DT_Q6K, q_dim / 256, nullptr, att, q_dim,
@@ -1271,8 +1279,9 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
     if ((st = launch_norm(x, proj, m->residual_scale, m->output_norm, m->rms_eps, dim, xn, qx, s))) return st;
     if (d_hidden) CK(cudaMemcpyAsync(d_hidden, xn, dim * 4, cudaMemcpyDeviceToDevice, s));
     if ((st = gemv_image(m->lm_head, m->lm_head_dtype, m->vocab, dim, qx, logits, s))) return st;
-    ArgmaxArgs ga = {logits, m->vocab, d_state, d_token};
-    CK(launch_pdl((const void *)argmax_kernel, 1, ARGMAX_THREADS, 0, s, &ga));
+    ArgmaxArgs ga = {logits, m->vocab, d_state, d_token, (unsigned long long *)(sc + L.amax),
+                     (unsigned *)(sc + L.amax + ARGMAX_CTAS * 8)};
+    CK(launch_pdl((const void *)argmax_kernel, ARGMAX_CTAS, ARGMAX_THREADS, 0, s, &ga));
     return SG_OK;
 }
 

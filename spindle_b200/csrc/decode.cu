@@ -136,118 +136,156 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const __grid_cons
     }
 }
 
-// One warp per head: q heads first, then k heads (each also writes its v head).
-__global__ void rope_kv_kernel(const __grid_constant__ RopeArgs a) {
-    grid_dependency_wait();
-    grid_launch_dependents();
-    const uint32_t h = blockIdx.x, lane = threadIdx.x, hd = a.head_dim, half = hd / 2;
-    const bool is_q = h < a.n_heads;
-    const uint32_t kh = is_q ? 0u : h - a.n_heads;
-    const uint32_t pos = (uint32_t)a.state[1];
-    if (hd > 256 || (hd & 63u) || pos >= a.max_seq || blockDim.x != 32) {
-        if (lane == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
-        return;
-    }
-    const float *src = is_q ? a.q + h * hd : a.k + kh * hd;
-    const float *nw = is_q ? a.qn_w : a.kn_w;
-    // lane holds the pairs (i, i + half), i = lane + 32 j
-    constexpr int MAXP = 4;
-    const uint32_t np = half / 32;
-    float x0[MAXP], x1[MAXP];
-    __shared__ __align__(16) float hs[256];
-#pragma unroll
-    for (int j = 0; j < MAXP; j++)
-        if ((uint32_t)j < np) {
-            const uint32_t i = lane + 32u * j;
-            const uint32_t ia = a.neox ? i : 2 * i, ib = a.neox ? i + half : 2 * i + 1;
-            x0[j] = src[ia];
-            x1[j] = src[ib];
-            hs[ia] = x0[j];
-            hs[ib] = x1[j];
-        }
-    if (nw) {
-        // rmsnorm_heads: the head's sum of squares in element order, by lane 0
-        __syncwarp();
-        float inv = 0.0f;
-        if (lane == 0) inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(seq_sum_squares(hs, hd), (float)hd), a.eps)));
-        inv = __shfl_sync(0xffffffffu, inv, 0);
-#pragma unroll
-        for (int j = 0; j < MAXP; j++)
-            if ((uint32_t)j < np) {
-                const uint32_t i = lane + 32u * j;
-                const uint32_t ia = a.neox ? i : 2 * i, ib = a.neox ? i + half : 2 * i + 1;
-                x0[j] = __fmul_rn(__fmul_rn(x0[j], inv), nw[ia]);
-                x1[j] = __fmul_rn(__fmul_rn(x1[j], inv), nw[ib]);
-            }
-    }
-    const float fpos = (float)pos;
-    const uint32_t kv_dim = a.n_kv * hd;
-#pragma unroll
-    for (int j = 0; j < MAXP; j++)
-        if ((uint32_t)j < np) {
-            const uint32_t i = lane + 32u * j;
-            const uint32_t ia = a.neox ? i : 2 * i, ib = a.neox ? i + half : 2 * i + 1;
-            const float ang = __fmul_rn(fpos, a.inv_freq[i]);
-            const float s = (float)sin((double)ang), c = (float)cos((double)ang);
-            const float y0 = __fsub_rn(__fmul_rn(x0[j], c), __fmul_rn(x1[j], s));
-            const float y1 = __fadd_rn(__fmul_rn(x0[j], s), __fmul_rn(x1[j], c));
-            if (is_q) {
-                a.q[h * hd + ia] = y0;
-                a.q[h * hd + ib] = y1;
-            } else {
-                uint16_t *kr = a.kc + (uint64_t)pos * kv_dim + kh * hd;
-                kr[ia] = __half_as_ushort(__float2half_rn(y0));
-                kr[ib] = __half_as_ushort(__float2half_rn(y1));
-            }
-        }
-    if (!is_q) {
-        uint16_t *vr = a.vc + (uint64_t)pos * kv_dim + kh * hd;
-        for (uint32_t i = lane; i < hd; i += 32) vr[i] = __half_as_ushort(__float2half_rn(a.v[kh * hd + i]));
-    }
-}
-
-// One CTA per query head: compute_head_fn (smollm_chat.rs:3463-3495) with the
-// reference's bits.  Its online softmax is a recurrence over positions, but
-// most of it does not depend on the recurrence: the scores (dot_f16_row_avx2,
-// quant.rs:1412-1425, times scale), the running maxima m_t (a prefix maximum
-// under f32::max), alpha_t = exp(m_{t-1} - m_t) and p_t = exp(s_t - m_t) are
-// computed for all positions in parallel; only l_t = l_{t-1} * alpha_t + p_t
-// (one thread) and acc_t[d] = fma(p_t, v_t[d], acc_{t-1}[d] * alpha_t) (one
-// thread per d) run position by position.
-__global__ void __launch_bounds__(ATTN_THREADS) attention_kernel(const __grid_constant__ AttnArgs a) {
-    extern __shared__ __align__(16) float sm[];
-    grid_dependency_wait();
-    grid_launch_dependents();
-    const uint32_t h = blockIdx.x, hd = a.head_dim, tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+// One CTA per query head: this position's QK-norm, RoPE and f16 K/V (as
+// rmsnorm_heads, Rope::rotate and the cache write of forward_slice,
+// smollm_chat.rs:578-584, :1408-1419, :3431-3445), then compute_head_fn
+// (:3463-3495) with the reference's bits.  Its online softmax is a recurrence
+// over positions, but most of it does not depend on the recurrence: the scores
+// (dot_f16_row_avx2, quant.rs:1412-1425, times scale), the running maxima m_t (a
+// prefix maximum under f32::max), alpha_t = exp(m_{t-1} - m_t) and
+// p_t = exp(s_t - m_t) are computed for all positions in parallel; only
+// l_t = l_{t-1} * alpha_t + p_t (one thread) and
+// acc_t[d] = fma(p_t, v_t[d], acc_{t-1}[d] * alpha_t) (one thread per d) run
+// position by position.  The K and V rows of earlier positions were written by
+// earlier steps, so their bulk copies into shared memory are issued before the
+// kernel waits for its predecessor; positions go through in chunks of
+// ATTN_CHUNK rows.
+template <int HD>
+__global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const __grid_constant__ AttnArgs a) {
+    extern __shared__ __align__(16) uint8_t sm8[];
+    constexpr uint32_t RS = 2 * HD + ATTN_ROW_PAD, HALF = HD / 2;
+    const uint32_t h = blockIdx.x, tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint32_t nwarps = blockDim.x / 32, pos = (uint32_t)a.state[1], T = pos + 1;
-    if (hd > 256 || (hd & 63u) || pos >= a.max_seq || attn_smem_bytes(hd, a.max_seq) > dynamic_smem_size() ||
-        blockDim.x != ATTN_THREADS) {
+    const uint32_t msq = attn_seq4(a.max_seq);
+    if (a.head_dim != HD || pos >= a.max_seq || attn_smem_bytes(HD, a.max_seq) > dynamic_smem_size() ||
+        blockDim.x != attn_threads(HD) || a.n_heads % a.n_kv) {
+        grid_dependency_wait();
         if (tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
         return;
     }
-    // q | s (scores, then p) | al (alpha) | l
-    float *qs = sm, *sc = sm + hd, *al = sc + a.max_seq, *lsh = al + a.max_seq;
-    const uint32_t kvh = h / (a.n_heads / a.n_kv), kv_dim = a.n_kv * hd;
-    for (uint32_t d = tid; d < hd; d += blockDim.x) qs[d] = a.q[h * hd + d];
-    __syncthreads();
-    // scores: 8 lanes per position (the 8 AVX lanes), 4 positions per warp
-    const uint32_t grp = lane >> 3, l8 = lane & 7u, nsteps = hd / 8;
-    for (uint32_t t0 = warp * 4; t0 < T; t0 += nwarps * 4) {
-        const uint32_t t = t0 + grp;
-        float acc = 0.0f;
-        if (t < T) {
-            const uint16_t *kr = a.kc + (uint64_t)t * kv_dim + kvh * hd;
-            for (uint32_t i = 0; i < nsteps; i++)
-                acc = __fmaf_rn(__half2float(__ushort_as_half(kr[8 * i + l8])), qs[8 * i + l8], acc);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm8);       // [0] K rows, [1] V rows
+    float *lsh = reinterpret_cast<float *>(sm8 + 16);          // 1/l, then inv_q, inv_k
+    float *qs = reinterpret_cast<float *>(sm8 + 32);
+    float *hs = qs + HD;                                       // q, then k, before RoPE
+    float *sc = hs + 2 * HD, *al = sc + msq;
+    uint8_t *kbuf = reinterpret_cast<uint8_t *>(al + msq), *vbuf = kbuf + ATTN_CHUNK * RS;
+    uint16_t *kcur = reinterpret_cast<uint16_t *>(vbuf + ATTN_CHUNK * RS), *vcur = kcur + HD;
+    const uint32_t kvh = h / (a.n_heads / a.n_kv), kv_dim = a.n_kv * HD;
+    const uint16_t *kg = a.kc + kvh * HD, *vg = a.vc + kvh * HD;
+
+    // rows [c0, c1) of the earlier positions into the K (which = 0) or V
+    // buffer; staged[which] counts the copies issued (every thread alike)
+    bool ok = true;
+    uint32_t staged[2] = {0, 0};
+    auto stage = [&](uint32_t which, uint32_t c0, uint32_t c1) {
+        if (c1 <= c0 || !ok) return;
+        staged[which]++;
+        if (warp != 0) return;
+        if (lane == 0) mbar_arrive_expect_tx(&bars[which], (c1 - c0) * 2 * HD);
+        __syncwarp();
+        const uint16_t *src = which ? vg : kg;
+        uint8_t *dst = which ? vbuf : kbuf;
+        for (uint32_t t = c0 + lane; t < c1; t += 32) bulk_g2s(dst + (t - c0) * RS, src + (uint64_t)t * kv_dim, 2 * HD, &bars[which]);
+    };
+    auto wait_rows = [&](uint32_t which, uint32_t phase) {
+        if (!ok) return;
+        if (!mbar_wait_bounded(&bars[which], phase & 1u, WAIT_LIMIT_NS)) {
+            ok = false;
+            if (lane == 0) atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_TMA);
         }
-        // hsum_avx2: ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7)), + the empty tail (0.0)
-        const float x4 = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
-        const float x1 = __fadd_rn(x4, __shfl_down_sync(0xffffffffu, x4, 1));
-        const float x2 = __fadd_rn(x1, __shfl_down_sync(0xffffffffu, x1, 2));
-        if (t < T && l8 == 0) sc[t] = __fmul_rn(__fadd_rn(x2, 0.0f), a.scale);
+    };
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
     }
     __syncthreads();
-    // running maxima (f32::max ignores NaN: any grouping gives the same), by warp 0
+    const uint32_t first = pos < ATTN_CHUNK ? pos : ATTN_CHUNK;
+    stage(0, 0, first);
+    stage(1, 0, first);
+
+    grid_dependency_wait();
+    grid_launch_dependents();
+
+    // ---- this position: head norms, RoPE, f16 K and V ----
+    for (uint32_t d = tid; d < 2 * HD; d += blockDim.x) hs[d] = d < HD ? a.q[h * HD + d] : a.k[kvh * HD + d - HD];
+    for (uint32_t d = tid; d < HD; d += blockDim.x) vcur[d] = __half_as_ushort(__float2half_rn(a.v[kvh * HD + d]));
+    __syncthreads();
+    if ((tid == 0 && a.qn_w) || (tid == 32 && a.kn_w)) {
+        // rmsnorm_heads: the head's sum of squares in element order, one thread each for q and k
+        const float ss = seq_sum_squares(hs + (tid ? HD : 0), HD);
+        lsh[tid ? 2 : 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), a.eps)));
+    }
+    __syncthreads();
+    const float fpos = (float)pos;
+    for (uint32_t j = tid; j < HD; j += blockDim.x) {  // j < HALF: q pair j; else k pair j - HALF
+        const bool is_k = j >= HALF;
+        const uint32_t i = is_k ? j - HALF : j;
+        const uint32_t ia = a.neox ? i : 2 * i, ib = a.neox ? i + HALF : 2 * i + 1;
+        const float *src = hs + (is_k ? HD : 0);
+        float x0 = src[ia], x1 = src[ib];
+        const float *nw = is_k ? a.kn_w : a.qn_w;
+        if (nw) {
+            const float inv = lsh[is_k ? 2 : 1];
+            x0 = __fmul_rn(__fmul_rn(x0, inv), nw[ia]);
+            x1 = __fmul_rn(__fmul_rn(x1, inv), nw[ib]);
+        }
+        const float ang = __fmul_rn(fpos, a.inv_freq[i]);
+        const float s = (float)sin((double)ang), c = (float)cos((double)ang);
+        const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        if (!is_k) {
+            qs[ia] = y0;
+            qs[ib] = y1;
+        } else {
+            kcur[ia] = __half_as_ushort(__float2half_rn(y0));
+            kcur[ib] = __half_as_ushort(__float2half_rn(y1));
+        }
+    }
+    __syncthreads();
+    if (h % (a.n_heads / a.n_kv) == 0) {  // the group's first head stores this position's rows
+        for (uint32_t d = tid; d < HD; d += blockDim.x) {
+            a.kc[(uint64_t)pos * kv_dim + kvh * HD + d] = kcur[d];
+            a.vc[(uint64_t)pos * kv_dim + kvh * HD + d] = vcur[d];
+        }
+    }
+
+    // ---- scores, chunk by chunk: 8 lanes per position (the 8 AVX lanes) ----
+    const uint32_t grp = lane >> 3, l8 = lane & 7u;
+    uint32_t kph = 0;
+    for (uint32_t c0 = 0; c0 < T; c0 += ATTN_CHUNK) {
+        const uint32_t cn = T - c0 < ATTN_CHUNK ? T - c0 : ATTN_CHUNK;
+        const uint32_t cend = c0 + ATTN_CHUNK < pos ? c0 + ATTN_CHUNK : pos;  // rows copied: [c0, cend)
+        if (c0 > 0) {
+            __syncthreads();  // the previous chunk's rows are read
+            stage(0, c0, cend);
+        }
+        if (cend > c0) wait_rows(0, kph++);
+        if (pos < c0 + cn) {
+            for (uint32_t d = tid; d < HD; d += blockDim.x)
+                reinterpret_cast<uint16_t *>(kbuf + (pos - c0) * RS)[d] = kcur[d];
+        }
+        __syncthreads();
+        for (uint32_t t0 = warp * 4; t0 < cn; t0 += nwarps * 4) {
+            const uint32_t t = t0 + grp;
+            float acc = 0.0f;
+            if (t < cn && ok) {
+                const uint16_t *kr = reinterpret_cast<const uint16_t *>(kbuf + t * RS);
+#pragma unroll
+                for (uint32_t i = 0; i < HD / 8; i++)
+                    acc = __fmaf_rn(__half2float(__ushort_as_half(kr[8 * i + l8])), qs[8 * i + l8], acc);
+            }
+            // hsum_avx2: ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7)), + the empty tail (0.0)
+            const float x4 = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+            const float x1 = __fadd_rn(x4, __shfl_down_sync(0xffffffffu, x4, 1));
+            const float x2 = __fadd_rn(x1, __shfl_down_sync(0xffffffffu, x1, 2));
+            if (t < cn && l8 == 0) sc[c0 + t] = __fmul_rn(__fadd_rn(x2, 0.0f), a.scale);
+        }
+    }
+    __syncthreads();
+    // the next V chunk can land while the maxima are formed
+    uint32_t vph = 0;
+    // ---- running maxima (f32::max ignores NaN: any grouping gives the same), by warp 0 ----
     if (warp == 0) {
         float carry = -INFINITY;
         for (uint32_t t0 = 0; t0 < T; t0 += 32) {
@@ -270,49 +308,90 @@ __global__ void __launch_bounds__(ATTN_THREADS) attention_kernel(const __grid_co
             carry = __shfl_sync(0xffffffffu, m, 31);
         }
     }
-    __syncthreads();
-    if (tid == 0) {
-        float l = 0.0f;
-        for (uint32_t t = 0; t < T; t++) l = __fadd_rn(__fmul_rn(l, al[t]), sc[t]);
-        *lsh = __fdiv_rn(1.0f, l > 1e-9f ? l : 1e-9f);  // 1 / l.max(1e-9): a NaN l gives 1e-9
-    }
-    // acc[d] over positions, one thread per d (V loads run ahead of the chain)
-    float acc = 0.0f;
-    if (tid < hd) {
-        const uint16_t *vr = a.vc + kvh * hd + tid;
+    // ---- the two recurrences, chunk by chunk over V ----
+    float acc = 0.0f, l = 0.0f;
+    for (uint32_t c0 = 0; c0 < T; c0 += ATTN_CHUNK) {
+        const uint32_t cn = T - c0 < ATTN_CHUNK ? T - c0 : ATTN_CHUNK;
+        const uint32_t cend = c0 + ATTN_CHUNK < pos ? c0 + ATTN_CHUNK : pos;
+        __syncthreads();  // maxima done; the previous chunk's rows are read
+        if (c0 > 0) stage(1, c0, cend);
+        if (cend > c0) wait_rows(1, vph++);
+        if (pos < c0 + cn) {
+            for (uint32_t d = tid; d < HD; d += blockDim.x)
+                reinterpret_cast<uint16_t *>(vbuf + (pos - c0) * RS)[d] = vcur[d];
+        }
+        __syncthreads();
+        if (tid < HD && ok) {
+            const uint16_t *vr = reinterpret_cast<const uint16_t *>(vbuf) + tid;
 #pragma unroll 8
-        for (uint32_t t = 0; t < T; t++)
-            acc = __fmaf_rn(sc[t], __half2float(__ushort_as_half(vr[(uint64_t)t * kv_dim])), __fmul_rn(acc, al[t]));
+            for (uint32_t t = 0; t < cn; t++)
+                acc = __fmaf_rn(sc[c0 + t], __half2float(__ushort_as_half(vr[t * (RS / 2)])), __fmul_rn(acc, al[c0 + t]));
+        } else if (tid == HD) {
+            for (uint32_t t = 0; t < cn; t++) l = __fadd_rn(__fmul_rn(l, al[c0 + t]), sc[c0 + t]);
+        }
+    }
+    if (tid == HD) lsh[0] = __fdiv_rn(1.0f, l > 1e-9f ? l : 1e-9f);  // 1 / l.max(1e-9): a NaN l gives 1e-9
+    if (!ok && warp == 0) {
+        // a wait gave up: let the copies still in flight land (bounded) before the CTA exits
+        for (uint32_t w = 0; w < 2; w++)
+            if (staged[w]) mbar_wait_bounded(&bars[w], (staged[w] - 1) & 1u, WAIT_LIMIT_NS);
     }
     __syncthreads();
-    if (tid < hd) a.out[h * hd + tid] = __fmul_rn(acc, *lsh);
+    if (tid < HD) a.out[h * HD + tid] = ok ? __fmul_rn(acc, lsh[0]) : __int_as_float(0x7fc00000);
 }
 
-// One CTA: (total_cmp key, index) maximum with the larger index on ties.
+template __global__ void attention_kernel<64>(const __grid_constant__ AttnArgs);
+template __global__ void attention_kernel<128>(const __grid_constant__ AttnArgs);
+template __global__ void attention_kernel<256>(const __grid_constant__ AttnArgs);
+
+// ARGMAX_CTAS blocks: (total_cmp key, index) maxima with the larger index on
+// ties, then the last block to finish reduces them.
 __global__ void __launch_bounds__(ARGMAX_THREADS) argmax_kernel(const __grid_constant__ ArgmaxArgs a) {
-    __shared__ unsigned long long red[32];
+    __shared__ unsigned long long red[ARGMAX_THREADS / 32];
+    __shared__ bool last;
     grid_dependency_wait();
     grid_launch_dependents();
+    auto block_max = [&](unsigned long long best) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long u = __shfl_xor_sync(0xffffffffu, best, o);
+            best = u > best ? u : best;
+        }
+        if ((threadIdx.x & 31u) == 0) red[threadIdx.x >> 5] = best;
+        __syncthreads();
+        best = red[0];
+        for (uint32_t w = 1; w < blockDim.x / 32; w++) best = red[w] > best ? red[w] : best;
+        return best;
+    };
     unsigned long long best = 0;
-    for (uint32_t i = threadIdx.x; i < a.n; i += blockDim.x) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += gridDim.x * blockDim.x) {
         const int32_t b = __float_as_int(a.logits[i]);
         const uint32_t key = (uint32_t)(b ^ (int32_t)((uint32_t)(b >> 31) >> 1)) ^ 0x80000000u;
         const unsigned long long v = ((unsigned long long)key << 32) | i;
         best = v > best ? v : best;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long u = __shfl_xor_sync(0xffffffffu, best, o);
-        best = u > best ? u : best;
-    }
-    if ((threadIdx.x & 31u) == 0) red[threadIdx.x >> 5] = best;
-    __syncthreads();
+    best = block_max(best);
     if (threadIdx.x == 0) {
-        for (uint32_t w = 1; w < blockDim.x / 32; w++) best = red[w] > best ? red[w] : best;
+        a.partial[blockIdx.x] = best;
+        __threadfence();
+        last = atomicAdd(a.count, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    best = 0;
+    for (uint32_t b = threadIdx.x; b < gridDim.x; b += blockDim.x) {
+        const unsigned long long v = __ldcg(a.partial + b);
+        best = v > best ? v : best;
+    }
+    __syncthreads();  // red[] is reused
+    best = block_max(best);
+    if (threadIdx.x == 0) {
         const int32_t tok = (int32_t)(best & 0xFFFFFFFFull);
         a.state[0] = tok;
         a.state[1] = a.state[1] + 1;
         if (a.out) *a.out = tok;
+        *a.count = 0;
     }
 }
 

@@ -21,8 +21,8 @@
 namespace sg {
 
 constexpr uint32_t NORM_THREADS = 1024;
-constexpr uint32_t ATTN_THREADS = 256;
-constexpr uint32_t ARGMAX_THREADS = 1024;
+constexpr uint32_t ARGMAX_THREADS = 512;
+constexpr uint32_t ARGMAX_CTAS = 128;
 
 // x = dequant_row(embed[token]) * scale (dequant_row, quant.rs:1527-1660).
 struct EmbedArgs {
@@ -47,48 +47,55 @@ struct NormArgs {
     uint8_t *qx;
 };
 
-// Per-head RMSNorm of q and k (when weights are given), RoPE on both, and the
-// K and V rows of this position into the f16 caches (round to nearest even).
-struct RopeArgs {
-    float *q;
-    const float *k, *v;
+// One query head of grouped-query attention over positions 0..pos, with this
+// position's part done in the same kernel: the per-head RMSNorm of q and k
+// (when weights are given), RoPE on both, and K and V rounded to f16 (round to
+// nearest even).  The first query head of each KV group writes this position's
+// K and V rows into the caches; every head uses its own copy of them.
+struct AttnArgs {
+    const float *q, *k, *v;     // this position: [n_heads*hd], [n_kv*hd], [n_kv*hd]
     const float *qn_w, *kn_w;   // [head_dim] or null
     float eps;
     const float *inv_freq;      // [head_dim / 2], from the host (glibc powf)
-    uint32_t head_dim, n_heads, n_kv;
+    uint32_t head_dim, n_heads, n_kv, max_seq;
     int32_t neox;
+    float scale;
     const int32_t *state;       // state[1] = pos
     uint16_t *kc, *vc;          // this layer's caches: [max_seq][n_kv * head_dim]
-    uint32_t max_seq;
-};
-
-// Grouped-query attention of one token over positions 0..pos.
-struct AttnArgs {
-    const float *q;
-    const uint16_t *kc, *vc;
-    uint32_t n_heads, n_kv, head_dim, max_seq;
-    float scale;
-    const int32_t *state;
-    float *out;
+    float *out;                 // [n_heads * head_dim]
 };
 
 // The greedy token (f32::total_cmp, last maximum on ties), written as the next
-// step's token; the position advances.
+// step's token; the position advances.  ARGMAX_CTAS blocks each reduce a
+// strided share to one (key, index) pair in partial[]; the last block to
+// finish (ticket count) reduces those and resets the count to 0.
 struct ArgmaxArgs {
     const float *logits;
     uint32_t n;
     int32_t *state;
     int64_t *out;               // optional: the token, also kept here
+    unsigned long long *partial;  // [ARGMAX_CTAS]
+    unsigned *count;            // 0 before the launch, 0 after it
 };
 
-// q | scores, then p | alpha | 1/l
+// Positions of K and V staged in shared memory at a time, and the padding of a
+// staged row (spreads the rows of one warp's positions over the banks).
+constexpr uint32_t ATTN_CHUNK = 128;
+constexpr uint32_t ATTN_ROW_PAD = 16;
+
+__host__ __device__ inline uint32_t attn_threads(uint32_t head_dim) { return head_dim < 256 ? 256u : 288u; }
+
+// bars, 1/l, inverse norms | q | q, k before RoPE | scores, then p | alpha |
+// K rows | V rows | this position's K, V (f16); every part 16-byte aligned
+__host__ __device__ inline uint32_t attn_seq4(uint32_t max_seq) { return (max_seq + 3u) & ~3u; }
 __host__ __device__ inline uint32_t attn_smem_bytes(uint32_t head_dim, uint32_t max_seq) {
-    return (head_dim + 2u * max_seq + 4u) * 4u;
+    return 32u + 3u * head_dim * 4u + 2u * attn_seq4(max_seq) * 4u + 2u * ATTN_CHUNK * (2u * head_dim + ATTN_ROW_PAD) +
+           2u * head_dim * 2u;
 }
 
 __global__ void embed_kernel(const __grid_constant__ EmbedArgs a);
 __global__ void rmsnorm_kernel(const __grid_constant__ NormArgs a);
-__global__ void rope_kv_kernel(const __grid_constant__ RopeArgs a);
+template <int HD>
 __global__ void attention_kernel(const __grid_constant__ AttnArgs a);
 __global__ void argmax_kernel(const __grid_constant__ ArgmaxArgs a);
 

@@ -59,9 +59,11 @@ def _ptr(t):
 class Decoder:
     """Device weights, KV cache, scratch and the {token, pos} state of one model."""
 
-    def __init__(self, cfg, weights, dtypes, device):
+    def __init__(self, cfg, weights, dtypes, device, qk_adjacent=True):
         """weights: name -> CUDA tensor (uint8 GGUF rows for matrices, float32
-        vectors); dtypes: name -> GGML dtype of each matrix."""
+        vectors); dtypes: name -> GGML dtype of each matrix.  qk_adjacent: store
+        each layer's wk right after its wq when both have one format, which lets
+        sg_forward compute q and k in one launch."""
         self.cfg, self.dev = dict(cfg), device
         c = self.cfg
         self.keep = []  # every device buffer the model points at
@@ -72,6 +74,16 @@ class Decoder:
             t, _ = repack_tiled16(dtypes[name], weights[name], rows, cols)
             self.keep.append(t)
             return t.data_ptr()
+
+        def tiled_pair(a, rows_a, b, rows_b, cols):
+            # both matrices in one buffer, b's tiles right after a's
+            na, nb = tiled16_bytes(dtypes[a], rows_a, cols), tiled16_bytes(dtypes[b], rows_b, cols)
+            t = torch.empty(na + nb, dtype=torch.uint8, device=device)
+            for name, rows, off in [(a, rows_a, 0), (b, rows_b, na)]:
+                _lib.check(lib().sg_repack_tiled16(dtypes[name], C.c_void_p(weights[name].data_ptr()), rows, cols,
+                                                   C.c_void_p(t.data_ptr() + off), _stream()), "repack_tiled16")
+            self.keep.append(t)
+            return t.data_ptr(), t.data_ptr() + na
 
         def vec(name):
             t = weights.get(name)
@@ -88,8 +100,11 @@ class Decoder:
             y = SgLayer()
             y.attn_norm, y.ffn_norm = vec(p + "attn_norm"), vec(p + "ffn_norm")
             y.q_norm, y.k_norm = vec(p + "q_norm"), vec(p + "k_norm")
-            y.wq, y.wq_dtype = tiled(p + "wq", q_dim, dim), dtypes[p + "wq"]
-            y.wk, y.wk_dtype = tiled(p + "wk", kv_dim, dim), dtypes[p + "wk"]
+            if qk_adjacent and dtypes[p + "wq"] == dtypes[p + "wk"]:
+                y.wq, y.wk = tiled_pair(p + "wq", q_dim, p + "wk", kv_dim, dim)
+            else:
+                y.wq, y.wk = tiled(p + "wq", q_dim, dim), tiled(p + "wk", kv_dim, dim)
+            y.wq_dtype, y.wk_dtype = dtypes[p + "wq"], dtypes[p + "wk"]
             y.wv, y.wv_dtype = tiled(p + "wv", kv_dim, dim), dtypes[p + "wv"]
             y.wo, y.wo_dtype = tiled(p + "wo", dim, q_dim), dtypes[p + "wo"]
             if moe:
