@@ -170,6 +170,45 @@ SG_API sg_status sg_matmul_rows_float(const uint8_t *d_base, const sg_mat *m, co
                                       float *d_out, uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1,
                                       void *stream);
 
+/* ---- Row-split tensor parallelism over NVLink (one process per GPU) --------
+ *
+ * par_rows (smollm_chat.rs:332-337) splits a matvec's rows across threads;
+ * sg_matvec_tp splits them across GPUs the same way (rank p of P owns rows
+ * [R*p/P, R*(p+1)/P), results independent of the split, quant_q8k.rs:393-394)
+ * and fuses the gather that follows: the GEMV's epilogue stores each row of
+ * its shard straight into the output buffer of every rank (peer stores over
+ * NVLink, through CUDA IPC mappings; no copy kernel, no NCCL call), then the
+ * rank's last block adds 1 to every rank's arrival counter, and the launch
+ * ends only when its own counter shows all ranks for this call.  Every rank
+ * must make the same sequence of calls.  A wait that runs out (2 s) makes
+ * sg_device_status return SG_ERR_TIMEOUT.  A call's output buffer must not be
+ * rewritten by a later call before its readers are done (alternate two).
+ *
+ * Set-up: each rank allocates a comm block of sg_tp_comm_bytes() (256-byte
+ * aligned, device memory from cudaMalloc / sg_alloc), zeroes it with
+ * sg_tp_comm_init, and shares it and its full-size output buffer with the
+ * others through sg_ipc_get_handle / sg_ipc_open (the handle is
+ * sg_ipc_handle_bytes() long; the exchange itself is the caller's, e.g. an
+ * all-gather over its process group). */
+#define SG_TP_MAX_RANKS 8
+#define SG_TP_COMM_BYTES 256
+typedef struct {
+    uint32_t n_ranks, rank;
+    float *outs[SG_TP_MAX_RANKS];   /* the call's output on every rank (this rank's own pointer at [rank]) */
+    void *comms[SG_TP_MAX_RANKS];   /* every rank's comm block, likewise */
+} sg_tp_group;
+SG_API uint64_t sg_ipc_handle_bytes(void);
+SG_API sg_status sg_ipc_get_handle(void *d_ptr, void *handle_out);
+SG_API sg_status sg_ipc_open(const void *handle, void **d_out);
+SG_API sg_status sg_ipc_close(void *d_ptr);
+SG_API uint64_t sg_tp_comm_bytes(void);
+SG_API sg_status sg_tp_comm_init(void *d_comm, void *stream);
+/* This rank's shard (TILED16, m->rows rows, global rows row0 .. row0 + rows)
+ * times x_b (fp32, b < n_vec <= 8, 16-byte aligned, ldx apart); row r of
+ * vector b lands at outs[q][b*ldo + row0 + r] on every rank q. */
+SG_API sg_status sg_matvec_tp(const uint8_t *d_shard, const sg_mat *m, const float *d_x, uint64_t ldx,
+                              uint64_t n_vec, uint64_t row0, uint64_t ldo, const sg_tp_group *grp, void *stream);
+
 /* The same matvec for either layout with the Q8_K images in caller-owned
  * scratch (the reference keeps them in thread-local scratch, quant_q8k.rs:
  * 123-142): quantizes x_b into d_scratch (>= sg_matvec_scratch_bytes(cols,

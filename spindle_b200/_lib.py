@@ -50,6 +50,14 @@ class SgMoe(C.Structure):
                 ("shared_n_ff", C.c_uint64), ("shared_gate", C.c_void_p)]
 
 
+TP_MAX_RANKS = 8
+
+
+class SgTpGroup(C.Structure):
+    _fields_ = [("n_ranks", C.c_uint32), ("rank", C.c_uint32), ("outs", C.c_void_p * TP_MAX_RANKS),
+                ("comms", C.c_void_p * TP_MAX_RANKS)]
+
+
 P, U64, I32 = C.c_void_p, C.c_uint64, C.c_int32
 
 # name -> (restype, argtypes); every function the header declares.
@@ -74,6 +82,13 @@ SIGNATURES = {
     "sg_matvec": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
     "sg_matvec_rows_float": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
     "sg_matmul_rows_float": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
+    "sg_ipc_handle_bytes": (U64, []),
+    "sg_ipc_get_handle": (I32, [P, P]),
+    "sg_ipc_open": (I32, [P, C.POINTER(P)]),
+    "sg_ipc_close": (I32, [P]),
+    "sg_tp_comm_bytes": (U64, []),
+    "sg_tp_comm_init": (I32, [P, P]),
+    "sg_matvec_tp": (I32, [P, C.POINTER(SgMat), P, U64, U64, U64, U64, P, P]),
     "sg_matvec_scratch_bytes": (U64, [U64, U64]),
     "sg_matvec_scratch": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P, U64, P]),
     "sg_matvec_static": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),

@@ -383,9 +383,22 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
 // One of xq (Q8_K inputs) or x (fp32 inputs, vector b at x + b*ldx) is given.
 // With image (one vector): x is the Q8_K shared-memory image made by the
 // kernel before (act_bytes(nb) bytes), copied in by one bulk copy.
+// Row-split tensor parallelism of one launch: where the rows go and the
+// arrival counters (see TGemvArgs).
+struct TpSpec {
+    uint32_t n;
+    uint32_t row_off;
+    float *out[TP_MAX_RANKS];   // vector 0, row 0 of the full output on every rank
+    uint64_t ldo;
+    unsigned long long *flag[TP_MAX_RANKS];
+    unsigned long long *my_flag;
+    unsigned *ticket;
+    unsigned long long *epoch;
+};
+
 sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, const float *x, uint64_t ldx,
                        float *const *outs, uint64_t n_vec, uint64_t r0, uint64_t r1, cudaStream_t stream,
-                       const uint8_t *image = nullptr) {
+                       const uint8_t *image = nullptr, const TpSpec *tp = nullptr) {
     if (image && n_vec != 1) return SG_ERR_INVALID;
     const uint32_t t0 = (uint32_t)(r0 / TILE_ROWS), t1 = (uint32_t)((r1 + TILE_ROWS - 1) / TILE_ROWS);
     const bool qx = x != nullptr;
@@ -397,6 +410,8 @@ sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, 
         while ((st = tiled_plan(dt, nb, t1 - t0, nv, qx ? IN_F32 : IN_Q8K, 0, &p)) == SG_ERR_SHAPE && nv > 1)
             nv = nv > 4 ? 4 : nv / 2;
         if (st) return st;
+        // a row-split call is one launch on every rank (each launch is one arrival round)
+        if (tp && (uint64_t)nv < n_vec) return SG_ERR_SHAPE;
         TGemvArgs a;
         memset(&a, 0, sizeof a);
         a.w = w;
@@ -426,7 +441,19 @@ sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, 
                 a.xs[v] = xq[g + v].qs;
                 a.xb[v] = xq[g + v].bsums;
             }
-            a.out[v] = outs[g + v];
+            if (outs) a.out[v] = outs[g + v];
+        }
+        if (tp) {
+            a.npeers = tp->n;
+            a.row_off = tp->row_off;
+            a.out_stride = tp->ldo;
+            for (uint32_t q = 0; q < tp->n; q++) {
+                a.peer_out[q] = tp->out[q] + g * tp->ldo;
+                a.peer_flag[q] = tp->flag[q];
+            }
+            a.my_flag = tp->my_flag;
+            a.ticket = tp->ticket;
+            a.epoch = tp->epoch;
         }
         CK(launch_pdl((const void *)p.fn, p.grid, p.warps * 32, p.smem, stream, &a));
         g += (uint64_t)nv;
@@ -843,7 +870,7 @@ sg_status sg_device_status(void) {
     unsigned v = 0, zero = 0;
     CK(cudaMemcpyFromSymbol(&v, g_dev_status, sizeof v));
     if (v) CK(cudaMemcpyToSymbol(g_dev_status, &zero, sizeof zero));
-    return v == DEV_OK ? SG_OK : v == DEV_BAD_LAUNCH ? SG_ERR_INVALID : SG_ERR_TIMEOUT;
+    return v == DEV_OK ? SG_OK : v == DEV_BAD_LAUNCH ? SG_ERR_INVALID : SG_ERR_TIMEOUT;  // TMA or peer wait
 }
 
 sg_status sg_matmul_rows(const uint8_t *d_base, const sg_mat *m, const sg_q8k *xq, float *const *outs,
@@ -973,6 +1000,70 @@ sg_status sg_matvec_rows_float(const uint8_t *d_base, const sg_mat *m, const flo
 sg_status sg_matmul_rows_float(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
                                uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, void *stream) {
     return float_matvec(d_base, m, d_x, ldx, d_out, ldo, n_vec, r0, r1, true, (cudaStream_t)stream);
+}
+
+uint64_t sg_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+sg_status sg_ipc_get_handle(void *d_ptr, void *handle_out) {
+    if (!d_ptr || !handle_out) return SG_ERR_INVALID;
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, d_ptr));
+    memcpy(handle_out, &h, sizeof h);
+    return SG_OK;
+}
+
+sg_status sg_ipc_open(const void *handle, void **d_out) {
+    if (!handle || !d_out) return SG_ERR_INVALID;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    CK(cudaIpcOpenMemHandle(d_out, h, cudaIpcMemLazyEnablePeerAccess));
+    return SG_OK;
+}
+
+sg_status sg_ipc_close(void *d_ptr) {
+    if (!d_ptr) return SG_ERR_INVALID;
+    CK(cudaIpcCloseMemHandle(d_ptr));
+    return SG_OK;
+}
+
+uint64_t sg_tp_comm_bytes(void) { return SG_TP_COMM_BYTES; }
+
+sg_status sg_tp_comm_init(void *d_comm, void *stream) {
+    if (!d_comm) return SG_ERR_INVALID;
+    if (!aligned(d_comm, 256)) return SG_ERR_ALIGN;
+    CK(cudaMemsetAsync(d_comm, 0, SG_TP_COMM_BYTES, (cudaStream_t)stream));
+    return SG_OK;
+}
+
+sg_status sg_matvec_tp(const uint8_t *d_shard, const sg_mat *m, const float *d_x, uint64_t ldx, uint64_t n_vec,
+                       uint64_t row0, uint64_t ldo, const sg_tp_group *grp, void *stream) {
+    int dt;
+    sg_status st = check_mat(d_shard, m, 0, m ? m->rows : 0, &dt);
+    if (st) return st;
+    if (m->layout != SG_LAYOUT_TILED16 || !grp || !grp->n_ranks || grp->n_ranks > SG_TP_MAX_RANKS ||
+        grp->rank >= grp->n_ranks)
+        return SG_ERR_INVALID;
+    if (m->rows == 0 || n_vec == 0) return SG_ERR_INVALID;  // every rank must arrive, so no empty calls
+    if (!d_x || (n_vec > 1 && ldx < m->cols) || row0 + m->rows > ldo || row0 + m->rows > 0xFFFFFFFFull)
+        return SG_ERR_INVALID;
+    if (!aligned(d_x, 16) || (n_vec > 1 && ldx % 4)) return SG_ERR_ALIGN;
+    TpSpec tp;
+    memset(&tp, 0, sizeof tp);
+    tp.n = grp->n_ranks;
+    tp.row_off = (uint32_t)row0;
+    tp.ldo = ldo;
+    for (uint32_t q = 0; q < grp->n_ranks; q++) {
+        if (!grp->outs[q] || !grp->comms[q]) return SG_ERR_INVALID;
+        if (!aligned(grp->outs[q], 4) || !aligned(grp->comms[q], 256)) return SG_ERR_ALIGN;
+        tp.out[q] = grp->outs[q];
+        tp.flag[q] = (unsigned long long *)grp->comms[q];
+    }
+    uint8_t *mine = (uint8_t *)grp->comms[grp->rank];
+    tp.my_flag = (unsigned long long *)mine;
+    tp.ticket = (unsigned *)(mine + 64);
+    tp.epoch = (unsigned long long *)(mine + 128);
+    return launch_tiled(d_shard + m->offset, dt, (uint32_t)(m->cols / 256), nullptr, d_x, ldx, nullptr, n_vec, 0,
+                        m->rows, (cudaStream_t)stream, nullptr, &tp);
 }
 
 uint64_t sg_matvec_scratch_bytes(uint64_t cols, uint64_t n_vec) { return n_vec * sg_q8k_bytes(cols); }

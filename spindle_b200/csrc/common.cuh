@@ -11,7 +11,7 @@ namespace sg {
 
 // Device-side status word: bounded waits record where they gave up instead of
 // hanging or trapping; the host reads it with sg_device_status().
-enum : unsigned { DEV_OK = 0, DEV_TIMEOUT_TMA = 1, DEV_BAD_LAUNCH = 2 };
+enum : unsigned { DEV_OK = 0, DEV_TIMEOUT_TMA = 1, DEV_BAD_LAUNCH = 2, DEV_TIMEOUT_PEER = 3 };
 extern __device__ unsigned g_dev_status;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -84,7 +84,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
 }
 
 // Global -> shared bulk copy completing on `bar` (16-byte aligned addresses,
-// size a multiple of 16).  No multicast.
+// size a multiple of 16), one destination CTA.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

@@ -6,6 +6,38 @@
 namespace sg {
 using namespace tiled;
 
+// The end of a row-split launch: every thread's peer stores are made visible
+// system-wide, the CTAs take tickets, and the last one adds 1 to every rank's
+// arrival counter (release), then waits until its own counter shows all ranks
+// for this call (acquire; bounded, DEV_TIMEOUT_PEER on expiry) and advances the
+// epoch.  Counters only grow, so no rank ever resets another's.
+__device__ __noinline__ void tp_arrive_and_wait(const TGemvArgs &a) {
+    __threadfence_system();
+    __syncthreads();
+    bool mine = false;
+    if (threadIdx.x == 0) mine = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+    // no static shared memory here: the launch gives all 227 KB to the dynamic part
+    const bool last = __syncthreads_or(mine);
+    if (!last || threadIdx.x != 0) return;
+    __threadfence_system();
+    *a.ticket = 0;  // every CTA of this launch has its ticket
+    for (uint32_t p = 0; p < a.npeers; p++)
+        asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(a.peer_flag[p]) : "memory");
+    const unsigned long long target = (*a.epoch + 1ull) * a.npeers;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a.my_flag) : "memory");
+        if (v >= target) break;
+        if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+            atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_PEER);
+            break;
+        }
+        __nanosleep(64);
+    }
+    *a.epoch += 1ull;
+}
+
 template <int DT, int NV, int MODE>
 __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const __grid_constant__ TGemvArgs a) {
     constexpr uint32_t CB = tiled_col_bytes(DT);
@@ -24,6 +56,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
         (MOE && a.swiglu && (MODE != IN_MOE_X || a.nvec != 1)) ||
         (MOE && (a.max_slots > MOE_MAXK || a.tiles_per_mat == 0 || nact == 0 ||
                  (uint64_t)a.ntiles * gridDim.x >= (1ull << 32) || a.ntiles < a.max_slots * a.tiles_per_mat)) ||
+        (a.npeers && (MOE || a.npeers > TP_MAX_RANKS || !a.my_flag || !a.ticket || !a.epoch)) ||
         (MODE == IN_MOE_X && a.logits &&
          (a.n_expert == 0 || a.n_used == 0 || a.n_used > a.n_expert || a.n_used > MOE_MAXK ||
           moe_select_bytes(a.n_expert) > nwarps * a.nstages * a.stage_bytes))) {
@@ -379,10 +412,19 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                     const uint32_t j = mt * 8 + r;
                     if (g == 0 && r < 8 && 2 * j < a.r1) dst[j] = silu_mul(yv, up);
                 } else if (g == 0 && v < (int)a.nvec && row >= a.r0 && row < a.r1) {
-                    dst[row] = yv;
+                    if (!MOE && a.npeers) {
+                        // the row shard goes straight into every rank's output (NVLink peer stores)
+                        const uint64_t o = (uint64_t)v * a.out_stride + a.row_off + row;
+                        for (uint32_t p = 0; p < a.npeers; p++) a.peer_out[p][o] = yv;
+                    } else {
+                        dst[row] = yv;
+                    }
                 }
             }
         }
+    }
+    if constexpr (!MOE) {
+        if (a.npeers) tp_arrive_and_wait(a);
     }
 }
 

@@ -61,6 +61,8 @@ __host__ __device__ inline uint32_t act_bytes(uint32_t nb) { return nb * 256u + 
 constexpr int IN_Q8K = 0, IN_F32 = 1, IN_MOE_X = 2, IN_MOE_H = 3;
 constexpr uint32_t MOE_MAXK = SG_MOE_MAX_USED;
 
+constexpr uint32_t TP_MAX_RANKS = 8;
+
 struct TGemvArgs {
     const uint8_t *w;     // TILED16 buffer (16-byte aligned)
     uint32_t nb;          // super-blocks per row
@@ -98,6 +100,18 @@ struct TGemvArgs {
     uint32_t n_ff;        // IN_MOE_H
     const float *gu;      // IN_MOE_H
     uint64_t gu_stride;   // IN_MOE_H, floats
+    // Row-split tensor parallelism (IN_Q8K / IN_F32, npeers > 0): row r of
+    // vector v goes to peer_out[p][v * out_stride + row_off + r] on every rank
+    // p (out[] unused); then each rank's last CTA adds 1 to every rank's
+    // arrival counter and waits until its own counter reaches
+    // (*epoch + 1) * npeers.
+    uint32_t npeers;
+    uint32_t row_off;
+    float *peer_out[TP_MAX_RANKS];
+    unsigned long long *peer_flag[TP_MAX_RANKS];
+    unsigned long long *my_flag;
+    unsigned *ticket;
+    unsigned long long *epoch;
 };
 
 // In the MoE modes the choice is kept at the top of the barrier area: n at

@@ -1,0 +1,105 @@
+"""Rank bodies for the multi-process tests of spindle_b200.tp (run under
+torch.multiprocessing spawn; 127.0.0.1 rendezvous)."""
+import datetime
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def init(rank, world, port, backend):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    kw = {}
+    if backend == "nccl":
+        import torch
+        torch.cuda.set_device(rank)
+        kw["device_id"] = torch.device("cuda", rank)
+    dist.init_process_group(backend, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60), **kw)
+
+
+def cpu_rank(rank, world, port, out):
+    # host logic only: the shard split and the rank-ordered exchange
+    import torch.distributed as dist
+    from spindle_b200.tp import exchange, shard_rows
+    init(rank, world, port, "gloo")
+    try:
+        got = exchange(("rank", rank, b"\x01" * 64), None)
+        assert got == [("rank", q, b"\x01" * 64) for q in range(world)]
+        for rows in [1, 7, 16, 1000, 4096, 151936]:
+            parts = exchange(shard_rows(rows, world, rank), None)
+            assert parts[0][0] == 0 and parts[-1][1] == rows
+            assert all(parts[q][1] == parts[q + 1][0] for q in range(world - 1))
+        out.put((rank, "ok"))
+    except Exception as e:  # reported to the parent
+        out.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+SHAPES = [(12, 4096, 4096), (14, 1000, 1024), (12, 14336, 2048), (14, 2048, 768 * 4)]
+
+
+def gpu_rank(rank, world, port, out):
+    # the fused row-split GEMV against the whole matrix on one GPU, bit for bit
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import spindle_b200 as sg
+    from spindle_b200.tp import ShardedMatrix, TpGroup, matvec_tp
+    init(rank, world, port, "nccl")
+    dev = torch.device("cuda", rank)
+    grp = None
+    try:
+        grp = TpGroup(device=dev)
+        g = torch.Generator(device=dev).manual_seed(3)
+        for dt, rows, cols in SHAPES:
+            w = sg.quantize_weights(dt, torch.randn(rows, cols, device=dev, generator=g) * 0.02)
+            full, mf = sg.repack_tiled16(dt, w, rows, cols)
+            shard = ShardedMatrix(dt, w, rows, cols, world, rank)
+            for nv in [1, 3]:
+                buf = grp.buffer(nv, rows)
+                for it in range(4):
+                    xs = torch.randn(nv, cols, device=dev, generator=g)
+                    got = matvec_tp(shard, xs, grp, buf)
+                    want = sg.matvec(full, mf, xs)
+                    torch.cuda.synchronize(dev)
+                    ok = np.array_equal(got.cpu().numpy().view(np.uint32), want.cpu().numpy().view(np.uint32))
+                    dist.barrier()  # no rank writes the next call's rows while another still reads these
+                    assert ok, (dt, rows, cols, nv, it)
+                # a captured call replayed: the epoch lives on the device
+                xs = torch.randn(nv, cols, device=dev, generator=g)
+                s = torch.cuda.Stream(device=dev)
+                s.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(s):
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph, stream=s):
+                        matvec_tp(shard, xs, grp, buf, stream=s)
+                    want = sg.matvec(full, mf, xs, stream=s)
+                    for _ in range(3):
+                        buf.tensor.fill_(float("nan"))
+                        torch.cuda.synchronize(dev)
+                        dist.barrier()  # every rank's buffer is cleared before any rank writes
+                        graph.replay()
+                        torch.cuda.synchronize(dev)
+                        ok = np.array_equal(buf.tensor.cpu().numpy().view(np.uint32),
+                                            want.cpu().numpy().view(np.uint32))
+                        dist.barrier()
+                        assert ok, (dt, rows, "graph")
+                del graph
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+        sg.device_status()
+        out.put((rank, "ok"))
+    except Exception as e:
+        out.put((rank, repr(e)))
+    finally:
+        if grp is not None:
+            try:
+                grp.close()
+            except Exception as e:
+                out.put((rank, "close: " + repr(e)))
+        dist.destroy_process_group()
