@@ -188,9 +188,11 @@ def run_reference(args):
         O.pool_destroy()
     value = bytes_step * args.steps / el / 1e9
     sample = "each step: rows [0, %.4g x rows) of every sweep matrix" % frac if frac < 1 else "each step: the full sweep"
-    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int32 + fp32",
+    tp = getattr(args, "workload", "gemv") == "gemv_tp"
+    line = {"impl": "reference", "metric": TP_METRIC if tp else METRIC, "value": round(value, 3), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "int8/int32 + fp32",
             "data": "synthetic", "config": config_block(args, 1),
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": sample + "; oracle = C restatement of quant_q8k.rs with the worker pool"},
@@ -676,6 +678,156 @@ def run_gpu_moe(args):
 # One step = one token through forward_slice + LM head + argmax, replayed from
 # one captured graph (the token and position are device state).
 
+TP_METRIC = "K-quant GEMV HBM GB/s, rows split over the GPUs with the gather fused in (Q4_K/Q6_K x Q8_K sweep)"
+
+
+def run_gpu_tp(args):
+    """The sweep's matrices split by rows over the ranks (strong scaling): every
+    rank holds its par_rows shard of all seven, and one sg_matvec_tp per
+    matrix leaves the whole output on every rank (peer stores over NVLink,
+    arrival counters; no NCCL call on the data path)."""
+    import torch
+    import torch.distributed as dist
+
+    import spindle_b200 as sg
+    from spindle_b200 import _lib
+    from spindle_b200.tp import ShardedMatrix, TpGroup, matvec_tp
+
+    rank, world, local = rank_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    nvec = args.nvec
+    gen = torch.Generator(device=dev).manual_seed(1000)  # the same full matrices on every rank
+    grp = TpGroup(device=dev)
+    shards, X, BUF = [], [], []
+    for dt, r, c in SHAPES:
+        wf = torch.randn(r, c, device=dev, generator=gen) * 0.02
+        wq = sg.quantize_weights(dt, wf)
+        del wf
+        shards.append(ShardedMatrix(dt, wq, r, c, world, rank))
+        del wq
+        X.append(torch.randn(nvec, c, device=dev, generator=gen))
+        BUF.append(grp.buffer(nvec, r))
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        for k in range(len(SHAPES)):
+            matvec_tp(shards[k], X[k], grp, BUF[k], stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    lib = sg.lib()
+    with torch.cuda.stream(stream):
+        step()
+        torch.cuda.synchronize()
+        g_step = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_step, stream=stream):
+            step()
+        for _ in range(args.warmup):
+            g_step.replay()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(stream)
+            for _ in range(args.steps):
+                g_step.replay()
+            e1.record(stream)
+            e1.synchronize()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+        # e2e: the step's activations from pinned host in one copy, the seven
+        # calls, the whole outputs back (every rank holds them; rank 0's count)
+        xsz = [nvec * c for _, _, c in SHAPES]
+        XC = torch.empty(sum(xsz), device=dev)
+        h_x = torch.empty(sum(xsz), dtype=torch.float32).pin_memory()
+        osz = [nvec * r for _, r, _ in SHAPES]
+        h_o = torch.empty(sum(osz), dtype=torch.float32).pin_memory()
+        XV, off = [], 0
+        for k in range(len(SHAPES)):
+            XV.append(XC[off:off + xsz[k]].view(nvec, -1))
+            h_x[off:off + xsz[k]].copy_(X[k].reshape(-1).cpu())
+            off += xsz[k]
+        sp = C.c_void_p(stream.cuda_stream)
+
+        def e2e_step():
+            _lib.check(lib.sg_memcpy_h2d(C.c_void_p(XC.data_ptr()), C.c_void_p(h_x.data_ptr()), h_x.numel() * 4,
+                                         sp), "h2d")
+            o = 0
+            for k in range(len(SHAPES)):
+                matvec_tp(shards[k], XV[k], grp, BUF[k], stream=stream)
+                _lib.check(lib.sg_memcpy_d2h(C.c_void_p(h_o.data_ptr() + 4 * o), C.c_void_p(BUF[k].tensor.data_ptr()),
+                                             osz[k] * 4, sp), "d2h")
+                o += osz[k]
+
+        e2e_step()
+        torch.cuda.synchronize()
+        g_e2e = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_e2e, stream=stream):
+            e2e_step()
+        for _ in range(args.warmup):
+            g_e2e.replay()
+        barrier()
+        reps = max(3, min(args.steps, 2000))
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(stream)
+        for _ in range(reps):
+            g_e2e.replay()
+        b1.record(stream)
+        b1.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(b0.elapsed_time(b1)) / reps
+    sg.device_status()
+    total = step_bytes(nvec)
+    value = total / (ms * 1e-3) / 1e9
+    peak, peak_src = 6650.0, "fallback 6.65 TB/s"
+    try:
+        peak, peak_src = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"], "MEASURED_PEAKS.json hbm_gbs"
+    except Exception:
+        pass
+    per_gpu = value / world
+    nvl = sum(4 * nvec * (s.r1 - s.r0) * (world - 1) for s in shards)
+    line = None
+    if rank == 0:
+        line = {"metric": TP_METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "int8 x int4/int6 -> int32, fp32 epilogue", "data": "synthetic",
+                "config": dict(config_block(args, world), workload="gemv_tp_sweep_n%d" % nvec,
+                               parallelism="row-split x%d, gather fused (peer stores)" % world,
+                               global_batch=nvec),
+                "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(per_gpu / peak, 4), "traffic": None, "peak_source": peak_src,
+                             "kernel": "gemv_tiled_kernel (row-split, peer-store epilogue)",
+                             "nvlink_bytes_out_per_rank": nvl,
+                             "how": "per GPU: the step's algorithmic bytes / n_gpus / step time; the rows each rank "
+                                    "sends over NVLink are nvlink_bytes_out_per_rank (770 GB/s measured per "
+                                    "direction makes that term small next to HBM)"},
+                "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                        "h2d_bytes_per_step": h_x.numel() * 4, "d2h_bytes_per_step": h_o.numel() * 4,
+                        "how": "every step: one sg_memcpy_h2d of all activations from pinned host, sg_matvec_tp per "
+                               "matrix, sg_memcpy_d2h of each whole output"},
+                "gpu_launches": len(SHAPES) * args.steps,
+                "clocks": clk.summary()}
+    del g_step, g_e2e
+    grp.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return line
+
+
 DECODE_MODELS = {
     "qwen3_30b_a3b": dict(dim=2048, n_heads=32, n_kv_heads=4, head_dim=128, n_layers=48, vocab=151936,
                           rope_theta=1e6, rms_eps=1e-6, rope_neox=True,
@@ -878,9 +1030,10 @@ def main():
     ap.add_argument("--shape", type=int, default=None, help="profiling: run only this sweep entry")
     ap.add_argument("--profile", action="store_true",
                     help="profiling: only the timed step loop (no e2e, per-shape or CPU legs)")
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "moe", "decode"],
-                    help="gemv: the headline K-quant GEMV sweep; moe: the Qwen3-30B-A3B MoE layer; "
-                         "decode: greedy decode of a whole random-init model")
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "gemv_tp", "moe", "decode"],
+                    help="gemv: the headline K-quant GEMV sweep; gemv_tp: the same sweep split by rows over the "
+                         "GPUs with the gather fused in; moe: the Qwen3-30B-A3B MoE layer; decode: greedy decode "
+                         "of a whole random-init model")
     ap.add_argument("--model", default="qwen3_30b_a3b", choices=sorted(DECODE_MODELS),
                     help="decode workload: the model architecture")
     args = ap.parse_args()
@@ -926,6 +1079,11 @@ def main():
         SHAPES[:] = [SHAPES[args.shape]]
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload == "gemv_tp":
+        line = run_gpu_tp(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
         return
     line, W = run_gpu(args)
     rank, world, _ = rank_env()

@@ -6,16 +6,20 @@
 namespace sg {
 using namespace tiled;
 
-// The end of a row-split launch: every thread's peer stores are made visible
-// system-wide, the CTAs take tickets, and the last one adds 1 to every rank's
-// arrival counter (release), then waits until its own counter shows all ranks
-// for this call (acquire; bounded, DEV_TIMEOUT_PEER on expiry) and advances the
-// epoch.  Counters only grow, so no rank ever resets another's.
+// The end of a row-split launch: after the CTA's barrier, one system-scope
+// fence per CTA orders the CTA's peer stores before its ticket (the barrier
+// makes the other threads' stores precede thread 0's fence); the last CTA to
+// take a ticket fences again and adds 1 to every rank's arrival counter
+// (release), then waits until its own counter shows all ranks for this call
+// (acquire; bounded, DEV_TIMEOUT_PEER on expiry) and advances the epoch.
+// Counters only grow, so no rank ever resets another's.
 __device__ __noinline__ void tp_arrive_and_wait(const TGemvArgs &a) {
-    __threadfence_system();
     __syncthreads();
     bool mine = false;
-    if (threadIdx.x == 0) mine = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        mine = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+    }
     // no static shared memory here: the launch gives all 227 KB to the dynamic part
     const bool last = __syncthreads_or(mine);
     if (!last || threadIdx.x != 0) return;
