@@ -174,28 +174,29 @@ SG_API sg_status sg_matmul_rows_float(const uint8_t *d_base, const sg_mat *m, co
  *
  * par_rows (smollm_chat.rs:332-337) splits a matvec's rows across threads;
  * sg_matvec_tp splits them across GPUs the same way (rank p of P owns rows
- * [R*p/P, R*(p+1)/P), results independent of the split, quant_q8k.rs:393-394)
- * and fuses the gather that follows: the GEMV's epilogue stores each row of
- * its shard straight into the output buffer of every rank (peer stores over
- * NVLink, through CUDA IPC mappings; no copy kernel, no NCCL call), then the
- * rank's last block adds 1 to every rank's arrival counter, and the launch
- * ends only when its own counter shows all ranks for this call.  Every rank
- * must make the same sequence of calls.  A wait that runs out (2 s) makes
- * sg_device_status return SG_ERR_TIMEOUT.  A call's output buffer must not be
- * rewritten by a later call before its readers are done (alternate two).
+ * [R*p/P, R*(p+1)/P); results do not depend on the split, quant_q8k.rs:393-394)
+ * and fuses the gather that follows into the same kernel: the GEMV epilogue
+ * stores each row of its shard, tagged with the call's epoch, straight into
+ * every rank's receive buffer (8-byte peer stores over NVLink through CUDA IPC
+ * mappings; no copy kernel, no NCCL call, no memory fence), and each rank's
+ * blocks then read their share of its own receive buffer, each row as soon as
+ * it carries the epoch, into the plain output.  After the call every rank
+ * holds the whole output.  Every rank must make the same sequence of calls
+ * (the epoch counts them); a wait that runs out (2 s) writes NaN and makes
+ * sg_device_status return SG_ERR_TIMEOUT.
  *
- * Set-up: each rank allocates a comm block of sg_tp_comm_bytes() (256-byte
- * aligned, device memory from cudaMalloc / sg_alloc), zeroes it with
- * sg_tp_comm_init, and shares it and its full-size output buffer with the
- * others through sg_ipc_get_handle / sg_ipc_open (the handle is
- * sg_ipc_handle_bytes() long; the exchange itself is the caller's, e.g. an
- * all-gather over its process group). */
+ * Set-up, per rank: a comm block of sg_tp_comm_bytes() (device memory, 256-byte
+ * aligned, zeroed by sg_tp_comm_init), kept for all calls; per output, a
+ * receive buffer of sg_tp_recv_bytes(n_vec, rows) (cudaMalloc / sg_alloc,
+ * zeroed) shared with the other ranks through sg_ipc_get_handle /
+ * sg_ipc_open (the handle is sg_ipc_handle_bytes() long; the exchange itself
+ * is the caller's, e.g. an all-gather over its process group). */
 #define SG_TP_MAX_RANKS 8
 #define SG_TP_COMM_BYTES 256
 typedef struct {
     uint32_t n_ranks, rank;
-    float *outs[SG_TP_MAX_RANKS];   /* the call's output on every rank (this rank's own pointer at [rank]) */
-    void *comms[SG_TP_MAX_RANKS];   /* every rank's comm block, likewise */
+    void *recv[SG_TP_MAX_RANKS];   /* the output's receive buffer on every rank (this rank's own at [rank]) */
+    void *comm;                    /* this rank's comm block */
 } sg_tp_group;
 SG_API uint64_t sg_ipc_handle_bytes(void);
 SG_API sg_status sg_ipc_get_handle(void *d_ptr, void *handle_out);
@@ -203,11 +204,14 @@ SG_API sg_status sg_ipc_open(const void *handle, void **d_out);
 SG_API sg_status sg_ipc_close(void *d_ptr);
 SG_API uint64_t sg_tp_comm_bytes(void);
 SG_API sg_status sg_tp_comm_init(void *d_comm, void *stream);
-/* This rank's shard (TILED16, m->rows rows, global rows row0 .. row0 + rows)
- * times x_b (fp32, b < n_vec <= 8, 16-byte aligned, ldx apart); row r of
- * vector b lands at outs[q][b*ldo + row0 + r] on every rank q. */
+SG_API uint64_t sg_tp_recv_bytes(uint64_t n_vec, uint64_t rows);
+/* This rank's shard (TILED16, m->rows rows = global rows row0 .. row0 +
+ * m->rows of a rows-row matrix) times x_b (fp32, b < n_vec <= 8, 16-byte
+ * aligned, ldx apart); afterwards d_out[b*ldo + r] = row r of W x_b for every
+ * r < rows, on every rank. */
 SG_API sg_status sg_matvec_tp(const uint8_t *d_shard, const sg_mat *m, const float *d_x, uint64_t ldx,
-                              uint64_t n_vec, uint64_t row0, uint64_t ldo, const sg_tp_group *grp, void *stream);
+                              uint64_t n_vec, uint64_t row0, uint64_t rows, float *d_out, uint64_t ldo,
+                              const sg_tp_group *grp, void *stream);
 
 /* The same matvec for either layout with the Q8_K images in caller-owned
  * scratch (the reference keeps them in thread-local scratch, quant_q8k.rs:

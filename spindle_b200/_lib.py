@@ -54,8 +54,8 @@ TP_MAX_RANKS = 8
 
 
 class SgTpGroup(C.Structure):
-    _fields_ = [("n_ranks", C.c_uint32), ("rank", C.c_uint32), ("outs", C.c_void_p * TP_MAX_RANKS),
-                ("comms", C.c_void_p * TP_MAX_RANKS)]
+    _fields_ = [("n_ranks", C.c_uint32), ("rank", C.c_uint32), ("recv", C.c_void_p * TP_MAX_RANKS),
+                ("comm", C.c_void_p)]
 
 
 P, U64, I32 = C.c_void_p, C.c_uint64, C.c_int32
@@ -88,7 +88,8 @@ SIGNATURES = {
     "sg_ipc_close": (I32, [P]),
     "sg_tp_comm_bytes": (U64, []),
     "sg_tp_comm_init": (I32, [P, P]),
-    "sg_matvec_tp": (I32, [P, C.POINTER(SgMat), P, U64, U64, U64, U64, P, P]),
+    "sg_tp_recv_bytes": (U64, [U64, U64]),
+    "sg_matvec_tp": (I32, [P, C.POINTER(SgMat), P, U64, U64, U64, U64, P, U64, P, P]),
     "sg_matvec_scratch_bytes": (U64, [U64, U64]),
     "sg_matvec_scratch": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P, U64, P]),
     "sg_matvec_static": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),

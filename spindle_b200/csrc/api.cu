@@ -387,13 +387,13 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
 // arrival counters (see TGemvArgs).
 struct TpSpec {
     uint32_t n;
-    uint32_t row_off;
-    float *out[TP_MAX_RANKS];   // vector 0, row 0 of the full output on every rank
+    uint32_t row_off, rows;                     // this shard's first row; rows of the whole matrix
+    unsigned long long *recv[TP_MAX_RANKS];     // every rank's receive buffer
+    const unsigned long long *my_recv;
+    float *out;                                 // this rank's plain output, vector b at out + b * ldo
     uint64_t ldo;
-    unsigned long long *flag[TP_MAX_RANKS];
-    unsigned long long *my_flag;
     unsigned *ticket;
-    unsigned long long *epoch;
+    unsigned *epoch;
 };
 
 sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, const float *x, uint64_t ldx,
@@ -443,15 +443,14 @@ sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, 
             }
             if (outs) a.out[v] = outs[g + v];
         }
-        if (tp) {
+        if (tp) {  // one launch per call (checked above), so g == 0 here
             a.npeers = tp->n;
             a.row_off = tp->row_off;
+            a.tp_rows = tp->rows;
+            a.out[0] = tp->out;
             a.out_stride = tp->ldo;
-            for (uint32_t q = 0; q < tp->n; q++) {
-                a.peer_out[q] = tp->out[q] + g * tp->ldo;
-                a.peer_flag[q] = tp->flag[q];
-            }
-            a.my_flag = tp->my_flag;
+            for (uint32_t q = 0; q < tp->n; q++) a.peer_recv[q] = tp->recv[q];
+            a.my_recv = tp->my_recv;
             a.ticket = tp->ticket;
             a.epoch = tp->epoch;
         }
@@ -1035,33 +1034,38 @@ sg_status sg_tp_comm_init(void *d_comm, void *stream) {
     return SG_OK;
 }
 
+uint64_t sg_tp_recv_bytes(uint64_t n_vec, uint64_t rows) { return 2ull * 8ull * n_vec * rows; }
+
 sg_status sg_matvec_tp(const uint8_t *d_shard, const sg_mat *m, const float *d_x, uint64_t ldx, uint64_t n_vec,
-                       uint64_t row0, uint64_t ldo, const sg_tp_group *grp, void *stream) {
+                       uint64_t row0, uint64_t rows, float *d_out, uint64_t ldo, const sg_tp_group *grp,
+                       void *stream) {
     int dt;
     sg_status st = check_mat(d_shard, m, 0, m ? m->rows : 0, &dt);
     if (st) return st;
     if (m->layout != SG_LAYOUT_TILED16 || !grp || !grp->n_ranks || grp->n_ranks > SG_TP_MAX_RANKS ||
-        grp->rank >= grp->n_ranks)
+        grp->rank >= grp->n_ranks || !grp->comm)
         return SG_ERR_INVALID;
-    if (m->rows == 0 || n_vec == 0) return SG_ERR_INVALID;  // every rank must arrive, so no empty calls
-    if (!d_x || (n_vec > 1 && ldx < m->cols) || row0 + m->rows > ldo || row0 + m->rows > 0xFFFFFFFFull)
+    if (m->rows == 0 || n_vec == 0 || n_vec > TGEMV_MAXV) return SG_ERR_INVALID;  // every rank must arrive
+    if (!d_x || !d_out || (n_vec > 1 && ldx < m->cols) || row0 + m->rows > rows || rows > 0xFFFFFFFFull ||
+        (n_vec > 1 && ldo < rows))
         return SG_ERR_INVALID;
-    if (!aligned(d_x, 16) || (n_vec > 1 && ldx % 4)) return SG_ERR_ALIGN;
+    if (!aligned(d_x, 16) || (n_vec > 1 && ldx % 4) || !aligned(d_out, 4) || !aligned(grp->comm, 256))
+        return SG_ERR_ALIGN;
     TpSpec tp;
     memset(&tp, 0, sizeof tp);
     tp.n = grp->n_ranks;
     tp.row_off = (uint32_t)row0;
-    tp.ldo = ldo;
+    tp.rows = (uint32_t)rows;
     for (uint32_t q = 0; q < grp->n_ranks; q++) {
-        if (!grp->outs[q] || !grp->comms[q]) return SG_ERR_INVALID;
-        if (!aligned(grp->outs[q], 4) || !aligned(grp->comms[q], 256)) return SG_ERR_ALIGN;
-        tp.out[q] = grp->outs[q];
-        tp.flag[q] = (unsigned long long *)grp->comms[q];
+        if (!grp->recv[q]) return SG_ERR_INVALID;
+        if (!aligned(grp->recv[q], 8)) return SG_ERR_ALIGN;
+        tp.recv[q] = (unsigned long long *)grp->recv[q];
     }
-    uint8_t *mine = (uint8_t *)grp->comms[grp->rank];
-    tp.my_flag = (unsigned long long *)mine;
-    tp.ticket = (unsigned *)(mine + 64);
-    tp.epoch = (unsigned long long *)(mine + 128);
+    tp.my_recv = tp.recv[grp->rank];
+    tp.out = d_out;
+    tp.ldo = n_vec > 1 ? ldo : rows;
+    tp.ticket = (unsigned *)((uint8_t *)grp->comm + 64);
+    tp.epoch = (unsigned *)((uint8_t *)grp->comm + 128);
     return launch_tiled(d_shard + m->offset, dt, (uint32_t)(m->cols / 256), nullptr, d_x, ldx, nullptr, n_vec, 0,
                         m->rows, (cudaStream_t)stream, nullptr, &tp);
 }

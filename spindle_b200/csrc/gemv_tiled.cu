@@ -6,40 +6,41 @@
 namespace sg {
 using namespace tiled;
 
-// The end of a row-split launch: after the CTA's barrier, one system-scope
-// fence per CTA orders the CTA's peer stores before its ticket (the barrier
-// makes the other threads' stores precede thread 0's fence); the last CTA to
-// take a ticket fences again and adds 1 to every rank's arrival counter
-// (release), then waits until its own counter shows all ranks for this call
-// (acquire; bounded, DEV_TIMEOUT_PEER on expiry) and advances the epoch.
-// Counters only grow, so no rank ever resets another's.
-__device__ __noinline__ void tp_arrive_and_wait(const TGemvArgs &a) {
-    __syncthreads();
-    bool mine = false;
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        mine = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
-    }
-    // no static shared memory here: the launch gives all 227 KB to the dynamic part
-    const bool last = __syncthreads_or(mine);
-    if (!last || threadIdx.x != 0) return;
-    __threadfence_system();
-    *a.ticket = 0;  // every CTA of this launch has its ticket
-    for (uint32_t p = 0; p < a.npeers; p++)
-        asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(a.peer_flag[p]) : "memory");
-    const unsigned long long target = (*a.epoch + 1ull) * a.npeers;
-    const uint64_t t0 = globaltimer_ns();
-    for (;;) {
-        unsigned long long v;
-        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a.my_flag) : "memory");
-        if (v >= target) break;
-        if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
-            atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_PEER);
-            break;
+// The end of a row-split launch (see TGemvArgs): CTA c of G reads pairs
+// [n*c/G, n*(c+1)/G) of this rank's receive buffer (n = nvec * rows), each as
+// soon as it carries this call's epoch, into the plain output.  The pairs are
+// 8-byte stores, single-copy atomic, so no fence orders data and flag; the
+// epoch alternates the buffer's halves, and a rank can be at most one call
+// ahead of another (its next call ends only with this rank's rows of that
+// call), so a half is never overwritten before it is read.
+__device__ __noinline__ void tp_gather(const TGemvArgs &a, uint32_t e) {
+    const uint64_t R = a.tp_rows, n = (uint64_t)a.nvec * R;
+    const unsigned long long *half = a.my_recv + (uint64_t)(e & 1u) * n;
+    const uint64_t lo = n * blockIdx.x / gridDim.x, hi = n * (blockIdx.x + 1) / gridDim.x;
+    uint64_t t0 = 0;
+    for (uint64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        unsigned long long p;
+        for (;;) {
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(p) : "l"(half + i) : "memory");
+            if ((uint32_t)(p >> 32) == e) break;
+            const uint64_t t = globaltimer_ns();
+            if (t0 == 0) {
+                t0 = t;
+            } else if (t - t0 > WAIT_LIMIT_NS) {
+                atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_PEER);
+                p = 0x7fc00000ull;  // NaN
+                break;
+            }
+            __nanosleep(32);
         }
-        __nanosleep(64);
+        const uint64_t v = i / R, r = i - v * R;
+        a.out[0][v * a.out_stride + r] = __uint_as_float((uint32_t)p);
     }
-    *a.epoch += 1ull;
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(a.ticket, 1u) == gridDim.x - 1) {
+        *a.ticket = 0;  // every CTA of this launch has its ticket
+        *a.epoch = e;
+    }
 }
 
 template <int DT, int NV, int MODE>
@@ -60,7 +61,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
         (MOE && a.swiglu && (MODE != IN_MOE_X || a.nvec != 1)) ||
         (MOE && (a.max_slots > MOE_MAXK || a.tiles_per_mat == 0 || nact == 0 ||
                  (uint64_t)a.ntiles * gridDim.x >= (1ull << 32) || a.ntiles < a.max_slots * a.tiles_per_mat)) ||
-        (a.npeers && (MOE || a.npeers > TP_MAX_RANKS || !a.my_flag || !a.ticket || !a.epoch)) ||
+        (a.npeers && (MOE || a.npeers > TP_MAX_RANKS || !a.ticket || !a.epoch || !a.out[0] || !a.my_recv)) ||
         (MODE == IN_MOE_X && a.logits &&
          (a.n_expert == 0 || a.n_used == 0 || a.n_used > a.n_expert || a.n_used > MOE_MAXK ||
           moe_select_bytes(a.n_expert) > nwarps * a.nstages * a.stage_bytes))) {
@@ -216,6 +217,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     }
     // The activations do: wait for the grid that wrote them, then stage them.
     grid_dependency_wait();
+    const uint32_t tp_e = (!MOE && a.npeers) ? *a.epoch + 1u : 0u;  // this call's epoch (row split)
     const uint32_t nb = a.nb;
     bool failed = false;
     if constexpr (MODE == IN_MOE_H) {
@@ -417,9 +419,13 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                     if (g == 0 && r < 8 && 2 * j < a.r1) dst[j] = silu_mul(yv, up);
                 } else if (g == 0 && v < (int)a.nvec && row >= a.r0 && row < a.r1) {
                     if (!MOE && a.npeers) {
-                        // the row shard goes straight into every rank's output (NVLink peer stores)
-                        const uint64_t o = (uint64_t)v * a.out_stride + a.row_off + row;
-                        for (uint32_t p = 0; p < a.npeers; p++) a.peer_out[p][o] = yv;
+                        // the row shard goes straight into every rank's receive buffer (NVLink peer stores)
+                        const uint64_t o = (uint64_t)(tp_e & 1u) * a.nvec * a.tp_rows +
+                                           (uint64_t)v * a.tp_rows + a.row_off + row;
+                        const unsigned long long pr = ((unsigned long long)tp_e << 32) | __float_as_uint(yv);
+                        for (uint32_t p = 0; p < a.npeers; p++)
+                            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a.peer_recv[p] + o), "l"(pr)
+                                         : "memory");
                     } else {
                         dst[row] = yv;
                     }
@@ -428,7 +434,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
         }
     }
     if constexpr (!MOE) {
-        if (a.npeers) tp_arrive_and_wait(a);
+        if (a.npeers) tp_gather(a, tp_e);
     }
 }
 

@@ -100,18 +100,19 @@ struct TGemvArgs {
     uint32_t n_ff;        // IN_MOE_H
     const float *gu;      // IN_MOE_H
     uint64_t gu_stride;   // IN_MOE_H, floats
-    // Row-split tensor parallelism (IN_Q8K / IN_F32, npeers > 0): row r of
-    // vector v goes to peer_out[p][v * out_stride + row_off + r] on every rank
-    // p (out[] unused); then each rank's last CTA adds 1 to every rank's
-    // arrival counter and waits until its own counter reaches
-    // (*epoch + 1) * npeers.
+    // Row-split tensor parallelism (IN_Q8K / IN_F32, npeers > 0).  The call's
+    // epoch e is *epoch + 1.  Row r of vector v is stored as the pair
+    // (e << 32 | value bits) at peer_recv[p][h*nvec*tp_rows + v*tp_rows +
+    // row_off + r] on every rank p, h = e & 1; then every CTA reads its share
+    // of this rank's receive buffer, waiting for each pair to carry e, into
+    // out[0][v * out_stride + row]; the last CTA to finish stores e in *epoch.
     uint32_t npeers;
     uint32_t row_off;
-    float *peer_out[TP_MAX_RANKS];
-    unsigned long long *peer_flag[TP_MAX_RANKS];
-    unsigned long long *my_flag;
+    uint32_t tp_rows;     // rows of the whole matrix
+    unsigned long long *peer_recv[TP_MAX_RANKS];
+    const unsigned long long *my_recv;  // this rank's receive buffer
     unsigned *ticket;
-    unsigned long long *epoch;
+    unsigned *epoch;
 };
 
 // In the MoE modes the choice is kept at the top of the barrier area: n at

@@ -5,11 +5,11 @@ One process per GPU.  par_rows (smollm_chat.rs:332-337) splits a matvec's rows
 slice of every matrix, and the GEMV kernel stores each row of its slice
 straight into the output buffer of every rank (CUDA IPC mappings, NVLink peer
 stores), so that after the call every rank holds the whole output: the matvec
-and the all-gather that follows it are one kernel.
+and the all-gather that follows it are one kernel.  Rows travel as 8-byte (epoch, value) pairs, so the receiving
+blocks know a row has arrived without any memory fence.
 
-Buffers that other ranks write into are plain cudaMalloc allocations (IPC
-handles name whole allocations), made by the library (sg_alloc) and shown to
-torch through __cuda_array_interface__.
+Receive buffers that other ranks write into are plain cudaMalloc allocations
+(IPC handles name whole allocations), made by the library (sg_alloc).
 """
 import ctypes as C
 
@@ -50,17 +50,18 @@ class _DeviceArray:
 
 
 class TpBuffer:
-    """A [n_vec, rows] fp32 output that every rank of the group can write:
-    .tensor is this rank's copy; .ptrs[q] addresses rank q's copy."""
+    """One row-split output: .tensor [n_vec, rows] is this rank's plain copy
+    (every rank gets the whole output); .recv[q] addresses rank q's receive
+    buffer of epoch-tagged rows."""
 
-    def __init__(self, tensor, ptrs, n_vec, rows):
-        self.tensor, self.ptrs, self.n_vec, self.rows = tensor, ptrs, n_vec, rows
+    def __init__(self, tensor, recv, n_vec, rows):
+        self.tensor, self.recv, self.n_vec, self.rows = tensor, recv, n_vec, rows
 
 
 class TpGroup:
-    """This rank's comm block, the other ranks' (mapped), and the shared output
-    buffers made through it.  Every rank constructs it and its buffers in the
-    same order (each step is a collective over the process group)."""
+    """This rank's comm block and the shared receive buffers made through it.
+    Every rank constructs it and its buffers in the same order (each is a
+    collective over the process group)."""
 
     def __init__(self, group=None, device=None):
         import torch.distributed as dist
@@ -70,10 +71,9 @@ class TpGroup:
             raise ValueError("at most %d ranks" % TP_MAX_RANKS)
         self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         self._own, self._opened = [], []
-        comm = self._alloc(lib().sg_tp_comm_bytes())
-        _lib.check(lib().sg_tp_comm_init(C.c_void_p(comm), None), "sg_tp_comm_init")
+        self.comm = self._alloc(lib().sg_tp_comm_bytes())
+        _lib.check(lib().sg_tp_comm_init(C.c_void_p(self.comm), None), "sg_tp_comm_init")
         torch.cuda.synchronize(self.device)
-        self.comms = self._share(comm)
 
     def _alloc(self, nbytes):
         p = C.c_void_p()
@@ -98,16 +98,20 @@ class TpGroup:
         return ptrs
 
     def buffer(self, n_vec, rows):
-        ptr = self._alloc(max(1, n_vec * rows) * 4)
-        t = torch.as_tensor(_DeviceArray(ptr, (n_vec, rows), self.device), device=self.device)
-        return TpBuffer(t, self._share(ptr), n_vec, rows)
+        nbytes = lib().sg_tp_recv_bytes(n_vec, rows)
+        ptr = self._alloc(nbytes)
+        # epoch 0 never runs: a zeroed buffer holds no row of any call
+        torch.as_tensor(_DeviceArray(ptr, (nbytes // 4,), self.device), device=self.device).zero_()
+        torch.cuda.synchronize(self.device)
+        out = torch.empty(n_vec, rows, dtype=torch.float32, device=self.device)
+        return TpBuffer(out, self._share(ptr), n_vec, rows)
 
     def c(self, buf):
         g = SgTpGroup()
         g.n_ranks, g.rank = self.n, self.rank
         for q in range(self.n):
-            g.outs[q] = buf.ptrs[q]
-            g.comms[q] = self.comms[q]
+            g.recv[q] = buf.recv[q]
+        g.comm = self.comm
         return g
 
     def close(self):
@@ -143,7 +147,8 @@ def matvec_tp(shard, xs, grp, buf, stream=None):
     if xs2.dtype != torch.float32 or xs2.stride(-1) != 1:
         raise ValueError("xs must be float32 with contiguous rows")
     g = grp.c(buf)
+    out = buf.tensor
     _lib.check(lib().sg_matvec_tp(C.c_void_p(shard.w.data_ptr()), C.byref(shard.m.c()), C.c_void_p(xs2.data_ptr()),
-                                  xs2.stride(0), xs2.shape[0], shard.r0, buf.rows, C.byref(g), _stream(stream)),
-               "sg_matvec_tp")
-    return buf.tensor
+                                  xs2.stride(0), xs2.shape[0], shard.r0, buf.rows, C.c_void_p(out.data_ptr()),
+                                  out.stride(0), C.byref(g), _stream(stream)), "sg_matvec_tp")
+    return out

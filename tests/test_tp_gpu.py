@@ -62,6 +62,7 @@ def test_tp_one_rank(dev):
 
 
 def test_tp_bad_args(dev):
+    import ctypes as C
     grp = TpGroup(device=dev)
     try:
         w = sg.quantize_weights(sg.Q4_K, torch.randn(64, 256, device=dev) * 0.02)
@@ -69,20 +70,20 @@ def test_tp_bad_args(dev):
         buf = grp.buffer(1, 64)
         x = torch.randn(256, device=dev)
         lib = sg.lib()
-        import ctypes as C
+
+        def call(m, wptr, row0, rows, g):
+            return lib.sg_matvec_tp(C.c_void_p(wptr), C.byref(m.c()), C.c_void_p(x.data_ptr()), 256, 1, row0, rows,
+                                    C.c_void_p(buf.tensor.data_ptr()), 64, C.byref(g), None)
+
         g = grp.c(buf)
         g.rank = 1  # outside the group
-        st = lib.sg_matvec_tp(C.c_void_p(shard.w.data_ptr()), C.byref(shard.m.c()), C.c_void_p(x.data_ptr()), 256, 1,
-                              0, 64, C.byref(g), None)
-        assert st == 1
+        assert call(shard.m, shard.w.data_ptr(), 0, 64, g) == 1
         g = grp.c(buf)
-        st = lib.sg_matvec_tp(C.c_void_p(shard.w.data_ptr()), C.byref(shard.m.c()), C.c_void_p(x.data_ptr()), 256, 1,
-                              8, 64, C.byref(g), None)  # rows past the output
-        assert st == 1
-        gm = sg.Mat(sg.Q4_K, 256, 64)  # GGUF layout
-        st = lib.sg_matvec_tp(C.c_void_p(w.data_ptr()), C.byref(gm.c()), C.c_void_p(x.data_ptr()), 256, 1, 0, 64,
-                              C.byref(g), None)
-        assert st == 1
+        assert call(shard.m, shard.w.data_ptr(), 8, 64, g) == 1  # rows past the whole matrix
+        assert call(sg.Mat(sg.Q4_K, 256, 64), w.data_ptr(), 0, 64, g) == 1  # GGUF layout
+        g.comm = None
+        assert call(shard.m, shard.w.data_ptr(), 0, 64, g) == 1
+        sg.device_status()
     finally:
         grp.close()
 
