@@ -308,6 +308,21 @@ SG_API uint64_t sg_moe_scratch_bytes(const sg_moe *m);
 SG_API sg_status sg_moe_forward(const sg_moe *m, const float *d_x, float *d_out, void *d_scratch,
                                 uint64_t scratch_bytes, sg_moe_choice *d_choice, float *d_probs, void *stream);
 
+/* moe_forward_batch (smollm_chat.rs:928-1174): n_tok tokens through the same
+ * layer, out_t = moe_forward(x_t), bit for bit what n_tok one-token calls give
+ * (the reference's batch is one-token-identical too, :4699-4736).  x_t =
+ * d_x + t*ldx (16-byte aligned), out_t = d_out + t*ldo; n_tok <= 64 and
+ * n_expert <= 256.  The router runs once over all tokens, one launch makes
+ * every token's choice and a table of (expert, token) slots, and the gate/up
+ * and down passes each run over all slots in one launch (each block stages
+ * the Q8_K image of every token its slots use).  d_choices (optional,
+ * [n_tok]) receives the choices. */
+#define SG_MOE_MAX_BATCH 64
+SG_API uint64_t sg_moe_batch_scratch_bytes(const sg_moe *m, uint64_t n_tok);
+SG_API sg_status sg_moe_forward_batch(const sg_moe *m, const float *d_x, uint64_t ldx, uint64_t n_tok, float *d_out,
+                                      uint64_t ldo, void *d_scratch, uint64_t scratch_bytes,
+                                      sg_moe_choice *d_choices, void *stream);
+
 /* ---- Decoder step (forward_slice, smollm_chat.rs:3371-3552, with greedy
  * sampling, :3565-3602 and :3661-3671) -----------------------------------------
  *

@@ -8,6 +8,8 @@ Host-side mirror of the reference's kernel API (WiseHax/spindle 1.1.0, src/):
   matmul_rows              quant_q8k.rs:255-295
   matvec_rows_float        quant.rs:939-1094 (float path, one vector at a time)
   matmul_rows_float        quant_multi.rs:232-273 (float path, shared decode)
+  Moe, moe_forward         smollm_chat.rs:1178-1382
+  moe_forward_batch        smollm_chat.rs:928-1174
 Every call goes through the C ABI of include/spindle_gpu.h (libspindle_b200.so);
 torch tensors are only the device-memory plumbing.  There is no CPU path: a
 missing library or a failed call raises.
@@ -325,6 +327,27 @@ def moe_forward(m, x, out=None, scratch=None, choice=None, probs=None, stream=No
     ptr = lambda t: None if t is None else C.c_void_p(t.data_ptr())
     _lib.check(lib().sg_moe_forward(C.byref(m.c()), ptr(x), ptr(out), ptr(scratch), scratch.numel(), ptr(choice),
                                     ptr(probs), _stream(stream)), "moe_forward")
+    return out
+
+
+def moe_forward_batch(m, xs, out=None, scratch=None, choices=None, stream=None):
+    """moe_forward_batch (smollm_chat.rs:928-1174): out[t] = moe_forward(xs[t])
+    for xs float32 CUDA [n_tok, dim], bit for bit the one-token results.
+    choices: optional int32 CUDA [n_tok, 36] receiving each token's choice."""
+    if xs.dtype != torch.float32 or xs.dim() != 2 or xs.stride(-1) != 1:
+        raise ValueError("xs must be float32 [n_tok, dim] with contiguous rows")
+    n_tok = xs.shape[0]
+    if out is None:
+        out = torch.empty(n_tok, m.dim, dtype=torch.float32, device=xs.device)
+    if scratch is None:
+        n = lib().sg_moe_batch_scratch_bytes(C.byref(m.c()), n_tok)
+        if not n:
+            raise SgError(1, "moe_batch_scratch_bytes")
+        scratch = torch.empty(n, dtype=torch.uint8, device=xs.device)
+    ptr = lambda t: None if t is None else C.c_void_p(t.data_ptr())
+    _lib.check(lib().sg_moe_forward_batch(C.byref(m.c()), ptr(xs), xs.stride(0), n_tok, ptr(out), out.stride(0),
+                                          ptr(scratch), scratch.numel(), ptr(choices), _stream(stream)),
+               "moe_forward_batch")
     return out
 
 

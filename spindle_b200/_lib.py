@@ -102,6 +102,8 @@ SIGNATURES = {
     "sg_moe_pack_down": (I32, [I32, P, U64, U64, U64, P, P]),
     "sg_moe_scratch_bytes": (U64, [C.POINTER(SgMoe)]),
     "sg_moe_forward": (I32, [C.POINTER(SgMoe), P, P, P, U64, P, P, P]),
+    "sg_moe_batch_scratch_bytes": (U64, [C.POINTER(SgMoe), U64]),
+    "sg_moe_forward_batch": (I32, [C.POINTER(SgMoe), P, U64, U64, P, U64, P, U64, P, P]),
     "sg_model_scratch_bytes": (U64, [P]),
     "sg_model_kv_bytes": (U64, [P]),
     "sg_model_prepare": (I32, [P, P, U64, P]),

@@ -214,9 +214,9 @@ sg_status check_q8k(const sg_q8k &q, uint64_t n) {
 // the previous kernel in the stream finishes; it waits for it (griddepcontrol)
 // before reading anything that kernel wrote.
 template <typename Args>
-cudaError_t launch_pdl(const void *fn, uint32_t grid, uint32_t block, size_t smem, cudaStream_t stream, Args *args) {
+cudaError_t launch_pdl(const void *fn, dim3 grid, uint32_t block, size_t smem, cudaStream_t stream, Args *args) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
+    cfg.gridDim = grid;
     cfg.blockDim = dim3(block);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -568,6 +568,39 @@ MoeScratch moe_scratch(const sg_moe *m) {
     return L;
 }
 
+// Scratch of the batched layer (moe_forward_batch) for n_tok tokens.
+struct MoeBatchScratch {
+    uint64_t choices, slot_base, slots, n_slots, slots_sh, n_slots_sh, shsel, scale, logits, qx, h, y, hsh, ysh, total;
+};
+
+MoeBatchScratch moe_batch_scratch(const sg_moe *m, uint64_t n_tok) {
+    MoeBatchScratch L;
+    uint64_t off = 0;
+    auto take = [&](uint64_t bytes) {
+        const uint64_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const bool sh = m->shared_gate_up != nullptr;
+    const uint64_t slots = n_tok * m->n_used;
+    L.choices = take(n_tok * sizeof(sg_moe_choice));
+    L.slot_base = take(n_tok * 4);
+    L.slots = take(slots * 8);
+    L.n_slots = take(4);
+    L.slots_sh = take(sh ? n_tok * 8 : 0);
+    L.n_slots_sh = take(4);
+    L.shsel = take(sizeof(sg_moe_choice));
+    L.scale = take(n_tok * 4);
+    L.logits = take(n_tok * m->n_expert * 4);
+    L.qx = take(n_tok * act_bytes((uint32_t)(m->dim / 256)));
+    L.h = take(slots * m->n_ff * 4);
+    L.y = take(slots * m->dim * 4);
+    L.hsh = take(sh ? n_tok * m->shared_n_ff * 4 : 0);
+    L.ysh = take(sh ? n_tok * m->dim * 4 : 0);
+    L.total = off;
+    return L;
+}
+
 // The expert choice of a grouped launch: made from the router's logits in the
 // kernel (IN_MOE_X with logits), or read from `sel`.
 struct MoeRoute {
@@ -580,10 +613,18 @@ struct MoeRoute {
 };
 
 // One grouped launch of the tiled GEMV over the chosen experts (IN_MOE_X or IN_MOE_H).
+// Batched form: the slots come from a device table of (expert, token) pairs.
+struct MoeSlots {
+    const int32_t *slots;
+    const uint32_t *n_slots;
+    const uint8_t *qx_tokens;  // IN_MOE_X: the tokens' Q8_K images
+};
+
 sg_status launch_moe_group(int32_t dtype, int mode, const uint8_t *w, uint64_t mat_stride, uint64_t rows,
                            uint64_t cols, uint32_t max_slots, uint32_t n_expert, const sg_moe_choice *sel,
                            const MoeRoute *route, const float *x, const uint8_t *qx, const float *h,
-                           uint64_t h_stride, float *out, uint64_t out_stride, cudaStream_t stream) {
+                           uint64_t h_stride, float *out, uint64_t out_stride, cudaStream_t stream,
+                           const MoeSlots *slots = nullptr) {
     const int dt = dtype == SG_Q4_K ? DT_Q4K : DT_Q6K;
     const uint32_t nb = (uint32_t)(cols / 256), tiles = (uint32_t)((rows + TILE_ROWS - 1) / TILE_ROWS);
     TPlan p;
@@ -624,6 +665,14 @@ sg_status launch_moe_group(int32_t dtype, int mode, const uint8_t *w, uint64_t m
     a.n_expert = n_expert;
     a.gu = h;
     a.gu_stride = h_stride;
+    if (slots) {
+        if (p.nact > MOE_MAXK) return SG_ERR_SHAPE;
+        a.slots = slots->slots;
+        a.n_slots = slots->n_slots;
+        a.qx_tokens = slots->qx_tokens;
+        a.sel = nullptr;
+        a.qx_image = nullptr;
+    }
     CK(launch_pdl((const void *)p.fn, p.grid, p.warps * 32, p.smem, stream, &a));
     return SG_OK;
 }
@@ -631,7 +680,7 @@ sg_status launch_moe_group(int32_t dtype, int mode, const uint8_t *w, uint64_t m
 // Router logits over the whole GPU (a few rows per CTA), plus one CTA for the
 // shared expert's gate and one-slot choice when the layer has a shared expert.
 sg_status launch_router(const sg_moe *m, const float *x, float *logits, uint8_t *qx, sg_moe_choice *shsel, float *scale,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, uint32_t n_tok = 1, uint64_t ldx = 0) {
     static std::atomic<uint64_t> attr_done{0};  // bit d: the smem attribute is set on device d
     int dev;
     CK(cudaGetDevice(&dev));
@@ -663,6 +712,8 @@ sg_status launch_router(const sg_moe *m, const float *x, float *logits, uint8_t 
     a.shared_sel = sh ? shsel : nullptr;
     a.shared_gate = sh ? m->shared_gate : nullptr;
     a.shared_scale = sh ? scale : nullptr;
+    a.n_tok = n_tok;
+    a.ldx = n_tok > 1 ? ldx : m->dim;
     const uint32_t threads = (8 * rpc + 31) / 32 * 32;
     CK(launch_pdl((const void *)moe_router_kernel, a.row_ctas + (sh ? 1 : 0), threads, smem, stream, &a));
     return SG_OK;
@@ -1169,6 +1220,72 @@ sg_status sg_moe_forward(const sg_moe *m, const float *d_x, float *d_out, void *
     c.dim = (uint32_t)m->dim;
     c.max_slots = k;
     CK(launch_pdl((const void *)moe_combine_kernel, (uint32_t)((m->dim + 255) / 256), 256, 0, s, &c));
+    return SG_OK;
+}
+
+uint64_t sg_moe_batch_scratch_bytes(const sg_moe *m, uint64_t n_tok) {
+    if (check_moe(m) || n_tok == 0 || n_tok > SG_MOE_MAX_BATCH) return 0;
+    return moe_batch_scratch(m, n_tok).total;
+}
+
+sg_status sg_moe_forward_batch(const sg_moe *m, const float *d_x, uint64_t ldx, uint64_t n_tok, float *d_out,
+                               uint64_t ldo, void *d_scratch, uint64_t scratch_bytes, sg_moe_choice *d_choices,
+                               void *stream) {
+    sg_status st = check_moe(m);
+    if (st) return st;
+    if (n_tok == 0) return SG_OK;
+    if (n_tok > SG_MOE_MAX_BATCH || m->n_expert > 256) return SG_ERR_SHAPE;
+    if (!d_x || !d_out || !d_scratch || (n_tok > 1 && (ldx < m->dim || ldo < m->dim))) return SG_ERR_INVALID;
+    if (!aligned(d_x, 16) || (n_tok > 1 && ldx % 4) || !aligned(d_out, 4) || !aligned(d_scratch, 256) ||
+        !aligned(d_choices, 16))
+        return SG_ERR_ALIGN;
+    const MoeBatchScratch L = moe_batch_scratch(m, n_tok);
+    if (scratch_bytes < L.total) return SG_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t *sc = (uint8_t *)d_scratch;
+    sg_moe_choice *choices = d_choices ? d_choices : (sg_moe_choice *)(sc + L.choices);
+    uint32_t *slot_base = (uint32_t *)(sc + L.slot_base), *n_slots = (uint32_t *)(sc + L.n_slots);
+    int32_t *slots = (int32_t *)(sc + L.slots), *slots_sh = (int32_t *)(sc + L.slots_sh);
+    uint32_t *n_slots_sh = (uint32_t *)(sc + L.n_slots_sh);
+    float *scale = (float *)(sc + L.scale), *logits = (float *)(sc + L.logits);
+    float *h = (float *)(sc + L.h), *y = (float *)(sc + L.y), *hsh = (float *)(sc + L.hsh), *ysh = (float *)(sc + L.ysh);
+    uint8_t *qx = sc + L.qx;
+    const bool sh = m->shared_gate_up != nullptr;
+    const uint32_t k = (uint32_t)m->n_used, ne = (uint32_t)m->n_expert, nt = (uint32_t)n_tok;
+    // router (every token) -> choices and slot table -> gate/up over all slots
+    // -> down -> [shared gate/up, down over one slot per token] -> combine
+    if ((st = launch_router(m, d_x, logits, qx, (sg_moe_choice *)(sc + L.shsel), scale, s, nt, ldx))) return st;
+    {
+        static std::atomic<uint64_t> attr_done{0};
+        int dev;
+        CK(cudaGetDevice(&dev));
+        if (!(attr_done.load() >> dev & 1)) {
+            CK(cudaFuncSetAttribute((const void *)moe_select_batch_kernel,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+            attr_done.fetch_or(1ull << dev);
+        }
+        SelectBatchArgs sa = {logits, nt, ne, k, m->norm, m->moe_prune, choices, slot_base, slots, n_slots,
+                              sh ? slots_sh : nullptr, sh ? n_slots_sh : nullptr};
+        CK(launch_pdl((const void *)moe_select_batch_kernel, 1, SELECT_BATCH_THREADS, select_batch_smem(nt), s, &sa));
+    }
+    const MoeSlots ms = {slots, n_slots, qx};
+    if ((st = launch_moe_group(m->gate_up_dtype, IN_MOE_X, m->gate_up, m->gate_up_stride, 2 * m->n_ff, m->dim, nt * k,
+                               ne, nullptr, nullptr, nullptr, nullptr, nullptr, 0, h, m->n_ff, s, &ms)) ||
+        (st = launch_moe_group(m->down_dtype, IN_MOE_H, m->down, m->down_stride, m->dim, m->n_ff, nt * k, ne,
+                               nullptr, nullptr, nullptr, nullptr, h, m->n_ff, y, m->dim, s, &ms)))
+        return st;
+    if (sh) {
+        const MoeSlots mss = {slots_sh, n_slots_sh, qx};
+        if ((st = launch_moe_group(m->shared_gate_up_dtype, IN_MOE_X, m->shared_gate_up, 0, 2 * m->shared_n_ff,
+                                   m->dim, nt, 1, nullptr, nullptr, nullptr, nullptr, nullptr, 0, hsh,
+                                   m->shared_n_ff, s, &mss)) ||
+            (st = launch_moe_group(m->shared_down_dtype, IN_MOE_H, m->shared_down, 0, m->dim, m->shared_n_ff, nt, 1,
+                                   nullptr, nullptr, nullptr, nullptr, hsh, m->shared_n_ff, ysh, m->dim, s, &mss)))
+            return st;
+    }
+    CombineBatchArgs c = {choices, slot_base, y, sh ? ysh : nullptr, scale, d_out, n_tok > 1 ? ldo : m->dim,
+                          (uint32_t)m->dim, k};
+    CK(launch_pdl((const void *)moe_combine_batch_kernel, dim3((uint32_t)((m->dim + 255) / 256), nt), 256, 0, s, &c));
     return SG_OK;
 }
 

@@ -59,9 +59,10 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
         a.nstages * nwarps * 8 > ((MOE || a.qx_image) ? MOE_QX_BAR_OFF : TGEMV_BAR_BYTES) ||
         (MODE == IN_Q8K && a.qx_image && a.nvec != 1) ||
         (MOE && a.swiglu && (MODE != IN_MOE_X || a.nvec != 1)) ||
-        (MOE && (a.max_slots > MOE_MAXK || a.tiles_per_mat == 0 || nact == 0 ||
+        (MOE && ((!a.slots && a.max_slots > MOE_MAXK) || a.tiles_per_mat == 0 || nact == 0 ||
                  (uint64_t)a.ntiles * gridDim.x >= (1ull << 32) || a.ntiles < a.max_slots * a.tiles_per_mat)) ||
         (a.npeers && (MOE || a.npeers > TP_MAX_RANKS || !a.ticket || !a.epoch || !a.out[0] || !a.my_recv)) ||
+        (a.slots && (!MOE || !a.n_slots || a.logits || nact > MOE_MAXK || (MODE == IN_MOE_X && !a.qx_tokens))) ||
         (MODE == IN_MOE_X && a.logits &&
          (a.n_expert == 0 || a.n_used == 0 || a.n_used > a.n_expert || a.n_used > MOE_MAXK ||
           moe_select_bytes(a.n_expert) > nwarps * a.nstages * a.stage_bytes))) {
@@ -97,7 +98,10 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
             mbar_arrive_expect_tx(qbar, act_bytes(a.nb));
             bulk_g2s(act, a.qx_image, act_bytes(a.nb), qbar);
         }
-        if (MODE == IN_MOE_X && a.logits) {
+        if (a.slots) {
+            // batched: the slot table was written by the kernel before
+            if (threadIdx.x == 0) msel[0] = min(__ldcg(a.n_slots), a.max_slots);
+        } else if (MODE == IN_MOE_X && a.logits) {
             // every CTA makes the router's choice itself (identical results);
             // the rings are free until the first weight copy is issued
             float *P = reinterpret_cast<float *>(rings);
@@ -168,10 +172,35 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
             s_lo = lo / a.tiles_per_mat;
             s_hi = (hi - 1) / a.tiles_per_mat;
         }
-        if (MODE == IN_MOE_H && lo < hi && s_hi - s_lo + 1 > nact) {  // the host sized nact for this
+        if ((MODE == IN_MOE_H || a.slots) && lo < hi && s_hi - s_lo + 1 > nact) {  // the host sized nact for this
             if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
             my_tiles = 0;
             s_hi = s_lo;
+        }
+        if (a.slots) {
+            // this CTA's slots s_lo..s_hi: expert ids into msel[16..], and for
+            // IN_MOE_X each slot's token image into activation image s - s_lo
+            const uint32_t nloc = my_tiles ? s_hi - s_lo + 1 : 0u;
+            bool bad = false;
+            if (threadIdx.x < nloc) {
+                const int32_t e = __ldcg(a.slots + 2 * (s_lo + threadIdx.x));
+                bad = e < 0 || (uint32_t)e >= a.n_expert;
+                msel[16 + threadIdx.x] = bad ? 0u : (uint32_t)e;
+            }
+            if (MODE == IN_MOE_X && threadIdx.x == 0) {
+                uint64_t *qbar = reinterpret_cast<uint64_t *>(smem + MOE_QX_BAR_OFF);
+                mbar_init(qbar, 1);
+                fence_mbar_init();
+                mbar_arrive_expect_tx(qbar, nloc * act_bytes(a.nb));
+                for (uint32_t j = 0; j < nloc; j++) {
+                    const int32_t tok = __ldcg(a.slots + 2 * (s_lo + j) + 1);
+                    bulk_g2s(act + j * astride, a.qx_tokens + (uint64_t)tok * astride, act_bytes(a.nb), qbar);
+                }
+            }
+            if (__syncthreads_or(bad)) {
+                if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+                my_tiles = 0;
+            }
         }
     } else {
         const uint32_t gid = group * gridDim.x + blockIdx.x;
@@ -189,7 +218,8 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     auto tile_ptr = [&](uint32_t tt) -> const uint8_t * {
         if constexpr (MOE) {
             const uint32_t s = tt / a.tiles_per_mat;
-            return a.w + (uint64_t)sids[s] * a.mat_stride + (uint64_t)(tt - s * a.tiles_per_mat) * tile_bytes;
+            return a.w + (uint64_t)sids[a.slots ? s - s_lo : s] * a.mat_stride +
+                   (uint64_t)(tt - s * a.tiles_per_mat) * tile_bytes;
         } else {
             return a.w + tt * tile_bytes;
         }
@@ -230,7 +260,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                       reinterpret_cast<int16_t *>(av + 256u * nb + 32u * b),
                       reinterpret_cast<float *>(av + 288u * nb + 4u * b), lane);
         }
-    } else if (MODE == IN_MOE_X && a.qx_image) {
+    } else if (MODE == IN_MOE_X && (a.qx_image || a.slots)) {
         if (!mbar_wait_bounded(reinterpret_cast<uint64_t *>(smem + MOE_QX_BAR_OFF), 0, WAIT_LIMIT_NS)) {
             // record it, let this warp's weight copies land (bounded), issue no
             // more; the tile loop keeps its barrier protocol so the CTA exits
@@ -310,7 +340,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
             ms = tt / a.tiles_per_mat;
             mt = tt - ms * a.tiles_per_mat;
         }
-        const uint8_t *tact = MODE == IN_MOE_H ? act + (ms - s_lo) * astride : act;
+        const uint8_t *tact = (MODE == IN_MOE_H || (MODE == IN_MOE_X && a.slots)) ? act + (ms - s_lo) * astride : act;
         float acc[NV][4], corr[NV];
 #pragma unroll
         for (int v = 0; v < NV; v++) {

@@ -100,6 +100,13 @@ struct TGemvArgs {
     uint32_t n_ff;        // IN_MOE_H
     const float *gu;      // IN_MOE_H
     uint64_t gu_stride;   // IN_MOE_H, floats
+    // Batched MoE (several tokens): the slots are (expert, token) pairs in
+    // device memory, *n_slots of them (at most max_slots), instead of one
+    // token's choice; IN_MOE_X stages each slot's token image from qx_tokens
+    // (act_bytes(nb) apart).
+    const int32_t *slots;
+    const uint32_t *n_slots;
+    const uint8_t *qx_tokens;
     // Row-split tensor parallelism (IN_Q8K / IN_F32, npeers > 0).  The call's
     // epoch e is *epoch + 1.  Row r of vector v is stored as the pair
     // (e << 32 | value bits) at peer_recv[p][h*nvec*tp_rows + v*tp_rows +
@@ -127,7 +134,7 @@ __host__ __device__ inline uint32_t moe_select_bytes(uint32_t n_expert) { return
 
 // Activation images staged per CTA.
 __host__ __device__ inline uint32_t tiled_nact(int mode, uint32_t nv, uint32_t nact) {
-    return mode == IN_MOE_H ? nact : mode == IN_MOE_X ? 1u : nv;
+    return (mode == IN_MOE_H || mode == IN_MOE_X) ? (nact ? nact : 1u) : nv;
 }
 
 // Dynamic shared memory of one CTA of `warps` warps:

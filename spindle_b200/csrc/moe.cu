@@ -13,7 +13,7 @@ __global__ void __launch_bounds__(ROUTER_MAX_ROWS * 8) moe_router_kernel(const _
     if (router_smem_bytes(dim, a.rows_per_cta) > dynamic_smem_size() || dim % 8 || a.rows_per_cta == 0 ||
         a.rows_per_cta > ROUTER_MAX_ROWS || blockDim.x < 8 * a.rows_per_cta || (blockDim.x & 31) ||
         a.row_ctas * a.rows_per_cta < a.n_expert || (a.row_ctas - 1) * a.rows_per_cta >= a.n_expert ||
-        blockIdx.x > a.row_ctas || (gate_cta && !a.shared_scale)) {
+        blockIdx.x > a.row_ctas || (gate_cta && !a.shared_scale) || a.n_tok == 0 || (a.n_tok > 1 && a.ldx < dim)) {
         if (tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
         return;
     }
@@ -39,63 +39,73 @@ __global__ void __launch_bounds__(ROUTER_MAX_ROWS * 8) moe_router_kernel(const _
         }
     }
     grid_dependency_wait();
-    if (tid == 0) {
-        mbar_arrive_expect_tx(&bars[1], rowb);
-        bulk_g2s(xs, a.x, rowb, &bars[1]);
-    }
-    __syncthreads();
-    bool ok = mbar_wait_bounded(&bars[1], 0, WAIT_LIMIT_NS);
-    if (loads) ok = mbar_wait_bounded(&bars[0], 0, WAIT_LIMIT_NS) && ok;
-    if (!ok && tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_TMA);
-    // x's Q8_K image for the expert GEMVs (the layout they stage in shared
-    // memory: qs | bsums | d), one 256-block per CTA and warp 0
-    if (a.qx && ok && tid < 32) {
-        const uint32_t nb = dim / 256;
-        for (uint32_t b = blockIdx.x; b < nb; b += gridDim.x)
-            q8k_block(xs + 256u * b, reinterpret_cast<int8_t *>(a.qx + 256u * b),
-                      reinterpret_cast<int16_t *>(a.qx + 256u * nb + 32u * b),
-                      reinterpret_cast<float *>(a.qx + 288u * nb + 4u * b), tid);
-    }
-    if (gate_cta) {
-        // The shared expert's gate: sigmoid(sum over c of w[c] * x[c]), summed
-        // in order as the reference's iterator does (smollm_chat.rs:1374-1377).
+    const uint32_t nb = dim / 256;
+    bool ok = true;
+    for (uint32_t t = 0; t < a.n_tok; t++) {
+        // token t's x (the rows stay), one token after the other
         if (tid == 0) {
-            float gsc = 1.0f;
-            if (want_gate) {
-                if (ok) {
-                    const float *gv = reinterpret_cast<const float *>(rows);
-                    float z = 0.0f;
+            mbar_arrive_expect_tx(&bars[1], rowb);
+            bulk_g2s(xs, a.x + (uint64_t)t * a.ldx, rowb, &bars[1]);
+        }
+        __syncthreads();
+        bool okt = mbar_wait_bounded(&bars[1], t & 1u, WAIT_LIMIT_NS);
+        if (t == 0 && loads) ok = mbar_wait_bounded(&bars[0], 0, WAIT_LIMIT_NS);
+        okt = okt && ok;
+        if (!okt && tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_TMA);
+        // x's Q8_K image for the expert GEMVs (the layout they stage in shared
+        // memory: qs | bsums | d), one 256-block per CTA and warp 0
+        if (a.qx && okt && tid < 32) {
+            uint8_t *qx = a.qx + (uint64_t)t * act_bytes(nb);
+            for (uint32_t b = blockIdx.x; b < nb; b += gridDim.x)
+                q8k_block(xs + 256u * b, reinterpret_cast<int8_t *>(qx + 256u * b),
+                          reinterpret_cast<int16_t *>(qx + 256u * nb + 32u * b),
+                          reinterpret_cast<float *>(qx + 288u * nb + 4u * b), tid);
+        }
+        if (gate_cta) {
+            // The shared expert's gate: sigmoid(sum over c of w[c] * x[c]), summed
+            // in order as the reference's iterator does (smollm_chat.rs:1374-1377).
+            if (tid == 0) {
+                float gsc = 1.0f;
+                if (want_gate) {
+                    if (okt) {
+                        const float *gv = reinterpret_cast<const float *>(rows);
+                        float z = 0.0f;
 #pragma unroll 8
-                    for (uint32_t c = 0; c < dim; c++) z = __fadd_rn(z, __fmul_rn(gv[c], xs[c]));
-                    gsc = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-z)));
-                } else {
-                    gsc = __int_as_float(0x7fc00000);
+                        for (uint32_t c = 0; c < dim; c++) z = __fadd_rn(z, __fmul_rn(gv[c], xs[c]));
+                        gsc = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-z)));
+                    } else {
+                        gsc = __int_as_float(0x7fc00000);
+                    }
+                }
+                a.shared_scale[t] = gsc;
+                if (t == 0) {
+                    sg_moe_choice *c = a.shared_sel;
+                    for (uint32_t i = 0; i < MOE_MAXK; i++) {
+                        c->id[i] = 0;
+                        c->weight[i] = i == 0 ? 1.0f : 0.0f;
+                    }
+                    c->pad_[0] = c->pad_[1] = c->pad_[2] = 0;
+                    c->n = 1;
                 }
             }
-            *a.shared_scale = gsc;
-            sg_moe_choice *t = a.shared_sel;
-            for (uint32_t i = 0; i < MOE_MAXK; i++) {
-                t->id[i] = 0;
-                t->weight[i] = i == 0 ? 1.0f : 0.0f;
-            }
-            t->pad_[0] = t->pad_[1] = t->pad_[2] = 0;
-            t->n = 1;
-        }
-        return;
-    }
-    // thread j of row q: the FMA chain of AVX lane j (elements j, j+8, ...)
-    const uint32_t q = tid >> 3, j = tid & 7u;
-    float acc = 0.0f;
-    if (q < nrows && ok) {
-        const float *row = reinterpret_cast<const float *>(rows + q * rstride);
+        } else {
+            // thread j of row q: the FMA chain of AVX lane j (elements j, j+8, ...)
+            const uint32_t q = tid >> 3, j = tid & 7u;
+            float acc = 0.0f;
+            if (q < nrows && okt) {
+                const float *row = reinterpret_cast<const float *>(rows + q * rstride);
 #pragma unroll 8
-        for (uint32_t i = j; i < dim; i += 8) acc = __fmaf_rn(row[i], xs[i], acc);
+                for (uint32_t i = j; i < dim; i += 8) acc = __fmaf_rn(row[i], xs[i], acc);
+            }
+            // hsum_avx2: ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7)), then + the empty tail (0.0)
+            const float tv = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+            const float u = __fadd_rn(tv, __shfl_down_sync(0xffffffffu, tv, 1));
+            const float v = __fadd_rn(u, __shfl_down_sync(0xffffffffu, u, 2));
+            if (q < nrows && j == 0)
+                a.logits[(uint64_t)t * a.n_expert + e0 + q] = okt ? __fadd_rn(v, 0.0f) : __int_as_float(0x7fc00000);
+        }
+        __syncthreads();  // xs is rewritten for the next token
     }
-    // hsum_avx2: ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7)), then + the empty tail (0.0)
-    const float t = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
-    const float u = __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 1));
-    const float v = __fadd_rn(u, __shfl_down_sync(0xffffffffu, u, 2));
-    if (q < nrows && j == 0) a.logits[e0 + q] = ok ? __fadd_rn(v, 0.0f) : __int_as_float(0x7fc00000);
 }
 
 __global__ void moe_combine_kernel(const __grid_constant__ CombineArgs a) {
@@ -118,6 +128,97 @@ __global__ void moe_combine_kernel(const __grid_constant__ CombineArgs a) {
         acc = __fadd_rn(acc, __fmul_rn(*a.shared_scale, tmp));
     }
     a.out[r] = acc;
+}
+
+// One CTA, one warp per token: each token's choice (select_warp, the same
+// code as the one-token path), then thread 0 lays out the slot table in token
+// order.  Bit for bit the choices of one-token steps (moe_forward_batch takes
+// each token's top-k on its own, smollm_chat.rs:958-1010).
+__global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(const __grid_constant__ SelectBatchArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5, nwarps = blockDim.x / 32;
+    if (a.n_expert == 0 || a.n_expert > 256 || a.n_used == 0 || a.n_used > a.n_expert || a.n_used > MOE_MAXK ||
+        select_batch_smem(a.n_tok) > dynamic_smem_size() || blockDim.x != SELECT_BATCH_THREADS) {
+        if (tid == 0) {
+            atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+            *a.n_slots = 0;
+            if (a.n_slots_sh) *a.n_slots_sh = 0;
+        }
+        return;
+    }
+    float *S = reinterpret_cast<float *>(smem) + warp * 256u;
+    moe::Choice *ch = reinterpret_cast<moe::Choice *>(smem + nwarps * 256u * 4u);
+    for (uint32_t t = warp; t < a.n_tok; t += nwarps) {
+        const float *lg = a.logits + (uint64_t)t * a.n_expert;
+        if (a.n_expert <= 64)
+            moe::select_warp<2>(lg, a.n_expert, a.n_used, a.norm, a.prune, ch + t, nullptr, S, lane);
+        else if (a.n_expert <= 128)
+            moe::select_warp<4>(lg, a.n_expert, a.n_used, a.norm, a.prune, ch + t, nullptr, S, lane);
+        else
+            moe::select_warp<8>(lg, a.n_expert, a.n_used, a.norm, a.prune, ch + t, nullptr, S, lane);
+        __syncwarp();
+    }
+    __syncthreads();
+    for (uint32_t t = warp; t < a.n_tok; t += nwarps) {
+        sg_moe_choice *o = a.choices + t;
+        if (lane < MOE_MAXK) {
+            o->id[lane] = ch[t].id[lane];
+            o->weight[lane] = ch[t].w[lane];
+        }
+        if (lane == 0) {
+            o->n = ch[t].n;
+            o->pad_[0] = o->pad_[1] = o->pad_[2] = 0;
+        }
+    }
+    if (tid == 0) {
+        uint32_t base = 0;
+        for (uint32_t t = 0; t < a.n_tok; t++) {
+            const uint32_t n = min(ch[t].n, a.n_used);
+            a.slot_base[t] = base;
+            for (uint32_t i = 0; i < n; i++) {
+                a.slots[2 * (base + i)] = ch[t].id[i];
+                a.slots[2 * (base + i) + 1] = (int32_t)t;
+            }
+            base += n;
+        }
+        *a.n_slots = base;
+        if (a.slots_sh) {
+            for (uint32_t t = 0; t < a.n_tok; t++) {
+                a.slots_sh[2 * t] = 0;
+                a.slots_sh[2 * t + 1] = (int32_t)t;
+            }
+            *a.n_slots_sh = a.n_tok;
+        }
+    }
+}
+
+// Token blockIdx.y: out = ((0 + w_0*y_0) + w_1*y_1) + ... over its slots in
+// router order (the accumulation of moe_forward_batch, smollm_chat.rs:1134-1140,
+// on a zeroed output), then + g * shared (:1150-1163).
+__global__ void moe_combine_batch_kernel(const __grid_constant__ CombineBatchArgs a) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    __shared__ float w[MOE_MAXK];
+    __shared__ uint32_t n_s, base_s;
+    const uint32_t t = blockIdx.y;
+    if (threadIdx.x < MOE_MAXK) w[threadIdx.x] = a.choices[t].weight[threadIdx.x];
+    if (threadIdx.x == 0) {
+        n_s = min(a.choices[t].n, a.n_used);
+        base_s = a.slot_base[t];
+    }
+    __syncthreads();
+    const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= a.dim) return;
+    float acc = 0.0f;
+    for (uint32_t i = 0; i < n_s; i++)
+        acc = __fadd_rn(acc, __fmul_rn(w[i], a.y[(uint64_t)(base_s + i) * a.dim + r]));
+    if (a.ysh) {
+        const float tmp = __fadd_rn(0.0f, __fmul_rn(1.0f, a.ysh[(uint64_t)t * a.dim + r]));
+        acc = __fadd_rn(acc, __fmul_rn(a.shared_scale[t], tmp));
+    }
+    a.out[(uint64_t)t * a.ldo + r] = acc;
 }
 
 }  // namespace sg

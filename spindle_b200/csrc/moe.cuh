@@ -14,6 +14,7 @@
 #pragma once
 
 #include "gemv_tiled.cuh"
+#include "moe_select.cuh"
 
 namespace sg {
 
@@ -23,16 +24,49 @@ constexpr uint32_t ROUTER_MAX_ROWS = 16; // rows per CTA (8 threads each)
 
 struct RouterArgs {
     const float *w;             // F32 [n_expert][dim]
-    const float *x;             // [dim]
+    const float *x;             // token t at x + t * ldx, [dim]
     uint32_t dim, n_expert;
     uint32_t rows_per_cta;      // CTA b < row_ctas computes rows [b * rows_per_cta, ...)
     uint32_t row_ctas;
-    float *logits;              // [n_expert]
-    uint8_t *qx;                // optional: Q8_K image of x (act_bytes(dim / 256) bytes)
+    float *logits;              // token t at logits + t * n_expert
+    uint8_t *qx;                // optional: Q8_K images of the tokens, act_bytes(dim / 256) apart
     // shared expert (CTA row_ctas, when shared_scale is set)
     sg_moe_choice *shared_sel;  // written as {1, id 0, weight 1}
     const float *shared_gate;   // F32 [dim] or null
-    float *shared_scale;        // sigmoid(shared_gate . x), or 1 without a gate
+    float *shared_scale;        // per token: sigmoid(shared_gate . x), or 1 without a gate
+    uint32_t n_tok;             // tokens (1 for moe_forward)
+    uint64_t ldx;
+};
+
+// Batched MoE (moe_forward_batch): every token's choice from its logits (one
+// warp per token, select_warp), then the flat slot table: token t's chosen
+// experts, in router order, are slots slot_base[t] .. + n_t as (expert, t).
+struct SelectBatchArgs {
+    const float *logits;        // [n_tok][n_expert]
+    uint32_t n_tok, n_expert, n_used;
+    int32_t norm;
+    float prune;
+    sg_moe_choice *choices;     // [n_tok]
+    uint32_t *slot_base;        // [n_tok]
+    int32_t *slots;             // [n_tok * n_used][2]
+    uint32_t *n_slots;
+    int32_t *slots_sh;          // shared expert: [n_tok][2] = (0, t), or null
+    uint32_t *n_slots_sh;
+};
+constexpr uint32_t SELECT_BATCH_THREADS = 1024;
+__host__ __device__ inline uint32_t select_batch_smem(uint32_t n_tok) {
+    return (SELECT_BATCH_THREADS / 32) * 256u * 4u + n_tok * (uint32_t)sizeof(moe::Choice);
+}
+
+struct CombineBatchArgs {
+    const sg_moe_choice *choices;
+    const uint32_t *slot_base;
+    const float *y;             // slot s at y + s * dim
+    const float *ysh;           // shared expert: token t at ysh + t * dim, or null
+    const float *shared_scale;  // [n_tok]
+    float *out;                 // token t at out + t * ldo
+    uint64_t ldo;
+    uint32_t dim, n_used;
 };
 
 // bars (64) | x (dim floats) | rows (rows_per_cta, padded) ; the gate CTA puts
@@ -54,5 +88,7 @@ struct CombineArgs {
 
 __global__ void moe_router_kernel(const __grid_constant__ RouterArgs a);
 __global__ void moe_combine_kernel(const __grid_constant__ CombineArgs a);
+__global__ void moe_select_batch_kernel(const __grid_constant__ SelectBatchArgs a);
+__global__ void moe_combine_batch_kernel(const __grid_constant__ CombineBatchArgs a);
 
 }  // namespace sg
