@@ -373,6 +373,22 @@ SG_API sg_status sg_model_prepare(const sg_model *m, void *d_scratch, uint64_t s
 SG_API sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_scratch, uint64_t scratch_bytes,
                             float *d_hidden, float *d_logits, int64_t *d_token, void *stream);
 
+/* forward_batch_slice + compute_logits_batch (smollm_chat.rs:3146-3362,
+ * :3591-3620): the n tokens d_tokens[0..n) at positions *d_pos .. *d_pos +
+ * n - 1 (device int32, left unchanged; the caller advances it) through every
+ * layer, each attending to every earlier position, its own batch included;
+ * their K/V rows go into the caches.  Per token, bit for bit the one-token
+ * sg_forward step at that position.  d_logits (optional): [n][ldl] floats;
+ * d_greedy (optional): int64[n], each token's greedy next token.  Scratch:
+ * sg_model_batch_scratch_bytes(m, n_max) bytes made ready once by
+ * sg_model_batch_prepare; n <= n_max <= 64 (MoE layers: n_expert <= 256). */
+SG_API uint64_t sg_model_batch_scratch_bytes(const sg_model *m, uint64_t n_max);
+SG_API sg_status sg_model_batch_prepare(const sg_model *m, uint64_t n_max, void *d_scratch, uint64_t scratch_bytes,
+                                        void *stream);
+SG_API sg_status sg_forward_batch(const sg_model *m, const int32_t *d_tokens, uint64_t n, const int32_t *d_pos,
+                                  void *d_kv, void *d_scratch, uint64_t scratch_bytes, uint64_t n_max,
+                                  float *d_logits, uint64_t ldl, int64_t *d_greedy, void *stream);
+
 /* ---- weight quantizer (no reference counterpart: its tests use random bytes)
  * f32 [rows, cols] -> Q4_K or Q6_K rows, deterministic; cols % 256 == 0. */
 SG_API sg_status sg_quantize_weights(int32_t dtype, const float *d_w, uint64_t rows, uint64_t cols,

@@ -108,6 +108,9 @@ SIGNATURES = {
     "sg_model_kv_bytes": (U64, [P]),
     "sg_model_prepare": (I32, [P, P, U64, P]),
     "sg_forward": (I32, [P, P, P, P, U64, P, P, P, P]),
+    "sg_model_batch_scratch_bytes": (U64, [P, U64]),
+    "sg_model_batch_prepare": (I32, [P, U64, P, U64, P]),
+    "sg_forward_batch": (I32, [P, P, U64, P, P, P, U64, U64, P, U64, P, P]),
 }
 
 _lib = None

@@ -1366,10 +1366,59 @@ ModelScratch model_scratch(const sg_model *m) {
 }
 
 sg_status launch_norm(float *x, const float *add, float rs, const float *w, float eps, uint32_t n, float *xn,
-                      uint8_t *qx, cudaStream_t s) {
+                      uint8_t *qx, cudaStream_t s, uint32_t ntok = 1) {
     NormArgs a = {x, add, rs, w, eps, n, xn, qx};
-    CK(launch_pdl((const void *)rmsnorm_kernel, 1, NORM_THREADS, n * 4, s, &a));
+    CK(launch_pdl((const void *)rmsnorm_kernel, ntok, NORM_THREADS, n * 4, s, &a));
     return SG_OK;
+}
+
+// Scratch of sg_forward_batch for up to n_max tokens per call.
+struct ModelBatchScratch {
+    uint64_t x, xn, qx, qkv, att, proj, logits, h, freqs, amax, slots, n_slots, moe, moe_bytes, total;
+};
+
+ModelBatchScratch model_batch_scratch(const sg_model *m, uint64_t n) {
+    ModelBatchScratch L;
+    uint64_t off = 0;
+    auto take = [&](uint64_t bytes) {
+        const uint64_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const uint64_t q_dim = (uint64_t)m->n_heads * m->head_dim, kv_dim = (uint64_t)m->n_kv_heads * m->head_dim;
+    uint64_t n_ff = 0, moe = 0;
+    for (uint32_t l = 0; l < m->n_layers; l++) {
+        const sg_layer &y = m->layers[l];
+        if (y.is_moe) {
+            const uint64_t b = sg_moe_batch_scratch_bytes(&y.moe, n);
+            moe = b > moe ? b : moe;
+        } else if (y.n_ff > n_ff) {
+            n_ff = y.n_ff;
+        }
+    }
+    L.x = take(n * m->dim * 4);
+    L.xn = take(n * m->dim * 4);
+    L.qx = take(n * act_bytes(m->dim / 256));
+    L.qkv = take(n * (q_dim + 2 * kv_dim) * 4);
+    L.att = take(n * q_dim * 4);
+    L.proj = take(n * m->dim * 4);
+    L.logits = take(n * (uint64_t)m->vocab * 4);
+    L.h = take(n * n_ff * 4);
+    L.freqs = take(m->head_dim / 2 * 4);
+    L.amax = take(n * (ARGMAX_CTAS * 8 + 4));  // partial maxima, then the ticket counts
+    L.slots = take(n * 8);                       // dense FFN: slot t = (0, t)
+    L.n_slots = take(4);
+    L.moe = take(moe);
+    L.moe_bytes = moe;
+    L.total = off;
+    return L;
+}
+
+// Rows of a TILED16 matrix for n fp32 vectors (cols apart), outs[t] per vector.
+sg_status gemv_rows(const uint8_t *w, int32_t dtype, uint64_t rows, uint64_t cols, const float *x,
+                    std::vector<float *> &outs, uint32_t n, cudaStream_t s) {
+    return launch_tiled(w, dtype == SG_Q4_K ? DT_Q4K : DT_Q6K, (uint32_t)(cols / 256), nullptr, x, cols, outs.data(), n,
+                        0, rows, s);
 }
 
 sg_status gemv_image(const uint8_t *w, int32_t dtype, uint64_t rows, uint64_t cols, const uint8_t *image, float *out,
@@ -1411,6 +1460,138 @@ sg_status sg_model_prepare(const sg_model *m, void *d_scratch, uint64_t scratch_
     CK(cudaMemcpyAsync(sc + L.sel1, &one, sizeof one, cudaMemcpyHostToDevice, (cudaStream_t)stream));
     CK(cudaMemsetAsync(sc + L.amax + ARGMAX_CTAS * 8, 0, 8, (cudaStream_t)stream));
     CK(cudaStreamSynchronize((cudaStream_t)stream));  // the host sources go out of scope
+    return SG_OK;
+}
+
+uint64_t sg_model_batch_scratch_bytes(const sg_model *m, uint64_t n_max) {
+    if (check_model(m) || n_max == 0 || n_max > SG_MOE_MAX_BATCH) return 0;
+    for (uint32_t l = 0; l < m->n_layers; l++)
+        if (m->layers[l].is_moe && m->layers[l].moe.n_expert > 256) return 0;
+    return model_batch_scratch(m, n_max).total;
+}
+
+sg_status sg_model_batch_prepare(const sg_model *m, uint64_t n_max, void *d_scratch, uint64_t scratch_bytes,
+                                 void *stream) {
+    sg_status st = check_model(m);
+    if (st) return st;
+    if (n_max == 0 || n_max > SG_MOE_MAX_BATCH) return SG_ERR_SHAPE;
+    const ModelBatchScratch L = model_batch_scratch(m, n_max);
+    if (!d_scratch || scratch_bytes < L.total) return SG_ERR_INVALID;
+    if (!aligned(d_scratch, 256)) return SG_ERR_ALIGN;
+    std::vector<float> f(m->head_dim / 2);
+    for (uint32_t i = 0; i < m->head_dim / 2; i++) {
+        const float e = (2.0f * (float)i) / (float)m->head_dim;
+        f[i] = 1.0f / powf(m->rope_theta, e);
+    }
+    std::vector<int32_t> slots(2 * n_max);
+    for (uint64_t t = 0; t < n_max; t++) {
+        slots[2 * t] = 0;
+        slots[2 * t + 1] = (int32_t)t;
+    }
+    uint8_t *sc = (uint8_t *)d_scratch;
+    cudaStream_t s = (cudaStream_t)stream;
+    CK(cudaMemcpyAsync(sc + L.freqs, f.data(), f.size() * 4, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(sc + L.slots, slots.data(), slots.size() * 4, cudaMemcpyHostToDevice, s));
+    CK(cudaMemsetAsync(sc + L.amax + n_max * ARGMAX_CTAS * 8, 0, n_max * 4, s));
+    CK(cudaStreamSynchronize(s));  // the host sources go out of scope
+    return SG_OK;
+}
+
+sg_status sg_forward_batch(const sg_model *m, const int32_t *d_tokens, uint64_t n, const int32_t *d_pos, void *d_kv,
+                           void *d_scratch, uint64_t scratch_bytes, uint64_t n_max, float *d_logits, uint64_t ldl,
+                           int64_t *d_greedy, void *stream) {
+    sg_status st = check_model(m);
+    if (st) return st;
+    if (n == 0) return SG_OK;
+    if (!d_tokens || !d_pos || !d_kv || !d_scratch || n > n_max || n_max > SG_MOE_MAX_BATCH) return SG_ERR_INVALID;
+    if (d_logits && n > 1 && ldl < m->vocab) return SG_ERR_INVALID;
+    if (!aligned(d_scratch, 256) || !aligned(d_kv, 16) || !aligned(d_tokens, 4) || !aligned(d_pos, 4) ||
+        !aligned(d_logits, 4) || !aligned(d_greedy, 8))
+        return SG_ERR_ALIGN;
+    const ModelBatchScratch L = model_batch_scratch(m, n_max);
+    if (scratch_bytes < L.total) return SG_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t *sc = (uint8_t *)d_scratch;
+    const uint32_t dim = m->dim, hd = m->head_dim, q_dim = m->n_heads * hd, kv_dim = m->n_kv_heads * hd;
+    const uint32_t nt = (uint32_t)n, qkv_stride = q_dim + 2 * kv_dim;
+    float *x = (float *)(sc + L.x), *xn = (float *)(sc + L.xn), *qkv = (float *)(sc + L.qkv);
+    float *att = (float *)(sc + L.att), *proj = (float *)(sc + L.proj), *h = (float *)(sc + L.h);
+    float *logits = d_logits ? d_logits : (float *)(sc + L.logits);
+    const uint64_t lstride = d_logits && n > 1 ? ldl : m->vocab;
+    uint8_t *qx = sc + L.qx;
+    const float *freqs = (const float *)(sc + L.freqs);
+    const uint64_t cache = (uint64_t)m->max_seq * kv_dim;
+    uint16_t *kc = (uint16_t *)d_kv, *vc = kc + (uint64_t)m->n_layers * cache;
+    const float scale = m->attn_scale != 0.0f ? m->attn_scale : 1.0f / sqrtf((float)hd);
+    const void *attn_fn = hd == 64 ? (const void *)attention_kernel<64>
+                          : hd == 128 ? (const void *)attention_kernel<128> : (const void *)attention_kernel<256>;
+    {
+        static std::atomic<uint64_t> attr_done{0};
+        int dev;
+        CK(cudaGetDevice(&dev));
+        if (!(attr_done.load() >> dev & 1)) {
+            for (const void *fn : {(const void *)attention_kernel<64>, (const void *)attention_kernel<128>,
+                                   (const void *)attention_kernel<256>})
+                CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+            attr_done.fetch_or(1ull << dev);
+        }
+    }
+    std::vector<float *> oq(nt), ok_(nt), ov(nt), oo(nt), ol(nt);
+    for (uint32_t t = 0; t < nt; t++) {
+        oq[t] = qkv + (uint64_t)t * qkv_stride;
+        ok_[t] = oq[t] + q_dim;
+        ov[t] = ok_[t] + kv_dim;
+        oo[t] = proj + (uint64_t)t * dim;
+        ol[t] = logits + (uint64_t)t * lstride;
+    }
+    uint32_t *n_slots = (uint32_t *)(sc + L.n_slots);
+    EmbedArgs ea = {m->embed, m->embed_dtype, dim, m->vocab, m->embedding_scale, nullptr, x, d_tokens, n_slots};
+    CK(launch_pdl((const void *)embed_kernel, dim3((dim + 255) / 256, nt), 256, 0, s, &ea));
+    for (uint32_t l = 0; l < m->n_layers; l++) {
+        const sg_layer &y = m->layers[l];
+        if ((st = launch_norm(x, l ? proj : nullptr, m->residual_scale, y.attn_norm, m->rms_eps, dim, xn, nullptr, s,
+                              nt)))
+            return st;
+        uint64_t wq_bytes = 0;
+        const bool qk_one = y.wk_dtype == y.wq_dtype && !sg_tiled16_bytes(y.wq_dtype, q_dim, dim, &wq_bytes) &&
+                            y.wk == y.wq + wq_bytes;
+        auto gemv = [&](const uint8_t *w, int32_t dt, uint32_t rows, uint32_t cols, const float *xin,
+                        std::vector<float *> &outs) {
+            return launch_tiled(w, dt == SG_Q4_K ? DT_Q4K : DT_Q6K, cols / 256, nullptr, xin, cols, outs.data(), nt, 0,
+                                rows, s);
+        };
+        if (qk_one) {
+            if ((st = gemv(y.wq, y.wq_dtype, q_dim + kv_dim, dim, xn, oq))) return st;
+        } else if ((st = gemv(y.wq, y.wq_dtype, q_dim, dim, xn, oq)) || (st = gemv(y.wk, y.wk_dtype, kv_dim, dim, xn, ok_))) {
+            return st;
+        }
+        if ((st = gemv(y.wv, y.wv_dtype, kv_dim, dim, xn, ov))) return st;
+        RopeBatchArgs ra = {qkv, qkv + q_dim, qkv + q_dim + kv_dim, qkv_stride, y.q_norm, y.k_norm, m->rms_eps, freqs,
+                            hd, m->n_heads, m->n_kv_heads, m->rope_neox, d_pos, kc + l * cache, vc + l * cache,
+                            m->max_seq};
+        CK(launch_pdl((const void *)rope_kv_batch_kernel, dim3(m->n_heads + m->n_kv_heads, nt), 32, 0, s, &ra));
+        AttnArgs aa = {qkv, nullptr, nullptr, nullptr, nullptr, m->rms_eps, freqs, hd, m->n_heads, m->n_kv_heads,
+                       m->max_seq, m->rope_neox, scale, d_pos, kc + l * cache, vc + l * cache, att, 1, qkv_stride};
+        CK(launch_pdl(attn_fn, dim3(m->n_heads, nt), attn_threads(hd), attn_smem_bytes(hd, m->max_seq), s, &aa));
+        if ((st = gemv(y.wo, y.wo_dtype, dim, q_dim, att, oo))) return st;
+        if ((st = launch_norm(x, proj, m->residual_scale, y.ffn_norm, m->rms_eps, dim, xn, qx, s, nt))) return st;
+        if (y.is_moe) {
+            if ((st = sg_moe_forward_batch(&y.moe, xn, dim, n, proj, dim, sc + L.moe, L.moe_bytes, nullptr, stream)))
+                return st;
+        } else {
+            const MoeSlots ms = {(const int32_t *)(sc + L.slots), n_slots, qx};
+            if ((st = launch_moe_group(y.ffn_gate_up_dtype, IN_MOE_X, y.ffn_gate_up, 0, 2 * y.n_ff, dim, nt, 1,
+                                       nullptr, nullptr, nullptr, nullptr, nullptr, 0, h, y.n_ff, s, &ms)) ||
+                (st = launch_moe_group(y.ffn_down_dtype, IN_MOE_H, y.ffn_down, 0, dim, y.n_ff, nt, 1, nullptr, nullptr,
+                                       nullptr, nullptr, h, y.n_ff, proj, dim, s, &ms)))
+                return st;
+        }
+    }
+    if ((st = launch_norm(x, proj, m->residual_scale, m->output_norm, m->rms_eps, dim, xn, nullptr, s, nt))) return st;
+    if ((st = gemv_rows(m->lm_head, m->lm_head_dtype, m->vocab, dim, xn, ol, nt, s))) return st;
+    ArgmaxArgs ga = {logits, m->vocab, nullptr, d_greedy, (unsigned long long *)(sc + L.amax),
+                     (unsigned *)(sc + L.amax + n_max * ARGMAX_CTAS * 8), 1, lstride};
+    if (d_greedy) CK(launch_pdl((const void *)argmax_kernel, dim3(ARGMAX_CTAS, nt), ARGMAX_THREADS, 0, s, &ga));
     return SG_OK;
 }
 

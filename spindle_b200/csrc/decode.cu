@@ -21,11 +21,13 @@ __global__ void embed_kernel(const __grid_constant__ EmbedArgs a) {
     grid_dependency_wait();
     grid_launch_dependents();
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (a.n_out && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *a.n_out = gridDim.y;
     if (i >= a.dim) return;
-    const int32_t tok = a.state[0];
+    const int32_t tok = a.tokens ? a.tokens[blockIdx.y] : a.state[0];
+    float *const xo = a.x + (uint64_t)blockIdx.y * a.dim;
     if (tok < 0 || (uint32_t)tok >= a.vocab) {
         if (i == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
-        a.x[i] = __int_as_float(0x7fc00000);
+        xo[i] = __int_as_float(0x7fc00000);
         return;
     }
     float y;
@@ -56,7 +58,7 @@ __global__ void embed_kernel(const __grid_constant__ EmbedArgs a) {
         y = __fmul_rn(__fmul_rn(d, (float)sc[l / 16 + 2 * quad]), (float)q);
     }
     if (a.scale != 1.0f) y = __fmul_rn(y, a.scale);
-    a.x[i] = y;
+    xo[i] = y;
 }
 
 // The sum of squares of n values in shared memory, one element after the other
@@ -95,16 +97,21 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const __grid_cons
         if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
         return;
     }
+    // CTA t: token t of a batch (one token: t = 0)
+    const uint64_t to = (uint64_t)blockIdx.x * a.n;
+    float *const X = a.x + to, *const XN = a.xn + to;
+    const float *const ADD = a.add ? a.add + to : nullptr;
+    uint8_t *const QX = a.qx ? a.qx + (uint64_t)blockIdx.x * act_bytes(a.n / 256) : nullptr;
     float v[PER];
 #pragma unroll
     for (int j = 0; j < PER; j++) {
         const uint32_t i = threadIdx.x + j * blockDim.x;
         v[j] = 0.0f;
         if (i < a.n) {
-            float x = a.x[i];
-            if (a.add) {
-                x = __fadd_rn(x, __fmul_rn(a.rs, a.add[i]));
-                a.x[i] = x;
+            float x = X[i];
+            if (ADD) {
+                x = __fadd_rn(x, __fmul_rn(a.rs, ADD[i]));
+                X[i] = x;
             }
             v[j] = x;
             xs[i] = x;
@@ -122,17 +129,17 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const __grid_cons
         const uint32_t i = threadIdx.x + j * blockDim.x;
         if (i < a.n) {
             const float y = __fmul_rn(__fmul_rn(v[j], inv), a.w[i]);
-            a.xn[i] = y;
-            if (a.qx) xs[i] = y;
+            XN[i] = y;
+            if (QX) xs[i] = y;
         }
     }
-    if (a.qx) {
+    if (QX) {
         __syncthreads();
         const uint32_t nb = a.n / 256, warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
         for (uint32_t b = warp; b < nb; b += blockDim.x / 32)
-            q8k_block(xs + 256u * b, reinterpret_cast<int8_t *>(a.qx + 256u * b),
-                      reinterpret_cast<int16_t *>(a.qx + 256u * nb + 32u * b),
-                      reinterpret_cast<float *>(a.qx + 288u * nb + 4u * b), lane);
+            q8k_block(xs + 256u * b, reinterpret_cast<int8_t *>(QX + 256u * b),
+                      reinterpret_cast<int16_t *>(QX + 256u * nb + 32u * b),
+                      reinterpret_cast<float *>(QX + 288u * nb + 4u * b), lane);
     }
 }
 
@@ -155,7 +162,9 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
     extern __shared__ __align__(16) uint8_t sm8[];
     constexpr uint32_t RS = 2 * HD + ATTN_ROW_PAD, HALF = HD / 2;
     const uint32_t h = blockIdx.x, tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-    const uint32_t nwarps = blockDim.x / 32, pos = (uint32_t)a.state[1], T = pos + 1;
+    const bool prep = a.prepared != 0;
+    const uint32_t nwarps = blockDim.x / 32, pos = prep ? (uint32_t)a.state[0] + blockIdx.y : (uint32_t)a.state[1];
+    const uint32_t T = pos + 1;
     const uint32_t msq = attn_seq4(a.max_seq);
     if (a.head_dim != HD || pos >= a.max_seq || attn_smem_bytes(HD, a.max_seq) > dynamic_smem_size() ||
         blockDim.x != attn_threads(HD) || a.n_heads % a.n_kv) {
@@ -200,12 +209,23 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
         fence_mbar_init();
     }
     __syncthreads();
-    const uint32_t first = pos < ATTN_CHUNK ? pos : ATTN_CHUNK;
-    stage(0, 0, first);
-    stage(1, 0, first);
+    // rows copied from the caches: [0, pos) here (this position's come from
+    // registers), [0, T) in the prepared batch form
+    const uint32_t cached = prep ? T : pos;
+    const uint32_t first = cached < ATTN_CHUNK ? cached : ATTN_CHUNK;
+    if (!prep) {  // earlier steps wrote these rows: copy them before waiting
+        stage(0, 0, first);
+        stage(1, 0, first);
+    }
 
     grid_dependency_wait();
     grid_launch_dependents();
+    if (prep) {  // the kernel before this one wrote the batch's rows
+        stage(0, 0, first);
+        stage(1, 0, first);
+        for (uint32_t d = tid; d < HD; d += blockDim.x) qs[d] = a.q[(uint64_t)blockIdx.y * a.q_stride + h * HD + d];
+    }
+    if (!prep) {
 
     // ---- this position: head norms, RoPE, f16 K and V ----
     for (uint32_t d = tid; d < 2 * HD; d += blockDim.x) hs[d] = d < HD ? a.q[h * HD + d] : a.k[kvh * HD + d - HD];
@@ -249,19 +269,21 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
             a.vc[(uint64_t)pos * kv_dim + kvh * HD + d] = vcur[d];
         }
     }
+    }  // !prep
+    __syncthreads();
 
     // ---- scores, chunk by chunk: 8 lanes per position (the 8 AVX lanes) ----
     const uint32_t grp = lane >> 3, l8 = lane & 7u;
     uint32_t kph = 0;
     for (uint32_t c0 = 0; c0 < T; c0 += ATTN_CHUNK) {
         const uint32_t cn = T - c0 < ATTN_CHUNK ? T - c0 : ATTN_CHUNK;
-        const uint32_t cend = c0 + ATTN_CHUNK < pos ? c0 + ATTN_CHUNK : pos;  // rows copied: [c0, cend)
+        const uint32_t cend = c0 + ATTN_CHUNK < cached ? c0 + ATTN_CHUNK : cached;  // rows copied: [c0, cend)
         if (c0 > 0) {
             __syncthreads();  // the previous chunk's rows are read
             stage(0, c0, cend);
         }
         if (cend > c0) wait_rows(0, kph++);
-        if (pos < c0 + cn) {
+        if (!prep && pos < c0 + cn) {
             for (uint32_t d = tid; d < HD; d += blockDim.x)
                 reinterpret_cast<uint16_t *>(kbuf + (pos - c0) * RS)[d] = kcur[d];
         }
@@ -312,11 +334,11 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
     float acc = 0.0f, l = 0.0f;
     for (uint32_t c0 = 0; c0 < T; c0 += ATTN_CHUNK) {
         const uint32_t cn = T - c0 < ATTN_CHUNK ? T - c0 : ATTN_CHUNK;
-        const uint32_t cend = c0 + ATTN_CHUNK < pos ? c0 + ATTN_CHUNK : pos;
+        const uint32_t cend = c0 + ATTN_CHUNK < cached ? c0 + ATTN_CHUNK : cached;
         __syncthreads();  // maxima done; the previous chunk's rows are read
         if (c0 > 0) stage(1, c0, cend);
         if (cend > c0) wait_rows(1, vph++);
-        if (pos < c0 + cn) {
+        if (!prep && pos < c0 + cn) {
             for (uint32_t d = tid; d < HD; d += blockDim.x)
                 reinterpret_cast<uint16_t *>(vbuf + (pos - c0) * RS)[d] = vcur[d];
         }
@@ -337,7 +359,8 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
             if (staged[w]) mbar_wait_bounded(&bars[w], (staged[w] - 1) & 1u, WAIT_LIMIT_NS);
     }
     __syncthreads();
-    if (tid < HD) a.out[h * HD + tid] = ok ? __fmul_rn(acc, lsh[0]) : __int_as_float(0x7fc00000);
+    if (tid < HD)
+        a.out[(uint64_t)blockIdx.y * a.n_heads * HD + h * HD + tid] = ok ? __fmul_rn(acc, lsh[0]) : __int_as_float(0x7fc00000);
 }
 
 template __global__ void attention_kernel<64>(const __grid_constant__ AttnArgs);
@@ -363,35 +386,119 @@ __global__ void __launch_bounds__(ARGMAX_THREADS) argmax_kernel(const __grid_con
         for (uint32_t w = 1; w < blockDim.x / 32; w++) best = red[w] > best ? red[w] : best;
         return best;
     };
+    // batch: token blockIdx.y (its logits, partial maxima and ticket)
+    const uint32_t tb = blockIdx.y;
+    const float *const lg = a.logits + (uint64_t)tb * a.ldl;
+    unsigned long long *const part = a.partial + (uint64_t)tb * gridDim.x;
+    unsigned *const cnt = a.count + tb;
     unsigned long long best = 0;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += gridDim.x * blockDim.x) {
-        const int32_t b = __float_as_int(a.logits[i]);
+        const int32_t b = __float_as_int(lg[i]);
         const uint32_t key = (uint32_t)(b ^ (int32_t)((uint32_t)(b >> 31) >> 1)) ^ 0x80000000u;
         const unsigned long long v = ((unsigned long long)key << 32) | i;
         best = v > best ? v : best;
     }
     best = block_max(best);
     if (threadIdx.x == 0) {
-        a.partial[blockIdx.x] = best;
+        part[blockIdx.x] = best;
         __threadfence();
-        last = atomicAdd(a.count, 1u) == gridDim.x - 1;
+        last = atomicAdd(cnt, 1u) == gridDim.x - 1;
     }
     __syncthreads();
     if (!last) return;
     __threadfence();
     best = 0;
     for (uint32_t b = threadIdx.x; b < gridDim.x; b += blockDim.x) {
-        const unsigned long long v = __ldcg(a.partial + b);
+        const unsigned long long v = __ldcg(part + b);
         best = v > best ? v : best;
     }
     __syncthreads();  // red[] is reused
     best = block_max(best);
     if (threadIdx.x == 0) {
         const int32_t tok = (int32_t)(best & 0xFFFFFFFFull);
-        a.state[0] = tok;
-        a.state[1] = a.state[1] + 1;
-        if (a.out) *a.out = tok;
-        *a.count = 0;
+        if (a.batch) {
+            if (a.out) a.out[tb] = tok;
+        } else {
+            a.state[0] = tok;
+            a.state[1] = a.state[1] + 1;
+            if (a.out) *a.out = tok;
+        }
+        *cnt = 0;
+    }
+}
+
+// Batch: token blockIdx.y at position *pos + blockIdx.y.  Warp h < n_heads:
+// q head h (normed, rotated in place); else kv head h - n_heads: k normed and
+// rotated, K and V rows rounded to f16 into the caches.  The arithmetic of the
+// one-token attention kernel's first part.
+__global__ void rope_kv_batch_kernel(const __grid_constant__ RopeBatchArgs a) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const uint32_t h = blockIdx.x, lane = threadIdx.x, hd = a.head_dim, half = hd / 2, t = blockIdx.y;
+    const bool is_q = h < a.n_heads;
+    const uint32_t kh = is_q ? 0u : h - a.n_heads;
+    const uint32_t pos = (uint32_t)*a.pos + t;
+    if (hd > 256 || (hd & 63u) || pos >= a.max_seq || blockDim.x != 32) {
+        if (lane == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+        return;
+    }
+    float *const q = a.q + (uint64_t)t * a.qkv_stride;
+    const float *const k = a.k + (uint64_t)t * a.qkv_stride, *const v = a.v + (uint64_t)t * a.qkv_stride;
+    const float *src = is_q ? q + h * hd : k + kh * hd;
+    const float *nw = is_q ? a.qn_w : a.kn_w;
+    // lane holds the pairs (i, i + half), i = lane + 32 j
+    constexpr int MAXP = 4;
+    const uint32_t np = half / 32;
+    float x0[MAXP], x1[MAXP];
+    __shared__ __align__(16) float hs[256];
+#pragma unroll
+    for (int j = 0; j < MAXP; j++)
+        if ((uint32_t)j < np) {
+            const uint32_t i = lane + 32u * j;
+            const uint32_t ia = a.neox ? i : 2 * i, ib = a.neox ? i + half : 2 * i + 1;
+            x0[j] = src[ia];
+            x1[j] = src[ib];
+            hs[ia] = x0[j];
+            hs[ib] = x1[j];
+        }
+    if (nw) {
+        // rmsnorm_heads: the head's sum of squares in element order, by lane 0
+        __syncwarp();
+        float inv = 0.0f;
+        if (lane == 0) inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(seq_sum_squares(hs, hd), (float)hd), a.eps)));
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+#pragma unroll
+        for (int j = 0; j < MAXP; j++)
+            if ((uint32_t)j < np) {
+                const uint32_t i = lane + 32u * j;
+                const uint32_t ia = a.neox ? i : 2 * i, ib = a.neox ? i + half : 2 * i + 1;
+                x0[j] = __fmul_rn(__fmul_rn(x0[j], inv), nw[ia]);
+                x1[j] = __fmul_rn(__fmul_rn(x1[j], inv), nw[ib]);
+            }
+    }
+    const float fpos = (float)pos;
+    const uint32_t kv_dim = a.n_kv * hd;
+#pragma unroll
+    for (int j = 0; j < MAXP; j++)
+        if ((uint32_t)j < np) {
+            const uint32_t i = lane + 32u * j;
+            const uint32_t ia = a.neox ? i : 2 * i, ib = a.neox ? i + half : 2 * i + 1;
+            const float ang = __fmul_rn(fpos, a.inv_freq[i]);
+            const float sn = (float)sin((double)ang), cs = (float)cos((double)ang);
+            const float y0 = __fsub_rn(__fmul_rn(x0[j], cs), __fmul_rn(x1[j], sn));
+            const float y1 = __fadd_rn(__fmul_rn(x0[j], sn), __fmul_rn(x1[j], cs));
+            if (is_q) {
+                q[h * hd + ia] = y0;
+                q[h * hd + ib] = y1;
+            } else {
+                uint16_t *kr = a.kc + (uint64_t)pos * kv_dim + kh * hd;
+                kr[ia] = __half_as_ushort(__float2half_rn(y0));
+                kr[ib] = __half_as_ushort(__float2half_rn(y1));
+            }
+        }
+    if (!is_q) {
+        uint16_t *vr = a.vc + (uint64_t)pos * kv_dim + kh * hd;
+        for (uint32_t i = lane; i < hd; i += 32) vr[i] = __half_as_ushort(__float2half_rn(v[kh * hd + i]));
     }
 }
 

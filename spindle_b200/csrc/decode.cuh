@@ -32,6 +32,10 @@ struct EmbedArgs {
     float scale;
     const int32_t *state;   // state[0] = token
     float *x;
+    // batch (grid.y tokens): token blockIdx.y is tokens[blockIdx.y], its x at x + blockIdx.y * dim;
+    // block (0, 0) also stores the token count in *n_out when set
+    const int32_t *tokens;
+    uint32_t *n_out;
 };
 
 // x += rs * add (when add); xn = (x * inv) * w with inv = 1 / sqrt(mean(x^2) + eps);
@@ -45,6 +49,24 @@ struct NormArgs {
     uint32_t n;
     float *xn;
     uint8_t *qx;
+    // batch: CTA t normalizes token t (x, add, xn at + t * n; qx at + t * act_bytes(n / 256))
+};
+
+// Batch: this position's QK-norm, RoPE and f16 K/V rows of token blockIdx.y
+// (position *pos + blockIdx.y), one warp per head (q heads, then kv heads);
+// q is rotated in place.  Tokens are qkv_stride floats apart in q, k and v.
+struct RopeBatchArgs {
+    float *q;
+    const float *k, *v;
+    uint64_t qkv_stride;
+    const float *qn_w, *kn_w;
+    float eps;
+    const float *inv_freq;
+    uint32_t head_dim, n_heads, n_kv;
+    int32_t neox;
+    const int32_t *pos;
+    uint16_t *kc, *vc;
+    uint32_t max_seq;
 };
 
 // One query head of grouped-query attention over positions 0..pos, with this
@@ -63,6 +85,11 @@ struct AttnArgs {
     const int32_t *state;       // state[1] = pos
     uint16_t *kc, *vc;          // this layer's caches: [max_seq][n_kv * head_dim]
     float *out;                 // [n_heads * head_dim]
+    // batch ("prepared"): token blockIdx.y at position state[0] + blockIdx.y,
+    // q already normed and rotated at q + blockIdx.y * q_stride, this position's
+    // K/V rows already in the caches; out at out + blockIdx.y * n_heads * head_dim
+    uint32_t prepared;
+    uint64_t q_stride;
 };
 
 // The greedy token (f32::total_cmp, last maximum on ties), written as the next
@@ -76,6 +103,10 @@ struct ArgmaxArgs {
     int64_t *out;               // optional: the token, also kept here
     unsigned long long *partial;  // [ARGMAX_CTAS]
     unsigned *count;            // 0 before the launch, 0 after it
+    // batch (grid.y tokens): token t's logits at logits + t * ldl, partial +
+    // t * ARGMAX_CTAS, count + t; out[t] gets its greedy token; state untouched
+    uint32_t batch;
+    uint64_t ldl;
 };
 
 // Positions of K and V staged in shared memory at a time, and the padding of a
@@ -98,5 +129,6 @@ __global__ void rmsnorm_kernel(const __grid_constant__ NormArgs a);
 template <int HD>
 __global__ void attention_kernel(const __grid_constant__ AttnArgs a);
 __global__ void argmax_kernel(const __grid_constant__ ArgmaxArgs a);
+__global__ void rope_kv_batch_kernel(const __grid_constant__ RopeBatchArgs a);
 
 }  // namespace sg

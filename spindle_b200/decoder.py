@@ -48,6 +48,13 @@ def _sigs():
         L.sg_model_prepare.argtypes = [C.POINTER(SgModel), P, C.c_uint64, P]
         L.sg_forward.restype = C.c_int32
         L.sg_forward.argtypes = [C.POINTER(SgModel), P, P, P, C.c_uint64, P, P, P, P]
+        L.sg_model_batch_scratch_bytes.restype = C.c_uint64
+        L.sg_model_batch_scratch_bytes.argtypes = [C.POINTER(SgModel), C.c_uint64]
+        L.sg_model_batch_prepare.restype = C.c_int32
+        L.sg_model_batch_prepare.argtypes = [C.POINTER(SgModel), C.c_uint64, P, C.c_uint64, P]
+        L.sg_forward_batch.restype = C.c_int32
+        L.sg_forward_batch.argtypes = [C.POINTER(SgModel), P, C.c_uint64, P, P, P, C.c_uint64, C.c_uint64, P,
+                                       C.c_uint64, P, P]
         L._dec_ready = True
     return L
 
@@ -164,6 +171,32 @@ class Decoder:
                                 C.c_void_p(self.hidden.data_ptr()) if hidden else None,
                                 C.c_void_p(self.logits.data_ptr()) if logits else None,
                                 C.c_void_p(self.token.data_ptr()), _stream(stream)), "sg_forward")
+
+    def forward_batch(self, tokens, pos0, logits=True, n_max=64, stream=None):
+        """forward_batch_slice + compute_logits_batch: tokens at positions
+        pos0 .. pos0 + n - 1 in one call (their K/V rows enter the cache).
+        Returns (logits [n, vocab] or None, greedy next tokens int64 [n]); per
+        token bit for bit the one-token step."""
+        L = _sigs()
+        n = len(tokens)
+        if getattr(self, "_bscratch", None) is None or self._bn < n_max:
+            nbytes = L.sg_model_batch_scratch_bytes(C.byref(self.model), n_max)
+            if not nbytes:
+                raise SgError(3, "sg_model_batch_scratch_bytes")
+            self._bscratch = torch.empty(nbytes, dtype=torch.uint8, device=self.dev)
+            self._bn = n_max
+            _lib.check(L.sg_model_batch_prepare(C.byref(self.model), n_max, C.c_void_p(self._bscratch.data_ptr()),
+                                                nbytes, _stream(stream)), "sg_model_batch_prepare")
+        toks = torch.tensor(list(tokens), dtype=torch.int32, device=self.dev)
+        pos = torch.tensor([pos0], dtype=torch.int32, device=self.dev)
+        lg = torch.empty(n, self.cfg["vocab"], dtype=torch.float32, device=self.dev) if logits else None
+        greedy = torch.empty(n, dtype=torch.int64, device=self.dev)
+        _lib.check(L.sg_forward_batch(C.byref(self.model), C.c_void_p(toks.data_ptr()), n, C.c_void_p(pos.data_ptr()),
+                                      C.c_void_p(self.kv.data_ptr()), C.c_void_p(self._bscratch.data_ptr()),
+                                      self._bscratch.numel(), self._bn,
+                                      C.c_void_p(lg.data_ptr()) if logits else None, self.cfg["vocab"],
+                                      C.c_void_p(greedy.data_ptr()), _stream(stream)), "sg_forward_batch")
+        return lg, greedy
 
     def generate(self, prompt, n_new):
         """Greedy decode: feed the prompt, then n_new tokens; returns the new tokens."""
