@@ -883,6 +883,10 @@ def run_gpu_decode(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     name = args.model
     cfg = dict(DECODE_MODELS[name], max_seq=PROMPT + args.warmup + args.steps + 8)
+    if args.profile:
+        # profiling case: the model's first two layers, the state set straight to
+        # position PROMPT (no prompt pass), then the captured step replayed
+        cfg["n_layers"] = 2
     dtypes = qwen3_dtypes(cfg, embed=Q4_K)
     W = random_weights(cfg, dtypes, dev, seed=5000 + rank)
     host = None
@@ -893,6 +897,23 @@ def run_gpu_decode(args):
     dec = Decoder(cfg, W, dtypes, dev)
     del W
     torch.cuda.synchronize()
+    if args.profile:
+        dec.set_state(5, PROMPT)
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            dec.step(stream=s, hidden=False, logits=False)
+            dec.set_state(5, PROMPT)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                dec.step(stream=s, hidden=False, logits=False)
+            for _ in range(args.warmup + args.steps):
+                graph.replay()
+            torch.cuda.synchronize()
+        sg.device_status()
+        if rank == 0:
+            print(json.dumps({"profile": True, "workload": "decode_%s_2_layers" % name, "pos": PROMPT}), flush=True)
+        return None, None, cfg, dtypes
     g = torch.Generator().manual_seed(77 + rank)
     prompt = torch.randint(0, cfg["vocab"], (PROMPT,), generator=g).tolist()
     for i, t in enumerate(prompt):
