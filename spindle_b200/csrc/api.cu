@@ -1174,8 +1174,14 @@ sg_status sg_moe_pack_down(int32_t dtype, const uint8_t *d_down_exps, uint64_t n
 
 uint64_t sg_moe_scratch_bytes(const sg_moe *m) { return check_moe(m) ? 0 : moe_scratch(m).total; }
 
-sg_status sg_moe_forward(const sg_moe *m, const float *d_x, float *d_out, void *d_scratch, uint64_t scratch_bytes,
-                         sg_moe_choice *d_choice, float *d_probs, void *stream) {
+}  // extern "C"
+
+namespace {
+
+// moe_forward; with `defer` set, the combine is not launched: its arguments
+// are returned there for the kernel that consumes the layer's output.
+sg_status moe_forward_impl(const sg_moe *m, const float *d_x, float *d_out, void *d_scratch, uint64_t scratch_bytes,
+                           sg_moe_choice *d_choice, float *d_probs, void *stream, CombineArgs *defer) {
     sg_status st = check_moe(m);
     if (st) return st;
     if (!d_x || !d_out || !d_scratch) return SG_ERR_INVALID;
@@ -1219,8 +1225,21 @@ sg_status sg_moe_forward(const sg_moe *m, const float *d_x, float *d_out, void *
     c.out = d_out;
     c.dim = (uint32_t)m->dim;
     c.max_slots = k;
+    if (defer) {
+        *defer = c;
+        return SG_OK;
+    }
     CK(launch_pdl((const void *)moe_combine_kernel, (uint32_t)((m->dim + 255) / 256), 256, 0, s, &c));
     return SG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+sg_status sg_moe_forward(const sg_moe *m, const float *d_x, float *d_out, void *d_scratch, uint64_t scratch_bytes,
+                         sg_moe_choice *d_choice, float *d_probs, void *stream) {
+    return moe_forward_impl(m, d_x, d_out, d_scratch, scratch_bytes, d_choice, d_probs, stream, nullptr);
 }
 
 uint64_t sg_moe_batch_scratch_bytes(const sg_moe *m, uint64_t n_tok) {
@@ -1631,11 +1650,29 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
 
     EmbedArgs ea = {m->embed, m->embed_dtype, dim, m->vocab, m->embedding_scale, d_state, x};
     CK(launch_pdl((const void *)embed_kernel, (dim + 255) / 256, 256, 0, s, &ea));
+    // an MoE layer's combine runs inside the norm that consumes its output
+    CombineArgs comb;
+    bool deferred = false;
+    auto norm_after_ffn = [&](const float *w) {
+        NormArgs a = {x, deferred ? nullptr : proj, m->residual_scale, w, m->rms_eps, dim, xn, qx};
+        if (deferred) {
+            a.csel = comb.sel;
+            a.cy = comb.y;
+            a.cysh = comb.ysh;
+            a.cscale = comb.shared_scale;
+            a.cmax_slots = comb.max_slots;
+        }
+        deferred = false;
+        return launch_pdl((const void *)rmsnorm_kernel, 1, NORM_THREADS, dim * 4, s, &a);
+    };
     for (uint32_t l = 0; l < m->n_layers; l++) {
         const sg_layer &y = m->layers[l];
         // attention: norm (+ the previous layer's FFN residual), Q/K/V, head norms, RoPE, KV, attention
-        if ((st = launch_norm(x, l ? proj : nullptr, m->residual_scale, y.attn_norm, m->rms_eps, dim, xn, qx, s)))
+        if (l) {
+            CK(norm_after_ffn(y.attn_norm));
+        } else if ((st = launch_norm(x, nullptr, m->residual_scale, y.attn_norm, m->rms_eps, dim, xn, qx, s))) {
             return st;
+        }
         // wk stored right after wq in the same format: one launch computes q and k (k follows q in scratch)
         uint64_t wq_bytes = 0;
         const bool qk_one = y.wk_dtype == y.wq_dtype && !sg_tiled16_bytes(y.wq_dtype, q_dim, dim, &wq_bytes) &&
@@ -1659,7 +1696,9 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
         // feed-forward: norm (+ attention residual), then the dense SwiGLU or the MoE layer
         if ((st = launch_norm(x, proj, m->residual_scale, y.ffn_norm, m->rms_eps, dim, xn, qx, s))) return st;
         if (y.is_moe) {
-            if ((st = sg_moe_forward(&y.moe, xn, proj, sc + L.moe, L.moe_bytes, nullptr, nullptr, stream))) return st;
+            if ((st = moe_forward_impl(&y.moe, xn, proj, sc + L.moe, L.moe_bytes, nullptr, nullptr, stream, &comb)))
+                return st;
+            deferred = true;
         } else {
             if ((st = launch_moe_group(y.ffn_gate_up_dtype, IN_MOE_X, y.ffn_gate_up, 0, 2 * y.n_ff, dim, 1, 1, sel1,
                                        nullptr, xn, qx, nullptr, 0, h, 0, s)) ||
@@ -1669,7 +1708,7 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
         }
     }
     // output norm (+ the last FFN residual), LM head, greedy token
-    if ((st = launch_norm(x, proj, m->residual_scale, m->output_norm, m->rms_eps, dim, xn, qx, s))) return st;
+    CK(norm_after_ffn(m->output_norm));
     if (d_hidden) CK(cudaMemcpyAsync(d_hidden, xn, dim * 4, cudaMemcpyDeviceToDevice, s));
     if ((st = gemv_image(m->lm_head, m->lm_head_dtype, m->vocab, dim, qx, logits, s))) return st;
     ArgmaxArgs ga = {logits, m->vocab, d_state, d_token, (unsigned long long *)(sc + L.amax),

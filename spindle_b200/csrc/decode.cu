@@ -84,16 +84,28 @@ __device__ float seq_sum_squares(const float *xs, uint32_t n) {
     return s;
 }
 
-// One CTA.  Each thread keeps up to 8 of the n values in registers; the sum of
-// squares is the reference's sequential one, so xn (and its Q8_K image) are
-// the reference's bits.
+// One CTA per token; warp w holds 256-block w of the n values (lane l: values
+// 8l..8l+7), so that the block's Q8_K image is made from registers.  The norm
+// weights do not depend on the kernel before and are loaded before waiting for
+// it.  The sum of squares is the reference's sequential one (thread 0), so xn
+// and its Q8_K image are the reference's bits.
 __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const __grid_constant__ NormArgs a) {
     __shared__ float inv_s;
-    extern __shared__ __align__(16) float xs[];  // x, then the normed vector for the Q8_K image
+    __shared__ float cw[MOE_MAXK];
+    __shared__ uint32_t cn_s;
+    extern __shared__ __align__(16) float xs[];  // x in element order, for the sequential sum
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, nb = a.n / 256;
+    const bool bad = a.n % 256 || nb * 32 > blockDim.x || a.n * 4 > dynamic_smem_size() || (a.csel && gridDim.x != 1);
+    const bool mine = !bad && warp < nb;
+    const uint32_t i0 = 256u * warp + 8u * lane;
+    float wv[8];
+    if (mine) {
+        const float4 w0 = reinterpret_cast<const float4 *>(a.w + i0)[0], w1 = reinterpret_cast<const float4 *>(a.w + i0)[1];
+        wv[0] = w0.x, wv[1] = w0.y, wv[2] = w0.z, wv[3] = w0.w, wv[4] = w1.x, wv[5] = w1.y, wv[6] = w1.z, wv[7] = w1.w;
+    }
     grid_dependency_wait();
     grid_launch_dependents();
-    constexpr int PER = 8;
-    if (a.n > PER * blockDim.x || a.n % 4 || a.n * 4 > dynamic_smem_size() || (a.qx && a.n % 256)) {
+    if (bad) {
         if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
         return;
     }
@@ -101,21 +113,47 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const __grid_cons
     const uint64_t to = (uint64_t)blockIdx.x * a.n;
     float *const X = a.x + to, *const XN = a.xn + to;
     const float *const ADD = a.add ? a.add + to : nullptr;
-    uint8_t *const QX = a.qx ? a.qx + (uint64_t)blockIdx.x * act_bytes(a.n / 256) : nullptr;
-    float v[PER];
-#pragma unroll
-    for (int j = 0; j < PER; j++) {
-        const uint32_t i = threadIdx.x + j * blockDim.x;
-        v[j] = 0.0f;
-        if (i < a.n) {
-            float x = X[i];
+    uint8_t *const QX = a.qx ? a.qx + (uint64_t)blockIdx.x * act_bytes(nb) : nullptr;
+    if (a.csel) {
+        if (threadIdx.x < MOE_MAXK) cw[threadIdx.x] = a.csel->weight[threadIdx.x];
+        if (threadIdx.x == 0) cn_s = min(a.csel->n, a.cmax_slots);
+        __syncthreads();
+    }
+    float v[8];
+    if (mine) {
+        const float4 p0 = reinterpret_cast<const float4 *>(X + i0)[0], p1 = reinterpret_cast<const float4 *>(X + i0)[1];
+        v[0] = p0.x, v[1] = p0.y, v[2] = p0.z, v[3] = p0.w, v[4] = p1.x, v[5] = p1.y, v[6] = p1.z, v[7] = p1.w;
+        if (ADD || a.csel) {
+            float ad[8];
             if (ADD) {
-                x = __fadd_rn(x, __fmul_rn(a.rs, ADD[i]));
-                X[i] = x;
+                const float4 q0 = reinterpret_cast<const float4 *>(ADD + i0)[0], q1 = reinterpret_cast<const float4 *>(ADD + i0)[1];
+                ad[0] = q0.x, ad[1] = q0.y, ad[2] = q0.z, ad[3] = q0.w, ad[4] = q1.x, ad[5] = q1.y, ad[6] = q1.z, ad[7] = q1.w;
+            } else {
+                // ffns_fused on a zeroed output: 0 + w_0*y_0 + w_1*y_1 + ... (smollm_chat.rs:431-438),
+                // then the shared expert's g * (0 + 1 * ysh) (:1370-1382)
+#pragma unroll
+                for (int j = 0; j < 8; j++) ad[j] = 0.0f;
+                for (uint32_t q = 0; q < cn_s; q++) {
+                    const float4 y0 = reinterpret_cast<const float4 *>(a.cy + (uint64_t)q * a.n + i0)[0];
+                    const float4 y1 = reinterpret_cast<const float4 *>(a.cy + (uint64_t)q * a.n + i0)[1];
+                    const float yv[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
+#pragma unroll
+                    for (int j = 0; j < 8; j++) ad[j] = __fadd_rn(ad[j], __fmul_rn(cw[q], yv[j]));
+                }
+                if (a.cysh) {
+                    const float g = *a.cscale;
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        ad[j] = __fadd_rn(ad[j], __fmul_rn(g, __fadd_rn(0.0f, __fmul_rn(1.0f, a.cysh[i0 + j]))));
+                }
             }
-            v[j] = x;
-            xs[i] = x;
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = __fadd_rn(v[j], __fmul_rn(a.rs, ad[j]));
+            reinterpret_cast<float4 *>(X + i0)[0] = make_float4(v[0], v[1], v[2], v[3]);
+            reinterpret_cast<float4 *>(X + i0)[1] = make_float4(v[4], v[5], v[6], v[7]);
         }
+        reinterpret_cast<float4 *>(xs + i0)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4 *>(xs + i0)[1] = make_float4(v[4], v[5], v[6], v[7]);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -123,23 +161,17 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const __grid_cons
         inv_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.n), a.eps)));
     }
     __syncthreads();
-    const float inv = inv_s;
+    if (mine) {
+        const float inv = inv_s;
+        float y[8];
 #pragma unroll
-    for (int j = 0; j < PER; j++) {
-        const uint32_t i = threadIdx.x + j * blockDim.x;
-        if (i < a.n) {
-            const float y = __fmul_rn(__fmul_rn(v[j], inv), a.w[i]);
-            XN[i] = y;
-            if (QX) xs[i] = y;
-        }
-    }
-    if (QX) {
-        __syncthreads();
-        const uint32_t nb = a.n / 256, warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-        for (uint32_t b = warp; b < nb; b += blockDim.x / 32)
-            q8k_block(xs + 256u * b, reinterpret_cast<int8_t *>(QX + 256u * b),
-                      reinterpret_cast<int16_t *>(QX + 256u * nb + 32u * b),
-                      reinterpret_cast<float *>(QX + 288u * nb + 4u * b), lane);
+        for (int j = 0; j < 8; j++) y[j] = __fmul_rn(__fmul_rn(v[j], inv), wv[j]);
+        reinterpret_cast<float4 *>(XN + i0)[0] = make_float4(y[0], y[1], y[2], y[3]);
+        reinterpret_cast<float4 *>(XN + i0)[1] = make_float4(y[4], y[5], y[6], y[7]);
+        if (QX)
+            q8k_block_regs(y, reinterpret_cast<int8_t *>(QX + 256u * warp),
+                           reinterpret_cast<int16_t *>(QX + 256u * nb + 32u * warp),
+                           reinterpret_cast<float *>(QX + 288u * nb + 4u * warp), lane);
     }
 }
 

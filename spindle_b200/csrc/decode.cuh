@@ -50,6 +50,14 @@ struct NormArgs {
     float *xn;
     uint8_t *qx;
     // batch: CTA t normalizes token t (x, add, xn at + t * n; qx at + t * act_bytes(n / 256))
+    // Optional, one token: add is the combine of the MoE layer before, made
+    // here with moe_combine_kernel's arithmetic (sum over csel's slots of
+    // w_i * cy_i[r] in router order, then + cscale * cysh[r]).
+    const sg_moe_choice *csel;
+    const float *cy;            // slot s at cy + s * n
+    const float *cysh;          // shared expert output, or null
+    const float *cscale;
+    uint32_t cmax_slots;
 };
 
 // Batch: this position's QK-norm, RoPE and f16 K/V rows of token blockIdx.y
