@@ -323,6 +323,31 @@ SG_API sg_status sg_moe_forward_batch(const sg_moe *m, const float *d_x, uint64_
                                       uint64_t ldo, void *d_scratch, uint64_t scratch_bytes,
                                       sg_moe_choice *d_choices, void *stream);
 
+/* Expert parallelism for the batched layer (SURVEY: experts shard across
+ * GPUs, the router stays replicated): rank p keeps experts [expert_lo,
+ * expert_hi) -- m->gate_up / m->down hold only those, packed as usual, while
+ * m->router and m->n_expert stay whole -- and computes the choices of every
+ * token (identically on every rank) but only the slots whose expert it owns.
+ * The down pass stores each of those slot outputs, tagged with the call's
+ * epoch, straight into every rank's receive buffer at the slot's place (8-byte
+ * peer stores over NVLink, the protocol of sg_matvec_tp), and every rank's
+ * combine sums all slots of a token in router order as they arrive: bit for
+ * bit the one-GPU result.  Set-up per rank: a zeroed comm block
+ * (sg_tp_comm_bytes, sg_tp_comm_init) and a zeroed receive buffer of
+ * sg_moe_ep_recv_bytes(m, n_tok_max) bytes shared through sg_ipc_get_handle /
+ * sg_ipc_open; every rank makes the same sequence of calls. */
+typedef struct {
+    uint32_t n_ranks, rank;
+    uint64_t expert_lo, expert_hi;
+    uint64_t recv_slots;                /* n_tok_max * n_used: the receive buffers' slots per half */
+    void *recv[SG_TP_MAX_RANKS];        /* every rank's receive buffer (this rank's own at [rank]) */
+    void *comm;                         /* this rank's comm block */
+} sg_moe_ep;
+SG_API uint64_t sg_moe_ep_recv_bytes(const sg_moe *m, uint64_t n_tok_max);
+SG_API sg_status sg_moe_forward_batch_ep(const sg_moe *m, const sg_moe_ep *ep, const float *d_x, uint64_t ldx,
+                                         uint64_t n_tok, float *d_out, uint64_t ldo, void *d_scratch,
+                                         uint64_t scratch_bytes, sg_moe_choice *d_choices, void *stream);
+
 /* ---- Decoder step (forward_slice, smollm_chat.rs:3371-3552, with greedy
  * sampling, :3565-3602 and :3661-3671) -----------------------------------------
  *

@@ -58,6 +58,11 @@ class SgTpGroup(C.Structure):
                 ("comm", C.c_void_p)]
 
 
+class SgMoeEp(C.Structure):
+    _fields_ = [("n_ranks", C.c_uint32), ("rank", C.c_uint32), ("expert_lo", C.c_uint64), ("expert_hi", C.c_uint64),
+                ("recv_slots", C.c_uint64), ("recv", C.c_void_p * TP_MAX_RANKS), ("comm", C.c_void_p)]
+
+
 P, U64, I32 = C.c_void_p, C.c_uint64, C.c_int32
 
 # name -> (restype, argtypes); every function the header declares.
@@ -104,6 +109,8 @@ SIGNATURES = {
     "sg_moe_forward": (I32, [C.POINTER(SgMoe), P, P, P, U64, P, P, P]),
     "sg_moe_batch_scratch_bytes": (U64, [C.POINTER(SgMoe), U64]),
     "sg_moe_forward_batch": (I32, [C.POINTER(SgMoe), P, U64, U64, P, U64, P, U64, P, P]),
+    "sg_moe_ep_recv_bytes": (U64, [C.POINTER(SgMoe), U64]),
+    "sg_moe_forward_batch_ep": (I32, [C.POINTER(SgMoe), C.POINTER(SgMoeEp), P, U64, U64, P, U64, P, U64, P, P]),
     "sg_model_scratch_bytes": (U64, [P]),
     "sg_model_kv_bytes": (U64, [P]),
     "sg_model_prepare": (I32, [P, P, U64, P]),

@@ -570,7 +570,8 @@ MoeScratch moe_scratch(const sg_moe *m) {
 
 // Scratch of the batched layer (moe_forward_batch) for n_tok tokens.
 struct MoeBatchScratch {
-    uint64_t choices, slot_base, slots, n_slots, slots_sh, n_slots_sh, shsel, scale, logits, qx, h, y, hsh, ysh, total;
+    uint64_t choices, slot_base, slots, n_slots, slots_sh, n_slots_sh, shsel, scale, logits, qx, h, y, hsh, ysh;
+    uint64_t slots_local, slot_global, n_local, total;
 };
 
 MoeBatchScratch moe_batch_scratch(const sg_moe *m, uint64_t n_tok) {
@@ -597,6 +598,9 @@ MoeBatchScratch moe_batch_scratch(const sg_moe *m, uint64_t n_tok) {
     L.y = take(slots * m->dim * 4);
     L.hsh = take(sh ? n_tok * m->shared_n_ff * 4 : 0);
     L.ysh = take(sh ? n_tok * m->dim * 4 : 0);
+    L.slots_local = take(slots * 8);  // expert parallelism: this rank's slots
+    L.slot_global = take(slots * 4);
+    L.n_local = take(4);
     L.total = off;
     return L;
 }
@@ -618,6 +622,12 @@ struct MoeSlots {
     const int32_t *slots;
     const uint32_t *n_slots;
     const uint8_t *qx_tokens;  // IN_MOE_X: the tokens' Q8_K images
+    // IN_MOE_H with expert parallelism: slot outputs to every rank (see TGemvArgs)
+    uint32_t npeers;
+    const uint32_t *slot_global;
+    unsigned long long *recv[TP_MAX_RANKS];
+    uint64_t ep_half;
+    unsigned *epoch;
 };
 
 sg_status launch_moe_group(int32_t dtype, int mode, const uint8_t *w, uint64_t mat_stride, uint64_t rows,
@@ -672,6 +682,13 @@ sg_status launch_moe_group(int32_t dtype, int mode, const uint8_t *w, uint64_t m
         a.qx_tokens = slots->qx_tokens;
         a.sel = nullptr;
         a.qx_image = nullptr;
+        if (slots->npeers) {
+            a.npeers = slots->npeers;
+            a.slot_global = slots->slot_global;
+            for (uint32_t q = 0; q < slots->npeers; q++) a.peer_recv[q] = slots->recv[q];
+            a.ep_half = slots->ep_half;
+            a.epoch = slots->epoch;
+        }
     }
     CK(launch_pdl((const void *)p.fn, p.grid, p.warps * 32, p.smem, stream, &a));
     return SG_OK;
@@ -1247,9 +1264,15 @@ uint64_t sg_moe_batch_scratch_bytes(const sg_moe *m, uint64_t n_tok) {
     return moe_batch_scratch(m, n_tok).total;
 }
 
-sg_status sg_moe_forward_batch(const sg_moe *m, const float *d_x, uint64_t ldx, uint64_t n_tok, float *d_out,
-                               uint64_t ldo, void *d_scratch, uint64_t scratch_bytes, sg_moe_choice *d_choices,
-                               void *stream) {
+}  // extern "C"
+
+namespace {
+
+// moe_forward_batch, on one GPU (ep null) or with this rank's experts only
+// (expert parallelism: slot outputs exchanged through the ranks' receive buffers).
+sg_status moe_batch_impl(const sg_moe *m, const sg_moe_ep *ep, const float *d_x, uint64_t ldx, uint64_t n_tok,
+                         float *d_out, uint64_t ldo, void *d_scratch, uint64_t scratch_bytes, sg_moe_choice *d_choices,
+                         void *stream) {
     sg_status st = check_moe(m);
     if (st) return st;
     if (n_tok == 0) return SG_OK;
@@ -1258,6 +1281,14 @@ sg_status sg_moe_forward_batch(const sg_moe *m, const float *d_x, uint64_t ldx, 
     if (!aligned(d_x, 16) || (n_tok > 1 && ldx % 4) || !aligned(d_out, 4) || !aligned(d_scratch, 256) ||
         !aligned(d_choices, 16))
         return SG_ERR_ALIGN;
+    if (ep) {
+        if (!ep->n_ranks || ep->n_ranks > SG_TP_MAX_RANKS || ep->rank >= ep->n_ranks || !ep->comm ||
+            ep->expert_lo > ep->expert_hi || ep->expert_hi > m->n_expert || n_tok * m->n_used > ep->recv_slots)
+            return SG_ERR_INVALID;
+        for (uint32_t q = 0; q < ep->n_ranks; q++)
+            if (!ep->recv[q] || !aligned(ep->recv[q], 8)) return SG_ERR_INVALID;
+        if (!aligned(ep->comm, 256)) return SG_ERR_ALIGN;
+    }
     const MoeBatchScratch L = moe_batch_scratch(m, n_tok);
     if (scratch_bytes < L.total) return SG_ERR_INVALID;
     cudaStream_t s = (cudaStream_t)stream;
@@ -1271,8 +1302,11 @@ sg_status sg_moe_forward_batch(const sg_moe *m, const float *d_x, uint64_t ldx, 
     uint8_t *qx = sc + L.qx;
     const bool sh = m->shared_gate_up != nullptr;
     const uint32_t k = (uint32_t)m->n_used, ne = (uint32_t)m->n_expert, nt = (uint32_t)n_tok;
+    int32_t *slots_local = (int32_t *)(sc + L.slots_local);
+    uint32_t *slot_global = (uint32_t *)(sc + L.slot_global), *n_local = (uint32_t *)(sc + L.n_local);
     // router (every token) -> choices and slot table -> gate/up over all slots
-    // -> down -> [shared gate/up, down over one slot per token] -> combine
+    // (this rank's, with expert parallelism) -> down -> [shared gate/up, down
+    // over one slot per token] -> combine
     if ((st = launch_router(m, d_x, logits, qx, (sg_moe_choice *)(sc + L.shsel), scale, s, nt, ldx))) return st;
     {
         static std::atomic<uint64_t> attr_done{0};
@@ -1284,15 +1318,35 @@ sg_status sg_moe_forward_batch(const sg_moe *m, const float *d_x, uint64_t ldx, 
             attr_done.fetch_or(1ull << dev);
         }
         SelectBatchArgs sa = {logits, nt, ne, k, m->norm, m->moe_prune, choices, slot_base, slots, n_slots,
-                              sh ? slots_sh : nullptr, sh ? n_slots_sh : nullptr};
+                              sh ? slots_sh : nullptr, sh ? n_slots_sh : nullptr,
+                              ep ? slots_local : nullptr, slot_global, n_local,
+                              ep ? (uint32_t)ep->expert_lo : 0u, ep ? (uint32_t)ep->expert_hi : 0u};
         CK(launch_pdl((const void *)moe_select_batch_kernel, 1, SELECT_BATCH_THREADS, select_batch_smem(nt), s, &sa));
     }
-    const MoeSlots ms = {slots, n_slots, qx};
-    if ((st = launch_moe_group(m->gate_up_dtype, IN_MOE_X, m->gate_up, m->gate_up_stride, 2 * m->n_ff, m->dim, nt * k,
-                               ne, nullptr, nullptr, nullptr, nullptr, nullptr, 0, h, m->n_ff, s, &ms)) ||
-        (st = launch_moe_group(m->down_dtype, IN_MOE_H, m->down, m->down_stride, m->dim, m->n_ff, nt * k, ne,
-                               nullptr, nullptr, nullptr, nullptr, h, m->n_ff, y, m->dim, s, &ms)))
-        return st;
+    const uint32_t ne_run = ep ? (uint32_t)(ep->expert_hi - ep->expert_lo) : ne;
+    MoeSlots ms;
+    memset(&ms, 0, sizeof ms);
+    ms.slots = ep ? slots_local : slots;
+    ms.n_slots = ep ? n_local : n_slots;
+    ms.qx_tokens = qx;
+    MoeSlots md = ms;
+    unsigned *ep_epoch = ep ? (unsigned *)((uint8_t *)ep->comm + 128) : nullptr;
+    if (ep) {
+        md.npeers = ep->n_ranks;
+        md.slot_global = slot_global;
+        for (uint32_t q = 0; q < ep->n_ranks; q++) md.recv[q] = (unsigned long long *)ep->recv[q];
+        md.ep_half = ep->recv_slots * m->dim;
+        md.epoch = ep_epoch;
+    }
+    if (!ep || ne_run > 0) {
+        if ((st = launch_moe_group(m->gate_up_dtype, IN_MOE_X, m->gate_up, m->gate_up_stride, 2 * m->n_ff, m->dim,
+                                   nt * k, ne_run ? ne_run : 1, nullptr, nullptr, nullptr, nullptr, nullptr, 0, h,
+                                   m->n_ff, s, &ms)) ||
+            (st = launch_moe_group(m->down_dtype, IN_MOE_H, m->down, m->down_stride, m->dim, m->n_ff, nt * k,
+                                   ne_run ? ne_run : 1, nullptr, nullptr, nullptr, nullptr, h, m->n_ff, y, m->dim, s,
+                                   &md)))
+            return st;
+    }
     if (sh) {
         const MoeSlots mss = {slots_sh, n_slots_sh, qx};
         if ((st = launch_moe_group(m->shared_gate_up_dtype, IN_MOE_X, m->shared_gate_up, 0, 2 * m->shared_n_ff,
@@ -1302,10 +1356,47 @@ sg_status sg_moe_forward_batch(const sg_moe *m, const float *d_x, uint64_t ldx, 
                                    nullptr, nullptr, nullptr, nullptr, hsh, m->shared_n_ff, ysh, m->dim, s, &mss)))
             return st;
     }
-    CombineBatchArgs c = {choices, slot_base, y, sh ? ysh : nullptr, scale, d_out, n_tok > 1 ? ldo : m->dim,
-                          (uint32_t)m->dim, k};
+    CombineBatchArgs c;
+    memset(&c, 0, sizeof c);
+    c.choices = choices;
+    c.slot_base = slot_base;
+    c.y = y;
+    c.ysh = sh ? ysh : nullptr;
+    c.shared_scale = scale;
+    c.out = d_out;
+    c.ldo = n_tok > 1 ? ldo : m->dim;
+    c.dim = (uint32_t)m->dim;
+    c.n_used = k;
+    if (ep) {
+        c.recv = (const unsigned long long *)ep->recv[ep->rank];
+        c.half = ep->recv_slots * m->dim;
+        c.ticket = (unsigned *)((uint8_t *)ep->comm + 64);
+        c.epoch = ep_epoch;
+    }
     CK(launch_pdl((const void *)moe_combine_batch_kernel, dim3((uint32_t)((m->dim + 255) / 256), nt), 256, 0, s, &c));
     return SG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+sg_status sg_moe_forward_batch(const sg_moe *m, const float *d_x, uint64_t ldx, uint64_t n_tok, float *d_out,
+                               uint64_t ldo, void *d_scratch, uint64_t scratch_bytes, sg_moe_choice *d_choices,
+                               void *stream) {
+    return moe_batch_impl(m, nullptr, d_x, ldx, n_tok, d_out, ldo, d_scratch, scratch_bytes, d_choices, stream);
+}
+
+uint64_t sg_moe_ep_recv_bytes(const sg_moe *m, uint64_t n_tok_max) {
+    if (check_moe(m) || n_tok_max == 0 || n_tok_max > SG_MOE_MAX_BATCH) return 0;
+    return 2ull * 8ull * n_tok_max * m->n_used * m->dim;
+}
+
+sg_status sg_moe_forward_batch_ep(const sg_moe *m, const sg_moe_ep *ep, const float *d_x, uint64_t ldx,
+                                  uint64_t n_tok, float *d_out, uint64_t ldo, void *d_scratch, uint64_t scratch_bytes,
+                                  sg_moe_choice *d_choices, void *stream) {
+    if (!ep) return SG_ERR_INVALID;
+    return moe_batch_impl(m, ep, d_x, ldx, n_tok, d_out, ldo, d_scratch, scratch_bytes, d_choices, stream);
 }
 
 }  // extern "C"

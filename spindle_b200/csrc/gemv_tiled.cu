@@ -61,7 +61,8 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
         (MOE && a.swiglu && (MODE != IN_MOE_X || a.nvec != 1)) ||
         (MOE && ((!a.slots && a.max_slots > MOE_MAXK) || a.tiles_per_mat == 0 || nact == 0 ||
                  (uint64_t)a.ntiles * gridDim.x >= (1ull << 32) || a.ntiles < a.max_slots * a.tiles_per_mat)) ||
-        (a.npeers && (MOE || a.npeers > TP_MAX_RANKS || !a.ticket || !a.epoch || !a.out[0] || !a.my_recv)) ||
+        (a.npeers && !MOE && (a.npeers > TP_MAX_RANKS || !a.ticket || !a.epoch || !a.out[0] || !a.my_recv)) ||
+        (a.npeers && MOE && (MODE != IN_MOE_H || a.npeers > TP_MAX_RANKS || !a.slots || !a.slot_global || !a.epoch)) ||
         (a.slots && (!MOE || !a.n_slots || a.logits || nact > MOE_MAXK || (MODE == IN_MOE_X && !a.qx_tokens))) ||
         (MODE == IN_MOE_X && a.logits &&
          (a.n_expert == 0 || a.n_used == 0 || a.n_used > a.n_expert || a.n_used > MOE_MAXK ||
@@ -247,7 +248,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     }
     // The activations do: wait for the grid that wrote them, then stage them.
     grid_dependency_wait();
-    const uint32_t tp_e = (!MOE && a.npeers) ? *a.epoch + 1u : 0u;  // this call's epoch (row split)
+    const uint32_t tp_e = a.npeers ? *a.epoch + 1u : 0u;  // this call's epoch (row split, expert parallelism)
     const uint32_t nb = a.nb;
     bool failed = false;
     if constexpr (MODE == IN_MOE_H) {
@@ -441,7 +442,17 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                 for (int m = 0; m < 4; m++) x[m] = __fadd_rn(acc[v][m], __shfl_down_sync(0xffffffffu, acc[v][m], 16));
                 const float yv = __fsub_rn(__fadd_rn(__fadd_rn(x[0], x[2]), __fadd_rn(x[1], x[3])), corr[v]);
                 float *dst = MOE ? a.out[0] + ms * a.out_stride : a.out[v];
-                if (MODE == IN_MOE_X && a.swiglu) {
+                if (MODE == IN_MOE_H && a.npeers) {
+                    // this rank's expert output goes to every rank's receive buffer (NVLink peer stores)
+                    if (g == 0 && row >= a.r0 && row < a.r1) {
+                        const uint64_t o = (uint64_t)(tp_e & 1u) * a.ep_half +
+                                           (uint64_t)__ldcg(a.slot_global + ms) * a.out_stride + row;
+                        const unsigned long long pr = ((unsigned long long)tp_e << 32) | __float_as_uint(yv);
+                        for (uint32_t p = 0; p < a.npeers; p++)
+                            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a.peer_recv[p] + o), "l"(pr)
+                                         : "memory");
+                    }
+                } else if (MODE == IN_MOE_X && a.swiglu) {
                     // rows r < 8 are gate rows, rows r + 8 the up rows of the
                     // same outputs: h = silu(gate) * up (smollm_chat.rs:357-359)
                     const float up = __shfl_down_sync(0xffffffffu, yv, 8);

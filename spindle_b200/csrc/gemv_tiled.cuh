@@ -107,6 +107,11 @@ struct TGemvArgs {
     const int32_t *slots;
     const uint32_t *n_slots;
     const uint8_t *qx_tokens;
+    // expert parallelism (IN_MOE_H with slots, npeers > 0): row r of local
+    // slot j goes as the pair (epoch << 32 | value) to peer_recv[p][(e & 1) *
+    // ep_half + slot_global[j] * out_stride + r] on every rank, e = *epoch + 1
+    const uint32_t *slot_global;
+    uint64_t ep_half;
     // Row-split tensor parallelism (IN_Q8K / IN_F32, npeers > 0).  The call's
     // epoch e is *epoch + 1.  Row r of vector v is stored as the pair
     // (e << 32 | value bits) at peer_recv[p][h*nvec*tp_rows + v*tp_rows +

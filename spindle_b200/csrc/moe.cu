@@ -184,6 +184,20 @@ __global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(
             base += n;
         }
         *a.n_slots = base;
+        if (a.slots_local) {
+            // this rank's slots (expert parallelism), in global slot order
+            uint32_t j = 0;
+            for (uint32_t q = 0; q < base; q++) {
+                const int32_t e = a.slots[2 * q];
+                if ((uint32_t)e >= a.ep_lo && (uint32_t)e < a.ep_hi) {
+                    a.slots_local[2 * j] = e - (int32_t)a.ep_lo;
+                    a.slots_local[2 * j + 1] = a.slots[2 * q + 1];
+                    a.slot_global[j] = q;
+                    j++;
+                }
+            }
+            *a.n_local = j;
+        }
         if (a.slots_sh) {
             for (uint32_t t = 0; t < a.n_tok; t++) {
                 a.slots_sh[2 * t] = 0;
@@ -210,15 +224,49 @@ __global__ void moe_combine_batch_kernel(const __grid_constant__ CombineBatchArg
     }
     __syncthreads();
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= a.dim) return;
-    float acc = 0.0f;
-    for (uint32_t i = 0; i < n_s; i++)
-        acc = __fadd_rn(acc, __fmul_rn(w[i], a.y[(uint64_t)(base_s + i) * a.dim + r]));
-    if (a.ysh) {
-        const float tmp = __fadd_rn(0.0f, __fmul_rn(1.0f, a.ysh[(uint64_t)t * a.dim + r]));
-        acc = __fadd_rn(acc, __fmul_rn(a.shared_scale[t], tmp));
+    const uint32_t e = a.recv ? *a.epoch + 1u : 0u;
+    if (r < a.dim) {
+        float acc = 0.0f;
+        for (uint32_t i = 0; i < n_s; i++) {
+            float yv;
+            if (a.recv) {
+                // slot outputs of every rank's experts, each as soon as it carries this call's epoch
+                const unsigned long long *src = a.recv + (uint64_t)(e & 1u) * a.half + (uint64_t)(base_s + i) * a.dim + r;
+                unsigned long long p;
+                uint64_t t0 = 0;
+                for (;;) {
+                    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(p) : "l"(src) : "memory");
+                    if ((uint32_t)(p >> 32) == e) break;
+                    const uint64_t tn = globaltimer_ns();
+                    if (t0 == 0) {
+                        t0 = tn;
+                    } else if (tn - t0 > WAIT_LIMIT_NS) {
+                        atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_PEER);
+                        p = 0x7fc00000ull;
+                        break;
+                    }
+                    __nanosleep(32);
+                }
+                yv = __uint_as_float((uint32_t)p);
+            } else {
+                yv = a.y[(uint64_t)(base_s + i) * a.dim + r];
+            }
+            acc = __fadd_rn(acc, __fmul_rn(w[i], yv));
+        }
+        if (a.ysh) {
+            const float tmp = __fadd_rn(0.0f, __fmul_rn(1.0f, a.ysh[(uint64_t)t * a.dim + r]));
+            acc = __fadd_rn(acc, __fmul_rn(a.shared_scale[t], tmp));
+        }
+        a.out[(uint64_t)t * a.ldo + r] = acc;
     }
-    a.out[(uint64_t)t * a.ldo + r] = acc;
+    if (a.recv) {
+        __syncthreads();
+        const uint32_t nblocks = gridDim.x * gridDim.y;
+        if (threadIdx.x == 0 && atomicAdd(a.ticket, 1u) == nblocks - 1) {
+            *a.ticket = 0;  // every block of this launch has its ticket
+            *a.epoch = e;
+        }
+    }
 }
 
 }  // namespace sg

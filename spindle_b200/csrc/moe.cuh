@@ -52,6 +52,12 @@ struct SelectBatchArgs {
     uint32_t *n_slots;
     int32_t *slots_sh;          // shared expert: [n_tok][2] = (0, t), or null
     uint32_t *n_slots_sh;
+    // expert parallelism (slots_local set): the slots whose expert is in
+    // [ep_lo, ep_hi), as (expert - ep_lo, token), and their global slot indices
+    int32_t *slots_local;
+    uint32_t *slot_global;
+    uint32_t *n_local;
+    uint32_t ep_lo, ep_hi;
 };
 constexpr uint32_t SELECT_BATCH_THREADS = 1024;
 __host__ __device__ inline uint32_t select_batch_smem(uint32_t n_tok) {
@@ -67,6 +73,13 @@ struct CombineBatchArgs {
     float *out;                 // token t at out + t * ldo
     uint64_t ldo;
     uint32_t dim, n_used;
+    // expert parallelism (recv set): slot s row r arrives as the pair
+    // (epoch << 32 | value) at recv[(e & 1) * half + s * dim + r], e =
+    // *epoch + 1; the last CTA to finish stores e in *epoch
+    const unsigned long long *recv;
+    uint64_t half;
+    unsigned *ticket;
+    unsigned *epoch;
 };
 
 // bars (64) | x (dim floats) | rows (rows_per_cta, padded) ; the gate CTA puts

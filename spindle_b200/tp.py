@@ -152,3 +152,68 @@ def matvec_tp(shard, xs, grp, buf, stream=None):
                                   xs2.stride(0), xs2.shape[0], shard.r0, buf.rows, C.c_void_p(out.data_ptr()),
                                   out.stride(0), C.byref(g), _stream(stream)), "sg_matvec_tp")
     return out
+
+
+class EpMoe:
+    """This rank's part of an expert-parallel MoE layer (sg_moe_forward_batch_ep).
+
+    Rank p of P keeps experts [E*p/P, E*(p+1)/P) (par_rows's split over the
+    experts) and the whole router; every rank computes every token's choice,
+    runs the slots of its own experts, and their outputs reach every rank's
+    receive buffer over NVLink, where each rank's combine sums them in router
+    order: each rank ends with the whole layer output, bit for bit the one-GPU
+    result.  Build it on every rank, in the same order as the group's other
+    buffers (its set-up is collective)."""
+
+    def __init__(self, grp, router, gate_exps, up_exps, down_exps, gate_up_dtype, down_dtype, n_expert, n_used, dim,
+                 n_ff, n_tok_max=16, norm=True, moe_prune=0.0):
+        from . import Moe
+        self.grp, self.n_tok_max = grp, n_tok_max
+        self.lo, self.hi = shard_rows(n_expert, grp.n, grp.rank)
+        rg, rd = row_bytes(gate_up_dtype, dim), row_bytes(down_dtype, n_ff)
+        sl = lambda t, rb, rows: t[self.lo * rows * rb:self.hi * rows * rb]
+        n_loc = self.hi - self.lo
+        self.moe = Moe.pack(router, sl(gate_exps, rg, n_ff), sl(up_exps, rg, n_ff), sl(down_exps, rd, dim),
+                            gate_up_dtype, down_dtype, max(n_loc, 1), n_used, dim, n_ff, norm=norm,
+                            moe_prune=moe_prune) if n_loc else None
+        if self.moe is None:  # a rank without experts still takes part
+            self.moe = Moe.pack(router, gate_exps[:rg * n_ff], up_exps[:rg * n_ff], down_exps[:rd * dim],
+                                gate_up_dtype, down_dtype, 1, n_used, dim, n_ff, norm=norm, moe_prune=moe_prune)
+        self.moe.n_expert = n_expert  # the router and the choice span every expert
+        self.comm = grp._alloc(lib().sg_tp_comm_bytes())
+        _lib.check(lib().sg_tp_comm_init(C.c_void_p(self.comm), None), "sg_tp_comm_init")
+        nbytes = lib().sg_moe_ep_recv_bytes(C.byref(self.moe.c()), n_tok_max)
+        if not nbytes:
+            raise ValueError("sg_moe_ep_recv_bytes: unsupported layer or batch")
+        recv = grp._alloc(nbytes)
+        torch.as_tensor(_DeviceArray(recv, (nbytes // 4,), grp.device), device=grp.device).zero_()
+        torch.cuda.synchronize(grp.device)
+        self.recv = grp._share(recv)
+        self._scratch = {}
+
+    def c(self):
+        from ._lib import SgMoeEp
+        e = SgMoeEp()
+        e.n_ranks, e.rank = self.grp.n, self.grp.rank
+        e.expert_lo, e.expert_hi = self.lo, self.hi
+        e.recv_slots = self.n_tok_max * self.moe.n_used
+        for q in range(self.grp.n):
+            e.recv[q] = self.recv[q]
+        e.comm = self.comm
+        return e
+
+    def forward(self, xs, out=None, stream=None):
+        """out[t] = the layer on xs[t] (float32 CUDA [n_tok, dim]), on every rank."""
+        n_tok = xs.shape[0]
+        if out is None:
+            out = torch.empty(n_tok, self.moe.dim, dtype=torch.float32, device=xs.device)
+        sc = self._scratch.get(n_tok)
+        if sc is None:
+            nb = lib().sg_moe_batch_scratch_bytes(C.byref(self.moe.c()), n_tok)
+            sc = self._scratch[n_tok] = torch.empty(nb, dtype=torch.uint8, device=xs.device)
+        m, e = self.moe.c(), self.c()
+        _lib.check(lib().sg_moe_forward_batch_ep(C.byref(m), C.byref(e), C.c_void_p(xs.data_ptr()), xs.stride(0),
+                                                 n_tok, C.c_void_p(out.data_ptr()), out.stride(0),
+                                                 C.c_void_p(sc.data_ptr()), sc.numel(), None, _stream(stream)),
+                   "sg_moe_forward_batch_ep")
+        return out

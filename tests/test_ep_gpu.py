@@ -1,0 +1,45 @@
+"""Expert parallelism of the batched MoE layer (sg_moe_forward_batch_ep):
+each rank keeps a slice of the experts, the slot outputs travel to every rank
+over NVLink peer stores, and every rank's output equals the whole layer on
+one GPU bit for bit.  One rank runs on any GPU box; two ranks need two GPUs."""
+import os
+import socket
+import sys
+
+import pytest
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+import tp_util  # noqa: E402
+
+from spindle_b200.tp import TpGroup  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def test_ep_one_rank(dev):
+    grp = TpGroup(device=dev)
+    try:
+        assert tp_util.ep_check(dev, grp, None) == []
+    finally:
+        grp.close()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_ep_two_ranks():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    procs = [ctx.Process(target=tp_util.ep_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, msg = q.get(timeout=600)
+        res.setdefault(r, []).append(msg)
+    for p in procs:
+        p.join(timeout=120)
+    assert res == {0: ["ok"], 1: ["ok"]}, res

@@ -103,3 +103,78 @@ def gpu_rank(rank, world, port, out):
             except Exception as e:
                 out.put((rank, "close: " + repr(e)))
         dist.destroy_process_group()
+
+
+def ep_layer(dev, seed=9, ne=32, k=4, dim=512, ff=256):
+    """A random MoE layer, the same on every rank (GGUF expert tensors)."""
+    import torch
+    import spindle_b200 as sg
+    g = torch.Generator(device=dev).manual_seed(seed)
+    router = torch.randn(ne, dim, device=dev, generator=g) / dim ** 0.5
+    gq = sg.quantize_weights(sg.Q4_K, torch.randn(ne * ff, dim, device=dev, generator=g) * 0.02)
+    uq = sg.quantize_weights(sg.Q4_K, torch.randn(ne * ff, dim, device=dev, generator=g) * 0.02)
+    dq = sg.quantize_weights(sg.Q6_K, torch.randn(ne * dim, ff, device=dev, generator=g) * 0.02)
+    return router, gq, uq, dq, ne, k, dim, ff
+
+
+def ep_check(dev, grp, out_fail):
+    """EpMoe against the whole layer on this GPU, bit for bit, over batches,
+    repeated calls and a graph replay; returns a list of failures."""
+    import numpy as np
+    import torch
+    import spindle_b200 as sg
+    from spindle_b200.tp import EpMoe
+    router, gq, uq, dq, ne, k, dim, ff = ep_layer(dev)
+    full = sg.Moe.pack(router, gq, uq, dq, sg.Q4_K, sg.Q6_K, ne, k, dim, ff)
+    ep = EpMoe(grp, router, gq, uq, dq, sg.Q4_K, sg.Q6_K, ne, k, dim, ff, n_tok_max=17)
+    g = torch.Generator(device=dev).manual_seed(21)
+    bad = []
+    for it, nt in enumerate([1, 9, 17, 3, 9]):
+        xs = torch.randn(nt, dim, device=dev, generator=g)
+        got = ep.forward(xs)
+        want = sg.moe_forward_batch(full, xs)
+        torch.cuda.synchronize(dev)
+        if not np.array_equal(got.cpu().numpy().view(np.uint32), want.cpu().numpy().view(np.uint32)):
+            bad.append(("batch", it, nt))
+    xs = torch.randn(9, dim, device=dev, generator=g)
+    out = torch.empty(9, dim, device=dev)
+    want = sg.moe_forward_batch(full, xs)
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        ep.forward(xs, out, stream=s)  # allocates its scratch outside the capture
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            ep.forward(xs, out, stream=s)
+        for r in range(3):
+            out.fill_(float("nan"))
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            if not np.array_equal(out.cpu().numpy().view(np.uint32), want.cpu().numpy().view(np.uint32)):
+                bad.append(("graph", r))
+    del graph
+    sg.device_status()
+    return bad
+
+
+def ep_rank(rank, world, port, out):
+    import torch
+    import torch.distributed as dist
+    from spindle_b200.tp import TpGroup
+    init(rank, world, port, "nccl")
+    dev = torch.device("cuda", rank)
+    grp = None
+    try:
+        grp = TpGroup(device=dev)
+        bad = ep_check(dev, grp, out)
+        out.put((rank, "ok" if not bad else repr(bad)))
+    except Exception as e:
+        out.put((rank, repr(e)))
+    finally:
+        if grp is not None:
+            try:
+                grp.close()
+            except Exception as e:
+                out.put((rank, "close: " + repr(e)))
+        dist.destroy_process_group()
