@@ -414,6 +414,32 @@ SG_API sg_status sg_forward_batch(const sg_model *m, const int32_t *d_tokens, ui
                                   void *d_kv, void *d_scratch, uint64_t scratch_bytes, uint64_t n_max,
                                   float *d_logits, uint64_t ldl, int64_t *d_greedy, void *stream);
 
+/* The stages of a layer split over ranks (forward_slice with a layer range,
+ * smollm_chat.rs:3371-3552; the two-PC split of docs/cluster.md): layers
+ * [l0, l1) of sg_forward_batch.  l0 > 0: the input is d_hidden_in [n][dim],
+ * the raw residual of the stage before (d_tokens unused); l1 < n_layers: the
+ * output is the raw residual d_hidden_out [n][dim] (no output norm, no head,
+ * d_logits / d_greedy unused).  A stage's KV cache rows are its own layers'. */
+SG_API sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, const int32_t *d_tokens,
+                                        const float *d_hidden_in, uint64_t n, const int32_t *d_pos, void *d_kv,
+                                        void *d_scratch, uint64_t scratch_bytes, uint64_t n_max,
+                                        float *d_hidden_out, float *d_logits, uint64_t ldl, int64_t *d_greedy,
+                                        void *stream);
+/* A one-way link between two ranks for the residual between stages (the STEP /
+ * PREFILL frames of cluster_net.rs, over NVLink): sg_pipe_send stores n <=
+ * n_max floats as epoch-tagged pairs into the receiver's buffer
+ * (sg_pipe_recv_bytes(n_max), zeroed, IPC-shared), after the receiver has
+ * taken the call two before (the buffer alternates halves); sg_pipe_recv waits
+ * for them, writes them to d_dst and acknowledges to the sender (d_peer_comm:
+ * the sender's comm block, IPC-mapped).  Each side has its own zeroed comm
+ * block (sg_tp_comm_bytes) per link; both make the same sequence of calls;
+ * waits are bounded (2 s, then SG_ERR_TIMEOUT from sg_device_status). */
+SG_API uint64_t sg_pipe_recv_bytes(uint64_t n_max);
+SG_API sg_status sg_pipe_send(const float *d_src, uint64_t n, uint64_t n_max, void *d_peer_recv, void *d_comm,
+                              void *stream);
+SG_API sg_status sg_pipe_recv(float *d_dst, uint64_t n, uint64_t n_max, void *d_recv, void *d_comm, void *d_peer_comm,
+                              void *stream);
+
 /* ---- weight quantizer (no reference counterpart: its tests use random bytes)
  * f32 [rows, cols] -> Q4_K or Q6_K rows, deterministic; cols % 256 == 0. */
 SG_API sg_status sg_quantize_weights(int32_t dtype, const float *d_w, uint64_t rows, uint64_t cols,

@@ -1610,10 +1610,22 @@ sg_status sg_model_batch_prepare(const sg_model *m, uint64_t n_max, void *d_scra
 sg_status sg_forward_batch(const sg_model *m, const int32_t *d_tokens, uint64_t n, const int32_t *d_pos, void *d_kv,
                            void *d_scratch, uint64_t scratch_bytes, uint64_t n_max, float *d_logits, uint64_t ldl,
                            int64_t *d_greedy, void *stream) {
+    return sg_forward_batch_range(m, 0, m ? m->n_layers : 0, d_tokens, nullptr, n, d_pos, d_kv, d_scratch,
+                                  scratch_bytes, n_max, nullptr, d_logits, ldl, d_greedy, stream);
+}
+
+sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, const int32_t *d_tokens,
+                                 const float *d_hidden_in, uint64_t n, const int32_t *d_pos, void *d_kv,
+                                 void *d_scratch, uint64_t scratch_bytes, uint64_t n_max, float *d_hidden_out,
+                                 float *d_logits, uint64_t ldl, int64_t *d_greedy, void *stream) {
     sg_status st = check_model(m);
     if (st) return st;
+    if (l0 >= l1 || l1 > m->n_layers) return SG_ERR_INVALID;
     if (n == 0) return SG_OK;
-    if (!d_tokens || !d_pos || !d_kv || !d_scratch || n > n_max || n_max > SG_MOE_MAX_BATCH) return SG_ERR_INVALID;
+    if ((l0 == 0 ? !d_tokens : !d_hidden_in) || (l1 < m->n_layers && !d_hidden_out) || !d_pos || !d_kv ||
+        !d_scratch || n > n_max || n_max > SG_MOE_MAX_BATCH)
+        return SG_ERR_INVALID;
+    if (!aligned(d_hidden_in, 16) || !aligned(d_hidden_out, 16)) return SG_ERR_ALIGN;
     if (d_logits && n > 1 && ldl < m->vocab) return SG_ERR_INVALID;
     if (!aligned(d_scratch, 256) || !aligned(d_kv, 16) || !aligned(d_tokens, 4) || !aligned(d_pos, 4) ||
         !aligned(d_logits, 4) || !aligned(d_greedy, 8))
@@ -1655,12 +1667,19 @@ sg_status sg_forward_batch(const sg_model *m, const int32_t *d_tokens, uint64_t 
         ol[t] = logits + (uint64_t)t * lstride;
     }
     uint32_t *n_slots = (uint32_t *)(sc + L.n_slots);
-    EmbedArgs ea = {m->embed, m->embed_dtype, dim, m->vocab, m->embedding_scale, nullptr, x, d_tokens, n_slots};
-    CK(launch_pdl((const void *)embed_kernel, dim3((dim + 255) / 256, nt), 256, 0, s, &ea));
-    for (uint32_t l = 0; l < m->n_layers; l++) {
+    if (l0 == 0) {
+        EmbedArgs ea = {m->embed, m->embed_dtype, dim, m->vocab, m->embedding_scale, nullptr, x, d_tokens, n_slots};
+        CK(launch_pdl((const void *)embed_kernel, dim3((dim + 255) / 256, nt), 256, 0, s, &ea));
+    } else {
+        // a later pipeline stage: the raw residual of the stage before
+        CK(cudaMemcpyAsync(x, d_hidden_in, (uint64_t)nt * dim * 4, cudaMemcpyDeviceToDevice, s));
+        CK(cudaMemsetAsync(n_slots, 0, 4, s));
+        CK(cudaMemsetAsync(n_slots, (int)nt, 1, s));  // nt <= 64: the low byte
+    }
+    for (uint32_t l = l0; l < l1; l++) {
         const sg_layer &y = m->layers[l];
-        if ((st = launch_norm(x, l ? proj : nullptr, m->residual_scale, y.attn_norm, m->rms_eps, dim, xn, nullptr, s,
-                              nt)))
+        if ((st = launch_norm(x, l > l0 ? proj : nullptr, m->residual_scale, y.attn_norm, m->rms_eps, dim, xn,
+                              nullptr, s, nt)))
             return st;
         uint64_t wq_bytes = 0;
         const bool qk_one = y.wk_dtype == y.wq_dtype && !sg_tiled16_bytes(y.wq_dtype, q_dim, dim, &wq_bytes) &&
@@ -1697,11 +1716,52 @@ sg_status sg_forward_batch(const sg_model *m, const int32_t *d_tokens, uint64_t 
                 return st;
         }
     }
+    if (l1 < m->n_layers) {
+        // a middle stage returns the raw residual (smollm_chat.rs:3546-3551)
+        const uint64_t tot = (uint64_t)nt * dim;
+        void *args[] = {&x, &proj, (void *)&m->residual_scale, &d_hidden_out, (void *)&tot};
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((uint32_t)((tot + 255) / 256));
+        cfg.blockDim = dim3(256);
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        CK(cudaLaunchKernelExC(&cfg, (const void *)residual_kernel, args));
+        return SG_OK;
+    }
     if ((st = launch_norm(x, proj, m->residual_scale, m->output_norm, m->rms_eps, dim, xn, nullptr, s, nt))) return st;
     if ((st = gemv_rows(m->lm_head, m->lm_head_dtype, m->vocab, dim, xn, ol, nt, s))) return st;
     ArgmaxArgs ga = {logits, m->vocab, nullptr, d_greedy, (unsigned long long *)(sc + L.amax),
                      (unsigned *)(sc + L.amax + n_max * ARGMAX_CTAS * 8), 1, lstride};
     if (d_greedy) CK(launch_pdl((const void *)argmax_kernel, dim3(ARGMAX_CTAS, nt), ARGMAX_THREADS, 0, s, &ga));
+    return SG_OK;
+}
+
+uint64_t sg_pipe_recv_bytes(uint64_t n_max) { return 2ull * 8ull * n_max; }
+
+sg_status sg_pipe_send(const float *d_src, uint64_t n, uint64_t n_max, void *d_peer_recv, void *d_comm, void *stream) {
+    if (!d_src || !d_peer_recv || !d_comm || n > n_max) return SG_ERR_INVALID;
+    if (!aligned(d_peer_recv, 8) || !aligned(d_comm, 256)) return SG_ERR_ALIGN;
+    if (n == 0) return SG_OK;
+    PipeArgs a = {d_src, nullptr, (unsigned long long *)d_peer_recv, n, n_max, (unsigned *)((uint8_t *)d_comm + 128),
+                  (unsigned *)((uint8_t *)d_comm + 64), (unsigned *)((uint8_t *)d_comm + 192)};
+    const uint32_t grid = (uint32_t)((n + 255) / 256 < 148 ? (n + 255) / 256 : 148);
+    CK(launch_pdl((const void *)pipe_send_kernel, grid, 256, 0, (cudaStream_t)stream, &a));
+    return SG_OK;
+}
+
+sg_status sg_pipe_recv(float *d_dst, uint64_t n, uint64_t n_max, void *d_recv, void *d_comm, void *d_peer_comm,
+                       void *stream) {
+    if (!d_dst || !d_recv || !d_comm || !d_peer_comm || n > n_max) return SG_ERR_INVALID;
+    if (!aligned(d_recv, 8) || !aligned(d_comm, 256) || !aligned(d_peer_comm, 256)) return SG_ERR_ALIGN;
+    if (n == 0) return SG_OK;
+    PipeArgs a = {nullptr, d_dst, (unsigned long long *)d_recv, n, n_max, (unsigned *)((uint8_t *)d_comm + 128),
+                  (unsigned *)((uint8_t *)d_comm + 64), (unsigned *)((uint8_t *)d_peer_comm + 192)};
+    const uint32_t grid = (uint32_t)((n + 255) / 256 < 148 ? (n + 255) / 256 : 148);
+    CK(launch_pdl((const void *)pipe_recv_kernel, grid, 256, 0, (cudaStream_t)stream, &a));
     return SG_OK;
 }
 

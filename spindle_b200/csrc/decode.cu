@@ -534,4 +534,84 @@ __global__ void rope_kv_batch_kernel(const __grid_constant__ RopeBatchArgs a) {
     }
 }
 
+// The sender: every CTA first waits (bounded) until the receiver has
+// acknowledged epoch e - 2, so that half e & 1 of its buffer is read; then the
+// pairs go out.  The last CTA to finish (ticket) advances the epoch.
+__global__ void pipe_send_kernel(const __grid_constant__ PipeArgs a) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const unsigned e = *a.epoch + 1u;
+    __shared__ bool ok;
+    if (threadIdx.x == 0) {
+        ok = true;
+        if (e > 2) {
+            const uint64_t t0 = globaltimer_ns();
+            for (;;) {
+                unsigned v;
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.ack) : "memory");
+                if (v + 2u >= e) break;
+                if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+                    atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_PEER);
+                    ok = false;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+    }
+    __syncthreads();
+    unsigned long long *half = a.recv + (uint64_t)(e & 1u) * a.half;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const unsigned long long pr = ((unsigned long long)e << 32) | __float_as_uint(ok ? a.src[i] : __int_as_float(0x7fc00000));
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(half + i), "l"(pr) : "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(a.ticket, 1u) == gridDim.x - 1) {
+        *a.ticket = 0;
+        *a.epoch = e;
+    }
+}
+
+// The receiver: each value as soon as its pair carries epoch e; the last CTA
+// to finish acknowledges e to the sender (release) and advances the epoch.
+__global__ void pipe_recv_kernel(const __grid_constant__ PipeArgs a) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const unsigned e = *a.epoch + 1u;
+    const unsigned long long *half = a.recv + (uint64_t)(e & 1u) * a.half;
+    uint64_t t0 = 0;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += (uint64_t)gridDim.x * blockDim.x) {
+        unsigned long long p;
+        for (;;) {
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(p) : "l"(half + i) : "memory");
+            if ((uint32_t)(p >> 32) == e) break;
+            const uint64_t t = globaltimer_ns();
+            if (t0 == 0) {
+                t0 = t;
+            } else if (t - t0 > WAIT_LIMIT_NS) {
+                atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_PEER);
+                p = 0x7fc00000ull;
+                break;
+            }
+            __nanosleep(32);
+        }
+        a.dst[i] = __uint_as_float((uint32_t)p);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(a.ticket, 1u) == gridDim.x - 1) {
+        *a.ticket = 0;
+        *a.epoch = e;
+        // every block has read its values from half e & 1: the sender may reuse it
+        __threadfence_system();
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.ack), "r"(e) : "memory");
+    }
+}
+
+__global__ void residual_kernel(const float *x, const float *add, float rs, float *out, uint64_t n) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __fadd_rn(x[i], __fmul_rn(rs, add[i]));
+}
+
 }  // namespace sg

@@ -132,6 +132,28 @@ __host__ __device__ inline uint32_t attn_smem_bytes(uint32_t head_dim, uint32_t 
            2u * head_dim * 2u;
 }
 
+// Pipeline link between two ranks (forward_slice stages on different GPUs):
+// the sender stores n floats as (epoch << 32 | value) pairs into the
+// receiver's buffer (two halves by epoch parity), after the receiver has
+// acknowledged the call two before (so the half is free); the receiver waits
+// for each pair, writes the plain floats, and its last block acknowledges the
+// epoch in the sender's comm block.
+struct PipeArgs {
+    const float *src;               // send: the values
+    float *dst;                     // recv: the values
+    unsigned long long *recv;       // send: the receiver's buffer; recv: this rank's
+    uint64_t n, half;               // values; pairs per half
+    unsigned *epoch;                // this rank's epoch of the link (comm block)
+    unsigned *ticket;               // this rank's ticket
+    unsigned *ack;                  // send: this rank's ack word (written by the receiver);
+                                    // recv: the sender's ack word (a peer address)
+};
+__global__ void pipe_send_kernel(const __grid_constant__ PipeArgs a);
+__global__ void pipe_recv_kernel(const __grid_constant__ PipeArgs a);
+
+// out = x + rs * add (the residual add of the last layer of a pipeline stage)
+__global__ void residual_kernel(const float *x, const float *add, float rs, float *out, uint64_t n);
+
 __global__ void embed_kernel(const __grid_constant__ EmbedArgs a);
 __global__ void rmsnorm_kernel(const __grid_constant__ NormArgs a);
 template <int HD>

@@ -52,6 +52,9 @@ def _sigs():
         L.sg_model_batch_scratch_bytes.argtypes = [C.POINTER(SgModel), C.c_uint64]
         L.sg_model_batch_prepare.restype = C.c_int32
         L.sg_model_batch_prepare.argtypes = [C.POINTER(SgModel), C.c_uint64, P, C.c_uint64, P]
+        L.sg_forward_batch_range.restype = C.c_int32
+        L.sg_forward_batch_range.argtypes = [C.POINTER(SgModel), C.c_uint32, C.c_uint32, P, P, C.c_uint64, P, P, P,
+                                             C.c_uint64, C.c_uint64, P, P, C.c_uint64, P, P]
         L.sg_forward_batch.restype = C.c_int32
         L.sg_forward_batch.argtypes = [C.POINTER(SgModel), P, C.c_uint64, P, P, P, C.c_uint64, C.c_uint64, P,
                                        C.c_uint64, P, P]
@@ -197,6 +200,34 @@ class Decoder:
                                       C.c_void_p(lg.data_ptr()) if logits else None, self.cfg["vocab"],
                                       C.c_void_p(greedy.data_ptr()), _stream(stream)), "sg_forward_batch")
         return lg, greedy
+
+    def forward_batch_range(self, pos0, l0, l1, tokens=None, hidden=None, n_max=64, stream=None):
+        """A pipeline stage: layers [l0, l1) for positions pos0 .. pos0 + n - 1.
+        The first stage takes tokens, later ones the raw residual `hidden`
+        (float32 CUDA [n, dim]); a middle stage returns the raw residual, the
+        last one (logits [n, vocab], greedy tokens int64 [n])."""
+        L = _sigs()
+        n = len(tokens) if tokens is not None else hidden.shape[0]
+        if getattr(self, "_bscratch", None) is None or self._bn < n_max:
+            nbytes = L.sg_model_batch_scratch_bytes(C.byref(self.model), n_max)
+            if not nbytes:
+                raise SgError(3, "sg_model_batch_scratch_bytes")
+            self._bscratch = torch.empty(nbytes, dtype=torch.uint8, device=self.dev)
+            self._bn = n_max
+            _lib.check(L.sg_model_batch_prepare(C.byref(self.model), n_max, C.c_void_p(self._bscratch.data_ptr()),
+                                                nbytes, _stream(stream)), "sg_model_batch_prepare")
+        toks = None if tokens is None else torch.tensor(list(tokens), dtype=torch.int32, device=self.dev)
+        pos = torch.tensor([pos0], dtype=torch.int32, device=self.dev)
+        last = l1 == self.cfg["n_layers"]
+        out = None if last else torch.empty(n, self.cfg["dim"], dtype=torch.float32, device=self.dev)
+        lg = torch.empty(n, self.cfg["vocab"], dtype=torch.float32, device=self.dev) if last else None
+        greedy = torch.empty(n, dtype=torch.int64, device=self.dev) if last else None
+        ptr = lambda t: None if t is None else C.c_void_p(t.data_ptr())
+        _lib.check(L.sg_forward_batch_range(C.byref(self.model), l0, l1, ptr(toks), ptr(hidden), n, ptr(pos),
+                                            ptr(self.kv), ptr(self._bscratch), self._bscratch.numel(), self._bn,
+                                            ptr(out), ptr(lg), self.cfg["vocab"], ptr(greedy), _stream(stream)),
+                   "sg_forward_batch_range")
+        return (out,) if not last else (lg, greedy)
 
     def generate(self, prompt, n_new):
         """Greedy decode: feed the prompt, then n_new tokens; returns the new tokens."""

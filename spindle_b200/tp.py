@@ -217,3 +217,33 @@ class EpMoe:
                                                  C.c_void_p(sc.data_ptr()), sc.numel(), None, _stream(stream)),
                    "sg_moe_forward_batch_ep")
         return out
+
+
+class PipeLink:
+    """A one-way link src -> dst for up to n_max floats per call: the residual
+    between pipeline stages (sg_pipe_send / sg_pipe_recv).  Every rank of the
+    group builds it (the set-up is collective); only src sends, only dst
+    receives, each call of one matched by a call of the other."""
+
+    def __init__(self, grp, src, dst, n_max):
+        self.grp, self.src, self.dst, self.n_max = grp, src, dst, n_max
+        self.comm = grp._alloc(lib().sg_tp_comm_bytes())
+        _lib.check(lib().sg_tp_comm_init(C.c_void_p(self.comm), None), "sg_tp_comm_init")
+        nbytes = lib().sg_pipe_recv_bytes(n_max)
+        recv = grp._alloc(nbytes)
+        torch.as_tensor(_DeviceArray(recv, (nbytes // 4,), grp.device), device=grp.device).zero_()
+        torch.cuda.synchronize(grp.device)
+        self.comms = grp._share(self.comm)
+        self.recvs = grp._share(recv)
+
+    def send(self, x, stream=None):
+        x = x.contiguous()
+        _lib.check(lib().sg_pipe_send(C.c_void_p(x.data_ptr()), x.numel(), self.n_max,
+                                      C.c_void_p(self.recvs[self.dst]), C.c_void_p(self.comm), _stream(stream)),
+                   "sg_pipe_send")
+
+    def recv(self, out, stream=None):
+        _lib.check(lib().sg_pipe_recv(C.c_void_p(out.data_ptr()), out.numel(), self.n_max,
+                                      C.c_void_p(self.recvs[self.dst]), C.c_void_p(self.comm),
+                                      C.c_void_p(self.comms[self.src]), _stream(stream)), "sg_pipe_recv")
+        return out

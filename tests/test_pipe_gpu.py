@@ -1,0 +1,59 @@
+"""The layer split over two GPUs (sg_forward_batch_range + sg_pipe_send /
+sg_pipe_recv): stage 0 runs the first half of the layers on each prompt
+chunk and sends the raw residual over NVLink, stage 1 runs the rest and the
+head; its logits and greedy tokens equal the whole model's on one GPU bit
+for bit.  One GPU checks the stages back to back on the same device."""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+import decoder_util as U  # noqa: E402
+import tp_util  # noqa: E402
+
+from spindle_b200.decoder import Decoder  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("kind", ["dense", "moe"])
+def test_stages_on_one_gpu(dev, kind):
+    cfg = dict(U.DENSE if kind == "dense" else U.MOE, n_layers=4, max_seq=128)
+    dtypes = U.dtypes_for(cfg)
+    W = U.device_weights(U.host_weights(cfg, dtypes, seed=62), dev)
+    a, b, whole = Decoder(cfg, W, dtypes, dev), Decoder(cfg, W, dtypes, dev), Decoder(cfg, W, dtypes, dev)
+    toks = np.random.default_rng(4).integers(0, cfg["vocab"], 30).tolist()
+    pos = 0
+    for c in [1, 9, 20]:
+        (h,) = a.forward_batch_range(pos, 0, 1, tokens=toks[pos:pos + c])
+        (h2,) = a.forward_batch_range(pos, 1, 3, hidden=h)
+        lg, gr = b.forward_batch_range(pos, 3, 4, hidden=h2)
+        wl, wg = whole.forward_batch(toks[pos:pos + c], pos)
+        torch.cuda.synchronize()
+        assert np.array_equal(lg.cpu().numpy().view(np.uint32), wl.cpu().numpy().view(np.uint32)), pos
+        assert torch.equal(gr, wg)
+        pos += c
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_stage_pipeline():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    procs = [ctx.Process(target=tp_util.pipe_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, msg = q.get(timeout=600)
+        res.setdefault(r, []).append(msg)
+    for p in procs:
+        p.join(timeout=120)
+    assert res == {0: ["ok"], 1: ["ok"]}, res
