@@ -15,6 +15,12 @@ __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_
 __device__ __forceinline__ uint32_t w4(const uint4 &v, int m) { return m == 0 ? v.x : m == 1 ? v.y : m == 2 ? v.z : v.w; }
 __device__ __forceinline__ int sbyte(uint32_t w, int b) { return (int)(int8_t)(w >> (8 * b)); }
 __device__ __forceinline__ int ubyte(uint32_t w, int b) { return (int)((w >> (8 * b)) & 0xFFu); }
+// dot of 4 unsigned bytes of a with 4 signed bytes of b
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(0));
+    return d;
+}
 __device__ __forceinline__ float h2f_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
 __device__ __forceinline__ float h2f_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
 
@@ -77,6 +83,8 @@ __device__ __forceinline__ void block_q4k(const uint8_t *col, uint32_t g, uint32
     const uint32_t mnw = g ? (((hd.w >> 4) & M4) | ((hd.z >> 2) & B45)) : (hd.z & 0x3F3F3F3Fu);
     const int sc[8] = {ubyte(sclo, 0), ubyte(sclo, 1), ubyte(sclo, 2), ubyte(sclo, 3),
                        ubyte(schi, 0), ubyte(schi, 1), ubyte(schi, 2), ubyte(schi, 3)};
+    // high nibbles stay in place (16 x the value): an unsigned x signed dp4a
+    // of them is exactly 16 x the nibble dot, shifted back once per block
     uint32_t lo[4][4], hi[4][4];
 #pragma unroll
     for (int cc = 0; cc < 4; cc++) {
@@ -84,7 +92,7 @@ __device__ __forceinline__ void block_q4k(const uint8_t *col, uint32_t g, uint32
 #pragma unroll
         for (int m = 0; m < 4; m++) {
             lo[cc][m] = w4(qv, m) & M4;
-            hi[cc][m] = (w4(qv, m) >> 4) & M4;
+            hi[cc][m] = w4(qv, m) & 0xF0F0F0F0u;
         }
     }
 #pragma unroll
@@ -97,15 +105,18 @@ __device__ __forceinline__ void block_q4k(const uint8_t *col, uint32_t g, uint32
         for (int kk = 0; kk < 8; kk++) Y[kk] = lds128(y + 32 * kk);
         const uint4 B = lds128(av + 256u * nb + 32u * i + 16u * g);
         const float xd = *reinterpret_cast<const float *>(av + 288u * nb + 4u * i);
+        int sh[4];
 #pragma unroll
-        for (int m = 0; m < 4; m++) s[v][m] = 0;
+        for (int m = 0; m < 4; m++) s[v][m] = sh[m] = 0;
 #pragma unroll
         for (int cc = 0; cc < 4; cc++)
 #pragma unroll
             for (int m = 0; m < 4; m++) {
                 s[v][m] += sc[2 * cc] * __dp4a((int)lo[cc][m], (int)w4(Y[2 * cc], m), 0);
-                s[v][m] += sc[2 * cc + 1] * __dp4a((int)hi[cc][m], (int)w4(Y[2 * cc + 1], m), 0);
+                sh[m] += sc[2 * cc + 1] * dp4a_us(hi[cc][m], (int)w4(Y[2 * cc + 1], m));
             }
+#pragma unroll
+        for (int m = 0; m < 4; m++) s[v][m] += sh[m] >> 4;  // sh is a multiple of 16: exact
         cd[v] = __fmul_rn(d, xd);
         // mins: sum over sub-blocks j = 4g..4g+3 of mn_j * (bsums[2j] + bsums[2j+1]),
         // one dp2a per pair with mn_j in both low bytes
