@@ -678,6 +678,164 @@ def run_gpu_moe(args):
 # One step = one token through forward_slice + LM head + argmax, replayed from
 # one captured graph (the token and position are device state).
 
+FLOAT_METRIC = "float-path GEMV HBM GB/s (F16 / Q8_0 / float-mode Q4_K, Q6_K / F32 router, one vector)"
+F32_, F16_, Q8_0_ = 0, 1, 8
+FLOAT_SHAPES = [(F16_, 14336, 4096), (Q8_0_, 14336, 4096), (Q4_K, 14336, 4096), (Q6_K, 14336, 4096), (F32_, 128, 2048)]
+FLOAT_NAME = {F32_: "F32", F16_: "F16", Q8_0_: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
+
+
+def float_row_bytes(dt, cols):
+    return {F32_: 4 * cols, F16_: 2 * cols, Q8_0_: cols // 32 * 34, Q4_K: cols // 256 * 144, Q6_K: cols // 256 * 210}[dt]
+
+
+def float_bytes():
+    """Weights + fp32 activation + fp32 output of each matvec of the float sweep."""
+    return sum(r * float_row_bytes(dt, c) + 4 * c + 4 * r for dt, r, c in FLOAT_SHAPES)
+
+
+def run_float(args):
+    """The float path (matvec_rows_avx2, quant.rs:939-1094) over FLOAT_SHAPES,
+    one sg_matvec_rows_float per matrix; 261 MB of weights (> L2)."""
+    import torch
+    import spindle_b200 as sg
+    from spindle_b200 import _lib
+    rank, world, local = rank_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    gen = torch.Generator(device=dev).manual_seed(4000 + rank)
+    W, M, X, OUT = [], [], [], []
+    for dt, r, c in FLOAT_SHAPES:
+        wf = torch.randn(r, c, device=dev, generator=gen) * 0.02
+        if dt in (Q4_K, Q6_K):
+            w = sg.quantize_weights(dt, wf)
+        elif dt == F16_:
+            w = wf.half().view(torch.uint8).reshape(-1)
+        elif dt == F32_:
+            w = wf.view(torch.uint8).reshape(-1).clone()
+        else:  # Q8_0 blocks: f16 d then 32 int8 (random bytes with a small d)
+            w = torch.randint(0, 256, (r * c // 32 * 34,), dtype=torch.uint8, device=dev, generator=gen)
+            w.view(r, c // 32, 34)[:, :, 0] = 0
+            w.view(r, c // 32, 34)[:, :, 1] = 0x20
+        del wf
+        W.append(w)
+        M.append(sg.Mat(dt, c, r))
+        X.append(torch.randn(1, c, device=dev, generator=gen))
+        OUT.append(torch.empty(1, r, device=dev))
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    lib = sg.lib()
+
+    def step():
+        for k in range(len(FLOAT_SHAPES)):
+            sg.matvec_rows_float(W[k], M[k], X[k], OUT[k], stream=stream)
+
+    with torch.cuda.stream(stream):
+        step()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step()
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(stream)
+            for _ in range(args.steps):
+                g.replay()
+            e1.record(stream)
+            e1.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        if args.profile:
+            return None
+        h_x = [torch.empty(1, c).pin_memory() for _, _, c in FLOAT_SHAPES]
+        h_o = [torch.empty(1, r).pin_memory() for _, r, _ in FLOAT_SHAPES]
+        sp = C.c_void_p(stream.cuda_stream)
+
+        def e2e_step():
+            for k in range(len(FLOAT_SHAPES)):
+                _lib.check(lib.sg_memcpy_h2d(C.c_void_p(X[k].data_ptr()), C.c_void_p(h_x[k].data_ptr()),
+                                             h_x[k].numel() * 4, sp), "h2d")
+                sg.matvec_rows_float(W[k], M[k], X[k], OUT[k], stream=stream)
+                _lib.check(lib.sg_memcpy_d2h(C.c_void_p(h_o[k].data_ptr()), C.c_void_p(OUT[k].data_ptr()),
+                                             h_o[k].numel() * 4, sp), "d2h")
+
+        e2e_step()
+        torch.cuda.synchronize()
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=stream):
+            e2e_step()
+        for _ in range(args.warmup):
+            g2.replay()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(3, min(args.steps, 1000))
+        b0.record(stream)
+        for _ in range(reps):
+            g2.replay()
+        b1.record(stream)
+        b1.synchronize()
+        e2e_ms = b0.elapsed_time(b1) / reps
+    sg.device_status()
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+    total = float_bytes()
+    value = total * world / (ms * 1e-3) / 1e9
+    peak, peak_src = 6650.0, "fallback 6.65 TB/s"
+    try:
+        peak, peak_src = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"], "MEASURED_PEAKS.json hbm_gbs"
+    except Exception:
+        pass
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and args.cpu_budget > 0:
+            import oracle as O
+            hw = [w.cpu().numpy() for w in W]
+            hx = [x.cpu().numpy()[0] for x in X]
+            n, t0 = 0, time.perf_counter()
+            while True:
+                for k, (dt, r, c) in enumerate(FLOAT_SHAPES):
+                    rows = max(1, int(r * 0.05))  # a bounded sample: the first 5% of each matrix's rows
+                    O.matvec_rows(hw[k], O.Mat(dt, c, r), hx[k], 0, rows)
+                n += 1
+                if time.perf_counter() - t0 > min(args.cpu_budget, 10.0):
+                    break
+            el = (time.perf_counter() - t0) / n
+            sample_bytes = sum(max(1, int(r * 0.05)) * float_row_bytes(dt, c) for dt, r, c in FLOAT_SHAPES)
+            cpu = {"value": round(sample_bytes / el / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                   "sample": "%d passes of the oracle's matvec_rows (the restated AVX2 float kernels, one thread) "
+                             "over the first 5%% of each matrix's rows" % n}
+        line = {"metric": FLOAT_METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (f16 / int8 / int4 / int6 weights)",
+                "data": "synthetic",
+                "config": {"workload": "float_sweep_n1",
+                           "shapes": ["%s %dx%d" % (FLOAT_NAME[dt], r, c) for dt, r, c in FLOAT_SHAPES],
+                           "global_batch": world, "parallelism": "replicas x%d (weak)" % world,
+                           "l2": "261 MB of weights per step > 126 MB L2"},
+                "roofline": {"bound": "hbm", "achieved": round(total / (ms * 1e-3) / 1e9, 1), "peak": peak,
+                             "unit": "GB/s", "frac": round(total / (ms * 1e-3) / 1e9 / peak, 4), "traffic": None,
+                             "peak_source": peak_src, "kernel": "gemv_float_kernel",
+                             "how": "weights + x + out of the 5 matvecs / replayed step time"},
+                "e2e": {"value": round(total * world / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                        "h2d_bytes_per_step": sum(4 * c for _, _, c in FLOAT_SHAPES),
+                        "d2h_bytes_per_step": sum(4 * r for _, r, _ in FLOAT_SHAPES),
+                        "how": "per matrix: sg_memcpy_h2d of x from pinned host, sg_matvec_rows_float, "
+                               "sg_memcpy_d2h of the output"},
+                "cpu_baseline": cpu,
+                "gpu_launches": len(FLOAT_SHAPES) * args.steps,
+                "clocks": clk.summary()}
+    if world > 1:
+        dist.destroy_process_group()
+    return line
+
+
 TP_METRIC = "K-quant GEMV HBM GB/s, rows split over the GPUs with the gather fused in (Q4_K/Q6_K x Q8_K sweep)"
 
 
@@ -997,6 +1155,205 @@ def run_gpu_decode(args):
     return line, host, cfg, dtypes
 
 
+# ---- prefill + verify workload (--workload prefill) ---------------------------
+# BASELINE configs[4] on the configs[3] model: a 2048-token random-ID prompt
+# fed through the batch forward (feed, smollm_chat.rs:3042-3106: chunks of
+# positions, K/V rows into the caches, hidden states only), the greedy token of
+# its last position, then N=9 verify passes (forward_batch + compute_logits_batch)
+# at the positions after it.  One step = the whole 2048-token prefill.
+
+PREFILL_PROMPT = 2048
+PREFILL_CHUNK = 64
+VERIFY_N = 9
+
+
+def active_params(cfg):
+    """Weights one token multiplies through (attention, router, the chosen
+    experts or the dense FFN) over all layers; the LM head is left out (the
+    prefill runs it for one position)."""
+    d, hd = cfg["dim"], cfg["head_dim"]
+    q, kv = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    attn = 2 * q * d + 2 * kv * d
+    if cfg.get("moe"):
+        m = cfg["moe"]
+        ffn = m["n_expert"] * d + m["n_used"] * 3 * m["n_ff"] * d
+    else:
+        ffn = 3 * cfg["n_ff"] * d
+    return cfg["n_layers"] * (attn + ffn)
+
+
+def run_gpu_prefill(args):
+    import torch
+    import torch.distributed as dist
+
+    import spindle_b200 as sg
+    from spindle_b200 import _lib
+    from spindle_b200.decoder import Decoder, _sigs, qwen3_dtypes, random_weights
+
+    rank, world, local = rank_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    name = "qwen3_30b_a3b"
+    n_prompt = 128 if args.profile else PREFILL_PROMPT
+    cfg = dict(DECODE_MODELS[name], max_seq=n_prompt + 2 * VERIFY_N + 8)
+    if args.profile:
+        cfg["n_layers"] = 2  # profiling case: the model's first two layers, two chunks
+    dtypes = qwen3_dtypes(cfg, embed=Q4_K)
+    W = random_weights(cfg, dtypes, dev, seed=5000 + rank)
+    dec = Decoder(cfg, W, dtypes, dev)
+    del W
+    L = _sigs()
+    lib = sg.lib()
+    C_ = PREFILL_CHUNK
+    nbytes = L.sg_model_batch_scratch_bytes(C.byref(dec.model), C_)
+    scr = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    _lib.check(L.sg_model_batch_prepare(C.byref(dec.model), C_, C.c_void_p(scr.data_ptr()), nbytes, None), "prepare")
+    g = torch.Generator().manual_seed(78 + rank)
+    h_tok = torch.randint(0, cfg["vocab"], (n_prompt + VERIFY_N,), generator=g, dtype=torch.int32).pin_memory()
+    # calls: full chunks without the head, then the last position alone with it
+    calls = [(c0, min(C_, n_prompt - 1 - c0)) for c0 in range(0, n_prompt - 1, C_)] + [(n_prompt - 1, 1)]
+    h_pos = torch.tensor([c0 for c0, _ in calls] + [n_prompt], dtype=torch.int32).pin_memory()
+    toks = h_tok.to(dev)
+    pos = h_pos.to(dev)
+    hid = torch.empty(C_, cfg["dim"], dtype=torch.float32, device=dev)
+    greedy = torch.empty(C_, dtype=torch.int64, device=dev)
+    vlog = torch.empty(VERIFY_N, cfg["vocab"], dtype=torch.float32, device=dev)
+    vgreedy = torch.empty(VERIFY_N, dtype=torch.int64, device=dev)
+    nl = cfg["n_layers"]
+    ptr = lambda t, off=0: C.c_void_p(t.data_ptr() + off)
+
+    def prefill(st):
+        sp = C.c_void_p(st.cuda_stream)
+        for i, (c0, n) in enumerate(calls):
+            head = i == len(calls) - 1
+            _lib.check(L.sg_forward_batch_range(C.byref(dec.model), 0, nl, ptr(toks, 4 * c0), None, n,
+                                                ptr(pos, 4 * i), ptr(dec.kv), ptr(scr), nbytes, C_,
+                                                None if head else ptr(hid), None, cfg["vocab"],
+                                                ptr(greedy) if head else None, sp), "prefill")
+
+    def verify(st):
+        _lib.check(L.sg_forward_batch(C.byref(dec.model), ptr(toks, 4 * n_prompt), VERIFY_N, ptr(pos, 4 * len(calls)),
+                                      ptr(dec.kv), ptr(scr), nbytes, C_, ptr(vlog), cfg["vocab"], ptr(vgreedy),
+                                      C.c_void_p(st.cuda_stream)), "verify")
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        prefill(s)
+        verify(s)
+        torch.cuda.synchronize()
+        gp = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gp, stream=s):
+            prefill(s)
+        gv = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gv, stream=s):
+            verify(s)
+        if args.profile:
+            for _ in range(args.warmup + args.steps):
+                gp.replay()
+                gv.replay()
+            torch.cuda.synchronize()
+            sg.device_status()
+            if rank == 0:
+                print(json.dumps({"profile": True, "workload": "prefill_%s_2_layers" % name, "prompt": n_prompt}),
+                      flush=True)
+            return None
+        for _ in range(args.warmup):
+            gp.replay()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(s)
+            for _ in range(args.steps):
+                gp.replay()
+            e1.record(s)
+            e1.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        # verify passes at positions n_prompt .. n_prompt + 8 (rewritten each pass)
+        for _ in range(3):
+            gv.replay()
+        v0, v1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        nv = 20
+        v0.record(s)
+        for _ in range(nv):
+            gv.replay()
+        v1.record(s)
+        v1.synchronize()
+        v_ms = v0.elapsed_time(v1) / nv
+        # e2e: prompt tokens and chunk positions from pinned host memory, the
+        # prefill, the greedy next token back to the host
+        h_out = torch.zeros(1, dtype=torch.int64).pin_memory()
+        sp = C.c_void_p(s.cuda_stream)
+        tok_bytes, pos_bytes = 4 * (n_prompt + VERIFY_N), 4 * (len(calls) + 1)
+
+        def e2e():
+            _lib.check(lib.sg_memcpy_h2d(ptr(toks), ptr(h_tok), tok_bytes, sp), "h2d")
+            _lib.check(lib.sg_memcpy_h2d(ptr(pos), ptr(h_pos), pos_bytes, sp), "h2d")
+            gp.replay()
+            _lib.check(lib.sg_memcpy_d2h(ptr(h_out), ptr(greedy), 8, sp), "d2h")
+
+        e2e()
+        torch.cuda.synchronize()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(1, min(3, args.steps))
+        b0.record(s)
+        for _ in range(n_e2e):
+            e2e()
+        b1.record(s)
+        b1.synchronize()
+        e2e_ms = b0.elapsed_time(b1) / n_e2e
+        if world > 1:
+            t = torch.tensor([ms, v_ms, e2e_ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms, v_ms, e2e_ms = float(t[0]), float(t[1]), float(t[2])
+    sg.device_status()
+    ops = 2.0 * n_prompt * active_params(cfg)
+    peak, peak_src = 2 * 1596.4, "fallback: 2 x bf16 burst"
+    try:
+        pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        peak, peak_src = 2 * pk["bf16_tflops"], "2 x MEASURED_PEAKS.json bf16_tflops (dense int8 = 2 x bf16 on B200)"
+    except Exception:
+        pass
+    line = None
+    if rank == 0:
+        achieved = ops / (ms * 1e-3) / 1e12
+        line = {"metric": "prefill tokens/s, %s (random-init, Q4_K_M mix), %d-token prompt" % (name, n_prompt),
+                "value": round(n_prompt * world / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None,
+                "dtype": "int8 x int4/int6 -> int32 (dp4a), fp32 norms/attention/router, f16 KV",
+                "data": "synthetic",
+                "config": dict(decode_config(name, cfg, world), workload="prefill_verify_%s" % name,
+                               prompt=n_prompt, seq_len=n_prompt, chunk=C_, verify_n=VERIFY_N,
+                               calls="%d chunks of up to %d positions without the head, then the last position "
+                                     "with the LM head and argmax" % (len(calls) - 1, C_),
+                               l2="2.0 GB of weights touched per chunk > 126 MB L2"),
+                "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": peak, "unit": "TOP/s",
+                             "frac": round(achieved / peak, 5), "traffic": None, "peak_source": peak_src,
+                             "kernel": "the whole prefill (dp4a GEMV kernels; no tcgen05 kind::i8 path yet)",
+                             "how": "2 x prompt x active params (%.3f G) / step time" % (active_params(cfg) / 1e9)},
+                "verify": {"n": VERIFY_N, "ms_per_pass": round(v_ms, 3),
+                           "tok_per_s_if_all_accepted": round(VERIFY_N * 1e3 / v_ms, 1),
+                           "tok_per_s_at_half_acceptance": round((1 + (VERIFY_N - 1) // 2) * 1e3 / v_ms, 1),
+                           "how": "forward_batch + LM head + argmax for 9 positions after the prompt, graph replays"},
+                "e2e": {"value": round(n_prompt * world / (e2e_ms * 1e-3), 1), "unit": "tok/s",
+                        "h2d_bytes_per_step": tok_bytes + pos_bytes, "d2h_bytes_per_step": 8,
+                        "how": "sg_memcpy_h2d of the prompt tokens and chunk positions from pinned host, the "
+                               "prefill, sg_memcpy_d2h of the greedy next token (%d steps)" % n_e2e},
+                "gpu_launches": len(calls) * (1 + nl * 12) * args.steps,
+                "clocks": clk.summary()}
+    if world > 1:
+        dist.barrier()
+        del gp, gv
+        dist.destroy_process_group()
+    return line
+
+
 def decode_cpu_sample(cfg, dtypes, host, budget_s):
     """Per-token time of the oracle's forward_slice (one thread), measured on a
     two-layer model made of the real model's first two layers, embedding and
@@ -1051,10 +1408,11 @@ def main():
     ap.add_argument("--shape", type=int, default=None, help="profiling: run only this sweep entry")
     ap.add_argument("--profile", action="store_true",
                     help="profiling: only the timed step loop (no e2e, per-shape or CPU legs)")
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "gemv_tp", "moe", "decode"],
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "gemv_tp", "float", "moe", "decode", "prefill"],
                     help="gemv: the headline K-quant GEMV sweep; gemv_tp: the same sweep split by rows over the "
-                         "GPUs with the gather fused in; moe: the Qwen3-30B-A3B MoE layer; decode: greedy decode "
-                         "of a whole random-init model")
+                         "GPUs with the gather fused in; float: the float-path matvecs; moe: the Qwen3-30B-A3B "
+                         "MoE layer; decode: greedy decode of a whole random-init model; prefill: a 2048-token prompt "
+                         "through the batch forward, then N=9 verify passes")
     ap.add_argument("--model", default="qwen3_30b_a3b", choices=sorted(DECODE_MODELS),
                     help="decode workload: the model architecture")
     args = ap.parse_args()
@@ -1079,6 +1437,17 @@ def main():
                                                   % (n, cfg["n_layers"])}
             print(json.dumps(line), flush=True)
         return
+    if args.workload == "prefill":
+        if args.steps == 20000:
+            args.steps = 3  # one step is a whole 2048-token prompt
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "prefill reference arm: the oracle forward runs "
+                              "about 1 token/s on one core; the decode line's cpu_baseline covers it"}), flush=True)
+            return
+        line = run_gpu_prefill(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
     if args.workload == "moe":
         if args.steps == 20000:
             args.steps = 2000  # one step is 8 token-layers
@@ -1094,6 +1463,15 @@ def main():
                                         "sample": "%d token-layers through the oracle's moe_forward (same layer "
                                                   "shape, host-quantized weights), one thread, %.1f s"
                                                   % (n, per_layer * n)}
+            print(json.dumps(line), flush=True)
+        return
+    if args.workload == "float":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "float reference arm: use the cpu_baseline of the "
+                              "GPU line (the oracle's float kernels on a bounded sample)"}), flush=True)
+            return
+        line = run_float(args)
+        if line is not None:
             print(json.dumps(line), flush=True)
         return
     if args.shape is not None:

@@ -150,6 +150,20 @@ SG_API sg_status sg_unpack_tiled16(int32_t dtype, const uint8_t *d_tiled, uint64
 SG_API sg_status sg_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
                            uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, void *stream);
 
+/* Many vectors at once (matvec_multi, smollm_chat.rs:447-512, over
+ * quant_q8k.rs:255-295 matmul_rows): the rows r0..r1 of a TILED16 Q4_K/Q6_K
+ * matrix for n_vec <= SG_BATCH_MAX_VEC fp32 vectors (x_b = d_x + b*ldx),
+ * out_b[r] = d_out[b*ldo + r]; each vector is quantized to Q8_K once and every
+ * weight column is read once for all of them (one quantize launch plus one
+ * GEMM launch).  Bit for bit the results of sg_matvec (and of the reference's
+ * integer kernel).  Scratch: sg_matmul_batch_scratch_bytes(m, n_vec) device
+ * bytes, 16-byte aligned, caller-owned; ldx % 4 == 0. */
+#define SG_BATCH_MAX_VEC 64
+SG_API uint64_t sg_matmul_batch_scratch_bytes(const sg_mat *m, uint64_t n_vec);
+SG_API sg_status sg_matmul_batch(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx,
+                                 float *d_out, uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1,
+                                 void *d_scratch, uint64_t scratch_bytes, void *stream);
+
 /* The float path (quant.rs:939-1094 matvec_rows_avx2; quant_multi.rs:232-273
  * matmul_rows_avx2), for formats or switches that keep a matrix off the integer
  * kernels: out_b[r] = d_out[b*ldo + r] for r in r0..r1, x_b = d_x + b*ldx (cols
@@ -419,7 +433,11 @@ SG_API sg_status sg_forward_batch(const sg_model *m, const int32_t *d_tokens, ui
  * [l0, l1) of sg_forward_batch.  l0 > 0: the input is d_hidden_in [n][dim],
  * the raw residual of the stage before (d_tokens unused); l1 < n_layers: the
  * output is the raw residual d_hidden_out [n][dim] (no output norm, no head,
- * d_logits / d_greedy unused).  A stage's KV cache rows are its own layers'. */
+ * d_logits / d_greedy unused).  l1 == n_layers: d_hidden_out (optional) gets
+ * the output-normed hidden states [n][dim] (forward_batch_slice's return
+ * value), and the LM head and argmax run only when d_logits or d_greedy is
+ * given (a prompt fed through feed(), smollm_chat.rs:3042-3106, needs no
+ * logits).  A stage's KV cache rows are its own layers'. */
 SG_API sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, const int32_t *d_tokens,
                                         const float *d_hidden_in, uint64_t n, const int32_t *d_pos, void *d_kv,
                                         void *d_scratch, uint64_t scratch_bytes, uint64_t n_max,

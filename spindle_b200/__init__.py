@@ -6,6 +6,7 @@ Host-side mirror of the reference's kernel API (WiseHax/spindle 1.1.0, src/):
   supports / set_enabled   quant_q8k.rs:22-57
   Q8K, Q8K.quantize        quant_q8k.rs:61-81
   matmul_rows              quant_q8k.rs:255-295
+  matmul_batch             smollm_chat.rs:447-512 (matvec_multi, 9..64 vectors, one pass)
   matvec_rows_float        quant.rs:939-1094 (float path, one vector at a time)
   matmul_rows_float        quant_multi.rs:232-273 (float path, shared decode)
   Moe, moe_forward         smollm_chat.rs:1178-1382
@@ -189,6 +190,28 @@ def matvec_rows_float(base, m, xs, out=None, r0=0, r1=None, stream=None):
     xs [n_vec, cols] (or [cols]) -> out [n_vec, rows] (rows outside r0..r1
     untouched).  GGUF rows of F32, F16, Q8_0, Q4_K or Q6_K."""
     return _float_call(lib().sg_matvec_rows_float, "matvec_rows_float", base, m, xs, out, r0, r1, stream)
+
+
+def matmul_batch(base, m, xs, out=None, r0=0, r1=None, stream=None):
+    """matvec_multi (smollm_chat.rs:447-512) for up to 64 vectors in one pass
+    over a TILED16 Q4_K / Q6_K matrix: fp32 CUDA xs [n_vec, cols] -> out
+    [n_vec, rows] (rows outside r0..r1 untouched), bit for bit the GEMV's."""
+    xs2 = xs.reshape(1, -1) if xs.dim() == 1 else xs
+    if xs2.dtype != torch.float32 or xs2.stride(-1) != 1:
+        raise ValueError("xs must be float32 with contiguous rows")
+    r1 = m.rows if r1 is None else r1
+    if out is None:
+        out = torch.full((xs2.shape[0], m.rows), float("nan"), dtype=torch.float32, device=xs2.device)
+    out2 = out.reshape(1, -1) if out.dim() == 1 else out
+    L = lib()
+    nbytes = L.sg_matmul_batch_scratch_bytes(C.byref(m.c()), xs2.shape[0])
+    if not nbytes:
+        raise SgError(3, "matmul_batch_scratch_bytes")
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=xs2.device)
+    _lib.check(L.sg_matmul_batch(C.c_void_p(base.data_ptr()), C.byref(m.c()), C.c_void_p(xs2.data_ptr()),
+                                 xs2.stride(0), C.c_void_p(out2.data_ptr()), out2.stride(0), xs2.shape[0], r0, r1,
+                                 C.c_void_p(scratch.data_ptr()), nbytes, _stream(stream)), "matmul_batch")
+    return out
 
 
 def matmul_rows_float(base, m, xs, out=None, r0=0, r1=None, stream=None):

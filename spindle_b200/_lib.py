@@ -86,6 +86,8 @@ SIGNATURES = {
     "sg_matmul_rows": (I32, [P, C.POINTER(SgMat), C.POINTER(SgQ8K), C.POINTER(P), U64, U64, U64, P]),
     "sg_matvec": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
     "sg_matvec_rows_float": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
+    "sg_matmul_batch_scratch_bytes": (U64, [C.POINTER(SgMat), U64]),
+    "sg_matmul_batch": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P, U64, P]),
     "sg_matmul_rows_float": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
     "sg_ipc_handle_bytes": (U64, []),
     "sg_ipc_get_handle": (I32, [P, P]),

@@ -15,6 +15,7 @@
 #include "moe.cuh"
 #include "decode.cuh"
 #include "gemv_float.cuh"
+#include "gemm_batch.cuh"
 
 using namespace sg;
 
@@ -460,6 +461,68 @@ sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, 
     return SG_OK;
 }
 
+// ---- batch GEMM (9..64 vectors) ----------------------------------------------
+
+// QB image (gemm_batch.cuh) of n fp32 vectors x + t * ldx of 256 * nb values.
+sg_status launch_q8k_batch(const float *x, uint64_t ldx, uint32_t n, uint32_t nb, uint8_t *qb, cudaStream_t s) {
+    if (n == 0 || nb == 0) return SG_OK;
+    QbArgs a = {x, ldx, n, nb, qb};
+    const uint64_t warps = (uint64_t)n * nb;
+    CK(launch_pdl((const void *)q8k_batch_kernel, dim3((uint32_t)((warps + 7) / 8)), 256, 0, s, &a));
+    return SG_OK;
+}
+
+// Rows r0..r1 of a TILED16 matrix for ntok <= 64 vectors given as a QB image:
+// vector t, row r at out + t * ldo + r (swiglu: the packed gate/up form, see
+// GemmBatchArgs).  One launch; every weight column is read once.
+sg_status launch_gemm_batch(const uint8_t *w, int dt, uint32_t nb, uint64_t r0, uint64_t r1, const uint8_t *qb,
+                            uint32_t ntok, float *out, uint64_t ldo, bool swiglu, cudaStream_t s) {
+    if (ntok == 0 || r1 <= r0) return SG_OK;
+    if (ntok > GB_MAX_TOK) return SG_ERR_SHAPE;
+    static std::atomic<uint64_t> attr_done{0};
+    int dev;
+    CK(cudaGetDevice(&dev));
+    if (!(attr_done.load() >> dev & 1)) {
+        for (const void *fn : {(const void *)gemm_batch_kernel<0, 4>, (const void *)gemm_batch_kernel<1, 4>,
+                               (const void *)gemm_batch_kernel<0, 8>, (const void *)gemm_batch_kernel<1, 8>})
+            CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        attr_done.fetch_or(1ull << dev);
+    }
+    static const int tpw = env_int("SG_GEMM_TPW", 4) == 8 ? 8 : 4;
+    const uint32_t cons = gb_consumers(tpw);
+    DevInfo *di;
+    sg_status st = dev_info(&di);
+    if (st) return st;
+    GemmBatchArgs a;
+    memset(&a, 0, sizeof a);
+    a.w = w;
+    a.nb = nb;
+    a.t0 = (uint32_t)(r0 / TILE_ROWS);
+    a.ntiles = (uint32_t)((r1 + TILE_ROWS - 1) / TILE_ROWS) - a.t0;
+    a.r0 = (uint32_t)r0;
+    a.r1 = (uint32_t)r1;
+    a.qb = qb;
+    a.ntok = ntok;
+    a.nq = 1;
+    while (a.nq * (uint32_t)tpw < ntok) a.nq *= 2;
+    a.tps = cons / a.nq;
+    const uint32_t cb = tiled_col_bytes(dt);
+    a.stage_bytes = a.tps * cb + qb_block_bytes(ntok);
+    const uint32_t budget = 220u * 1024u - GB_BAR_BYTES;
+    a.nstages = budget / a.stage_bytes;
+    if (a.nstages > GB_MAX_STAGES) a.nstages = GB_MAX_STAGES;
+    if (a.nstages < 2) return SG_ERR_SHAPE;
+    a.out = out;
+    a.ldo = ldo;
+    a.swiglu = swiglu ? 1u : 0u;
+    const uint32_t nsteps = (a.ntiles + a.tps - 1) / a.tps;
+    const uint32_t grid = nsteps < (uint32_t)di->sms ? nsteps : (uint32_t)di->sms;
+    const void *fn = tpw == 4 ? (dt == DT_Q4K ? (const void *)gemm_batch_kernel<0, 4> : (const void *)gemm_batch_kernel<1, 4>)
+                              : (dt == DT_Q4K ? (const void *)gemm_batch_kernel<0, 8> : (const void *)gemm_batch_kernel<1, 8>);
+    CK(launch_pdl(fn, dim3(grid), cons * 32, GB_BAR_BYTES + a.nstages * a.stage_bytes, s, &a));
+    return SG_OK;
+}
+
 sg_status launch_gemv(const uint8_t *d_base, const sg_mat *m, const sg_q8k *xq, float *const *outs,
                       uint64_t n_vec, uint64_t r0, uint64_t r1, int32_t *dbg, cudaStream_t stream) {
     int dt;
@@ -718,8 +781,12 @@ sg_status launch_router(const sg_moe *m, const float *x, float *logits, uint8_t 
     // about one CTA per SM; fewer rows per CTA when they do not fit in 200 KB
     uint32_t rpc = (a.n_expert + di->sms - 1) / di->sms;
     if (rpc > ROUTER_MAX_ROWS) rpc = ROUTER_MAX_ROWS;
-    while (rpc > 1 && router_smem_bytes(a.dim, rpc) > 200 * 1024) rpc--;
-    const uint32_t smem = router_smem_bytes(a.dim, rpc);
+    // tokens staged together: all of a small batch, at most 32
+    uint32_t tc = n_tok < 32 ? n_tok : 32u;
+    if (tc == 0) tc = 1;
+    while (tc > 1 && router_smem_bytes(a.dim, rpc, tc) > 160 * 1024) tc--;
+    while (rpc > 1 && router_smem_bytes(a.dim, rpc, tc) > 200 * 1024) rpc--;
+    const uint32_t smem = router_smem_bytes(a.dim, rpc, tc);
     if (smem > 227 * 1024) return SG_ERR_SHAPE;
     a.rows_per_cta = rpc;
     a.row_ctas = (a.n_expert + rpc - 1) / rpc;
@@ -731,7 +798,10 @@ sg_status launch_router(const sg_moe *m, const float *x, float *logits, uint8_t 
     a.shared_scale = sh ? scale : nullptr;
     a.n_tok = n_tok;
     a.ldx = n_tok > 1 ? ldx : m->dim;
-    const uint32_t threads = (8 * rpc + 31) / 32 * 32;
+    a.tok_chunk = tc;
+    // 8 threads per (row, token): one warp for a lone token, up to 256 threads for a batch
+    uint32_t threads = (8 * rpc * tc + 31) / 32 * 32;
+    if (threads > ROUTER_MAX_THREADS) threads = ROUTER_MAX_THREADS;
     CK(launch_pdl((const void *)moe_router_kernel, a.row_ctas + (sh ? 1 : 0), threads, smem, stream, &a));
     return SG_OK;
 }
@@ -1057,6 +1127,30 @@ sg_status sg_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x, ui
         if (st) return st;
     }
     return SG_OK;
+}
+
+uint64_t sg_matmul_batch_scratch_bytes(const sg_mat *m, uint64_t n_vec) {
+    if (!m || m->cols % 256 || n_vec == 0 || n_vec > SG_BATCH_MAX_VEC) return 0;
+    return (uint64_t)(m->cols / 256) * qb_block_bytes((uint32_t)n_vec);
+}
+
+sg_status sg_matmul_batch(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
+                          uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, void *d_scratch,
+                          uint64_t scratch_bytes, void *stream) {
+    int dt;
+    sg_status st = check_mat(d_base, m, r0, r1, &dt);
+    if (st) return st;
+    if (m->layout != SG_LAYOUT_TILED16 || n_vec > SG_BATCH_MAX_VEC) return SG_ERR_INVALID;
+    if (r1 == r0 || n_vec == 0) return SG_OK;
+    if (!d_x || !d_out || !d_scratch || (n_vec > 1 && (ldx < m->cols || ldo < m->rows)) ||
+        scratch_bytes < sg_matmul_batch_scratch_bytes(m, n_vec))
+        return SG_ERR_INVALID;
+    if (!aligned(d_x, 16) || ldx % 4 || !aligned(d_out, 4) || !aligned(d_scratch, 16)) return SG_ERR_ALIGN;
+    const uint32_t nb = (uint32_t)(m->cols / 256);
+    cudaStream_t s = (cudaStream_t)stream;
+    if ((st = launch_q8k_batch(d_x, ldx, (uint32_t)n_vec, nb, (uint8_t *)d_scratch, s))) return st;
+    return launch_gemm_batch(d_base + m->offset, dt, nb, r0, r1, (const uint8_t *)d_scratch, (uint32_t)n_vec, d_out,
+                             n_vec > 1 ? ldo : m->rows, false, s);
 }
 
 sg_status sg_matvec_rows_float(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
@@ -1412,7 +1506,7 @@ sg_status check_model(const sg_model *m) {
     if (!m->n_heads || !m->n_kv_heads || m->n_heads % m->n_kv_heads || !m->n_layers || !m->vocab || !m->max_seq)
         return SG_ERR_INVALID;
     if (m->dim % 256 || m->dim == 0 || m->dim > 8192 || m->head_dim % 64 || m->head_dim == 0 || m->head_dim > 256 ||
-        (m->n_heads * m->head_dim) % 256 || attn_smem_bytes(m->head_dim, m->max_seq) > 227 * 1024)
+        (m->n_heads * m->head_dim) % 256 || attn_smem_bytes(m->head_dim, m->max_seq, 2) > 227 * 1024)
         return SG_ERR_SHAPE;
     if (m->embed_dtype != SG_F32 && m->embed_dtype != SG_F16 && !kq(m->embed_dtype)) return SG_ERR_DTYPE;
     if (!kq(m->lm_head_dtype)) return SG_ERR_DTYPE;
@@ -1484,7 +1578,7 @@ sg_status launch_norm(float *x, const float *add, float rs, const float *w, floa
 
 // Scratch of sg_forward_batch for up to n_max tokens per call.
 struct ModelBatchScratch {
-    uint64_t x, xn, qx, qkv, att, proj, logits, h, freqs, amax, slots, n_slots, moe, moe_bytes, total;
+    uint64_t x, xn, qx, qkv, att, proj, logits, h, freqs, amax, slots, n_slots, moe, moe_bytes, qb, total;
 };
 
 ModelBatchScratch model_batch_scratch(const sg_model *m, uint64_t n) {
@@ -1520,6 +1614,10 @@ ModelBatchScratch model_batch_scratch(const sg_model *m, uint64_t n) {
     L.n_slots = take(4);
     L.moe = take(moe);
     L.moe_bytes = moe;
+    // QB image of the widest input of a batch GEMM (dim, q_dim or a dense n_ff)
+    uint64_t widest = m->dim > q_dim ? m->dim : q_dim;
+    if (n_ff > widest) widest = n_ff;
+    L.qb = take(widest / 256 * qb_block_bytes((uint32_t)n));
     L.total = off;
     return L;
 }
@@ -1667,6 +1765,8 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
         ol[t] = logits + (uint64_t)t * lstride;
     }
     uint32_t *n_slots = (uint32_t *)(sc + L.n_slots);
+    uint8_t *qb = sc + L.qb;
+    const bool batch_gemm = nt >= (uint32_t)env_int("SG_BATCH_GEMM_MIN", 9);
     if (l0 == 0) {
         EmbedArgs ea = {m->embed, m->embed_dtype, dim, m->vocab, m->embedding_scale, nullptr, x, d_tokens, n_slots};
         CK(launch_pdl((const void *)embed_kernel, dim3((dim + 255) / 256, nt), 256, 0, s, &ea));
@@ -1684,11 +1784,17 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
         uint64_t wq_bytes = 0;
         const bool qk_one = y.wk_dtype == y.wq_dtype && !sg_tiled16_bytes(y.wq_dtype, q_dim, dim, &wq_bytes) &&
                             y.wk == y.wq + wq_bytes;
+        // many tokens: one quantize per input and one batch GEMM per matrix;
+        // few: the GEMV with up to 8 vectors per launch
         auto gemv = [&](const uint8_t *w, int32_t dt, uint32_t rows, uint32_t cols, const float *xin,
                         std::vector<float *> &outs) {
+            if (batch_gemm)
+                return launch_gemm_batch(w, dt == SG_Q4_K ? DT_Q4K : DT_Q6K, cols / 256, 0, rows, qb, nt, outs[0],
+                                         outs.size() > 1 ? (uint64_t)(outs[1] - outs[0]) : rows, false, s);
             return launch_tiled(w, dt == SG_Q4_K ? DT_Q4K : DT_Q6K, cols / 256, nullptr, xin, cols, outs.data(), nt, 0,
                                 rows, s);
         };
+        if (batch_gemm && (st = launch_q8k_batch(xn, dim, nt, dim / 256, qb, s))) return st;
         if (qk_one) {
             if ((st = gemv(y.wq, y.wq_dtype, q_dim + kv_dim, dim, xn, oq))) return st;
         } else if ((st = gemv(y.wq, y.wq_dtype, q_dim, dim, xn, oq)) || (st = gemv(y.wk, y.wk_dtype, kv_dim, dim, xn, ok_))) {
@@ -1700,12 +1806,23 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
                             m->max_seq};
         CK(launch_pdl((const void *)rope_kv_batch_kernel, dim3(m->n_heads + m->n_kv_heads, nt), 32, 0, s, &ra));
         AttnArgs aa = {qkv, nullptr, nullptr, nullptr, nullptr, m->rms_eps, freqs, hd, m->n_heads, m->n_kv_heads,
-                       m->max_seq, m->rope_neox, scale, d_pos, kc + l * cache, vc + l * cache, att, 1, qkv_stride};
-        CK(launch_pdl(attn_fn, dim3(m->n_heads, nt), attn_threads(hd), attn_smem_bytes(hd, m->max_seq), s, &aa));
+                       m->max_seq, m->rope_neox, scale, d_pos, kc + l * cache, vc + l * cache, att, 1, qkv_stride,
+                       2};  // two buffers: many CTAs, two of them per SM
+        CK(launch_pdl(attn_fn, dim3(m->n_heads, nt), attn_threads(hd), attn_smem_bytes(hd, m->max_seq, 2), s, &aa));
+        if (batch_gemm && (st = launch_q8k_batch(att, q_dim, nt, q_dim / 256, qb, s))) return st;
         if ((st = gemv(y.wo, y.wo_dtype, dim, q_dim, att, oo))) return st;
         if ((st = launch_norm(x, proj, m->residual_scale, y.ffn_norm, m->rms_eps, dim, xn, qx, s, nt))) return st;
         if (y.is_moe) {
             if ((st = sg_moe_forward_batch(&y.moe, xn, dim, n, proj, dim, sc + L.moe, L.moe_bytes, nullptr, stream)))
+                return st;
+        } else if (batch_gemm) {
+            // dense FFN: gate/up with SiLU*up in the epilogue, then down
+            if ((st = launch_q8k_batch(xn, dim, nt, dim / 256, qb, s)) ||
+                (st = launch_gemm_batch(y.ffn_gate_up, y.ffn_gate_up_dtype == SG_Q4_K ? DT_Q4K : DT_Q6K, dim / 256, 0,
+                                        2 * (uint64_t)y.n_ff, qb, nt, h, y.n_ff, true, s)) ||
+                (st = launch_q8k_batch(h, y.n_ff, nt, y.n_ff / 256, qb, s)) ||
+                (st = launch_gemm_batch(y.ffn_down, y.ffn_down_dtype == SG_Q4_K ? DT_Q4K : DT_Q6K, y.n_ff / 256, 0,
+                                        dim, qb, nt, proj, dim, false, s)))
                 return st;
         } else {
             const MoeSlots ms = {(const int32_t *)(sc + L.slots), n_slots, qx};
@@ -1732,8 +1849,20 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
         CK(cudaLaunchKernelExC(&cfg, (const void *)residual_kernel, args));
         return SG_OK;
     }
-    if ((st = launch_norm(x, proj, m->residual_scale, m->output_norm, m->rms_eps, dim, xn, nullptr, s, nt))) return st;
-    if ((st = gemv_rows(m->lm_head, m->lm_head_dtype, m->vocab, dim, xn, ol, nt, s))) return st;
+    // the last stage: output-normed hidden states (what forward_batch_slice
+    // returns), then the head only when logits or greedy tokens are asked for
+    // (a prompt fed by feed(), smollm_chat.rs:3042-3106, keeps hidden states only)
+    float *xo = d_hidden_out ? d_hidden_out : xn;
+    if ((st = launch_norm(x, proj, m->residual_scale, m->output_norm, m->rms_eps, dim, xo, nullptr, s, nt))) return st;
+    if (!d_logits && !d_greedy) return SG_OK;
+    if (batch_gemm) {
+        if ((st = launch_q8k_batch(xo, dim, nt, dim / 256, qb, s)) ||
+            (st = launch_gemm_batch(m->lm_head, m->lm_head_dtype == SG_Q4_K ? DT_Q4K : DT_Q6K, dim / 256, 0, m->vocab,
+                                    qb, nt, logits, lstride, false, s)))
+            return st;
+    } else if ((st = gemv_rows(m->lm_head, m->lm_head_dtype, m->vocab, dim, xo, ol, nt, s))) {
+        return st;
+    }
     ArgmaxArgs ga = {logits, m->vocab, nullptr, d_greedy, (unsigned long long *)(sc + L.amax),
                      (unsigned *)(sc + L.amax + n_max * ARGMAX_CTAS * 8), 1, lstride};
     if (d_greedy) CK(launch_pdl((const void *)argmax_kernel, dim3(ARGMAX_CTAS, nt), ARGMAX_THREADS, 0, s, &ga));
@@ -1835,9 +1964,12 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
             return st;
         }
         if ((st = gemv_image(y.wv, y.wv_dtype, kv_dim, dim, qx, v, s))) return st;
+        // one CTA per head: as many chunk buffers as fit, so that every K and V
+        // chunk of a short context is in flight before the dependency wait
+        const uint32_t nbuf = attn_smem_bytes(hd, m->max_seq, ATTN_MAX_BUF) <= 227 * 1024 ? ATTN_MAX_BUF : 2u;
         AttnArgs aa = {q, k, v, y.q_norm, y.k_norm, m->rms_eps, freqs, hd, m->n_heads, m->n_kv_heads, m->max_seq,
-                       m->rope_neox, scale, d_state, kc + l * cache, vc + l * cache, att};
-        CK(launch_pdl(attn_fn, m->n_heads, attn_threads(hd), attn_smem_bytes(hd, m->max_seq), s, &aa));
+                       m->rope_neox, scale, d_state, kc + l * cache, vc + l * cache, att, 0, 0, nbuf};
+        CK(launch_pdl(attn_fn, m->n_heads, attn_threads(hd), attn_smem_bytes(hd, m->max_seq, nbuf), s, &aa));
         {
             float *outs[1] = {proj};
             if ((st = launch_tiled(y.wo, y.wo_dtype == SG_Q4_K ? DT_Q4K : DT_Q6K, q_dim / 256, nullptr, att, q_dim,

@@ -198,63 +198,73 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
     const uint32_t nwarps = blockDim.x / 32, pos = prep ? (uint32_t)a.state[0] + blockIdx.y : (uint32_t)a.state[1];
     const uint32_t T = pos + 1;
     const uint32_t msq = attn_seq4(a.max_seq);
-    if (a.head_dim != HD || pos >= a.max_seq || attn_smem_bytes(HD, a.max_seq) > dynamic_smem_size() ||
+    const uint32_t NB = a.nbuf;
+    if (a.head_dim != HD || pos >= a.max_seq || NB < 2 || NB > ATTN_MAX_BUF ||
+        attn_smem_bytes(HD, a.max_seq, NB) > dynamic_smem_size() ||
         blockDim.x != attn_threads(HD) || a.n_heads % a.n_kv) {
         grid_dependency_wait();
         if (tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
         return;
     }
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm8);       // [0] K rows, [1] V rows
-    float *lsh = reinterpret_cast<float *>(sm8 + 16);          // 1/l, then inv_q, inv_k
-    float *qs = reinterpret_cast<float *>(sm8 + 32);
+    float *lsh = reinterpret_cast<float *>(sm8 + 32);          // 1/l, then inv_q, inv_k
+    float *qs = reinterpret_cast<float *>(sm8 + 64);
     float *hs = qs + HD;                                       // q, then k, before RoPE
     float *sc = hs + 2 * HD, *al = sc + msq;
-    uint8_t *kbuf = reinterpret_cast<uint8_t *>(al + msq), *vbuf = kbuf + ATTN_CHUNK * RS;
-    uint16_t *kcur = reinterpret_cast<uint16_t *>(vbuf + ATTN_CHUNK * RS), *vcur = kcur + HD;
+    uint8_t *bufs = reinterpret_cast<uint8_t *>(al + msq);
+    uint16_t *kcur = reinterpret_cast<uint16_t *>(bufs + NB * ATTN_CHUNK * RS), *vcur = kcur + HD;
     const uint32_t kvh = h / (a.n_heads / a.n_kv), kv_dim = a.n_kv * HD;
     const uint16_t *kg = a.kc + kvh * HD, *vg = a.vc + kvh * HD;
 
-    // rows [c0, c1) of the earlier positions into the K (which = 0) or V
-    // buffer; staged[which] counts the copies issued (every thread alike)
+    // Rows of the earlier positions move in items: K chunks 0..nc-1, then V
+    // chunks 0..nc-1 (ATTN_CHUNK positions each).  Item i goes to buffer
+    // i % NB and completes on bars[i % NB]; items i + 1 .. i + NB - 1 are in
+    // flight while item i is used.  Items whose rows all come from registers
+    // (the current position) issue no copy; iss / wtd count the phases of
+    // each barrier (every thread alike).
+    const uint32_t cached = prep ? T : pos;  // rows copied from the caches: [0, cached)
+    const uint32_t nc = (T + ATTN_CHUNK - 1) / ATTN_CHUNK, nitems = 2 * nc;
     bool ok = true;
-    uint32_t staged[2] = {0, 0};
-    auto stage = [&](uint32_t which, uint32_t c0, uint32_t c1) {
-        if (c1 <= c0 || !ok) return;
-        staged[which]++;
-        if (warp != 0) return;
-        if (lane == 0) mbar_arrive_expect_tx(&bars[which], (c1 - c0) * 2 * HD);
-        __syncwarp();
-        const uint16_t *src = which ? vg : kg;
-        uint8_t *dst = which ? vbuf : kbuf;
-        for (uint32_t t = c0 + lane; t < c1; t += 32) bulk_g2s(dst + (t - c0) * RS, src + (uint64_t)t * kv_dim, 2 * HD, &bars[which]);
+    uint32_t iss[ATTN_MAX_BUF] = {0, 0, 0, 0}, wtd[ATTN_MAX_BUF] = {0, 0, 0, 0};
+    auto rows_of = [&](uint32_t it, uint32_t &c0, uint32_t &cend) {
+        c0 = (it < nc ? it : it - nc) * ATTN_CHUNK;
+        cend = c0 + ATTN_CHUNK < cached ? c0 + ATTN_CHUNK : cached;
     };
-    auto wait_rows = [&](uint32_t which, uint32_t phase) {
-        if (!ok) return;
-        if (!mbar_wait_bounded(&bars[which], phase & 1u, WAIT_LIMIT_NS)) {
+    auto issue = [&](uint32_t it) {
+        uint32_t c0, cend;
+        rows_of(it, c0, cend);
+        if (it >= nitems || cend <= c0 || !ok) return;
+        const uint32_t b = it % NB;
+        iss[b]++;
+        if (warp != 0) return;
+        if (lane == 0) mbar_arrive_expect_tx(&bars[b], (cend - c0) * 2 * HD);
+        __syncwarp();
+        const uint16_t *src = it < nc ? kg : vg;
+        uint8_t *dst = bufs + b * ATTN_CHUNK * RS;
+        for (uint32_t t = c0 + lane; t < cend; t += 32) bulk_g2s(dst + (t - c0) * RS, src + (uint64_t)t * kv_dim, 2 * HD, &bars[b]);
+    };
+    auto wait_item = [&](uint32_t it) {
+        uint32_t c0, cend;
+        rows_of(it, c0, cend);
+        if (cend <= c0 || !ok) return;
+        const uint32_t b = it % NB;
+        if (!mbar_wait_bounded(&bars[b], wtd[b]++ & 1u, WAIT_LIMIT_NS)) {
             ok = false;
             if (lane == 0) atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_TMA);
         }
     };
     if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+        for (uint32_t b = 0; b < NB; b++) mbar_init(&bars[b], 1);
         fence_mbar_init();
     }
     __syncthreads();
-    // rows copied from the caches: [0, pos) here (this position's come from
-    // registers), [0, T) in the prepared batch form
-    const uint32_t cached = prep ? T : pos;
-    const uint32_t first = cached < ATTN_CHUNK ? cached : ATTN_CHUNK;
-    if (!prep) {  // earlier steps wrote these rows: copy them before waiting
-        stage(0, 0, first);
-        stage(1, 0, first);
-    }
+    if (!prep)  // earlier steps wrote these rows: copy them before waiting
+        for (uint32_t it = 0; it < NB; it++) issue(it);
 
     grid_dependency_wait();
     grid_launch_dependents();
     if (prep) {  // the kernel before this one wrote the batch's rows
-        stage(0, 0, first);
-        stage(1, 0, first);
+        for (uint32_t it = 0; it < NB; it++) issue(it);
         for (uint32_t d = tid; d < HD; d += blockDim.x) qs[d] = a.q[(uint64_t)blockIdx.y * a.q_stride + h * HD + d];
     }
     if (!prep) {
@@ -306,25 +316,27 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
 
     // ---- scores, chunk by chunk: 8 lanes per position (the 8 AVX lanes) ----
     const uint32_t grp = lane >> 3, l8 = lane & 7u;
-    uint32_t kph = 0;
-    for (uint32_t c0 = 0; c0 < T; c0 += ATTN_CHUNK) {
-        const uint32_t cn = T - c0 < ATTN_CHUNK ? T - c0 : ATTN_CHUNK;
-        const uint32_t cend = c0 + ATTN_CHUNK < cached ? c0 + ATTN_CHUNK : cached;  // rows copied: [c0, cend)
-        if (c0 > 0) {
-            __syncthreads();  // the previous chunk's rows are read
-            stage(0, c0, cend);
+    for (uint32_t c = 0; c < nc; c++) {
+        const uint32_t c0 = c * ATTN_CHUNK, cn = T - c0 < ATTN_CHUNK ? T - c0 : ATTN_CHUNK;
+        uint8_t *buf = bufs + (c % NB) * ATTN_CHUNK * RS;
+        if (c > 0) {
+            // item c - 1 is read (and this position's row, written by the
+            // threads, is ordered before the copies that reuse its buffer)
+            fence_proxy_async();
+            __syncthreads();
+            issue(c + NB - 1);
         }
-        if (cend > c0) wait_rows(0, kph++);
+        wait_item(c);
         if (!prep && pos < c0 + cn) {
             for (uint32_t d = tid; d < HD; d += blockDim.x)
-                reinterpret_cast<uint16_t *>(kbuf + (pos - c0) * RS)[d] = kcur[d];
+                reinterpret_cast<uint16_t *>(buf + (pos - c0) * RS)[d] = kcur[d];
         }
         __syncthreads();
         for (uint32_t t0 = warp * 4; t0 < cn; t0 += nwarps * 4) {
             const uint32_t t = t0 + grp;
             float acc = 0.0f;
             if (t < cn && ok) {
-                const uint16_t *kr = reinterpret_cast<const uint16_t *>(kbuf + t * RS);
+                const uint16_t *kr = reinterpret_cast<const uint16_t *>(buf + t * RS);
 #pragma unroll
                 for (uint32_t i = 0; i < HD / 8; i++)
                     acc = __fmaf_rn(__half2float(__ushort_as_half(kr[8 * i + l8])), qs[8 * i + l8], acc);
@@ -337,14 +349,27 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
         }
     }
     __syncthreads();
-    // the next V chunk can land while the maxima are formed
-    uint32_t vph = 0;
-    // ---- running maxima (f32::max ignores NaN: any grouping gives the same), by warp 0 ----
-    if (warp == 0) {
+    // ---- running maxima (f32::max ignores NaN: any grouping gives the same),
+    // over all warps: warp w takes positions [w*seg, (w+1)*seg); its carry-in
+    // is the maximum of the segments before it ----
+    {
+        float *segmax = hs;  // free after RoPE
+        const uint32_t seg = ((T + nwarps - 1) / nwarps + 31) & ~31u;
+        const uint32_t s0 = warp * seg, s1 = s0 + seg < T ? s0 + seg : T;
+        float mw = -INFINITY;
+        for (uint32_t t = s0 + lane; t < s1; t += 32) {
+            const float v = sc[t];
+            if (!isnan(v)) mw = fmaxf(mw, v);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, o));
+        if (lane == 0) segmax[warp] = mw;
+        __syncthreads();
         float carry = -INFINITY;
-        for (uint32_t t0 = 0; t0 < T; t0 += 32) {
+        for (uint32_t w = 0; w < warp; w++) carry = fmaxf(carry, segmax[w]);
+        for (uint32_t t0 = s0; t0 < s1; t0 += 32) {
             const uint32_t t = t0 + lane;
-            float m = t < T ? sc[t] : -INFINITY;
+            float m = t < s1 ? sc[t] : -INFINITY;
             if (isnan(m)) m = -INFINITY;  // f32::max(prev, NaN) = prev
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -354,7 +379,7 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
             m = fmaxf(m, carry);
             const float prev = __shfl_up_sync(0xffffffffu, m, 1);
             const float mprev = lane == 0 ? carry : prev;
-            if (t < T) {
+            if (t < s1) {
                 // alpha_t = exp(m_{t-1} - m_t), p_t = exp(s_t - m_t)
                 al[t] = expf_cr(__fsub_rn(mprev, m));
                 sc[t] = expf_cr(__fsub_rn(sc[t], m));
@@ -364,19 +389,20 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
     }
     // ---- the two recurrences, chunk by chunk over V ----
     float acc = 0.0f, l = 0.0f;
-    for (uint32_t c0 = 0; c0 < T; c0 += ATTN_CHUNK) {
-        const uint32_t cn = T - c0 < ATTN_CHUNK ? T - c0 : ATTN_CHUNK;
-        const uint32_t cend = c0 + ATTN_CHUNK < cached ? c0 + ATTN_CHUNK : cached;
-        __syncthreads();  // maxima done; the previous chunk's rows are read
-        if (c0 > 0) stage(1, c0, cend);
-        if (cend > c0) wait_rows(1, vph++);
+    for (uint32_t c = 0; c < nc; c++) {
+        const uint32_t it = nc + c, c0 = c * ATTN_CHUNK, cn = T - c0 < ATTN_CHUNK ? T - c0 : ATTN_CHUNK;
+        uint8_t *buf = bufs + (it % NB) * ATTN_CHUNK * RS;
+        fence_proxy_async();
+        __syncthreads();  // maxima done; item it - 1 is read: its buffer takes item it + NB - 1
+        issue(it + NB - 1);
+        wait_item(it);
         if (!prep && pos < c0 + cn) {
             for (uint32_t d = tid; d < HD; d += blockDim.x)
-                reinterpret_cast<uint16_t *>(vbuf + (pos - c0) * RS)[d] = vcur[d];
+                reinterpret_cast<uint16_t *>(buf + (pos - c0) * RS)[d] = vcur[d];
         }
         __syncthreads();
         if (tid < HD && ok) {
-            const uint16_t *vr = reinterpret_cast<const uint16_t *>(vbuf) + tid;
+            const uint16_t *vr = reinterpret_cast<const uint16_t *>(buf) + tid;
 #pragma unroll 8
             for (uint32_t t = 0; t < cn; t++)
                 acc = __fmaf_rn(sc[c0 + t], __half2float(__ushort_as_half(vr[t * (RS / 2)])), __fmul_rn(acc, al[c0 + t]));
@@ -387,8 +413,8 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
     if (tid == HD) lsh[0] = __fdiv_rn(1.0f, l > 1e-9f ? l : 1e-9f);  // 1 / l.max(1e-9): a NaN l gives 1e-9
     if (!ok && warp == 0) {
         // a wait gave up: let the copies still in flight land (bounded) before the CTA exits
-        for (uint32_t w = 0; w < 2; w++)
-            if (staged[w]) mbar_wait_bounded(&bars[w], (staged[w] - 1) & 1u, WAIT_LIMIT_NS);
+        for (uint32_t b = 0; b < NB; b++)
+            if (iss[b]) mbar_wait_bounded(&bars[b], (iss[b] - 1) & 1u, WAIT_LIMIT_NS);
     }
     __syncthreads();
     if (tid < HD)

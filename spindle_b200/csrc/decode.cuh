@@ -98,6 +98,7 @@ struct AttnArgs {
     // K/V rows already in the caches; out at out + blockIdx.y * n_heads * head_dim
     uint32_t prepared;
     uint64_t q_stride;
+    uint32_t nbuf;              // chunk buffers in shared memory (2..ATTN_MAX_BUF)
 };
 
 // The greedy token (f32::total_cmp, last maximum on ties), written as the next
@@ -124,11 +125,13 @@ constexpr uint32_t ATTN_ROW_PAD = 16;
 
 __host__ __device__ inline uint32_t attn_threads(uint32_t head_dim) { return head_dim < 256 ? 256u : 288u; }
 
-// bars, 1/l, inverse norms | q | q, k before RoPE | scores, then p | alpha |
-// K rows | V rows | this position's K, V (f16); every part 16-byte aligned
+constexpr uint32_t ATTN_MAX_BUF = 4;
+// bars (32 B), 1/l and the inverse norms (16 B), pad | q | q, k before RoPE |
+// scores, then p | alpha | nbuf chunk buffers of K or V rows | this
+// position's K, V (f16); every part 16-byte aligned
 __host__ __device__ inline uint32_t attn_seq4(uint32_t max_seq) { return (max_seq + 3u) & ~3u; }
-__host__ __device__ inline uint32_t attn_smem_bytes(uint32_t head_dim, uint32_t max_seq) {
-    return 32u + 3u * head_dim * 4u + 2u * attn_seq4(max_seq) * 4u + 2u * ATTN_CHUNK * (2u * head_dim + ATTN_ROW_PAD) +
+__host__ __device__ inline uint32_t attn_smem_bytes(uint32_t head_dim, uint32_t max_seq, uint32_t nbuf) {
+    return 64u + 3u * head_dim * 4u + 2u * attn_seq4(max_seq) * 4u + nbuf * ATTN_CHUNK * (2u * head_dim + ATTN_ROW_PAD) +
            2u * head_dim * 2u;
 }
 

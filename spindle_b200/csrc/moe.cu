@@ -6,11 +6,12 @@
 namespace sg {
 using namespace tiled;
 
-__global__ void __launch_bounds__(ROUTER_MAX_ROWS * 8) moe_router_kernel(const __grid_constant__ RouterArgs a) {
+__global__ void __launch_bounds__(ROUTER_MAX_THREADS) moe_router_kernel(const __grid_constant__ RouterArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t tid = threadIdx.x, dim = a.dim;
     const bool gate_cta = blockIdx.x == a.row_ctas;
-    if (router_smem_bytes(dim, a.rows_per_cta) > dynamic_smem_size() || dim % 8 || a.rows_per_cta == 0 ||
+    if (router_smem_bytes(dim, a.rows_per_cta, a.tok_chunk) > dynamic_smem_size() || dim % 8 || a.rows_per_cta == 0 ||
+        a.tok_chunk == 0 ||
         a.rows_per_cta > ROUTER_MAX_ROWS || blockDim.x < 8 * a.rows_per_cta || (blockDim.x & 31) ||
         a.row_ctas * a.rows_per_cta < a.n_expert || (a.row_ctas - 1) * a.rows_per_cta >= a.n_expert ||
         blockIdx.x > a.row_ctas || (gate_cta && !a.shared_scale) || a.n_tok == 0 || (a.n_tok > 1 && a.ldx < dim)) {
@@ -20,7 +21,7 @@ __global__ void __launch_bounds__(ROUTER_MAX_ROWS * 8) moe_router_kernel(const _
     grid_launch_dependents();
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);  // [0]: rows (or the gate vector), [1]: x
     float *xs = reinterpret_cast<float *>(smem + 64);
-    uint8_t *rows = smem + 64 + dim * 4u;
+    uint8_t *rows = smem + 64 + a.tok_chunk * dim * 4u;
     const uint32_t rstride = router_row_stride(dim), rowb = dim * 4u;
     const uint32_t e0 = blockIdx.x * a.rows_per_cta;
     const uint32_t nrows = gate_cta ? 0u : min(a.rows_per_cta, a.n_expert - e0);
@@ -39,72 +40,87 @@ __global__ void __launch_bounds__(ROUTER_MAX_ROWS * 8) moe_router_kernel(const _
         }
     }
     grid_dependency_wait();
-    const uint32_t nb = dim / 256;
+    const uint32_t nb = dim / 256, tc = a.tok_chunk;
+    const uint32_t nwarps = blockDim.x >> 5, warp = tid >> 5, lane = tid & 31u;
     bool ok = true;
-    for (uint32_t t = 0; t < a.n_tok; t++) {
-        // token t's x (the rows stay), one token after the other
+    // tok_chunk tokens at a time: their x staged together (the rows stay)
+    for (uint32_t c = 0, t0 = 0; t0 < a.n_tok; c++, t0 += tc) {
+        const uint32_t nt = min(tc, a.n_tok - t0);
         if (tid == 0) {
-            mbar_arrive_expect_tx(&bars[1], rowb);
-            bulk_g2s(xs, a.x + (uint64_t)t * a.ldx, rowb, &bars[1]);
+            mbar_arrive_expect_tx(&bars[1], nt * rowb);
+            for (uint32_t u = 0; u < nt; u++) bulk_g2s(xs + u * dim, a.x + (uint64_t)(t0 + u) * a.ldx, rowb, &bars[1]);
         }
         __syncthreads();
-        bool okt = mbar_wait_bounded(&bars[1], t & 1u, WAIT_LIMIT_NS);
-        if (t == 0 && loads) ok = mbar_wait_bounded(&bars[0], 0, WAIT_LIMIT_NS);
+        bool okt = mbar_wait_bounded(&bars[1], c & 1u, WAIT_LIMIT_NS);
+        if (c == 0 && loads) ok = mbar_wait_bounded(&bars[0], 0, WAIT_LIMIT_NS);
         okt = okt && ok;
         if (!okt && tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_TMA);
-        // x's Q8_K image for the expert GEMVs (the layout they stage in shared
-        // memory: qs | bsums | d), one 256-block per CTA and warp 0
-        if (a.qx && okt && tid < 32) {
-            uint8_t *qx = a.qx + (uint64_t)t * act_bytes(nb);
-            for (uint32_t b = blockIdx.x; b < nb; b += gridDim.x)
-                q8k_block(xs + 256u * b, reinterpret_cast<int8_t *>(qx + 256u * b),
+        // the tokens' Q8_K images for the expert GEMVs (the layout they stage in
+        // shared memory: qs | bsums | d): (token, 256-block) pairs over the
+        // grid's warps
+        if (a.qx && okt) {
+            for (uint32_t p = blockIdx.x * nwarps + warp; p < nt * nb; p += gridDim.x * nwarps) {
+                const uint32_t u = p / nb, b = p - u * nb;
+                uint8_t *qx = a.qx + (uint64_t)(t0 + u) * act_bytes(nb);
+                q8k_block(xs + u * dim + 256u * b, reinterpret_cast<int8_t *>(qx + 256u * b),
                           reinterpret_cast<int16_t *>(qx + 256u * nb + 32u * b),
-                          reinterpret_cast<float *>(qx + 288u * nb + 4u * b), tid);
+                          reinterpret_cast<float *>(qx + 288u * nb + 4u * b), lane);
+            }
         }
         if (gate_cta) {
             // The shared expert's gate: sigmoid(sum over c of w[c] * x[c]), summed
-            // in order as the reference's iterator does (smollm_chat.rs:1374-1377).
-            if (tid == 0) {
+            // in order as the reference's iterator does (smollm_chat.rs:1374-1377);
+            // one thread per token.
+            for (uint32_t u = tid; u < nt; u += blockDim.x) {
                 float gsc = 1.0f;
                 if (want_gate) {
                     if (okt) {
                         const float *gv = reinterpret_cast<const float *>(rows);
+                        const float *xv = xs + u * dim;
                         float z = 0.0f;
 #pragma unroll 8
-                        for (uint32_t c = 0; c < dim; c++) z = __fadd_rn(z, __fmul_rn(gv[c], xs[c]));
+                        for (uint32_t k = 0; k < dim; k++) z = __fadd_rn(z, __fmul_rn(gv[k], xv[k]));
                         gsc = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-z)));
                     } else {
                         gsc = __int_as_float(0x7fc00000);
                     }
                 }
-                a.shared_scale[t] = gsc;
-                if (t == 0) {
-                    sg_moe_choice *c = a.shared_sel;
-                    for (uint32_t i = 0; i < MOE_MAXK; i++) {
-                        c->id[i] = 0;
-                        c->weight[i] = i == 0 ? 1.0f : 0.0f;
-                    }
-                    c->pad_[0] = c->pad_[1] = c->pad_[2] = 0;
-                    c->n = 1;
+                a.shared_scale[t0 + u] = gsc;
+            }
+            if (tid == 0 && c == 0) {
+                sg_moe_choice *ch = a.shared_sel;
+                for (uint32_t i = 0; i < MOE_MAXK; i++) {
+                    ch->id[i] = 0;
+                    ch->weight[i] = i == 0 ? 1.0f : 0.0f;
                 }
+                ch->pad_[0] = ch->pad_[1] = ch->pad_[2] = 0;
+                ch->n = 1;
             }
         } else {
-            // thread j of row q: the FMA chain of AVX lane j (elements j, j+8, ...)
-            const uint32_t q = tid >> 3, j = tid & 7u;
-            float acc = 0.0f;
-            if (q < nrows && okt) {
-                const float *row = reinterpret_cast<const float *>(rows + q * rstride);
+            // 8 threads per (row q, token u): thread j runs the FMA chain of AVX
+            // lane j (elements j, j+8, ...); the loop is uniform over the block
+            const uint32_t grp = tid >> 3, j = tid & 7u, ngrp = blockDim.x >> 3, npairs = nrows * nt;
+            for (uint32_t p0 = 0; p0 < npairs; p0 += ngrp) {
+                const uint32_t p = p0 + grp;
+                const bool act = p < npairs;
+                const uint32_t q = act ? p / nt : 0u, u = act ? p - q * nt : 0u;
+                float acc = 0.0f;
+                if (act && okt) {
+                    const float *row = reinterpret_cast<const float *>(rows + q * rstride);
+                    const float *xv = xs + u * dim;
 #pragma unroll 8
-                for (uint32_t i = j; i < dim; i += 8) acc = __fmaf_rn(row[i], xs[i], acc);
+                    for (uint32_t i = j; i < dim; i += 8) acc = __fmaf_rn(row[i], xv[i], acc);
+                }
+                // hsum_avx2: ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7)), then + the empty tail (0.0)
+                const float tv = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+                const float uu = __fadd_rn(tv, __shfl_down_sync(0xffffffffu, tv, 1));
+                const float v = __fadd_rn(uu, __shfl_down_sync(0xffffffffu, uu, 2));
+                if (act && j == 0)
+                    a.logits[(uint64_t)(t0 + u) * a.n_expert + e0 + q] =
+                        okt ? __fadd_rn(v, 0.0f) : __int_as_float(0x7fc00000);
             }
-            // hsum_avx2: ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7)), then + the empty tail (0.0)
-            const float tv = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
-            const float u = __fadd_rn(tv, __shfl_down_sync(0xffffffffu, tv, 1));
-            const float v = __fadd_rn(u, __shfl_down_sync(0xffffffffu, u, 2));
-            if (q < nrows && j == 0)
-                a.logits[(uint64_t)t * a.n_expert + e0 + q] = okt ? __fadd_rn(v, 0.0f) : __int_as_float(0x7fc00000);
         }
-        __syncthreads();  // xs is rewritten for the next token
+        __syncthreads();  // xs is rewritten for the next chunk
     }
 }
 
@@ -172,30 +188,41 @@ __global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(
             o->pad_[0] = o->pad_[1] = o->pad_[2] = 0;
         }
     }
+    // slot bases (a prefix sum over the tokens), then every warp writes its
+    // tokens' slots
+    uint32_t *bases = reinterpret_cast<uint32_t *>(ch + a.n_tok);
     if (tid == 0) {
         uint32_t base = 0;
         for (uint32_t t = 0; t < a.n_tok; t++) {
-            const uint32_t n = min(ch[t].n, a.n_used);
-            a.slot_base[t] = base;
-            for (uint32_t i = 0; i < n; i++) {
-                a.slots[2 * (base + i)] = ch[t].id[i];
-                a.slots[2 * (base + i) + 1] = (int32_t)t;
-            }
-            base += n;
+            bases[t] = base;
+            base += min(ch[t].n, a.n_used);
         }
-        *a.n_slots = base;
+        bases[a.n_tok] = base;
+    }
+    __syncthreads();
+    for (uint32_t t = warp; t < a.n_tok; t += nwarps) {
+        const uint32_t n = min(ch[t].n, a.n_used), base = bases[t];
+        if (lane < n) {
+            a.slots[2 * (base + lane)] = ch[t].id[lane];
+            a.slots[2 * (base + lane) + 1] = (int32_t)t;
+        }
+        if (lane == 0) a.slot_base[t] = base;
+    }
+    if (tid == 0) {
+        *a.n_slots = bases[a.n_tok];
         if (a.slots_local) {
             // this rank's slots (expert parallelism), in global slot order
             uint32_t j = 0;
-            for (uint32_t q = 0; q < base; q++) {
-                const int32_t e = a.slots[2 * q];
-                if ((uint32_t)e >= a.ep_lo && (uint32_t)e < a.ep_hi) {
-                    a.slots_local[2 * j] = e - (int32_t)a.ep_lo;
-                    a.slots_local[2 * j + 1] = a.slots[2 * q + 1];
-                    a.slot_global[j] = q;
-                    j++;
+            for (uint32_t t = 0; t < a.n_tok; t++)
+                for (uint32_t i = 0; i < min(ch[t].n, a.n_used); i++) {
+                    const int32_t e = ch[t].id[i];
+                    if ((uint32_t)e >= a.ep_lo && (uint32_t)e < a.ep_hi) {
+                        a.slots_local[2 * j] = e - (int32_t)a.ep_lo;
+                        a.slots_local[2 * j + 1] = (int32_t)t;
+                        a.slot_global[j] = bases[t] + i;
+                        j++;
+                    }
                 }
-            }
             *a.n_local = j;
         }
         if (a.slots_sh) {

@@ -21,6 +21,7 @@ namespace sg {
 constexpr uint32_t ROUTER_MAX_EXPERTS = 4096;
 constexpr uint32_t ROUTER_ROW_PAD = 32;  // bytes between staged rows (spreads rows over banks)
 constexpr uint32_t ROUTER_MAX_ROWS = 16; // rows per CTA (8 threads each)
+constexpr uint32_t ROUTER_MAX_THREADS = 256;
 
 struct RouterArgs {
     const float *w;             // F32 [n_expert][dim]
@@ -36,6 +37,7 @@ struct RouterArgs {
     float *shared_scale;        // per token: sigmoid(shared_gate . x), or 1 without a gate
     uint32_t n_tok;             // tokens (1 for moe_forward)
     uint64_t ldx;
+    uint32_t tok_chunk;         // tokens staged in shared memory at a time
 };
 
 // Batched MoE (moe_forward_batch): every token's choice from its logits (one
@@ -61,7 +63,7 @@ struct SelectBatchArgs {
 };
 constexpr uint32_t SELECT_BATCH_THREADS = 1024;
 __host__ __device__ inline uint32_t select_batch_smem(uint32_t n_tok) {
-    return (SELECT_BATCH_THREADS / 32) * 256u * 4u + n_tok * (uint32_t)sizeof(moe::Choice);
+    return (SELECT_BATCH_THREADS / 32) * 256u * 4u + n_tok * (uint32_t)sizeof(moe::Choice) + (n_tok + 1u) * 4u;
 }
 
 struct CombineBatchArgs {
@@ -82,11 +84,11 @@ struct CombineBatchArgs {
     unsigned *epoch;
 };
 
-// bars (64) | x (dim floats) | rows (rows_per_cta, padded) ; the gate CTA puts
-// the gate vector where the rows go.
+// bars (64) | x of tok_chunk tokens (dim floats each) | rows (rows_per_cta,
+// padded) ; the gate CTA puts the gate vector where the rows go.
 __host__ __device__ inline uint32_t router_row_stride(uint32_t dim) { return dim * 4u + ROUTER_ROW_PAD; }
-__host__ __device__ inline uint32_t router_smem_bytes(uint32_t dim, uint32_t rows_per_cta) {
-    return 64u + dim * 4u + (rows_per_cta ? rows_per_cta : 1u) * router_row_stride(dim);
+__host__ __device__ inline uint32_t router_smem_bytes(uint32_t dim, uint32_t rows_per_cta, uint32_t tok_chunk) {
+    return 64u + (tok_chunk ? tok_chunk : 1u) * dim * 4u + (rows_per_cta ? rows_per_cta : 1u) * router_row_stride(dim);
 }
 
 struct CombineArgs {

@@ -201,11 +201,13 @@ class Decoder:
                                       C.c_void_p(greedy.data_ptr()), _stream(stream)), "sg_forward_batch")
         return lg, greedy
 
-    def forward_batch_range(self, pos0, l0, l1, tokens=None, hidden=None, n_max=64, stream=None):
+    def forward_batch_range(self, pos0, l0, l1, tokens=None, hidden=None, n_max=64, stream=None, head=True):
         """A pipeline stage: layers [l0, l1) for positions pos0 .. pos0 + n - 1.
         The first stage takes tokens, later ones the raw residual `hidden`
         (float32 CUDA [n, dim]); a middle stage returns the raw residual, the
-        last one (logits [n, vocab], greedy tokens int64 [n])."""
+        last one (logits [n, vocab], greedy tokens int64 [n]), or with
+        head=False the output-normed hidden states (forward_batch_slice's
+        return value) and no LM head."""
         L = _sigs()
         n = len(tokens) if tokens is not None else hidden.shape[0]
         if getattr(self, "_bscratch", None) is None or self._bn < n_max:
@@ -219,15 +221,30 @@ class Decoder:
         toks = None if tokens is None else torch.tensor(list(tokens), dtype=torch.int32, device=self.dev)
         pos = torch.tensor([pos0], dtype=torch.int32, device=self.dev)
         last = l1 == self.cfg["n_layers"]
-        out = None if last else torch.empty(n, self.cfg["dim"], dtype=torch.float32, device=self.dev)
-        lg = torch.empty(n, self.cfg["vocab"], dtype=torch.float32, device=self.dev) if last else None
-        greedy = torch.empty(n, dtype=torch.int64, device=self.dev) if last else None
+        with_head = last and head
+        out = None if with_head else torch.empty(n, self.cfg["dim"], dtype=torch.float32, device=self.dev)
+        lg = torch.empty(n, self.cfg["vocab"], dtype=torch.float32, device=self.dev) if with_head else None
+        greedy = torch.empty(n, dtype=torch.int64, device=self.dev) if with_head else None
         ptr = lambda t: None if t is None else C.c_void_p(t.data_ptr())
         _lib.check(L.sg_forward_batch_range(C.byref(self.model), l0, l1, ptr(toks), ptr(hidden), n, ptr(pos),
                                             ptr(self.kv), ptr(self._bscratch), self._bscratch.numel(), self._bn,
                                             ptr(out), ptr(lg), self.cfg["vocab"], ptr(greedy), _stream(stream)),
                    "sg_forward_batch_range")
-        return (out,) if not last else (lg, greedy)
+        return (lg, greedy) if with_head else (out,)
+
+    def feed(self, tokens, pos0=0, chunk=64, stream=None):
+        """feed (smollm_chat.rs:3042-3106): the prompt in chunks of `chunk`
+        positions (the reference uses 128; the batch path here takes up to 64),
+        K/V rows into the caches, no LM head; returns the last position's
+        output-normed hidden state (float32 CUDA [dim])."""
+        tokens = list(tokens)
+        last = None
+        for c0 in range(0, len(tokens), chunk):
+            part = tokens[c0:c0 + chunk]
+            (last,) = self.forward_batch_range(pos0 + c0, 0, self.cfg["n_layers"], tokens=part,
+                                               n_max=max(chunk, getattr(self, "_bn", 0) or 0), stream=stream,
+                                               head=False)
+        return None if last is None else last[-1]
 
     def generate(self, prompt, n_new):
         """Greedy decode: feed the prompt, then n_new tokens; returns the new tokens."""

@@ -82,3 +82,23 @@ def test_batch_moe_verify_chunks(dev):
     cfg = dict(U.MOE)
     toks = np.random.default_rng(8).integers(0, cfg["vocab"], 18).tolist()
     run(cfg, U.dtypes_for(cfg), 75, toks, [9, 9], dev)
+
+
+@pytest.mark.parametrize("kind", ["dense", "moe"])
+def test_feed_matches_steps(dev, kind):
+    # feed (smollm_chat.rs:3042-3106): chunks without the LM head; the last
+    # output-normed hidden state and every K/V row equal the one-token steps'
+    cfg = dict(U.DENSE if kind == "dense" else U.MOE, max_seq=160)
+    dtypes = U.dtypes_for(cfg)
+    dw = U.device_weights(U.host_weights(cfg, dtypes, seed=76), dev)
+    seq = Decoder(cfg, dw, dtypes, dev)
+    bat = Decoder(cfg, dw, dtypes, dev)
+    toks = np.random.default_rng(9).integers(0, cfg["vocab"], 150).tolist()
+    for pos, t in enumerate(toks):
+        seq.set_state(t, pos)
+        seq.step(logits=False)
+    h = bat.feed(toks, 0, chunk=64)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(h.cpu().numpy()), bits(seq.hidden.cpu().numpy()))
+    assert torch.equal(seq.kv, bat.kv)
+    __import__("spindle_b200").device_status()
