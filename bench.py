@@ -1197,7 +1197,7 @@ def run_gpu_prefill(args):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     name = "qwen3_30b_a3b"
-    n_prompt = 128 if args.profile else PREFILL_PROMPT
+    n_prompt = args.prompt if args.prompt else (128 if args.profile else PREFILL_PROMPT)
     cfg = dict(DECODE_MODELS[name], max_seq=n_prompt + 2 * VERIFY_N + 8)
     if args.profile:
         cfg["n_layers"] = 2  # profiling case: the model's first two layers, two chunks
@@ -1413,6 +1413,8 @@ def main():
                          "GPUs with the gather fused in; float: the float-path matvecs; moe: the Qwen3-30B-A3B "
                          "MoE layer; decode: greedy decode of a whole random-init model; prefill: a 2048-token prompt "
                          "through the batch forward, then N=9 verify passes")
+    ap.add_argument("--prompt", type=int, default=0,
+                    help="prefill workload: prompt length (default 2048; 128 with --profile)")
     ap.add_argument("--model", default="qwen3_30b_a3b", choices=sorted(DECODE_MODELS),
                     help="decode workload: the model architecture")
     args = ap.parse_args()

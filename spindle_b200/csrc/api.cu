@@ -1931,7 +1931,7 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
     EmbedArgs ea = {m->embed, m->embed_dtype, dim, m->vocab, m->embedding_scale, d_state, x};
     CK(launch_pdl((const void *)embed_kernel, (dim + 255) / 256, 256, 0, s, &ea));
     // an MoE layer's combine runs inside the norm that consumes its output
-    CombineArgs comb;
+    CombineArgs comb{};
     bool deferred = false;
     auto norm_after_ffn = [&](const float *w) {
         NormArgs a = {x, deferred ? nullptr : proj, m->residual_scale, w, m->rms_eps, dim, xn, qx};

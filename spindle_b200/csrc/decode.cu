@@ -206,7 +206,6 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
         if (tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
         return;
     }
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sm8);       // [0] K rows, [1] V rows
     float *lsh = reinterpret_cast<float *>(sm8 + 32);          // 1/l, then inv_q, inv_k
     float *qs = reinterpret_cast<float *>(sm8 + 64);
     float *hs = qs + HD;                                       // q, then k, before RoPE
@@ -218,46 +217,42 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
 
     // Rows of the earlier positions move in items: K chunks 0..nc-1, then V
     // chunks 0..nc-1 (ATTN_CHUNK positions each).  Item i goes to buffer
-    // i % NB and completes on bars[i % NB]; items i + 1 .. i + NB - 1 are in
-    // flight while item i is used.  Items whose rows all come from registers
-    // (the current position) issue no copy; iss / wtd count the phases of
-    // each barrier (every thread alike).
+    // i % NB; items i + 1 .. i + NB - 1 are in flight while item i is used.
+    // Every thread copies 16-byte pieces of the rows (cp.async, one commit
+    // group per item, empty for items whose rows all come from registers);
+    // waiting for item i = waiting until no more than the groups committed
+    // after it are pending, then a barrier.
     const uint32_t cached = prep ? T : pos;  // rows copied from the caches: [0, cached)
     const uint32_t nc = (T + ATTN_CHUNK - 1) / ATTN_CHUNK, nitems = 2 * nc;
-    bool ok = true;
-    uint32_t iss[ATTN_MAX_BUF] = {0, 0, 0, 0}, wtd[ATTN_MAX_BUF] = {0, 0, 0, 0};
-    auto rows_of = [&](uint32_t it, uint32_t &c0, uint32_t &cend) {
-        c0 = (it < nc ? it : it - nc) * ATTN_CHUNK;
-        cend = c0 + ATTN_CHUNK < cached ? c0 + ATTN_CHUNK : cached;
-    };
+    constexpr uint32_t SEGS = 2 * HD / 16;   // 16-byte pieces per row
+    uint32_t committed = 0;
     auto issue = [&](uint32_t it) {
-        uint32_t c0, cend;
-        rows_of(it, c0, cend);
-        if (it >= nitems || cend <= c0 || !ok) return;
-        const uint32_t b = it % NB;
-        iss[b]++;
-        if (warp != 0) return;
-        if (lane == 0) mbar_arrive_expect_tx(&bars[b], (cend - c0) * 2 * HD);
-        __syncwarp();
+        if (it >= nitems) return;
+        const uint32_t c0 = (it < nc ? it : it - nc) * ATTN_CHUNK;
+        const uint32_t cend = c0 + ATTN_CHUNK < cached ? c0 + ATTN_CHUNK : cached;
         const uint16_t *src = it < nc ? kg : vg;
-        uint8_t *dst = bufs + b * ATTN_CHUNK * RS;
-        for (uint32_t t = c0 + lane; t < cend; t += 32) bulk_g2s(dst + (t - c0) * RS, src + (uint64_t)t * kv_dim, 2 * HD, &bars[b]);
+        uint8_t *dst = bufs + (it % NB) * ATTN_CHUNK * RS;
+        const uint32_t n = cend > c0 ? (cend - c0) * SEGS : 0u;
+        for (uint32_t u = tid; u < n; u += blockDim.x) {
+            const uint32_t row = u / SEGS, sg = u - row * SEGS;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst + row * RS + 16 * sg)),
+                         "l"(src + (uint64_t)(c0 + row) * kv_dim + 8 * sg)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        committed++;
     };
     auto wait_item = [&](uint32_t it) {
-        uint32_t c0, cend;
-        rows_of(it, c0, cend);
-        if (cend <= c0 || !ok) return;
-        const uint32_t b = it % NB;
-        if (!mbar_wait_bounded(&bars[b], wtd[b]++ & 1u, WAIT_LIMIT_NS)) {
-            ok = false;
-            if (lane == 0) atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_TMA);
-        }
+        const uint32_t after = committed - (it + 1);  // groups committed after item it's
+        if (after == 0)
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        else if (after == 1)
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        else if (after == 2)
+            asm volatile("cp.async.wait_group 2;" ::: "memory");
+        else
+            asm volatile("cp.async.wait_group 3;" ::: "memory");
     };
-    if (tid == 0) {
-        for (uint32_t b = 0; b < NB; b++) mbar_init(&bars[b], 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
     if (!prep)  // earlier steps wrote these rows: copy them before waiting
         for (uint32_t it = 0; it < NB; it++) issue(it);
 
@@ -320,10 +315,7 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
         const uint32_t c0 = c * ATTN_CHUNK, cn = T - c0 < ATTN_CHUNK ? T - c0 : ATTN_CHUNK;
         uint8_t *buf = bufs + (c % NB) * ATTN_CHUNK * RS;
         if (c > 0) {
-            // item c - 1 is read (and this position's row, written by the
-            // threads, is ordered before the copies that reuse its buffer)
-            fence_proxy_async();
-            __syncthreads();
+            __syncthreads();  // item c - 1 is read: its buffer takes item c + NB - 1
             issue(c + NB - 1);
         }
         wait_item(c);
@@ -335,7 +327,7 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
         for (uint32_t t0 = warp * 4; t0 < cn; t0 += nwarps * 4) {
             const uint32_t t = t0 + grp;
             float acc = 0.0f;
-            if (t < cn && ok) {
+            if (t < cn) {
                 const uint16_t *kr = reinterpret_cast<const uint16_t *>(buf + t * RS);
 #pragma unroll
                 for (uint32_t i = 0; i < HD / 8; i++)
@@ -392,7 +384,6 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
     for (uint32_t c = 0; c < nc; c++) {
         const uint32_t it = nc + c, c0 = c * ATTN_CHUNK, cn = T - c0 < ATTN_CHUNK ? T - c0 : ATTN_CHUNK;
         uint8_t *buf = bufs + (it % NB) * ATTN_CHUNK * RS;
-        fence_proxy_async();
         __syncthreads();  // maxima done; item it - 1 is read: its buffer takes item it + NB - 1
         issue(it + NB - 1);
         wait_item(it);
@@ -401,7 +392,7 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
                 reinterpret_cast<uint16_t *>(buf + (pos - c0) * RS)[d] = vcur[d];
         }
         __syncthreads();
-        if (tid < HD && ok) {
+        if (tid < HD) {
             const uint16_t *vr = reinterpret_cast<const uint16_t *>(buf) + tid;
 #pragma unroll 8
             for (uint32_t t = 0; t < cn; t++)
@@ -411,14 +402,9 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
         }
     }
     if (tid == HD) lsh[0] = __fdiv_rn(1.0f, l > 1e-9f ? l : 1e-9f);  // 1 / l.max(1e-9): a NaN l gives 1e-9
-    if (!ok && warp == 0) {
-        // a wait gave up: let the copies still in flight land (bounded) before the CTA exits
-        for (uint32_t b = 0; b < NB; b++)
-            if (iss[b]) mbar_wait_bounded(&bars[b], (iss[b] - 1) & 1u, WAIT_LIMIT_NS);
-    }
     __syncthreads();
     if (tid < HD)
-        a.out[(uint64_t)blockIdx.y * a.n_heads * HD + h * HD + tid] = ok ? __fmul_rn(acc, lsh[0]) : __int_as_float(0x7fc00000);
+        a.out[(uint64_t)blockIdx.y * a.n_heads * HD + h * HD + tid] = __fmul_rn(acc, lsh[0]);
 }
 
 template __global__ void attention_kernel<64>(const __grid_constant__ AttnArgs);

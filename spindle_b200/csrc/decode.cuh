@@ -126,7 +126,7 @@ constexpr uint32_t ATTN_ROW_PAD = 16;
 __host__ __device__ inline uint32_t attn_threads(uint32_t head_dim) { return head_dim < 256 ? 256u : 288u; }
 
 constexpr uint32_t ATTN_MAX_BUF = 4;
-// bars (32 B), 1/l and the inverse norms (16 B), pad | q | q, k before RoPE |
+// reserved (32 B), 1/l and the inverse norms (16 B), pad | q | q, k before RoPE |
 // scores, then p | alpha | nbuf chunk buffers of K or V rows | this
 // position's K, V (f16); every part 16-byte aligned
 __host__ __device__ inline uint32_t attn_seq4(uint32_t max_seq) { return (max_seq + 3u) & ~3u; }

@@ -151,7 +151,7 @@ __global__ void moe_combine_kernel(const __grid_constant__ CombineArgs a) {
 // order.  Bit for bit the choices of one-token steps (moe_forward_batch takes
 // each token's top-k on its own, smollm_chat.rs:958-1010).
 __global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(const __grid_constant__ SelectBatchArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
     grid_dependency_wait();
     grid_launch_dependents();
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5, nwarps = blockDim.x / 32;
