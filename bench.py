@@ -1165,6 +1165,7 @@ def run_gpu_decode(args):
 PREFILL_PROMPT = 2048
 PREFILL_CHUNK = 64
 VERIFY_N = 9
+SPEC_TOKENS = 64
 
 
 def active_params(cfg):
@@ -1198,7 +1199,7 @@ def run_gpu_prefill(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     name = "qwen3_30b_a3b"
     n_prompt = args.prompt if args.prompt else (128 if args.profile else PREFILL_PROMPT)
-    cfg = dict(DECODE_MODELS[name], max_seq=n_prompt + 2 * VERIFY_N + 8)
+    cfg = dict(DECODE_MODELS[name], max_seq=n_prompt + SPEC_TOKENS + 2 * VERIFY_N + 8)
     if args.profile:
         cfg["n_layers"] = 2  # profiling case: the model's first two layers, two chunks
     dtypes = qwen3_dtypes(cfg, embed=Q4_K)
@@ -1307,6 +1308,45 @@ def run_gpu_prefill(args):
         b1.record(s)
         b1.synchronize()
         e2e_ms = b0.elapsed_time(b1) / n_e2e
+        # speculative decode after the prompt (the rest of configs[4]): SPEC_TOKENS
+        # tokens with drafts of 8 whose first A tokens are the model's own
+        # continuation (A uniform in 0..k, seeded: 50% of drafted tokens right
+        # on average), the rest wrong; against the same tokens one position
+        # per call through the same batch path.  Host-driven loops, timed by
+        # the wall clock with a device sync on both sides.
+        from spindle_b200.spec import speculative_decode
+        torch.cuda.synchronize()
+        tok0, p_ = int(greedy[0].item()), n_prompt
+        want, t_ = [], tok0
+        t0 = time.perf_counter()
+        for _ in range(SPEC_TOKENS):
+            want.append(t_)
+            _, g1 = dec.forward_batch([t_], p_, logits=False, n_max=C_)
+            t_, p_ = int(g1[0].item()), p_ + 1
+        torch.cuda.synchronize()
+        plain_s = time.perf_counter() - t0
+        rs = __import__("numpy").random.default_rng(1234 + rank)
+
+        def drafter(ctx, k):
+            m = len(ctx) - n_prompt          # tokens generated so far (the pending one included)
+            right = want[m:m + k]
+            a = int(rs.integers(0, len(right) + 1))
+            return right[:a] + [(t + 1) % cfg["vocab"] for t in right[a:]]
+
+        st = {}
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        got = speculative_decode(dec, tok0, n_prompt, SPEC_TOKENS, h_tok[:n_prompt].tolist(), draft_len=8,
+                                 drafter=drafter, n_max=C_, stats=st)
+        torch.cuda.synchronize()
+        spec_s = time.perf_counter() - t0
+        spec = {"tokens": SPEC_TOKENS, "positions": "%d..%d" % (n_prompt, n_prompt + SPEC_TOKENS - 1),
+                "tok_per_s": round(SPEC_TOKENS / spec_s, 1), "plain_tok_per_s": round(SPEC_TOKENS / plain_s, 1),
+                "passes": st["passes"], "single_steps": st["steps"],
+                "accept_rate": round(st["accepted"] / max(st["drafted"], 1), 3),
+                "identical_to_plain": got == want,
+                "how": "spindle_b200.spec.speculative_decode (drafts of 8, verify passes through sg_forward_batch) "
+                       "vs one position per sg_forward_batch call; wall clock, host-synchronous loops"}
         if world > 1:
             t = torch.tensor([ms, v_ms, e2e_ms], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -1341,6 +1381,7 @@ def run_gpu_prefill(args):
                            "tok_per_s_if_all_accepted": round(VERIFY_N * 1e3 / v_ms, 1),
                            "tok_per_s_at_half_acceptance": round((1 + (VERIFY_N - 1) // 2) * 1e3 / v_ms, 1),
                            "how": "forward_batch + LM head + argmax for 9 positions after the prompt, graph replays"},
+                "spec_decode": spec,
                 "e2e": {"value": round(n_prompt * world / (e2e_ms * 1e-3), 1), "unit": "tok/s",
                         "h2d_bytes_per_step": tok_bytes + pos_bytes, "d2h_bytes_per_step": 8,
                         "how": "sg_memcpy_h2d of the prompt tokens and chunk positions from pinned host, the "
@@ -1442,6 +1483,8 @@ def main():
     if args.workload == "prefill":
         if args.steps == 20000:
             args.steps = 3  # one step is a whole 2048-token prompt
+        if args.warmup == 20:
+            args.warmup = 3
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "prefill reference arm: the oracle forward runs "
                               "about 1 token/s on one core; the decode line's cpu_baseline covers it"}), flush=True)
