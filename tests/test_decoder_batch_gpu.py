@@ -68,6 +68,14 @@ def test_batch_variants(dev):
     cfg = dict(U.DENSE, n_heads=4, n_kv_heads=2, head_dim=256)
     toks = np.random.default_rng(6).integers(0, cfg["vocab"], 20).tolist()
     run(cfg, U.dtypes_for(cfg), 73, toks, [5, 15], dev)
+    # a group of 3 query heads (not a divisor of 8): the per-head attention kernel
+    cfg = dict(U.DENSE, n_heads=12, n_kv_heads=4, head_dim=64)
+    toks = np.random.default_rng(16).integers(0, cfg["vocab"], 20).tolist()
+    run(cfg, U.dtypes_for(cfg), 77, toks, [9, 11], dev)
+    # one KV head for 4 query heads of 128, past two 64-position chunks
+    cfg = dict(U.DENSE, n_heads=4, n_kv_heads=1, head_dim=128, max_seq=200)
+    toks = np.random.default_rng(17).integers(0, cfg["vocab"], 150).tolist()
+    run(cfg, U.dtypes_for(cfg), 78, toks, [64, 63, 23], dev)
 
 
 def test_batch_long_context(dev):
