@@ -79,7 +79,6 @@ template <int DT, int NV, bool MULTI>
 __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_constant__ FGemvArgs a) {
     extern __shared__ __align__(16) float fsums[];
     grid_dependency_wait();
-    grid_launch_dependents();
     const uint32_t l = threadIdx.x & 7u, n = a.n, nv = a.nvec;
     uint32_t row = a.r0 + blockIdx.x * FGEMV_ROWS + (threadIdx.x >> 3);
     const bool valid = row < a.r1;
@@ -96,8 +95,48 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
         if constexpr (!MULTI) {
             // dot_f32_avx2 / dot_f16_row_avx2 (quant.rs:863-874, :1412-1425)
             const uint32_t steps = n / 8;
-            constexpr uint32_t U = 8;
+            // one vector: more steps' weights in flight per thread (2-byte loads)
+            constexpr uint32_t U = NV == 1 ? 32 : 8;
             uint32_t i = 0;
+            // With 16-byte aligned rows the weights move in 64-element spans:
+            // each thread of the row's 8 loads 16 bytes (a span of F16, half
+            // of one of F32), QS spans at a time, into this warp's part of
+            // shared memory; lane l then reads elements l, l+8, ... of each
+            // span from there, so the FMA chain is unchanged.
+            constexpr uint32_t EB = DT == FDT_F32 ? 4u : 2u, SPAN_B = 64u * EB, RSTR = SPAN_B + 16u,
+                           QS = NV == 1 && DT == FDT_F16 ? 8u : NV <= 2 ? 4u : 1u;
+            __shared__ __align__(16) uint8_t wsm[FGEMV_THREADS / 32][QS][4][RSTR];
+            const bool vec = ((reinterpret_cast<uintptr_t>(a.w) | a.row_bytes) & 15u) == 0;
+            if (vec) {
+                const uint32_t rw = (threadIdx.x >> 3) & 3u, wp = threadIdx.x >> 5;
+                for (; i + 8 * QS <= steps; i += 8 * QS) {
+                    uint4 v[QS][SPAN_B / 128];
+#pragma unroll
+                    for (uint32_t u = 0; u < QS; u++)
+#pragma unroll
+                        for (uint32_t p = 0; p < SPAN_B / 128; p++)
+                            v[u][p] = __ldg(reinterpret_cast<const uint4 *>(rp + (uint64_t)(8 * i + 64 * u) * EB +
+                                                                             128 * p + 16 * l));
+                    __syncwarp();
+#pragma unroll
+                    for (uint32_t u = 0; u < QS; u++)
+#pragma unroll
+                        for (uint32_t p = 0; p < SPAN_B / 128; p++)
+                            *reinterpret_cast<uint4 *>(&wsm[wp][u][rw][128 * p + 16 * l]) = v[u][p];
+                    __syncwarp();
+#pragma unroll
+                    for (uint32_t u = 0; u < QS; u++)
+#pragma unroll
+                        for (uint32_t j = 0; j < 8; j++) {
+                            const uint32_t e = 8 * j + l;  // element of the span
+                            const float w = DT == FDT_F32 ? *reinterpret_cast<const float *>(&wsm[wp][u][rw][4 * e])
+                                                          : h2f(*reinterpret_cast<const unsigned short *>(&wsm[wp][u][rw][2 * e]));
+#pragma unroll
+                            for (int b = 0; b < NV; b++)
+                                if ((uint32_t)b < nv) acc[b] = __fmaf_rn(w, __ldg(xv[b] + 8 * (i + 8 * u + j) + l), acc[b]);
+                        }
+                }
+            }
             for (; i + U <= steps; i += U) {
                 float wv[U];
 #pragma unroll
@@ -143,7 +182,8 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
     } else if constexpr (DT == FDT_Q8_0) {
         // dot_q8_0_row_avx2 (quant.rs:51-71) / rows_multi Q8_0 arm (quant_multi.rs:158-176)
         const uint32_t nbk = n / 32;
-#pragma unroll 2
+        constexpr int UQ8 = NV == 1 ? 8 : 2;  // blocks in flight
+#pragma unroll UQ8
         for (uint32_t k = 0; k < nbk; k++) {
             const uint8_t *bp = rp + k * 34;
             const float d = h2f(ld_u16(bp));
@@ -178,7 +218,8 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
             }
             __syncthreads();
         }
-#pragma unroll 2
+        constexpr int UQ4 = NV == 1 ? 4 : 2;
+#pragma unroll UQ4
         for (uint32_t k = 0; k < nbk; k++) {
             const uint8_t *bp = rp + k * 144;
             const uint4 hd = __ldg(reinterpret_cast<const uint4 *>(bp));
@@ -249,7 +290,8 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
         }
     } else {  // FDT_Q6_K
         const uint32_t nbk = n / 256;
-#pragma unroll 1
+        constexpr int UQ6 = NV == 1 ? 2 : 1;
+#pragma unroll UQ6
         for (uint32_t k = 0; k < nbk; k++) {
             const uint8_t *bp = rp + k * 210;
             const float d = h2f(ld_u16(bp + 208));
@@ -309,6 +351,9 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
         }
     }
 
+    // the next kernel may launch now: its CTAs would otherwise sit on this
+    // kernel's SMs waiting, taking the occupancy its loads need
+    grid_launch_dependents();
     float res[NV];
 #pragma unroll
     for (int b = 0; b < NV; b++) {
