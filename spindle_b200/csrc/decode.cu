@@ -257,7 +257,10 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
         for (uint32_t it = 0; it < NB; it++) issue(it);
 
     grid_dependency_wait();
-    grid_launch_dependents();
+    // one token: the next kernel (a GEMV) may launch now and prefetch its
+    // weights; the batch form runs many waves of CTAs, whose slots the next
+    // kernel's waiting CTAs would take, so it lets it launch at its end
+    if (!prep) grid_launch_dependents();
     if (prep) {  // the kernel before this one wrote the batch's rows
         for (uint32_t it = 0; it < NB; it++) issue(it);
         for (uint32_t d = tid; d < HD; d += blockDim.x) qs[d] = a.q[(uint64_t)blockIdx.y * a.q_stride + h * HD + d];
@@ -402,6 +405,7 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
         }
     }
     if (tid == HD) lsh[0] = __fdiv_rn(1.0f, l > 1e-9f ? l : 1e-9f);  // 1 / l.max(1e-9): a NaN l gives 1e-9
+    if (prep) grid_launch_dependents();
     __syncthreads();
     if (tid < HD)
         a.out[(uint64_t)blockIdx.y * a.n_heads * HD + h * HD + tid] = __fmul_rn(acc, lsh[0]);
