@@ -33,6 +33,25 @@ __device__ __forceinline__ uint32_t ld4(const uint8_t *p, uint32_t l) {
            ((uint32_t)__ldg(p + 24 + l) << 24);
 }
 
+// The same loads through generic pointers (global or shared memory).
+__device__ __forceinline__ uint32_t gu16(const uint8_t *p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
+__device__ __forceinline__ uint32_t gld4(const uint8_t *p, uint32_t l) {
+    return (uint32_t)p[l] | ((uint32_t)p[8 + l] << 8) | ((uint32_t)p[16 + l] << 16) | ((uint32_t)p[24 + l] << 24);
+}
+
+// Stage the next `pieces` 16-byte pieces of this row (from rp) into dst:
+// thread l of the row's 8 takes pieces l, l + 8, ...; P pieces per thread at most.
+template <int P>
+__device__ __forceinline__ void stage_row(const uint8_t *rp, uint8_t *dst, uint32_t pieces, uint32_t l) {
+    uint4 v[P];
+#pragma unroll
+    for (int p = 0; p < P; p++)
+        if (l + 8u * p < pieces) v[p] = __ldg(reinterpret_cast<const uint4 *>(rp) + l + 8u * p);
+#pragma unroll
+    for (int p = 0; p < P; p++)
+        if (l + 8u * p < pieces) reinterpret_cast<uint4 *>(dst)[l + 8u * p] = v[p];
+}
+
 // hsum_avx2 (quant.rs:903-908) over the 8 lanes of a row group:
 // ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7)); every lane gets the sum.
 __device__ __forceinline__ float hsum_hadd8(float v) {
@@ -182,12 +201,10 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
     } else if constexpr (DT == FDT_Q8_0) {
         // dot_q8_0_row_avx2 (quant.rs:51-71) / rows_multi Q8_0 arm (quant_multi.rs:158-176)
         const uint32_t nbk = n / 32;
-        constexpr int UQ8 = NV == 1 ? 8 : 2;  // blocks in flight
-#pragma unroll UQ8
-        for (uint32_t k = 0; k < nbk; k++) {
-            const uint8_t *bp = rp + k * 34;
-            const float d = h2f(ld_u16(bp));
-            const uint32_t qw = ld4(bp + 2, l);
+        // block k at bp (global or shared memory)
+        auto q8_block = [&](const uint8_t *bp, uint32_t k) {
+            const float d = h2f(gu16(bp));
+            const uint32_t qw = gld4(bp + 2, l);
             float q[4];
 #pragma unroll
             for (uint32_t i = 0; i < 4; i++) q[i] = sbyte_f(qw, i);
@@ -201,7 +218,24 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
                     if (MULTI && (k & 1u)) acc1[b] = __fmaf_rn(d, s, acc1[b]);
                     else acc[b] = __fmaf_rn(d, s, acc[b]);
                 }
+        };
+        uint32_t k = 0;
+        // 16-byte aligned rows: spans of 8 blocks (272 bytes = 17 pieces), two
+        // at a time, staged through this warp's part of shared memory
+        constexpr uint32_t KB = 8, SB = KB * 34, SP = SB / 16;
+        __shared__ __align__(16) uint8_t qsm[FGEMV_THREADS / 32][2][4][SB + 16];
+        if (((reinterpret_cast<uintptr_t>(a.w) | a.row_bytes) & 15u) == 0) {
+            const uint32_t rw = (threadIdx.x >> 3) & 3u, wp = threadIdx.x >> 5;
+            for (; k + 2 * KB <= nbk; k += 2 * KB) {
+                __syncwarp();
+                stage_row<3>(rp + 34 * k, qsm[wp][0][rw], SP, l);
+                stage_row<3>(rp + 34 * (k + KB), qsm[wp][1][rw], SP, l);
+                __syncwarp();
+#pragma unroll 4
+                for (uint32_t kk = 0; kk < 2 * KB; kk++) q8_block(&qsm[wp][kk / KB][rw][34 * (kk % KB)], k + kk);
+            }
         }
+        for (; k < nbk; k++) q8_block(rp + k * 34, k);
     } else if constexpr (DT == FDT_Q4_K) {
         const uint32_t nbk = n / 256, ns = n / 32;
         if constexpr (!MULTI) {
@@ -218,18 +252,16 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
             }
             __syncthreads();
         }
-        constexpr int UQ4 = NV == 1 ? 4 : 2;
-#pragma unroll UQ4
-        for (uint32_t k = 0; k < nbk; k++) {
-            const uint8_t *bp = rp + k * 144;
-            const uint4 hd = __ldg(reinterpret_cast<const uint4 *>(bp));
+        // block k at bp (global or shared memory)
+        auto q4_block = [&](const uint8_t *bp, uint32_t k) {
+            const uint4 hd = *reinterpret_cast<const uint4 *>(bp);
             const float d = h2f(hd.x & 0xFFFFu), dmin = h2f(hd.x >> 16);
             float sc[8], mn[8];
             q4k_scales(hd.y, hd.z, hd.w, sc, mn);
             uint32_t lo[4], hi[4];
 #pragma unroll
             for (uint32_t c = 0; c < 4; c++) {
-                const uint32_t qw = ld4(bp + 16 + 32 * c, l);
+                const uint32_t qw = gld4(bp + 16 + 32 * c, l);
                 lo[c] = qw & 0x0F0F0F0Fu;
                 hi[c] = (qw >> 4) & 0x0F0F0F0Fu;
             }
@@ -287,7 +319,23 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
                         }
                 }
             }
+        };
+        uint32_t k = 0;
+        // 16-byte aligned rows: spans of 4 blocks (576 bytes = 36 pieces)
+        // staged through this warp's part of shared memory
+        constexpr uint32_t KB = 4, SB = KB * 144, SP = SB / 16;
+        __shared__ __align__(16) uint8_t qsm[FGEMV_THREADS / 32][4][SB];
+        if (((reinterpret_cast<uintptr_t>(a.w) | a.row_bytes) & 15u) == 0) {
+            const uint32_t rw = (threadIdx.x >> 3) & 3u, wp = threadIdx.x >> 5;
+            for (; k + KB <= nbk; k += KB) {
+                __syncwarp();
+                stage_row<5>(rp + 144 * k, qsm[wp][rw], SP, l);
+                __syncwarp();
+#pragma unroll 2
+                for (uint32_t kk = 0; kk < KB; kk++) q4_block(&qsm[wp][rw][144 * kk], k + kk);
+            }
         }
+        for (; k < nbk; k++) q4_block(rp + k * 144, k);
     } else {  // FDT_Q6_K
         const uint32_t nbk = n / 256;
         constexpr int UQ6 = NV == 1 ? 2 : 1;
