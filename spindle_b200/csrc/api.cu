@@ -887,8 +887,11 @@ sg_status float_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x,
         a.out = d_out + g * ldo;
         a.ldo = ldo;
         const uint32_t grid = (uint32_t)((r1 - r0 + FGEMV_ROWS - 1) / FGEMV_ROWS);
-        const uint32_t smem = fgemv_smem_bytes(dt, multi, (uint32_t)nv, (uint32_t)m->cols);
-        CK(launch_pdl((const void *)pick_float(dt, multi, nv), grid, FGEMV_THREADS, smem, stream, &a));
+        a.stage_x = nv == 1 && m->cols % 4 == 0 && m->cols <= FGEMV_STAGE_X_MAX && aligned(a.x, 16) ? 1u : 0u;
+        const uint32_t smem = fgemv_smem_bytes(dt, multi, (uint32_t)nv, (uint32_t)m->cols, a.stage_x != 0);
+        const void *fn = (const void *)pick_float(dt, multi, nv);
+        if (smem) CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
+        CK(launch_pdl(fn, grid, FGEMV_THREADS, smem, stream, &a));
     }
     return SG_OK;
 }

@@ -52,6 +52,9 @@ __device__ __forceinline__ void stage_row(const uint8_t *rp, uint8_t *dst, uint3
         if (l + 8u * p < pieces) reinterpret_cast<uint4 *>(dst)[l + 8u * p] = v[p];
 }
 
+// x: global memory or the CTA's shared copy (a generic load serves both)
+__device__ __forceinline__ float xld(const float *p) { return *p; }
+
 // hsum_avx2 (quant.rs:903-908) over the 8 lanes of a row group:
 // ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7)); every lane gets the sum.
 __device__ __forceinline__ float hsum_hadd8(float v) {
@@ -105,6 +108,15 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
     const float *xv[NV];
 #pragma unroll
     for (int b = 0; b < NV; b++) xv[b] = a.x + (uint64_t)((uint32_t)b < nv ? b : 0) * a.ldx;
+    if (a.stage_x) {
+        // one vector: x is read by every row of the CTA, so it is copied once
+        // into shared memory (after the Q4_K sub-block sums' area)
+        float *xs = fsums + fgemv_presum_floats(DT, MULTI, nv, n);
+        for (uint32_t i = threadIdx.x; i < n / 4; i += blockDim.x)
+            reinterpret_cast<float4 *>(xs)[i] = __ldg(reinterpret_cast<const float4 *>(a.x) + i);
+        __syncthreads();
+        xv[0] = xs;
+    }
     const uint8_t *rp = a.w + (uint64_t)row * a.row_bytes;
     float acc[NV], acc1[NV], extra[NV];
 #pragma unroll
@@ -152,7 +164,7 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
                                                           : h2f(*reinterpret_cast<const unsigned short *>(&wsm[wp][u][rw][2 * e]));
 #pragma unroll
                             for (int b = 0; b < NV; b++)
-                                if ((uint32_t)b < nv) acc[b] = __fmaf_rn(w, __ldg(xv[b] + 8 * (i + 8 * u + j) + l), acc[b]);
+                                if ((uint32_t)b < nv) acc[b] = __fmaf_rn(w, xld(xv[b] + 8 * (i + 8 * u + j) + l), acc[b]);
                         }
                 }
             }
@@ -164,19 +176,19 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
                 for (uint32_t u = 0; u < U; u++)
 #pragma unroll
                     for (int b = 0; b < NV; b++)
-                        if ((uint32_t)b < nv) acc[b] = __fmaf_rn(wv[u], __ldg(xv[b] + 8 * (i + u) + l), acc[b]);
+                        if ((uint32_t)b < nv) acc[b] = __fmaf_rn(wv[u], xld(xv[b] + 8 * (i + u) + l), acc[b]);
             }
             for (; i < steps; i++) {
                 const float w = wload<DT>(rp, 8 * i + l);
 #pragma unroll
                 for (int b = 0; b < NV; b++)
-                    if ((uint32_t)b < nv) acc[b] = __fmaf_rn(w, __ldg(xv[b] + 8 * i + l), acc[b]);
+                    if ((uint32_t)b < nv) acc[b] = __fmaf_rn(w, xld(xv[b] + 8 * i + l), acc[b]);
             }
             for (uint32_t j = steps * 8; j < n; j++) {  // scalar tail, every lane alike
                 const float w = wload<DT>(rp, j);
 #pragma unroll
                 for (int b = 0; b < NV; b++)
-                    if ((uint32_t)b < nv) extra[b] = __fadd_rn(extra[b], __fmul_rn(w, __ldg(xv[b] + j)));
+                    if ((uint32_t)b < nv) extra[b] = __fadd_rn(extra[b], __fmul_rn(w, xld(xv[b] + j)));
             }
         } else {
             // rows_multi F32 arm (quant_multi.rs:139-157): n % 8 == 0
@@ -187,15 +199,15 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
 #pragma unroll
                 for (int b = 0; b < NV; b++)
                     if ((uint32_t)b < nv) {
-                        acc[b] = __fmaf_rn(w0, __ldg(xv[b] + j + l), acc[b]);
-                        acc1[b] = __fmaf_rn(w1, __ldg(xv[b] + j + 8 + l), acc1[b]);
+                        acc[b] = __fmaf_rn(w0, xld(xv[b] + j + l), acc[b]);
+                        acc1[b] = __fmaf_rn(w1, xld(xv[b] + j + 8 + l), acc1[b]);
                     }
             }
             if (j < n) {
                 const float w0 = wload<DT>(rp, j + l);
 #pragma unroll
                 for (int b = 0; b < NV; b++)
-                    if ((uint32_t)b < nv) acc[b] = __fmaf_rn(w0, __ldg(xv[b] + j + l), acc[b]);
+                    if ((uint32_t)b < nv) acc[b] = __fmaf_rn(w0, xld(xv[b] + j + l), acc[b]);
             }
         }
     } else if constexpr (DT == FDT_Q8_0) {
@@ -212,9 +224,9 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
             for (int b = 0; b < NV; b++)
                 if ((uint32_t)b < nv) {
                     const float *xb = xv[b] + 32 * k + l;
-                    float s = __fmaf_rn(q[0], __ldg(xb), 0.0f);
+                    float s = __fmaf_rn(q[0], xld(xb), 0.0f);
 #pragma unroll
-                    for (uint32_t i = 1; i < 4; i++) s = __fmaf_rn(q[i], __ldg(xb + 8 * i), s);
+                    for (uint32_t i = 1; i < 4; i++) s = __fmaf_rn(q[i], xld(xb + 8 * i), s);
                     if (MULTI && (k & 1u)) acc1[b] = __fmaf_rn(d, s, acc1[b]);
                     else acc[b] = __fmaf_rn(d, s, acc[b]);
                 }
@@ -283,15 +295,15 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
                     for (int b = 0; b < NV; b++)
                         if ((uint32_t)b < nv) {
                             const float *xb = xv[b] + 256 * k + 64 * c + l;
-                            float s = __fmaf_rn(byte_f(lo[c], 0), __ldg(xb), 0.0f);
-                            s = __fmaf_rn(byte_f(lo[c], 1), __ldg(xb + 8), s);
-                            s = __fmaf_rn(byte_f(lo[c], 2), __ldg(xb + 16), s);
-                            s = __fmaf_rn(byte_f(lo[c], 3), __ldg(xb + 24), s);
+                            float s = __fmaf_rn(byte_f(lo[c], 0), xld(xb), 0.0f);
+                            s = __fmaf_rn(byte_f(lo[c], 1), xld(xb + 8), s);
+                            s = __fmaf_rn(byte_f(lo[c], 2), xld(xb + 16), s);
+                            s = __fmaf_rn(byte_f(lo[c], 3), xld(xb + 24), s);
                             acc[b] = __fmaf_rn(ds0, s, acc[b]);
-                            s = __fmaf_rn(byte_f(hi[c], 0), __ldg(xb + 32), 0.0f);
-                            s = __fmaf_rn(byte_f(hi[c], 1), __ldg(xb + 40), s);
-                            s = __fmaf_rn(byte_f(hi[c], 2), __ldg(xb + 48), s);
-                            s = __fmaf_rn(byte_f(hi[c], 3), __ldg(xb + 56), s);
+                            s = __fmaf_rn(byte_f(hi[c], 0), xld(xb + 32), 0.0f);
+                            s = __fmaf_rn(byte_f(hi[c], 1), xld(xb + 40), s);
+                            s = __fmaf_rn(byte_f(hi[c], 2), xld(xb + 48), s);
+                            s = __fmaf_rn(byte_f(hi[c], 3), xld(xb + 56), s);
                             acc[b] = __fmaf_rn(ds1, s, acc[b]);
                         }
                 }
@@ -313,8 +325,8 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
                             const float *xb = xv[b] + 256 * k + 64 * c + l;
 #pragma unroll
                             for (uint32_t i = 0; i < 8; i += 2) {
-                                acc[b] = __fmaf_rn(w[i], __ldg(xb + 8 * i), acc[b]);
-                                acc1[b] = __fmaf_rn(w[i + 1], __ldg(xb + 8 * i + 8), acc1[b]);
+                                acc[b] = __fmaf_rn(w[i], xld(xb + 8 * i), acc[b]);
+                                acc1[b] = __fmaf_rn(w[i + 1], xld(xb + 8 * i + 8), acc1[b]);
                             }
                         }
                 }
@@ -324,7 +336,7 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
         // 16-byte aligned rows: spans of 4 blocks (576 bytes = 36 pieces)
         // staged through this warp's part of shared memory
         constexpr uint32_t KB = 4, SB = KB * 144, SP = SB / 16;
-        __shared__ __align__(16) uint8_t qsm[FGEMV_THREADS / 32][4][SB];
+        __shared__ __align__(16) uint8_t qsm[FGEMV_THREADS / 32][4][SB + 16];  // padded: rows on other banks
         if (((reinterpret_cast<uintptr_t>(a.w) | a.row_bytes) & 15u) == 0) {
             const uint32_t rw = (threadIdx.x >> 3) & 3u, wp = threadIdx.x >> 5;
             for (; k + KB <= nbk; k += KB) {
@@ -371,7 +383,7 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
 #pragma unroll
                             for (int b = 0; b < NV; b++)
                                 if ((uint32_t)b < nv)
-                                    blk[b] = __fmaf_rn(w, __ldg(xv[b] + 256 * k + 128 * h + 32 * g + 8 * kk + l), blk[b]);
+                                    blk[b] = __fmaf_rn(w, xld(xv[b] + 256 * k + 128 * h + 32 * g + 8 * kk + l), blk[b]);
                         }
                 } else {
                     // deq_q6k (quant_multi.rs:77-110), then the a0/a1 chains
@@ -384,10 +396,10 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
                         for (int b = 0; b < NV; b++)
                             if ((uint32_t)b < nv) {
                                 const float *xb = xv[b] + 256 * k + 128 * h + 32 * g + l;
-                                acc[b] = __fmaf_rn(w0, __ldg(xb), acc[b]);
-                                acc1[b] = __fmaf_rn(w1, __ldg(xb + 8), acc1[b]);
-                                acc[b] = __fmaf_rn(w2, __ldg(xb + 16), acc[b]);
-                                acc1[b] = __fmaf_rn(w3, __ldg(xb + 24), acc1[b]);
+                                acc[b] = __fmaf_rn(w0, xld(xb), acc[b]);
+                                acc1[b] = __fmaf_rn(w1, xld(xb + 8), acc1[b]);
+                                acc[b] = __fmaf_rn(w2, xld(xb + 16), acc[b]);
+                                acc1[b] = __fmaf_rn(w3, xld(xb + 24), acc1[b]);
                             }
                     }
                 }

@@ -47,14 +47,20 @@ struct FGemvArgs {
     uint64_t ldx;
     float *out;             // out_b[r] = out[b * ldo + r]
     uint64_t ldo;
+    uint32_t stage_x;       // one vector: copy x into shared memory first (fgemv_smem_bytes counts it)
 };
 
 // dtype codes of the kernel template (the C ABI's SG_* values)
 enum : int { FDT_F32 = 0, FDT_F16 = 1, FDT_Q8_0 = 8, FDT_Q4_K = 12, FDT_Q6_K = 14 };
 
 // Q4_K single-vector path: sums of x over each 32 values, per vector, in shared memory
-__host__ __device__ inline uint32_t fgemv_smem_bytes(int dt, bool multi, uint32_t nv, uint32_t n) {
-    return (dt == FDT_Q4_K && !multi) ? nv * (n / 32) * 4u : 0u;
+__host__ __device__ inline uint32_t fgemv_presum_floats(int dt, bool multi, uint32_t nv, uint32_t n) {
+    return (dt == FDT_Q4_K && !multi) ? ((nv * (n / 32) + 3u) & ~3u) : 0u;
+}
+// x staged in shared memory for one vector up to this many columns
+constexpr uint32_t FGEMV_STAGE_X_MAX = 8192;
+__host__ __device__ inline uint32_t fgemv_smem_bytes(int dt, bool multi, uint32_t nv, uint32_t n, bool stage_x = false) {
+    return fgemv_presum_floats(dt, multi, nv, n) * 4u + (stage_x ? n * 4u : 0u);
 }
 
 template <int DT, int NV, bool MULTI>
