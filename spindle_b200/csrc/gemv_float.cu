@@ -350,15 +350,13 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
         for (; k < nbk; k++) q4_block(rp + k * 144, k);
     } else {  // FDT_Q6_K
         const uint32_t nbk = n / 256;
-        constexpr int UQ6 = NV == 1 ? 2 : 1;
-#pragma unroll UQ6
-        for (uint32_t k = 0; k < nbk; k++) {
-            const uint8_t *bp = rp + k * 210;
-            const float d = h2f(ld_u16(bp + 208));
+        // block k at bp (global or shared memory)
+        auto q6_block = [&](const uint8_t *bp, uint32_t k) {
+            const float d = h2f(gu16(bp + 208));
             float sc[16];
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-                const uint32_t v = ld_u16(bp + 192 + 2 * j);
+                const uint32_t v = gu16(bp + 192 + 2 * j);
                 sc[2 * j] = (float)(int)(int8_t)(v & 0xFFu);
                 sc[2 * j + 1] = (float)(int)(int8_t)(v >> 8);
             }
@@ -368,7 +366,7 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
 #pragma unroll
             for (uint32_t h = 0; h < 2; h++) {
                 // q6_groups (quant.rs:574-607) for positions l, 8+l, 16+l, 24+l of this half
-                const uint32_t A = ld4(bp + 64 * h, l), B = ld4(bp + 64 * h + 32, l), H = ld4(bp + 128 + 32 * h, l);
+                const uint32_t A = gld4(bp + 64 * h, l), B = gld4(bp + 64 * h + 32, l), H = gld4(bp + 128 + 32 * h, l);
                 const uint32_t Q[4] = {(A & 0x0F0F0F0Fu) | ((H & 0x03030303u) << 4),
                                        (B & 0x0F0F0F0Fu) | (((H >> 2) & 0x03030303u) << 4),
                                        ((A >> 4) & 0x0F0F0F0Fu) | (((H >> 4) & 0x03030303u) << 4),
@@ -408,7 +406,29 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
 #pragma unroll
                 for (int b = 0; b < NV; b++) acc[b] = __fmaf_rn(d, blk[b], acc[b]);
             }
+        };
+        uint32_t k = 0;
+        if constexpr (!MULTI) {
+            // one vector with x staged: spans of 8 blocks (1680 bytes = 105
+            // pieces, 16-byte aligned in 16-byte aligned rows) staged through
+            // this warp's part of the dynamic shared memory, after x
+            if (a.stage_x && ((reinterpret_cast<uintptr_t>(a.w) | a.row_bytes) & 15u) == 0) {
+                constexpr uint32_t KB = 8, SB = KB * 210, SP = SB / 16, RST = SB + 16;
+                const uint32_t rw = (threadIdx.x >> 3) & 3u, wp = threadIdx.x >> 5;
+                uint8_t *buf = reinterpret_cast<uint8_t *>(fsums + fgemv_presum_floats(DT, MULTI, nv, n) + n) +
+                               (wp * 4u + rw) * RST;
+                for (; k + KB <= nbk; k += KB) {
+                    __syncwarp();
+                    stage_row<14>(rp + 210 * k, buf, SP, l);
+                    __syncwarp();
+#pragma unroll 1
+                    for (uint32_t kk = 0; kk < KB; kk++) q6_block(buf + 210 * kk, k + kk);
+                }
+            }
         }
+        constexpr int UQ6 = NV == 1 ? 2 : 1;
+#pragma unroll UQ6
+        for (; k < nbk; k++) q6_block(rp + k * 210, k);
     }
 
     // the next kernel may launch now: its CTAs would otherwise sit on this

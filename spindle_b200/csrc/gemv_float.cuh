@@ -59,8 +59,12 @@ __host__ __device__ inline uint32_t fgemv_presum_floats(int dt, bool multi, uint
 }
 // x staged in shared memory for one vector up to this many columns
 constexpr uint32_t FGEMV_STAGE_X_MAX = 8192;
+// Q6_K one vector with x staged: 8-block row spans (1680 bytes + 16 of
+// padding) for the 4 rows of each warp, after x
+constexpr uint32_t FGEMV_Q6_STAGE_BYTES = (FGEMV_THREADS / 32) * 4u * (8u * 210u + 16u);
 __host__ __device__ inline uint32_t fgemv_smem_bytes(int dt, bool multi, uint32_t nv, uint32_t n, bool stage_x = false) {
-    return fgemv_presum_floats(dt, multi, nv, n) * 4u + (stage_x ? n * 4u : 0u);
+    return fgemv_presum_floats(dt, multi, nv, n) * 4u + (stage_x ? n * 4u : 0u) +
+           (stage_x && dt == FDT_Q6_K && !multi ? FGEMV_Q6_STAGE_BYTES : 0u);
 }
 
 template <int DT, int NV, bool MULTI>
