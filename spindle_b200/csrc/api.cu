@@ -1746,15 +1746,14 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
     const uint64_t cache = (uint64_t)m->max_seq * kv_dim;
     uint16_t *kc = (uint16_t *)d_kv, *vc = kc + (uint64_t)m->n_layers * cache;
     const float scale = m->attn_scale != 0.0f ? m->attn_scale : 1.0f / sqrtf((float)hd);
-    const void *attn_fn = hd == 64 ? (const void *)attention_kernel<64>
-                          : hd == 128 ? (const void *)attention_kernel<128> : (const void *)attention_kernel<256>;
     {
         static std::atomic<uint64_t> attr_done{0};
         int dev;
         CK(cudaGetDevice(&dev));
         if (!(attr_done.load() >> dev & 1)) {
-            for (const void *fn : {(const void *)attention_kernel<64>, (const void *)attention_kernel<128>,
-                                   (const void *)attention_kernel<256>})
+            for (const void *fn : {(const void *)attention_kernel<64, 64>, (const void *)attention_kernel<128, 64>,
+                                   (const void *)attention_kernel<256, 64>, (const void *)attention_kernel<64, 128>,
+                                   (const void *)attention_kernel<128, 128>, (const void *)attention_kernel<256, 128>})
                 CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
             attr_done.fetch_or(1ull << dev);
         }
@@ -1770,6 +1769,18 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
     uint32_t *n_slots = (uint32_t *)(sc + L.n_slots);
     uint8_t *qb = sc + L.qb;
     const bool batch_gemm = nt >= (uint32_t)env_int("SG_BATCH_GEMM_MIN", 9);
+    // attention chunks: 64 positions (half the shared memory, more CTAs per
+    // SM) when the launch has several waves of CTAs; 128 otherwise
+    DevInfo *attn_di;
+    if ((st = dev_info(&attn_di))) return st;
+    const uint32_t attn_chunk = (uint64_t)nt * m->n_heads >= 8ull * (uint64_t)attn_di->sms ? 64u : 128u;
+    const void *attn_fn = attn_chunk == 64
+                              ? (hd == 64    ? (const void *)attention_kernel<64, 64>
+                                 : hd == 128 ? (const void *)attention_kernel<128, 64>
+                                             : (const void *)attention_kernel<256, 64>)
+                              : (hd == 64    ? (const void *)attention_kernel<64, 128>
+                                 : hd == 128 ? (const void *)attention_kernel<128, 128>
+                                             : (const void *)attention_kernel<256, 128>);
     if (l0 == 0) {
         EmbedArgs ea = {m->embed, m->embed_dtype, dim, m->vocab, m->embedding_scale, nullptr, x, d_tokens, n_slots};
         CK(launch_pdl((const void *)embed_kernel, dim3((dim + 255) / 256, nt), 256, 0, s, &ea));
@@ -1810,8 +1821,9 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
         CK(launch_pdl((const void *)rope_kv_batch_kernel, dim3(m->n_heads + m->n_kv_heads, nt), 32, 0, s, &ra));
         AttnArgs aa = {qkv, nullptr, nullptr, nullptr, nullptr, m->rms_eps, freqs, hd, m->n_heads, m->n_kv_heads,
                        m->max_seq, m->rope_neox, scale, d_pos, kc + l * cache, vc + l * cache, att, 1, qkv_stride,
-                       2};  // two buffers: many CTAs, two of them per SM
-        CK(launch_pdl(attn_fn, dim3(m->n_heads, nt), attn_threads(hd), attn_smem_bytes(hd, m->max_seq, 2), s, &aa));
+                       2, attn_chunk};  // two buffers: many CTAs, two or more of them per SM
+        CK(launch_pdl(attn_fn, dim3(m->n_heads, nt), attn_threads(hd), attn_smem_bytes(hd, m->max_seq, 2, attn_chunk),
+                      s, &aa));
         if (batch_gemm && (st = launch_q8k_batch(att, q_dim, nt, q_dim / 256, qb, s))) return st;
         if ((st = gemv(y.wo, y.wo_dtype, dim, q_dim, att, oo))) return st;
         if ((st = launch_norm(x, proj, m->residual_scale, y.ffn_norm, m->rms_eps, dim, xn, qx, s, nt))) return st;
@@ -1923,13 +1935,14 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
     int dev;
     CK(cudaGetDevice(&dev));
     if (!(attr_done.load() >> dev & 1)) {
-        for (const void *fn : {(const void *)attention_kernel<64>, (const void *)attention_kernel<128>,
-                               (const void *)attention_kernel<256>})
+        for (const void *fn : {(const void *)attention_kernel<64, ATTN_CHUNK>, (const void *)attention_kernel<128, ATTN_CHUNK>,
+                               (const void *)attention_kernel<256, ATTN_CHUNK>})
             CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         attr_done.fetch_or(1ull << dev);
     }
-    const void *attn_fn = hd == 64 ? (const void *)attention_kernel<64>
-                          : hd == 128 ? (const void *)attention_kernel<128> : (const void *)attention_kernel<256>;
+    const void *attn_fn = hd == 64    ? (const void *)attention_kernel<64, ATTN_CHUNK>
+                          : hd == 128 ? (const void *)attention_kernel<128, ATTN_CHUNK>
+                                      : (const void *)attention_kernel<256, ATTN_CHUNK>;
 
     EmbedArgs ea = {m->embed, m->embed_dtype, dim, m->vocab, m->embedding_scale, d_state, x};
     CK(launch_pdl((const void *)embed_kernel, (dim + 255) / 256, 256, 0, s, &ea));
@@ -1971,7 +1984,7 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
         // chunk of a short context is in flight before the dependency wait
         const uint32_t nbuf = attn_smem_bytes(hd, m->max_seq, ATTN_MAX_BUF) <= 227 * 1024 ? ATTN_MAX_BUF : 2u;
         AttnArgs aa = {q, k, v, y.q_norm, y.k_norm, m->rms_eps, freqs, hd, m->n_heads, m->n_kv_heads, m->max_seq,
-                       m->rope_neox, scale, d_state, kc + l * cache, vc + l * cache, att, 0, 0, nbuf};
+                       m->rope_neox, scale, d_state, kc + l * cache, vc + l * cache, att, 0, 0, nbuf, ATTN_CHUNK};
         CK(launch_pdl(attn_fn, m->n_heads, attn_threads(hd), attn_smem_bytes(hd, m->max_seq, nbuf), s, &aa));
         {
             float *outs[1] = {proj};

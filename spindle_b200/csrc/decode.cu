@@ -186,10 +186,10 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const __grid_cons
 // l_t = l_{t-1} * alpha_t + p_t (one thread) and
 // acc_t[d] = fma(p_t, v_t[d], acc_{t-1}[d] * alpha_t) (one thread per d) run
 // position by position.  The K and V rows of earlier positions were written by
-// earlier steps, so their bulk copies into shared memory are issued before the
+// earlier steps, so their copies into shared memory are issued before the
 // kernel waits for its predecessor; positions go through in chunks of
-// ATTN_CHUNK rows.
-template <int HD>
+// a.chunk rows (64 or 128).
+template <int HD, int CHK>
 __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(16) uint8_t sm8[];
     constexpr uint32_t RS = 2 * HD + ATTN_ROW_PAD, HALF = HD / 2;
@@ -199,8 +199,8 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
     const uint32_t T = pos + 1;
     const uint32_t msq = attn_seq4(a.max_seq);
     const uint32_t NB = a.nbuf;
-    if (a.head_dim != HD || pos >= a.max_seq || NB < 2 || NB > ATTN_MAX_BUF ||
-        attn_smem_bytes(HD, a.max_seq, NB) > dynamic_smem_size() ||
+    if (a.head_dim != HD || pos >= a.max_seq || NB < 2 || NB > ATTN_MAX_BUF || a.chunk != (uint32_t)CHK ||
+        attn_smem_bytes(HD, a.max_seq, NB, CHK) > dynamic_smem_size() ||
         blockDim.x != attn_threads(HD) || a.n_heads % a.n_kv) {
         grid_dependency_wait();
         if (tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
@@ -211,27 +211,27 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
     float *hs = qs + HD;                                       // q, then k, before RoPE
     float *sc = hs + 2 * HD, *al = sc + msq;
     uint8_t *bufs = reinterpret_cast<uint8_t *>(al + msq);
-    uint16_t *kcur = reinterpret_cast<uint16_t *>(bufs + NB * ATTN_CHUNK * RS), *vcur = kcur + HD;
+    uint16_t *kcur = reinterpret_cast<uint16_t *>(bufs + NB * CHK * RS), *vcur = kcur + HD;
     const uint32_t kvh = h / (a.n_heads / a.n_kv), kv_dim = a.n_kv * HD;
     const uint16_t *kg = a.kc + kvh * HD, *vg = a.vc + kvh * HD;
 
     // Rows of the earlier positions move in items: K chunks 0..nc-1, then V
-    // chunks 0..nc-1 (ATTN_CHUNK positions each).  Item i goes to buffer
+    // chunks 0..nc-1 (CHK positions each).  Item i goes to buffer
     // i % NB; items i + 1 .. i + NB - 1 are in flight while item i is used.
     // Every thread copies 16-byte pieces of the rows (cp.async, one commit
     // group per item, empty for items whose rows all come from registers);
     // waiting for item i = waiting until no more than the groups committed
     // after it are pending, then a barrier.
     const uint32_t cached = prep ? T : pos;  // rows copied from the caches: [0, cached)
-    const uint32_t nc = (T + ATTN_CHUNK - 1) / ATTN_CHUNK, nitems = 2 * nc;
+    const uint32_t nc = (T + CHK - 1) / CHK, nitems = 2 * nc;
     constexpr uint32_t SEGS = 2 * HD / 16;   // 16-byte pieces per row
     uint32_t committed = 0;
     auto issue = [&](uint32_t it) {
         if (it >= nitems) return;
-        const uint32_t c0 = (it < nc ? it : it - nc) * ATTN_CHUNK;
-        const uint32_t cend = c0 + ATTN_CHUNK < cached ? c0 + ATTN_CHUNK : cached;
+        const uint32_t c0 = (it < nc ? it : it - nc) * CHK;
+        const uint32_t cend = c0 + CHK < cached ? c0 + CHK : cached;
         const uint16_t *src = it < nc ? kg : vg;
-        uint8_t *dst = bufs + (it % NB) * ATTN_CHUNK * RS;
+        uint8_t *dst = bufs + (it % NB) * CHK * RS;
         const uint32_t n = cend > c0 ? (cend - c0) * SEGS : 0u;
         for (uint32_t u = tid; u < n; u += blockDim.x) {
             const uint32_t row = u / SEGS, sg = u - row * SEGS;
@@ -315,8 +315,8 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
     // ---- scores, chunk by chunk: 8 lanes per position (the 8 AVX lanes) ----
     const uint32_t grp = lane >> 3, l8 = lane & 7u;
     for (uint32_t c = 0; c < nc; c++) {
-        const uint32_t c0 = c * ATTN_CHUNK, cn = T - c0 < ATTN_CHUNK ? T - c0 : ATTN_CHUNK;
-        uint8_t *buf = bufs + (c % NB) * ATTN_CHUNK * RS;
+        const uint32_t c0 = c * CHK, cn = T - c0 < CHK ? T - c0 : CHK;
+        uint8_t *buf = bufs + (c % NB) * CHK * RS;
         if (c > 0) {
             __syncthreads();  // item c - 1 is read: its buffer takes item c + NB - 1
             issue(c + NB - 1);
@@ -385,8 +385,8 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
     // ---- the two recurrences, chunk by chunk over V ----
     float acc = 0.0f, l = 0.0f;
     for (uint32_t c = 0; c < nc; c++) {
-        const uint32_t it = nc + c, c0 = c * ATTN_CHUNK, cn = T - c0 < ATTN_CHUNK ? T - c0 : ATTN_CHUNK;
-        uint8_t *buf = bufs + (it % NB) * ATTN_CHUNK * RS;
+        const uint32_t it = nc + c, c0 = c * CHK, cn = T - c0 < CHK ? T - c0 : CHK;
+        uint8_t *buf = bufs + (it % NB) * CHK * RS;
         __syncthreads();  // maxima done; item it - 1 is read: its buffer takes item it + NB - 1
         issue(it + NB - 1);
         wait_item(it);
@@ -411,9 +411,12 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
         a.out[(uint64_t)blockIdx.y * a.n_heads * HD + h * HD + tid] = __fmul_rn(acc, lsh[0]);
 }
 
-template __global__ void attention_kernel<64>(const __grid_constant__ AttnArgs);
-template __global__ void attention_kernel<128>(const __grid_constant__ AttnArgs);
-template __global__ void attention_kernel<256>(const __grid_constant__ AttnArgs);
+template __global__ void attention_kernel<64, 64>(const __grid_constant__ AttnArgs);
+template __global__ void attention_kernel<128, 64>(const __grid_constant__ AttnArgs);
+template __global__ void attention_kernel<256, 64>(const __grid_constant__ AttnArgs);
+template __global__ void attention_kernel<64, 128>(const __grid_constant__ AttnArgs);
+template __global__ void attention_kernel<128, 128>(const __grid_constant__ AttnArgs);
+template __global__ void attention_kernel<256, 128>(const __grid_constant__ AttnArgs);
 
 // ARGMAX_CTAS blocks: (total_cmp key, index) maxima with the larger index on
 // ties, then the last block to finish reduces them.

@@ -99,6 +99,7 @@ struct AttnArgs {
     uint32_t prepared;
     uint64_t q_stride;
     uint32_t nbuf;              // chunk buffers in shared memory (2..ATTN_MAX_BUF)
+    uint32_t chunk;             // positions per chunk: 64 or 128 (smaller chunks, more CTAs per SM)
 };
 
 // The greedy token (f32::total_cmp, last maximum on ties), written as the next
@@ -120,7 +121,7 @@ struct ArgmaxArgs {
 
 // Positions of K and V staged in shared memory at a time, and the padding of a
 // staged row (spreads the rows of one warp's positions over the banks).
-constexpr uint32_t ATTN_CHUNK = 128;
+constexpr uint32_t ATTN_CHUNK = 128;     // largest chunk (a.chunk: 64 or 128)
 constexpr uint32_t ATTN_ROW_PAD = 16;
 
 __host__ __device__ inline uint32_t attn_threads(uint32_t head_dim) { return head_dim < 256 ? 256u : 288u; }
@@ -130,8 +131,9 @@ constexpr uint32_t ATTN_MAX_BUF = 4;
 // scores, then p | alpha | nbuf chunk buffers of K or V rows | this
 // position's K, V (f16); every part 16-byte aligned
 __host__ __device__ inline uint32_t attn_seq4(uint32_t max_seq) { return (max_seq + 3u) & ~3u; }
-__host__ __device__ inline uint32_t attn_smem_bytes(uint32_t head_dim, uint32_t max_seq, uint32_t nbuf) {
-    return 64u + 3u * head_dim * 4u + 2u * attn_seq4(max_seq) * 4u + nbuf * ATTN_CHUNK * (2u * head_dim + ATTN_ROW_PAD) +
+__host__ __device__ inline uint32_t attn_smem_bytes(uint32_t head_dim, uint32_t max_seq, uint32_t nbuf,
+                                                    uint32_t chunk = ATTN_CHUNK) {
+    return 64u + 3u * head_dim * 4u + 2u * attn_seq4(max_seq) * 4u + nbuf * chunk * (2u * head_dim + ATTN_ROW_PAD) +
            2u * head_dim * 2u;
 }
 
@@ -159,7 +161,7 @@ __global__ void residual_kernel(const float *x, const float *add, float rs, floa
 
 __global__ void embed_kernel(const __grid_constant__ EmbedArgs a);
 __global__ void rmsnorm_kernel(const __grid_constant__ NormArgs a);
-template <int HD>
+template <int HD, int CHK>
 __global__ void attention_kernel(const __grid_constant__ AttnArgs a);
 __global__ void argmax_kernel(const __grid_constant__ ArgmaxArgs a);
 __global__ void rope_kv_batch_kernel(const __grid_constant__ RopeBatchArgs a);
