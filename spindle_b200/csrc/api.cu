@@ -634,7 +634,7 @@ MoeScratch moe_scratch(const sg_moe *m) {
 // Scratch of the batched layer (moe_forward_batch) for n_tok tokens.
 struct MoeBatchScratch {
     uint64_t choices, slot_base, slots, n_slots, slots_sh, n_slots_sh, shsel, scale, logits, qx, h, y, hsh, ysh;
-    uint64_t slots_local, slot_global, n_local, total;
+    uint64_t slots_local, slot_global, n_local, ticket, total;
 };
 
 MoeBatchScratch moe_batch_scratch(const sg_moe *m, uint64_t n_tok) {
@@ -664,6 +664,7 @@ MoeBatchScratch moe_batch_scratch(const sg_moe *m, uint64_t n_tok) {
     L.slots_local = take(slots * 8);  // expert parallelism: this rank's slots
     L.slot_global = take(slots * 4);
     L.n_local = take(4);
+    L.ticket = take(4);  // the select kernel's last-CTA count (zeroed by the router kernel)
     L.total = off;
     return L;
 }
@@ -760,7 +761,7 @@ sg_status launch_moe_group(int32_t dtype, int mode, const uint8_t *w, uint64_t m
 // Router logits over the whole GPU (a few rows per CTA), plus one CTA for the
 // shared expert's gate and one-slot choice when the layer has a shared expert.
 sg_status launch_router(const sg_moe *m, const float *x, float *logits, uint8_t *qx, sg_moe_choice *shsel, float *scale,
-                        cudaStream_t stream, uint32_t n_tok = 1, uint64_t ldx = 0) {
+                        cudaStream_t stream, uint32_t n_tok = 1, uint64_t ldx = 0, unsigned *zero_word = nullptr) {
     static std::atomic<uint64_t> attr_done{0};  // bit d: the smem attribute is set on device d
     int dev;
     CK(cudaGetDevice(&dev));
@@ -798,6 +799,7 @@ sg_status launch_router(const sg_moe *m, const float *x, float *logits, uint8_t 
     a.shared_scale = sh ? scale : nullptr;
     a.n_tok = n_tok;
     a.ldx = n_tok > 1 ? ldx : m->dim;
+    a.zero_word = zero_word;
     a.tok_chunk = tc;
     // 8 threads per (row, token): one warp for a lone token, up to 256 threads for a batch
     uint32_t threads = (8 * rpc * tc + 31) / 32 * 32;
@@ -1404,7 +1406,9 @@ sg_status moe_batch_impl(const sg_moe *m, const sg_moe_ep *ep, const float *d_x,
     // router (every token) -> choices and slot table -> gate/up over all slots
     // (this rank's, with expert parallelism) -> down -> [shared gate/up, down
     // over one slot per token] -> combine
-    if ((st = launch_router(m, d_x, logits, qx, (sg_moe_choice *)(sc + L.shsel), scale, s, nt, ldx))) return st;
+    unsigned *sel_ticket = (unsigned *)(sc + L.ticket);
+    if ((st = launch_router(m, d_x, logits, qx, (sg_moe_choice *)(sc + L.shsel), scale, s, nt, ldx, sel_ticket)))
+        return st;
     {
         static std::atomic<uint64_t> attr_done{0};
         int dev;
@@ -1417,8 +1421,10 @@ sg_status moe_batch_impl(const sg_moe *m, const sg_moe_ep *ep, const float *d_x,
         SelectBatchArgs sa = {logits, nt, ne, k, m->norm, m->moe_prune, choices, slot_base, slots, n_slots,
                               sh ? slots_sh : nullptr, sh ? n_slots_sh : nullptr,
                               ep ? slots_local : nullptr, slot_global, n_local,
-                              ep ? (uint32_t)ep->expert_lo : 0u, ep ? (uint32_t)ep->expert_hi : 0u};
-        CK(launch_pdl((const void *)moe_select_batch_kernel, 1, SELECT_BATCH_THREADS, select_batch_smem(nt), s, &sa));
+                              ep ? (uint32_t)ep->expert_lo : 0u, ep ? (uint32_t)ep->expert_hi : 0u, sel_ticket};
+        const uint32_t sel_grid = (nt + SELECT_BATCH_THREADS / 32 - 1) / (SELECT_BATCH_THREADS / 32);
+        CK(launch_pdl((const void *)moe_select_batch_kernel, sel_grid, SELECT_BATCH_THREADS, select_batch_smem(nt), s,
+                      &sa));
     }
     const uint32_t ne_run = ep ? (uint32_t)(ep->expert_hi - ep->expert_lo) : ne;
     MoeSlots ms;

@@ -22,18 +22,9 @@ __device__ __forceinline__ float q6_f(uint32_t word, uint32_t k) {
 
 __device__ __forceinline__ float h2f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }
 
-__device__ __forceinline__ uint32_t ld_u16(const uint8_t *p) {
-    return __ldg(reinterpret_cast<const unsigned short *>(p));
-}
-
-// Bytes l, 8+l, 16+l, 24+l of the 32-byte span at p, packed into one word:
-// the four values AVX lane l of the reference takes from such a span.
-__device__ __forceinline__ uint32_t ld4(const uint8_t *p, uint32_t l) {
-    return (uint32_t)__ldg(p + l) | ((uint32_t)__ldg(p + 8 + l) << 8) | ((uint32_t)__ldg(p + 16 + l) << 16) |
-           ((uint32_t)__ldg(p + 24 + l) << 24);
-}
-
-// The same loads through generic pointers (global or shared memory).
+// Loads through generic pointers (global or shared memory): a 2-byte value,
+// and bytes l, 8+l, 16+l, 24+l of the 32-byte span at p packed into one word
+// (the four values AVX lane l of the reference takes from such a span).
 __device__ __forceinline__ uint32_t gu16(const uint8_t *p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
 __device__ __forceinline__ uint32_t gld4(const uint8_t *p, uint32_t l) {
     return (uint32_t)p[l] | ((uint32_t)p[8 + l] << 8) | ((uint32_t)p[16 + l] << 16) | ((uint32_t)p[24 + l] << 24);

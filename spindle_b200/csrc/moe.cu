@@ -40,6 +40,7 @@ __global__ void __launch_bounds__(ROUTER_MAX_THREADS) moe_router_kernel(const __
         }
     }
     grid_dependency_wait();
+    if (a.zero_word && blockIdx.x == 0 && tid == 0) *a.zero_word = 0;  // the batch select kernel's ticket
     const uint32_t nb = dim / 256, tc = a.tok_chunk;
     const uint32_t nwarps = blockDim.x >> 5, warp = tid >> 5, lane = tid & 31u;
     bool ok = true;
@@ -146,17 +147,20 @@ __global__ void moe_combine_kernel(const __grid_constant__ CombineArgs a) {
     a.out[r] = acc;
 }
 
-// One CTA, one warp per token: each token's choice (select_warp, the same
-// code as the one-token path), then thread 0 lays out the slot table in token
-// order.  Bit for bit the choices of one-token steps (moe_forward_batch takes
-// each token's top-k on its own, smollm_chat.rs:958-1010).
+// One warp per token over as many CTAs as it takes: each token's choice
+// (select_warp, the same code as the one-token path) into choices[t]; the
+// last CTA to finish (ticket count, zeroed by the router kernel before) lays
+// out the slot table in token order.  Bit for bit the choices of one-token
+// steps (moe_forward_batch takes each token's top-k on its own,
+// smollm_chat.rs:958-1010).
 __global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(const __grid_constant__ SelectBatchArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     grid_dependency_wait();
     grid_launch_dependents();
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5, nwarps = blockDim.x / 32;
     if (a.n_expert == 0 || a.n_expert > 256 || a.n_used == 0 || a.n_used > a.n_expert || a.n_used > MOE_MAXK ||
-        select_batch_smem(a.n_tok) > dynamic_smem_size() || blockDim.x != SELECT_BATCH_THREADS) {
+        select_batch_smem(a.n_tok) > dynamic_smem_size() || blockDim.x != SELECT_BATCH_THREADS || !a.ticket ||
+        gridDim.x * nwarps < a.n_tok) {
         if (tid == 0) {
             atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
             *a.n_slots = 0;
@@ -165,70 +169,79 @@ __global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(
         return;
     }
     float *S = reinterpret_cast<float *>(smem) + warp * 256u;
-    moe::Choice *ch = reinterpret_cast<moe::Choice *>(smem + nwarps * 256u * 4u);
-    for (uint32_t t = warp; t < a.n_tok; t += nwarps) {
+    moe::Choice *ch = reinterpret_cast<moe::Choice *>(smem + nwarps * 256u * 4u) + warp;
+    uint32_t *bases = reinterpret_cast<uint32_t *>(reinterpret_cast<moe::Choice *>(smem + nwarps * 256u * 4u) + nwarps);
+    const uint32_t t = blockIdx.x * nwarps + warp;
+    if (t < a.n_tok) {
         const float *lg = a.logits + (uint64_t)t * a.n_expert;
         if (a.n_expert <= 64)
-            moe::select_warp<2>(lg, a.n_expert, a.n_used, a.norm, a.prune, ch + t, nullptr, S, lane);
+            moe::select_warp<2>(lg, a.n_expert, a.n_used, a.norm, a.prune, ch, nullptr, S, lane);
         else if (a.n_expert <= 128)
-            moe::select_warp<4>(lg, a.n_expert, a.n_used, a.norm, a.prune, ch + t, nullptr, S, lane);
+            moe::select_warp<4>(lg, a.n_expert, a.n_used, a.norm, a.prune, ch, nullptr, S, lane);
         else
-            moe::select_warp<8>(lg, a.n_expert, a.n_used, a.norm, a.prune, ch + t, nullptr, S, lane);
+            moe::select_warp<8>(lg, a.n_expert, a.n_used, a.norm, a.prune, ch, nullptr, S, lane);
         __syncwarp();
-    }
-    __syncthreads();
-    for (uint32_t t = warp; t < a.n_tok; t += nwarps) {
         sg_moe_choice *o = a.choices + t;
         if (lane < MOE_MAXK) {
-            o->id[lane] = ch[t].id[lane];
-            o->weight[lane] = ch[t].w[lane];
+            o->id[lane] = ch->id[lane];
+            o->weight[lane] = ch->w[lane];
         }
         if (lane == 0) {
-            o->n = ch[t].n;
+            o->n = ch->n;
             o->pad_[0] = o->pad_[1] = o->pad_[2] = 0;
         }
     }
+    // the last CTA to finish sees every token's choice
+    __threadfence();
+    __syncthreads();
+    uint32_t last = 0;
+    if (tid == 0) last = atomicAdd(a.ticket, 1u) == gridDim.x - 1 ? 1u : 0u;
+    if (!__syncthreads_or(last)) return;
+    __threadfence();
+    const sg_moe_choice *chs = a.choices;
     // slot bases (a prefix sum over the tokens), then every warp writes its
     // tokens' slots
-    uint32_t *bases = reinterpret_cast<uint32_t *>(ch + a.n_tok);
     if (tid == 0) {
         uint32_t base = 0;
-        for (uint32_t t = 0; t < a.n_tok; t++) {
-            bases[t] = base;
-            base += min(ch[t].n, a.n_used);
+        for (uint32_t u = 0; u < a.n_tok; u++) {
+            bases[u] = base;
+            base += min((uint32_t)__ldcg(&chs[u].n), a.n_used);
         }
         bases[a.n_tok] = base;
+        *a.ticket = 0;  // for the next launch
     }
     __syncthreads();
-    for (uint32_t t = warp; t < a.n_tok; t += nwarps) {
-        const uint32_t n = min(ch[t].n, a.n_used), base = bases[t];
+    for (uint32_t u = warp; u < a.n_tok; u += nwarps) {
+        const uint32_t n = min((uint32_t)__ldcg(&chs[u].n), a.n_used), base = bases[u];
         if (lane < n) {
-            a.slots[2 * (base + lane)] = ch[t].id[lane];
-            a.slots[2 * (base + lane) + 1] = (int32_t)t;
+            a.slots[2 * (base + lane)] = __ldcg(&chs[u].id[lane]);
+            a.slots[2 * (base + lane) + 1] = (int32_t)u;
         }
-        if (lane == 0) a.slot_base[t] = base;
+        if (lane == 0) a.slot_base[u] = base;
     }
     if (tid == 0) {
         *a.n_slots = bases[a.n_tok];
         if (a.slots_local) {
             // this rank's slots (expert parallelism), in global slot order
             uint32_t j = 0;
-            for (uint32_t t = 0; t < a.n_tok; t++)
-                for (uint32_t i = 0; i < min(ch[t].n, a.n_used); i++) {
-                    const int32_t e = ch[t].id[i];
+            for (uint32_t u = 0; u < a.n_tok; u++) {
+                const uint32_t n = min((uint32_t)__ldcg(&chs[u].n), a.n_used);
+                for (uint32_t i = 0; i < n; i++) {
+                    const int32_t e = __ldcg(&chs[u].id[i]);
                     if ((uint32_t)e >= a.ep_lo && (uint32_t)e < a.ep_hi) {
                         a.slots_local[2 * j] = e - (int32_t)a.ep_lo;
-                        a.slots_local[2 * j + 1] = (int32_t)t;
-                        a.slot_global[j] = bases[t] + i;
+                        a.slots_local[2 * j + 1] = (int32_t)u;
+                        a.slot_global[j] = bases[u] + i;
                         j++;
                     }
                 }
+            }
             *a.n_local = j;
         }
         if (a.slots_sh) {
-            for (uint32_t t = 0; t < a.n_tok; t++) {
-                a.slots_sh[2 * t] = 0;
-                a.slots_sh[2 * t + 1] = (int32_t)t;
+            for (uint32_t u = 0; u < a.n_tok; u++) {
+                a.slots_sh[2 * u] = 0;
+                a.slots_sh[2 * u + 1] = (int32_t)u;
             }
             *a.n_slots_sh = a.n_tok;
         }

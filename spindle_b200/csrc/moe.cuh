@@ -38,6 +38,7 @@ struct RouterArgs {
     uint32_t n_tok;             // tokens (1 for moe_forward)
     uint64_t ldx;
     uint32_t tok_chunk;         // tokens staged in shared memory at a time
+    unsigned *zero_word;        // optional: set to 0 (the batch select kernel's ticket)
 };
 
 // Batched MoE (moe_forward_batch): every token's choice from its logits (one
@@ -60,10 +61,11 @@ struct SelectBatchArgs {
     uint32_t *slot_global;
     uint32_t *n_local;
     uint32_t ep_lo, ep_hi;
+    unsigned *ticket;           // 0 at launch (the router kernel zeroes it); back to 0 after
 };
-constexpr uint32_t SELECT_BATCH_THREADS = 1024;
+constexpr uint32_t SELECT_BATCH_THREADS = 128;  // one warp per token, ceil(n_tok / 4) CTAs
 __host__ __device__ inline uint32_t select_batch_smem(uint32_t n_tok) {
-    return (SELECT_BATCH_THREADS / 32) * 256u * 4u + n_tok * (uint32_t)sizeof(moe::Choice) + (n_tok + 1u) * 4u;
+    return (SELECT_BATCH_THREADS / 32) * (256u * 4u + (uint32_t)sizeof(moe::Choice)) + (n_tok + 1u) * 4u;
 }
 
 struct CombineBatchArgs {
