@@ -782,9 +782,11 @@ sg_status launch_router(const sg_moe *m, const float *x, float *logits, uint8_t 
     // about one CTA per SM; fewer rows per CTA when they do not fit in 200 KB
     uint32_t rpc = (a.n_expert + di->sms - 1) / di->sms;
     if (rpc > ROUTER_MAX_ROWS) rpc = ROUTER_MAX_ROWS;
-    // tokens staged together: all of a small batch, at most 32
-    uint32_t tc = n_tok < 32 ? n_tok : 32u;
-    if (tc == 0) tc = 1;
+    // a large batch: tiles of 8 experts x 8 tokens, one CTA each (every CTA
+    // stages its rows and its tokens' x once); a small one: rows spread over
+    // the SMs, all tokens staged together
+    uint32_t tc = n_tok < 32 ? (n_tok ? n_tok : 1u) : 8u;
+    if (n_tok >= 32) rpc = 8;
     while (tc > 1 && router_smem_bytes(a.dim, rpc, tc) > 160 * 1024) tc--;
     while (rpc > 1 && router_smem_bytes(a.dim, rpc, tc) > 200 * 1024) rpc--;
     const uint32_t smem = router_smem_bytes(a.dim, rpc, tc);
@@ -804,7 +806,8 @@ sg_status launch_router(const sg_moe *m, const float *x, float *logits, uint8_t 
     // 8 threads per (row, token): one warp for a lone token, up to 256 threads for a batch
     uint32_t threads = (8 * rpc * tc + 31) / 32 * 32;
     if (threads > ROUTER_MAX_THREADS) threads = ROUTER_MAX_THREADS;
-    CK(launch_pdl((const void *)moe_router_kernel, a.row_ctas + (sh ? 1 : 0), threads, smem, stream, &a));
+    CK(launch_pdl((const void *)moe_router_kernel, dim3(a.row_ctas + (sh ? 1 : 0), (n_tok + tc - 1) / tc), threads, smem,
+                  stream, &a));
     return SG_OK;
 }
 

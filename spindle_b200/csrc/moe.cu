@@ -40,12 +40,13 @@ __global__ void __launch_bounds__(ROUTER_MAX_THREADS) moe_router_kernel(const __
         }
     }
     grid_dependency_wait();
-    if (a.zero_word && blockIdx.x == 0 && tid == 0) *a.zero_word = 0;  // the batch select kernel's ticket
+    if (a.zero_word && blockIdx.x == 0 && blockIdx.y == 0 && tid == 0) *a.zero_word = 0;  // the select kernel's ticket
     const uint32_t nb = dim / 256, tc = a.tok_chunk;
     const uint32_t nwarps = blockDim.x >> 5, warp = tid >> 5, lane = tid & 31u;
     bool ok = true;
-    // tok_chunk tokens at a time: their x staged together (the rows stay)
-    for (uint32_t c = 0, t0 = 0; t0 < a.n_tok; c++, t0 += tc) {
+    // tok_chunk tokens at a time: their x staged together (the rows stay);
+    // CTA row blockIdx.y takes chunks blockIdx.y, blockIdx.y + gridDim.y, ...
+    for (uint32_t c = 0, t0 = blockIdx.y * tc; t0 < a.n_tok; c++, t0 += gridDim.y * tc) {
         const uint32_t nt = min(tc, a.n_tok - t0);
         if (tid == 0) {
             mbar_arrive_expect_tx(&bars[1], nt * rowb);
@@ -88,7 +89,7 @@ __global__ void __launch_bounds__(ROUTER_MAX_THREADS) moe_router_kernel(const __
                 }
                 a.shared_scale[t0 + u] = gsc;
             }
-            if (tid == 0 && c == 0) {
+            if (tid == 0 && c == 0 && blockIdx.y == 0) {
                 sg_moe_choice *ch = a.shared_sel;
                 for (uint32_t i = 0; i < MOE_MAXK; i++) {
                     ch->id[i] = 0;
