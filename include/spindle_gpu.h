@@ -337,8 +337,8 @@ SG_API sg_status sg_moe_forward_batch(const sg_moe *m, const float *d_x, uint64_
                                       uint64_t ldo, void *d_scratch, uint64_t scratch_bytes,
                                       sg_moe_choice *d_choices, void *stream);
 
-/* Expert parallelism for the batched layer (SURVEY: experts shard across
- * GPUs, the router stays replicated): rank p keeps experts [expert_lo,
+/* Expert parallelism for the batched layer (experts shard across GPUs, the
+ * router stays replicated): rank p keeps experts [expert_lo,
  * expert_hi) -- m->gate_up / m->down hold only those, packed as usual, while
  * m->router and m->n_expert stay whole -- and computes the choices of every
  * token (identically on every rank) but only the slots whose expert it owns.
