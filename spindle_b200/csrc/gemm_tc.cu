@@ -1,0 +1,326 @@
+// gemm_tc.cu — the tcgen05 batch kernel of gemm_tc.cuh.
+#include <cuda_fp16.h>
+
+#include "gemm_tc.cuh"
+#include "tiled_block.cuh"
+
+namespace sg {
+using namespace tiled;
+
+namespace {
+
+// Shared-memory operand layout (K-major, no swizzle): 8x8 f16 core matrices
+// of 128 contiguous bytes (8 rows of 16 bytes); the 32 core matrices along
+// K of one 8-row group follow each other (LBO = 128), 8-row groups are
+// TC_SBO apart.  Element (row, k) is at (row / 8) * TC_SBO + (k / 8) * 128 +
+// (row % 8) * 16 + (k % 8) * 2.
+constexpr uint32_t TC_SBO = 32u * 128u;
+// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B f16
+// (bits 7-9, 10-12 = 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t TC_IDESC = (1u << 4) | ((TC_TOK >> 3) << 17) | ((TC_ROWS >> 4) << 24);
+
+// Shared-memory matrix descriptor: start >> 4 (bits 0-13), LBO >> 4
+// (16-29), SBO >> 4 (32-45), version 1 (bits 46-47), no swizzle (61-63 = 0).
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128u >> 4) << 16) | ((uint64_t)(TC_SBO >> 4) << 32) |
+           (1ull << 46);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t ad, uint64_t bd, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(ad), "l"(bd), "r"(TC_IDESC), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 16 consecutive TMEM columns of this thread's lane (32x32b shape), waited for
+// inside the same statement so no use of the registers can move above it.
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t h2_splat(float v) {
+    const uint32_t h = __half_as_ushort(__float2half_rn(v));
+    return h | (h << 16);
+}
+
+__device__ __forceinline__ uint4 ldg128(const uint8_t *p) {
+    return __ldg(reinterpret_cast<const uint4 *>(p));
+}
+
+// f16 pairs of the magic 0x6400 | n = 1024 + n (n < 1024): nibbles (bytes 0,
+// 2) and (1, 3) of a word of four bytes, low or high nibble
+constexpr uint32_t H1024 = 0x64006400u;
+// -1152 in f16: 1024 + (y ^ 0x80) - 1152 = y for a signed byte y
+constexpr uint32_t HM1152 = 0xE480E480u;
+
+}  // namespace
+
+// One CTA: rows of 8 tiles (blockIdx.x) x tokens 16 * blockIdx.y .. +16.
+// Per super-block i (stage s = i & 1, TMEM buffer s):
+//   all threads stage A (thread = row rr, half g: lanes 4g..4g+3) and B
+//   (thread = token t, lane L, sub-blocks 4jj..4jj+3), then thread 0 issues
+//   16 MMAs (lane L, K half h: D[s][L] (+)= A[:, 32L+16h..] B[:, 32L+16h..]^T)
+//   and commits them to mma_done[s]; the epilogue of block i - 1 runs while
+//   they execute.
+// Epilogue thread (row rr = 32 (warp & 3) + lane, set th = warp >> 2) keeps
+// lanes {2th, 2th+1, 2th+4, 2th+5} of its row for all 16 tokens and the
+// correction of tokens 8th..8th+7.
+__global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q4k_kernel(const __grid_constant__ GemmTcArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t *mma_done = reinterpret_cast<uint64_t *>(smem);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + 64);
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    constexpr uint32_t CB = 2304;  // tiled_col_bytes(Q4_K)
+    if (blockDim.x != TC_THREADS || a.nb == 0 || a.ntok == 0 || a.ntok > GB_MAX_TOK ||
+        gridDim.y * TC_TOK < a.ntok || dynamic_smem_size() < TC_SMEM) {
+        if (tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+        return;
+    }
+    if (tid == 0) {
+        mbar_init(&mma_done[0], 1);
+        mbar_init(&mma_done[1], 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TC_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tmem_slot;
+
+    const uint64_t tile_bytes = (uint64_t)a.nb * CB;
+    const uint32_t qbb = qb_block_bytes(a.ntok);
+    // staging roles
+    const uint32_t rr = tid & 127u, g = tid >> 7, jt = rr >> 4, r = rr & 15u;
+    const bool tile_ok = blockIdx.x * 8u + jt < a.ntiles;
+    const uint32_t T = a.t0 + blockIdx.x * 8u + jt;
+    const uint8_t *wrow = a.w + (uint64_t)(tile_ok ? T : a.t0) * tile_bytes;
+    const uint32_t xt = tid >> 4, xc = tid & 15u, xL = xc >> 1, xjj = xc & 1u;
+    const uint32_t xtok = blockIdx.y * TC_TOK + xt;
+    const bool xok = xtok < a.ntok;
+    // epilogue roles
+    const uint32_t q = warp & 3u, th = warp >> 2;
+
+    uint4 qv[4], hd;
+    auto load_w = [&](uint32_t i) {
+        if (!tile_ok) return;
+        const uint8_t *col = wrow + (uint64_t)i * CB;
+        hd = ldg128(col + 2048 + 16 * r);
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++) qv[cc] = ldg128(col + 128 * r + 16 * q4k_chunk(2 * cc + g, r));
+    };
+    uint32_t yw[4], bsw = 0;
+    float xdv = 0.0f;
+    auto load_x = [&](uint32_t i) {
+        if (!xok) return;
+        const uint8_t *blk = a.qb + (uint64_t)i * qbb;
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            yw[j] = __ldg(reinterpret_cast<const uint32_t *>(blk + 256u * xtok + 32u * (4u * xjj + j) + 4u * xL));
+        if (xc < 8) bsw = __ldg(reinterpret_cast<const uint32_t *>(blk + 256u * a.ntok + 32u * xtok + 4u * xc));
+        if (xc == 8) xdv = __ldg(reinterpret_cast<const float *>(blk + 288u * a.ntok) + xtok);
+    };
+    auto stage = [&](uint32_t s) { return smem + TC_HDR_BYTES + s * TC_STAGE_BYTES; };
+    auto xslot = [&](uint32_t i) { return reinterpret_cast<int32_t *>(smem + 1024 + (i % 3u) * TC_XS_BYTES); };
+
+    auto store_a = [&](uint8_t *A) {
+        uint8_t *dst = A + (rr >> 3) * TC_SBO + (rr & 7u) * 16u;
+        if (!tile_ok) {
+#pragma unroll
+            for (int kk = 0; kk < 16; kk++)
+                *reinterpret_cast<uint4 *>(dst + (16u * g + kk) * 128u) = make_uint4(0, 0, 0, 0);
+            return;
+        }
+        const uint32_t sclo = hd.y & 0x3F3F3F3Fu, schi = (hd.w & M4) | ((hd.y >> 2) & B45);
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++) {
+            const int slo = ubyte(cc < 2 ? sclo : schi, (2 * cc) & 3), shi = ubyte(cc < 2 ? sclo : schi, (2 * cc + 1) & 3);
+            const uint32_t s_lo = h2_splat((float)slo), n_lo = h2_splat(-1024.0f * (float)slo);
+            const uint32_t s_hi = h2_splat((float)shi), n_hi = h2_splat(-1024.0f * (float)shi);
+#pragma unroll
+            for (int m = 0; m < 4; m++) {
+                const uint32_t wd = w4(qv[cc], m);
+                uint4 o;
+                o.x = hfma2((wd & 0x000F000Fu) | H1024, s_lo, n_lo);
+                o.y = hfma2(((wd >> 8) & 0x000F000Fu) | H1024, s_lo, n_lo);
+                o.z = hfma2(((wd >> 4) & 0x000F000Fu) | H1024, s_hi, n_hi);
+                o.w = hfma2(((wd >> 12) & 0x000F000Fu) | H1024, s_hi, n_hi);
+                const uint32_t kc = 4u * (4u * g + m) + cc;
+                *reinterpret_cast<uint4 *>(dst + kc * 128u) = o;
+            }
+        }
+    };
+    auto store_x = [&](uint8_t *B, int32_t *bs2, float *xd) {
+        uint8_t *dst = B + (xt >> 3) * TC_SBO + (xt & 7u) * 16u;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            uint4 o = make_uint4(0, 0, 0, 0);
+            if (xok) {
+                const uint32_t u0 = yw[2 * h] ^ 0x80808080u, u1 = yw[2 * h + 1] ^ 0x80808080u;
+                o.x = hadd2((u0 & 0x00FF00FFu) | H1024, HM1152);
+                o.y = hadd2(((u0 >> 8) & 0x00FF00FFu) | H1024, HM1152);
+                o.z = hadd2((u1 & 0x00FF00FFu) | H1024, HM1152);
+                o.w = hadd2(((u1 >> 8) & 0x00FF00FFu) | H1024, HM1152);
+            }
+            *reinterpret_cast<uint4 *>(dst + (4u * xL + 2u * xjj + h) * 128u) = o;
+        }
+        if (xc < 8) bs2[xt * 8 + xc] = xok ? (int32_t)(int16_t)(bsw & 0xFFFFu) + (int32_t)(int16_t)(bsw >> 16) : 0;
+        if (xc == 8) xd[xt] = xok ? xdv : 0.0f;
+    };
+
+    float acc[TC_TOK][4], corr[8];
+#pragma unroll
+    for (int t = 0; t < (int)TC_TOK; t++)
+#pragma unroll
+        for (int l = 0; l < 4; l++) acc[t][l] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 8; t++) corr[t] = 0.0f;
+    bool failed = false;
+
+    auto epilogue = [&](uint32_t i) {
+        const uint32_t s = i & 1u;
+        const int32_t *bs2 = xslot(i);
+        const float *xd = reinterpret_cast<const float *>(bs2 + TC_TOK * 8);
+        const uint4 eh = tile_ok ? ldg128(wrow + (uint64_t)i * CB + 2048 + 16 * r) : make_uint4(0, 0, 0, 0);
+        // warp-uniform outcome: the TMEM loads below are .sync.aligned
+        const bool ok = mbar_wait_bounded(&mma_done[s], (i >> 1) & 1u, WAIT_LIMIT_NS);
+        if (__any_sync(0xffffffffu, !ok)) {
+            if (lane == 0) atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_TMA);
+            failed = true;
+        }
+        tc_fence_after();
+        if (failed) return;
+        const float d = h2f_lo(eh.x), dmin = h2f_hi(eh.x);
+        const uint32_t mlo = eh.z & 0x3F3F3F3Fu, mhi = ((eh.w >> 4) & M4) | ((eh.z >> 2) & B45);
+        float cd[TC_TOK];
+#pragma unroll
+        for (int t = 0; t < (int)TC_TOK; t++) cd[t] = __fmul_rn(d, xd[t]);
+#pragma unroll
+        for (int li = 0; li < 4; li++) {
+            const uint32_t L = 2u * th + (li & 1) + (li >> 1) * 4u;
+            float v[16];
+            tc_ld16(tbase + ((32u * q) << 16) + s * 128u + 16u * L, v);
+#pragma unroll
+            for (int t = 0; t < (int)TC_TOK; t++) acc[t][li] = __fmaf_rn(cd[t], v[t], acc[t][li]);
+        }
+#pragma unroll
+        for (int t8 = 0; t8 < 8; t8++) {
+            const uint32_t t = 8u * th + t8;
+            const int4 b0 = *reinterpret_cast<const int4 *>(bs2 + 8 * t), b1 = *reinterpret_cast<const int4 *>(bs2 + 8 * t + 4);
+            const int sp = ubyte(mlo, 0) * b0.x + ubyte(mlo, 1) * b0.y + ubyte(mlo, 2) * b0.z + ubyte(mlo, 3) * b0.w +
+                           ubyte(mhi, 0) * b1.x + ubyte(mhi, 1) * b1.y + ubyte(mhi, 2) * b1.z + ubyte(mhi, 3) * b1.w;
+            corr[t8] = __fadd_rn(corr[t8], __fmul_rn(__fmul_rn(dmin, xd[t]), __int2float_rn(sp)));
+        }
+        tc_fence_before();
+    };
+
+    load_w(0);
+    grid_dependency_wait();
+    load_x(0);
+    for (uint32_t i = 0; i < a.nb; i++) {
+        const uint32_t s = i & 1u;
+        uint8_t *A = stage(s), *B = A + TC_A_BYTES;
+        int32_t *bs2 = xslot(i);
+        store_a(A);
+        store_x(B, bs2, reinterpret_cast<float *>(bs2 + TC_TOK * 8));
+        if (i + 1 < a.nb) {
+            load_w(i + 1);
+            load_x(i + 1);
+        }
+        fence_proxy_async();
+        tc_fence_before();
+        if (__syncthreads_or(failed)) {
+            failed = true;
+            break;
+        }
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(A), b0 = smem_u32(B);
+#pragma unroll
+            for (uint32_t L = 0; L < 8; L++)
+#pragma unroll
+                for (uint32_t h = 0; h < 2; h++) {
+                    const uint32_t koff = (4u * L + 2u * h) * 128u;
+                    tc_mma(tbase + s * 128u + 16u * L, tc_desc(a0 + koff), tc_desc(b0 + koff), h);
+                }
+            tc_commit(&mma_done[s]);
+        }
+        if (i > 0) epilogue(i - 1);
+    }
+    if (!failed) epilogue(a.nb - 1);
+    grid_launch_dependents();
+    failed = __syncthreads_or(failed);
+
+    if (!failed) {
+        // every MMA has completed (the last commit covers all before it):
+        // stage 0 holds the lane pairs x_m = a_m + a_{m+4} and the corrections
+        float *finx = reinterpret_cast<float *>(stage(0));   // [4][16 tokens][128 rows]
+        float *finc = finx + 4 * TC_TOK * TC_ROWS;           // [16 tokens][128 rows]
+#pragma unroll
+        for (int t = 0; t < (int)TC_TOK; t++) {
+            finx[((2 * th + 0) * TC_TOK + t) * TC_ROWS + rr] = __fadd_rn(acc[t][0], acc[t][2]);
+            finx[((2 * th + 1) * TC_TOK + t) * TC_ROWS + rr] = __fadd_rn(acc[t][1], acc[t][3]);
+        }
+#pragma unroll
+        for (int t8 = 0; t8 < 8; t8++) finc[(8 * th + t8) * TC_ROWS + rr] = corr[t8];
+        __syncthreads();
+#pragma unroll
+        for (int t8 = 0; t8 < 8; t8++) {
+            const uint32_t t = 8u * th + t8, tok = blockIdx.y * TC_TOK + t;
+            const float x0 = finx[(0 * TC_TOK + t) * TC_ROWS + rr], x1 = finx[(1 * TC_TOK + t) * TC_ROWS + rr];
+            const float x2 = finx[(2 * TC_TOK + t) * TC_ROWS + rr], x3 = finx[(3 * TC_TOK + t) * TC_ROWS + rr];
+            const float yv = __fsub_rn(__fadd_rn(__fadd_rn(x0, x2), __fadd_rn(x1, x3)), finc[t * TC_ROWS + rr]);
+            if (a.swiglu) {
+                // rows r < 8 gate, r + 8 up of the same outputs (smollm_chat.rs:357-359)
+                const float up = __shfl_down_sync(0xffffffffu, yv, 8);
+                const uint32_t jo = T * 8 + r;
+                if (tok < a.ntok && tile_ok && r < 8 && 2 * jo < a.r1) a.out[(uint64_t)tok * a.ldo + jo] = silu_mul(yv, up);
+            } else {
+                const uint32_t row = T * TILE_ROWS + r;
+                if (tok < a.ntok && tile_ok && row >= a.r0 && row < a.r1) a.out[(uint64_t)tok * a.ldo + row] = yv;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TC_TMEM_COLS)
+                     : "memory");
+    }
+}
+
+}  // namespace sg

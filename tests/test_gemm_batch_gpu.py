@@ -1,4 +1,4 @@
-"""GPU parity of the batch GEMM (sg_matmul_batch: matvec_multi over 9..64
+"""GPU parity of the dp4a batch GEMM (sg_matmul_batch: matvec_multi over 9..64
 vectors in one pass, smollm_chat.rs:447-512): bit-identical to the oracle's
 Q8K::quantize + matmul_rows (quant_q8k.rs:84-121, :255-295) and to the GEMV,
 including non-finite inputs, ragged row counts, row ranges and every token
@@ -11,6 +11,13 @@ import oracle as O
 import spindle_b200 as sg
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def dp4a_path(monkeypatch):
+    # Q4_K batches run on the tensor cores by default (test_gemm_tc_gpu.py);
+    # this file checks the dp4a kernel
+    monkeypatch.setenv("SG_GEMM_TC", "0")
 
 
 def to_dev(a, dev):
