@@ -476,15 +476,17 @@ sg_status launch_q8k_batch(const float *x, uint64_t ldx, uint32_t n, uint32_t nb
 // Rows r0..r1 of a TILED16 matrix for ntok <= 64 vectors given as a QB image:
 // vector t, row r at out + t * ldo + r (swiglu: the packed gate/up form, see
 // GemmBatchArgs).  One launch; every weight column is read once.
-// Q4_K on the tensor cores (gemm_tc.cu): CTAs of 128 rows x 16 tokens.
-sg_status launch_gemm_tc(const uint8_t *w, uint32_t nb, uint64_t r0, uint64_t r1, const uint8_t *qb, uint32_t ntok,
-                         float *out, uint64_t ldo, bool swiglu, cudaStream_t s) {
+// Q4_K / Q6_K on the tensor cores (gemm_tc.cu): CTAs of 128 rows x 16 tokens.
+sg_status launch_gemm_tc(const uint8_t *w, int dt, uint32_t nb, uint64_t r0, uint64_t r1, const uint8_t *qb,
+                         uint32_t ntok, float *out, uint64_t ldo, bool swiglu, cudaStream_t s) {
     static std::atomic<uint64_t> attr_done{0};
     int dev;
     CK(cudaGetDevice(&dev));
     if (!(attr_done.load() >> dev & 1)) {
         CK(cudaFuncSetAttribute((const void *)gemm_tc_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 TC_SMEM));
+        CK(cudaFuncSetAttribute((const void *)gemm_tc_q6k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                TC6_SMEM));
         attr_done.fetch_or(1ull << dev);
     }
     GemmTcArgs a;
@@ -501,7 +503,10 @@ sg_status launch_gemm_tc(const uint8_t *w, uint32_t nb, uint64_t r0, uint64_t r1
     a.ldo = ldo;
     a.swiglu = swiglu ? 1u : 0u;
     const dim3 grid((a.ntiles + 7) / 8, (ntok + TC_TOK - 1) / TC_TOK);
-    CK(launch_pdl((const void *)gemm_tc_q4k_kernel, grid, TC_THREADS, TC_SMEM, s, &a));
+    if (dt == DT_Q4K)
+        CK(launch_pdl((const void *)gemm_tc_q4k_kernel, grid, TC_THREADS, TC_SMEM, s, &a));
+    else
+        CK(launch_pdl((const void *)gemm_tc_q6k_kernel, grid, TC_THREADS, TC6_SMEM, s, &a));
     return SG_OK;
 }
 
@@ -509,8 +514,11 @@ sg_status launch_gemm_batch(const uint8_t *w, int dt, uint32_t nb, uint64_t r0, 
                             uint32_t ntok, float *out, uint64_t ldo, bool swiglu, cudaStream_t s) {
     if (ntok == 0 || r1 <= r0) return SG_OK;
     if (ntok > GB_MAX_TOK) return SG_ERR_SHAPE;
-    // Q4_K runs on the tensor cores unless SG_GEMM_TC=0 selects the dp4a kernel
-    if (dt == DT_Q4K && env_int("SG_GEMM_TC", 1)) return launch_gemm_tc(w, nb, r0, r1, qb, ntok, out, ldo, swiglu, s);
+    // tensor cores: Q4_K by default, Q6_K with SG_GEMM_TC=2; SG_GEMM_TC=0 keeps
+    // both on the dp4a kernel
+    const int tc = env_int("SG_GEMM_TC", 1);
+    if ((dt == DT_Q4K && tc >= 1) || (dt == DT_Q6K && tc >= 2))
+        return launch_gemm_tc(w, dt, nb, r0, r1, qb, ntok, out, ldo, swiglu, s);
     static std::atomic<uint64_t> attr_done{0};
     int dev;
     CK(cudaGetDevice(&dev));

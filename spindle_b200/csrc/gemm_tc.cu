@@ -21,8 +21,8 @@ constexpr uint32_t TC_IDESC = (1u << 4) | ((TC_TOK >> 3) << 17) | ((TC_ROWS >> 4
 
 // Shared-memory matrix descriptor: start >> 4 (bits 0-13), LBO >> 4
 // (16-29), SBO >> 4 (32-45), version 1 (bits 46-47), no swizzle (61-63 = 0).
-__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128u >> 4) << 16) | ((uint64_t)(TC_SBO >> 4) << 32) |
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t sbo = TC_SBO) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128u >> 4) << 16) | ((uint64_t)(sbo >> 4) << 32) |
            (1ull << 46);
 }
 
@@ -67,6 +67,16 @@ __device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
     asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
     return d;
 }
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
 __device__ __forceinline__ uint32_t h2_splat(float v) {
     const uint32_t h = __half_as_ushort(__float2half_rn(v));
     return h | (h << 16);
@@ -81,6 +91,65 @@ __device__ __forceinline__ uint4 ldg128(const uint8_t *p) {
 constexpr uint32_t H1024 = 0x64006400u;
 // -1152 in f16: 1024 + (y ^ 0x80) - 1152 = y for a signed byte y
 constexpr uint32_t HM1152 = 0xE480E480u;
+
+
+// After the last super-block (every MMA complete): the lane pairs x_m = a_m +
+// a_{m+4} and the corrections meet in shared memory (scratch: 40 KB), then
+// thread (rr, th) writes tokens 8th..8th+7 of row rr as
+// ((x0 + x2) + (x1 + x3)) - corr, or silu(gate) * up for the packed gate/up
+// layout.
+__device__ __forceinline__ void tc_finish(const GemmTcArgs &a, uint8_t *scratch, const float (&acc)[TC_TOK][4],
+                                          const float (&corr)[8], uint32_t th, uint32_t rr, uint32_t r, uint32_t T,
+                                          bool tile_ok) {
+    float *finx = reinterpret_cast<float *>(scratch);  // [4][16 tokens][128 rows]
+    float *finc = finx + 4 * TC_TOK * TC_ROWS;          // [16 tokens][128 rows]
+#pragma unroll
+    for (int t = 0; t < (int)TC_TOK; t++) {
+        finx[((2 * th + 0) * TC_TOK + t) * TC_ROWS + rr] = __fadd_rn(acc[t][0], acc[t][2]);
+        finx[((2 * th + 1) * TC_TOK + t) * TC_ROWS + rr] = __fadd_rn(acc[t][1], acc[t][3]);
+    }
+#pragma unroll
+    for (int t8 = 0; t8 < 8; t8++) finc[(8 * th + t8) * TC_ROWS + rr] = corr[t8];
+    __syncthreads();
+#pragma unroll
+    for (int t8 = 0; t8 < 8; t8++) {
+        const uint32_t t = 8u * th + t8, tok = blockIdx.y * TC_TOK + t;
+        const float x0 = finx[(0 * TC_TOK + t) * TC_ROWS + rr], x1 = finx[(1 * TC_TOK + t) * TC_ROWS + rr];
+        const float x2 = finx[(2 * TC_TOK + t) * TC_ROWS + rr], x3 = finx[(3 * TC_TOK + t) * TC_ROWS + rr];
+        const float yv = __fsub_rn(__fadd_rn(__fadd_rn(x0, x2), __fadd_rn(x1, x3)), finc[t * TC_ROWS + rr]);
+        if (a.swiglu) {
+            // rows r < 8 gate, r + 8 up of the same outputs (smollm_chat.rs:357-359)
+            const float up = __shfl_down_sync(0xffffffffu, yv, 8);
+            const uint32_t jo = T * 8 + r;
+            if (tok < a.ntok && tile_ok && r < 8 && 2 * jo < a.r1) a.out[(uint64_t)tok * a.ldo + jo] = silu_mul(yv, up);
+        } else {
+            const uint32_t row = T * TILE_ROWS + r;
+            if (tok < a.ntok && tile_ok && row >= a.r0 && row < a.r1) a.out[(uint64_t)tok * a.ldo + row] = yv;
+        }
+    }
+}
+
+__device__ __forceinline__ bool tc_alloc(uint32_t *slot, uint32_t cols, uint32_t warp) {
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                     "r"(cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    return true;
+}
+
+__device__ __forceinline__ void tc_dealloc(uint32_t tbase, uint32_t cols, uint32_t warp) {
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(cols) : "memory");
+    }
+}
 
 }  // namespace
 
@@ -110,15 +179,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q4k_kernel(const __grid
         mbar_init(&mma_done[1], 1);
         fence_mbar_init();
     }
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TC_TMEM_COLS)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
+    tc_alloc(tmem_slot, TC_TMEM_COLS, warp);
     const uint32_t tbase = *tmem_slot;
 
     const uint64_t tile_bytes = (uint64_t)a.nb * CB;
@@ -284,43 +345,236 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q4k_kernel(const __grid
     grid_launch_dependents();
     failed = __syncthreads_or(failed);
 
-    if (!failed) {
-        // every MMA has completed (the last commit covers all before it):
-        // stage 0 holds the lane pairs x_m = a_m + a_{m+4} and the corrections
-        float *finx = reinterpret_cast<float *>(stage(0));   // [4][16 tokens][128 rows]
-        float *finc = finx + 4 * TC_TOK * TC_ROWS;           // [16 tokens][128 rows]
+    if (!failed) tc_finish(a, stage(0), acc, corr, th, rr, r, T, tile_ok);
+    tc_dealloc(tbase, TC_TMEM_COLS, warp);
+}
+
+// Q6_K: per super-block i (TMEM buffer b = i & 1) two units u = 0, 1 (stage
+// u): lanes 4u..4u+3.  Staging thread (row rr, half h) builds sub-blocks
+// 4h..4h+3 of those lanes from TILED16 chunks 4h+u, 4h+2+u, 8+2h+u; token
+// thread (t, c) builds lane 4u + (c >> 2), sub-blocks 2(c & 3), 2(c & 3)+1.
+// Thread 0 issues 16 MMAs per unit (lane, K half, lo / hi) into
+// D_lo[L] = b*256 + 16L and D_hi[L] = b*256 + 128 + 16L.  A unit's stage is
+// refilled once the MMAs of the same unit of the block before are complete.
+__global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q6k_kernel(const __grid_constant__ GemmTcArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t *mma_done = reinterpret_cast<uint64_t *>(smem);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + 64);
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    constexpr uint32_t CB = 3360;  // tiled_col_bytes(Q6_K)
+    constexpr uint32_t SBO6 = 16u * 128u;  // 16 core matrices along K per 8-row group
+    if (blockDim.x != TC_THREADS || a.nb == 0 || a.ntok == 0 || a.ntok > GB_MAX_TOK ||
+        gridDim.y * TC_TOK < a.ntok || dynamic_smem_size() < TC6_SMEM) {
+        if (tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+        return;
+    }
+    if (tid == 0) {
+        mbar_init(&mma_done[0], 1);
+        mbar_init(&mma_done[1], 1);
+        fence_mbar_init();
+    }
+    tc_alloc(tmem_slot, TC6_TMEM_COLS, warp);
+    const uint32_t tbase = *tmem_slot;
+
+    const uint64_t tile_bytes = (uint64_t)a.nb * CB;
+    const uint32_t qbb = qb_block_bytes(a.ntok);
+    const uint32_t rr = tid & 127u, h = tid >> 7, jt = rr >> 4, r = rr & 15u;
+    const bool tile_ok = blockIdx.x * 8u + jt < a.ntiles;
+    const uint32_t T = a.t0 + blockIdx.x * 8u + jt;
+    const uint8_t *wrow = a.w + (uint64_t)(tile_ok ? T : a.t0) * tile_bytes;
+    const uint32_t xt = tid >> 4, xc = tid & 15u, xm = xc >> 2, xq = xc & 3u;
+    const uint32_t xtok = blockIdx.y * TC_TOK + xt;
+    const bool xok = xtok < a.ntok;
+    const uint32_t q = warp & 3u, th = warp >> 2;
+    auto stage = [&](uint32_t u) { return smem + TC6_HDR_BYTES + u * TC6_STAGE_BYTES; };
+    auto xslot = [&](uint32_t i) { return reinterpret_cast<int32_t *>(smem + 1024 + (i % 3u) * TC6_XS_BYTES); };
+
+    uint4 L0, L1, HH, SC;
+    uint32_t yw[2], bsw = 0;
+    float xdv = 0.0f;
+    auto load_w = [&](uint32_t i, uint32_t u) {
+        if (!tile_ok) return;
+        const uint8_t *col = wrow + (uint64_t)i * CB, *qrow = col + 192 * r;
+        L0 = ldg128(qrow + 16 * q6k_chunk(4 * h + u, r));
+        L1 = ldg128(qrow + 16 * q6k_chunk(4 * h + 2 + u, r));
+        HH = ldg128(qrow + 16 * q6k_chunk(8 + 2 * h + u, r));
+        SC = ldg128(col + 3072 + 16 * r);
+    };
+    auto load_x = [&](uint32_t i, uint32_t u) {
+        if (!xok) return;
+        const uint8_t *blk = a.qb + (uint64_t)i * qbb;
+        const uint32_t L = 4u * u + xm;
 #pragma unroll
-        for (int t = 0; t < (int)TC_TOK; t++) {
-            finx[((2 * th + 0) * TC_TOK + t) * TC_ROWS + rr] = __fadd_rn(acc[t][0], acc[t][2]);
-            finx[((2 * th + 1) * TC_TOK + t) * TC_ROWS + rr] = __fadd_rn(acc[t][1], acc[t][3]);
+        for (int j = 0; j < 2; j++)
+            yw[j] = __ldg(reinterpret_cast<const uint32_t *>(blk + 256u * xtok + 32u * (2u * xq + j) + 4u * L));
+        if (u == 0) {
+            bsw = (uint32_t)__ldg(reinterpret_cast<const unsigned short *>(blk + 256u * a.ntok + 32u * xtok) + xc);
+            if (xc == 0) xdv = __ldg(reinterpret_cast<const float *>(blk + 288u * a.ntok) + xtok);
+        }
+    };
+    // two 16-bit lanes holding n < 1024 -> f16 pair n * sc, exact (|n sc| <= 1920)
+    auto cvt = [&](uint32_t v, uint32_t sc2) { return hmul2(hsub2(v | H1024, H1024), sc2); };
+    auto store_a = [&](uint32_t u) {
+        uint8_t *Alo = stage(u), *Ahi = Alo + TC6_A_BYTES;
+        const uint32_t off = (rr >> 3) * SBO6 + (rr & 7u) * 16u;
+        if (!tile_ok) {
+#pragma unroll
+            for (int m = 0; m < 4; m++)
+#pragma unroll
+                for (int c2 = 0; c2 < 2; c2++) {
+                    const uint32_t kc = 4u * m + 2u * h + c2;
+                    *reinterpret_cast<uint4 *>(Alo + off + kc * 128u) = make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4 *>(Ahi + off + kc * 128u) = make_uint4(0, 0, 0, 0);
+                }
+            return;
+        }
+        uint32_t sc2[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint32_t si = 2u * (4u * h + j) + u;  // scale of sub-block 4h + j, lanes 4u..4u+3
+            sc2[j] = h2_splat((float)sbyte(w4(SC, si >> 2), si & 3u));
         }
 #pragma unroll
-        for (int t8 = 0; t8 < 8; t8++) finc[(8 * th + t8) * TC_ROWS + rr] = corr[t8];
-        __syncthreads();
+        for (int m = 0; m < 4; m++) {
+            const uint32_t l0 = w4(L0, m), l1 = w4(L1, m), hh = w4(HH, m);
+            // sub-blocks 4h + j: low 4 bits and the 2 high bits of w
+            const uint32_t lo[4] = {l0 & M4, l1 & M4, (l0 >> 4) & M4, (l1 >> 4) & M4};
+            const uint32_t hi[4] = {hh & 0x03030303u, (hh >> 2) & 0x03030303u, (hh >> 4) & 0x03030303u,
+                                    (hh >> 6) & 0x03030303u};
 #pragma unroll
-        for (int t8 = 0; t8 < 8; t8++) {
-            const uint32_t t = 8u * th + t8, tok = blockIdx.y * TC_TOK + t;
-            const float x0 = finx[(0 * TC_TOK + t) * TC_ROWS + rr], x1 = finx[(1 * TC_TOK + t) * TC_ROWS + rr];
-            const float x2 = finx[(2 * TC_TOK + t) * TC_ROWS + rr], x3 = finx[(3 * TC_TOK + t) * TC_ROWS + rr];
-            const float yv = __fsub_rn(__fadd_rn(__fadd_rn(x0, x2), __fadd_rn(x1, x3)), finc[t * TC_ROWS + rr]);
-            if (a.swiglu) {
-                // rows r < 8 gate, r + 8 up of the same outputs (smollm_chat.rs:357-359)
-                const float up = __shfl_down_sync(0xffffffffu, yv, 8);
-                const uint32_t jo = T * 8 + r;
-                if (tok < a.ntok && tile_ok && r < 8 && 2 * jo < a.r1) a.out[(uint64_t)tok * a.ldo + jo] = silu_mul(yv, up);
-            } else {
-                const uint32_t row = T * TILE_ROWS + r;
-                if (tok < a.ntok && tile_ok && row >= a.r0 && row < a.r1) a.out[(uint64_t)tok * a.ldo + row] = yv;
+            for (int c2 = 0; c2 < 2; c2++) {
+                const int j0 = 2 * c2, j1 = 2 * c2 + 1;
+                const uint32_t kc = 4u * m + 2u * h + c2;
+                uint4 o;
+                o.x = cvt(lo[j0] & 0x000F000Fu, sc2[j0]);
+                o.y = cvt((lo[j0] >> 8) & 0x000F000Fu, sc2[j0]);
+                o.z = cvt(lo[j1] & 0x000F000Fu, sc2[j1]);
+                o.w = cvt((lo[j1] >> 8) & 0x000F000Fu, sc2[j1]);
+                *reinterpret_cast<uint4 *>(Alo + off + kc * 128u) = o;
+                o.x = cvt(hi[j0] & 0x000F000Fu, sc2[j0]);
+                o.y = cvt((hi[j0] >> 8) & 0x000F000Fu, sc2[j0]);
+                o.z = cvt(hi[j1] & 0x000F000Fu, sc2[j1]);
+                o.w = cvt((hi[j1] >> 8) & 0x000F000Fu, sc2[j1]);
+                *reinterpret_cast<uint4 *>(Ahi + off + kc * 128u) = o;
             }
         }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
+    };
+    auto store_x = [&](uint32_t i, uint32_t u) {
+        uint8_t *B = stage(u) + 2u * TC6_A_BYTES;
+        uint4 o = make_uint4(0, 0, 0, 0);
+        if (xok) {
+            const uint32_t u0 = yw[0] ^ 0x80808080u, u1 = yw[1] ^ 0x80808080u;
+            o.x = hadd2((u0 & 0x00FF00FFu) | H1024, HM1152);
+            o.y = hadd2(((u0 >> 8) & 0x00FF00FFu) | H1024, HM1152);
+            o.z = hadd2((u1 & 0x00FF00FFu) | H1024, HM1152);
+            o.w = hadd2(((u1 >> 8) & 0x00FF00FFu) | H1024, HM1152);
+        }
+        *reinterpret_cast<uint4 *>(B + (xt >> 3) * SBO6 + (4u * xm + xq) * 128u + (xt & 7u) * 16u) = o;
+        if (u == 0) {
+            int32_t *bs = xslot(i);
+            bs[xt * 16 + xc] = xok ? (int32_t)(int16_t)bsw : 0;
+            if (xc == 0) reinterpret_cast<float *>(bs + 256)[xt] = xok ? xdv : 0.0f;
+        }
+    };
+
+    float acc[TC_TOK][4], corr[8];
+#pragma unroll
+    for (int t = 0; t < (int)TC_TOK; t++)
+#pragma unroll
+        for (int l = 0; l < 4; l++) acc[t][l] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 8; t++) corr[t] = 0.0f;
+    bool failed = false;
+    auto wait_done = [&](uint32_t u, uint32_t parity) {
+        const bool ok = mbar_wait_bounded(&mma_done[u], parity, WAIT_LIMIT_NS);
+        if (__any_sync(0xffffffffu, !ok)) {
+            if (lane == 0) atomicExch(&g_dev_status, (unsigned)DEV_TIMEOUT_TMA);
+            failed = true;
+        }
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TC_TMEM_COLS)
-                     : "memory");
+    };
+    // block i's MMAs are complete (the caller waited for its last unit)
+    auto epilogue = [&](uint32_t i) {
+        const uint32_t b = i & 1u;
+        const int32_t *bs = xslot(i);
+        const float *xd = reinterpret_cast<const float *>(bs + 256);
+        const uint8_t *col = wrow + (uint64_t)i * CB;
+        const uint4 esc = tile_ok ? ldg128(col + 3072 + 16 * r) : make_uint4(0, 0, 0, 0);
+        const float d = tile_ok ? __half2float(__ldg(reinterpret_cast<const __half *>(col + 3328) + r)) : 0.0f;
+        float cd[TC_TOK];
+#pragma unroll
+        for (int t = 0; t < (int)TC_TOK; t++) cd[t] = __fmul_rn(d, xd[t]);
+#pragma unroll
+        for (int li = 0; li < 4; li++) {
+            const uint32_t L = 2u * th + (li & 1) + (li >> 1) * 4u;
+            float vlo[16], vhi[16];
+            const uint32_t ta = tbase + ((32u * q) << 16) + b * 256u + 16u * L;
+            tc_ld16(ta, vlo);
+            tc_ld16(ta + 128u, vhi);
+#pragma unroll
+            for (int t = 0; t < (int)TC_TOK; t++) {
+                const int s = 16 * __float2int_rn(vhi[t]) + __float2int_rn(vlo[t]);
+                acc[t][li] = __fmaf_rn(cd[t], __int2float_rn(s), acc[t][li]);
+            }
+        }
+#pragma unroll
+        for (int t8 = 0; t8 < 8; t8++) {
+            const uint32_t t = 8u * th + t8;
+            int sp = 0;
+#pragma unroll
+            for (int c = 0; c < 16; c++) sp += sbyte(w4(esc, c >> 2), c & 3) * bs[t * 16 + c];
+            corr[t8] = __fadd_rn(corr[t8], __fmul_rn(cd[t], __int2float_rn(32 * sp)));
+        }
+        tc_fence_before();
+    };
+
+    load_w(0, 0);
+    grid_dependency_wait();
+    load_x(0, 0);
+    for (uint32_t i = 0; i < a.nb && !failed; i++) {
+        const uint32_t b = i & 1u;
+        for (uint32_t u = 0; u < 2; u++) {
+            if (i > 0) wait_done(u, (i - 1) & 1u);
+            store_a(u);
+            store_x(i, u);
+            if (u == 0) {
+                load_w(i, 1);
+                load_x(i, 1);
+            } else if (i + 1 < a.nb) {
+                load_w(i + 1, 0);
+                load_x(i + 1, 0);
+            }
+            fence_proxy_async();
+            tc_fence_before();
+            if (__syncthreads_or(failed)) {
+                failed = true;
+                break;
+            }
+            if (tid == 0) {
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(stage(u)), b0 = a0 + 2u * TC6_A_BYTES;
+#pragma unroll
+                for (uint32_t m = 0; m < 4; m++)
+#pragma unroll
+                    for (uint32_t k2 = 0; k2 < 2; k2++) {
+                        const uint32_t koff = (4u * m + 2u * k2) * 128u, L = 4u * u + m;
+                        const uint32_t d = tbase + b * 256u + 16u * L;
+                        tc_mma(d, tc_desc(a0 + koff, SBO6), tc_desc(b0 + koff, SBO6), k2);
+                        tc_mma(d + 128u, tc_desc(a0 + TC6_A_BYTES + koff, SBO6), tc_desc(b0 + koff, SBO6), k2);
+                    }
+                tc_commit(&mma_done[u]);
+            }
+        }
+        if (!failed && i > 0) epilogue(i - 1);
     }
+    if (!failed) {
+        wait_done(1, (a.nb - 1) & 1u);
+        if (!failed) epilogue(a.nb - 1);
+    }
+    grid_launch_dependents();
+    failed = __syncthreads_or(failed);
+    if (!failed) tc_finish(a, stage(0), acc, corr, th, rr, r, T, tile_ok);
+    tc_dealloc(tbase, TC6_TMEM_COLS, warp);
 }
 
 }  // namespace sg

@@ -1,7 +1,7 @@
-// gemm_tc.cuh — Q4_K weights x Q8_K activations for a batch of up to 64
+// gemm_tc.cuh — Q4_K / Q6_K weights x Q8_K activations for a batch of up to 64
 // vectors on the 5th-generation tensor cores (tcgen05.mma, accumulators in
 // TMEM), bit for bit the GEMV's and the reference's matmul_rows
-// (quant_q8k.rs:166-295, Q4_K block layout of q4k_gemv.rs:26-31).
+// (quant_q8k.rs:166-295, block layouts of q4k_gemv.rs:26-31 and quant.rs:34-39).
 //
 // The reference's dot keeps, per row and super-block, eight int32 "AVX lanes":
 // lane L holds sum_j sc_j * sum_e q[32j + 4L + e] * y[32j + 4L + e] over the
@@ -42,6 +42,20 @@ constexpr uint32_t TC_XS_BYTES = 1024;
 constexpr uint32_t TC_HDR_BYTES = 1024 + 3u * TC_XS_BYTES;
 constexpr uint32_t TC_SMEM = TC_HDR_BYTES + 2u * TC_STAGE_BYTES;
 
+// Q6_K: sc * w (|sc| <= 128, w <= 63) needs 13 bits and a lane sum can reach
+// 32 * 8064 * 128 > 2^24, so w = 16 w_hi + w_lo gives two exact products per
+// lane, A_lo = sc * w_lo (|.| <= 1920) and A_hi = sc * w_hi (|.| <= 384), each
+// summed below 2^23 in its own TMEM accumulator; lane = 16 hi + lo in int32.
+// A super-block is staged in two units of four lanes (lanes 4u..4u+3, the
+// TILED16 chunks of parity u): A_lo | A_hi | B of one unit in 68 KB.
+constexpr uint32_t TC6_A_BYTES = TC_ROWS * 128u * 2u;
+constexpr uint32_t TC6_B_BYTES = TC_TOK * 128u * 2u;
+constexpr uint32_t TC6_STAGE_BYTES = 2u * TC6_A_BYTES + TC6_B_BYTES;
+constexpr uint32_t TC6_XS_BYTES = 2048;  // bsum[16][16] (int32) | xd[16]
+constexpr uint32_t TC6_HDR_BYTES = 1024 + 3u * TC6_XS_BYTES;
+constexpr uint32_t TC6_SMEM = TC6_HDR_BYTES + 2u * TC6_STAGE_BYTES;
+constexpr uint32_t TC6_TMEM_COLS = 512;  // two buffers of (lo, hi) x 8 lanes x 16 tokens
+
 struct GemmTcArgs {
     const uint8_t *w;           // TILED16 Q4_K tiles (16-byte aligned)
     uint32_t nb;                // super-blocks per row
@@ -55,5 +69,6 @@ struct GemmTcArgs {
 };
 
 __global__ void gemm_tc_q4k_kernel(const __grid_constant__ GemmTcArgs a);
+__global__ void gemm_tc_q6k_kernel(const __grid_constant__ GemmTcArgs a);
 
 }  // namespace sg
