@@ -57,6 +57,23 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 consecutive TMEM columns of this thread's lane, waited for in the same statement
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;
     asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -189,7 +206,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q4k_kernel(const __grid
     const bool tile_ok = blockIdx.x * 8u + jt < a.ntiles;
     const uint32_t T = a.t0 + blockIdx.x * 8u + jt;
     const uint8_t *wrow = a.w + (uint64_t)(tile_ok ? T : a.t0) * tile_bytes;
-    const uint32_t xt = tid >> 4, xc = tid & 15u, xL = xc >> 1, xjj = xc & 1u;
+    // token staging: 8 consecutive threads take 8 tokens of one core matrix
+    // (one 128-byte shared-memory wavefront per store phase)
+    const uint32_t xt = (tid & 7u) | ((tid >> 4) & 8u), xc = (tid >> 3) & 15u, xL = xc >> 1, xjj = xc & 1u;
     const uint32_t xtok = blockIdx.y * TC_TOK + xt;
     const bool xok = xtok < a.ntok;
     // epilogue roles
@@ -271,11 +290,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q4k_kernel(const __grid
     for (int t = 0; t < 8; t++) corr[t] = 0.0f;
     bool failed = false;
 
-    auto epilogue = [&](uint32_t i) {
+    // eh: block i's row header (d, dmin, scales and mins), kept from its staging
+    auto epilogue = [&](uint32_t i, const uint4 eh) {
         const uint32_t s = i & 1u;
         const int32_t *bs2 = xslot(i);
         const float *xd = reinterpret_cast<const float *>(bs2 + TC_TOK * 8);
-        const uint4 eh = tile_ok ? ldg128(wrow + (uint64_t)i * CB + 2048 + 16 * r) : make_uint4(0, 0, 0, 0);
         // warp-uniform outcome: the TMEM loads below are .sync.aligned
         const bool ok = mbar_wait_bounded(&mma_done[s], (i >> 1) & 1u, WAIT_LIMIT_NS);
         if (__any_sync(0xffffffffu, !ok)) {
@@ -289,13 +308,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q4k_kernel(const __grid
         float cd[TC_TOK];
 #pragma unroll
         for (int t = 0; t < (int)TC_TOK; t++) cd[t] = __fmul_rn(d, xd[t]);
+        // lanes 2th, 2th+1 (then 2th+4, 2th+5) are 32 adjacent columns
 #pragma unroll
-        for (int li = 0; li < 4; li++) {
-            const uint32_t L = 2u * th + (li & 1) + (li >> 1) * 4u;
-            float v[16];
-            tc_ld16(tbase + ((32u * q) << 16) + s * 128u + 16u * L, v);
+        for (int pr = 0; pr < 2; pr++) {
+            float v[32];
+            tc_ld32(tbase + ((32u * q) << 16) + s * 128u + 16u * (2u * th + 4u * pr), v);
 #pragma unroll
-            for (int t = 0; t < (int)TC_TOK; t++) acc[t][li] = __fmaf_rn(cd[t], v[t], acc[t][li]);
+            for (int t = 0; t < (int)TC_TOK; t++) {
+                acc[t][2 * pr] = __fmaf_rn(cd[t], v[t], acc[t][2 * pr]);
+                acc[t][2 * pr + 1] = __fmaf_rn(cd[t], v[16 + t], acc[t][2 * pr + 1]);
+            }
         }
 #pragma unroll
         for (int t8 = 0; t8 < 8; t8++) {
@@ -308,14 +330,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q4k_kernel(const __grid
         tc_fence_before();
     };
 
+    hd = make_uint4(0, 0, 0, 0);
     load_w(0);
     grid_dependency_wait();
     load_x(0);
+    uint4 hd_cur = hd, hd_prev = hd;
     for (uint32_t i = 0; i < a.nb; i++) {
         const uint32_t s = i & 1u;
         uint8_t *A = stage(s), *B = A + TC_A_BYTES;
         int32_t *bs2 = xslot(i);
         store_a(A);
+        hd_prev = hd_cur;
+        hd_cur = hd;
         store_x(B, bs2, reinterpret_cast<float *>(bs2 + TC_TOK * 8));
         if (i + 1 < a.nb) {
             load_w(i + 1);
@@ -339,9 +365,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q4k_kernel(const __grid
                 }
             tc_commit(&mma_done[s]);
         }
-        if (i > 0) epilogue(i - 1);
+        if (i > 0) epilogue(i - 1, hd_prev);
     }
-    if (!failed) epilogue(a.nb - 1);
+    if (!failed) epilogue(a.nb - 1, hd_cur);
     grid_launch_dependents();
     failed = __syncthreads_or(failed);
 
