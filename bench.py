@@ -1366,7 +1366,7 @@ def run_gpu_prefill(args):
                 "value": round(n_prompt * world / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None,
-                "dtype": "int8 x int4/int6 -> int32 (dp4a), fp32 norms/attention/router, f16 KV",
+                "dtype": "Q4_K projections: exact-integer f16 x f16 -> f32 on tcgen05; Q6_K and the MoE experts: int8 x int6/int4 -> int32 (dp4a); fp32 norms/attention/router, f16 KV",
                 "data": "synthetic",
                 "config": dict(decode_config(name, cfg, world), workload="prefill_verify_%s" % name,
                                prompt=n_prompt, seq_len=n_prompt, chunk=C_, verify_n=VERIFY_N,
@@ -1375,7 +1375,7 @@ def run_gpu_prefill(args):
                                l2="2.0 GB of weights touched per chunk > 126 MB L2"),
                 "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": peak, "unit": "TOP/s",
                              "frac": round(achieved / peak, 5), "traffic": None, "peak_source": peak_src,
-                             "kernel": "the whole prefill (dp4a GEMV kernels; no tcgen05 kind::i8 path yet)",
+                             "kernel": "the whole prefill (Q4_K projections on tcgen05 kind::f16, the rest dp4a)",
                              "how": "2 x prompt x active params (%.3f G) / step time" % (active_params(cfg) / 1e9)},
                 "verify": {"n": VERIFY_N, "ms_per_pass": round(v_ms, 3),
                            "tok_per_s_if_all_accepted": round(VERIFY_N * 1e3 / v_ms, 1),
