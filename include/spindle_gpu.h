@@ -5,8 +5,7 @@
  * The reference (WiseHax/spindle 1.1.0, Rust) has no plugin system: its drop-in
  * boundary is the crate-internal kernel API that the engine calls.  Each entry
  * point below replaces one of those functions; the comment names it by
- * file:line under the reference's src/.  A Rust binding is shown in
- * INTEGRATION.md.
+ * file:line under the reference's src/.
  *
  * Conventions
  *   - Every function returns sg_status (0 = SG_OK) and never aborts the process.
@@ -243,9 +242,10 @@ SG_API sg_status sg_matvec_scratch(const uint8_t *d_base, const sg_mat *m, const
  * thread-local heap memory.  The Q8_K scratch is a static device array of
  * SG_NOALLOC_SCRATCH_BYTES bytes inside the library: requests needing more
  * (sg_matvec_scratch_bytes(cols, n_vec)) return SG_ERR_NOALLOC_LIMIT; it
- * allocates nothing.  The first call on a device looks the array up (make it
- * before any stream capture); all calls share the array, so calls that
- * overlap on the GPU race and must be serialized by the caller. */
+ * allocates nothing.  The first call on a device (and the first after a
+ * device reset) looks the array up: make it before any stream capture.  All
+ * calls share the array, so calls that overlap on the GPU race and must be
+ * serialized by the caller. */
 #define SG_NOALLOC_SCRATCH_BYTES 262144
 SG_API sg_status sg_matvec_static(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx,
                                   float *d_out, uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1,
@@ -256,6 +256,20 @@ SG_API sg_status sg_matvec_static(const uint8_t *d_base, const sg_mat *m, const 
  * of row r.  Exists to check per-super-block sums bit for bit.  GGUF layout only. */
 SG_API sg_status sg_block_sums(const uint8_t *d_base, const sg_mat *m, const sg_q8k *xq,
                         int32_t *d_out, uint64_t r0, uint64_t r1, void *stream);
+
+/* The kernels' expf / sinf / cosf (fn 0 / 1 / 2): glibc's single-precision
+ * functions, which f32::exp and f32::sin_cos call on Linux (smollm_chat.rs:
+ * 586-588 SiLU, :1200-1203 router softmax, :1397-1420 RoPE, :3463-3495
+ * attention), restated for the device.  d_out[i] = f(the float whose bits are
+ * (start + i * stride) mod 2^32), i < count.  Exists to check the device build
+ * against the host's libm. */
+SG_API sg_status sg_libm_eval(int32_t fn, uint64_t start, uint64_t stride, uint64_t count, float *d_out,
+                              void *stream);
+
+/* The architecture the runtime loaded the library's kernels for, as
+ * major * 10 + minor (cudaFuncAttributes.binaryVersion): 100 on B200 (the
+ * library ships sm_100a code only).  No counterpart in the reference. */
+SG_API sg_status sg_binary_version(int32_t *out);
 
 /* ---- MoE layer (smollm_chat.rs:1178-1382, moe_forward with the fused expert
  * FFNs of ffns_fused, :382-442) ------------------------------------------------

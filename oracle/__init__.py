@@ -319,10 +319,6 @@ def _fwd_sigs():
         L.or_forward.argtypes = [P, C.POINTER(Model), P, P, C.c_int64, P, C.c_uint32, C.c_int, P, P]
         L.or_argmax.restype = C.c_int64
         L.or_argmax.argtypes = [P, C.c_size_t]
-        L.or_set_cr_math.restype = None
-        L.or_set_cr_math.argtypes = [C.c_int]
-        L.or_cr_math.restype = C.c_int
-        L.or_cr_math.argtypes = []
         L.or_rmsnorm.restype = None
         L.or_rmsnorm.argtypes = [P, P, P, C.c_size_t, C.c_float]
         L.or_rope_freqs.restype = None
@@ -387,21 +383,3 @@ def rope_rotate(v, head_dim, inv_freq, neox, pos):
     _fwd_sigs().or_rope_rotate(_p(v), v.size, head_dim, _p(f), int(neox), pos)
     return v
 
-
-class cr_math:
-    """Context manager: inside it the oracle's exp / sin / cos are the
-    correctly rounded values (what the CUDA kernels compute) instead of
-    glibc's expf / sinf / cosf (what the reference calls); see libm.c."""
-
-    def __init__(self, on=True):
-        self.on = on
-
-    def __enter__(self):
-        L = _fwd_sigs()
-        self.prev = L.or_cr_math()
-        L.or_set_cr_math(int(self.on))
-        return self
-
-    def __exit__(self, *exc):
-        _fwd_sigs().or_set_cr_math(self.prev)
-        return False

@@ -2,23 +2,17 @@
  * libm.c — the transcendental functions of the oracle.
  * TEST INFRASTRUCTURE ONLY (see sg_oracle.h).
  *
- * The reference calls f32::exp / sin / cos, which Rust's std takes from the
- * platform libm (glibc expf, sinf, cosf on Linux, within about half an ulp but
- * not correctly rounded).  The CUDA kernels compute the correctly rounded value
- * instead (the double-precision function rounded to float).  Mode 0 (default)
- * is glibc, mode 1 the correctly rounded value: with mode 1 the oracle and the
- * GPU share every rounding, so a test can check the rest of the arithmetic bit
- * for bit, and a second test measures what the libm choice alone changes.
+ * The reference calls f32::exp / sin / cos (smollm_chat.rs:586-588,
+ * :1200-1203, :1397-1420, :3463-3495), which Rust's std takes from the
+ * platform libm: glibc's expf, sinf and cosf on Linux.  The oracle calls the
+ * same functions of the host's glibc.  (The CUDA kernels compute glibc's
+ * results bit for bit from a restatement of its algorithm; tests/test_libm.py
+ * checks that restatement against this same libm over every float.)
  */
 #include <math.h>
 
 #include "sg_oracle.h"
 
-static int cr_math;
-
-void or_set_cr_math(int on) { cr_math = on != 0; }
-int or_cr_math(void) { return cr_math; }
-
-float or_expf(float x) { return cr_math ? (float)exp((double)x) : expf(x); }
-float or_sinf(float x) { return cr_math ? (float)sin((double)x) : sinf(x); }
-float or_cosf(float x) { return cr_math ? (float)cos((double)x) : cosf(x); }
+float or_expf(float x) { return expf(x); }
+float or_sinf(float x) { return sinf(x); }
+float or_cosf(float x) { return cosf(x); }

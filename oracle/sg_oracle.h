@@ -155,10 +155,8 @@ int or_forward(const uint8_t *base, const or_model *m, uint16_t *kcache, uint16_
  * last one on ties (Iterator::max_by). */
 int64_t or_argmax(const float *logits, size_t n);
 
-/* exp / sin / cos of the restatements (libm.c): glibc's (mode 0, default) or
- * correctly rounded (mode 1, what the CUDA kernels compute).  Process-wide. */
-void or_set_cr_math(int on);
-int or_cr_math(void);
+/* exp / sin / cos of the restatements (libm.c): the host's glibc expf / sinf /
+ * cosf, what f32::exp / sin / cos call on Linux. */
 float or_expf(float x);
 float or_sinf(float x);
 float or_cosf(float x);

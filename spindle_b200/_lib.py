@@ -101,6 +101,8 @@ SIGNATURES = {
     "sg_matvec_scratch": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P, U64, P]),
     "sg_matvec_static": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
     "sg_block_sums": (I32, [P, C.POINTER(SgMat), C.POINTER(SgQ8K), P, U64, U64, P]),
+    "sg_libm_eval": (I32, [I32, U64, U64, U64, P, P]),
+    "sg_binary_version": (I32, [P]),
     "sg_quantize_weights": (I32, [I32, P, U64, U64, P, P]),
     "sg_tiled16_bytes": (I32, [I32, U64, U64, C.POINTER(U64)]),
     "sg_repack_tiled16": (I32, [I32, P, U64, U64, P, P]),

@@ -25,7 +25,8 @@ def sources(csrc=CSRC):
 
 
 def headers(csrc=CSRC):
-    return sorted(glob.glob(os.path.join(csrc, "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h")))
+    return sorted(glob.glob(os.path.join(csrc, "*.cuh")) + glob.glob(os.path.join(csrc, "*.h")) +
+                  glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 
 def _newer(target, deps):

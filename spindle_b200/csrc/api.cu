@@ -1280,7 +1280,10 @@ sg_status sg_matvec_tp(const uint8_t *d_shard, const sg_mat *m, const float *d_x
                         m->rows, (cudaStream_t)stream, nullptr, &tp);
 }
 
-uint64_t sg_matvec_scratch_bytes(uint64_t cols, uint64_t n_vec) { return n_vec * sg_q8k_bytes(cols); }
+uint64_t sg_matvec_scratch_bytes(uint64_t cols, uint64_t n_vec) {
+    const uint64_t qb = sg_q8k_bytes(cols);
+    return qb && n_vec > UINT64_MAX / qb ? UINT64_MAX : n_vec * qb;  // saturates instead of wrapping
+}
 
 sg_status sg_matvec_scratch(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
                             uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, void *d_scratch,
@@ -1290,9 +1293,9 @@ sg_status sg_matvec_scratch(const uint8_t *d_base, const sg_mat *m, const float 
     if (st) return st;
     if (r1 == r0 || n_vec == 0) return SG_OK;
     if (!d_x || !d_out || !d_scratch || (n_vec > 1 && (ldx < m->cols || ldo < m->rows))) return SG_ERR_INVALID;
-    if (scratch_bytes < sg_matvec_scratch_bytes(m->cols, n_vec)) return SG_ERR_INVALID;
+    const uint64_t qb = sg_q8k_bytes(m->cols);  // > 0: check_mat rejected cols == 0
+    if (n_vec > scratch_bytes / qb) return SG_ERR_INVALID;  // a division, so a huge n_vec cannot wrap past it
     if (!aligned(d_scratch, 16)) return SG_ERR_ALIGN;
-    const uint64_t qb = sg_q8k_bytes(m->cols);
     for (uint64_t g = 0; g < n_vec; g += Q8K_MAXV) {
         const uint64_t nv = n_vec - g < Q8K_MAXV ? n_vec - g : Q8K_MAXV;
         sg_q8k q[Q8K_MAXV];

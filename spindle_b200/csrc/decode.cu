@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
             x1 = __fmul_rn(__fmul_rn(x1, inv), nw[ib]);
         }
         const float ang = __fmul_rn(fpos, a.inv_freq[i]);
-        const float s = (float)sin((double)ang), c = (float)cos((double)ang);
+        const float s = gm_sinf(ang), c = gm_cosf(ang);
         const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
         const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
         if (!is_k) {
@@ -376,8 +376,8 @@ __global__ void __launch_bounds__(HD < 256 ? 256 : 288) attention_kernel(const _
             const float mprev = lane == 0 ? carry : prev;
             if (t < s1) {
                 // alpha_t = exp(m_{t-1} - m_t), p_t = exp(s_t - m_t)
-                al[t] = expf_cr(__fsub_rn(mprev, m));
-                sc[t] = expf_cr(__fsub_rn(sc[t], m));
+                al[t] = expf_ref(__fsub_rn(mprev, m));
+                sc[t] = expf_ref(__fsub_rn(sc[t], m));
             }
             carry = __shfl_sync(0xffffffffu, m, 31);
         }
@@ -535,7 +535,7 @@ __global__ void rope_kv_batch_kernel(const __grid_constant__ RopeBatchArgs a) {
             const uint32_t i = lane + 32u * j;
             const uint32_t ia = a.neox ? i : 2 * i, ib = a.neox ? i + half : 2 * i + 1;
             const float ang = __fmul_rn(fpos, a.inv_freq[i]);
-            const float sn = (float)sin((double)ang), cs = (float)cos((double)ang);
+            const float sn = gm_sinf(ang), cs = gm_cosf(ang);
             const float y0 = __fsub_rn(__fmul_rn(x0[j], cs), __fmul_rn(x1[j], sn));
             const float y1 = __fadd_rn(__fmul_rn(x0[j], sn), __fmul_rn(x1[j], cs));
             if (is_q) {

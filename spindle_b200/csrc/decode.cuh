@@ -6,14 +6,11 @@
 //
 // Every fp32 operation follows the reference's order: the RMSNorm and head-norm
 // sums of squares are sequential, the attention recurrence runs position by
-// position, the GEMVs and MoE passes are the exact integer kernels.  The one
-// difference is the transcendental functions: sin/cos/exp here are correctly
-// rounded (double precision rounded to float) where the reference calls
-// glibc's sinf/cosf/expf (within an ulp), so an element can differ by one ulp
-// and the f16 KV rounding can carry that on.  Parity is therefore within
-// tolerance (logits 1e-3 relative, identical greedy tokens), checked against
-// the oracle's restatement; the reference holds no golden vectors for the
-// forward pass.
+// position, the GEMVs and MoE passes are the exact integer kernels, and
+// sin/cos/exp are glibc's sinf/cosf/expf bit for bit (glibc_math.h), the
+// functions the reference's f32::sin_cos / f32::exp call on Linux.  The step
+// is therefore bit-identical to the oracle's restatement of forward_slice
+// with the host's glibc; the reference holds no golden vectors for it.
 #pragma once
 
 #include "common.cuh"

@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(ROUTER_MAX_THREADS) moe_router_kernel(const __
                         float z = 0.0f;
 #pragma unroll 8
                         for (uint32_t k = 0; k < dim; k++) z = __fadd_rn(z, __fmul_rn(gv[k], xv[k]));
-                        gsc = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-z)));
+                        gsc = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_ref(-z)));
                     } else {
                         gsc = __int_as_float(0x7fc00000);
                     }

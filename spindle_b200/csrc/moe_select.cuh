@@ -95,7 +95,7 @@ __device__ __forceinline__ void select_warp(const float *logits, uint32_t ne, ui
     for (int o = 16; o > 0; o >>= 1) m = rmax(m, __shfl_xor_sync(0xffffffffu, m, o));
 #pragma unroll
     for (int i = 0; i < R; i++)
-        if (valid[i]) p[i] = tiled::expf_cr(__fsub_rn(p[i], m));
+        if (valid[i]) p[i] = tiled::expf_ref(__fsub_rn(p[i], m));
     // the sum in expert order (Iterator::sum), replayed identically by every
     // lane from shared memory; each group of loads is issued before its adds
 #pragma unroll
@@ -169,7 +169,7 @@ static __device__ void select(const float *logits, uint32_t ne, uint32_t k, int3
     __syncthreads();
     float mx = red[0];
     for (uint32_t w = 1; w < nt / 32; w++) mx = rmax(mx, red[w]);
-    for (uint32_t e = tid; e < ne; e += nt) P[e] = tiled::expf_cr(__fsub_rn(P[e], mx));
+    for (uint32_t e = tid; e < ne; e += nt) P[e] = tiled::expf_ref(__fsub_rn(P[e], mx));
     __syncthreads();
     if (tid == 0) {
         // the sum, in order (Iterator::sum); each group of loads is issued

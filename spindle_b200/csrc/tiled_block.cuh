@@ -4,6 +4,7 @@
 #pragma once
 
 #include "gemv_tiled.cuh"
+#include "glibc_math.h"
 
 namespace sg {
 
@@ -50,16 +51,14 @@ __device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddep
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// exp for the reference's f32::exp: the double exponential rounded to float,
-// i.e. the correctly rounded expf.  glibc's expf (what f32::exp calls on
-// Linux) is within 0.502 ulp, so the two agree except where the exact value
-// lies within a hair of a rounding midpoint between floats.
-__device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
+// exp for the reference's f32::exp: glibc's expf, bit for bit (what f32::exp
+// calls on Linux; glibc_math.h restates it).
+__device__ __forceinline__ float expf_ref(float x) { return gm_expf(x); }
 
 // silu(x) * u with the reference's roundings (smollm_chat.rs:586-588, :411):
 // x / (1 + exp(-x)), then times u.
 __device__ __forceinline__ float silu_mul(float x, float u) {
-    const float e = expf_cr(-x);
+    const float e = expf_ref(-x);
     return __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, e)), u);
 }
 

@@ -66,19 +66,24 @@ def host_weights(cfg, dtypes, seed=0, wscale=0.05):
 
 
 def oracle_decoder(cfg, dtypes, W):
-    """The oracle's Decoder over one byte buffer holding W (32-byte aligned)."""
-    parts, off = [], {}
-    pos = 0
+    """The oracle's Decoder over one byte buffer holding W (32-byte aligned).
+    W's values may be numpy arrays or torch tensors (CUDA ones are copied
+    straight into their slice of the buffer, so a model of many GB is held on
+    the host once)."""
+    off, pos = {}, 0
     for name, arr in W.items():
-        b = np.ascontiguousarray(arr).reshape(-1).view(np.uint8)
-        pad = (-pos) % 32
-        if pad:
-            parts.append(np.zeros(pad, np.uint8))
-            pos += pad
+        pos += (-pos) % 32
         off[name] = pos
-        parts.append(b)
-        pos += b.nbytes
-    buf = np.concatenate(parts)
+        pos += arr.nbytes if isinstance(arr, np.ndarray) else arr.numel() * arr.element_size()
+    buf = np.zeros(pos, np.uint8)
+    for name, arr in W.items():
+        if isinstance(arr, np.ndarray):
+            b = np.ascontiguousarray(arr).reshape(-1).view(np.uint8)
+            buf[off[name]:off[name] + b.nbytes] = b
+        else:
+            import torch
+            b = arr.contiguous().reshape(-1).view(torch.uint8)
+            torch.from_numpy(buf[off[name]:off[name] + b.numel()]).copy_(b)
     c = cfg
     dim, hd = c["dim"], c["head_dim"]
     q_dim, kv_dim = c["n_heads"] * hd, c["n_kv_heads"] * hd

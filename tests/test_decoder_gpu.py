@@ -1,10 +1,9 @@
 """The GPU decoder step (sg_forward) against the oracle's forward_slice.
 
-Every fp32 operation of the step follows the reference's order on the GPU, so
-with the oracle's exp/sin/cos switched to the correctly rounded values the
-kernels compute (oracle.cr_math) the logits, the KV caches and the greedy
-tokens are equal bit for bit.  The reference itself calls glibc's expf, sinf
-and cosf; test_oracle_forward.py measures what that choice alone changes.
+Every fp32 operation of the step follows the reference's order on the GPU and
+exp / sin / cos are glibc's expf / sinf / cosf bit for bit (the functions the
+reference's f32::exp / sin_cos call, which the oracle calls too), so the
+logits, the KV caches and the greedy tokens are equal bit for bit.
 """
 import os
 import sys
@@ -26,33 +25,35 @@ def bits(a):
     return np.where(np.isnan(a), np.float32(np.nan), a).view(np.uint32)
 
 
-def run_pair(cfg, dtypes, seed, prompt, n_new, dev, qk_adjacent=True):
-    """Token by token against the oracle with correctly rounded exp/sin/cos
-    (oracle.cr_math, the kernels' libm): logits bit for bit, the same greedy
-    tokens and device state.  What glibc's expf/sinf/cosf change on their own
-    is measured in test_oracle_forward.py."""
-    W = U.host_weights(cfg, dtypes, seed=seed)
-    ref = U.oracle_decoder(cfg, dtypes, W)
-    gpu = Decoder(cfg, U.device_weights(W, dev), dtypes, dev, qk_adjacent=qk_adjacent)
+def run_pair(cfg, dtypes, seed, prompt, n_new, dev, qk_adjacent=True, W=None):
+    """Token by token against the oracle (glibc's expf/sinf/cosf, as the
+    reference): logits bit for bit, the same greedy tokens and device state.
+    W: CUDA weights to use instead of seeded host ones."""
+    if W is None:
+        W = U.host_weights(cfg, dtypes, seed=seed)
+        ref = U.oracle_decoder(cfg, dtypes, W)
+        W = U.device_weights(W, dev)
+    else:
+        ref = U.oracle_decoder(cfg, dtypes, W)
+    gpu = Decoder(cfg, W, dtypes, dev, qk_adjacent=qk_adjacent)
     toks_ref, toks_gpu = [], []
     seq = list(prompt)
-    with O.cr_math():
-        for pos in range(len(prompt) + n_new):
-            t = seq[pos]
-            _, lr = ref.forward(t, pos)
-            gpu.set_state(t, pos)
-            gpu.step()
-            torch.cuda.synchronize()
-            lg = gpu.logits.cpu().numpy()
-            assert np.array_equal(bits(lg), bits(lr)), (pos, float(np.abs(lg - lr).max()))
-            nxt_ref = O.argmax(lr)
-            nxt_gpu = int(gpu.token.item())
-            assert int(gpu.state[0].item()) == nxt_gpu and int(gpu.state[1].item()) == pos + 1
-            if pos >= len(prompt) - 1:
-                toks_ref.append(nxt_ref)
-                toks_gpu.append(nxt_gpu)
-                if len(seq) == pos + 1:
-                    seq.append(nxt_ref)
+    for pos in range(len(prompt) + n_new):
+        t = seq[pos]
+        _, lr = ref.forward(t, pos)
+        gpu.set_state(t, pos)
+        gpu.step()
+        torch.cuda.synchronize()
+        lg = gpu.logits.cpu().numpy()
+        assert np.array_equal(bits(lg), bits(lr)), (pos, float(np.abs(lg - lr).max()))
+        nxt_ref = O.argmax(lr)
+        nxt_gpu = int(gpu.token.item())
+        assert int(gpu.state[0].item()) == nxt_gpu and int(gpu.state[1].item()) == pos + 1
+        if pos >= len(prompt) - 1:
+            toks_ref.append(nxt_ref)
+            toks_gpu.append(nxt_gpu)
+            if len(seq) == pos + 1:
+                seq.append(nxt_ref)
     assert toks_gpu == toks_ref
     return ref, gpu
 
@@ -126,11 +127,26 @@ def test_decoder_graph_replay(dev):
 
 def test_decoder_qwen3_0_6b_shape(dev):
     # Qwen3-0.6B architecture, full size (28 layers, hidden
-    # 1024, FFN 3072, 16/8 heads of 128, vocab 151936), a few steps
+    # 1024, FFN 3072, 16/8 heads of 128, vocab 151936): 2 prompt tokens, then
+    # 40 greedy tokens, every step's logits bit for bit
     cfg = dict(dim=1024, n_heads=16, n_kv_heads=8, head_dim=128, n_layers=28, vocab=151936, max_seq=64,
                rope_theta=1e6, rms_eps=1e-6, n_ff=3072, rope_neox=True)
     dtypes = U.dtypes_for(cfg)
-    run_pair(cfg, dtypes, 3, [100, 2000], 2, dev)
+    run_pair(cfg, dtypes, 3, [100, 2000], 40, dev)
+
+
+def test_decoder_qwen3_30b_a3b_shape(dev):
+    # Qwen3-30B-A3B architecture at full size (48 layers,
+    # hidden 2048, 32 / 4 heads of 128, 128 experts of FFN 768, top 8, vocab
+    # 151936, Q4_K_M mix), random-init on the GPU with the library's quantizer
+    # (the bench's model): a 4-token prompt, then 10 greedy tokens, logits bit
+    # for bit against the oracle at every position, and the same tokens
+    from spindle_b200.decoder import qwen3_dtypes, random_weights
+    cfg = dict(dim=2048, n_heads=32, n_kv_heads=4, head_dim=128, n_layers=48, vocab=151936, max_seq=32,
+               rope_theta=1e6, rms_eps=1e-6, rope_neox=True, moe=dict(n_expert=128, n_used=8, n_ff=768, norm=True))
+    dtypes = qwen3_dtypes(cfg, embed=U.Q4_K)
+    W = random_weights(cfg, dtypes, dev, seed=5)
+    run_pair(cfg, dtypes, 0, [11, 151000, 42, 7000], 10, dev, W=W)
 
 
 def test_decoder_bad_args(dev):

@@ -181,31 +181,3 @@ def test_rope_matches_reference_and_composes(neox):
     a = O.rope_rotate(a, hd, f, neox, -5.0)
     b = O.rope_rotate(v, hd, f, neox, 12.0)
     assert np.abs(a - b).max() < 1e-4
-
-
-def test_glibc_vs_correctly_rounded_libm_long_context():
-    # The reference's libm (glibc expf/sinf/cosf, within about half an ulp)
-    # against the correctly rounded values the CUDA kernels compute: a one-ulp
-    # difference now and then in a softmax weight can move an activation by an
-    # ulp, and the next integer matvec's Q8_K rounding can turn that into one
-    # quantization step.  Over a 262-token context the greedy tokens stay the
-    # same and the logits stay close, with rare single-position spikes.
-    cfg = dict(U.DENSE, max_seq=300)
-    dtypes = U.dtypes_for(cfg)
-    W = U.host_weights(cfg, dtypes, seed=51)
-    a, b = U.oracle_decoder(cfg, dtypes, W), U.oracle_decoder(cfg, dtypes, W)
-    toks = np.random.default_rng(8).integers(0, cfg["vocab"], 262).tolist()
-    rels, ties = [], 0
-    for pos, t in enumerate(toks):
-        _, lg = a.forward(t, pos)
-        with O.cr_math():
-            _, lc = b.forward(t, pos)
-        rels.append(float(np.abs(lg - lc).max() / np.abs(lc).max()))
-        if O.argmax(lg) != O.argmax(lc):
-            top2 = np.sort(lc)[-2:]
-            assert top2[1] - top2[0] <= 1e-2 * np.abs(lc).max(), pos  # only a near tie may flip
-            ties += 1
-    rels = np.array(rels)
-    assert ties <= 2
-    assert rels.max() <= 5e-2
-    assert (rels > 1e-3).mean() <= 0.05
