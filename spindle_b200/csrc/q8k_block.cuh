@@ -56,29 +56,65 @@ __device__ __forceinline__ float q8k_amax(const float (&xv)[8], uint32_t lane) {
 
 // Values in registers (lane t: x[8t .. 8t+7]); qs: 256 int8 (8-byte aligned);
 // bsums: 16 int16; d: one float.  All 32 lanes of the warp call it.
+//
+// Fast path (no NaN or Inf in the block, 127/amax finite): |x * (127/amax)|
+// stays below 127.5, so cvtps_epi32 needs no saturation, and adding 1.5 * 2^23
+// to the rounded product rounds it to the nearest integer, ties to even, as
+// cvtps_epi32 does: the low byte of the sum's bits is the int8 value.  Any
+// other block takes the general path, which replays the reference's NaN,
+// Inf and overflow behaviour.
 __device__ __forceinline__ void q8k_block_regs(const float (&xv)[8], int8_t *qs, int16_t *bsums, float *d,
                                                uint32_t lane) {
-    const float amax = q8k_amax(xv, lane);
-    int8_t q[8];
-    if (!(amax > 0.0f) || isinf(amax)) {
+    bool special = false;
+    float m = 0.0f;
 #pragma unroll
-        for (int k = 0; k < 8; k++) q[k] = 0;
-        if (lane == 0) *d = 0.0f;
-    } else {
-        const float inv = __fdiv_rn(127.0f, amax);
-        if (lane == 0) *d = __fdiv_rn(amax, 127.0f);
-#pragma unroll
-        for (int k = 0; k < 8; k++) q[k] = cvt_pack_i8(__fmul_rn(xv[k], inv));
+    for (int k = 0; k < 8; k++) {
+        const float a = fabsf(xv[k]);
+        special |= !(a <= 3.402823466e38f);  // NaN or Inf
+        m = fmaxf(m, a);
     }
     uint32_t w0 = 0, w1 = 0;
-    int s = 0;
+    bool general = __any_sync(0xffffffffu, special);
+    if (!general) {
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-        w0 |= (uint32_t)(uint8_t)q[k] << (8 * k);
-        w1 |= (uint32_t)(uint8_t)q[k + 4] << (8 * k);
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (m > 0.0f) {
+            const float inv = __fdiv_rn(127.0f, m);
+            if (isinf(inv)) {
+                general = true;  // a subnormal amax: the products overflow
+            } else {
+                if (lane == 0) *d = __fdiv_rn(m, 127.0f);
+                uint32_t u[8];
+#pragma unroll
+                for (int k = 0; k < 8; k++) u[k] = __float_as_uint(__fadd_rn(__fmul_rn(xv[k], inv), 12582912.0f));
+                w0 = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410);
+                w1 = __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410);
+            }
+        } else if (lane == 0) {
+            *d = 0.0f;  // all zero: d = 0, q = 0
+        }
     }
+    if (general) {
+        const float amax = q8k_amax(xv, lane);
+        int8_t q[8];
+        if (!(amax > 0.0f) || isinf(amax)) {
 #pragma unroll
-    for (int k = 0; k < 8; k++) s += q[k];
+            for (int k = 0; k < 8; k++) q[k] = 0;
+            if (lane == 0) *d = 0.0f;
+        } else {
+            const float inv = __fdiv_rn(127.0f, amax);
+            if (lane == 0) *d = __fdiv_rn(amax, 127.0f);
+#pragma unroll
+            for (int k = 0; k < 8; k++) q[k] = cvt_pack_i8(__fmul_rn(xv[k], inv));
+        }
+        w0 = w1 = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            w0 |= (uint32_t)(uint8_t)q[k] << (8 * k);
+            w1 |= (uint32_t)(uint8_t)q[k + 4] << (8 * k);
+        }
+    }
+    int s = __dp4a((int)w0, 0x01010101, __dp4a((int)w1, 0x01010101, 0));
     reinterpret_cast<uint2 *>(qs)[lane] = make_uint2(w0, w1);
     s += __shfl_xor_sync(0xffffffffu, s, 1);  // a group of 16 values = lanes 2g, 2g+1
     if ((lane & 1u) == 0) bsums[lane / 2] = (int16_t)s;

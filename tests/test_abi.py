@@ -37,7 +37,7 @@ def test_library_is_self_contained():
 
 
 @pytest.mark.gpu
-def test_library_kernels_are_sm100():
+def test_library_kernels_are_sm100(dev):
     # the architecture the runtime loaded the kernels for, as it reports it
     v = C.c_int32()
     assert _lib.load().sg_binary_version(C.byref(v)) == 0
@@ -89,3 +89,20 @@ def test_q8k_layout():
     assert lib.sg_q8k_view(C.c_void_p(0x10000), 1024, C.byref(q)) == 0
     assert (q.d, q.qs, q.bsums, q.n) == (0x10000, 0x10010, 0x10410, 1024)
     assert lib.sg_q8k_view(C.c_void_p(0x10004), 1024, C.byref(q)) == 4
+
+
+def test_scratch_limits_do_not_wrap():
+    # n_vec * sg_q8k_bytes(cols) would wrap a 64-bit product for n_vec near
+    # 2^64 / qb; both scratch entry points compare by division, so such a
+    # request is rejected before anything is launched
+    lib = _lib.load()
+    fake = C.c_void_p(0x100000)
+    m = _lib.SgMat(12, 0, 0, 1024, 16)
+    qb = lib.sg_q8k_bytes(1024)
+    big = (1 << 64) // qb + 1          # big * qb wraps to a small number
+    assert (big * qb) % (1 << 64) < 262144
+    assert lib.sg_matvec_scratch_bytes(1024, big) == (1 << 64) - 1  # saturates
+    huge_ld = 1 << 40
+    assert lib.sg_matvec_static(fake, C.byref(m), fake, huge_ld, fake, huge_ld, big, 0, 16, None) == 9
+    assert lib.sg_matvec_scratch(fake, C.byref(m), fake, huge_ld, fake, huge_ld, big, 0, 16, fake, 1 << 20,
+                                 None) == 1

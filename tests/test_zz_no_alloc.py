@@ -66,3 +66,24 @@ def test_static_scratch_limit_and_row_range(dev):
     assert torch.equal(got[:, 5:33].view(torch.int32), want[:, 5:33].view(torch.int32))
     assert torch.isnan(got[:, :5]).all() and torch.isnan(got[:, 33:]).all()
     sg.device_status()
+
+
+def test_static_scratch_allocates_nothing(dev):
+    # the property the entry point exists for: after its first call on the
+    # device (which only looks the array up), further calls leave the
+    # device's free memory exactly as it was, so nothing was allocated
+    rng = O.Rng(123)
+    n, rows, nvec = 4096, 300, 4
+    w = torch.from_numpy(O.random_matrix(sg.Q4_K, n, rows, rng)).to(dev)
+    t, mt = sg.repack_tiled16(sg.Q4_K, w, rows, n)
+    xs = torch.from_numpy(np.stack([rng.fill(-2.0, 2.0, n) for _ in range(nvec)])).to(dev)
+    out = torch.empty(nvec, rows, device=dev)
+    assert call_static(t, mt, xs, out) == 0
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(50):
+        assert call_static(t, mt, xs, out) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    want = sg.matvec_scratch(t, mt, xs)
+    assert torch.equal(out.view(torch.int32), want.view(torch.int32))
