@@ -12,9 +12,12 @@ read again.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--nvec B] [--impl reference]
 
-N > 1 (under torchrun): weak scaling.  Every rank owns a full-size row shard
-of its own (seeded by rank); rows are independent, so the data path has no
-collective.  value = all ranks' bytes / max-over-ranks time.
+N > 1 (under torchrun): strong scaling.  Every matrix of the sweep is split
+by rows over the ranks (par_rows's split, smollm_chat.rs:332-337); one
+sg_matvec_tp per matrix leaves the whole output on every rank, its rows
+stored by each rank's GEMV epilogue straight into every peer's receive buffer
+over NVLink (no NCCL call on the data path).  value = the whole sweep's
+algorithmic bytes / max-over-ranks step time.
 --impl reference: the reference's CPU algorithm (the oracle's C restatement
 of the AVX2 kernels with its worker pool) on all host cores, same metric.
 """
@@ -34,8 +37,20 @@ Q4_K, Q6_K = 12, 14
 SHAPES = [(Q4_K, 4096, 4096), (Q6_K, 4096, 4096), (Q4_K, 14336, 4096), (Q6_K, 14336, 4096),
           (Q4_K, 4096, 14336), (Q6_K, 4096, 14336), (Q6_K, 151936, 1024)]
 BLK = {Q4_K: 144, Q6_K: 210}
+L2_BYTES = 126 * 1024 * 1024
 NAME = {Q4_K: "Q4_K", Q6_K: "Q6_K"}
 METRIC = "K-quant GEMV HBM GB/s (Q4_K/Q6_K x Q8_K sweep)"
+
+
+def cpu_model():
+    """The host CPU's model name (the cpu_baseline's hardware)."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def alg_bytes(dt, rows, cols, n):
@@ -192,9 +207,9 @@ def run_reference(args):
     line = {"impl": "reference", "metric": TP_METRIC if tp else METRIC, "value": round(value, 3), "unit": "GB/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True,
-            "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "int8/int32 + fp32",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8/int32 + fp32",
             "data": "synthetic", "config": config_block(args, 1),
-            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port", "cpu_model": cpu_model(),
                              "sample": sample + "; oracle = C restatement of quant_q8k.rs with the worker pool"},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -203,7 +218,8 @@ def run_reference(args):
 def config_block(args, world):
     return {"workload": "gemv_sweep_n%d" % args.nvec, "layout": getattr(args, "layout", "tiled"),
             "shapes": ["%s %dx%d" % (NAME[dt], r, c) for dt, r, c in SHAPES],
-            "n_vec": args.nvec, "global_batch": args.nvec * world, "parallelism": "row-shard x%d (weak)" % world,
+            "n_vec": args.nvec, "global_batch": args.nvec,
+            "parallelism": "single GPU" if world == 1 else "row-split x%d (strong)" % world,
             "l2": "314 MB of weights per step > 126 MB L2: each matrix is evicted before its next read",
             "weights": "N(0,0.02) seeded, own Q4_K/Q6_K quantizer", "activations": "N(0,1) seeded"}
 
@@ -403,7 +419,7 @@ def run_gpu(args):
     line = None
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "int8 x int4/int6 -> int32, fp32 epilogue", "data": "synthetic",
                 "config": config_block(args, world),
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -524,7 +540,7 @@ def run_reference_moe(args):
             "steps": steps, "warmup": args.warmup, "ms_per_step": round(per_layer * MOE_LAYERS * 1e3, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8/int32 + fp32", "data": "synthetic", "config": moe_config(1),
-            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port", "cpu_model": cpu_model(),
                              "sample": "%d token-layers through the oracle's moe_forward (C restatement of "
                                        "smollm_chat.rs moe_forward/ffns_fused), one thread" % n},
             "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -808,7 +824,7 @@ def run_float(args):
                     break
             el = (time.perf_counter() - t0) / n
             sample_bytes = sum(max(1, int(r * 0.05)) * float_row_bytes(dt, c) for dt, r, c in FLOAT_SHAPES)
-            cpu = {"value": round(sample_bytes / el / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            cpu = {"value": round(sample_bytes / el / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port", "cpu_model": cpu_model(),
                    "sample": "%d passes of the oracle's matvec_rows (the restated AVX2 float kernels, one thread) "
                              "over the first 5%% of each matrix's rows" % n}
         line = {"metric": FLOAT_METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
@@ -839,7 +855,7 @@ def run_float(args):
 TP_METRIC = "K-quant GEMV HBM GB/s, rows split over the GPUs with the gather fused in (Q4_K/Q6_K x Q8_K sweep)"
 
 
-def run_gpu_tp(args):
+def run_gpu_tp(args, metric=None):
     """The sweep's matrices split by rows over the ranks (strong scaling): every
     rank holds its par_rows shard of all seven, and one sg_matvec_tp per
     matrix leaves the whole output on every rank (peer stores over NVLink,
@@ -869,12 +885,26 @@ def run_gpu_tp(args):
         del wq
         X.append(torch.randn(nvec, c, device=dev, generator=gen))
         BUF.append(grp.buffer(nvec, r))
+    # A rank's shard of the sweep is 314 MB / N: from 4 GPUs on it fits in the
+    # 126 MB L2, so the steps cycle through copies of the shards holding at
+    # least 2.5x L2 per rank, and every matrix is read from HBM.
+    import copy
+    shard_bytes = sum(sh.w.numel() for sh in shards)
+    ncopies = max(1, -(-int(2.5 * L2_BYTES) // shard_bytes)) if world > 1 else 1
+    copies = [shards]
+    for _ in range(1, ncopies):
+        cs = []
+        for sh in shards:
+            sc = copy.copy(sh)
+            sc.w = sh.w.clone()
+            cs.append(sc)
+        copies.append(cs)
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(device=dev)
 
-    def step():
+    def step(c=0):
         for k in range(len(SHAPES)):
-            matvec_tp(shards[k], X[k], grp, BUF[k], stream=stream)
+            matvec_tp(copies[c][k], X[k], grp, BUF[k], stream=stream)
 
     def barrier():
         if world > 1:
@@ -892,17 +922,20 @@ def run_gpu_tp(args):
     with torch.cuda.stream(stream):
         step()
         torch.cuda.synchronize()
-        g_step = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_step, stream=stream):
-            step()
-        for _ in range(args.warmup):
-            g_step.replay()
+        g_steps = []
+        for c in range(ncopies):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step(c)
+            g_steps.append(g)
+        for i in range(args.warmup):
+            g_steps[i % ncopies].replay()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local) as clk:
             e0.record(stream)
-            for _ in range(args.steps):
-                g_step.replay()
+            for i in range(args.steps):
+                g_steps[i % ncopies].replay()
             e1.record(stream)
             e1.synchronize()
         barrier()
@@ -921,29 +954,32 @@ def run_gpu_tp(args):
             off += xsz[k]
         sp = C.c_void_p(stream.cuda_stream)
 
-        def e2e_step():
+        def e2e_step(c=0):
             _lib.check(lib.sg_memcpy_h2d(C.c_void_p(XC.data_ptr()), C.c_void_p(h_x.data_ptr()), h_x.numel() * 4,
                                          sp), "h2d")
             o = 0
             for k in range(len(SHAPES)):
-                matvec_tp(shards[k], XV[k], grp, BUF[k], stream=stream)
+                matvec_tp(copies[c][k], XV[k], grp, BUF[k], stream=stream)
                 _lib.check(lib.sg_memcpy_d2h(C.c_void_p(h_o.data_ptr() + 4 * o), C.c_void_p(BUF[k].tensor.data_ptr()),
                                              osz[k] * 4, sp), "d2h")
                 o += osz[k]
 
         e2e_step()
         torch.cuda.synchronize()
-        g_e2e = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_e2e, stream=stream):
-            e2e_step()
-        for _ in range(args.warmup):
-            g_e2e.replay()
+        g_e2es = []
+        for c in range(ncopies):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                e2e_step(c)
+            g_e2es.append(g)
+        for i in range(args.warmup):
+            g_e2es[i % ncopies].replay()
         barrier()
         reps = max(3, min(args.steps, 2000))
         b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         b0.record(stream)
-        for _ in range(reps):
-            g_e2e.replay()
+        for i in range(reps):
+            g_e2es[i % ncopies].replay()
         b1.record(stream)
         b1.synchronize()
         barrier()
@@ -960,12 +996,17 @@ def run_gpu_tp(args):
     nvl = sum(4 * nvec * (s.r1 - s.r0) * (world - 1) for s in shards)
     line = None
     if rank == 0:
-        line = {"metric": TP_METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        line = {"metric": metric or TP_METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "int8 x int4/int6 -> int32, fp32 epilogue", "data": "synthetic",
-                "config": dict(config_block(args, world), workload="gemv_tp_sweep_n%d" % nvec,
-                               parallelism="row-split x%d, gather fused (peer stores)" % world,
-                               global_batch=nvec),
+                "config": dict(config_block(args, world),
+                               workload=("gemv_sweep_n%d" if metric else "gemv_tp_sweep_n%d") % nvec,
+                               parallelism="row-split x%d (strong), gather fused (peer stores)" % world,
+                               global_batch=nvec,
+                               l2="%d copies of this rank's %.1f MB of shards, cycled step by step (%.0f MB > "
+                                  "2.5 x the 126 MB L2): every matrix is read from HBM"
+                                  % (ncopies, shard_bytes / 1e6, ncopies * shard_bytes / 1e6)),
                 "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(per_gpu / peak, 4), "traffic": None, "peak_source": peak_src,
                              "kernel": "gemv_tiled_kernel (row-split, peer-store epilogue)",
@@ -979,7 +1020,7 @@ def run_gpu_tp(args):
                                "matrix, sg_memcpy_d2h of each whole output"},
                 "gpu_launches": len(SHAPES) * args.steps,
                 "clocks": clk.summary()}
-    del g_step, g_e2e
+    del g_steps, g_e2es, g
     grp.close()
     if world > 1:
         dist.destroy_process_group()
@@ -1473,7 +1514,7 @@ def main():
         if rank == 0 and line is not None:
             if host is not None:
                 per_tok, n = decode_cpu_sample(cfg, dtypes, host, args.cpu_budget)
-                line["cpu_baseline"] = {"value": round(1.0 / per_tok, 3), "unit": "tok/s", "cores": 1, "kind": "port",
+                line["cpu_baseline"] = {"value": round(1.0 / per_tok, 3), "unit": "tok/s", "cores": 1, "kind": "port", "cpu_model": cpu_model(),
                                         "sample": "the oracle's forward_slice (one thread) on the model's first 2 "
                                                   "layers + embedding + head, %d tokens; per-token time = "
                                                   "(2-layer time - head time) x %d / 2 + head time"
@@ -1504,7 +1545,7 @@ def main():
         if rank == 0 and line is not None:
             if world == 1 and args.cpu_budget > 0:
                 per_layer, gbs, n = moe_cpu_sample([host0], args.cpu_budget)
-                line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port", "cpu_model": cpu_model(),
                                         "sample": "%d token-layers through the oracle's moe_forward (same layer "
                                                   "shape, host-quantized weights), one thread, %.1f s"
                                                   % (n, per_layer * n)}
@@ -1524,8 +1565,10 @@ def main():
     if args.impl == "reference":
         run_reference(args)
         return
-    if args.workload == "gemv_tp":
-        line = run_gpu_tp(args)
+    rank, world, _ = rank_env()
+    if args.workload == "gemv_tp" or world > 1:
+        # N > 1: the headline sweep row-split over the GPUs (strong scaling)
+        line = run_gpu_tp(args, metric=METRIC if args.workload == "gemv" else None)
         if line is not None:
             print(json.dumps(line), flush=True)
         return
@@ -1539,7 +1582,7 @@ def main():
             threads = os.cpu_count() or 1
             sweep_s, n = cpu_sample(wh, args.nvec, args.cpu_budget, threads)
             cpu_v = step_bytes(args.nvec) / sweep_s / 1e9
-            line["cpu_baseline"] = {"value": round(cpu_v, 2), "unit": "GB/s", "cores": threads, "kind": "port",
+            line["cpu_baseline"] = {"value": round(cpu_v, 2), "unit": "GB/s", "cores": threads, "kind": "port", "cpu_model": cpu_model(),
                                     "sample": "%d full sweeps (same 7 matrices, same bytes) through the oracle's "
                                               "pooled matvec, %.1f s" % (n, sweep_s * n)}
         print(json.dumps(line), flush=True)

@@ -39,21 +39,23 @@ def test_stages_on_one_gpu(dev, kind):
         pos += c
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_stage_pipeline():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_pipeline_ranks(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with socket.socket() as sk:
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
-    procs = [ctx.Process(target=tp_util.pipe_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=tp_util.pipe_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
-    for _ in range(2):
-        r, msg = q.get(timeout=600)
+    for _ in range(world):
+        r, msg = q.get(timeout=900)
         res.setdefault(r, []).append(msg)
     for p in procs:
         p.join(timeout=120)
-    assert res == {0: ["ok"], 1: ["ok"]}, res
+    assert res == {r: ["ok"] for r in range(world)}, res

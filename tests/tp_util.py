@@ -181,48 +181,52 @@ def ep_rank(rank, world, port, out):
 
 
 def pipe_rank(rank, world, port, out):
-    # two pipeline stages: rank 0 runs the first half of the layers on each
-    # prompt chunk and sends the residual; rank 1 receives it, runs the rest
-    # and the head, and compares with the whole model on its own GPU
+    # a pipeline of `world` stages: stage p runs layers [L*p/P, L*(p+1)/P) of
+    # each prompt chunk (par_rows's split over the layers), receiving the
+    # residual from stage p-1 and sending it to stage p+1; the last stage runs
+    # the head and compares with the whole model on its own GPU
     import numpy as np
     import torch
     import torch.distributed as dist
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import decoder_util as U
     from spindle_b200.decoder import Decoder
-    from spindle_b200.tp import PipeLink, TpGroup
+    from spindle_b200.tp import PipeLink, TpGroup, shard_rows
     init(rank, world, port, "nccl")
     dev = torch.device("cuda", rank)
     grp = None
     try:
         grp = TpGroup(device=dev)
         msgs = []
-        for kind, cfg in [("moe", dict(U.MOE, n_layers=4, max_seq=128)), ("dense", dict(U.DENSE, n_layers=4))]:
+        for kind, cfg in [("moe", dict(U.MOE, n_layers=8, max_seq=128)), ("dense", dict(U.DENSE, n_layers=8))]:
             dtypes = U.dtypes_for(cfg)
             W = U.device_weights(U.host_weights(cfg, dtypes, seed=61), dev)
             stage = Decoder(cfg, W, dtypes, dev)
-            link = PipeLink(grp, 0, 1, 32 * cfg["dim"])
+            links = [PipeLink(grp, p, p + 1, 32 * cfg["dim"]) for p in range(world - 1)]
             toks = np.random.default_rng(3).integers(0, cfg["vocab"], 50).tolist()
             chunks = [9, 32, 1, 8]
-            half = cfg["n_layers"] // 2
+            L = cfg["n_layers"]
+            l0, l1 = shard_rows(L, world, rank)
+            whole = Decoder(cfg, W, dtypes, dev) if rank == world - 1 else None
             pos = 0
-            if rank == 0:
-                for c in chunks:
-                    (h,) = stage.forward_batch_range(pos, 0, half, tokens=toks[pos:pos + c])
-                    link.send(h)
-                    pos += c
-                torch.cuda.synchronize(dev)
-            else:
-                whole = Decoder(cfg, W, dtypes, dev)
-                for c in chunks:
-                    h = link.recv(torch.empty(c, cfg["dim"], device=dev))
-                    lg, gr = stage.forward_batch_range(pos, half, cfg["n_layers"], hidden=h)
+            for c in chunks:
+                if rank == 0:
+                    (h,) = stage.forward_batch_range(pos, l0, l1, tokens=toks[pos:pos + c])
+                else:
+                    h = links[rank - 1].recv(torch.empty(c, cfg["dim"], device=dev))
+                    if rank < world - 1:
+                        (h,) = stage.forward_batch_range(pos, l0, l1, hidden=h)
+                if rank < world - 1:
+                    links[rank].send(h)
+                else:
+                    lg, gr = stage.forward_batch_range(pos, l0, l1, hidden=h)
                     wl, wg = whole.forward_batch(toks[pos:pos + c], pos)
                     torch.cuda.synchronize(dev)
                     if not (np.array_equal(lg.cpu().numpy().view(np.uint32), wl.cpu().numpy().view(np.uint32))
                             and torch.equal(gr, wg)):
                         msgs.append((kind, pos, c))
-                    pos += c
+                pos += c
+            torch.cuda.synchronize(dev)
             dist.barrier()
         __import__("spindle_b200").device_status()
         out.put((rank, "ok" if not msgs else repr(msgs)))
