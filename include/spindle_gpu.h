@@ -426,6 +426,24 @@ SG_API sg_status sg_model_prepare(const sg_model *m, void *d_scratch, uint64_t s
 SG_API sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_scratch, uint64_t scratch_bytes,
                             float *d_hidden, float *d_logits, int64_t *d_token, void *stream);
 
+/* The decoder step with expert parallelism (moe_forward under the layer split
+ * of cluster_net.rs:776-795 and smollm_chat.rs:1178-1392, the experts spread
+ * over GPUs instead of over PCs): every rank holds the whole model except the
+ * experts -- each MoE layer's m->layers[l].moe keeps only this rank's experts
+ * [eps[l].expert_lo, eps[l].expert_hi), packed, with the whole router and
+ * n_expert -- and runs the same step on the same state.  Each MoE layer is
+ * sg_moe_forward_batch_ep for one token: every rank computes the choice, runs
+ * its own experts' slots and stores their outputs into every rank's receive
+ * buffer over NVLink, and every rank sums them in router order, so every rank
+ * ends the step with the same logits and greedy token as sg_forward on one
+ * GPU, bit for bit.  eps: host array [n_layers] (entries of dense layers are
+ * not read), each set up as for sg_moe_forward_batch_ep with n_tok_max >= 1.
+ * Scratch: sg_model_ep_scratch_bytes(m) bytes, prepared by sg_model_prepare. */
+SG_API uint64_t sg_model_ep_scratch_bytes(const sg_model *m);
+SG_API sg_status sg_forward_ep(const sg_model *m, const sg_moe_ep *eps, int32_t *d_state, void *d_kv,
+                               void *d_scratch, uint64_t scratch_bytes, float *d_hidden, float *d_logits,
+                               int64_t *d_token, void *stream);
+
 /* forward_batch_slice + compute_logits_batch (smollm_chat.rs:3146-3362,
  * :3591-3620): the n tokens d_tokens[0..n) at positions *d_pos .. *d_pos +
  * n - 1 (device int32, left unchanged; the caller advances it) through every

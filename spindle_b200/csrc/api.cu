@@ -1697,6 +1697,17 @@ extern "C" {
 
 uint64_t sg_model_scratch_bytes(const sg_model *m) { return check_model(m) ? 0 : model_scratch(m).total; }
 
+uint64_t sg_model_ep_scratch_bytes(const sg_model *m) {
+    if (check_model(m)) return 0;
+    uint64_t moe = 0;
+    for (uint32_t l = 0; l < m->n_layers; l++)
+        if (m->layers[l].is_moe) {
+            const uint64_t b = moe_batch_scratch(&m->layers[l].moe, 1).total;
+            moe = b > moe ? b : moe;
+        }
+    return align_up(model_scratch(m).total, 256) + moe;
+}
+
 uint64_t sg_model_kv_bytes(const sg_model *m) {
     if (check_model(m)) return 0;
     return 2ull * m->n_layers * m->max_seq * m->n_kv_heads * m->head_dim * 2;
@@ -1961,8 +1972,13 @@ sg_status sg_pipe_recv(float *d_dst, uint64_t n, uint64_t n_max, void *d_recv, v
     return SG_OK;
 }
 
-sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_scratch, uint64_t scratch_bytes,
-                     float *d_hidden, float *d_logits, int64_t *d_token, void *stream) {
+// sg_forward and sg_forward_ep: eps (host, [n_layers]) runs every MoE layer
+// on this rank's experts, its slot outputs exchanged with the other ranks
+// (moe_forward_batch for one token, expert-parallel), in scratch past the
+// one-GPU step's.
+static sg_status forward_one(const sg_model *m, const sg_moe_ep *eps, int32_t *d_state, void *d_kv, void *d_scratch,
+                             uint64_t scratch_bytes, float *d_hidden, float *d_logits, int64_t *d_token,
+                             void *stream) {
     sg_status st = check_model(m);
     if (st) return st;
     if (!d_state || !d_kv || !d_scratch) return SG_ERR_INVALID;
@@ -1970,7 +1986,8 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
         !aligned(d_logits, 4) || !aligned(d_token, 8))
         return SG_ERR_ALIGN;
     const ModelScratch L = model_scratch(m);
-    if (scratch_bytes < L.total) return SG_ERR_INVALID;
+    if (scratch_bytes < (eps ? sg_model_ep_scratch_bytes(m) : L.total)) return SG_ERR_INVALID;
+    const uint64_t ep_off = align_up(L.total, 256), ep_bytes = scratch_bytes - (eps ? ep_off : 0);
     cudaStream_t s = (cudaStream_t)stream;
     uint8_t *sc = (uint8_t *)d_scratch;
     float *x = (float *)(sc + L.x), *xn = (float *)(sc + L.xn), *q = (float *)(sc + L.q), *k = (float *)(sc + L.k);
@@ -2046,7 +2063,11 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
         }
         // feed-forward: norm (+ attention residual), then the dense SwiGLU or the MoE layer
         if ((st = launch_norm(x, proj, m->residual_scale, y.ffn_norm, m->rms_eps, dim, xn, qx, s))) return st;
-        if (y.is_moe) {
+        if (y.is_moe && eps) {
+            // this rank's experts; every rank's combine writes the whole layer output
+            if ((st = moe_batch_impl(&y.moe, &eps[l], xn, dim, 1, proj, dim, sc + ep_off, ep_bytes, nullptr, stream)))
+                return st;
+        } else if (y.is_moe) {
             if ((st = moe_forward_impl(&y.moe, xn, proj, sc + L.moe, L.moe_bytes, nullptr, nullptr, stream, &comb)))
                 return st;
             deferred = true;
@@ -2066,6 +2087,17 @@ sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_sc
                      (unsigned *)(sc + L.amax + ARGMAX_CTAS * 8)};
     CK(launch_pdl((const void *)argmax_kernel, ARGMAX_CTAS, ARGMAX_THREADS, 0, s, &ga));
     return SG_OK;
+}
+
+sg_status sg_forward(const sg_model *m, int32_t *d_state, void *d_kv, void *d_scratch, uint64_t scratch_bytes,
+                     float *d_hidden, float *d_logits, int64_t *d_token, void *stream) {
+    return forward_one(m, nullptr, d_state, d_kv, d_scratch, scratch_bytes, d_hidden, d_logits, d_token, stream);
+}
+
+sg_status sg_forward_ep(const sg_model *m, const sg_moe_ep *eps, int32_t *d_state, void *d_kv, void *d_scratch,
+                        uint64_t scratch_bytes, float *d_hidden, float *d_logits, int64_t *d_token, void *stream) {
+    if (!eps) return SG_ERR_INVALID;
+    return forward_one(m, eps, d_state, d_kv, d_scratch, scratch_bytes, d_hidden, d_logits, d_token, stream);
 }
 
 }  // extern "C"

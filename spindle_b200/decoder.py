@@ -48,6 +48,10 @@ def _sigs():
         L.sg_model_prepare.argtypes = [C.POINTER(SgModel), P, C.c_uint64, P]
         L.sg_forward.restype = C.c_int32
         L.sg_forward.argtypes = [C.POINTER(SgModel), P, P, P, C.c_uint64, P, P, P, P]
+        L.sg_model_ep_scratch_bytes.restype = C.c_uint64
+        L.sg_model_ep_scratch_bytes.argtypes = [C.POINTER(SgModel)]
+        L.sg_forward_ep.restype = C.c_int32
+        L.sg_forward_ep.argtypes = [C.POINTER(SgModel), P, P, P, P, C.c_uint64, P, P, P, P]
         L.sg_model_batch_scratch_bytes.restype = C.c_uint64
         L.sg_model_batch_scratch_bytes.argtypes = [C.POINTER(SgModel), C.c_uint64]
         L.sg_model_batch_prepare.restype = C.c_int32
@@ -69,12 +73,15 @@ def _ptr(t):
 class Decoder:
     """Device weights, KV cache, scratch and the {token, pos} state of one model."""
 
-    def __init__(self, cfg, weights, dtypes, device, qk_adjacent=True):
+    def __init__(self, cfg, weights, dtypes, device, qk_adjacent=True, ep=None):
         """weights: name -> CUDA tensor (uint8 GGUF rows for matrices, float32
         vectors); dtypes: name -> GGML dtype of each matrix.  qk_adjacent: store
         each layer's wk right after its wq when both have one format, which lets
-        sg_forward compute q and k in one launch."""
-        self.cfg, self.dev = dict(cfg), device
+        sg_forward compute q and k in one launch.  ep: a spindle_b200.tp.TpGroup
+        to spread every MoE layer's experts over its ranks (sg_forward_ep; every
+        rank builds the Decoder with the same weights, in the same order, and
+        steps it with the same state); the batch forms are then unavailable."""
+        self.cfg, self.dev, self.ep = dict(cfg), device, ep
         c = self.cfg
         self.keep = []  # every device buffer the model points at
         dim, hd = c["dim"], c["head_dim"]
@@ -105,6 +112,7 @@ class Decoder:
 
         layers = []
         moe = c.get("moe")
+        self._eps = []
         for i in range(c["n_layers"]):
             p = "l%d." % i
             y = SgLayer()
@@ -117,7 +125,17 @@ class Decoder:
             y.wq_dtype, y.wk_dtype = dtypes[p + "wq"], dtypes[p + "wk"]
             y.wv, y.wv_dtype = tiled(p + "wv", kv_dim, dim), dtypes[p + "wv"]
             y.wo, y.wo_dtype = tiled(p + "wo", dim, q_dim), dtypes[p + "wo"]
-            if moe:
+            if moe and ep is not None:
+                # this rank's experts only; the router and the choice stay whole
+                from .tp import EpMoe
+                em = EpMoe(ep, weights[p + "router"].float(), weights[p + "gate_exps"], weights[p + "up_exps"],
+                           weights[p + "down_exps"], dtypes[p + "gate_exps"], dtypes[p + "down_exps"],
+                           moe["n_expert"], moe["n_used"], dim, moe["n_ff"], n_tok_max=1,
+                           norm=moe.get("norm", True), moe_prune=moe.get("prune", 0.0))
+                self.keep.append(em)
+                y.is_moe, y.moe = 1, em.moe.c()
+                self._eps.append(em.c())
+            elif moe:
                 from . import Moe
                 m = Moe.pack(weights[p + "router"].float(), weights[p + "gate_exps"], weights[p + "up_exps"],
                              weights[p + "down_exps"], dtypes[p + "gate_exps"], dtypes[p + "down_exps"],
@@ -134,6 +152,9 @@ class Decoder:
                 y.is_moe = 0
                 y.ffn_gate_up, y.ffn_down = one.gate_up.data_ptr(), one.down.data_ptr()
                 y.ffn_gate_up_dtype, y.ffn_down_dtype, y.n_ff = dtypes[p + "gate"], dtypes[p + "down"], f
+            if ep is not None and not moe:
+                from ._lib import SgMoeEp
+                self._eps.append(SgMoeEp())  # not read for a dense layer
             layers.append(y)
         self.layers = (SgLayer * len(layers))(*layers)
         m = SgModel()
@@ -150,7 +171,10 @@ class Decoder:
         m.layers = self.layers
         self.model = m
         L = _sigs()
-        nbytes = L.sg_model_scratch_bytes(C.byref(m))
+        if ep is not None:
+            from ._lib import SgMoeEp
+            self.eps = (SgMoeEp * len(self._eps))(*self._eps)
+        nbytes = L.sg_model_ep_scratch_bytes(C.byref(m)) if ep is not None else L.sg_model_scratch_bytes(C.byref(m))
         if not nbytes:
             raise SgError(1, "sg_model_scratch_bytes (invalid model)")
         self.scratch = torch.empty(nbytes, dtype=torch.uint8, device=device)
@@ -169,17 +193,22 @@ class Decoder:
         """One decoder step on the device state; the state then holds the greedy
         token and the next position."""
         L = _sigs()
-        _lib.check(L.sg_forward(C.byref(self.model), C.c_void_p(self.state.data_ptr()), C.c_void_p(self.kv.data_ptr()),
-                                C.c_void_p(self.scratch.data_ptr()), self.scratch.numel(),
-                                C.c_void_p(self.hidden.data_ptr()) if hidden else None,
-                                C.c_void_p(self.logits.data_ptr()) if logits else None,
-                                C.c_void_p(self.token.data_ptr()), _stream(stream)), "sg_forward")
+        args = (C.c_void_p(self.state.data_ptr()), C.c_void_p(self.kv.data_ptr()), C.c_void_p(self.scratch.data_ptr()),
+                self.scratch.numel(), C.c_void_p(self.hidden.data_ptr()) if hidden else None,
+                C.c_void_p(self.logits.data_ptr()) if logits else None, C.c_void_p(self.token.data_ptr()),
+                _stream(stream))
+        if self.ep is not None:
+            _lib.check(L.sg_forward_ep(C.byref(self.model), C.cast(self.eps, C.c_void_p), *args), "sg_forward_ep")
+        else:
+            _lib.check(L.sg_forward(C.byref(self.model), *args), "sg_forward")
 
     def forward_batch(self, tokens, pos0, logits=True, n_max=64, stream=None):
         """forward_batch_slice + compute_logits_batch: tokens at positions
         pos0 .. pos0 + n - 1 in one call (their K/V rows enter the cache).
         Returns (logits [n, vocab] or None, greedy next tokens int64 [n]); per
         token bit for bit the one-token step."""
+        if self.ep is not None:
+            raise ValueError("the batch forward is not expert-parallel; build the Decoder without ep")
         L = _sigs()
         n = len(tokens)
         if getattr(self, "_bscratch", None) is None or self._bn < n_max:
@@ -208,6 +237,8 @@ class Decoder:
         last one (logits [n, vocab], greedy tokens int64 [n]), or with
         head=False the output-normed hidden states (forward_batch_slice's
         return value) and no LM head."""
+        if self.ep is not None:
+            raise ValueError("the batch forward is not expert-parallel; build the Decoder without ep")
         L = _sigs()
         n = len(tokens) if tokens is not None else hidden.shape[0]
         if getattr(self, "_bscratch", None) is None or self._bn < n_max:

@@ -239,3 +239,85 @@ def pipe_rank(rank, world, port, out):
             except Exception as e:
                 out.put((rank, "close: " + repr(e)))
         dist.destroy_process_group()
+
+
+def decoder_ep_rank(rank, world, port, out):
+    # the decoder step with expert parallelism (sg_forward_ep) against the
+    # whole model on this GPU (sg_forward): logits bit for bit and the same
+    # greedy tokens, eager and replayed as a CUDA graph, on a small MoE model
+    # and on two layers of the Qwen3-30B-A3B shape
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import decoder_util as U
+    from spindle_b200.decoder import Decoder, qwen3_dtypes, random_weights
+    from spindle_b200.tp import TpGroup
+    init(rank, world, port, "nccl")
+    dev = torch.device("cuda", rank)
+    grp = None
+    try:
+        grp = TpGroup(device=dev)
+        msgs = []
+        small = dict(U.MOE, n_layers=3, max_seq=64)
+        big = dict(dim=2048, n_heads=32, n_kv_heads=4, head_dim=128, n_layers=2, vocab=151936, max_seq=64,
+                   rope_theta=1e6, rms_eps=1e-6, rope_neox=True,
+                   moe=dict(n_expert=128, n_used=8, n_ff=768, norm=True))
+        for kind, cfg in [("small", small), ("qwen3_30b_a3b_2layers", big)]:
+            if kind == "small":
+                dtypes = U.dtypes_for(cfg)
+                W = U.device_weights(U.host_weights(cfg, dtypes, seed=71), dev)
+            else:
+                dtypes = qwen3_dtypes(cfg, embed=U.Q4_K)
+                W = random_weights(cfg, dtypes, dev, seed=72)
+            full = Decoder(cfg, W, dtypes, dev)
+            epd = Decoder(cfg, W, dtypes, dev, ep=grp)
+            seq = [5, 77, 130, 9]
+            for pos in range(16):
+                t = seq[pos]
+                full.set_state(t, pos)
+                full.step()
+                epd.set_state(t, pos)
+                epd.step()
+                torch.cuda.synchronize(dev)
+                if not (np.array_equal(full.logits.cpu().numpy().view(np.uint32),
+                                       epd.logits.cpu().numpy().view(np.uint32))
+                        and int(full.token.item()) == int(epd.token.item())
+                        and torch.equal(full.state, epd.state)):
+                    msgs.append((kind, "eager", pos))
+                if len(seq) == pos + 1:
+                    seq.append(int(full.token.item()))
+            # one captured step replayed token after token: the epoch counters live on the device
+            want = full.generate(seq[:4], 8)
+            for i, t in enumerate(seq[:4]):
+                epd.set_state(t, i)
+                epd.step(hidden=False, logits=False)
+            s = torch.cuda.Stream(device=dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            got = []
+            with torch.cuda.stream(s):
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=s):
+                    epd.step(stream=s, hidden=False, logits=False)
+                for _ in range(8):
+                    got.append(int(epd.state[0].item()))
+                    graph.replay()
+                    torch.cuda.synchronize(dev)
+            torch.cuda.current_stream(dev).wait_stream(s)
+            del graph
+            if got != want:
+                msgs.append((kind, "graph", got, want))
+            del full, epd, W
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+        __import__("spindle_b200").device_status()
+        out.put((rank, "ok" if not msgs else repr(msgs)))
+    except Exception as e:
+        out.put((rank, repr(e)))
+    finally:
+        if grp is not None:
+            try:
+                grp.close()
+            except Exception as e:
+                out.put((rank, "close: " + repr(e)))
+        dist.destroy_process_group()
