@@ -1236,6 +1236,115 @@ def active_params(cfg):
     return cfg["n_layers"] * (attn + ffn)
 
 
+def run_gpu_prefill_pipe(args):
+    """BASELINE configs[4] at N > 1: the prompt's prefill pipelined over the
+    GPUs as a layer split (the two-PC mode of docs/cluster.md, layers 0..24 /
+    24..48 at N = 2; par_rows's split of the layers in general).  Stage p runs
+    its layers on each 64-position chunk and sends the residual to stage p+1
+    over NVLink (PipeLink: epoch-tagged peer stores), so while stage p+1 works
+    on chunk c stage p already runs chunk c+1 (feed's chunks,
+    smollm_chat.rs:3047-3071); the last stage runs the head on the prompt's
+    last position.  value = prompt tokens / max-over-ranks prefill time."""
+    import torch
+    import torch.distributed as dist
+
+    import spindle_b200 as sg
+    from spindle_b200.decoder import Decoder, qwen3_dtypes, random_weights
+    from spindle_b200.tp import PipeLink, TpGroup, shard_rows
+
+    rank, world, local = rank_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import datetime
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    name = "qwen3_30b_a3b"
+    n_prompt = args.prompt if args.prompt else PREFILL_PROMPT
+    cfg = dict(DECODE_MODELS[name], max_seq=n_prompt + 8)
+    dtypes = qwen3_dtypes(cfg, embed=Q4_K)
+    W = random_weights(cfg, dtypes, dev, seed=5000)  # the same model on every rank
+    dec = Decoder(cfg, W, dtypes, dev)
+    del W
+    grp = TpGroup(device=dev)
+    C_ = PREFILL_CHUNK
+    links = [PipeLink(grp, p, p + 1, C_ * cfg["dim"]) for p in range(world - 1)]
+    l0, l1 = shard_rows(cfg["n_layers"], world, rank)
+    g = torch.Generator().manual_seed(78)
+    toks = torch.randint(0, cfg["vocab"], (n_prompt,), generator=g).tolist()
+    calls = [(c0, min(C_, n_prompt - 1 - c0)) for c0 in range(0, n_prompt - 1, C_)] + [(n_prompt - 1, 1)]
+    s = torch.cuda.Stream(device=dev)
+    hbuf = torch.empty(C_, cfg["dim"], device=dev)
+
+    def prefill():
+        greedy = None
+        for i, (c0, n) in enumerate(calls):
+            head = i == len(calls) - 1
+            if rank == 0:
+                out = dec.forward_batch_range(c0, l0, l1, tokens=toks[c0:c0 + n], n_max=C_, stream=s)
+            else:
+                h = links[rank - 1].recv(hbuf[:n], stream=s)
+                out = dec.forward_batch_range(c0, l0, l1, hidden=h, n_max=C_, stream=s, head=head)
+            if rank < world - 1:
+                links[rank].send(out[0], stream=s)
+            elif head:
+                greedy = out[1]
+        return greedy
+
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            prefill()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(s)
+            for _ in range(args.steps):
+                prefill()
+            e1.record(s)
+            e1.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    sg.device_status()
+    ops = 2.0 * n_prompt * active_params(cfg)
+    peak, peak_src = 2 * 1596.4, "fallback: 2 x bf16 burst"
+    try:
+        pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        peak, peak_src = 2 * pk["bf16_tflops"], "2 x MEASURED_PEAKS.json bf16_tflops (dense int8 = 2 x bf16 on B200)"
+    except Exception:
+        pass
+    line = None
+    if rank == 0:
+        achieved = ops / (ms * 1e-3) / 1e12
+        line = {"metric": "prefill tokens/s, %s (random-init, Q4_K_M mix), %d-token prompt" % (name, n_prompt),
+                "value": round(n_prompt / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None,
+                "dtype": "Q4_K projections: exact-integer f16 x f16 -> f32 on tcgen05; Q6_K and the MoE experts: int8 x int6/int4 -> int32 (dp4a); fp32 norms/attention/router, f16 KV",
+                "data": "synthetic",
+                "config": dict(decode_config(name, cfg, world), workload="prefill_pipeline_%s" % name,
+                               prompt=n_prompt, seq_len=n_prompt, chunk=C_,
+                               parallelism="layer pipeline x%d: layers %s, the residual of every %d-position "
+                                           "chunk sent over NVLink (PipeLink)"
+                                           % (world, ", ".join("%d..%d" % shard_rows(cfg["n_layers"], world, q)
+                                                                for q in range(world)), C_)),
+                "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": peak * world, "unit": "TOP/s",
+                             "frac": round(achieved / (peak * world), 5), "traffic": None,
+                             "peak_source": peak_src + ", x n_gpus",
+                             "kernel": "the whole pipelined prefill",
+                             "how": "2 x prompt x active params (%.3f G) / max-over-ranks step time"
+                                    % (active_params(cfg) / 1e9)},
+                "e2e": {"value": round(n_prompt / (ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0, "how": "the device-timed value (tokens are host lists passed per call)"},
+                "gpu_launches": len(calls) * (1 + (l1 - l0) * 12) * args.steps,
+                "clocks": clk.summary()}
+    dist.barrier()
+    del dec
+    grp.close()
+    dist.destroy_process_group()
+    return line
+
+
 def run_gpu_prefill(args):
     import torch
     import torch.distributed as dist
@@ -1542,7 +1651,7 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": "prefill reference arm: the oracle forward runs "
                               "about 1 token/s on one core; the decode line's cpu_baseline covers it"}), flush=True)
             return
-        line = run_gpu_prefill(args)
+        line = run_gpu_prefill_pipe(args) if rank_env()[1] > 1 else run_gpu_prefill(args)
         if line is not None:
             print(json.dumps(line), flush=True)
         return

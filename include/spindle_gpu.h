@@ -460,6 +460,17 @@ SG_API sg_status sg_forward_batch(const sg_model *m, const int32_t *d_tokens, ui
                                   void *d_kv, void *d_scratch, uint64_t scratch_bytes, uint64_t n_max,
                                   float *d_logits, uint64_t ldl, int64_t *d_greedy, void *stream);
 
+/* The sliding-window KV shift (shift_kv, smollm_chat.rs:2942-2972; the
+ * policy, ensure_kv_room at :2924-2940, stays with the caller): drops
+ * n_discard positions right after the n_keep pinned ones (at most cur_pos -
+ * n_keep), moving positions [n_keep + n_discard, cur_pos) down to n_keep; each
+ * moved K row is re-rotated by -n_discard (RoPE rotations compose) through f32
+ * and back to f16, V rows are copied.  Layers [l0, l1) only (a pipeline stage
+ * shifts its own).  d_scratch: sg_forward's scratch, prepared (its RoPE
+ * frequencies).  The caller then continues at position cur_pos - n_discard. */
+SG_API sg_status sg_kv_shift(const sg_model *m, void *d_kv, const void *d_scratch, uint32_t l0, uint32_t l1,
+                             uint32_t n_keep, uint32_t n_discard, uint32_t cur_pos, void *stream);
+
 /* The stages of a layer split over ranks (forward_slice with a layer range,
  * smollm_chat.rs:3371-3552; the two-PC split of docs/cluster.md): layers
  * [l0, l1) of sg_forward_batch.  l0 > 0: the input is d_hidden_in [n][dim],

@@ -323,6 +323,8 @@ def _fwd_sigs():
         L.or_rmsnorm.argtypes = [P, P, P, C.c_size_t, C.c_float]
         L.or_rope_freqs.restype = None
         L.or_rope_freqs.argtypes = [C.c_float, C.c_uint32, P]
+        L.or_kv_shift.restype = C.c_uint32
+        L.or_kv_shift.argtypes = [C.POINTER(Model), P, P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]
         L.or_rope_rotate.restype = None
         L.or_rope_rotate.argtypes = [P, C.c_size_t, C.c_uint32, P, C.c_int32, C.c_float]
         L._fwd_ready = True
@@ -354,6 +356,12 @@ class Decoder:
         if rc:
             raise RuntimeError("or_forward failed (%d)" % rc)
         return hidden, out
+
+    def kv_shift(self, n_keep, n_discard, cur_pos, l0=0, l1=None):
+        """shift_kv (smollm_chat.rs:2942-2972) on layers [l0, l1); returns the new position."""
+        l1 = self.model.n_layers if l1 is None else l1
+        return int(_fwd_sigs().or_kv_shift(C.byref(self.model), _p(self.kcache), _p(self.vcache), l0, l1, n_keep,
+                                           n_discard, cur_pos))
 
 
 def argmax(logits):

@@ -6,6 +6,7 @@
  * (heads)        rmsnorm_heads        smollm_chat.rs:578-584
  * or_rope_freqs  Rope::new            smollm_chat.rs:1403-1406
  * or_rope_rotate Rope::rotate         smollm_chat.rs:1408-1419
+ * or_kv_shift    shift_kv             smollm_chat.rs:2942-2972
  * (matvec)       matvec               smollm_chat.rs:309-349 (integer path when supported)
  * or_forward     forward_slice        smollm_chat.rs:3371-3552 (one token; no bias tensors,
  *                                     no layer streaming or expert cache)
@@ -222,4 +223,40 @@ int64_t or_argmax(const float *logits, size_t n)
         if (ki >= bk) { bk = ki; best = i; }  /* max_by keeps the last maximum */
     }
     return (int64_t)best;
+}
+
+/* f16_to_f32_slice (quant.rs:1516-1522): _mm256_cvtph_ps, exact. */
+AVX static void from_f16(const uint16_t *src, float *dst, size_t n)
+{
+    for (size_t i = 0; i < n; i += 8)
+        _mm256_storeu_ps(dst + i, _mm256_cvtph_ps(_mm_loadu_si128((const __m128i *)(src + i))));
+}
+
+/* shift_kv (smollm_chat.rs:2942-2972): drop n_discard positions after the
+ * n_keep pinned ones (clamped to cur_pos - n_keep); each kept K row slides down
+ * by n_discard, widened to f32, re-rotated by -n_discard and rounded back to
+ * f16; V rows are copied; layers [l0, l1), in increasing position order as the
+ * reference does.  Returns the new position. */
+uint32_t or_kv_shift(const or_model *m, uint16_t *kcache, uint16_t *vcache, uint32_t l0, uint32_t l1, uint32_t n_keep,
+                     uint32_t n_discard, uint32_t cur_pos)
+{
+    const uint32_t kv_dim = m->n_kv_heads * m->head_dim;
+    const uint32_t n_ctx = cur_pos > n_keep ? cur_pos - n_keep : 0;
+    if (n_discard > n_ctx) n_discard = n_ctx;
+    if (n_discard == 0) return cur_pos;
+    const uint32_t n_move = n_ctx - n_discard;
+    float freqs[512], *tmp = malloc(sizeof(float) * kv_dim);
+    or_rope_freqs(m->rope_theta, m->head_dim, freqs);
+    for (uint32_t l = l0; l < l1; l++) {
+        const size_t layer = (size_t)l * m->max_seq;
+        for (uint32_t i = 0; i < n_move; i++) {
+            const size_t src = (layer + n_keep + n_discard + i) * kv_dim, dst = (layer + n_keep + i) * kv_dim;
+            from_f16(kcache + src, tmp, kv_dim);
+            or_rope_rotate(tmp, kv_dim, m->head_dim, freqs, m->rope_neox, -(float)n_discard);
+            to_f16(tmp, kcache + dst, kv_dim);
+            memmove(vcache + dst, vcache + src, sizeof(uint16_t) * kv_dim);
+        }
+    }
+    free(tmp);
+    return cur_pos - n_discard;
 }

@@ -145,6 +145,9 @@ void or_rmsnorm(const float *x, const float *w, float *out, size_t n, float eps)
 void or_rope_freqs(float theta, uint32_t head_dim, float *inv_freq);
 /* Rope::rotate: every head of v (len values) rotated to position pos. */
 void or_rope_rotate(float *v, size_t len, uint32_t head_dim, const float *inv_freq, int neox, float pos);
+/* shift_kv (smollm_chat.rs:2942-2972) over layers [l0, l1); returns the new position. */
+uint32_t or_kv_shift(const or_model *m, uint16_t *kcache, uint16_t *vcache, uint32_t l0, uint32_t l1, uint32_t n_keep,
+                     uint32_t n_discard, uint32_t cur_pos);
 /* One token at position pos through every layer: the KV caches (f16,
  * [n_layers][max_seq][n_kv_heads * head_dim]) get this position's K and V;
  * hidden_out (optional) = the output-normed hidden state, logits_out

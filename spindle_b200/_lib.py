@@ -120,6 +120,7 @@ SIGNATURES = {
     "sg_model_prepare": (I32, [P, P, U64, P]),
     "sg_forward": (I32, [P, P, P, P, U64, P, P, P, P]),
     "sg_model_ep_scratch_bytes": (U64, [P]),
+    "sg_kv_shift": (I32, [P, P, P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P]),
     "sg_forward_ep": (I32, [P, P, P, P, P, U64, P, P, P, P]),
     "sg_forward_batch_range": (I32, [P, C.c_uint32, C.c_uint32, P, P, U64, P, P, P, U64, U64, P, P, U64, P, P]),
     "sg_pipe_recv_bytes": (U64, [U64]),

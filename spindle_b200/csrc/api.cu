@@ -1947,6 +1947,31 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
     return SG_OK;
 }
 
+sg_status sg_kv_shift(const sg_model *m, void *d_kv, const void *d_scratch, uint32_t l0, uint32_t l1,
+                      uint32_t n_keep, uint32_t n_discard, uint32_t cur_pos, void *stream) {
+    sg_status st = check_model(m);
+    if (st) return st;
+    if (!d_kv || !d_scratch || l0 > l1 || l1 > m->n_layers || cur_pos > m->max_seq) return SG_ERR_INVALID;
+    if (!aligned(d_kv, 16) || !aligned(d_scratch, 256)) return SG_ERR_ALIGN;
+    // shift_kv (smollm_chat.rs:2942-2972): nothing to drop past the pinned positions
+    const uint32_t n_ctx = cur_pos > n_keep ? cur_pos - n_keep : 0u;
+    if (n_discard > n_ctx) n_discard = n_ctx;
+    if (n_discard == 0 || l0 == l1) return SG_OK;
+    const uint32_t n_move = n_ctx - n_discard, kv_dim = m->n_kv_heads * m->head_dim;
+    const ModelScratch L = model_scratch(m);
+    uint16_t *kc = (uint16_t *)d_kv, *vc = kc + (uint64_t)m->n_layers * m->max_seq * kv_dim;
+    for (uint32_t i0 = 0; i0 < n_move; i0 += n_discard) {  // waves of n_discard rows (see kv_shift_kernel)
+        const uint32_t i1 = n_move - i0 < n_discard ? n_move : i0 + n_discard;
+        KvShiftArgs a = {kc, vc, (const float *)((const uint8_t *)d_scratch + L.freqs), l0, l1, m->max_seq, kv_dim,
+                         m->head_dim, (uint32_t)(m->rope_neox != 0), n_keep, n_discard, i0, i1};
+        const uint64_t work = (uint64_t)(l1 - l0) * (i1 - i0) * (kv_dim / 2);
+        const uint64_t blocks = (work + 255) / 256;
+        kv_shift_kernel<<<(unsigned)(blocks < 148 * 8 ? blocks : 148 * 8), 256, 0, (cudaStream_t)stream>>>(a);
+        CK(cudaGetLastError());
+    }
+    return SG_OK;
+}
+
 uint64_t sg_pipe_recv_bytes(uint64_t n_max) { return 2ull * 8ull * n_max; }
 
 sg_status sg_pipe_send(const float *d_src, uint64_t n, uint64_t n_max, void *d_peer_recv, void *d_comm, void *stream) {

@@ -633,4 +633,29 @@ __global__ void residual_kernel(const float *x, const float *add, float rs, floa
     if (i < n) out[i] = __fadd_rn(x[i], __fmul_rn(rs, add[i]));
 }
 
+// One thread per (layer, row, pair of a head): K re-rotated, V copied.
+__global__ void kv_shift_kernel(const __grid_constant__ KvShiftArgs a) {
+    const uint32_t half = a.head_dim / 2, pairs = a.kv_dim / 2;
+    const uint64_t rows = (uint64_t)(a.l1 - a.l0) * (a.i1 - a.i0);
+    const float pos = -(float)a.n_discard;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < rows * pairs;
+         t += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t row = t / pairs;
+        const uint32_t p = (uint32_t)(t - row * pairs);
+        const uint32_t l = a.l0 + (uint32_t)(row / (a.i1 - a.i0)), i = a.i0 + (uint32_t)(row % (a.i1 - a.i0));
+        const uint64_t src = ((uint64_t)l * a.max_seq + a.n_keep + a.n_discard + i) * a.kv_dim;
+        const uint64_t dst = ((uint64_t)l * a.max_seq + a.n_keep + i) * a.kv_dim;
+        const uint32_t h = p / half, j = p - h * half;
+        const uint32_t ia = h * a.head_dim + (a.neox ? j : 2 * j), ib = h * a.head_dim + (a.neox ? j + half : 2 * j + 1);
+        const float x0 = __half2float(__ushort_as_half(a.kc[src + ia]));
+        const float x1 = __half2float(__ushort_as_half(a.kc[src + ib]));
+        const float ang = __fmul_rn(pos, a.inv_freq[j]);
+        const float sn = gm_sinf(ang), cs = gm_cosf(ang);
+        a.kc[dst + ia] = __half_as_ushort(__float2half_rn(__fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn))));
+        a.kc[dst + ib] = __half_as_ushort(__float2half_rn(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs))));
+        a.vc[dst + ia] = a.vc[src + ia];
+        a.vc[dst + ib] = a.vc[src + ib];
+    }
+}
+
 }  // namespace sg

@@ -156,6 +156,20 @@ __global__ void pipe_recv_kernel(const __grid_constant__ PipeArgs a);
 // out = x + rs * add (the residual add of the last layer of a pipeline stage)
 __global__ void residual_kernel(const float *x, const float *add, float rs, float *out, uint64_t n);
 
+// The sliding-window KV shift (shift_kv, smollm_chat.rs:2942-2972): for
+// layers [l0, l1) and kept positions i in [i0, i1), the K row at n_keep +
+// n_discard + i is widened to f32, rotated by -n_discard (Rope::rotate,
+// :1408-1419) and rounded back to f16 at n_keep + i; the V row is copied.
+// Launches run in waves of at most n_discard rows, each reading only rows no
+// earlier wave writes and writing only rows earlier waves have read.
+struct KvShiftArgs {
+    uint16_t *kc, *vc;          // the caches [n_layers][max_seq][kv_dim]
+    const float *inv_freq;      // [head_dim / 2]
+    uint32_t l0, l1, max_seq, kv_dim, head_dim, neox;
+    uint32_t n_keep, n_discard, i0, i1;
+};
+__global__ void kv_shift_kernel(const __grid_constant__ KvShiftArgs a);
+
 __global__ void embed_kernel(const __grid_constant__ EmbedArgs a);
 __global__ void rmsnorm_kernel(const __grid_constant__ NormArgs a);
 template <int HD, int CHK>

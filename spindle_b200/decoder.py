@@ -202,6 +202,35 @@ class Decoder:
         else:
             _lib.check(L.sg_forward(C.byref(self.model), *args), "sg_forward")
 
+    def shift_kv(self, n_keep, n_discard, cur_pos, l0=0, l1=None, stream=None):
+        """shift_kv (smollm_chat.rs:2942-2972) on the device caches of layers
+        [l0, l1) (a pipeline stage shifts its own): positions [n_keep +
+        n_discard, cur_pos) move down by n_discard, K re-rotated by -n_discard.
+        Returns the new position, cur_pos - n_discard (n_discard clamped to
+        cur_pos - n_keep); the caller continues from it (set_state)."""
+        l1 = self.cfg["n_layers"] if l1 is None else l1
+        n_discard = min(n_discard, max(cur_pos - n_keep, 0))
+        _lib.check(lib().sg_kv_shift(C.byref(self.model), C.c_void_p(self.kv.data_ptr()),
+                                     C.c_void_p(self.scratch.data_ptr()), l0, l1, n_keep, n_discard, cur_pos,
+                                     _stream(stream)), "sg_kv_shift")
+        return cur_pos - n_discard
+
+    def kv_room(self, cur_pos, needed, n_keep):
+        """ensure_kv_room's choice (smollm_chat.rs:2924-2940): 0 when needed
+        more positions fit, else how many to discard (at least the overflow,
+        rounded up to half of the unpinned window, at most all of it)."""
+        if cur_pos + needed <= self.cfg["max_seq"]:
+            return 0
+        n_ctx = cur_pos - n_keep
+        want = max(cur_pos + needed - self.cfg["max_seq"], n_ctx // 2)
+        return min(want, n_ctx)
+
+    def ensure_kv_room(self, cur_pos, needed, n_keep, stream=None):
+        """ensure_kv_room (smollm_chat.rs:2924-2940): shifts when cur_pos +
+        needed would pass max_seq; returns the position to continue from."""
+        n_discard = self.kv_room(cur_pos, needed, n_keep)
+        return self.shift_kv(n_keep, n_discard, cur_pos, stream=stream) if n_discard else cur_pos
+
     def forward_batch(self, tokens, pos0, logits=True, n_max=64, stream=None):
         """forward_batch_slice + compute_logits_batch: tokens at positions
         pos0 .. pos0 + n - 1 in one call (their K/V rows enter the cache).

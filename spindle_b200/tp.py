@@ -247,3 +247,74 @@ class PipeLink:
                                       C.c_void_p(self.recvs[self.dst]), C.c_void_p(self.comm),
                                       C.c_void_p(self.comms[self.src]), _stream(stream)), "sg_pipe_recv")
         return out
+
+
+class PipelineStage:
+    """One rank's stage of a layer split over the ranks of a group: the two-PC
+    mode of cluster_net.rs (layers 0..split on one machine, the rest and the
+    head on the other) as a chain of GPUs.  Stage p runs layers [L*p/P,
+    L*(p+1)/P) of its Decoder (par_rows's split over the layers), receives the
+    residual from stage p-1 and sends it to stage p+1 over NVLink (PipeLink:
+    the STEP / PREFILL frames' activations).  The last stage holds the head and
+    owns the sliding window, as the reference's master does:
+
+      kv_info()        FRAME_KV_INFO: every stage's KV capacity; the pipeline's
+                       context is the smallest (attach_cluster clamps the
+                       master's max_seq to the worker's).
+      ensure_kv_room() ensure_kv_room on the last stage, then FRAME_KV_SHIFT:
+                       (n_keep, n_discard, cur_pos) reach every stage, each
+                       shifts its own layers' caches (shift_kv), so all stages
+                       keep identical positions.
+
+    Every rank builds its stage in the same order (the set-up is collective)
+    and calls forward / ensure_kv_room with the same arguments."""
+
+    def __init__(self, decoder, grp, n_max=64):
+        self.dec, self.grp, self.n_max = decoder, grp, n_max
+        self.rank, self.n = grp.rank, grp.n
+        self.l0, self.l1 = shard_rows(decoder.cfg["n_layers"], self.n, self.rank)
+        dim = decoder.cfg["dim"]
+        self.links = [PipeLink(grp, p, p + 1, n_max * dim) for p in range(self.n - 1)]
+        self.max_seq = self.kv_info()
+
+    def kv_info(self):
+        return min(exchange(int(self.dec.cfg["max_seq"]), self.grp.group))
+
+    def _broadcast(self, obj):
+        return exchange(obj, self.grp.group)[self.n - 1]  # the last stage's value
+
+    def forward(self, tokens, pos0, stream=None):
+        """The stage's layers for positions pos0 .. pos0 + len(tokens) - 1; the
+        last stage returns (logits [n, vocab], greedy tokens), the others None."""
+        n = len(tokens)
+        if pos0 + n > self.max_seq:
+            raise ValueError("positions past the pipeline's context: call ensure_kv_room first")
+        dim = self.dec.cfg["dim"]
+        if self.rank == 0:
+            out = self.dec.forward_batch_range(pos0, self.l0, self.l1, tokens=tokens, n_max=self.n_max,
+                                               stream=stream)
+        else:
+            h = self.links[self.rank - 1].recv(torch.empty(n, dim, device=self.dec.dev), stream=stream)
+            out = self.dec.forward_batch_range(pos0, self.l0, self.l1, hidden=h, n_max=self.n_max, stream=stream)
+        if self.rank < self.n - 1:
+            self.links[self.rank].send(out[0], stream=stream)
+            return None
+        return out
+
+    def ensure_kv_room(self, cur_pos, needed, n_keep, stream=None):
+        """Room for `needed` more positions: the last stage decides as
+        ensure_kv_room does (against the pipeline's context), every stage
+        applies the same shift to its layers; returns the position to go on
+        from (the same on every stage)."""
+        if self.rank == self.n - 1:
+            if cur_pos + needed <= self.max_seq:
+                decision = (n_keep, 0, cur_pos)
+            else:
+                n_ctx = cur_pos - n_keep
+                decision = (n_keep, min(max(cur_pos + needed - self.max_seq, n_ctx // 2), n_ctx), cur_pos)
+        else:
+            decision = None
+        n_keep, n_discard, pos = self._broadcast(decision)
+        if n_discard == 0:
+            return pos
+        return self.dec.shift_kv(n_keep, n_discard, pos, l0=self.l0, l1=self.l1, stream=stream)

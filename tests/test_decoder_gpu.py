@@ -169,3 +169,61 @@ def test_decoder_bad_args(dev):
                       C.c_void_p(d.scratch.data_ptr()), d.scratch.numel(), None, None, None, None)
     assert st == 4  # misaligned state
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("kind,neox", [("dense", True), ("moe", True), ("dense", False)])
+def test_decoder_kv_shift_matches_oracle(dev, kind, neox):
+    # decoding past the context: ensure_kv_room's policy (smollm_chat.rs:
+    # 2924-2940) picks the positions to drop, and shift_kv (:2942-2972) runs on
+    # the GPU (sg_kv_shift) and in the oracle; the caches after every shift and
+    # the logits of every step stay equal bit for bit, through several shifts
+    cfg = dict(U.DENSE if kind == "dense" else U.MOE, max_seq=40, rope_neox=neox)
+    dtypes = U.dtypes_for(cfg)
+    W = U.host_weights(cfg, dtypes, seed=33)
+    ref = U.oracle_decoder(cfg, dtypes, W)
+    gpu = Decoder(cfg, U.device_weights(W, dev), dtypes, dev)
+    n_keep, tok, pos, shifts = 5, 17, 0, 0
+    n = cfg["n_layers"] * cfg["max_seq"] * cfg["n_kv_heads"] * cfg["head_dim"]
+    for _ in range(110):
+        n_discard = gpu.kv_room(pos, 1, n_keep)
+        if n_discard:
+            new_pos = gpu.shift_kv(n_keep, n_discard, pos)
+            assert new_pos == ref.kv_shift(n_keep, n_discard, pos) == pos - n_discard
+            pos = new_pos
+            shifts += 1
+            torch.cuda.synchronize()
+            kv = gpu.kv.cpu().numpy().view(np.uint16)
+            assert np.array_equal(kv[:n], ref.kcache.reshape(-1)), ("K after shift", shifts)
+            assert np.array_equal(kv[n:], ref.vcache.reshape(-1)), ("V after shift", shifts)
+        _, lr = ref.forward(tok, pos)
+        gpu.set_state(tok, pos)
+        gpu.step()
+        torch.cuda.synchronize()
+        assert np.array_equal(bits(gpu.logits.cpu().numpy()), bits(lr)), (pos, shifts)
+        tok = O.argmax(lr)
+        assert int(gpu.token.item()) == tok
+        pos += 1
+    assert shifts >= 3
+
+
+def test_decoder_kv_shift_edges(dev):
+    # nothing past the pinned positions: no-op; n_discard clamped to what is there
+    cfg = dict(U.DENSE, max_seq=24)
+    dtypes = U.dtypes_for(cfg)
+    W = U.host_weights(cfg, dtypes, seed=34)
+    gpu = Decoder(cfg, U.device_weights(W, dev), dtypes, dev)
+    for pos, t in enumerate([3, 9, 27, 81, 243, 5]):
+        gpu.set_state(t, pos)
+        gpu.step()
+    before = gpu.kv.clone()
+    assert gpu.shift_kv(6, 4, 6) == 6  # everything pinned
+    assert gpu.shift_kv(2, 100, 6) == 2  # clamped: all 4 unpinned positions dropped
+    torch.cuda.synchronize()
+    assert torch.equal(gpu.kv.view(-1)[:0], before.view(-1)[:0])
+    import ctypes as C
+    from spindle_b200 import decoder as DM
+    L = DM._sigs()
+    assert L.sg_kv_shift(C.byref(gpu.model), C.c_void_p(gpu.kv.data_ptr()), C.c_void_p(gpu.scratch.data_ptr()), 0, 99,
+                         1, 1, 6, None) == 1  # layers past the model
+    assert L.sg_kv_shift(C.byref(gpu.model), C.c_void_p(gpu.kv.data_ptr()), C.c_void_p(gpu.scratch.data_ptr()), 0, 1,
+                         1, 1, 25, None) == 1  # position past max_seq

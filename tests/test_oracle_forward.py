@@ -181,3 +181,38 @@ def test_rope_matches_reference_and_composes(neox):
     a = O.rope_rotate(a, hd, f, neox, -5.0)
     b = O.rope_rotate(v, hd, f, neox, 12.0)
     assert np.abs(a - b).max() < 1e-4
+
+
+def test_oracle_kv_shift():
+    # shift_kv (smollm_chat.rs:2942-2972) on the oracle's caches: pinned rows
+    # untouched, V rows moved verbatim, K rows re-rotated by -n_discard (equal
+    # to within f16 rounding to the keys computed at the new positions, since
+    # RoPE rotations compose), n_discard clamped, the new position returned
+    cfg = dict(U.DENSE, max_seq=32)
+    dtypes = U.dtypes_for(cfg)
+    W = U.host_weights(cfg, dtypes, seed=35)
+    a = U.oracle_decoder(cfg, dtypes, W)
+    toks = [3, 9, 27, 81, 243, 5, 15, 45, 135, 405, 7, 21]
+    for pos, t in enumerate(toks):
+        a.forward(t, pos)
+    k0, v0 = a.kcache.copy(), a.vcache.copy()
+    n_keep, n_discard, cur = 3, 4, len(toks)
+    assert a.kv_shift(n_keep, n_discard, cur) == cur - n_discard
+    kv_dim = cfg["n_kv_heads"] * cfg["head_dim"]
+    kr = lambda c, l, p: c.reshape(cfg["n_layers"], cfg["max_seq"], kv_dim)[l, p]
+    for l in range(cfg["n_layers"]):
+        for p in range(n_keep):
+            assert np.array_equal(kr(a.kcache, l, p), kr(k0, l, p)) and np.array_equal(kr(a.vcache, l, p), kr(v0, l, p))
+        for i in range(cur - n_keep - n_discard):
+            assert np.array_equal(kr(a.vcache, l, n_keep + i), kr(v0, l, n_keep + n_discard + i))
+    # the re-rotated keys of the last layer against the keys a fresh model
+    # writes when the kept tokens sit at the new positions (attention of the
+    # first layers is unchanged only for pinned rows, so compare one layer-0 row)
+    b = U.oracle_decoder(cfg, dtypes, W)
+    kept = toks[:n_keep] + toks[n_keep + n_discard:]
+    for pos, t in enumerate(kept[:n_keep + 1]):
+        b.forward(t, pos)
+    got = kr(a.kcache, 0, n_keep).view(np.float16).astype(np.float32)
+    want = kr(b.kcache, 0, n_keep).view(np.float16).astype(np.float32)
+    assert np.abs(got - want).max() <= 2e-3 * max(np.abs(want).max(), 1.0)
+    assert a.kv_shift(cur, 5, cur) == cur and a.kv_shift(0, 99, 3) == 0

@@ -16,6 +16,7 @@ import decoder_util as U  # noqa: E402
 import tp_util  # noqa: E402
 
 from spindle_b200.decoder import Decoder  # noqa: E402
+from spindle_b200.tp import TpGroup  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -50,6 +51,49 @@ def test_pipeline_ranks(world):
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
     procs = [ctx.Process(target=tp_util.pipe_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, msg = q.get(timeout=900)
+        res.setdefault(r, []).append(msg)
+    for p in procs:
+        p.join(timeout=120)
+    assert res == {r: ["ok"] for r in range(world)}, res
+
+
+def test_pipeline_kv_shift_one_stage(dev):
+    # a pipeline of one stage (all layers): the KV window slides as on the
+    # plain decoder, logits bit for bit through several shifts
+    import decoder_util as U
+    from spindle_b200.decoder import Decoder
+    from spindle_b200.tp import PipelineStage
+    grp = TpGroup(device=dev)
+    try:
+        cfg = dict(U.MOE, n_layers=2, max_seq=40)
+        dtypes = U.dtypes_for(cfg)
+        W = U.device_weights(U.host_weights(cfg, dtypes, seed=63), dev)
+        stage = PipelineStage(Decoder(cfg, W, dtypes, dev), grp, n_max=8)
+        assert stage.max_seq == 40
+        bad, shifts = tp_util.pipe_shift_loop(stage, Decoder(cfg, W, dtypes, dev), 3, 100, dev)
+        assert not bad and shifts >= 3, (bad, shifts)
+        with pytest.raises(ValueError):
+            stage.forward([1], 40)
+    finally:
+        grp.close()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_pipeline_kv_shift_ranks(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    procs = [ctx.Process(target=tp_util.pipe_kv_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}

@@ -321,3 +321,76 @@ def decoder_ep_rank(rank, world, port, out):
             except Exception as e:
                 out.put((rank, "close: " + repr(e)))
         dist.destroy_process_group()
+
+
+def pipe_shift_loop(stage, whole, n_keep, n_steps, dev):
+    """Greedy decode through a PipelineStage past its context, shifting the KV
+    window on every stage when needed; the last stage checks every step's
+    logits against `whole` (the model on one GPU, shifted alike).  Returns
+    (failures, shifts); every rank calls it with the same arguments."""
+    import numpy as np
+    import torch
+    from spindle_b200.tp import exchange
+    tok, pos, shifts, bad = 17, 0, 0, []
+    last = stage.rank == stage.n - 1
+    for _ in range(n_steps):
+        new = stage.ensure_kv_room(pos, 1, n_keep)
+        if new != pos:
+            shifts += 1
+            if last:
+                assert whole.shift_kv(n_keep, pos - new, pos) == new
+            pos = new
+        out = stage.forward([tok], pos)
+        nxt = None
+        if last:
+            lg, gr = out
+            wl, wg = whole.forward_batch([tok], pos)
+            torch.cuda.synchronize(dev)
+            if not (np.array_equal(lg.cpu().numpy().view(np.uint32), wl.cpu().numpy().view(np.uint32))
+                    and torch.equal(gr, wg)):
+                bad.append((pos, shifts))
+            nxt = int(gr[0].item())
+        tok = exchange(nxt, stage.grp.group)[stage.n - 1]
+        pos += 1
+    return bad, shifts
+
+
+def pipe_kv_rank(rank, world, port, out):
+    # KV_SHIFT / KV_INFO across a pipeline of `world` stages: decoding past the
+    # context keeps every stage's window in step, bit for bit the one-GPU model
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import decoder_util as U
+    from spindle_b200.decoder import Decoder
+    from spindle_b200.tp import PipelineStage, TpGroup
+    init(rank, world, port, "nccl")
+    dev = torch.device("cuda", rank)
+    grp = None
+    try:
+        grp = TpGroup(device=dev)
+        # the last stage has the smaller cache: kv_info clamps the pipeline to it
+        cfg = dict(U.MOE, n_layers=8, max_seq=48 if rank == world - 1 else 64)
+        dtypes = U.dtypes_for(cfg)
+        W = U.device_weights(U.host_weights(cfg, dtypes, seed=62), dev)
+        stage = PipelineStage(Decoder(cfg, W, dtypes, dev), grp, n_max=8)
+        whole = Decoder(dict(cfg, max_seq=48), W, dtypes, dev) if rank == world - 1 else None
+        msgs = []
+        if stage.max_seq != 48:
+            msgs.append(("kv_info", stage.max_seq))
+        bad, shifts = pipe_shift_loop(stage, whole, 4, 120, dev)
+        if bad or shifts < 3:
+            msgs.append(("shift", bad, shifts))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        __import__("spindle_b200").device_status()
+        out.put((rank, "ok" if not msgs else repr(msgs)))
+    except Exception as e:
+        out.put((rank, repr(e)))
+    finally:
+        if grp is not None:
+            try:
+                grp.close()
+            except Exception as e:
+                out.put((rank, "close: " + repr(e)))
+        dist.destroy_process_group()
