@@ -302,14 +302,28 @@ def run_gpu(args):
             g_step.replay()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local) as clk:
             e0.record(stream)
             for _ in range(args.steps):
                 g_step.replay()
             e1.record(stream)
             e1.synchronize()
+            # a soak of about a second of the same step right after, still
+            # sampled, so that the clock record holds many samples under load
+            n_soak = 0
+            if not args.profile:
+                s0.record(stream)
+                t_end = time.time() + 1.0
+                while time.time() < t_end:
+                    for _ in range(200):
+                        g_step.replay()
+                    n_soak += 200
+                    s1.record(stream)
+                    s1.synchronize()
         barrier()
         ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+        soak_ms = s0.elapsed_time(s1) / n_soak if n_soak else None
         if args.profile:
             if rank == 0:
                 print(json.dumps({"profile": True, "shapes": [list(s) for s in SHAPES], "ms_per_step": ms}))
@@ -347,6 +361,91 @@ def run_gpu(args):
             us = tot / n_rep * 1e3
             per_shape.append({"shape": "%s %dx%d" % (NAME[dt], r, c), "us": round(us, 2),
                               "GB_s": round(alg_bytes(dt, r, c, nvec) / (us * 1e-6) / 1e9, 1)})
+
+        # one Q4_K 3072 x 1024 GEMV (1.78 MB).  Its
+        # single-launch latency, read from HBM after the sweep has evicted it,
+        # and a chain of launches over copies that hold 2.5x the L2 (each read
+        # from HBM), for an aggregate rate.
+        c1 = {}
+        if args.nvec == 1 and args.layout == "tiled":
+            w1 = sg.quantize_weights(Q4_K, torch.randn(3072, 1024, device=dev, generator=gen) * 0.02)
+            t1, m1 = sg.repack_tiled16(Q4_K, w1, 3072, 1024)
+            x1 = torch.randn(1, 1024, device=dev, generator=gen)
+            o1 = torch.empty(1, 3072, device=dev)
+            cb = alg_bytes(Q4_K, 3072, 1024, 1)
+            ncp = -(-int(2.5 * L2_BYTES) // t1.numel())
+            cps = [t1] + [t1.clone() for _ in range(ncp - 1)]
+            gs = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gs, stream=stream):
+                sg.matvec(t1, m1, x1, o1)
+            gc = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gc, stream=stream):
+                for w_ in cps:
+                    sg.matvec(w_, m1, x1, o1)
+            tot = 0.0
+            for _ in range(20):
+                g_gemv.replay()
+                a0.record(stream)
+                gs.replay()
+                a1.record(stream)
+                a1.synchronize()
+                tot += a0.elapsed_time(a1)
+            for _ in range(2):
+                gc.replay()
+            a0.record(stream)
+            for _ in range(10):
+                gc.replay()
+            a1.record(stream)
+            a1.synchronize()
+            per = a0.elapsed_time(a1) / 10 / ncp
+            c1 = {"shape": "Q4_K 3072x1024 (configs[0])", "us_single_launch": round(tot / 20 * 1e3, 2),
+                  "GB_s_single_launch": round(cb / (tot / 20 * 1e-3) / 1e9, 1),
+                  "us_per_launch_in_chain": round(per * 1e3, 2),
+                  "GB_s_in_chain": round(cb / (per * 1e-3) / 1e9, 1),
+                  "chain": "%d launches over %d copies (%.0f MB > 2.5 x L2), one graph" % (ncp, ncp, ncp * cb / 1e6)}
+            del cps, gc, gs
+        # BASELINE configs[1]'s vector counts (speculative-verify batches):
+        # the same sweep with N = 2, 4, 8 and 16 vectors per matrix
+        nvec_sweep = []
+        if args.nvec == 1 and args.layout == "tiled":
+            for nv in (2, 4, 8, 16):
+                Xn = [torch.randn(nv, c, device=dev, generator=gen) for _, _, c in SHAPES]
+                On = [torch.empty(nv, r, device=dev) for _, r, _ in SHAPES]
+                SCn = [torch.empty(lib.sg_matmul_batch_scratch_bytes(C.byref(M[k].c()), nv), dtype=torch.uint8,
+                                   device=dev) for k in range(len(SHAPES))]
+                sp_ = C.c_void_p(stream.cuda_stream)
+
+                def tiled_n():  # sg_matvec: the tiled GEMV, up to 8 vectors per launch
+                    for k in range(len(SHAPES)):
+                        sg.matvec(W[k], M[k], Xn[k], On[k])
+
+                def batch_n():  # sg_matmul_batch: one Q8_K batch image, then the batch GEMM
+                    for k in range(len(SHAPES)):
+                        _lib.check(lib.sg_matmul_batch(C.c_void_p(W[k].data_ptr()), C.byref(M[k].c()),
+                                                       C.c_void_p(Xn[k].data_ptr()), Xn[k].stride(0),
+                                                       C.c_void_p(On[k].data_ptr()), On[k].stride(0), nv, 0,
+                                                       M[k].rows, C.c_void_p(SCn[k].data_ptr()), SCn[k].numel(),
+                                                       sp_), "matmul_batch")
+
+                entry = {"n_vec": nv}
+                for label, fn in [("matvec", tiled_n), ("matmul_batch", batch_n)]:
+                    fn()
+                    torch.cuda.synchronize()
+                    gn = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gn, stream=stream):
+                        fn()
+                    for _ in range(3):
+                        gn.replay()
+                    a0.record(stream)
+                    for _ in range(30):
+                        gn.replay()
+                    a1.record(stream)
+                    a1.synchronize()
+                    t_ = a0.elapsed_time(a1) / 30
+                    entry[label] = {"us": round(t_ * 1e3, 2), "GB_s": round(step_bytes(nv) / (t_ * 1e-3) / 1e9, 1)}
+                    del gn
+                nvec_sweep.append(entry)
+                del Xn, On, SCn
 
         # ---- e2e through the C ABI with host buffers -----------------------
         # All activations of a step sit in one pinned host buffer and go up in
@@ -424,12 +523,21 @@ def run_gpu(args):
                 "config": config_block(args, world),
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args),
+                             "traffic_source": "profiles/bench_launch_list.md: ncu dram__bytes_read.sum + "
+                                               "dram__bytes_write.sum of the same 7 launches (committed capture)",
                              "algorithmic_bytes": gemv_bytes, "peak_source": peak_src,
                              "kernel": "gemv_tiled_kernel" if args.layout == "tiled" else "gemv_q8k_kernel",
                              "how": "algorithmic bytes of the 7 GEMV launches / their replayed duration "
                                     "(CUDA events on the launch stream); traffic = DRAM read + write "
                                     "of the same 7 launches from the committed ncu launch list"},
                 "per_shape": per_shape,
+                "config1": c1,
+                "nvec_sweep": [dict(e, best_frac=round(max(e["matvec"]["GB_s"], e["matmul_batch"]["GB_s"]) / peak, 4))
+                               for e in nvec_sweep],
+                "soak": {"seconds": round(soak_ms * n_soak / 1e3, 2) if soak_ms else None,
+                         "value": round(bytes_rank / (soak_ms * 1e-3) / 1e9, 1) if soak_ms else None,
+                         "how": "the step replayed for about a second right after the timed region, inside the "
+                                "clock record (same graph, same bytes per step)"},
                 "e2e": {"value": round(bytes_rank * world / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "how": "every step: one sg_memcpy_h2d of all fp32 activations from pinned host, "
@@ -1090,8 +1198,16 @@ def run_gpu_decode(args):
         # position PROMPT (no prompt pass), then the captured step replayed
         cfg["n_layers"] = 2
     dtypes = qwen3_dtypes(cfg, embed=Q4_K)
-    # the same model on every rank: N > 1 decodes one stream expert-parallel
-    W = random_weights(cfg, dtypes, dev, seed=5000)
+    if args.gguf:
+        # a model file (a real Q4_K_M GGUF, or one made by spindle_b200.gguf.write_model)
+        from spindle_b200 import gguf
+        gf = gguf.GgufFile(args.gguf)
+        cfg = dict(gguf.model_config(gf), max_seq=PROMPT + args.warmup + args.steps + 8)
+        name = "gguf:" + os.path.basename(args.gguf)
+        W, dtypes = gguf.load_weights(gf, cfg, dev)
+    else:
+        # the same model on every rank: N > 1 decodes one stream expert-parallel
+        W = random_weights(cfg, dtypes, dev, seed=5000)
     host = None
     if rank == 0 and world == 1 and args.cpu_budget > 0:
         # two layers' GGUF bytes plus embedding and head, for the CPU baseline
@@ -1620,6 +1736,7 @@ def main():
                     help="prefill workload: prompt length (default 2048; 128 with --profile)")
     ap.add_argument("--model", default="qwen3_30b_a3b", choices=sorted(DECODE_MODELS),
                     help="decode workload: the model architecture")
+    ap.add_argument("--gguf", default=None, help="decode workload: load the model from this GGUF file instead")
     args = ap.parse_args()
     if args.warmup < 3 and not args.profile:
         args.warmup = 3
