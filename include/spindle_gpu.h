@@ -501,6 +501,33 @@ SG_API sg_status sg_pipe_send(const float *d_src, uint64_t n, uint64_t n_max, vo
 SG_API sg_status sg_pipe_recv(float *d_dst, uint64_t n, uint64_t n_max, void *d_recv, void *d_comm, void *d_peer_comm,
                               void *stream);
 
+/* ---- the reference's synthetic benchmark kernels ----------------------------
+ * Prototypes driven by the reference's early benchmark (main.rs), not by its
+ * chat engine; fixed shapes (4096-wide rows of 16 Q4_K blocks, 8 experts, 32
+ * query / 8 KV heads of 128, 32 layers, 512 positions); results bit for bit
+ * the AVX2 kernels'. */
+/* q4k_gemv_4row_avx2 (q4k_gemv.rs:183-226): rows of d_chunk[chunk_len] in
+ * whole groups of four (*rows_done, optional, host), y[(row_offset + r) &
+ * 4095] += the row's dot with x (float [4096]); weights' d / dmin decoded by
+ * the module's own f16 conversion (q4k_gemv.rs:37-68, exponents clamped). */
+SG_API sg_status sg_q4k_gemv_4row(const uint8_t *d_chunk, uint64_t chunk_len, const float *d_x, float *d_y,
+                                  uint64_t row_offset, uint64_t *rows_done, void *stream);
+/* q4k_gemm_spec4_slice_avx2 (q4k_gemv.rs:361-403): rows [r0, r1) against four
+ * vectors x4 [4][4096], y4[k][(base + r) & 4095] += each row's dot. */
+SG_API sg_status sg_q4k_gemm_spec4(const uint8_t *d_chunk, uint64_t r0, uint64_t r1, const float *d_x4,
+                                   float *d_y4, uint64_t base, void *stream);
+/* route_moe_top2 (moe_engine.rs:124-164): the top 2 of 8 experts for x
+ * [4096] against gates [8][4096] (every 16th element), softmax weights. */
+SG_API sg_status sg_route_moe_top2(const float *d_x, const float *d_gates, uint64_t layer, int32_t *d_experts,
+                                   float *d_weights, void *stream);
+/* flash_decoding_gqa_spec4_avx2 (transformer.rs:541-600) on q_spec [4][4096]
+ * (replaced by the attention output) and the int8 KV cache of
+ * QuantizedKvCache (k, v: [32][512][1024] int8; ks, vs: [32][512][8] f32):
+ * the four tokens' K/V rows appended at seq_len (clamped to 508), then
+ * online-softmax attention over positions 0..seq_len + k. */
+SG_API sg_status sg_flash_gqa_spec4(float *d_q_spec, int8_t *d_kq, int8_t *d_vq, float *d_ks, float *d_vs,
+                                    uint64_t seq_len, uint64_t layer, void *stream);
+
 /* ---- weight quantizer (no reference counterpart: its tests use random bytes)
  * f32 [rows, cols] -> Q4_K or Q6_K rows, deterministic; cols % 256 == 0. */
 SG_API sg_status sg_quantize_weights(int32_t dtype, const float *d_w, uint64_t rows, uint64_t cols,

@@ -391,3 +391,84 @@ def rope_rotate(v, head_dim, inv_freq, neox, pos):
     _fwd_sigs().or_rope_rotate(_p(v), v.size, head_dim, _p(f), int(neox), pos)
     return v
 
+
+
+# ---- the reference's synthetic benchmark kernels (synth.c) -------------------
+
+SYNTH = dict(hidden=4096, row_bytes=2304, n_expert=8, layers=32, max_seq=512, kv_dim=1024, kv_heads=8, spec=4)
+
+
+def _synth_sigs():
+    L = lib()
+    if not hasattr(L, "_synth_ready"):
+        P, U64 = C.c_void_p, C.c_uint64
+        L.or_synth_f16.restype = C.c_float
+        L.or_synth_f16.argtypes = [C.c_uint16]
+        L.or_q4k_block_dot.restype = C.c_float
+        L.or_q4k_block_dot.argtypes = [P, P]
+        L.or_q4k_gemv_4row.restype = U64
+        L.or_q4k_gemv_4row.argtypes = [P, U64, P, P, U64]
+        L.or_q4k_gemm_spec4.restype = None
+        L.or_q4k_gemm_spec4.argtypes = [P, U64, U64, P, P, U64]
+        L.or_route_moe_top2.restype = None
+        L.or_route_moe_top2.argtypes = [P, P, U64, P, P]
+        L.or_kvcache_init.restype = None
+        L.or_kvcache_init.argtypes = [P, P, P, P, U64]
+        L.or_flash_gqa_spec4.restype = None
+        L.or_flash_gqa_spec4.argtypes = [P, P, P, P, P, U64, U64]
+        L._synth_ready = True
+    return L
+
+
+def synth_f16(h):
+    """q4k_gemv.rs's f16_to_f32 (non-IEEE: exponents clamped, 0x7C00.. finite)."""
+    return float(_synth_sigs().or_synth_f16(int(h)))
+
+
+def q4k_block_dot(blk, act):
+    """q4k_block_dot_avx2: one 144-byte block against 256 floats."""
+    blk = np.ascontiguousarray(blk, np.uint8)
+    act = np.ascontiguousarray(act, np.float32)
+    return float(_synth_sigs().or_q4k_block_dot(_p(blk), _p(act)))
+
+
+def q4k_gemv_4row(chunk, x, y, row_offset=0):
+    """q4k_gemv_4row_avx2 into y (float32 [4096], updated in place); rows done."""
+    chunk = np.ascontiguousarray(chunk, np.uint8)
+    x = np.ascontiguousarray(x, np.float32)
+    return int(_synth_sigs().or_q4k_gemv_4row(_p(chunk), chunk.size, _p(x), _p(y), row_offset))
+
+
+def q4k_gemm_spec4(chunk, r0, r1, x4, y4, base=0):
+    """q4k_gemm_spec4_slice_avx2: rows [r0, r1) for x4 [4][4096] into y4 [4][4096] (in place)."""
+    chunk = np.ascontiguousarray(chunk, np.uint8)
+    x4 = np.ascontiguousarray(x4, np.float32)
+    _synth_sigs().or_q4k_gemm_spec4(_p(chunk), r0, r1, _p(x4), _p(y4), base)
+
+
+def route_moe_top2(x, gates, layer):
+    """route_moe_top2: (experts [2], weights [2])."""
+    x = np.ascontiguousarray(x, np.float32)
+    gates = np.ascontiguousarray(gates, np.float32)
+    ex = np.zeros(2, np.int32)
+    w = np.zeros(2, np.float32)
+    _synth_sigs().or_route_moe_top2(_p(x), _p(gates), layer, _p(ex), _p(w))
+    return ex, w
+
+
+def kvcache_init(init_ctx):
+    """QuantizedKvCache::new(init_ctx): (k, v, k_scale, v_scale, seq_len)."""
+    S = SYNTH
+    k = np.zeros(S["layers"] * S["max_seq"] * S["kv_dim"], np.int8)
+    v = np.zeros_like(k)
+    ks = np.zeros(S["layers"] * S["max_seq"] * S["kv_heads"], np.float32)
+    vs = np.zeros_like(ks)
+    _synth_sigs().or_kvcache_init(_p(k), _p(v), _p(ks), _p(vs), init_ctx)
+    return k, v, ks, vs, min(init_ctx, S["max_seq"] - S["spec"])
+
+
+def flash_gqa_spec4(q_spec, cache, layer):
+    """flash_decoding_gqa_spec4_avx2 on q_spec [4][4096] (updated in place) and
+    the cache of kvcache_init (updated: the four new K/V rows)."""
+    k, v, ks, vs, seq = cache
+    _synth_sigs().or_flash_gqa_spec4(_p(q_spec), _p(k), _p(v), _p(ks), _p(vs), seq, layer)

@@ -11,7 +11,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_build")
 LIB = os.path.join(OUT_DIR, "libsg_oracle.so")
-SOURCES = ["gen.c", "q8k.c", "floatk.c", "pool.c", "kquant.c", "moe.c", "forward.c", "libm.c"]
+SOURCES = ["gen.c", "q8k.c", "floatk.c", "pool.c", "kquant.c", "moe.c", "forward.c", "libm.c", "synth.c"]
 CFLAGS = ["-O3", "-std=gnu11", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math",
           "-Wall", "-Wno-unused-function", "-pthread"]
 

@@ -164,6 +164,17 @@ float or_expf(float x);
 float or_sinf(float x);
 float or_cosf(float x);
 
+/* The reference's synthetic benchmark kernels (synth.c): q4k_gemv.rs,
+ * moe_engine.rs route_moe_top2, transformer.rs flash decoding. */
+float or_synth_f16(uint16_t h);
+float or_q4k_block_dot(const uint8_t *blk, const float *act);
+uint64_t or_q4k_gemv_4row(const uint8_t *chunk, uint64_t chunk_len, const float *x, float *y, uint64_t row_offset);
+void or_q4k_gemm_spec4(const uint8_t *chunk, uint64_t r0, uint64_t r1, const float *x4, float *y4, uint64_t base);
+void or_route_moe_top2(const float *x, const float *gates, uint64_t layer, int32_t *experts, float *weights);
+void or_kvcache_init(int8_t *k, int8_t *v, float *ks, float *vs, uint64_t init_ctx);
+void or_flash_gqa_spec4(float *q_spec, int8_t *kq, int8_t *vq, float *ks, float *vs, uint64_t seq_len,
+                        uint64_t layer);
+
 #ifdef __cplusplus
 }
 #endif

@@ -103,6 +103,10 @@ SIGNATURES = {
     "sg_block_sums": (I32, [P, C.POINTER(SgMat), C.POINTER(SgQ8K), P, U64, U64, P]),
     "sg_libm_eval": (I32, [I32, U64, U64, U64, P, P]),
     "sg_binary_version": (I32, [P]),
+    "sg_q4k_gemv_4row": (I32, [P, U64, P, P, U64, P, P]),
+    "sg_q4k_gemm_spec4": (I32, [P, U64, U64, P, P, U64, P]),
+    "sg_route_moe_top2": (I32, [P, P, U64, P, P, P]),
+    "sg_flash_gqa_spec4": (I32, [P, P, P, P, P, U64, U64, P]),
     "sg_quantize_weights": (I32, [I32, P, U64, U64, P, P]),
     "sg_tiled16_bytes": (I32, [I32, U64, U64, C.POINTER(U64)]),
     "sg_repack_tiled16": (I32, [I32, P, U64, U64, P, P]),
