@@ -375,28 +375,44 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
             for (uint32_t qq = 0; qq < ncols; qq++) {
                 const uint32_t q = c * bc + qq, i = b_lo + q;
                 const uint8_t *col = ring + st * a.stage_bytes + qq * CB;
-                int s[NV][4];
-                float cd[NV], ct[NV];
-                if constexpr (DT == 0)
-                    block_q4k<NV>(col, g, r, i, a.nvec, a.nb, tact, astride, s, cd, ct);
-                else
-                    block_q6k<NV>(col, g, r, i, a.nvec, a.nb, tact, astride, s, cd, ct);
-#pragma unroll
-                for (int v = 0; v < NV; v++) {
-                    if (v >= (int)a.nvec) break;
+                // the block's weights once, then the vectors one at a time, each
+                // vector's lane sums consumed by its chain (or handed to slot 0)
+                auto step = [&](int v, const int (&s)[4], float cd, float ct) {
                     if (slot == 0) {
 #pragma unroll
-                        for (int m = 0; m < 4; m++) acc[v][m] = __fmaf_rn(cd[v], lane_f<DT>(s[v][m]), acc[v][m]);
-                        corr[v] = __fadd_rn(corr[v], ct[v]);
+                        for (int m = 0; m < 4; m++) acc[v][m] = __fmaf_rn(cd, lane_f<DT>(s[m]), acc[v][m]);
+                        corr[v] = __fadd_rn(corr[v], ct);
                     } else {
                         float *e = mine + (q * NV + v) * CHAIN_FLOATS;
                         *reinterpret_cast<float4 *>(e + 64 * g + 4 * r) =
-                            make_float4(lane_f<DT>(s[v][0]), lane_f<DT>(s[v][1]), lane_f<DT>(s[v][2]),
-                                        lane_f<DT>(s[v][3]));
+                            make_float4(lane_f<DT>(s[0]), lane_f<DT>(s[1]), lane_f<DT>(s[2]), lane_f<DT>(s[3]));
                         if (g == 0) {
-                            e[128 + r] = cd[v];
-                            e[144 + r] = ct[v];
+                            e[128 + r] = cd;
+                            e[144 + r] = ct;
                         }
+                    }
+                };
+                if constexpr (DT == 0) {
+                    Q4KWeights wt;
+                    q4k_weights(col, g, r, wt);
+#pragma unroll
+                    for (int v = 0; v < NV; v++) {
+                        if (v >= (int)a.nvec) break;
+                        int s[4];
+                        float cd, ct;
+                        q4k_dot(wt, g, i, a.nb, tact + v * astride, s, cd, ct);
+                        step(v, s, cd, ct);
+                    }
+                } else {
+                    Q6KWeights wt;
+                    q6k_weights(col, g, r, wt);
+#pragma unroll
+                    for (int v = 0; v < NV; v++) {
+                        if (v >= (int)a.nvec) break;
+                        int s[4];
+                        float cd, ct;
+                        q6k_dot(wt, g, i, a.nb, tact + v * astride, s, cd, ct);
+                        step(v, s, cd, ct);
                     }
                 }
             }

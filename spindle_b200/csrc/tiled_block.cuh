@@ -70,6 +70,122 @@ __device__ __forceinline__ void named_arrive(uint32_t id, uint32_t n) {
     asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
+// The same per-block arithmetic split in two, so that a kernel running
+// several vectors decodes a block's weights once (q4k_weights / q6k_weights)
+// and then takes the vectors one at a time (q4k_dot / q6k_dot), each
+// vector's lane sums consumed before the next is computed (few live registers).
+struct Q4KWeights {
+    uint32_t lo[4][4], hi[4][4];
+    int sc[8];
+    float d, dmin;
+    uint32_t mnw;
+};
+
+__device__ __forceinline__ void q4k_weights(const uint8_t *col, uint32_t g, uint32_t r, Q4KWeights &w) {
+    const uint4 hd = lds128(col + 2048 + 16 * r);
+    w.d = h2f_lo(hd.x);
+    w.dmin = h2f_hi(hd.x);
+    const uint32_t sclo = hd.y & 0x3F3F3F3Fu, schi = (hd.w & M4) | ((hd.y >> 2) & B45);
+    w.mnw = g ? (((hd.w >> 4) & M4) | ((hd.z >> 2) & B45)) : (hd.z & 0x3F3F3F3Fu);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        w.sc[k] = ubyte(sclo, k);
+        w.sc[k + 4] = ubyte(schi, k);
+    }
+#pragma unroll
+    for (int cc = 0; cc < 4; cc++) {
+        const uint4 qv = lds128(col + 128 * r + 16 * q4k_chunk(2 * cc + g, r));
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            w.lo[cc][m] = w4(qv, m) & M4;
+            w.hi[cc][m] = w4(qv, m) & 0xF0F0F0F0u;
+        }
+    }
+}
+
+// av: one vector's activation image; s, cd, ct as block_q4k's for that vector
+__device__ __forceinline__ void q4k_dot(const Q4KWeights &w, uint32_t g, uint32_t i, uint32_t nb, const uint8_t *av,
+                                        int (&s)[4], float &cd, float &ct) {
+    const uint8_t *y = av + 256u * i + 16u * g;
+    const float xd = *reinterpret_cast<const float *>(av + 288u * nb + 4u * i);
+    int sh[4];
+#pragma unroll
+    for (int m = 0; m < 4; m++) s[m] = sh[m] = 0;
+#pragma unroll
+    for (int cc = 0; cc < 4; cc++) {
+        const uint4 Ylo = lds128(y + 64 * cc), Yhi = lds128(y + 64 * cc + 32);
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            s[m] += w.sc[2 * cc] * __dp4a((int)w.lo[cc][m], (int)w4(Ylo, m), 0);
+            sh[m] += w.sc[2 * cc + 1] * dp4a_us(w.hi[cc][m], (int)w4(Yhi, m));
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < 4; m++) s[m] += sh[m] >> 4;
+    cd = __fmul_rn(w.d, xd);
+    const uint4 B = lds128(av + 256u * nb + 32u * i + 16u * g);
+    int sp = 0;
+#pragma unroll
+    for (int m = 0; m < 4; m++) sp = __dp2a_lo((int)w4(B, m), (int)__byte_perm(w.mnw, 0, 0x11 * m), sp);
+    sp += __shfl_xor_sync(0xffffffffu, sp, 16);
+    ct = __fmul_rn(__fmul_rn(w.dmin, xd), __int2float_rn(sp));
+}
+
+struct Q6KWeights {
+    uint32_t w[8][4];
+    int scv[8];
+    float d;
+    uint32_t sw0, sw1;
+};
+
+__device__ __forceinline__ void q6k_weights(const uint8_t *col, uint32_t g, uint32_t r, Q6KWeights &q) {
+    const uint8_t *qrow = col + 192 * r;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const uint4 L0 = lds128(qrow + 16 * q6k_chunk(4 * h + g, r));
+        const uint4 L1 = lds128(qrow + 16 * q6k_chunk(4 * h + 2 + g, r));
+        const uint4 H = lds128(qrow + 16 * q6k_chunk(8 + 2 * h + g, r));
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            const uint32_t l0 = w4(L0, m), l1 = w4(L1, m), hh = w4(H, m);
+            q.w[4 * h + 0][m] = (l0 & M4) | ((hh << 4) & B45);
+            q.w[4 * h + 1][m] = (l1 & M4) | ((hh << 2) & B45);
+            q.w[4 * h + 2][m] = ((l0 >> 4) & M4) | (hh & B45);
+            q.w[4 * h + 3][m] = ((l1 >> 4) & M4) | ((hh >> 2) & B45);
+        }
+    }
+    const uint4 SC = lds128(col + 3072 + 16 * r);
+    q.d = __half2float(*reinterpret_cast<const __half *>(col + 3328 + 2 * r));
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) q.scv[4 * h + kk] = sbyte(w4(SC, 2 * h + (kk >> 1)), 2 * (kk & 1) + (int)g);
+    q.sw0 = g ? SC.z : SC.x;
+    q.sw1 = g ? SC.w : SC.y;
+}
+
+__device__ __forceinline__ void q6k_dot(const Q6KWeights &q, uint32_t g, uint32_t i, uint32_t nb, const uint8_t *av,
+                                        int (&s)[4], float &cd, float &ct) {
+    const uint8_t *y = av + 256u * i + 16u * g;
+    const float xd = *reinterpret_cast<const float *>(av + 288u * nb + 4u * i);
+#pragma unroll
+    for (int m = 0; m < 4; m++) s[m] = 0;
+#pragma unroll
+    for (int kk = 0; kk < 8; kk++) {
+        const uint4 Y = lds128(y + 32 * kk);
+#pragma unroll
+        for (int m = 0; m < 4; m++) s[m] += q.scv[kk] * __dp4a((int)q.w[kk][m], (int)w4(Y, m), 0);
+    }
+    cd = __fmul_rn(q.d, xd);
+    const uint4 B = lds128(av + 256u * nb + 32u * i + 16u * g);
+    int sp = __dp2a_lo((int)B.x, (int)q.sw0, 0);
+    sp = __dp2a_hi((int)B.y, (int)q.sw0, sp);
+    sp = __dp2a_lo((int)B.z, (int)q.sw1, sp);
+    sp = __dp2a_hi((int)B.w, (int)q.sw1, sp);
+    sp += __shfl_xor_sync(0xffffffffu, sp, 16);
+    ct = __fmul_rn(cd, __int2float_rn(32 * sp));
+}
+
 // One super-block of one 16-row tile for lanes 4g..4g+3 of row r: the exact
 // int32 lane sums s, d*xd (cd) and the correction term (ct) per vector.
 template <int NV>
