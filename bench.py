@@ -1332,7 +1332,7 @@ def run_gpu_decode(args):
 # at the positions after it.  One step = the whole 2048-token prefill.
 
 PREFILL_PROMPT = 2048
-PREFILL_CHUNK = 64
+PREFILL_CHUNK = 128  # feed's chunk (smollm_chat.rs:3090); --chunk overrides
 VERIFY_N = 9
 SPEC_TOKENS = 64
 
@@ -1356,7 +1356,7 @@ def run_gpu_prefill_pipe(args):
     """BASELINE configs[4] at N > 1: the prompt's prefill pipelined over the
     GPUs as a layer split (the two-PC mode of docs/cluster.md, layers 0..24 /
     24..48 at N = 2; par_rows's split of the layers in general).  Stage p runs
-    its layers on each 64-position chunk and sends the residual to stage p+1
+    its layers on each chunk of positions and sends the residual to stage p+1
     over NVLink (PipeLink: epoch-tagged peer stores), so while stage p+1 works
     on chunk c stage p already runs chunk c+1 (feed's chunks,
     smollm_chat.rs:3047-3071); the last stage runs the head on the prompt's
@@ -1381,7 +1381,7 @@ def run_gpu_prefill_pipe(args):
     dec = Decoder(cfg, W, dtypes, dev)
     del W
     grp = TpGroup(device=dev)
-    C_ = PREFILL_CHUNK
+    C_ = args.chunk or PREFILL_CHUNK
     links = [PipeLink(grp, p, p + 1, C_ * cfg["dim"]) for p in range(world - 1)]
     l0, l1 = shard_rows(cfg["n_layers"], world, rank)
     g = torch.Generator().manual_seed(78)
@@ -1486,7 +1486,7 @@ def run_gpu_prefill(args):
     del W
     L = _sigs()
     lib = sg.lib()
-    C_ = PREFILL_CHUNK
+    C_ = args.chunk or PREFILL_CHUNK
     nbytes = L.sg_model_batch_scratch_bytes(C.byref(dec.model), C_)
     scr = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     _lib.check(L.sg_model_batch_prepare(C.byref(dec.model), C_, C.c_void_p(scr.data_ptr()), nbytes, None), "prepare")
@@ -1737,6 +1737,7 @@ def main():
     ap.add_argument("--model", default="qwen3_30b_a3b", choices=sorted(DECODE_MODELS),
                     help="decode workload: the model architecture")
     ap.add_argument("--gguf", default=None, help="decode workload: load the model from this GGUF file instead")
+    ap.add_argument("--chunk", type=int, default=0, help="prefill workload: positions per batch call (default 128)")
     args = ap.parse_args()
     if args.warmup < 3 and not args.profile:
         args.warmup = 3

@@ -157,7 +157,7 @@ SG_API sg_status sg_matvec(const uint8_t *d_base, const sg_mat *m, const float *
  * GEMM launch).  Bit for bit the results of sg_matvec (and of the reference's
  * integer kernel).  Scratch: sg_matmul_batch_scratch_bytes(m, n_vec) device
  * bytes, 16-byte aligned, caller-owned; ldx % 4 == 0. */
-#define SG_BATCH_MAX_VEC 64
+#define SG_BATCH_MAX_VEC 128
 SG_API uint64_t sg_matmul_batch_scratch_bytes(const sg_mat *m, uint64_t n_vec);
 SG_API sg_status sg_matmul_batch(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx,
                                  float *d_out, uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1,
@@ -339,13 +339,13 @@ SG_API sg_status sg_moe_forward(const sg_moe *m, const float *d_x, float *d_out,
 /* moe_forward_batch (smollm_chat.rs:928-1174): n_tok tokens through the same
  * layer, out_t = moe_forward(x_t), bit for bit what n_tok one-token calls give
  * (the reference's batch is one-token-identical too, :4699-4736).  x_t =
- * d_x + t*ldx (16-byte aligned), out_t = d_out + t*ldo; n_tok <= 64 and
+ * d_x + t*ldx (16-byte aligned), out_t = d_out + t*ldo; n_tok <= 128 and
  * n_expert <= 256.  The router runs once over all tokens, one launch makes
  * every token's choice and a table of (expert, token) slots, and the gate/up
  * and down passes each run over all slots in one launch (each block stages
  * the Q8_K image of every token its slots use).  d_choices (optional,
  * [n_tok]) receives the choices. */
-#define SG_MOE_MAX_BATCH 64
+#define SG_MOE_MAX_BATCH 128
 SG_API uint64_t sg_moe_batch_scratch_bytes(const sg_moe *m, uint64_t n_tok);
 SG_API sg_status sg_moe_forward_batch(const sg_moe *m, const float *d_x, uint64_t ldx, uint64_t n_tok, float *d_out,
                                       uint64_t ldo, void *d_scratch, uint64_t scratch_bytes,
@@ -452,7 +452,8 @@ SG_API sg_status sg_forward_ep(const sg_model *m, const sg_moe_ep *eps, int32_t 
  * sg_forward step at that position.  d_logits (optional): [n][ldl] floats;
  * d_greedy (optional): int64[n], each token's greedy next token.  Scratch:
  * sg_model_batch_scratch_bytes(m, n_max) bytes made ready once by
- * sg_model_batch_prepare; n <= n_max <= 64 (MoE layers: n_expert <= 256). */
+ * sg_model_batch_prepare; n <= n_max <= 128, feed's chunk (smollm_chat.rs:3090)
+ * (MoE layers: n_expert <= 256). */
 SG_API uint64_t sg_model_batch_scratch_bytes(const sg_model *m, uint64_t n_max);
 SG_API sg_status sg_model_batch_prepare(const sg_model *m, uint64_t n_max, void *d_scratch, uint64_t scratch_bytes,
                                         void *stream);

@@ -462,7 +462,7 @@ sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, 
     return SG_OK;
 }
 
-// ---- batch GEMM (9..64 vectors) ----------------------------------------------
+// ---- batch GEMM (9..128 vectors) ----------------------------------------------
 
 // QB image (gemm_batch.cuh) of n fp32 vectors x + t * ldx of 256 * nb values.
 sg_status launch_q8k_batch(const float *x, uint64_t ldx, uint32_t n, uint32_t nb, uint8_t *qb, cudaStream_t s) {
@@ -473,7 +473,7 @@ sg_status launch_q8k_batch(const float *x, uint64_t ldx, uint32_t n, uint32_t nb
     return SG_OK;
 }
 
-// Rows r0..r1 of a TILED16 matrix for ntok <= 64 vectors given as a QB image:
+// Rows r0..r1 of a TILED16 matrix for ntok <= 128 vectors given as a QB image:
 // vector t, row r at out + t * ldo + r (swiglu: the packed gate/up form, see
 // GemmBatchArgs).  One launch; every weight column is read once.
 // Q4_K / Q6_K on the tensor cores (gemm_tc.cu): CTAs of 128 rows x 16 tokens.
@@ -513,12 +513,22 @@ sg_status launch_gemm_tc(const uint8_t *w, int dt, uint32_t nb, uint64_t r0, uin
 sg_status launch_gemm_batch(const uint8_t *w, int dt, uint32_t nb, uint64_t r0, uint64_t r1, const uint8_t *qb,
                             uint32_t ntok, float *out, uint64_t ldo, bool swiglu, cudaStream_t s) {
     if (ntok == 0 || r1 <= r0) return SG_OK;
-    if (ntok > GB_MAX_TOK) return SG_ERR_SHAPE;
+    if (ntok > QB_MAX_TOK) return SG_ERR_SHAPE;
     // tensor cores: Q4_K by default, Q6_K with SG_GEMM_TC=2; SG_GEMM_TC=0 keeps
     // both on the dp4a kernel
     const int tc = env_int("SG_GEMM_TC", 1);
     if ((dt == DT_Q4K && tc >= 1) || (dt == DT_Q6K && tc >= 2))
         return launch_gemm_tc(w, dt, nb, r0, r1, qb, ntok, out, ldo, swiglu, s);
+    if (ntok > GB_MAX_TOK) {
+        // the dp4a kernel takes one QB group (64 vectors) per launch
+        for (uint32_t q = 0; q * QB_GROUP < ntok; q++) {
+            const sg_status st = launch_gemm_batch(w, dt, nb, r0, r1, qb + qb_group_offset(q, nb),
+                                                   qb_group_tokens(ntok, q), out + (uint64_t)q * QB_GROUP * ldo, ldo,
+                                                   swiglu, s);
+            if (st) return st;
+        }
+        return SG_OK;
+    }
     static std::atomic<uint64_t> attr_done{0};
     int dev;
     CK(cudaGetDevice(&dev));
@@ -1179,7 +1189,7 @@ sg_status sg_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x, ui
 
 uint64_t sg_matmul_batch_scratch_bytes(const sg_mat *m, uint64_t n_vec) {
     if (!m || m->cols % 256 || n_vec == 0 || n_vec > SG_BATCH_MAX_VEC) return 0;
-    return (uint64_t)(m->cols / 256) * qb_block_bytes((uint32_t)n_vec);
+    return qb_image_bytes((uint32_t)n_vec, (uint32_t)(m->cols / 256));
 }
 
 sg_status sg_matmul_batch(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
@@ -1672,7 +1682,7 @@ ModelBatchScratch model_batch_scratch(const sg_model *m, uint64_t n) {
     // QB image of the widest input of a batch GEMM (dim, q_dim or a dense n_ff)
     uint64_t widest = m->dim > q_dim ? m->dim : q_dim;
     if (n_ff > widest) widest = n_ff;
-    L.qb = take(widest / 256 * qb_block_bytes((uint32_t)n));
+    L.qb = take(qb_image_bytes((uint32_t)n, (uint32_t)(widest / 256)));
     L.total = off;
     return L;
 }
@@ -1851,7 +1861,7 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
         // a later pipeline stage: the raw residual of the stage before
         CK(cudaMemcpyAsync(x, d_hidden_in, (uint64_t)nt * dim * 4, cudaMemcpyDeviceToDevice, s));
         CK(cudaMemsetAsync(n_slots, 0, 4, s));
-        CK(cudaMemsetAsync(n_slots, (int)nt, 1, s));  // nt <= 64: the low byte
+        CK(cudaMemsetAsync(n_slots, (int)nt, 1, s));  // nt <= 128: the low byte
     }
     for (uint32_t l = l0; l < l1; l++) {
         const sg_layer &y = m->layers[l];

@@ -130,9 +130,11 @@ __global__ void __launch_bounds__(256) q8k_batch_kernel(const __grid_constant__ 
     const uint64_t wid = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (wid >= (uint64_t)a.n * a.nb) return;
     const uint32_t t = (uint32_t)(wid / a.nb), i = (uint32_t)(wid % a.nb);
-    uint8_t *blk = a.qb + (uint64_t)i * qb_block_bytes(a.n);
-    q8k_block(a.x + t * a.ldx + 256u * i, reinterpret_cast<int8_t *>(blk + 256u * t),
-              reinterpret_cast<int16_t *>(blk + 256u * a.n + 32u * t), reinterpret_cast<float *>(blk + 288u * a.n) + t,
+    // token t is vector u of QB group q (gemm_batch.cuh)
+    const uint32_t q = t / QB_GROUP, u = t % QB_GROUP, n = qb_group_tokens(a.n, q);
+    uint8_t *blk = a.qb + qb_group_offset(q, a.nb) + (uint64_t)i * qb_block_bytes(n);
+    q8k_block(a.x + t * a.ldx + 256u * i, reinterpret_cast<int8_t *>(blk + 256u * u),
+              reinterpret_cast<int16_t *>(blk + 256u * n + 32u * u), reinterpret_cast<float *>(blk + 288u * n) + u,
               lane);
 }
 

@@ -1,5 +1,5 @@
 // gemm_batch.cuh — Q4_K / Q6_K weights x Q8_K activations for a batch of up
-// to 64 vectors (matvec_multi / matmul_rows with many vectors,
+// to 64 vectors per launch (matvec_multi / matmul_rows with many vectors,
 // smollm_chat.rs:447-512, quant_q8k.rs:255-295): the prefill chunks and the
 // verify batches of forward_batch_slice.
 //
@@ -25,16 +25,30 @@
 
 namespace sg {
 
-constexpr uint32_t GB_MAX_TOK = 64;
+constexpr uint32_t GB_MAX_TOK = 64;    // vectors of one gemm_batch_kernel launch (one QB group)
+constexpr uint32_t QB_MAX_TOK = 128;   // vectors of one QB image (prefill chunks of feed, smollm_chat.rs:3090)
 constexpr uint32_t GB_MAX_STAGES = 6;
 // warps per CTA for TPW vectors per warp
 __host__ __device__ constexpr uint32_t gb_consumers(int tpw) { return 64u / (uint32_t)tpw; }
 constexpr uint32_t GB_BAR_BYTES = 128;
 
-// QB: Q8_K images of n vectors, block-major.  Block i is at qb + i *
-// qb_block_bytes(n): qs[n][256] | bsums[n][16] (int16) | d[n] (float), the
-// whole padded to 16 bytes.
+// QB: Q8_K images of n vectors, block-major, in groups of QB_GROUP vectors.
+// Group q (vectors 64q .. 64q + n_q - 1, n_q = min(64, n - 64q)) starts at qb
+// + q * nb * qb_block_bytes(64); its block i is at + i * qb_block_bytes(n_q):
+// qs[n_q][256] | bsums[n_q][16] (int16) | d[n_q] (float), padded to 16
+// bytes.  With n <= 64 there is one group, the plain block-major image.
+constexpr uint32_t QB_GROUP = 64;
 __host__ __device__ inline uint32_t qb_block_bytes(uint32_t n) { return (n * 292u + 15u) & ~15u; }
+__host__ __device__ inline uint64_t qb_group_offset(uint32_t q, uint32_t nb) {
+    return (uint64_t)q * nb * qb_block_bytes(QB_GROUP);
+}
+__host__ __device__ inline uint32_t qb_group_tokens(uint32_t n, uint32_t q) {
+    return n - q * QB_GROUP < QB_GROUP ? n - q * QB_GROUP : QB_GROUP;
+}
+__host__ __device__ inline uint64_t qb_image_bytes(uint32_t n, uint32_t nb) {
+    const uint32_t full = n / QB_GROUP, rem = n % QB_GROUP;
+    return qb_group_offset(full, nb) + (rem ? (uint64_t)nb * qb_block_bytes(rem) : 0u);
+}
 
 // One warp per (vector, block): x_t = x + t * ldx (cols = 256 * nb floats,
 // 16-byte aligned rows), the exact Q8K::quantize of quant_q8k.rs:84-121.

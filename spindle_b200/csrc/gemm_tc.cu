@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q4k_kernel(const __grid
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + 64);
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     constexpr uint32_t CB = 2304;  // tiled_col_bytes(Q4_K)
-    if (blockDim.x != TC_THREADS || a.nb == 0 || a.ntok == 0 || a.ntok > GB_MAX_TOK ||
+    if (blockDim.x != TC_THREADS || a.nb == 0 || a.ntok == 0 || a.ntok > QB_MAX_TOK ||
         gridDim.y * TC_TOK < a.ntok || dynamic_smem_size() < TC_SMEM) {
         if (tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
         return;
@@ -200,7 +200,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q4k_kernel(const __grid
     const uint32_t tbase = *tmem_slot;
 
     const uint64_t tile_bytes = (uint64_t)a.nb * CB;
-    const uint32_t qbb = qb_block_bytes(a.ntok);
+    // this CTA's 16 tokens lie in QB group gq (TC_TOK divides QB_GROUP): its
+    // image holds gn vectors, token xtok is its vector xtok - 64 gq
+    const uint32_t gq = blockIdx.y * TC_TOK / QB_GROUP, gn = qb_group_tokens(a.ntok, gq);
+    const uint8_t *qimg = a.qb + qb_group_offset(gq, a.nb);
+    const uint32_t qbb = qb_block_bytes(gn);
     // staging roles
     const uint32_t rr = tid & 127u, g = tid >> 7, jt = rr >> 4, r = rr & 15u;
     const bool tile_ok = blockIdx.x * 8u + jt < a.ntiles;
@@ -209,7 +213,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q4k_kernel(const __grid
     // token staging: 8 consecutive threads take 8 tokens of one core matrix
     // (one 128-byte shared-memory wavefront per store phase)
     const uint32_t xt = (tid & 7u) | ((tid >> 4) & 8u), xc = (tid >> 3) & 15u, xL = xc >> 1, xjj = xc & 1u;
-    const uint32_t xtok = blockIdx.y * TC_TOK + xt;
+    const uint32_t xtok = blockIdx.y * TC_TOK + xt, xu = xtok - gq * QB_GROUP;
     const bool xok = xtok < a.ntok;
     // epilogue roles
     const uint32_t q = warp & 3u, th = warp >> 2;
@@ -226,12 +230,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q4k_kernel(const __grid
     float xdv = 0.0f;
     auto load_x = [&](uint32_t i) {
         if (!xok) return;
-        const uint8_t *blk = a.qb + (uint64_t)i * qbb;
+        const uint8_t *blk = qimg + (uint64_t)i * qbb;
 #pragma unroll
         for (int j = 0; j < 4; j++)
-            yw[j] = __ldg(reinterpret_cast<const uint32_t *>(blk + 256u * xtok + 32u * (4u * xjj + j) + 4u * xL));
-        if (xc < 8) bsw = __ldg(reinterpret_cast<const uint32_t *>(blk + 256u * a.ntok + 32u * xtok + 4u * xc));
-        if (xc == 8) xdv = __ldg(reinterpret_cast<const float *>(blk + 288u * a.ntok) + xtok);
+            yw[j] = __ldg(reinterpret_cast<const uint32_t *>(blk + 256u * xu + 32u * (4u * xjj + j) + 4u * xL));
+        if (xc < 8) bsw = __ldg(reinterpret_cast<const uint32_t *>(blk + 256u * gn + 32u * xu + 4u * xc));
+        if (xc == 8) xdv = __ldg(reinterpret_cast<const float *>(blk + 288u * gn) + xu);
     };
     auto stage = [&](uint32_t s) { return smem + TC_HDR_BYTES + s * TC_STAGE_BYTES; };
     auto xslot = [&](uint32_t i) { return reinterpret_cast<int32_t *>(smem + 1024 + (i % 3u) * TC_XS_BYTES); };
@@ -389,7 +393,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q6k_kernel(const __grid
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     constexpr uint32_t CB = 3360;  // tiled_col_bytes(Q6_K)
     constexpr uint32_t SBO6 = 16u * 128u;  // 16 core matrices along K per 8-row group
-    if (blockDim.x != TC_THREADS || a.nb == 0 || a.ntok == 0 || a.ntok > GB_MAX_TOK ||
+    if (blockDim.x != TC_THREADS || a.nb == 0 || a.ntok == 0 || a.ntok > QB_MAX_TOK ||
         gridDim.y * TC_TOK < a.ntok || dynamic_smem_size() < TC6_SMEM) {
         if (tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
         return;
@@ -403,13 +407,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q6k_kernel(const __grid
     const uint32_t tbase = *tmem_slot;
 
     const uint64_t tile_bytes = (uint64_t)a.nb * CB;
-    const uint32_t qbb = qb_block_bytes(a.ntok);
+    const uint32_t gq = blockIdx.y * TC_TOK / QB_GROUP, gn = qb_group_tokens(a.ntok, gq);  // as the Q4_K kernel
+    const uint8_t *qimg = a.qb + qb_group_offset(gq, a.nb);
+    const uint32_t qbb = qb_block_bytes(gn);
     const uint32_t rr = tid & 127u, h = tid >> 7, jt = rr >> 4, r = rr & 15u;
     const bool tile_ok = blockIdx.x * 8u + jt < a.ntiles;
     const uint32_t T = a.t0 + blockIdx.x * 8u + jt;
     const uint8_t *wrow = a.w + (uint64_t)(tile_ok ? T : a.t0) * tile_bytes;
     const uint32_t xt = tid >> 4, xc = tid & 15u, xm = xc >> 2, xq = xc & 3u;
-    const uint32_t xtok = blockIdx.y * TC_TOK + xt;
+    const uint32_t xtok = blockIdx.y * TC_TOK + xt, xu = xtok - gq * QB_GROUP;
     const bool xok = xtok < a.ntok;
     const uint32_t q = warp & 3u, th = warp >> 2;
     auto stage = [&](uint32_t u) { return smem + TC6_HDR_BYTES + u * TC6_STAGE_BYTES; };
@@ -428,14 +434,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_q6k_kernel(const __grid
     };
     auto load_x = [&](uint32_t i, uint32_t u) {
         if (!xok) return;
-        const uint8_t *blk = a.qb + (uint64_t)i * qbb;
+        const uint8_t *blk = qimg + (uint64_t)i * qbb;
         const uint32_t L = 4u * u + xm;
 #pragma unroll
         for (int j = 0; j < 2; j++)
-            yw[j] = __ldg(reinterpret_cast<const uint32_t *>(blk + 256u * xtok + 32u * (2u * xq + j) + 4u * L));
+            yw[j] = __ldg(reinterpret_cast<const uint32_t *>(blk + 256u * xu + 32u * (2u * xq + j) + 4u * L));
         if (u == 0) {
-            bsw = (uint32_t)__ldg(reinterpret_cast<const unsigned short *>(blk + 256u * a.ntok + 32u * xtok) + xc);
-            if (xc == 0) xdv = __ldg(reinterpret_cast<const float *>(blk + 288u * a.ntok) + xtok);
+            bsw = (uint32_t)__ldg(reinterpret_cast<const unsigned short *>(blk + 256u * gn + 32u * xu) + xc);
+            if (xc == 0) xdv = __ldg(reinterpret_cast<const float *>(blk + 288u * gn) + xu);
         }
     };
     // two 16-bit lanes holding n < 1024 -> f16 pair n * sc, exact (|n sc| <= 1920)

@@ -1,4 +1,4 @@
-// gemm_tc.cuh — Q4_K / Q6_K weights x Q8_K activations for a batch of up to 64
+// gemm_tc.cuh — Q4_K / Q6_K weights x Q8_K activations for a batch of up to 128
 // vectors on the 5th-generation tensor cores (tcgen05.mma, accumulators in
 // TMEM), bit for bit the GEMV's and the reference's matmul_rows
 // (quant_q8k.rs:166-295, block layouts of q4k_gemv.rs:26-31 and quant.rs:34-39).

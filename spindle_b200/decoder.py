@@ -240,6 +240,7 @@ class Decoder:
             raise ValueError("the batch forward is not expert-parallel; build the Decoder without ep")
         L = _sigs()
         n = len(tokens)
+        n_max = max(n_max, n)
         if getattr(self, "_bscratch", None) is None or self._bn < n_max:
             nbytes = L.sg_model_batch_scratch_bytes(C.byref(self.model), n_max)
             if not nbytes:
@@ -270,6 +271,7 @@ class Decoder:
             raise ValueError("the batch forward is not expert-parallel; build the Decoder without ep")
         L = _sigs()
         n = len(tokens) if tokens is not None else hidden.shape[0]
+        n_max = max(n_max, n)
         if getattr(self, "_bscratch", None) is None or self._bn < n_max:
             nbytes = L.sg_model_batch_scratch_bytes(C.byref(self.model), n_max)
             if not nbytes:
@@ -292,9 +294,9 @@ class Decoder:
                    "sg_forward_batch_range")
         return (lg, greedy) if with_head else (out,)
 
-    def feed(self, tokens, pos0=0, chunk=64, stream=None):
+    def feed(self, tokens, pos0=0, chunk=128, stream=None):
         """feed (smollm_chat.rs:3042-3106): the prompt in chunks of `chunk`
-        positions (the reference uses 128; the batch path here takes up to 64),
+        positions (128 as the reference's, at most SG_MOE_MAX_BATCH = 128),
         K/V rows into the caches, no LM head; returns the last position's
         output-normed hidden state (float32 CUDA [dim])."""
         tokens = list(tokens)

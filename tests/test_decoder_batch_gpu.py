@@ -79,10 +79,13 @@ def test_batch_variants(dev):
 
 
 def test_batch_long_context(dev):
-    # past the attention kernel's 128-position chunks, batches of 64
+    # past the attention kernel's 128-position chunks, batches of 64 and of
+    # 128 (feed's chunk, two QB groups per image)
     cfg = dict(U.DENSE, max_seq=300)
     toks = np.random.default_rng(7).integers(0, cfg["vocab"], 200).tolist()
     run(cfg, U.dtypes_for(cfg), 74, toks, [64, 64, 9, 63], dev)
+    toks = np.random.default_rng(10).integers(0, cfg["vocab"], 290).tolist()
+    run(cfg, U.dtypes_for(cfg), 79, toks, [128, 100, 62], dev)
 
 
 def test_batch_moe_verify_chunks(dev):
@@ -92,8 +95,9 @@ def test_batch_moe_verify_chunks(dev):
     run(cfg, U.dtypes_for(cfg), 75, toks, [9, 9], dev)
 
 
+@pytest.mark.parametrize("chunk", [64, 128])
 @pytest.mark.parametrize("kind", ["dense", "moe"])
-def test_feed_matches_steps(dev, kind):
+def test_feed_matches_steps(dev, kind, chunk):
     # feed (smollm_chat.rs:3042-3106): chunks without the LM head; the last
     # output-normed hidden state and every K/V row equal the one-token steps'
     cfg = dict(U.DENSE if kind == "dense" else U.MOE, max_seq=160)
@@ -105,7 +109,7 @@ def test_feed_matches_steps(dev, kind):
     for pos, t in enumerate(toks):
         seq.set_state(t, pos)
         seq.step(logits=False)
-    h = bat.feed(toks, 0, chunk=64)
+    h = bat.feed(toks, 0, chunk=chunk)
     torch.cuda.synchronize()
     assert np.array_equal(bits(h.cpu().numpy()), bits(seq.hidden.cpu().numpy()))
     assert torch.equal(seq.kv, bat.kv)

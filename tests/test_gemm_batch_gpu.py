@@ -1,5 +1,5 @@
-"""GPU parity of the dp4a batch GEMM (sg_matmul_batch: matvec_multi over 9..64
-vectors in one pass, smollm_chat.rs:447-512): bit-identical to the oracle's
+"""GPU parity of the dp4a batch GEMM (sg_matmul_batch: matvec_multi over 9..128
+vectors, one pass per group of 64, smollm_chat.rs:447-512): bit-identical to the oracle's
 Q8K::quantize + matmul_rows (quant_q8k.rs:84-121, :255-295) and to the GEMV,
 including non-finite inputs, ragged row counts, row ranges and every token
 group size."""
@@ -32,7 +32,7 @@ def bits(a):
 @pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
 def test_batch_gemm_matches_oracle(dev, dt):
     for n, rows, nvec in [(256, 37, 9), (1024, 301, 16), (2048, 45, 17), (512, 130, 33), (2048, 64, 64),
-                          (4096, 19, 40), (256, 16, 1), (768, 90, 5)]:
+                          (4096, 19, 40), (256, 16, 1), (768, 90, 5), (1024, 77, 65), (512, 40, 128), (768, 33, 100)]:
         rng = O.Rng(7 * n + rows + nvec)
         w = O.random_matrix(dt, n, rows, rng)
         xs = np.stack([rng.fill(-2.0, 2.0, n) for _ in range(nvec)])
@@ -58,7 +58,8 @@ def test_batch_gemm_matches_oracle(dev, dt):
 def test_batch_gemm_matches_gemv_at_model_shapes(dev, dt):
     # the decoder's projections and LM head at prefill / verify widths
     g = torch.Generator(device=dev).manual_seed(11)
-    for rows, cols, nvec in [(4608, 2048, 64), (512, 2048, 9), (2048, 4096, 64), (151936, 1024, 9), (3072, 1024, 24)]:
+    for rows, cols, nvec in [(4608, 2048, 64), (512, 2048, 9), (2048, 4096, 64), (151936, 1024, 9), (3072, 1024, 24),
+                             (512, 2048, 128), (2048, 4096, 128)]:
         wq = sg.quantize_weights(dt, torch.randn(rows, cols, device=dev, generator=g) * 0.02)
         t, m = sg.repack_tiled16(dt, wq, rows, cols)
         xs = torch.randn(nvec, cols, device=dev, generator=g)
@@ -73,5 +74,5 @@ def test_batch_gemm_rejects(dev):
     with pytest.raises(sg.SgError):   # GGUF layout
         sg.matmul_batch(w, sg.Mat(sg.Q4_K, 1024, 1), torch.zeros(9, 1024, device=dev))
     t, m = sg.repack_tiled16(O.Q4_K, torch.zeros(144 * 4 * 16, dtype=torch.uint8, device=dev), 16, 1024)
-    with pytest.raises(sg.SgError):   # more than 64 vectors
-        sg.matmul_batch(t, m, torch.zeros(65, 1024, device=dev))
+    with pytest.raises(sg.SgError):   # more than 128 vectors
+        sg.matmul_batch(t, m, torch.zeros(129, 1024, device=dev))

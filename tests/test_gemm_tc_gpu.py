@@ -32,7 +32,8 @@ def bits(a):
 @pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
 def test_tc_gemm_matches_oracle(dev, tc, dt):
     for n, rows, nvec in [(256, 37, 9), (1024, 301, 16), (2048, 45, 17), (512, 130, 33), (2048, 64, 64),
-                          (4096, 19, 40), (256, 16, 1), (768, 90, 5), (1536, 257, 63)]:
+                          (4096, 19, 40), (256, 16, 1), (768, 90, 5), (1536, 257, 63), (1024, 140, 65),
+                          (512, 40, 128), (768, 130, 97)]:
         rng = O.Rng(7 * n + rows + nvec)
         w = O.random_matrix(dt, n, rows, rng)
         xs = np.stack([rng.fill(-2.0, 2.0, n) for _ in range(nvec)])
@@ -75,7 +76,8 @@ def test_tc_gemm_extreme_blocks(dev, tc):
 @pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
 def test_tc_gemm_matches_gemv_at_model_shapes(dev, tc, dt):
     g = torch.Generator(device=dev).manual_seed(11)
-    for rows, cols, nvec in [(4608, 2048, 64), (512, 2048, 9), (2048, 4096, 64), (151936, 1024, 9), (3072, 1024, 24)]:
+    for rows, cols, nvec in [(4608, 2048, 64), (512, 2048, 9), (2048, 4096, 64), (151936, 1024, 9), (3072, 1024, 24),
+                             (4608, 2048, 128), (2048, 4096, 128)]:
         wq = sg.quantize_weights(dt, torch.randn(rows, cols, device=dev, generator=g) * 0.02)
         t, m = sg.repack_tiled16(dt, wq, rows, cols)
         xs = torch.randn(nvec, cols, device=dev, generator=g)

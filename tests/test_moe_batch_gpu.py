@@ -39,7 +39,7 @@ def run_batch(L, xs, dev, norm=True, prune=0.0):
     return got
 
 
-@pytest.mark.parametrize("n_tok", [1, 2, 9, 17])
+@pytest.mark.parametrize("n_tok", [1, 2, 9, 17, 128])
 def test_moe_batch_small(dev, n_tok):
     L = make_layer(7, 512, 256, 16, 4)
     xs = np.stack([O.Rng(100 + t).fill(-1.0, 1.0, 512) for t in range(n_tok)])
@@ -87,7 +87,7 @@ def test_moe_batch_bad_args(dev):
     L = make_layer(14, 256, 256, 16, 4)
     m = gpu_layer(L, dev)
     with pytest.raises(sg.SgError) as e:
-        sg.moe_forward_batch(m, torch.zeros(65, 256, device=dev), scratch=torch.empty(1 << 20, dtype=torch.uint8,
+        sg.moe_forward_batch(m, torch.zeros(129, 256, device=dev), scratch=torch.empty(1 << 20, dtype=torch.uint8,
                                                                                           device=dev))
     assert e.value.status == 3
     L2 = make_layer(15, 256, 256, 300, 4)
