@@ -193,7 +193,7 @@ def matvec_rows_float(base, m, xs, out=None, r0=0, r1=None, stream=None):
 
 
 def matmul_batch(base, m, xs, out=None, r0=0, r1=None, stream=None):
-    """matvec_multi (smollm_chat.rs:447-512) for up to 64 vectors in one pass
+    """matvec_multi (smollm_chat.rs:447-512) for up to 128 vectors in one pass
     over a TILED16 Q4_K / Q6_K matrix: fp32 CUDA xs [n_vec, cols] -> out
     [n_vec, rows] (rows outside r0..r1 untouched), bit for bit the GEMV's."""
     xs2 = xs.reshape(1, -1) if xs.dim() == 1 else xs

@@ -246,15 +246,19 @@ tgemv_fn pick_tiled_t(int nv) {
 tgemv_fn pick_tiled(int dt, int nv, int mode) {
     if (dt == DT_Q4K) {
         switch (mode) {
-        case IN_MOE_X: return gemv_tiled_kernel<0, 1, IN_MOE_X>;
-        case IN_MOE_H: return gemv_tiled_kernel<0, 1, IN_MOE_H>;
+        case IN_MOE_X: return nv <= 1 ? gemv_tiled_kernel<0, 1, IN_MOE_X> : nv <= 4 ? gemv_tiled_kernel<0, 4, IN_MOE_X>
+                                                                             : gemv_tiled_kernel<0, 8, IN_MOE_X>;
+        case IN_MOE_H: return nv <= 1 ? gemv_tiled_kernel<0, 1, IN_MOE_H> : nv <= 4 ? gemv_tiled_kernel<0, 4, IN_MOE_H>
+                                                                             : gemv_tiled_kernel<0, 8, IN_MOE_H>;
         case IN_F32: return pick_tiled_t<0, IN_F32>(nv);
         default: return pick_tiled_t<0, IN_Q8K>(nv);
         }
     }
     switch (mode) {
-    case IN_MOE_X: return gemv_tiled_kernel<1, 1, IN_MOE_X>;
-    case IN_MOE_H: return gemv_tiled_kernel<1, 1, IN_MOE_H>;
+    case IN_MOE_X: return nv <= 1 ? gemv_tiled_kernel<1, 1, IN_MOE_X> : nv <= 4 ? gemv_tiled_kernel<1, 4, IN_MOE_X>
+                                                                         : gemv_tiled_kernel<1, 8, IN_MOE_X>;
+    case IN_MOE_H: return nv <= 1 ? gemv_tiled_kernel<1, 1, IN_MOE_H> : nv <= 4 ? gemv_tiled_kernel<1, 4, IN_MOE_H>
+                                                                         : gemv_tiled_kernel<1, 8, IN_MOE_H>;
     case IN_F32: return pick_tiled_t<1, IN_F32>(nv);
     default: return pick_tiled_t<1, IN_Q8K>(nv);
     }
@@ -341,7 +345,9 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
         moe_nact = tpm ? (tpc + tpm - 2) / tpm + 1 : 1;
         if (moe_nact > max_slots) moe_nact = max_slots;
         if (moe_nact == 0) moe_nact = 1;
+        if (nv_inst > 1) moe_nact *= nv_inst;  // jobs: nv images per unit
     }
+    const uint32_t job_bytes = mode >= IN_MOE_X && nv_inst > 1 ? tiled_job_bytes(nv_inst) : 0u;
     // Fit the CTA in shared memory: fewer stages, then smaller stages, then
     // fewer warps per tile (less chain scratch).
     const size_t budget = warps == 16 ? 220 * 1024 : 110 * 1024;
@@ -352,7 +358,7 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
         p->nstages = ns;
         p->stage_bytes = p->bc * cb;
         p->smem = tiled_smem_bytes(warps, S, ns, p->stage_bytes, p->slot_blocks, nv_inst, nb,
-                                   tiled_nact(mode, nv_inst, moe_nact));
+                                   tiled_nact(mode, nv_inst, moe_nact), job_bytes);
         if (p->smem <= budget) break;
         if (ns > 2)
             ns--;
@@ -684,8 +690,15 @@ MoeScratch moe_scratch(const sg_moe *m) {
 // Scratch of the batched layer (moe_forward_batch) for n_tok tokens.
 struct MoeBatchScratch {
     uint64_t choices, slot_base, slots, n_slots, slots_sh, n_slots_sh, shsel, scale, logits, qx, h, y, hsh, ysh;
-    uint64_t slots_local, slot_global, n_local, ticket, total;
+    uint64_t slots_local, slot_global, n_local, ticket, jobs, n_jobs, total;
 };
+
+// Jobs of the batched layer (the slots of an expert grouped, up to job_max
+// per job): at most one per slot and at most n_slots / job_max + n_expert.
+uint64_t moe_max_jobs(uint64_t n_slots, uint64_t n_expert, uint64_t job_max) {
+    const uint64_t b = n_slots / job_max + n_expert;
+    return b < n_slots ? b : n_slots;
+}
 
 MoeBatchScratch moe_batch_scratch(const sg_moe *m, uint64_t n_tok) {
     MoeBatchScratch L;
@@ -715,6 +728,8 @@ MoeBatchScratch moe_batch_scratch(const sg_moe *m, uint64_t n_tok) {
     L.slot_global = take(slots * 4);
     L.n_local = take(4);
     L.ticket = take(4);  // the select kernel's last-CTA count (zeroed by the router kernel)
+    L.jobs = take(moe_max_jobs(slots, m->n_expert, 4) * MOE_JOB_INTS * 4);  // sized for the smallest jobs
+    L.n_jobs = take(4);
     L.total = off;
     return L;
 }
@@ -736,6 +751,11 @@ struct MoeSlots {
     const int32_t *slots;
     const uint32_t *n_slots;
     const uint8_t *qx_tokens;  // IN_MOE_X: the tokens' Q8_K images
+    // jobs mode (TGemvArgs::jobs): the select kernel's expert jobs, each unit
+    // job_nv vectors; max_slots then counts jobs
+    const int32_t *jobs;
+    const uint32_t *n_jobs;
+    uint32_t job_nv;
     // IN_MOE_H with expert parallelism: slot outputs to every rank (see TGemvArgs)
     uint32_t npeers;
     const uint32_t *slot_global;
@@ -751,8 +771,11 @@ sg_status launch_moe_group(int32_t dtype, int mode, const uint8_t *w, uint64_t m
                            const MoeSlots *slots = nullptr) {
     const int dt = dtype == SG_Q4_K ? DT_Q4K : DT_Q6K;
     const uint32_t nb = (uint32_t)(cols / 256), tiles = (uint32_t)((rows + TILE_ROWS - 1) / TILE_ROWS);
+    const bool jobs = slots && slots->jobs;
+    if (jobs && ((slots->job_nv != 4 && slots->job_nv != 8) || slots->job_nv + 2 > MOE_JOB_INTS || slots->npeers))
+        return SG_ERR_INVALID;
     TPlan p;
-    sg_status st = tiled_plan(dt, nb, max_slots * tiles, 1, mode, max_slots, &p);
+    sg_status st = tiled_plan(dt, nb, max_slots * tiles, jobs ? (int)slots->job_nv : 1, mode, max_slots, &p);
     if (st) return st;
     if (route && moe_select_bytes(n_expert) > p.warps * p.nstages * p.stage_bytes) return SG_ERR_SHAPE;
     TGemvArgs a;
@@ -790,7 +813,12 @@ sg_status launch_moe_group(int32_t dtype, int mode, const uint8_t *w, uint64_t m
     a.gu = h;
     a.gu_stride = h_stride;
     if (slots) {
-        if (p.nact > MOE_MAXK) return SG_ERR_SHAPE;
+        if (p.nact > MOE_MAXK * (jobs ? tiled_nv_inst((int)slots->job_nv) : 1u)) return SG_ERR_SHAPE;
+        if (jobs) {
+            a.jobs = slots->jobs;
+            a.n_jobs = slots->n_jobs;
+            a.job_ints = MOE_JOB_INTS;
+        }
         a.slots = slots->slots;
         a.n_slots = slots->n_slots;
         a.qx_tokens = slots->qx_tokens;
@@ -1463,6 +1491,12 @@ sg_status moe_batch_impl(const sg_moe *m, const sg_moe_ep *ep, const float *d_x,
     // (this rank's, with expert parallelism) -> down -> [shared gate/up, down
     // over one slot per token] -> combine
     unsigned *sel_ticket = (unsigned *)(sc + L.ticket);
+    // from this many tokens on, the expert passes run over jobs (each expert's
+    // weights decoded once for up to job_nv of its slots); SG_MOE_JOB_NV=0: per slot
+    const int job_nv = env_int("SG_MOE_JOB_NV", 4);
+    const bool use_jobs = !ep && (job_nv == 4 || job_nv == 8) && nt >= (uint32_t)env_int("SG_MOE_JOBS_MIN", 16);
+    int32_t *jobs = (int32_t *)(sc + L.jobs);
+    uint32_t *n_jobs = (uint32_t *)(sc + L.n_jobs);
     if ((st = launch_router(m, d_x, logits, qx, (sg_moe_choice *)(sc + L.shsel), scale, s, nt, ldx, sel_ticket)))
         return st;
     {
@@ -1471,13 +1505,15 @@ sg_status moe_batch_impl(const sg_moe *m, const sg_moe_ep *ep, const float *d_x,
         CK(cudaGetDevice(&dev));
         if (!(attr_done.load() >> dev & 1)) {
             CK(cudaFuncSetAttribute((const void *)moe_select_batch_kernel,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));  // + its static words
             attr_done.fetch_or(1ull << dev);
         }
         SelectBatchArgs sa = {logits, nt, ne, k, m->norm, m->moe_prune, choices, slot_base, slots, n_slots,
                               sh ? slots_sh : nullptr, sh ? n_slots_sh : nullptr,
                               ep ? slots_local : nullptr, slot_global, n_local,
-                              ep ? (uint32_t)ep->expert_lo : 0u, ep ? (uint32_t)ep->expert_hi : 0u, sel_ticket};
+                              ep ? (uint32_t)ep->expert_lo : 0u, ep ? (uint32_t)ep->expert_hi : 0u, sel_ticket,
+                              use_jobs ? jobs : nullptr, n_jobs, (uint32_t)job_nv,
+                              (uint32_t)moe_max_jobs((uint64_t)nt * k, ne, 4)};
         const uint32_t sel_grid = (nt + SELECT_BATCH_THREADS / 32 - 1) / (SELECT_BATCH_THREADS / 32);
         CK(launch_pdl((const void *)moe_select_batch_kernel, sel_grid, SELECT_BATCH_THREADS, select_batch_smem(nt), s,
                       &sa));
@@ -1497,11 +1533,18 @@ sg_status moe_batch_impl(const sg_moe *m, const sg_moe_ep *ep, const float *d_x,
         md.ep_half = ep->recv_slots * m->dim;
         md.epoch = ep_epoch;
     }
+    uint32_t units = nt * k;  // launch units: slots, or jobs
+    if (use_jobs) {
+        ms.jobs = md.jobs = jobs;
+        ms.n_jobs = md.n_jobs = n_jobs;
+        ms.job_nv = md.job_nv = (uint32_t)job_nv;
+        units = (uint32_t)moe_max_jobs((uint64_t)nt * k, ne, (uint64_t)job_nv);
+    }
     if (!ep || ne_run > 0) {
         if ((st = launch_moe_group(m->gate_up_dtype, IN_MOE_X, m->gate_up, m->gate_up_stride, 2 * m->n_ff, m->dim,
-                                   nt * k, ne_run ? ne_run : 1, nullptr, nullptr, nullptr, nullptr, nullptr, 0, h,
+                                   units, ne_run ? ne_run : 1, nullptr, nullptr, nullptr, nullptr, nullptr, 0, h,
                                    m->n_ff, s, &ms)) ||
-            (st = launch_moe_group(m->down_dtype, IN_MOE_H, m->down, m->down_stride, m->dim, m->n_ff, nt * k,
+            (st = launch_moe_group(m->down_dtype, IN_MOE_H, m->down, m->down_stride, m->dim, m->n_ff, units,
                                    ne_run ? ne_run : 1, nullptr, nullptr, nullptr, nullptr, h, m->n_ff, y, m->dim, s,
                                    &md)))
             return st;

@@ -52,18 +52,22 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     // and does nothing (uniform exit, before any barrier).
     const uint32_t nwarps = blockDim.x >> 5;
     const uint32_t nact = tiled_nact(MODE, NV, a.nact);
-    if (tiled_smem_bytes(nwarps, a.S, a.nstages, a.stage_bytes, a.slot_blocks, NV, a.nb, nact) >
+    const bool JOBS = MOE && a.jobs != nullptr;
+    const uint32_t job_bytes = JOBS ? tiled_job_bytes(NV) : 0u;
+    if (tiled_smem_bytes(nwarps, a.S, a.nstages, a.stage_bytes, a.slot_blocks, NV, a.nb, nact, job_bytes) >
             dynamic_smem_size() ||
         a.bc == 0 || a.stage_bytes < a.bc * CB || a.S == 0 || a.S != (1u << a.s_log2) || a.S > nwarps ||
         (nwarps & (a.S - 1)) || (blockDim.x & 31) ||
         a.nstages * nwarps * 8 > ((MOE || a.qx_image) ? MOE_QX_BAR_OFF : TGEMV_BAR_BYTES) ||
         (MODE == IN_Q8K && a.qx_image && a.nvec != 1) ||
-        (MOE && a.swiglu && (MODE != IN_MOE_X || a.nvec != 1)) ||
+        (MOE && a.swiglu && (MODE != IN_MOE_X || (a.nvec != 1 && !JOBS))) ||
+        (MOE && !JOBS && NV != 1) ||
+        (JOBS && (!a.slots || !a.n_jobs || a.npeers || a.job_ints < 2 + NV || nact % NV || nact > MOE_MAXK * NV)) ||
         (MOE && ((!a.slots && a.max_slots > MOE_MAXK) || a.tiles_per_mat == 0 || nact == 0 ||
                  (uint64_t)a.ntiles * gridDim.x >= (1ull << 32) || a.ntiles < a.max_slots * a.tiles_per_mat)) ||
         (a.npeers && !MOE && (a.npeers > TP_MAX_RANKS || !a.ticket || !a.epoch || !a.out[0] || !a.my_recv)) ||
         (a.npeers && MOE && (MODE != IN_MOE_H || a.npeers > TP_MAX_RANKS || !a.slots || !a.slot_global || !a.epoch)) ||
-        (a.slots && (!MOE || !a.n_slots || a.logits || nact > MOE_MAXK || (MODE == IN_MOE_X && !a.qx_tokens))) ||
+        (a.slots && (!MOE || !a.n_slots || a.logits || (!JOBS && nact > MOE_MAXK) || (MODE == IN_MOE_X && !a.qx_tokens))) ||
         (MODE == IN_MOE_X && a.logits &&
          (a.n_expert == 0 || a.n_used == 0 || a.n_used > a.n_expert || a.n_used > MOE_MAXK ||
           moe_select_bytes(a.n_expert) > nwarps * a.nstages * a.stage_bytes))) {
@@ -78,7 +82,9 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     const uint32_t astride = act_bytes(a.nb);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * a.nstages;
     uint8_t *act = smem + TGEMV_BAR_BYTES;
-    uint8_t *rings = act + nact * astride;
+    // jobs mode: local job j's slot count at jinfo[j], its slots at jinfo[MOE_MAXK + j * NV ..]
+    uint32_t *jinfo = reinterpret_cast<uint32_t *>(act + nact * astride);
+    uint8_t *rings = act + nact * astride + job_bytes;
     uint8_t *ring = rings + warp * a.nstages * a.stage_bytes;
     const uint32_t worker_floats = a.slot_blocks * NV * CHAIN_FLOATS;
     float *gscratch = reinterpret_cast<float *>(rings + nwarps * a.nstages * a.stage_bytes) +
@@ -100,8 +106,8 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
             bulk_g2s(act, a.qx_image, act_bytes(a.nb), qbar);
         }
         if (a.slots) {
-            // batched: the slot table was written by the kernel before
-            if (threadIdx.x == 0) msel[0] = min(__ldcg(a.n_slots), a.max_slots);
+            // batched: the slot table (and the jobs) were written by the kernel before
+            if (threadIdx.x == 0) msel[0] = min(__ldcg(JOBS ? a.n_jobs : a.n_slots), a.max_slots);
         } else if (MODE == IN_MOE_X && a.logits) {
             // every CTA makes the router's choice itself (identical results);
             // the rings are free until the first weight copy is issued
@@ -163,6 +169,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     // SMs.  MoE: each CTA takes a contiguous range, so that it needs the
     // activations of one or two slots only (slots s_lo..s_hi).
     uint32_t first, step, my_tiles, s_lo = 0, s_hi = 0;
+    uint32_t cta_units = 0;  // MoE: units s_lo..s_hi of this CTA (0: none), the same in every warp
     if constexpr (MOE) {
         // 32-bit products: the entry check bounds ntiles * gridDim.x below 2^32
         const uint32_t lo = ntiles * blockIdx.x / gridDim.x, hi = ntiles * (blockIdx.x + 1) / gridDim.x;
@@ -172,18 +179,37 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
         if (lo < hi) {
             s_lo = lo / a.tiles_per_mat;
             s_hi = (hi - 1) / a.tiles_per_mat;
+            cta_units = s_hi - s_lo + 1;
         }
-        if ((MODE == IN_MOE_H || a.slots) && lo < hi && s_hi - s_lo + 1 > nact) {  // the host sized nact for this
-            if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+        // activation images per unit: one per slot, NV per job (jobs mode)
+        if ((MODE == IN_MOE_H || a.slots) && cta_units * (JOBS ? NV : 1) > nact) {
+            if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);  // the host sized nact for this
             my_tiles = 0;
             s_hi = s_lo;
+            cta_units = 0;
         }
         if (a.slots) {
-            // this CTA's slots s_lo..s_hi: expert ids into msel[16..], and for
+            // this CTA's units s_lo..s_hi: expert ids into msel[16..], and for
             // IN_MOE_X each slot's token image into activation image s - s_lo
-            const uint32_t nloc = my_tiles ? s_hi - s_lo + 1 : 0u;
+            // (jobs: image (s - s_lo) * NV + member)
+            const uint32_t nloc = cta_units;
             bool bad = false;
-            if (threadIdx.x < nloc) {
+            if (JOBS) {
+                if (threadIdx.x < nloc) {
+                    const int32_t *jb = a.jobs + (uint64_t)(s_lo + threadIdx.x) * a.job_ints;
+                    const int32_t e = __ldcg(jb), n = __ldcg(jb + 1);
+                    const uint32_t ns = __ldcg(a.n_slots);
+                    bad = e < 0 || (uint32_t)e >= a.n_expert || n < 1 || n > NV;
+                    for (int v = 0; v < NV; v++) {
+                        const int32_t sl = v < n ? __ldcg(jb + 2 + v) : 0;
+                        bad = bad || sl < 0 || (uint32_t)sl >= ns;
+                        jinfo[MOE_MAXK + threadIdx.x * NV + v] = (uint32_t)sl;
+                    }
+                    msel[16 + threadIdx.x] = bad ? 0u : (uint32_t)e;
+                    jinfo[threadIdx.x] = bad ? 0u : (uint32_t)n;
+                }
+                __syncthreads();
+            } else if (threadIdx.x < nloc) {
                 const int32_t e = __ldcg(a.slots + 2 * (s_lo + threadIdx.x));
                 bad = e < 0 || (uint32_t)e >= a.n_expert;
                 msel[16 + threadIdx.x] = bad ? 0u : (uint32_t)e;
@@ -192,15 +218,26 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                 uint64_t *qbar = reinterpret_cast<uint64_t *>(smem + MOE_QX_BAR_OFF);
                 mbar_init(qbar, 1);
                 fence_mbar_init();
-                mbar_arrive_expect_tx(qbar, nloc * act_bytes(a.nb));
+                uint32_t nimg = nloc;
+                if (JOBS) {
+                    nimg = 0;
+                    for (uint32_t j = 0; j < nloc; j++) nimg += jinfo[j];
+                }
+                mbar_arrive_expect_tx(qbar, nimg * act_bytes(a.nb));
                 for (uint32_t j = 0; j < nloc; j++) {
-                    const int32_t tok = __ldcg(a.slots + 2 * (s_lo + j) + 1);
-                    bulk_g2s(act + j * astride, a.qx_tokens + (uint64_t)tok * astride, act_bytes(a.nb), qbar);
+                    const uint32_t nm = JOBS ? jinfo[j] : 1u;
+                    for (uint32_t v = 0; v < nm; v++) {
+                        const uint32_t sl = JOBS ? jinfo[MOE_MAXK + j * NV + v] : s_lo + j;
+                        const int32_t tok = __ldcg(a.slots + 2 * sl + 1);
+                        bulk_g2s(act + (j * (JOBS ? NV : 1u) + v) * astride, a.qx_tokens + (uint64_t)tok * astride,
+                                 act_bytes(a.nb), qbar);
+                    }
                 }
             }
             if (__syncthreads_or(bad)) {
                 if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
                 my_tiles = 0;
+                cta_units = 0;
             }
         }
     } else {
@@ -254,9 +291,12 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
     if constexpr (MODE == IN_MOE_H) {
         // one warp per (slot, 256-block) of this CTA's slots: the exact Q8_K
         // quantization of h
-        for (uint32_t wb = warp; wb < (s_hi - s_lo + 1) * nb; wb += nwarps) {
-            const uint32_t s = s_lo + wb / nb, b = wb % nb;
-            uint8_t *av = act + (wb / nb) * astride;
+        const uint32_t upj = JOBS ? NV : 1u, nimg = cta_units * upj;
+        for (uint32_t wb = warp; wb < nimg * nb; wb += nwarps) {
+            const uint32_t q = wb / nb, b = wb % nb, j = q / upj, v = q - j * upj;
+            if (JOBS && v >= jinfo[j]) continue;
+            const uint32_t s = JOBS ? jinfo[MOE_MAXK + j * NV + v] : s_lo + q;
+            uint8_t *av = act + q * astride;
             q8k_block(a.gu + s * a.gu_stride + 256u * b, reinterpret_cast<int8_t *>(av + 256u * b),
                       reinterpret_cast<int16_t *>(av + 256u * nb + 32u * b),
                       reinterpret_cast<float *>(av + 288u * nb + 4u * b), lane);
@@ -341,7 +381,9 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
             ms = tt / a.tiles_per_mat;
             mt = tt - ms * a.tiles_per_mat;
         }
-        const uint8_t *tact = (MODE == IN_MOE_H || (MODE == IN_MOE_X && a.slots)) ? act + (ms - s_lo) * astride : act;
+        const uint8_t *tact =
+            (MODE == IN_MOE_H || (MODE == IN_MOE_X && a.slots)) ? act + (ms - s_lo) * (JOBS ? NV : 1u) * astride : act;
+        const uint32_t nvu = JOBS ? jinfo[ms - s_lo] : a.nvec;  // this unit's vectors
         float acc[NV][4], corr[NV];
 #pragma unroll
         for (int v = 0; v < NV; v++) {
@@ -397,7 +439,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                     q4k_weights(col, g, r, wt);
 #pragma unroll
                     for (int v = 0; v < NV; v++) {
-                        if (v >= (int)a.nvec) break;
+                        if (v >= (int)nvu) break;
                         int s[4];
                         float cd, ct;
                         q4k_dot(wt, g, i, a.nb, tact + v * astride, s, cd, ct);
@@ -408,7 +450,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                     q6k_weights(col, g, r, wt);
 #pragma unroll
                     for (int v = 0; v < NV; v++) {
-                        if (v >= (int)a.nvec) break;
+                        if (v >= (int)nvu) break;
                         int s[4];
                         float cd, ct;
                         q6k_dot(wt, g, i, a.nb, tact + v * astride, s, cd, ct);
@@ -434,7 +476,7 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                     for (uint32_t q = 0; q < n_ws; q++)
 #pragma unroll
                         for (int v = 0; v < NV; v++) {
-                            if (v >= (int)a.nvec) break;
+                            if (v >= (int)nvu) break;
                             const float *e = src + (q * NV + v) * CHAIN_FLOATS;
                             const float4 f = *reinterpret_cast<const float4 *>(e + 64 * g + 4 * r);
                             const float c = e[128 + r];
@@ -457,7 +499,8 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
 #pragma unroll
                 for (int m = 0; m < 4; m++) x[m] = __fadd_rn(acc[v][m], __shfl_down_sync(0xffffffffu, acc[v][m], 16));
                 const float yv = __fsub_rn(__fadd_rn(__fadd_rn(x[0], x[2]), __fadd_rn(x[1], x[3])), corr[v]);
-                float *dst = MOE ? a.out[0] + ms * a.out_stride : a.out[v];
+                float *dst = MOE ? a.out[0] + (JOBS ? jinfo[MOE_MAXK + (ms - s_lo) * NV + v] : ms) * a.out_stride
+                                 : a.out[v];
                 if (MODE == IN_MOE_H && a.npeers) {
                     // this rank's expert output goes to every rank's receive buffer (NVLink peer stores)
                     if (g == 0 && row >= a.r0 && row < a.r1) {
@@ -473,8 +516,8 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
                     // same outputs: h = silu(gate) * up (smollm_chat.rs:357-359)
                     const float up = __shfl_down_sync(0xffffffffu, yv, 8);
                     const uint32_t j = mt * 8 + r;
-                    if (g == 0 && r < 8 && 2 * j < a.r1) dst[j] = silu_mul(yv, up);
-                } else if (g == 0 && v < (int)a.nvec && row >= a.r0 && row < a.r1) {
+                    if (g == 0 && r < 8 && 2 * j < a.r1 && v < (int)nvu) dst[j] = silu_mul(yv, up);
+                } else if (g == 0 && v < (int)nvu && row >= a.r0 && row < a.r1) {
                     if (!MOE && a.npeers) {
                         // the row shard goes straight into every rank's receive buffer (NVLink peer stores)
                         const uint64_t o = (uint64_t)(tp_e & 1u) * a.nvec * a.tp_rows +
@@ -501,7 +544,11 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
 #define SG_TINST(DT)                                                                                        \
     SG_TINST1(DT, 1) SG_TINST1(DT, 2) SG_TINST1(DT, 4) SG_TINST1(DT, 8)                                     \
     template __global__ void gemv_tiled_kernel<DT, 1, IN_MOE_X>(const __grid_constant__ TGemvArgs); \
-    template __global__ void gemv_tiled_kernel<DT, 1, IN_MOE_H>(const __grid_constant__ TGemvArgs);
+    template __global__ void gemv_tiled_kernel<DT, 1, IN_MOE_H>(const __grid_constant__ TGemvArgs); \
+    template __global__ void gemv_tiled_kernel<DT, 4, IN_MOE_X>(const __grid_constant__ TGemvArgs); \
+    template __global__ void gemv_tiled_kernel<DT, 4, IN_MOE_H>(const __grid_constant__ TGemvArgs); \
+    template __global__ void gemv_tiled_kernel<DT, 8, IN_MOE_X>(const __grid_constant__ TGemvArgs); \
+    template __global__ void gemv_tiled_kernel<DT, 8, IN_MOE_H>(const __grid_constant__ TGemvArgs);
 SG_TINST(0)
 SG_TINST(1)
 

@@ -125,6 +125,15 @@ struct TGemvArgs {
     const unsigned long long *my_recv;  // this rank's receive buffer
     unsigned *ticket;
     unsigned *epoch;
+    // Jobs mode (MoE with a slot table, NV > 1): the launch's units are jobs
+    // of the select kernel's table (SelectBatchArgs::jobs: {expert, n,
+    // slot_0 ..}, MOE_JOB_INTS ints each, *n_jobs of them, at most
+    // max_slots): every weight block of a job's expert is decoded once for
+    // its n slots; slot s's vector is its token's image (IN_MOE_X) or h at
+    // gu + s * gu_stride (IN_MOE_H), its rows go to out[0] + s * out_stride.
+    const int32_t *jobs;
+    const uint32_t *n_jobs;
+    uint32_t job_ints;
 };
 
 // In the MoE modes the choice is kept at the top of the barrier area: n at
@@ -155,11 +164,15 @@ __host__ __device__ inline uint32_t ilog2u(uint32_t v) {
 // (S a power of two, as the kernel requires)
 __host__ __device__ inline uint32_t tiled_smem_bytes(uint32_t warps, uint32_t S, uint32_t nstages,
                                                      uint32_t stage_bytes, uint32_t slot_blocks, uint32_t nv,
-                                                     uint32_t nb, uint32_t nact) {
+                                                     uint32_t nb, uint32_t nact, uint32_t job_bytes = 0) {
     const uint32_t groups = S ? warps >> ilog2u(S) : 0u;
-    return TGEMV_BAR_BYTES + nact * act_bytes(nb) + warps * nstages * stage_bytes +
+    return TGEMV_BAR_BYTES + nact * act_bytes(nb) + job_bytes + warps * nstages * stage_bytes +
            groups * (S - 1) * slot_blocks * nv * CHAIN_FLOATS * 4u;
 }
+
+// Jobs mode (TGemvArgs::jobs): per local job its slot count and NV slot
+// indices, after the activation images (MOE_MAXK local jobs at most).
+__host__ __device__ constexpr uint32_t tiled_job_bytes(uint32_t nv) { return MOE_MAXK * (1u + nv) * 4u; }
 
 template <int DT, int NV, int MODE>
 __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const __grid_constant__ TGemvArgs a);

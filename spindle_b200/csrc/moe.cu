@@ -200,16 +200,25 @@ __global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(
     if (!__syncthreads_or(last)) return;
     __threadfence();
     const sg_moe_choice *chs = a.choices;
-    // slot bases (a prefix sum over the tokens), then every warp writes its
-    // tokens' slots
-    if (tid == 0) {
-        uint32_t base = 0;
-        for (uint32_t u = 0; u < a.n_tok; u++) {
-            bases[u] = base;
-            base += min((uint32_t)__ldcg(&chs[u].n), a.n_used);
+    // slot bases: an exclusive prefix sum over the tokens' slot counts (one
+    // token per thread, n_tok <= SG_MOE_MAX_BATCH = SELECT_BATCH_THREADS),
+    // then every warp writes its tokens' slots
+    {
+        __shared__ uint32_t wsum[SELECT_BATCH_THREADS / 32];
+        const uint32_t c = tid < a.n_tok ? min((uint32_t)__ldcg(&chs[tid].n), a.n_used) : 0u;
+        uint32_t incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= (uint32_t)o) incl += t;
         }
-        bases[a.n_tok] = base;
-        *a.ticket = 0;  // for the next launch
+        if (lane == 31) wsum[warp] = incl;
+        __syncthreads();
+        uint32_t before = 0;
+        for (uint32_t w = 0; w < warp; w++) before += wsum[w];
+        if (tid < a.n_tok) bases[tid] = before + incl - c;
+        if (tid == SELECT_BATCH_THREADS - 1) bases[a.n_tok] = before + incl;
+        if (tid == 0) *a.ticket = 0;  // for the next launch
     }
     __syncthreads();
     for (uint32_t u = warp; u < a.n_tok; u += nwarps) {
@@ -245,6 +254,57 @@ __global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(
                 a.slots_sh[2 * u + 1] = (int32_t)u;
             }
             *a.n_slots_sh = a.n_tok;
+        }
+    }
+    if (!a.jobs) return;
+    const uint32_t jm = a.job_max < 1 ? 1u : a.job_max > MOE_JOB_MAX ? MOE_JOB_MAX : a.job_max;
+    // jobs: the slots of each expert (in any order: each slot's result does not
+    // depend on its job) in groups of at most MOE_JOB_MAX, experts in order
+    uint32_t *cnt = bases + a.n_tok + 1, *jbase = cnt + 256, *rank = jbase + 256;
+    for (uint32_t e = tid; e < 256; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (uint32_t u = warp; u < a.n_tok; u += nwarps) {
+        const uint32_t n = min((uint32_t)__ldcg(&chs[u].n), a.n_used), base = bases[u];
+        if (lane < n) rank[base + lane] = atomicAdd(&cnt[__ldcg(&chs[u].id[lane])], 1u);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // exclusive scan of the experts' job counts, 8 experts per lane
+        uint32_t nj[8], tot = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            nj[i] = (cnt[8 * lane + i] + jm - 1) / jm;
+            tot += nj[i];
+        }
+        uint32_t incl = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= (uint32_t)o) incl += t;
+        }
+        uint32_t b = incl - tot;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            jbase[8 * lane + i] = b;
+            b += nj[i];
+        }
+        if (lane == 31) {
+            *a.n_jobs = incl <= a.jobs_cap ? incl : 0u;
+            if (incl > a.jobs_cap) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+        }
+    }
+    __syncthreads();
+    for (uint32_t u = warp; u < a.n_tok; u += nwarps) {
+        const uint32_t n = min((uint32_t)__ldcg(&chs[u].n), a.n_used), base = bases[u];
+        if (lane < n) {
+            const uint32_t e = (uint32_t)__ldcg(&chs[u].id[lane]), r = rank[base + lane];
+            if (jbase[e] + r / jm >= a.jobs_cap) continue;  // over capacity: recorded above, no jobs run
+            int32_t *job = a.jobs + (uint64_t)(jbase[e] + r / jm) * MOE_JOB_INTS;
+            job[2 + r % jm] = (int32_t)(base + lane);
+            if (r % jm == 0) {
+                job[0] = (int32_t)e;
+                job[1] = (int32_t)min(jm, cnt[e] - r);
+            }
         }
     }
 }

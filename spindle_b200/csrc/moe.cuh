@@ -62,10 +62,23 @@ struct SelectBatchArgs {
     uint32_t *n_local;
     uint32_t ep_lo, ep_hi;
     unsigned *ticket;           // 0 at launch (the router kernel zeroes it); back to 0 after
+    // optional: the slots grouped by expert into jobs of at most job_max
+    // slots (moe_batch_fused's union jobs, smollm_chat.rs:1040-1120): job j
+    // is jobs[j * MOE_JOB_INTS ..] = {expert, n, slot_0 .. slot_{n-1}}, the
+    // jobs of an expert consecutive, *n_jobs of them
+    int32_t *jobs;
+    uint32_t *n_jobs;
+    uint32_t job_max;           // slots per job, 1 .. MOE_JOB_MAX
+    uint32_t jobs_cap;          // jobs the table holds
 };
+constexpr uint32_t MOE_JOB_MAX = 8;
+constexpr uint32_t MOE_JOB_INTS = 2 + MOE_JOB_MAX;
 constexpr uint32_t SELECT_BATCH_THREADS = 128;  // one warp per token, ceil(n_tok / 4) CTAs
+// per warp: 256 floats and a Choice; then the token bases (n_tok + 1), and the
+// job build's per-expert counts and job bases (256 each) and per-slot ranks
 __host__ __device__ inline uint32_t select_batch_smem(uint32_t n_tok) {
-    return (SELECT_BATCH_THREADS / 32) * (256u * 4u + (uint32_t)sizeof(moe::Choice)) + (n_tok + 1u) * 4u;
+    return (SELECT_BATCH_THREADS / 32) * (256u * 4u + (uint32_t)sizeof(moe::Choice)) + (n_tok + 1u) * 4u +
+           2u * 256u * 4u + n_tok * MOE_MAXK * 4u;
 }
 
 struct CombineBatchArgs {

@@ -47,6 +47,22 @@ def test_moe_batch_small(dev, n_tok):
     run_batch(L, xs, dev, norm=False)
 
 
+@pytest.mark.parametrize("job_nv", ["0", "4", "8"])
+def test_moe_batch_expert_jobs(dev, monkeypatch, job_nv):
+    # the expert passes over jobs (each expert's blocks decoded once for up to
+    # 4 or 8 of its slots, moe_batch_fused's union jobs) from one token on, and
+    # per slot (0): every token still bit for bit the one-token step
+    monkeypatch.setenv("SG_MOE_JOB_NV", job_nv)
+    monkeypatch.setenv("SG_MOE_JOBS_MIN", "1")
+    L = make_layer(9, 512, 256, 16, 4)
+    for n_tok in (1, 3, 40):
+        xs = np.stack([O.Rng(200 + t).fill(-1.0, 1.0, 512) for t in range(n_tok)])
+        run_batch(L, xs, dev)
+    L = make_layer(31, 2048, 768, 128, 8)
+    xs = np.stack([O.Rng(400 + t).fill(-1.0, 1.0, 2048) for t in range(33)])
+    run_batch(L, xs, dev, prune=4.0)
+
+
 def test_moe_batch_qwen3_verify(dev):
     # the Qwen3-30B-A3B layer at the verify batch of config 5 (N = 9), and 64 tokens
     L = make_layer(30, 2048, 768, 128, 8)
