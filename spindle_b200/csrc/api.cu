@@ -525,16 +525,7 @@ sg_status launch_gemm_batch(const uint8_t *w, int dt, uint32_t nb, uint64_t r0, 
     const int tc = env_int("SG_GEMM_TC", 1);
     if ((dt == DT_Q4K && tc >= 1) || (dt == DT_Q6K && tc >= 2))
         return launch_gemm_tc(w, dt, nb, r0, r1, qb, ntok, out, ldo, swiglu, s);
-    if (ntok > GB_MAX_TOK) {
-        // the dp4a kernel takes one QB group (64 vectors) per launch
-        for (uint32_t q = 0; q * QB_GROUP < ntok; q++) {
-            const sg_status st = launch_gemm_batch(w, dt, nb, r0, r1, qb + qb_group_offset(q, nb),
-                                                   qb_group_tokens(ntok, q), out + (uint64_t)q * QB_GROUP * ldo, ldo,
-                                                   swiglu, s);
-            if (st) return st;
-        }
-        return SG_OK;
-    }
+
     static std::atomic<uint64_t> attr_done{0};
     int dev;
     CK(cudaGetDevice(&dev));
@@ -559,11 +550,13 @@ sg_status launch_gemm_batch(const uint8_t *w, int dt, uint32_t nb, uint64_t r0, 
     a.r1 = (uint32_t)r1;
     a.qb = qb;
     a.ntok = ntok;
+    // the kernel takes one QB group (64 vectors) per CTA row (blockIdx.y): planned for the largest
+    const uint32_t gtok = ntok < GB_MAX_TOK ? ntok : GB_MAX_TOK, ngroups = (ntok + QB_GROUP - 1) / QB_GROUP;
     a.nq = 1;
-    while (a.nq * (uint32_t)tpw < ntok) a.nq *= 2;
+    while (a.nq * (uint32_t)tpw < gtok) a.nq *= 2;
     a.tps = cons / a.nq;
     const uint32_t cb = tiled_col_bytes(dt);
-    a.stage_bytes = a.tps * cb + qb_block_bytes(ntok);
+    a.stage_bytes = a.tps * cb + qb_block_bytes(gtok);
     const uint32_t budget = 220u * 1024u - GB_BAR_BYTES;
     a.nstages = budget / a.stage_bytes;
     if (a.nstages > GB_MAX_STAGES) a.nstages = GB_MAX_STAGES;
@@ -575,7 +568,7 @@ sg_status launch_gemm_batch(const uint8_t *w, int dt, uint32_t nb, uint64_t r0, 
     const uint32_t grid = nsteps < (uint32_t)di->sms ? nsteps : (uint32_t)di->sms;
     const void *fn = tpw == 4 ? (dt == DT_Q4K ? (const void *)gemm_batch_kernel<0, 4> : (const void *)gemm_batch_kernel<1, 4>)
                               : (dt == DT_Q4K ? (const void *)gemm_batch_kernel<0, 8> : (const void *)gemm_batch_kernel<1, 8>);
-    CK(launch_pdl(fn, dim3(grid), cons * 32, GB_BAR_BYTES + a.nstages * a.stage_bytes, s, &a));
+    CK(launch_pdl(fn, dim3(grid, ngroups), cons * 32, GB_BAR_BYTES + a.nstages * a.stage_bytes, s, &a));
     return SG_OK;
 }
 
@@ -1869,7 +1862,9 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
         if (!(attr_done.load() >> dev & 1)) {
             for (const void *fn : {(const void *)attention_kernel<64, 64>, (const void *)attention_kernel<128, 64>,
                                    (const void *)attention_kernel<256, 64>, (const void *)attention_kernel<64, 128>,
-                                   (const void *)attention_kernel<128, 128>, (const void *)attention_kernel<256, 128>})
+                                   (const void *)attention_kernel<128, 128>, (const void *)attention_kernel<256, 128>,
+                                   (const void *)attention_batch_kernel<64>, (const void *)attention_batch_kernel<128>,
+                                   (const void *)attention_batch_kernel<256>})
                 CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
             attr_done.fetch_or(1ull << dev);
         }
@@ -1890,6 +1885,13 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
     DevInfo *attn_di;
     if ((st = dev_info(&attn_di))) return st;
     const uint32_t attn_chunk = (uint64_t)nt * m->n_heads >= 8ull * (uint64_t)attn_di->sms ? 64u : 128u;
+    // from SG_ATTN_BATCH_MIN tokens on (default 16), the attention with shared K/V rows
+    const uint32_t grp = m->n_kv_heads ? m->n_heads / m->n_kv_heads : 0u;
+    const bool attn_shared = nt >= (uint32_t)env_int("SG_ATTN_BATCH_MIN", 16) && grp && ATTN_PAIRS % grp == 0 &&
+                             m->n_heads % m->n_kv_heads == 0 && (hd == 64 || hd == 128 || hd == 256);
+    const void *attn_batch_fn = hd == 64    ? (const void *)attention_batch_kernel<64>
+                                : hd == 128 ? (const void *)attention_batch_kernel<128>
+                                            : (const void *)attention_batch_kernel<256>;
     const void *attn_fn = attn_chunk == 64
                               ? (hd == 64    ? (const void *)attention_kernel<64, 64>
                                  : hd == 128 ? (const void *)attention_kernel<128, 64>
@@ -1937,9 +1939,16 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
         CK(launch_pdl((const void *)rope_kv_batch_kernel, dim3(m->n_heads + m->n_kv_heads, nt), 32, 0, s, &ra));
         AttnArgs aa = {qkv, nullptr, nullptr, nullptr, nullptr, m->rms_eps, freqs, hd, m->n_heads, m->n_kv_heads,
                        m->max_seq, m->rope_neox, scale, d_pos, kc + l * cache, vc + l * cache, att, 1, qkv_stride,
-                       2, attn_chunk};  // two buffers: many CTAs, two or more of them per SM
-        CK(launch_pdl(attn_fn, dim3(m->n_heads, nt), attn_threads(hd), attn_smem_bytes(hd, m->max_seq, 2, attn_chunk),
-                      s, &aa));
+                       2, attn_chunk, nt};  // two buffers: many CTAs, two or more of them per SM
+        if (attn_shared) {
+            // one CTA per (KV head, block of tokens): each K/V row staged once for the block's pairs
+            const uint32_t tb = ATTN_PAIRS / (m->n_heads / m->n_kv_heads);
+            CK(launch_pdl(attn_batch_fn, dim3(m->n_kv_heads, (nt + tb - 1) / tb), attn_batch_threads(hd),
+                          attn_batch_smem(hd), s, &aa));
+        } else {
+            CK(launch_pdl(attn_fn, dim3(m->n_heads, nt), attn_threads(hd),
+                          attn_smem_bytes(hd, m->max_seq, 2, attn_chunk), s, &aa));
+        }
         if (batch_gemm && (st = launch_q8k_batch(att, q_dim, nt, q_dim / 256, qb, s))) return st;
         if ((st = gemv(y.wo, y.wo_dtype, dim, q_dim, att, oo))) return st;
         if ((st = launch_norm(x, proj, m->residual_scale, y.ffn_norm, m->rms_eps, dim, xn, qx, s, nt))) return st;

@@ -418,6 +418,211 @@ template __global__ void attention_kernel<64, 128>(const __grid_constant__ AttnA
 template __global__ void attention_kernel<128, 128>(const __grid_constant__ AttnArgs);
 template __global__ void attention_kernel<256, 128>(const __grid_constant__ AttnArgs);
 
+// compute_head_fn (smollm_chat.rs:3463-3495) for a batch of positions in the
+// prepared form (q normed and rotated, the batch's K/V rows in the caches),
+// with the rows shared: CTA (g, b) takes KV head g's group of H = n_heads /
+// n_kv query heads for the TB = ATTN_PAIRS / H tokens b * TB .. of the batch,
+// pair p = (head g * H + p / TB, token b * TB + p % TB), and walks the
+// positions in chunks of CH = ATTN_BCH whose K and V rows are copied into
+// shared memory once for all pairs (the next chunk in flight meanwhile).  Per
+// chunk, every pair's result is attention_kernel's, operation for operation:
+//   scores: thread (pair, 2 positions): the 8 AVX lanes of dot_f16_row
+//     (lane l: fma over dims l, l + 8, ... in order), the lane tree
+//     ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7)), + 0.0, * scale;
+//   running maxima (f32::max, NaN ignored) by a warp scan per pair, carried
+//     across chunks; alpha_t = exp(m_{t-1} - m_t), p_t = exp(s_t - m_t);
+//   l_t = l_{t-1} * alpha_t + p_t (one thread per pair) and
+//     acc_t[d] = fma(p_t, v_t[d], acc_{t-1}[d] * alpha_t) (thread: 4 pairs x
+//     2 dims), position by position;
+// then out = acc * (1 / max(l, 1e-9)).  A pair stops at its token's position.
+template <int HD>
+__global__ void __launch_bounds__(2 * HD, HD < 256 ? 2 : 1) attention_batch_kernel(const __grid_constant__ AttnArgs a) {
+    constexpr uint32_t P = ATTN_PAIRS, CH = ATTN_BCH, ND = HD / 2, QS = HD + 4, SEG = HD * 2 / 16;
+    static_assert(P * CH / 2 == 2 * HD || HD != 128, "one score task per thread at head_dim 128");
+    extern __shared__ __align__(16) uint8_t sm8[];
+    float *qf = reinterpret_cast<float *>(sm8);                      // [P][QS]
+    uint16_t *kh = reinterpret_cast<uint16_t *>(qf + P * QS);        // [2][CH][HD]
+    uint16_t *vh = kh + 2 * CH * HD;                                 // [2][CH][HD]
+    float *kf = reinterpret_cast<float *>(vh + 2 * CH * HD);         // [CH][HD]
+    float *vf = kf + CH * HD;                                        // [CH][HD]
+    float *sc = vf + CH * HD;                                        // [P][CH]
+    float2 *pa = reinterpret_cast<float2 *>(sc + P * CH);            // [P][CH]: (p_t, alpha_t)
+    float *lsum = reinterpret_cast<float *>(pa + P * CH), *mrun = lsum + P;
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    const uint32_t H = a.n_kv ? a.n_heads / a.n_kv : 0u, TB = H ? P / H : 0u, g = blockIdx.x;
+    if (a.head_dim != HD || blockDim.x != 2 * HD || H == 0 || a.n_heads % a.n_kv || P % H ||
+        gridDim.x != a.n_kv || gridDim.y * TB < a.ntok || attn_batch_smem(HD) > dynamic_smem_size()) {
+        grid_dependency_wait();
+        if (tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+        return;
+    }
+    grid_dependency_wait();  // q and the batch's K/V rows come from the kernel before
+    const uint32_t pos0 = (uint32_t)a.state[0], t0 = blockIdx.y * TB;
+    const uint32_t tend = t0 + TB < a.ntok ? t0 + TB : a.ntok;
+    const uint32_t T = pos0 + tend;  // positions [0, T): the block's last token is at T - 1
+    if (t0 >= a.ntok || T > a.max_seq) {
+        if (t0 < a.ntok && tid == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
+        grid_launch_dependents();
+        return;
+    }
+    for (uint32_t i = tid; i < P * HD; i += blockDim.x) {
+        const uint32_t p = i / HD, d = i - p * HD, t = t0 + p % TB;
+        qf[p * QS + d] = t < tend ? a.q[(uint64_t)t * a.q_stride + (g * H + p / TB) * HD + d] : 0.0f;
+    }
+    for (uint32_t p = tid; p < P; p += blockDim.x) {
+        lsum[p] = 0.0f;
+        mrun[p] = -INFINITY;
+    }
+    const uint32_t kv_dim = a.n_kv * HD, nc = (T + CH - 1) / CH;
+    const uint16_t *kg = a.kc + g * HD, *vg = a.vc + g * HD;
+    auto issue = [&](uint32_t c) {  // chunk c's K and V rows into buffer c & 1 (one commit group, maybe empty)
+        if (c < nc) {
+            const uint32_t c0 = c * CH, n = T - c0 < CH ? T - c0 : CH, b = c & 1u;
+            for (uint32_t u = tid; u < 2 * n * SEG; u += blockDim.x) {
+                const uint32_t w = u / (n * SEG), rs = u - w * n * SEG, r = rs / SEG, sg = rs - r * SEG;
+                const uint16_t *src = (w ? vg : kg) + (uint64_t)(c0 + r) * kv_dim + 8 * sg;
+                uint16_t *dst = (w ? vh : kh) + (b * CH + r) * HD + 8 * sg;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // the positions pair p uses in chunk c0 .. c0 + n - 1: up to its token's position
+    auto valid = [&](uint32_t p, uint32_t c0, uint32_t n) -> uint32_t {
+        const uint32_t t = t0 + p % TB;
+        if (t >= tend || pos0 + t < c0) return 0u;
+        const uint32_t v = pos0 + t - c0 + 1;
+        return v < n ? v : n;
+    };
+    const uint32_t d2 = tid % ND, pq = tid / ND;  // recurrence: dims 2 d2, 2 d2 + 1, pairs 4 pq ..
+    float acc[4][2];
+#pragma unroll
+    for (int k = 0; k < 4; k++) acc[k][0] = acc[k][1] = 0.0f;
+    issue(0);
+    for (uint32_t c = 0; c < nc; c++) {
+        issue(c + 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();  // chunk c's rows are in, and everyone is done with chunk c - 1
+        const uint32_t c0 = c * CH, n = T - c0 < CH ? T - c0 : CH, b = c & 1u;
+        for (uint32_t i = tid; i < n * HD; i += blockDim.x) {
+            kf[i] = __half2float(__ushort_as_half(kh[b * CH * HD + i]));
+            vf[i] = __half2float(__ushort_as_half(vh[b * CH * HD + i]));
+        }
+        __syncthreads();
+        // scores: thread (pair p, positions 2 pg, 2 pg + 1): pairs fastest, so
+        // a warp reads the same K rows (broadcast) and padded q rows
+        for (uint32_t task = tid; task < P * (CH / 2); task += blockDim.x) {
+            const uint32_t p = task % P, pg = task / P;
+            if (2 * pg >= valid(p, c0, n)) continue;
+            float al[2][8];
+#pragma unroll
+            for (int j = 0; j < 2; j++)
+#pragma unroll
+                for (int l = 0; l < 8; l++) al[j][l] = 0.0f;
+            const float *qp = qf + p * QS;
+#pragma unroll 4
+            for (uint32_t i = 0; i < HD / 8; i++) {
+                const float4 q0 = *reinterpret_cast<const float4 *>(qp + 8 * i);
+                const float4 q1 = *reinterpret_cast<const float4 *>(qp + 8 * i + 4);
+                const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const float *kr = kf + (2 * pg + j) * HD + 8 * i;
+                    const float4 k0 = *reinterpret_cast<const float4 *>(kr);
+                    const float4 k1 = *reinterpret_cast<const float4 *>(kr + 4);
+                    const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+                    for (int l = 0; l < 8; l++) al[j][l] = __fmaf_rn(kv[l], qv[l], al[j][l]);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const float x = __fadd_rn(__fadd_rn(__fadd_rn(al[j][0], al[j][4]), __fadd_rn(al[j][1], al[j][5])),
+                                          __fadd_rn(__fadd_rn(al[j][2], al[j][6]), __fadd_rn(al[j][3], al[j][7])));
+                sc[p * CH + 2 * pg + j] = __fmul_rn(__fadd_rn(x, 0.0f), a.scale);
+            }
+        }
+        __syncthreads();
+        // running maxima, alpha and p: one warp per pair, lane = position
+        for (uint32_t p = warp; p < P; p += nwarps) {
+            const uint32_t vp = valid(p, c0, n);
+            if (vp == 0) continue;
+            const float s = lane < vp ? sc[p * CH + lane] : -INFINITY;
+            float m = isnan(s) ? -INFINITY : s;  // f32::max(prev, NaN) = prev
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float u = __shfl_up_sync(0xffffffffu, m, o);
+                if (lane >= (uint32_t)o) m = fmaxf(m, u);
+            }
+            const float carry = mrun[p];
+            m = fmaxf(m, carry);
+            const float prev = __shfl_up_sync(0xffffffffu, m, 1);
+            const float mprev = lane == 0 ? carry : prev;
+            if (lane < vp) pa[p * CH + lane] = make_float2(expf_ref(__fsub_rn(s, m)), expf_ref(__fsub_rn(mprev, m)));
+            const float mlast = __shfl_sync(0xffffffffu, m, 31);
+            __syncwarp();
+            if (lane == 0) mrun[p] = mlast;  // used only when all CH positions were the pair's
+        }
+        __syncthreads();
+        // the recurrences: l (thread p < P), acc (thread: 4 pairs x 4 dims)
+        if (tid < P) {
+            const uint32_t vp = valid(tid, c0, n);
+            float l = lsum[tid];
+            for (uint32_t t = 0; t < vp; t++) {
+                const float2 w = pa[tid * CH + t];
+                l = __fadd_rn(__fmul_rn(l, w.y), w.x);
+            }
+            lsum[tid] = l;
+        }
+        uint32_t vk[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) vk[k] = valid(4 * pq + k, c0, n);
+        const uint32_t vmax = max(max(vk[0], vk[1]), max(vk[2], vk[3]));
+        const uint32_t vmin = min(min(vk[0], vk[1]), min(vk[2], vk[3])) & ~1u;
+        const float4 *pa4 = reinterpret_cast<const float4 *>(pa);  // (p, alpha) of positions t, t + 1
+        // positions every pair of the thread uses, two at a time, no predicates
+        for (uint32_t t = 0; t < vmin; t += 2) {
+            const float2 va = *reinterpret_cast<const float2 *>(vf + t * HD + 2 * d2);
+            const float2 vb = *reinterpret_cast<const float2 *>(vf + (t + 1) * HD + 2 * d2);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float4 w = pa4[((4 * pq + k) * CH + t) / 2];
+                acc[k][0] = __fmaf_rn(w.x, va.x, __fmul_rn(acc[k][0], w.y));
+                acc[k][1] = __fmaf_rn(w.x, va.y, __fmul_rn(acc[k][1], w.y));
+                acc[k][0] = __fmaf_rn(w.z, vb.x, __fmul_rn(acc[k][0], w.w));
+                acc[k][1] = __fmaf_rn(w.z, vb.y, __fmul_rn(acc[k][1], w.w));
+            }
+        }
+        for (uint32_t t = vmin; t < vmax; t++) {
+            const float2 va = *reinterpret_cast<const float2 *>(vf + t * HD + 2 * d2);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                if (t < vk[k]) {
+                    const float2 w = pa[(4 * pq + k) * CH + t];
+                    acc[k][0] = __fmaf_rn(w.x, va.x, __fmul_rn(acc[k][0], w.y));
+                    acc[k][1] = __fmaf_rn(w.x, va.y, __fmul_rn(acc[k][1], w.y));
+                }
+            }
+        }
+    }
+    __syncthreads();
+    grid_launch_dependents();
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const uint32_t p = 4 * pq + k, t = t0 + p % TB;
+        if (t >= tend) continue;
+        const float l = lsum[p];
+        const float inv = __fdiv_rn(1.0f, l > 1e-9f ? l : 1e-9f);  // 1 / l.max(1e-9): a NaN l gives 1e-9
+        float *o = a.out + (uint64_t)t * a.n_heads * HD + (g * H + p / TB) * HD + 2 * d2;
+        o[0] = __fmul_rn(acc[k][0], inv);
+        o[1] = __fmul_rn(acc[k][1], inv);
+    }
+}
+
+template __global__ void attention_batch_kernel<64>(const __grid_constant__ AttnArgs);
+template __global__ void attention_batch_kernel<128>(const __grid_constant__ AttnArgs);
+template __global__ void attention_batch_kernel<256>(const __grid_constant__ AttnArgs);
+
 // ARGMAX_CTAS blocks: (total_cmp key, index) maxima with the larger index on
 // ties, then the last block to finish reduces them.
 __global__ void __launch_bounds__(ARGMAX_THREADS) argmax_kernel(const __grid_constant__ ArgmaxArgs a) {

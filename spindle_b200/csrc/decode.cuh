@@ -97,7 +97,21 @@ struct AttnArgs {
     uint64_t q_stride;
     uint32_t nbuf;              // chunk buffers in shared memory (2..ATTN_MAX_BUF)
     uint32_t chunk;             // positions per chunk: 64 or 128 (smaller chunks, more CTAs per SM)
+    uint32_t ntok;              // attention_batch_kernel: tokens of the batch
 };
+
+// Batch attention with the K/V rows shared (attention_batch_kernel): one CTA
+// per (KV head, block of ATTN_PAIRS / group tokens) computes the group's
+// ATTN_PAIRS (query head, token) pairs, staging each chunk of ATTN_BCH
+// positions of the KV head's K and V rows once for all of them.
+constexpr uint32_t ATTN_PAIRS = 16;
+constexpr uint32_t ATTN_BCH = 32;
+__host__ __device__ inline uint32_t attn_batch_threads(uint32_t head_dim) { return 2u * head_dim; }
+// q (f32, rows padded by 4) | K, V f16 x 2 buffers | K, V f32 | scores | (p, alpha) | l, running max
+__host__ __device__ inline uint32_t attn_batch_smem(uint32_t head_dim) {
+    return ATTN_PAIRS * (head_dim + 4u) * 4u + 2u * 2u * ATTN_BCH * head_dim * 2u + 2u * ATTN_BCH * head_dim * 4u +
+           ATTN_PAIRS * ATTN_BCH * 4u + ATTN_PAIRS * ATTN_BCH * 8u + 2u * ATTN_PAIRS * 4u;
+}
 
 // The greedy token (f32::total_cmp, last maximum on ties), written as the next
 // step's token; the position advances.  ARGMAX_CTAS blocks each reduce a
@@ -172,6 +186,8 @@ __global__ void kv_shift_kernel(const __grid_constant__ KvShiftArgs a);
 
 __global__ void embed_kernel(const __grid_constant__ EmbedArgs a);
 __global__ void rmsnorm_kernel(const __grid_constant__ NormArgs a);
+template <int HD>
+__global__ void attention_batch_kernel(const __grid_constant__ AttnArgs a);
 template <int HD, int CHK>
 __global__ void attention_kernel(const __grid_constant__ AttnArgs a);
 __global__ void argmax_kernel(const __grid_constant__ ArgmaxArgs a);

@@ -145,11 +145,15 @@ __global__ void __launch_bounds__(64 / TPW * 32, 1) gemm_batch_kernel(const __gr
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem), *empty = full + GB_MAX_STAGES;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t wbytes = a.tps * CB, abytes = qb_block_bytes(a.ntok);
+    // blockIdx.y: QB group (64 vectors) of the a.ntok: its image, its tokens, its outputs
+    const uint32_t ntok = a.ntok > blockIdx.y * QB_GROUP ? qb_group_tokens(a.ntok, blockIdx.y) : 0u;
+    const uint8_t *qb = a.qb + qb_group_offset(blockIdx.y, a.nb);
+    float *const out = a.out + (uint64_t)blockIdx.y * QB_GROUP * a.ldo;
+    const uint32_t wbytes = a.tps * CB, abytes = qb_block_bytes(ntok);
     // A launch this layout does not fit records an error and does nothing
     // (uniform exit, before any barrier).
-    if (blockDim.x != THREADS || a.nstages < 2 || a.nstages > GB_MAX_STAGES || a.ntok == 0 ||
-        a.ntok > GB_MAX_TOK || a.nq * a.tps != CONS || a.nq * (uint32_t)TPW < a.ntok || a.nb == 0 ||
+    if (blockDim.x != THREADS || a.nstages < 2 || a.nstages > GB_MAX_STAGES || ntok == 0 ||
+        a.ntok > QB_MAX_TOK || a.nq * a.tps != CONS || a.nq * (uint32_t)TPW < ntok || a.nb == 0 ||
         a.stage_bytes < wbytes + abytes || (a.stage_bytes & 15u) ||
         GB_BAR_BYTES + a.nstages * a.stage_bytes > dynamic_smem_size()) {
         if (threadIdx.x == 0) atomicExch(&g_dev_status, (unsigned)DEV_BAD_LAUNCH);
@@ -188,7 +192,7 @@ __global__ void __launch_bounds__(64 / TPW * 32, 1) gemm_batch_kernel(const __gr
             grid_dependency_wait();
             waited = true;
         }
-        bulk_g2s(st + wbytes, a.qb + (uint64_t)i * abytes, abytes, &full[s]);
+        bulk_g2s(st + wbytes, qb + (uint64_t)i * abytes, abytes, &full[s]);
         issued = k + 1;
     };
     if (threadIdx.x == 0) {
@@ -198,7 +202,7 @@ __global__ void __launch_bounds__(64 / TPW * 32, 1) gemm_batch_kernel(const __gr
 
     // Consumers: warp = (tile j of the step, token group q).
     const uint32_t j = warp / a.nq, q = warp % a.nq;
-    const uint32_t v0 = (uint32_t)TPW * q, nv = a.ntok > v0 ? min((uint32_t)TPW, a.ntok - v0) : 0u;
+    const uint32_t v0 = (uint32_t)TPW * q, nv = ntok > v0 ? min((uint32_t)TPW, ntok - v0) : 0u;
     const uint32_t g = lane >> 4, r = lane & 15u;
     float acc[TPW][4], corr[TPW];
 #pragma unroll
@@ -222,8 +226,8 @@ __global__ void __launch_bounds__(64 / TPW * 32, 1) gemm_batch_kernel(const __gr
         if (mine && !failed) {
             const uint8_t *st = stages + s * a.stage_bytes;
             const uint8_t *act = st + wbytes;
-            gb_block<DT, TPW>(st + j * CB, g, r, nv, act + 256u * v0, act + 256u * a.ntok + 32u * v0,
-                         reinterpret_cast<const float *>(act + 288u * a.ntok) + v0, acc, corr);
+            gb_block<DT, TPW>(st + j * CB, g, r, nv, act + 256u * v0, act + 256u * ntok + 32u * v0,
+                         reinterpret_cast<const float *>(act + 288u * ntok) + v0, acc, corr);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -251,7 +255,7 @@ __global__ void __launch_bounds__(64 / TPW * 32, 1) gemm_batch_kernel(const __gr
 #pragma unroll
                     for (int m = 0; m < 4; m++) x[m] = __fadd_rn(acc[v][m], __shfl_down_sync(0xffffffffu, acc[v][m], 16));
                     const float yv = __fsub_rn(__fadd_rn(__fadd_rn(x[0], x[2]), __fadd_rn(x[1], x[3])), corr[v]);
-                    float *dst = a.out + (uint64_t)(v0 + v) * a.ldo;
+                    float *dst = out + (uint64_t)(v0 + v) * a.ldo;
                     if (a.swiglu) {
                         // rows r < 8 gate, r + 8 up of the same outputs (smollm_chat.rs:357-359)
                         const float up = __shfl_down_sync(0xffffffffu, yv, 8);

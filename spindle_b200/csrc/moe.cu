@@ -200,12 +200,21 @@ __global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(
     if (!__syncthreads_or(last)) return;
     __threadfence();
     const sg_moe_choice *chs = a.choices;
+    // every token's slot count and experts into shared memory, all loads in
+    // flight at once (the passes below would otherwise walk the tokens with
+    // one L2 round trip each)
+    uint32_t *cnt = bases + a.n_tok + 1, *jbase = cnt + 256, *rank = jbase + 256;
+    uint32_t *tn = rank + a.n_tok * MOE_MAXK;
+    int32_t *tids = reinterpret_cast<int32_t *>(tn + a.n_tok);
+    for (uint32_t i = tid; i < a.n_tok * MOE_MAXK; i += blockDim.x) tids[i] = __ldcg(&chs[i / MOE_MAXK].id[i % MOE_MAXK]);
+    for (uint32_t u = tid; u < a.n_tok; u += blockDim.x) tn[u] = min((uint32_t)__ldcg(&chs[u].n), a.n_used);
+    __syncthreads();
     // slot bases: an exclusive prefix sum over the tokens' slot counts (one
     // token per thread, n_tok <= SG_MOE_MAX_BATCH = SELECT_BATCH_THREADS),
     // then every warp writes its tokens' slots
     {
         __shared__ uint32_t wsum[SELECT_BATCH_THREADS / 32];
-        const uint32_t c = tid < a.n_tok ? min((uint32_t)__ldcg(&chs[tid].n), a.n_used) : 0u;
+        const uint32_t c = tid < a.n_tok ? tn[tid] : 0u;
         uint32_t incl = c;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -222,9 +231,9 @@ __global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(
     }
     __syncthreads();
     for (uint32_t u = warp; u < a.n_tok; u += nwarps) {
-        const uint32_t n = min((uint32_t)__ldcg(&chs[u].n), a.n_used), base = bases[u];
+        const uint32_t n = tn[u], base = bases[u];
         if (lane < n) {
-            a.slots[2 * (base + lane)] = __ldcg(&chs[u].id[lane]);
+            a.slots[2 * (base + lane)] = tids[u * MOE_MAXK + lane];
             a.slots[2 * (base + lane) + 1] = (int32_t)u;
         }
         if (lane == 0) a.slot_base[u] = base;
@@ -235,9 +244,9 @@ __global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(
             // this rank's slots (expert parallelism), in global slot order
             uint32_t j = 0;
             for (uint32_t u = 0; u < a.n_tok; u++) {
-                const uint32_t n = min((uint32_t)__ldcg(&chs[u].n), a.n_used);
+                const uint32_t n = tn[u];
                 for (uint32_t i = 0; i < n; i++) {
-                    const int32_t e = __ldcg(&chs[u].id[i]);
+                    const int32_t e = tids[u * MOE_MAXK + i];
                     if ((uint32_t)e >= a.ep_lo && (uint32_t)e < a.ep_hi) {
                         a.slots_local[2 * j] = e - (int32_t)a.ep_lo;
                         a.slots_local[2 * j + 1] = (int32_t)u;
@@ -260,12 +269,11 @@ __global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(
     const uint32_t jm = a.job_max < 1 ? 1u : a.job_max > MOE_JOB_MAX ? MOE_JOB_MAX : a.job_max;
     // jobs: the slots of each expert (in any order: each slot's result does not
     // depend on its job) in groups of at most MOE_JOB_MAX, experts in order
-    uint32_t *cnt = bases + a.n_tok + 1, *jbase = cnt + 256, *rank = jbase + 256;
     for (uint32_t e = tid; e < 256; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (uint32_t u = warp; u < a.n_tok; u += nwarps) {
-        const uint32_t n = min((uint32_t)__ldcg(&chs[u].n), a.n_used), base = bases[u];
-        if (lane < n) rank[base + lane] = atomicAdd(&cnt[__ldcg(&chs[u].id[lane])], 1u);
+        const uint32_t n = tn[u], base = bases[u];
+        if (lane < n) rank[base + lane] = atomicAdd(&cnt[tids[u * MOE_MAXK + lane]], 1u);
     }
     __syncthreads();
     if (warp == 0) {
@@ -295,9 +303,9 @@ __global__ void __launch_bounds__(SELECT_BATCH_THREADS) moe_select_batch_kernel(
     }
     __syncthreads();
     for (uint32_t u = warp; u < a.n_tok; u += nwarps) {
-        const uint32_t n = min((uint32_t)__ldcg(&chs[u].n), a.n_used), base = bases[u];
+        const uint32_t n = tn[u], base = bases[u];
         if (lane < n) {
-            const uint32_t e = (uint32_t)__ldcg(&chs[u].id[lane]), r = rank[base + lane];
+            const uint32_t e = (uint32_t)tids[u * MOE_MAXK + lane], r = rank[base + lane];
             if (jbase[e] + r / jm >= a.jobs_cap) continue;  // over capacity: recorded above, no jobs run
             int32_t *job = a.jobs + (uint64_t)(jbase[e] + r / jm) * MOE_JOB_INTS;
             job[2 + r % jm] = (int32_t)(base + lane);

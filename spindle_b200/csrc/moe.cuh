@@ -74,11 +74,12 @@ struct SelectBatchArgs {
 constexpr uint32_t MOE_JOB_MAX = 8;
 constexpr uint32_t MOE_JOB_INTS = 2 + MOE_JOB_MAX;
 constexpr uint32_t SELECT_BATCH_THREADS = 128;  // one warp per token, ceil(n_tok / 4) CTAs
-// per warp: 256 floats and a Choice; then the token bases (n_tok + 1), and the
-// job build's per-expert counts and job bases (256 each) and per-slot ranks
+// per warp: 256 floats and a Choice; then the token bases (n_tok + 1), the
+// job build's per-expert counts and job bases (256 each) and per-slot ranks,
+// and every token's slot count and experts (the last CTA stages them once)
 __host__ __device__ inline uint32_t select_batch_smem(uint32_t n_tok) {
     return (SELECT_BATCH_THREADS / 32) * (256u * 4u + (uint32_t)sizeof(moe::Choice)) + (n_tok + 1u) * 4u +
-           2u * 256u * 4u + n_tok * MOE_MAXK * 4u;
+           2u * 256u * 4u + n_tok * MOE_MAXK * 4u + n_tok * (1u + MOE_MAXK) * 4u;
 }
 
 struct CombineBatchArgs {

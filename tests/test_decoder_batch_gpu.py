@@ -88,6 +88,21 @@ def test_batch_long_context(dev):
     run(cfg, U.dtypes_for(cfg), 79, toks, [128, 100, 62], dev)
 
 
+@pytest.mark.parametrize("amin", ["1", "1000"])
+def test_batch_attention_forms(dev, monkeypatch, amin):
+    # the batch attention with K/V rows shared by a CTA's (query head, token)
+    # pairs from one token on (1), and the per-(head, token) kernel only (1000):
+    # GQA groups of 1, 2, 4 and 8, head_dim 64 / 128 / 256, chunks crossing
+    # the 32-position staging chunks, every token still the one-token step
+    monkeypatch.setenv("SG_ATTN_BATCH_MIN", amin)
+    for cfg, chunks, seed in [(dict(U.DENSE, max_seq=160), [1, 40, 33, 70], 81),
+                              (dict(U.MOE, max_seq=160), [17, 2, 64, 40], 82),
+                              (dict(U.DENSE, n_heads=8, n_kv_heads=1, max_seq=100), [5, 31, 32, 9], 83),
+                              (dict(U.DENSE, n_heads=4, n_kv_heads=4, head_dim=256, max_seq=80), [3, 50], 84)]:
+        toks = np.random.default_rng(seed).integers(0, cfg["vocab"], sum(chunks)).tolist()
+        run(cfg, U.dtypes_for(cfg), seed, toks, chunks, dev)
+
+
 def test_batch_moe_verify_chunks(dev):
     # the verify batch of BASELINE config 5: 9 positions per call
     cfg = dict(U.MOE)
