@@ -441,6 +441,7 @@ sg_status launch_tiled(const uint8_t *w, int dt, uint32_t nb, const sg_q8k *xq, 
         a.slot_blocks = p.slot_blocks;
         a.nvec = (uint32_t)nv;
         a.qx_image = image;
+        a.pf_x = qx && env_int("SG_GEMV_PFX", 1) ? 1u : 0u;
         for (int v = 0; v < nv; v++) {
             if (qx) {
                 a.x[v] = x + (g + v) * ldx;

@@ -558,7 +558,11 @@ __global__ void __launch_bounds__(2 * HD, HD < 256 ? 2 : 1) attention_batch_kern
             m = fmaxf(m, carry);
             const float prev = __shfl_up_sync(0xffffffffu, m, 1);
             const float mprev = lane == 0 ? carry : prev;
-            if (lane < vp) pa[p * CH + lane] = make_float2(expf_ref(__fsub_rn(s, m)), expf_ref(__fsub_rn(mprev, m)));
+            // alpha = exp(0) = 1 exactly where the maximum did not move (a finite one:
+            // an infinite maximum takes the exp, whose NaN the reference carries)
+            if (lane < vp)
+                pa[p * CH + lane] = make_float2(expf_ref(__fsub_rn(s, m)),
+                                                mprev == m && isfinite(m) ? 1.0f : expf_ref(__fsub_rn(mprev, m)));
             const float mlast = __shfl_sync(0xffffffffu, m, 31);
             __syncwarp();
             if (lane == 0) mrun[p] = mlast;  // used only when all CH positions were the pair's

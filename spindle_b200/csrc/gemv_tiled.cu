@@ -283,6 +283,16 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
         fence_mbar_init();
         while (iss < nitems && iss < a.nstages) issue_next();
     }
+    // The fp32 activations' lines fetched into L2 now, so that their loads
+    // after the wait hit L2: a hint only (L2 is where every write lands, so a
+    // line the previous grid still writes is simply updated there); the
+    // grid's CTAs share the lines out.
+    if (MODE == IN_F32 && a.pf_x) {
+        const uint32_t lines = a.nb * 8u;  // 128-byte lines per vector
+        for (uint32_t v = 0; v < a.nvec; v++)
+            for (uint32_t l = blockIdx.x * blockDim.x + threadIdx.x; l < lines; l += gridDim.x * blockDim.x)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(a.x[v] + 32u * l));
+    }
     // The activations do: wait for the grid that wrote them, then stage them.
     grid_dependency_wait();
     const uint32_t tp_e = a.npeers ? *a.epoch + 1u : 0u;  // this call's epoch (row split, expert parallelism)

@@ -134,6 +134,7 @@ struct TGemvArgs {
     const int32_t *jobs;
     const uint32_t *n_jobs;
     uint32_t job_ints;
+    uint32_t pf_x;        // IN_F32: fetch the fp32 inputs into L2 before the dependency wait
 };
 
 // In the MoE modes the choice is kept at the top of the barrier area: n at
