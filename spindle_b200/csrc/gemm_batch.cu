@@ -15,7 +15,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 // One super-block column of one tile (col) against `nv` vectors whose QB data
 // for this block start at aq (qs, 256 B apart), ab (bsums, 32 B apart) and ad
 // (d): thread (g, r) folds AVX lanes 4g..4g+3 of row r into acc / corr, in the
-// order of block_q4k / block_q6k followed by the GEMV's single-slot chain step.
+// order of q4k_dot / q6k_dot followed by the GEMV's single-slot chain step.
 template <int DT, int TPW>
 __device__ __forceinline__ void gb_block(const uint8_t *col, uint32_t g, uint32_t r, uint32_t nv, const uint8_t *aq,
                                          const uint8_t *ab, const float *ad, float (&acc)[TPW][4],

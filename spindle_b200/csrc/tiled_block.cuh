@@ -103,7 +103,8 @@ __device__ __forceinline__ void q4k_weights(const uint8_t *col, uint32_t g, uint
     }
 }
 
-// av: one vector's activation image; s, cd, ct as block_q4k's for that vector
+// av: one vector's activation image; s: the int32 lane sums of lanes 4g..4g+3
+// of row r, cd = d * xd, ct: the min correction term, for that vector
 __device__ __forceinline__ void q4k_dot(const Q4KWeights &w, uint32_t g, uint32_t i, uint32_t nb, const uint8_t *av,
                                         int (&s)[4], float &cd, float &ct) {
     const uint8_t *y = av + 256u * i + 16u * g;
@@ -186,118 +187,6 @@ __device__ __forceinline__ void q6k_dot(const Q6KWeights &q, uint32_t g, uint32_
     ct = __fmul_rn(cd, __int2float_rn(32 * sp));
 }
 
-// One super-block of one 16-row tile for lanes 4g..4g+3 of row r: the exact
-// int32 lane sums s, d*xd (cd) and the correction term (ct) per vector.
-template <int NV>
-__device__ __forceinline__ void block_q4k(const uint8_t *col, uint32_t g, uint32_t r, uint32_t i,
-                                          uint32_t nvec, uint32_t nb, const uint8_t *act, uint32_t act_stride,
-                                          int (&s)[NV][4], float (&cd)[NV], float (&ct)[NV]) {
-    const uint4 hd = lds128(col + 2048 + 16 * r);
-    const float d = h2f_lo(hd.x), dmin = h2f_hi(hd.x);
-    const uint32_t sclo = hd.y & 0x3F3F3F3Fu, schi = (hd.w & M4) | ((hd.y >> 2) & B45);
-    const uint32_t mnw = g ? (((hd.w >> 4) & M4) | ((hd.z >> 2) & B45)) : (hd.z & 0x3F3F3F3Fu);
-    const int sc[8] = {ubyte(sclo, 0), ubyte(sclo, 1), ubyte(sclo, 2), ubyte(sclo, 3),
-                       ubyte(schi, 0), ubyte(schi, 1), ubyte(schi, 2), ubyte(schi, 3)};
-    // high nibbles stay in place (16 x the value): an unsigned x signed dp4a
-    // of them is exactly 16 x the nibble dot, shifted back once per block
-    uint32_t lo[4][4], hi[4][4];
-#pragma unroll
-    for (int cc = 0; cc < 4; cc++) {
-        const uint4 qv = lds128(col + 128 * r + 16 * q4k_chunk(2 * cc + g, r));
-#pragma unroll
-        for (int m = 0; m < 4; m++) {
-            lo[cc][m] = w4(qv, m) & M4;
-            hi[cc][m] = w4(qv, m) & 0xF0F0F0F0u;
-        }
-    }
-#pragma unroll
-    for (int v = 0; v < NV; v++) {
-        if (v >= (int)nvec) break;
-        const uint8_t *av = act + v * act_stride;
-        const uint8_t *y = av + 256u * i + 16u * g;
-        uint4 Y[8];
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) Y[kk] = lds128(y + 32 * kk);
-        const uint4 B = lds128(av + 256u * nb + 32u * i + 16u * g);
-        const float xd = *reinterpret_cast<const float *>(av + 288u * nb + 4u * i);
-        int sh[4];
-#pragma unroll
-        for (int m = 0; m < 4; m++) s[v][m] = sh[m] = 0;
-#pragma unroll
-        for (int cc = 0; cc < 4; cc++)
-#pragma unroll
-            for (int m = 0; m < 4; m++) {
-                s[v][m] += sc[2 * cc] * __dp4a((int)lo[cc][m], (int)w4(Y[2 * cc], m), 0);
-                sh[m] += sc[2 * cc + 1] * dp4a_us(hi[cc][m], (int)w4(Y[2 * cc + 1], m));
-            }
-#pragma unroll
-        for (int m = 0; m < 4; m++) s[v][m] += sh[m] >> 4;  // sh is a multiple of 16: exact
-        cd[v] = __fmul_rn(d, xd);
-        // mins: sum over sub-blocks j = 4g..4g+3 of mn_j * (bsums[2j] + bsums[2j+1]),
-        // one dp2a per pair with mn_j in both low bytes
-        int sp = 0;
-#pragma unroll
-        for (int m = 0; m < 4; m++) sp = __dp2a_lo((int)w4(B, m), (int)__byte_perm(mnw, 0, 0x11 * m), sp);
-        sp += __shfl_xor_sync(0xffffffffu, sp, 16);
-        ct[v] = __fmul_rn(__fmul_rn(dmin, xd), __int2float_rn(sp));
-    }
-}
-
-template <int NV>
-__device__ __forceinline__ void block_q6k(const uint8_t *col, uint32_t g, uint32_t r, uint32_t i,
-                                          uint32_t nvec, uint32_t nb, const uint8_t *act, uint32_t act_stride,
-                                          int (&s)[NV][4], float (&cd)[NV], float (&ct)[NV]) {
-    const uint8_t *qrow = col + 192 * r;
-    uint32_t w[8][4];
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const uint4 L0 = lds128(qrow + 16 * q6k_chunk(4 * h + g, r));
-        const uint4 L1 = lds128(qrow + 16 * q6k_chunk(4 * h + 2 + g, r));
-        const uint4 H = lds128(qrow + 16 * q6k_chunk(8 + 2 * h + g, r));
-#pragma unroll
-        for (int m = 0; m < 4; m++) {
-            const uint32_t l0 = w4(L0, m), l1 = w4(L1, m), hh = w4(H, m);
-            w[4 * h + 0][m] = (l0 & M4) | ((hh << 4) & B45);
-            w[4 * h + 1][m] = (l1 & M4) | ((hh << 2) & B45);
-            w[4 * h + 2][m] = ((l0 >> 4) & M4) | (hh & B45);
-            w[4 * h + 3][m] = ((l1 >> 4) & M4) | ((hh >> 2) & B45);
-        }
-    }
-    const uint4 SC = lds128(col + 3072 + 16 * r);
-    const float d = __half2float(*reinterpret_cast<const __half *>(col + 3328 + 2 * r));
-    // chunk 4h+k of lanes 4g..4g+3 uses scale 8h + 2k + g
-    int scv[8];
-#pragma unroll
-    for (int h = 0; h < 2; h++)
-#pragma unroll
-        for (int kk = 0; kk < 4; kk++) scv[4 * h + kk] = sbyte(w4(SC, 2 * h + (kk >> 1)), 2 * (kk & 1) + (int)g);
-#pragma unroll
-    for (int v = 0; v < NV; v++) {
-        if (v >= (int)nvec) break;
-        const uint8_t *av = act + v * act_stride;
-        const uint8_t *y = av + 256u * i + 16u * g;
-        uint4 Y[8];
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) Y[kk] = lds128(y + 32 * kk);
-        const uint4 B = lds128(av + 256u * nb + 32u * i + 16u * g);
-        const float xd = *reinterpret_cast<const float *>(av + 288u * nb + 4u * i);
-#pragma unroll
-        for (int m = 0; m < 4; m++) s[v][m] = 0;
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++)
-#pragma unroll
-            for (int m = 0; m < 4; m++) s[v][m] += scv[kk] * __dp4a((int)w[kk][m], (int)w4(Y[kk], m), 0);
-        cd[v] = __fmul_rn(d, xd);
-        // offset: sum over groups 8g..8g+7 of sc * bsums, one dp2a per pair
-        const uint32_t sw0 = g ? SC.z : SC.x, sw1 = g ? SC.w : SC.y;
-        int sp = __dp2a_lo((int)B.x, (int)sw0, 0);
-        sp = __dp2a_hi((int)B.y, (int)sw0, sp);
-        sp = __dp2a_lo((int)B.z, (int)sw1, sp);
-        sp = __dp2a_hi((int)B.w, (int)sw1, sp);
-        sp += __shfl_xor_sync(0xffffffffu, sp, 16);
-        ct[v] = __fmul_rn(cd[v], __int2float_rn(32 * sp));
-    }
-}
 
 }  // namespace tiled
 
