@@ -1333,6 +1333,7 @@ def run_gpu_decode(args):
 
 PREFILL_PROMPT = 2048
 PREFILL_CHUNK = 128  # feed's chunk (smollm_chat.rs:3090); --chunk overrides
+PREFILL_IN_FLIGHT = 6  # chunks in flight on as many streams; --overlap overrides
 VERIFY_N = 9
 SPEC_TOKENS = 64
 
@@ -1504,7 +1505,42 @@ def run_gpu_prefill(args):
     nl = cfg["n_layers"]
     ptr = lambda t, off=0: C.c_void_p(t.data_ptr() + off)
 
+    # chunks in flight: chunk i a layer at a time on stream i % K with its
+    # own scratch, its layer l after chunk i - 1's layer l (K = 1: one call
+    # per chunk on one stream)
+    K_ = max(1, args.overlap)
+    bufs = [scr] + [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(K_ - 1)]
+    for b in bufs[1:]:
+        _lib.check(L.sg_model_batch_prepare(C.byref(dec.model), C_, C.c_void_p(b.data_ptr()), nbytes, None), "prepare")
+    side = [torch.cuda.Stream(device=dev) for _ in range(K_ - 1)]
+
+    def prefill_overlapped(st):
+        sts, prev = [st] + side, None
+        for si in side:
+            si.wait_stream(st)
+        for i, (c0, n) in enumerate(calls[:-1]):
+            si, bi, evs = sts[i % K_], bufs[i % K_], []
+            for l in range(nl):
+                if prev is not None:
+                    si.wait_event(prev[l])
+                _lib.check(L.sg_forward_batch_range(C.byref(dec.model), l, l + 1, ptr(toks, 4 * c0) if l == 0 else None,
+                                                    None, n, ptr(pos, 4 * i), ptr(dec.kv), ptr(bi), nbytes, C_,
+                                                    ptr(hid) if l == nl - 1 else None, None, cfg["vocab"], None,
+                                                    C.c_void_p(si.cuda_stream)), "prefill")
+                ev = torch.cuda.Event()
+                ev.record(si)
+                evs.append(ev)
+            prev = evs
+        for si in side:
+            st.wait_stream(si)
+        i, (c0, n) = len(calls) - 1, calls[-1]
+        _lib.check(L.sg_forward_batch_range(C.byref(dec.model), 0, nl, ptr(toks, 4 * c0), None, n, ptr(pos, 4 * i),
+                                            ptr(dec.kv), ptr(scr), nbytes, C_, None, None, cfg["vocab"], ptr(greedy),
+                                            C.c_void_p(st.cuda_stream)), "prefill")
+
     def prefill(st):
+        if K_ > 1:
+            return prefill_overlapped(st)
         sp = C.c_void_p(st.cuda_stream)
         for i, (c0, n) in enumerate(calls):
             head = i == len(calls) - 1
@@ -1650,6 +1686,8 @@ def run_gpu_prefill(args):
                                prompt=n_prompt, seq_len=n_prompt, chunk=C_, verify_n=VERIFY_N,
                                calls="%d chunks of up to %d positions without the head, then the last position "
                                      "with the LM head and argmax" % (len(calls) - 1, C_),
+                               in_flight="%d chunks on %d streams, a layer at a time" % (K_, K_) if K_ > 1
+                               else "1 (one call per chunk)",
                                l2="2.0 GB of weights touched per chunk > 126 MB L2"),
                 "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": peak, "unit": "TOP/s",
                              "frac": round(achieved / peak, 5), "traffic": None, "peak_source": peak_src,
@@ -1738,6 +1776,9 @@ def main():
                     help="decode workload: the model architecture")
     ap.add_argument("--gguf", default=None, help="decode workload: load the model from this GGUF file instead")
     ap.add_argument("--chunk", type=int, default=0, help="prefill workload: positions per batch call (default 128)")
+    ap.add_argument("--overlap", type=int, default=PREFILL_IN_FLIGHT,
+                    help="prefill workload: chunks in flight on as many streams, a layer at a time (1: one call per "
+                         "chunk on one stream)"),
     args = ap.parse_args()
     if args.warmup < 3 and not args.profile:
         args.warmup = 3

@@ -481,7 +481,12 @@ SG_API sg_status sg_kv_shift(const sg_model *m, void *d_kv, const void *d_scratc
  * the output-normed hidden states [n][dim] (forward_batch_slice's return
  * value), and the LM head and argmax run only when d_logits or d_greedy is
  * given (a prompt fed through feed(), smollm_chat.rs:3042-3106, needs no
- * logits).  A stage's KV cache rows are its own layers'. */
+ * logits).  A stage's KV cache rows are its own layers'.
+ * Continuing on one scratch: l1 < n_layers with d_hidden_out null leaves the
+ * layers' state in d_scratch, and a following call with l0 equal to that l1,
+ * d_hidden_in null, the same scratch, tokens and positions picks it up (so a
+ * prompt can go through a layer at a time, e.g. two chunks on two streams,
+ * without moving the residual); the results are those of one call. */
 SG_API sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, const int32_t *d_tokens,
                                         const float *d_hidden_in, uint64_t n, const int32_t *d_pos, void *d_kv,
                                         void *d_scratch, uint64_t scratch_bytes, uint64_t n_max,

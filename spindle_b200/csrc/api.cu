@@ -1833,8 +1833,10 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
     if (st) return st;
     if (l0 >= l1 || l1 > m->n_layers) return SG_ERR_INVALID;
     if (n == 0) return SG_OK;
-    if ((l0 == 0 ? !d_tokens : !d_hidden_in) || (l1 < m->n_layers && !d_hidden_out) || !d_pos || !d_kv ||
-        !d_scratch || n > n_max || n_max > SG_MOE_MAX_BATCH)
+    // l0 > 0 without d_hidden_in: continue from the state a call ending at l0
+    // left in this scratch (l1 < n_layers without d_hidden_out leaves it)
+    const bool resume = l0 > 0 && !d_hidden_in;
+    if ((l0 == 0 && !d_tokens) || !d_pos || !d_kv || !d_scratch || n > n_max || n_max > SG_MOE_MAX_BATCH)
         return SG_ERR_INVALID;
     if (!aligned(d_hidden_in, 16) || !aligned(d_hidden_out, 16)) return SG_ERR_ALIGN;
     if (d_logits && n > 1 && ldl < m->vocab) return SG_ERR_INVALID;
@@ -1903,7 +1905,7 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
     if (l0 == 0) {
         EmbedArgs ea = {m->embed, m->embed_dtype, dim, m->vocab, m->embedding_scale, nullptr, x, d_tokens, n_slots};
         CK(launch_pdl((const void *)embed_kernel, dim3((dim + 255) / 256, nt), 256, 0, s, &ea));
-    } else {
+    } else if (!resume) {
         // a later pipeline stage: the raw residual of the stage before
         CK(cudaMemcpyAsync(x, d_hidden_in, (uint64_t)nt * dim * 4, cudaMemcpyDeviceToDevice, s));
         CK(cudaMemsetAsync(n_slots, 0, 4, s));
@@ -1911,7 +1913,7 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
     }
     for (uint32_t l = l0; l < l1; l++) {
         const sg_layer &y = m->layers[l];
-        if ((st = launch_norm(x, l > l0 ? proj : nullptr, m->residual_scale, y.attn_norm, m->rms_eps, dim, xn,
+        if ((st = launch_norm(x, l > l0 || resume ? proj : nullptr, m->residual_scale, y.attn_norm, m->rms_eps, dim, xn,
                               nullptr, s, nt)))
             return st;
         uint64_t wq_bytes = 0;
@@ -1974,6 +1976,7 @@ sg_status sg_forward_batch_range(const sg_model *m, uint32_t l0, uint32_t l1, co
                 return st;
         }
     }
+    if (l1 < m->n_layers && !d_hidden_out) return SG_OK;  // the state stays in the scratch (x, proj)
     if (l1 < m->n_layers) {
         // a middle stage returns the raw residual (smollm_chat.rs:3546-3551)
         const uint64_t tot = (uint64_t)nt * dim;

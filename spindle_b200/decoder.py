@@ -308,6 +308,66 @@ class Decoder:
                                                head=False)
         return None if last is None else last[-1]
 
+    def feed_overlapped(self, tokens, pos0=0, chunk=128, streams=None, in_flight=2):
+        """feed with in_flight chunks in flight: chunk c runs a layer at a
+        time on stream c % in_flight with its own scratch
+        (sg_forward_batch_range continuing on that scratch), its layer l after
+        chunk c - 1's layer l (whose K/V rows it reads), so one chunk's
+        latency-bound kernels overlap the others'.  Every layer's arithmetic
+        is feed's, so the caches and the returned hidden state are bit for
+        bit feed's.  streams: in_flight torch.cuda.Streams (made here if None;
+        the caller's current stream waits for all of them before this
+        returns)."""
+        if self.ep is not None:
+            raise ValueError("the batch forward is not expert-parallel; build the Decoder without ep")
+        L = _sigs()
+        tokens = list(tokens)
+        nl = self.cfg["n_layers"]
+        if streams is None:
+            streams = [torch.cuda.Stream(device=self.dev) for _ in range(in_flight)]
+        k = len(streams)
+        if k < 1:
+            raise ValueError("feed_overlapped needs at least one stream")
+        cur = torch.cuda.current_stream(self.dev)
+        for st in streams:
+            st.wait_stream(cur)
+        if getattr(self, "_ovl", None) is None or self._ovl[0] < chunk or len(self._ovl[1]) < k:
+            nbytes = L.sg_model_batch_scratch_bytes(C.byref(self.model), chunk)
+            if not nbytes:
+                raise SgError(3, "sg_model_batch_scratch_bytes")
+            bufs = [torch.empty(nbytes, dtype=torch.uint8, device=self.dev) for _ in range(k)]
+            for b in bufs:
+                _lib.check(L.sg_model_batch_prepare(C.byref(self.model), chunk, C.c_void_p(b.data_ptr()), nbytes,
+                                                    _stream(cur)), "sg_model_batch_prepare")
+            self._ovl = (chunk, bufs)
+        n_max, bufs = self._ovl
+        starts = list(range(0, len(tokens), chunk))
+        toks = torch.tensor(tokens, dtype=torch.int32, device=self.dev)
+        pos = torch.tensor([pos0 + c0 for c0 in starts], dtype=torch.int32, device=self.dev)
+        out = torch.empty(chunk, self.cfg["dim"], dtype=torch.float32, device=self.dev)
+        for st in streams:
+            st.wait_stream(cur)  # the token and position copies above
+        prev = None
+        ptr = lambda t, off=0: C.c_void_p(t.data_ptr() + off)
+        for c, c0 in enumerate(starts):
+            st, buf, n = streams[c % k], bufs[c % k], min(chunk, len(tokens) - c0)
+            evs = []
+            for l in range(nl):
+                if prev is not None:
+                    st.wait_event(prev[l])
+                last = l == nl - 1
+                _lib.check(L.sg_forward_batch_range(
+                    C.byref(self.model), l, l + 1, ptr(toks, 4 * c0) if l == 0 else None, None, n, ptr(pos, 4 * c),
+                    ptr(self.kv), ptr(buf), buf.numel(), n_max, ptr(out) if last else None, None,
+                    self.cfg["vocab"], None, _stream(st)), "sg_forward_batch_range")
+                ev = torch.cuda.Event()
+                ev.record(st)
+                evs.append(ev)
+            prev = evs
+        for st in streams:
+            cur.wait_stream(st)
+        return out[n - 1] if starts else None
+
     def generate(self, prompt, n_new):
         """Greedy decode: feed the prompt, then n_new tokens; returns the new tokens."""
         out = []

@@ -129,3 +129,22 @@ def test_feed_matches_steps(dev, kind, chunk):
     assert np.array_equal(bits(h.cpu().numpy()), bits(seq.hidden.cpu().numpy()))
     assert torch.equal(seq.kv, bat.kv)
     __import__("spindle_b200").device_status()
+
+
+@pytest.mark.parametrize("kind,chunk,k", [("dense", 64, 2), ("moe", 32, 2), ("moe", 128, 2), ("moe", 32, 3)])
+def test_feed_overlapped_matches_feed(dev, kind, chunk, k):
+    # k chunks in flight, a layer at a time on k streams with their own
+    # scratch (sg_forward_batch_range continuing on a scratch): the caches and
+    # the last hidden state bit for bit those of feed
+    cfg = dict(U.DENSE if kind == "dense" else U.MOE, max_seq=160, n_layers=3)
+    dtypes = U.dtypes_for(cfg)
+    dw = U.device_weights(U.host_weights(cfg, dtypes, seed=88), dev)
+    a = Decoder(cfg, dw, dtypes, dev)
+    b = Decoder(cfg, dw, dtypes, dev)
+    toks = np.random.default_rng(12).integers(0, cfg["vocab"], 150).tolist()
+    ha = a.feed(toks, 0, chunk=chunk)
+    hb = b.feed_overlapped(toks, 0, chunk=chunk, in_flight=k)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(ha.cpu().numpy()), bits(hb.cpu().numpy()))
+    assert torch.equal(a.kv, b.kv)
+    __import__("spindle_b200").device_status()
