@@ -259,6 +259,14 @@ def run_gpu(args):
         XQ.append([sg.Q8K(c, dev) for _ in range(nvec)])
         OUT.append(torch.empty(nvec, r, device=dev))
     torch.cuda.synchronize()
+    # One vector on TILED16: the step is the list form, the activations' Q8_K
+    # images in one launch (sg_q8k_images) and the 7 GEMVs in one persistent
+    # launch (sg_matvec_list_q8k); otherwise one launch (or two) per matrix.
+    as_list = nvec == 1 and args.layout == "tiled" and args.form == "list"
+    XS = [X[k][0] for k in range(len(SHAPES))]
+    IMGS = sg.q8k_images(XS) if as_list else None
+    EQ = [(W[k], M[k], IMGS[k]) for k in range(len(SHAPES))] if as_list else None
+    OUTS = [OUT[k][0] for k in range(len(SHAPES))]
 
     def gemv(k):
         if args.layout == "tiled":
@@ -267,9 +275,16 @@ def run_gpu(args):
             sg.quantize_into(X[k], XQ[k])
             sg.matmul_rows(W[k], M[k], XQ[k], [OUT[k][b] for b in range(nvec)], 0, M[k].rows)
 
-    def step():
+    def per_matrix():
         for k in range(len(SHAPES)):
             gemv(k)
+
+    def step():
+        if as_list:
+            sg.q8k_images(XS, IMGS)
+            sg.matvec_list_q8k(EQ, OUTS)
+        else:
+            per_matrix()
 
     # Warm-up outside capture (plans, function attributes), then capture.
     stream = torch.cuda.Stream(device=dev)
@@ -281,9 +296,23 @@ def run_gpu(args):
             step()
         g_gemv = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g_gemv, stream=stream):
-            for k in range(len(SHAPES)):
-                gemv(k)
-    launches_per_step = (1 if args.layout == "tiled" else 2) * len(SHAPES)
+            if as_list:
+                sg.matvec_list_q8k(EQ, OUTS)
+            else:
+                per_matrix()
+        g_per = None
+        if as_list:
+            # the same 7 GEMVs one launch per matrix, reported beside the list
+            # form; its outputs must be the list form's bit for bit
+            want = [o.clone() for o in OUTS]
+            per_matrix()
+            torch.cuda.synchronize()
+            if not all(torch.equal(a.view(torch.int32), b.view(torch.int32)) for a, b in zip(want, OUTS)):
+                raise RuntimeError("list form and per-matrix GEMVs differ")
+            g_per = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_per, stream=stream):
+                per_matrix()
+    launches_per_step = 2 if as_list else (1 if args.layout == "tiled" else 2) * len(SHAPES)
 
     def barrier():
         if world > 1:
@@ -339,7 +368,17 @@ def run_gpu(args):
             g_gemv.replay()
         f1.record(stream)
         f1.synchronize()
-        gemv_ms = f0.elapsed_time(f1) / reps  # 7 launches
+        gemv_ms = f0.elapsed_time(f1) / reps  # the list launch, or the 7 launches
+        per_ms = None
+        if g_per is not None:
+            for _ in range(args.warmup):
+                g_per.replay()
+            f0.record(stream)
+            for _ in range(reps):
+                g_per.replay()
+            f1.record(stream)
+            f1.synchronize()
+            per_ms = f0.elapsed_time(f1) / reps
 
         # Per-shape GEMV time: one launch, timed right after the whole sweep
         # has streamed 314 MB through L2, so the matrix is read from HBM.
@@ -469,9 +508,21 @@ def run_gpu(args):
         evs = [torch.cuda.Event() for _ in range(len(SHAPES) + 1)]
         sp, ssp = C.c_void_p(stream.cuda_stream), C.c_void_p(side.cuda_stream)
 
+        if as_list:
+            XE = [XV[k][0] for k in range(len(SHAPES))]
+            IE = sg.q8k_images(XE)
+            EE = [(W[k], M[k], IE[k]) for k in range(len(SHAPES))]
+            OE = [OV[k][0] for k in range(len(SHAPES))]
+
         def e2e_step():
             _lib.check(lib.sg_memcpy_h2d(C.c_void_p(XC.data_ptr()), C.c_void_p(h_x.data_ptr()), h_x.numel() * 4,
                                          sp), "h2d")
+            if as_list:
+                sg.q8k_images(XE, IE)
+                sg.matvec_list_q8k(EE, OE)
+                _lib.check(lib.sg_memcpy_d2h(C.c_void_p(h_o.data_ptr()), C.c_void_p(OC.data_ptr()), OC.numel() * 4,
+                                             sp), "d2h")
+                return
             for i, k in enumerate(order):
                 if args.layout == "tiled":
                     sg.matvec(W[k], M[k], XV[k], OV[k])
@@ -526,10 +577,19 @@ def run_gpu(args):
                              "traffic_source": "profiles/bench_launch_list.md: ncu dram__bytes_read.sum + "
                                                "dram__bytes_write.sum of the same 7 launches (committed capture)",
                              "algorithmic_bytes": gemv_bytes, "peak_source": peak_src,
-                             "kernel": "gemv_tiled_kernel" if args.layout == "tiled" else "gemv_q8k_kernel",
-                             "how": "algorithmic bytes of the 7 GEMV launches / their replayed duration "
-                                    "(CUDA events on the launch stream); traffic = DRAM read + write "
-                                    "of the same 7 launches from the committed ncu launch list"},
+                             "kernel": ("gemv_list_kernel" if as_list else "gemv_tiled_kernel") if args.layout == "tiled"
+                             else "gemv_q8k_kernel",
+                             "how": ("algorithmic bytes of the 7 GEMVs / the replayed duration of the one list "
+                                     "launch" if as_list else "algorithmic bytes of the 7 GEMV launches / their "
+                                     "replayed duration") + " (CUDA events on the launch stream); traffic = DRAM "
+                                    "read + write of the same launches from the committed ncu launch list"},
+                "form": ("list: sg_q8k_images (the 7 activations to Q8_K images, one launch) + sg_matvec_list_q8k "
+                         "(the 7 GEMVs in one persistent launch)") if as_list else "one sg_matvec launch per matrix",
+                "per_matrix_launches": {"us": round(per_ms * 1e3, 2),
+                                        "GB_s": round(gemv_bytes / (per_ms * 1e-3) / 1e9, 1),
+                                        "how": "the same 7 GEMVs as 7 sg_matvec launches (Q8_K quantization fused "
+                                               "in each), replayed; outputs checked equal to the list form's"}
+                if per_ms else None,
                 "per_shape": per_shape,
                 "config1": c1,
                 "nvec_sweep": [dict(e, best_frac=round(max(e["matvec"]["GB_s"], e["matmul_batch"]["GB_s"]) / peak, 4))
@@ -540,14 +600,17 @@ def run_gpu(args):
                                 "clock record (same graph, same bytes per step)"},
                 "e2e": {"value": round(bytes_rank * world / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                        "how": "every step: one sg_memcpy_h2d of all fp32 activations from pinned host, "
-                               "sg_matvec (quantize + GEMV) per matrix, sg_memcpy_d2h of each fp32 output "
-                               "on a side stream as soon as its GEMV ends (overlapping the next GEMVs)"},
+                        "how": ("every step: one sg_memcpy_h2d of all fp32 activations from pinned host, "
+                                "sg_q8k_images, sg_matvec_list_q8k, one sg_memcpy_d2h of all fp32 outputs")
+                        if as_list else
+                               ("every step: one sg_memcpy_h2d of all fp32 activations from pinned host, "
+                                "sg_matvec (quantize + GEMV) per matrix, sg_memcpy_d2h of each fp32 output "
+                                "on a side stream as soon as its GEMV ends (overlapping the next GEMVs)")},
                 "gpu_launches": launches_per_step * args.steps,
                 "clocks": clk.summary()}
     if world > 1:
         dist.barrier()
-        del g_step, g_gemv, g_e2e
+        del g_step, g_gemv, g_e2e, g_per
         dist.destroy_process_group()
     return line, WG
 
@@ -1776,6 +1839,9 @@ def main():
                     help="decode workload: the model architecture")
     ap.add_argument("--gguf", default=None, help="decode workload: load the model from this GGUF file instead")
     ap.add_argument("--chunk", type=int, default=0, help="prefill workload: positions per batch call (default 128)")
+    ap.add_argument("--form", default="list", choices=["list", "per-matrix"],
+                    help="gemv workload, one vector on TILED16: the 7 GEMVs as one list launch (after one Q8_K "
+                         "image launch) or one sg_matvec launch per matrix"),
     ap.add_argument("--overlap", type=int, default=PREFILL_IN_FLIGHT,
                     help="prefill workload: chunks in flight on as many streams, a layer at a time (1: one call per "
                          "chunk on one stream)"),

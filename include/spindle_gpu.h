@@ -149,6 +149,38 @@ SG_API sg_status sg_unpack_tiled16(int32_t dtype, const uint8_t *d_tiled, uint64
 SG_API sg_status sg_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x, uint64_t ldx, float *d_out,
                            uint64_t ldo, uint64_t n_vec, uint64_t r0, uint64_t r1, void *stream);
 
+/* Several matvecs in one launch: entry j computes d_out[j][r] = W_j * x_j for
+ * every row r of mats[j] (TILED16 Q4_K / Q6_K, based at d_base[j]), x_j =
+ * d_x[j] holding cols_j fp32 values (16-byte aligned); d_base, mats, d_x and
+ * d_out are host arrays of n <= SG_LIST_MAX entries.  The entries are
+ * independent (no output may be another entry's input).  One persistent
+ * kernel streams the matrices one after another without a launch boundary
+ * between them (each warp's copies of the next matrix are in flight while it
+ * finishes the current one); every output is bit for bit the one sg_matvec
+ * writes for that entry (smollm_chat.rs:309-318 per entry). */
+#define SG_LIST_MAX 16
+SG_API sg_status sg_matvec_list(const uint8_t *const *d_base, const sg_mat *mats, const float *const *d_x,
+                                float *const *d_out, uint64_t n, void *stream);
+
+/* The same list with Q8_K activations (quant_q8k.rs:255-295 matmul_rows per
+ * entry): entry j reads its vector as a Q8_K image d_img[j] made by
+ * sg_q8k_images (or by any producer writing that layout), staged by one bulk
+ * copy instead of being quantized in every CTA.  Bit for bit sg_matvec_list
+ * on the vectors the images were made from. */
+SG_API sg_status sg_matvec_list_q8k(const uint8_t *const *d_base, const sg_mat *mats, const uint8_t *const *d_img,
+                                    float *const *d_out, uint64_t n, void *stream);
+
+/* Q8_K image of a vector of cols fp32 values (Q8K::quantize, quant_q8k.rs:
+ * 73-121, bit for bit): one buffer of sg_q8k_image_bytes(cols) bytes holding
+ * qs[cols] (int8), then bsums[cols / 16] (int16), then d[cols / 256] (f32,
+ * padded to a multiple of 16 bytes).  sg_q8k_images quantizes n <= SG_LIST_MAX
+ * vectors (d_x[j]: cols[j] values, 16-byte aligned) into d_img[j] (16-byte
+ * aligned) in one launch; host arrays of n entries.  0 for a cols that is not
+ * a multiple of 256 in 256..SG_MAX_COLS. */
+SG_API uint64_t sg_q8k_image_bytes(uint64_t cols);
+SG_API sg_status sg_q8k_images(const float *const *d_x, const uint64_t *cols, uint8_t *const *d_img, uint64_t n,
+                               void *stream);
+
 /* Many vectors at once (matvec_multi, smollm_chat.rs:447-512, over
  * quant_q8k.rs:255-295 matmul_rows): the rows r0..r1 of a TILED16 Q4_K/Q6_K
  * matrix for n_vec <= SG_BATCH_MAX_VEC fp32 vectors (x_b = d_x + b*ldx),

@@ -150,7 +150,55 @@ def matvec(base, m, xs, out=None, r0=0, r1=None, stream=None):
     return out
 
 
-def matvec_scratch(base, m, xs, out=None, r0=0, r1=None, scratch=None, stream=None):
+def matvec_list(entries, outs=None, stream=None):
+    """Several matvecs in one launch (sg_matvec_list): entries is a list of
+    (base, Mat, x) with x an fp32 CUDA vector of Mat.cols values; returns (or
+    fills) one [rows] output per entry, bit for bit matvec's."""
+    n = len(entries)
+    if outs is None:
+        outs = [torch.empty(m.rows, dtype=torch.float32, device=x.device) for _, m, x in entries]
+    for _, m, x in entries:
+        if x.dtype != torch.float32 or not x.is_contiguous():
+            raise ValueError("every x must be a contiguous float32 vector")
+    P = C.c_void_p
+    bases = (P * n)(*[b.data_ptr() for b, _, _ in entries])
+    mats = (_lib.SgMat * n)(*[m.c() for _, m, _ in entries])
+    xs = (P * n)(*[x.data_ptr() for _, _, x in entries])
+    os_ = (P * n)(*[o.data_ptr() for o in outs])
+    _lib.check(lib().sg_matvec_list(bases, mats, xs, os_, n, _stream(stream)), "matvec_list")
+    return outs
+
+
+def q8k_images(xs, imgs=None, stream=None):
+    """Q8_K images of fp32 vectors (sg_q8k_images, one launch): a list of uint8
+    CUDA tensors of sg_q8k_image_bytes(cols) bytes each."""
+    n = len(xs)
+    for x in xs:
+        if x.dtype != torch.float32 or not x.is_contiguous():
+            raise ValueError("every x must be a contiguous float32 vector")
+    if imgs is None:
+        imgs = [torch.empty(lib().sg_q8k_image_bytes(x.numel()), dtype=torch.uint8, device=x.device) for x in xs]
+    P = C.c_void_p
+    _lib.check(lib().sg_q8k_images((P * n)(*[x.data_ptr() for x in xs]), (C.c_uint64 * n)(*[x.numel() for x in xs]),
+                                   (P * n)(*[t.data_ptr() for t in imgs]), n, _stream(stream)), "q8k_images")
+    return imgs
+
+
+def matvec_list_q8k(entries, outs=None, stream=None):
+    """matvec_list on Q8_K images (sg_matvec_list_q8k): entries is a list of
+    (base, Mat, img) with img from q8k_images."""
+    n = len(entries)
+    if outs is None:
+        outs = [torch.empty(m.rows, dtype=torch.float32, device=b.device) for b, m, _ in entries]
+    P = C.c_void_p
+    _lib.check(lib().sg_matvec_list_q8k((P * n)(*[b.data_ptr() for b, _, _ in entries]),
+                                        (_lib.SgMat * n)(*[m.c() for _, m, _ in entries]),
+                                        (P * n)(*[i.data_ptr() for _, _, i in entries]),
+                                        (P * n)(*[o.data_ptr() for o in outs]), n, _stream(stream)), "matvec_list_q8k")
+    return outs
+
+
+
     """matvec for either layout, Q8_K images in caller scratch (a uint8 CUDA
     tensor of at least sg_matvec_scratch_bytes bytes; allocated if None)."""
     single = xs.dim() == 1

@@ -85,6 +85,10 @@ SIGNATURES = {
     "sg_q8k_quantize": (I32, [P, U64, U64, U64, C.POINTER(SgQ8K), P]),
     "sg_matmul_rows": (I32, [P, C.POINTER(SgMat), C.POINTER(SgQ8K), C.POINTER(P), U64, U64, U64, P]),
     "sg_matvec": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
+    "sg_matvec_list": (I32, [C.POINTER(P), C.POINTER(SgMat), C.POINTER(P), C.POINTER(P), U64, P]),
+    "sg_matvec_list_q8k": (I32, [C.POINTER(P), C.POINTER(SgMat), C.POINTER(P), C.POINTER(P), U64, P]),
+    "sg_q8k_image_bytes": (U64, [U64]),
+    "sg_q8k_images": (I32, [C.POINTER(P), C.POINTER(U64), C.POINTER(P), U64, P]),
     "sg_matvec_rows_float": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P]),
     "sg_matmul_batch_scratch_bytes": (U64, [C.POINTER(SgMat), U64]),
     "sg_matmul_batch": (I32, [P, C.POINTER(SgMat), P, U64, P, U64, U64, U64, U64, P, U64, P]),

@@ -1,5 +1,6 @@
 // api.cu — the C ABI of include/spindle_gpu.h: argument checks, launch plans
 // and kernel dispatch.  Host code only; kernels live in the other .cu files.
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
@@ -11,6 +12,7 @@
 
 #include "gemv_q8k.cuh"
 #include "gemv_tiled.cuh"
+#include "gemv_list.cuh"
 #include "kernels.cuh"
 #include "moe.cuh"
 #include "decode.cuh"
@@ -40,6 +42,7 @@ std::atomic<int> g_int_enabled{0};  // 0 = undecided, 1 = on, 2 = off
 struct DevInfo {
     int sms = 0;
     bool attrs_set = false;
+    bool list_attr = false;
 };
 DevInfo g_dev[64];
 std::mutex g_mu;
@@ -1206,6 +1209,170 @@ sg_status sg_matvec(const uint8_t *d_base, const sg_mat *m, const float *d_x, ui
                           r1, (cudaStream_t)stream);
         if (st) return st;
     }
+    return SG_OK;
+}
+
+// ---- a list of GEMVs in one launch --------------------------------------------
+
+// Launch plan of gemv_list_kernel, one 16-warp CTA per SM: per matrix the S of
+// tiled_plan's cost model (S = 2 with 16 warps only where no group gets a
+// second tile: that case would need a 17th named barrier); one ring geometry
+// for the whole list (stages of two columns of the widest type, then smaller
+// until the CTA fits); each matrix's remainder tiles start at the CTA after
+// the last one that took the previous matrix's.
+sg_status list_plan(GlArgs *a, size_t *smem, uint32_t *grid) {
+    DevInfo *di;
+    sg_status st = dev_info(&di);
+    if (st) return st;
+    const uint32_t warps = 16, G = (uint32_t)di->sms;
+    const uint32_t warp_slots = G * warps;
+    const int forced = env_int("SG_LIST_S", 0);  // a fixed S where it is valid (tuning)
+    uint32_t act_max = 0, cb_max = 0, chain = 0;
+    for (uint32_t j = 0; j < a->n; j++) {
+        GlMat &m = a->m[j];
+        const uint32_t nb = m.nb, cb = tiled_col_bytes(m.dt ? 1 : 0);
+        uint32_t S = 1;
+        double best = 1e30;
+        for (uint32_t s = 1; s <= warps && s <= nb; s *= 2) {
+            const uint64_t groups = warp_slots / s;
+            const uint64_t tiles = (m.ntiles + groups - 1) / groups;
+            if (s > 1 && 2 * (warps / s) + 1 > 16 && tiles > 1) continue;
+            if (forced > 0 && s == (uint32_t)forced) {
+                S = s;
+                break;
+            }
+            const double per_tile = (double)((nb + s - 1) / s) + 0.06 * (double)(nb - nb / s) + (s > 1 ? 0.5 : 0.0);
+            const double cost = (double)tiles * per_tile;
+            if (cost < best * 0.98) {
+                best = cost;
+                S = s;
+            }
+        }
+        m.S = S;
+        m.s_log2 = ilog2u(S);
+        m.slot_blocks = (nb + S - 1) / S;
+        const uint32_t step = G * (warps / S);
+        m.tiles_q = m.ntiles / step;
+        m.tiles_r = m.ntiles % step;
+        if (act_bytes(nb) > act_max) act_max = act_bytes(nb);
+        if (cb > cb_max) cb_max = cb;
+        const uint32_t c = list_chain_floats(warps, S, m.slot_blocks);
+        if (c > chain) chain = c;
+    }
+    uint32_t ns = (uint32_t)std::min(std::max(env_int("SG_LIST_STAGES", 2), 2), 4);
+    uint32_t sb = (uint32_t)env_int("SG_LIST_STAGE_BYTES", 0);
+    if (sb < cb_max || sb % 16) sb = 2 * cb_max;
+    const size_t budget = 220 * 1024;
+    for (;;) {
+        *smem = list_smem_bytes(warps, ns, sb, act_max, chain);
+        if (*smem <= budget) break;
+        if (ns > 2)
+            ns--;
+        else if (sb > 2 * 2304u && 2 * 2304u >= cb_max)
+            sb = 2 * 2304u;  // Q4_K two columns a stage, Q6_K one
+        else if (sb > cb_max)
+            sb = cb_max;
+        else
+            return SG_ERR_SHAPE;
+    }
+    const bool rot = env_int("SG_LIST_ROT", 1) != 0;
+    uint32_t cur = 0;
+    for (uint32_t j = 0; j < a->n; j++) {
+        GlMat &m = a->m[j];
+        const uint32_t bc = sb / tiled_col_bytes(m.dt ? 1 : 0);
+        m.bc = bc < m.slot_blocks ? bc : m.slot_blocks;
+        m.rot = rot ? (G - cur) % G : 0u;
+        cur = (cur + m.tiles_r % G) % G;
+    }
+    a->nstages = ns;
+    a->stage_bytes = sb;
+    a->act_bytes = act_max;
+    a->chain_floats = chain;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!di->list_attr) {
+            CK(cudaFuncSetAttribute((const void *)gemv_list_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    227 * 1024));
+            di->list_attr = true;
+        }
+    }
+    *grid = G;
+    return SG_OK;
+}
+
+static_assert(GL_MAX == SG_LIST_MAX, "gemv_list_kernel's list length is the header's");
+
+// One of d_x (fp32 vectors) or d_img (Q8_K images) is given.
+sg_status matvec_list_impl(const uint8_t *const *d_base, const sg_mat *mats, const float *const *d_x,
+                           const uint8_t *const *d_img, float *const *d_out, uint64_t n, void *stream) {
+    if (n == 0) return SG_OK;
+    if (!d_base || !mats || (!d_x && !d_img) || !d_out || n > SG_LIST_MAX) return SG_ERR_INVALID;
+    GlArgs a;
+    memset(&a, 0, sizeof a);
+    uint32_t k = 0;
+    for (uint64_t j = 0; j < n; j++) {
+        const sg_mat *m = &mats[j];
+        int dt;
+        sg_status st = check_mat(d_base[j], m, 0, m->rows, &dt);
+        if (st) return st;
+        if (m->layout != SG_LAYOUT_TILED16 || m->rows > 0xFFFFFFF0ull) return SG_ERR_INVALID;
+        if (m->rows == 0) continue;
+        const void *in = d_x ? (const void *)d_x[j] : (const void *)d_img[j];
+        if (!in || !d_out[j]) return SG_ERR_INVALID;
+        if (!aligned(in, 16) || !aligned(d_out[j], 4)) return SG_ERR_ALIGN;
+        GlMat &g = a.m[k++];
+        g.w = d_base[j] + m->offset;
+        g.x = d_x ? d_x[j] : nullptr;
+        g.img = d_x ? nullptr : d_img[j];
+        g.out = d_out[j];
+        g.dt = dt == DT_Q4K ? 0u : 1u;
+        g.nb = (uint32_t)(m->cols / 256);
+        g.rows = (uint32_t)m->rows;
+        g.ntiles = (uint32_t)((m->rows + TILE_ROWS - 1) / TILE_ROWS);
+    }
+    if (k == 0) return SG_OK;
+    a.n = k;
+    size_t smem;
+    uint32_t grid;
+    sg_status st = list_plan(&a, &smem, &grid);
+    if (st) return st;
+    CK(launch_pdl((const void *)gemv_list_kernel, grid, 16 * 32, smem, (cudaStream_t)stream, &a));
+    return SG_OK;
+}
+
+sg_status sg_matvec_list(const uint8_t *const *d_base, const sg_mat *mats, const float *const *d_x,
+                         float *const *d_out, uint64_t n, void *stream) {
+    return d_x ? matvec_list_impl(d_base, mats, d_x, nullptr, d_out, n, stream) : SG_ERR_INVALID;
+}
+
+sg_status sg_matvec_list_q8k(const uint8_t *const *d_base, const sg_mat *mats, const uint8_t *const *d_img,
+                             float *const *d_out, uint64_t n, void *stream) {
+    return d_img ? matvec_list_impl(d_base, mats, nullptr, d_img, d_out, n, stream) : SG_ERR_INVALID;
+}
+
+uint64_t sg_q8k_image_bytes(uint64_t cols) {
+    if (cols == 0 || cols % 256 || cols > SG_MAX_COLS) return 0;
+    return act_bytes((uint32_t)(cols / 256));
+}
+
+sg_status sg_q8k_images(const float *const *d_x, const uint64_t *cols, uint8_t *const *d_img, uint64_t n,
+                        void *stream) {
+    if (n == 0) return SG_OK;
+    if (!d_x || !cols || !d_img || n > SG_LIST_MAX) return SG_ERR_INVALID;
+    QImgArgs a;
+    memset(&a, 0, sizeof a);
+    a.n = (uint32_t)n;
+    for (uint64_t j = 0; j < n; j++) {
+        if (cols[j] == 0 || cols[j] % 256 || cols[j] > SG_MAX_COLS) return SG_ERR_SHAPE;
+        if (!d_x[j] || !d_img[j]) return SG_ERR_INVALID;
+        if (!aligned(d_x[j], 16) || !aligned(d_img[j], 16)) return SG_ERR_ALIGN;
+        a.x[j] = d_x[j];
+        a.img[j] = d_img[j];
+        a.nb[j] = (uint32_t)(cols[j] / 256);
+        a.blk0[j + 1] = a.blk0[j] + a.nb[j];
+    }
+    const uint32_t warps = a.blk0[n];
+    CK(launch_pdl((const void *)q8k_images_kernel, dim3((warps + 7) / 8), 256, 0, (cudaStream_t)stream, &a));
     return SG_OK;
 }
 
