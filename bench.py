@@ -575,7 +575,7 @@ def run_gpu(args):
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(achieved / peak, 4), "traffic": profiled_traffic(args),
                              "traffic_source": "profiles/bench_launch_list.md: ncu dram__bytes_read.sum + "
-                                               "dram__bytes_write.sum of the same 7 launches (committed capture)",
+                                               "dram__bytes_write.sum of the step's launches (committed capture)",
                              "algorithmic_bytes": gemv_bytes, "peak_source": peak_src,
                              "kernel": ("gemv_list_kernel" if as_list else "gemv_tiled_kernel") if args.layout == "tiled"
                              else "gemv_q8k_kernel",
