@@ -173,7 +173,7 @@ SG_API sg_status sg_matvec_list_q8k(const uint8_t *const *d_base, const sg_mat *
 /* Q8_K image of a vector of cols fp32 values (Q8K::quantize, quant_q8k.rs:
  * 73-121, bit for bit): one buffer of sg_q8k_image_bytes(cols) bytes holding
  * qs[cols] (int8), then bsums[cols / 16] (int16), then d[cols / 256] (f32,
- * padded to a multiple of 16 bytes).  sg_q8k_images quantizes n <= SG_LIST_MAX
+ * padded with zero bytes to a multiple of 16 bytes).  sg_q8k_images quantizes n <= SG_LIST_MAX
  * vectors (d_x[j]: cols[j] values, 16-byte aligned) into d_img[j] (16-byte
  * aligned) in one launch; host arrays of n entries.  0 for a cols that is not
  * a multiple of 256 in 256..SG_MAX_COLS. */

@@ -198,7 +198,7 @@ def matvec_list_q8k(entries, outs=None, stream=None):
     return outs
 
 
-
+def matvec_scratch(base, m, xs, out=None, r0=0, r1=None, scratch=None, stream=None):
     """matvec for either layout, Q8_K images in caller scratch (a uint8 CUDA
     tensor of at least sg_matvec_scratch_bytes bytes; allocated if None)."""
     single = xs.dim() == 1

@@ -337,6 +337,9 @@ __global__ void __launch_bounds__(256) q8k_images_kernel(const __grid_constant__
     q8k_block(a.x[j] + 256u * b, reinterpret_cast<int8_t *>(img + 256u * b),
               reinterpret_cast<int16_t *>(img + 256u * nb + 32u * b), reinterpret_cast<float *>(img + 288u * nb + 4u * b),
               lane);
+    // the padding after d[nb] is zero, so that an image is the same bytes every time
+    const uint32_t pad = (act_bytes(nb) - 292u * nb) / 4u;
+    if (b == nb - 1u && lane < pad) reinterpret_cast<uint32_t *>(img + 292u * nb)[lane] = 0u;
 }
 
 }  // namespace sg

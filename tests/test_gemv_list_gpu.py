@@ -43,6 +43,9 @@ def image_of(q):
 def test_images_match_oracle(dev):
     rng = O.Rng(0x1A6E)
     xs = [rng.fill(-3.0, 3.0, n) for n in (256, 768, 1024, 4096, 14336)]
+    # images land in memory that held other bytes: the padding must still be zero
+    junk = torch.full((1 << 20,), 0x5A, dtype=torch.uint8, device=dev)
+    del junk
     xs[1][5] = 0.0
     xs[2][:256] = 0.0  # an all-zero block
     xs[3][300] = 1e30  # a large value in one block
