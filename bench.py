@@ -401,6 +401,43 @@ def run_gpu(args):
             per_shape.append({"shape": "%s %dx%d" % (NAME[dt], r, c), "us": round(us, 2),
                               "GB_s": round(alg_bytes(dt, r, c, nvec) / (us * 1e-6) / 1e9, 1)})
 
+        # Per shape as a throughput: the shape alone through the list kernel,
+        # over distinct copies that hold 2.5x the L2 (each read from HBM), in
+        # lists of up to 16 on the same Q8_K image.
+        per_shape_list = []
+        if as_list:
+            peak_ = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"] \
+                if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 6650.0
+            for k, (dt, r, c) in enumerate(SHAPES):
+                ncp = max(2, -(-int(2.5 * L2_BYTES) // W[k].numel()))
+                cps = [W[k]] + [W[k].clone() for _ in range(ncp - 1)]
+                o_ = [torch.empty(r, device=dev) for _ in range(min(ncp, 16))]
+                lists = [[(w_, M[k], IMGS[k]) for w_ in cps[i:i + 16]] for i in range(0, ncp, 16)]
+
+                def run_lists():
+                    for L_ in lists:
+                        sg.matvec_list_q8k(L_, o_[:len(L_)])
+
+                run_lists()
+                torch.cuda.synchronize()
+                gl_ = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gl_, stream=stream):
+                    run_lists()
+                for _ in range(3):
+                    gl_.replay()
+                q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                q0.record(stream)
+                for _ in range(10):
+                    gl_.replay()
+                q1.record(stream)
+                q1.synchronize()
+                per = q0.elapsed_time(q1) / 10 / ncp
+                gbs = alg_bytes(dt, r, c, 1) / (per * 1e-3) / 1e9
+                per_shape_list.append({"shape": "%s %dx%d" % (NAME[dt], r, c), "copies": ncp,
+                                       "launches": len(lists), "us_per_matrix": round(per * 1e3, 2),
+                                       "GB_s": round(gbs, 1), "frac": round(gbs / peak_, 4)})
+                del gl_, cps, o_, lists
+
         # one Q4_K 3072 x 1024 GEMV (1.78 MB).  Its
         # single-launch latency, read from HBM after the sweep has evicted it,
         # and a chain of launches over copies that hold 2.5x the L2 (each read
@@ -591,6 +628,10 @@ def run_gpu(args):
                                                "in each), replayed; outputs checked equal to the list form's"}
                 if per_ms else None,
                 "per_shape": per_shape,
+                "per_shape_list": {"entries": per_shape_list,
+                                   "how": "each shape alone: distinct copies holding 2.5x the L2, as lists of up "
+                                          "to 16 GEMVs (sg_matvec_list_q8k) on one Q8_K image, replayed; "
+                                          "per matrix = time / copies"} if per_shape_list else None,
                 "config1": c1,
                 "nvec_sweep": [dict(e, best_frac=round(max(e["matvec"]["GB_s"], e["matmul_batch"]["GB_s"]) / peak, 4))
                                for e in nvec_sweep],
