@@ -351,9 +351,33 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
         if (nv_inst > 1) moe_nact *= nv_inst;  // jobs: nv images per unit
     }
     const uint32_t job_bytes = mode >= IN_MOE_X && nv_inst > 1 ? tiled_job_bytes(nv_inst) : 0u;
+    const size_t budget = warps == 16 ? 220 * 1024 : 110 * 1024;
+    // Several vectors (plain GEMV): the chain scratch grows with the vector
+    // count, and a smaller S makes it larger per slot, so every S is tried
+    // with the rings shrunk to fit, and the cheapest that fits is taken (the
+    // loop below would fall back to S = 1 for long rows: 56 super-blocks on
+    // one warp per tile).
+    if (mode < IN_MOE_X && nv_inst > 1 && !(forced == 1 || forced == 2 || forced == 4 || forced == 8 || forced == 16)) {
+        double best = 1e30;
+        uint32_t bestS = 0;
+        for (uint32_t s = 1; s <= warps && s <= nb; s *= 2) {
+            const uint32_t sbk = (nb + s - 1) / s;
+            bool fits = false;
+            for (uint32_t b = bc < sbk ? bc : sbk; b >= 1 && !fits; b--)
+                fits = tiled_smem_bytes(warps, s, 2, b * cb, sbk, nv_inst, nb, nv_inst, 0) <= budget;
+            if (!fits) continue;
+            const uint64_t groups = warp_slots / s;
+            const uint64_t tiles = (ntiles + groups - 1) / groups;
+            const double cost = (double)tiles * ((double)sbk + 0.06 * (double)(nb - nb / s) + (s > 1 ? 0.5 : 0.0));
+            if (cost < best * 0.98) {
+                best = cost;
+                bestS = s;
+            }
+        }
+        if (bestS) S = bestS;
+    }
     // Fit the CTA in shared memory: fewer stages, then smaller stages, then
     // fewer warps per tile (less chain scratch).
-    const size_t budget = warps == 16 ? 220 * 1024 : 110 * 1024;
     for (;;) {
         p->S = S;
         p->slot_blocks = (nb + S - 1) / S;
