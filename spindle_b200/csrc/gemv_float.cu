@@ -43,6 +43,25 @@ __device__ __forceinline__ void stage_row(const uint8_t *rp, uint8_t *dst, uint3
         if (l + 8u * p < pieces) reinterpret_cast<uint4 *>(dst)[l + 8u * p] = v[p];
 }
 
+// The same as asynchronous copies (cp.async, 16 bytes each, L2 only), so
+// that a row's next span lands while the current one is used: the issuing
+// thread's copies are complete after cp_wait<N> (N later groups may still be
+// in flight), and a __syncwarp then shows them to the row's other threads.
+template <int P>
+__device__ __forceinline__ void stage_row_async(const uint8_t *rp, uint8_t *dst, uint32_t pieces, uint32_t l) {
+#pragma unroll
+    for (int p = 0; p < P; p++)
+        if (l + 8u * p < pieces)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst + 16u * (l + 8u * p))),
+                         "l"(rp + 16u * (l + 8u * p))
+                         : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // x: global memory or the CTA's shared copy (a generic load serves both)
 __device__ __forceinline__ float xld(const float *p) { return *p; }
 
@@ -89,7 +108,7 @@ __device__ __forceinline__ float wload(const uint8_t *row, uint32_t j) {
 }  // namespace
 
 template <int DT, int NV, bool MULTI>
-__global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_constant__ FGemvArgs a) {
+__global__ void __launch_bounds__(FGEMV_THREADS, NV == 1 && !MULTI ? 3 : 1) gemv_float_kernel(const __grid_constant__ FGemvArgs a) {
     extern __shared__ __align__(16) float fsums[];
     grid_dependency_wait();
     const uint32_t l = threadIdx.x & 7u, n = a.n, nv = a.nvec;
@@ -125,38 +144,40 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
             // of one of F32), QS spans at a time, into this warp's part of
             // shared memory; lane l then reads elements l, l+8, ... of each
             // span from there, so the FMA chain is unchanged.
+            // (two buffers of QS spans: the next QS spans are copied in
+            // asynchronously while the current ones are used)
             constexpr uint32_t EB = DT == FDT_F32 ? 4u : 2u, SPAN_B = 64u * EB, RSTR = SPAN_B + 16u,
-                           QS = NV == 1 && DT == FDT_F16 ? 8u : NV <= 2 ? 4u : 1u;
-            __shared__ __align__(16) uint8_t wsm[FGEMV_THREADS / 32][QS][4][RSTR];
+                           QS = NV <= 2 ? (DT == FDT_F16 ? 4u : 2u) : 1u;
+            __shared__ __align__(16) uint8_t wsm[2][FGEMV_THREADS / 32][QS][4][RSTR];
             const bool vec = ((reinterpret_cast<uintptr_t>(a.w) | a.row_bytes) & 15u) == 0;
             if (vec) {
-                const uint32_t rw = (threadIdx.x >> 3) & 3u, wp = threadIdx.x >> 5;
-                for (; i + 8 * QS <= steps; i += 8 * QS) {
-                    uint4 v[QS][SPAN_B / 128];
+                const uint32_t rw = (threadIdx.x >> 3) & 3u, wp = threadIdx.x >> 5, nit = steps / (8 * QS);
+                auto issue = [&](uint32_t it) {
+                    if (it < nit)
 #pragma unroll
-                    for (uint32_t u = 0; u < QS; u++)
-#pragma unroll
-                        for (uint32_t p = 0; p < SPAN_B / 128; p++)
-                            v[u][p] = __ldg(reinterpret_cast<const uint4 *>(rp + (uint64_t)(8 * i + 64 * u) * EB +
-                                                                             128 * p + 16 * l));
+                        for (uint32_t u = 0; u < QS; u++)
+                            stage_row_async<SPAN_B / 128>(rp + (uint64_t)(64 * QS * it + 64 * u) * EB,
+                                                          &wsm[it & 1u][wp][u][rw][0], SPAN_B / 16, l);
+                    cp_commit();
+                };
+                issue(0);
+                for (uint32_t it = 0; it < nit; it++, i += 8 * QS) {
+                    issue(it + 1);
+                    cp_wait<1>();
                     __syncwarp();
-#pragma unroll
-                    for (uint32_t u = 0; u < QS; u++)
-#pragma unroll
-                        for (uint32_t p = 0; p < SPAN_B / 128; p++)
-                            *reinterpret_cast<uint4 *>(&wsm[wp][u][rw][128 * p + 16 * l]) = v[u][p];
-                    __syncwarp();
+                    const uint32_t bf = it & 1u;
 #pragma unroll
                     for (uint32_t u = 0; u < QS; u++)
 #pragma unroll
                         for (uint32_t j = 0; j < 8; j++) {
                             const uint32_t e = 8 * j + l;  // element of the span
-                            const float w = DT == FDT_F32 ? *reinterpret_cast<const float *>(&wsm[wp][u][rw][4 * e])
-                                                          : h2f(*reinterpret_cast<const unsigned short *>(&wsm[wp][u][rw][2 * e]));
+                            const float w = DT == FDT_F32 ? *reinterpret_cast<const float *>(&wsm[bf][wp][u][rw][4 * e])
+                                                          : h2f(*reinterpret_cast<const unsigned short *>(&wsm[bf][wp][u][rw][2 * e]));
 #pragma unroll
                             for (int b = 0; b < NV; b++)
                                 if ((uint32_t)b < nv) acc[b] = __fmaf_rn(w, xld(xv[b] + 8 * (i + 8 * u + j) + l), acc[b]);
                         }
+                    __syncwarp();  // done with this buffer before it is refilled
                 }
             }
             for (; i + U <= steps; i += U) {
@@ -225,17 +246,28 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
         uint32_t k = 0;
         // 16-byte aligned rows: spans of 8 blocks (272 bytes = 17 pieces), two
         // at a time, staged through this warp's part of shared memory
+        // (two buffers: the next two spans are copied in asynchronously
+        // while the current two are used)
         constexpr uint32_t KB = 8, SB = KB * 34, SP = SB / 16;
-        __shared__ __align__(16) uint8_t qsm[FGEMV_THREADS / 32][2][4][SB + 16];
+        __shared__ __align__(16) uint8_t qsm[2][FGEMV_THREADS / 32][2][4][SB + 16];
         if (((reinterpret_cast<uintptr_t>(a.w) | a.row_bytes) & 15u) == 0) {
-            const uint32_t rw = (threadIdx.x >> 3) & 3u, wp = threadIdx.x >> 5;
-            for (; k + 2 * KB <= nbk; k += 2 * KB) {
-                __syncwarp();
-                stage_row<3>(rp + 34 * k, qsm[wp][0][rw], SP, l);
-                stage_row<3>(rp + 34 * (k + KB), qsm[wp][1][rw], SP, l);
+            const uint32_t rw = (threadIdx.x >> 3) & 3u, wp = threadIdx.x >> 5, nit = nbk / (2 * KB);
+            auto issue = [&](uint32_t it) {
+                if (it < nit) {
+                    stage_row_async<3>(rp + 34 * (2 * KB * it), qsm[it & 1u][wp][0][rw], SP, l);
+                    stage_row_async<3>(rp + 34 * (2 * KB * it + KB), qsm[it & 1u][wp][1][rw], SP, l);
+                }
+                cp_commit();
+            };
+            issue(0);
+            for (uint32_t it = 0; it < nit; it++, k += 2 * KB) {
+                issue(it + 1);
+                cp_wait<1>();
                 __syncwarp();
 #pragma unroll 4
-                for (uint32_t kk = 0; kk < 2 * KB; kk++) q8_block(&qsm[wp][kk / KB][rw][34 * (kk % KB)], k + kk);
+                for (uint32_t kk = 0; kk < 2 * KB; kk++)
+                    q8_block(&qsm[it & 1u][wp][kk / KB][rw][34 * (kk % KB)], k + kk);
+                __syncwarp();  // done with this buffer before it is refilled
             }
         }
         for (; k < nbk; k++) q8_block(rp + k * 34, k);
@@ -326,16 +358,24 @@ __global__ void __launch_bounds__(FGEMV_THREADS) gemv_float_kernel(const __grid_
         uint32_t k = 0;
         // 16-byte aligned rows: spans of 4 blocks (576 bytes = 36 pieces)
         // staged through this warp's part of shared memory
+        // (two buffers: the next span is copied in asynchronously while the
+        // current one is used)
         constexpr uint32_t KB = 4, SB = KB * 144, SP = SB / 16;
-        __shared__ __align__(16) uint8_t qsm[FGEMV_THREADS / 32][4][SB + 16];  // padded: rows on other banks
+        __shared__ __align__(16) uint8_t qsm[2][FGEMV_THREADS / 32][4][SB + 16];  // padded: rows on other banks
         if (((reinterpret_cast<uintptr_t>(a.w) | a.row_bytes) & 15u) == 0) {
-            const uint32_t rw = (threadIdx.x >> 3) & 3u, wp = threadIdx.x >> 5;
-            for (; k + KB <= nbk; k += KB) {
-                __syncwarp();
-                stage_row<5>(rp + 144 * k, qsm[wp][rw], SP, l);
+            const uint32_t rw = (threadIdx.x >> 3) & 3u, wp = threadIdx.x >> 5, nit = nbk / KB;
+            auto issue = [&](uint32_t it) {
+                if (it < nit) stage_row_async<5>(rp + 144 * (KB * it), qsm[it & 1u][wp][rw], SP, l);
+                cp_commit();
+            };
+            issue(0);
+            for (uint32_t it = 0; it < nit; it++, k += KB) {
+                issue(it + 1);
+                cp_wait<1>();
                 __syncwarp();
 #pragma unroll 2
-                for (uint32_t kk = 0; kk < KB; kk++) q4_block(&qsm[wp][rw][144 * kk], k + kk);
+                for (uint32_t kk = 0; kk < KB; kk++) q4_block(&qsm[it & 1u][wp][rw][144 * kk], k + kk);
+                __syncwarp();  // done with this buffer before it is refilled
             }
         }
         for (; k < nbk; k++) q4_block(rp + k * 144, k);
