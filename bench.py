@@ -1131,6 +1131,43 @@ def run_gpu_tp(args, metric=None):
         copies.append(cs)
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(device=dev)
+    # One vector: the list form, as on one GPU: the activations' Q8_K images
+    # (every rank, all of x) and one gemv_list_kernel launch over this rank's
+    # seven shards into one local buffer, then one NCCL all-gather of those
+    # buffers (north_star's "row split with an NCCL all-gather"): every rank
+    # ends with every matrix's whole output, as rank-major shard blocks.  The
+    # fused form (one sg_matvec_tp per matrix, the gather done by peer stores
+    # in the GEMV kernel) is timed beside it.
+    from spindle_b200.tp import shard_rows
+    as_list = nvec == 1 and args.form == "list" and world > 1
+    if as_list:
+        maxrows = [max(shard_rows(r, world, q)[1] - shard_rows(r, world, q)[0] for q in range(world))
+                   for _, r, _ in SHAPES]
+        loff = [sum(maxrows[:k]) for k in range(len(SHAPES))]
+        chunk = -(-sum(maxrows) // 64) * 64
+        LO = torch.zeros(chunk, device=dev)
+        GA = torch.empty(world * chunk, device=dev)
+        OL = [LO[loff[k]:loff[k] + (shards[k].r1 - shards[k].r0)] for k in range(len(SHAPES))]
+        XS = [X[k][0] for k in range(len(SHAPES))]
+        IMGS = sg.q8k_images(XS)
+        EQ = [[(copies[c][k].w, copies[c][k].m, IMGS[k]) for k in range(len(SHAPES))] for c in range(ncopies)]
+        # the list form's rows equal the fused form's, bit for bit (checked once)
+        for k in range(len(SHAPES)):
+            matvec_tp(shards[k], X[k], grp, BUF[k], stream=stream)
+        with torch.cuda.stream(stream):
+            sg.q8k_images(XS, IMGS)
+            sg.matvec_list_q8k(EQ[0], OL)
+            dist.all_gather_into_tensor(GA, LO)
+        torch.cuda.synchronize()
+        for k, (_, r, _) in enumerate(SHAPES):
+            got = torch.cat([GA[q * chunk + loff[k]:q * chunk + loff[k] + shard_rows(r, world, q)[1]
+                                - shard_rows(r, world, q)[0]] for q in range(world)])
+            if not torch.equal(got.view(torch.int32), BUF[k].tensor.reshape(-1)[:r].view(torch.int32)):
+                raise RuntimeError("list form and fused row-split GEMVs differ (matrix %d)" % k)
+
+    def list_part(c=0):
+        sg.q8k_images(XS, IMGS)
+        sg.matvec_list_q8k(EQ[c], OL)
 
     def step(c=0):
         for k in range(len(SHAPES)):
@@ -1158,18 +1195,46 @@ def run_gpu_tp(args, metric=None):
             with torch.cuda.graph(g, stream=stream):
                 step(c)
             g_steps.append(g)
-        for i in range(args.warmup):
-            g_steps[i % ncopies].replay()
+        g_lists = []
+        if as_list:
+            for c in range(ncopies):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    list_part(c)
+                g_lists.append(g)
+
+        def run_steps(n, start=0):
+            # the list form: the graph of images + list, then the collective
+            # (issued eagerly on the same stream, never inside a graph)
+            for i in range(start, start + n):
+                if as_list:
+                    g_lists[i % ncopies].replay()
+                    dist.all_gather_into_tensor(GA, LO)
+                else:
+                    g_steps[i % ncopies].replay()
+
+        run_steps(args.warmup)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local) as clk:
+            e0.record(stream)
+            run_steps(args.steps)
+            e1.record(stream)
+            e1.synchronize()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+        fused_ms = None
+        if as_list:
+            for i in range(args.warmup):
+                g_steps[i % ncopies].replay()
+            barrier()
             e0.record(stream)
             for i in range(args.steps):
                 g_steps[i % ncopies].replay()
             e1.record(stream)
             e1.synchronize()
-        barrier()
-        ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+            barrier()
+            fused_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
         # e2e: the step's activations from pinned host in one copy, the seven
         # calls, the whole outputs back (every rank holds them; rank 0's count)
         xsz = [nvec * c for _, _, c in SHAPES]
@@ -1184,9 +1249,19 @@ def run_gpu_tp(args, metric=None):
             off += xsz[k]
         sp = C.c_void_p(stream.cuda_stream)
 
+        if as_list:
+            XE = [XV[k][0] for k in range(len(SHAPES))]
+            IE = sg.q8k_images(XE)
+            EE = [[(copies[c][k].w, copies[c][k].m, IE[k]) for k in range(len(SHAPES))] for c in range(ncopies)]
+            h_ga = torch.empty(GA.numel(), dtype=torch.float32).pin_memory()
+
         def e2e_step(c=0):
             _lib.check(lib.sg_memcpy_h2d(C.c_void_p(XC.data_ptr()), C.c_void_p(h_x.data_ptr()), h_x.numel() * 4,
                                          sp), "h2d")
+            if as_list:
+                sg.q8k_images(XE, IE)
+                sg.matvec_list_q8k(EE[c], OL)
+                return
             o = 0
             for k in range(len(SHAPES)):
                 matvec_tp(copies[c][k], XV[k], grp, BUF[k], stream=stream)
@@ -1202,14 +1277,23 @@ def run_gpu_tp(args, metric=None):
             with torch.cuda.graph(g, stream=stream):
                 e2e_step(c)
             g_e2es.append(g)
-        for i in range(args.warmup):
-            g_e2es[i % ncopies].replay()
+
+        def run_e2e(n):
+            # the list form: after the graph (inputs up, images, list), the
+            # collective, then the gathered outputs back to the host
+            for i in range(n):
+                g_e2es[i % ncopies].replay()
+                if as_list:
+                    dist.all_gather_into_tensor(GA, LO)
+                    _lib.check(lib.sg_memcpy_d2h(C.c_void_p(h_ga.data_ptr()), C.c_void_p(GA.data_ptr()),
+                                                 GA.numel() * 4, sp), "d2h")
+
+        run_e2e(args.warmup)
         barrier()
         reps = max(3, min(args.steps, 2000))
         b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         b0.record(stream)
-        for i in range(reps):
-            g_e2es[i % ncopies].replay()
+        run_e2e(reps)
         b1.record(stream)
         b1.synchronize()
         barrier()
@@ -1232,25 +1316,36 @@ def run_gpu_tp(args, metric=None):
                 "vs_baseline": None, "dtype": "int8 x int4/int6 -> int32, fp32 epilogue", "data": "synthetic",
                 "config": dict(config_block(args, world),
                                workload=("gemv_sweep_n%d" if metric else "gemv_tp_sweep_n%d") % nvec,
-                               parallelism="row-split x%d (strong), gather fused (peer stores)" % world,
+                               parallelism=("row-split x%d (strong): images + one list launch over the rank's "
+                                            "shards, then one NCCL all-gather" % world) if as_list else
+                               "row-split x%d (strong), gather fused (peer stores)" % world,
                                global_batch=nvec,
                                l2="%d copies of this rank's %.1f MB of shards, cycled step by step (%.0f MB > "
                                   "2.5 x the 126 MB L2): every matrix is read from HBM"
                                   % (ncopies, shard_bytes / 1e6, ncopies * shard_bytes / 1e6)),
                 "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(per_gpu / peak, 4), "traffic": None, "peak_source": peak_src,
-                             "kernel": "gemv_tiled_kernel (row-split, peer-store epilogue)",
+                             "kernel": "gemv_list_kernel over the rank's shards (+ NCCL all-gather)" if as_list
+                             else "gemv_tiled_kernel (row-split, peer-store epilogue)",
                              "nvlink_bytes_out_per_rank": nvl,
                              "how": "per GPU: the step's algorithmic bytes / n_gpus / step time; the rows each rank "
                                     "sends over NVLink are nvlink_bytes_out_per_rank (770 GB/s measured per "
                                     "direction makes that term small next to HBM)"},
                 "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                        "h2d_bytes_per_step": h_x.numel() * 4, "d2h_bytes_per_step": h_o.numel() * 4,
-                        "how": "every step: one sg_memcpy_h2d of all activations from pinned host, sg_matvec_tp per "
-                               "matrix, sg_memcpy_d2h of each whole output"},
-                "gpu_launches": len(SHAPES) * args.steps,
+                        "h2d_bytes_per_step": h_x.numel() * 4,
+                        "d2h_bytes_per_step": (GA.numel() if as_list else h_o.numel()) * 4,
+                        "how": ("every step: one sg_memcpy_h2d of all activations from pinned host, "
+                                "sg_q8k_images, sg_matvec_list_q8k on the rank's shards, the NCCL all-gather, one "
+                                "sg_memcpy_d2h of the gathered outputs") if as_list else
+                               ("every step: one sg_memcpy_h2d of all activations from pinned host, sg_matvec_tp per "
+                                "matrix, sg_memcpy_d2h of each whole output")},
+                "fused_row_split": {"us": round(fused_ms * 1e3, 2), "GB_s": round(total / (fused_ms * 1e-3) / 1e9, 1),
+                                    "how": "the same sweep as one sg_matvec_tp per matrix (gather fused by peer "
+                                           "stores, no NCCL call), replayed; its rows checked equal to the list "
+                                           "form's"} if fused_ms else None,
+                "gpu_launches": (2 if as_list else len(SHAPES)) * args.steps,
                 "clocks": clk.summary()}
-    del g_steps, g_e2es, g
+    del g_steps, g_e2es, g, g_lists
     grp.close()
     if world > 1:
         dist.destroy_process_group()
