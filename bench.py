@@ -1138,36 +1138,26 @@ def run_gpu_tp(args, metric=None):
     # ends with every matrix's whole output, as rank-major shard blocks.  The
     # fused form (one sg_matvec_tp per matrix, the gather done by peer stores
     # in the GEMV kernel) is timed beside it.
-    from spindle_b200.tp import shard_rows
+    from spindle_b200.tp import ListTp, matvec_list_tp
     as_list = nvec == 1 and args.form == "list" and world > 1
     if as_list:
-        maxrows = [max(shard_rows(r, world, q)[1] - shard_rows(r, world, q)[0] for q in range(world))
-                   for _, r, _ in SHAPES]
-        loff = [sum(maxrows[:k]) for k in range(len(SHAPES))]
-        chunk = -(-sum(maxrows) // 64) * 64
-        LO = torch.zeros(chunk, device=dev)
-        GA = torch.empty(world * chunk, device=dev)
-        OL = [LO[loff[k]:loff[k] + (shards[k].r1 - shards[k].r0)] for k in range(len(SHAPES))]
+        lts = [ListTp(copies[c], world, dev) for c in range(ncopies)]
         XS = [X[k][0] for k in range(len(SHAPES))]
         IMGS = sg.q8k_images(XS)
-        EQ = [[(copies[c][k].w, copies[c][k].m, IMGS[k]) for k in range(len(SHAPES))] for c in range(ncopies)]
         # the list form's rows equal the fused form's, bit for bit (checked once)
         for k in range(len(SHAPES)):
             matvec_tp(shards[k], X[k], grp, BUF[k], stream=stream)
         with torch.cuda.stream(stream):
             sg.q8k_images(XS, IMGS)
-            sg.matvec_list_q8k(EQ[0], OL)
-            dist.all_gather_into_tensor(GA, LO)
+            matvec_list_tp(lts[0], IMGS)
         torch.cuda.synchronize()
-        for k, (_, r, _) in enumerate(SHAPES):
-            got = torch.cat([GA[q * chunk + loff[k]:q * chunk + loff[k] + shard_rows(r, world, q)[1]
-                                - shard_rows(r, world, q)[0]] for q in range(world)])
-            if not torch.equal(got.view(torch.int32), BUF[k].tensor.reshape(-1)[:r].view(torch.int32)):
+        for k, got in enumerate(lts[0].outputs()):
+            if not torch.equal(got.view(torch.int32), BUF[k].tensor.reshape(-1)[:got.numel()].view(torch.int32)):
                 raise RuntimeError("list form and fused row-split GEMVs differ (matrix %d)" % k)
 
     def list_part(c=0):
         sg.q8k_images(XS, IMGS)
-        sg.matvec_list_q8k(EQ[c], OL)
+        matvec_list_tp(lts[c], IMGS, gather=False)
 
     def step(c=0):
         for k in range(len(SHAPES)):
@@ -1209,7 +1199,7 @@ def run_gpu_tp(args, metric=None):
             for i in range(start, start + n):
                 if as_list:
                     g_lists[i % ncopies].replay()
-                    dist.all_gather_into_tensor(GA, LO)
+                    lts[i % ncopies].gather()
                 else:
                     g_steps[i % ncopies].replay()
 
@@ -1252,15 +1242,14 @@ def run_gpu_tp(args, metric=None):
         if as_list:
             XE = [XV[k][0] for k in range(len(SHAPES))]
             IE = sg.q8k_images(XE)
-            EE = [[(copies[c][k].w, copies[c][k].m, IE[k]) for k in range(len(SHAPES))] for c in range(ncopies)]
-            h_ga = torch.empty(GA.numel(), dtype=torch.float32).pin_memory()
+            h_ga = torch.empty(lts[0].gathered.numel(), dtype=torch.float32).pin_memory()
 
         def e2e_step(c=0):
             _lib.check(lib.sg_memcpy_h2d(C.c_void_p(XC.data_ptr()), C.c_void_p(h_x.data_ptr()), h_x.numel() * 4,
                                          sp), "h2d")
             if as_list:
                 sg.q8k_images(XE, IE)
-                sg.matvec_list_q8k(EE[c], OL)
+                matvec_list_tp(lts[c], IE, gather=False)
                 return
             o = 0
             for k in range(len(SHAPES)):
@@ -1284,9 +1273,10 @@ def run_gpu_tp(args, metric=None):
             for i in range(n):
                 g_e2es[i % ncopies].replay()
                 if as_list:
-                    dist.all_gather_into_tensor(GA, LO)
-                    _lib.check(lib.sg_memcpy_d2h(C.c_void_p(h_ga.data_ptr()), C.c_void_p(GA.data_ptr()),
-                                                 GA.numel() * 4, sp), "d2h")
+                    lt = lts[i % ncopies]
+                    lt.gather()
+                    _lib.check(lib.sg_memcpy_d2h(C.c_void_p(h_ga.data_ptr()), C.c_void_p(lt.gathered.data_ptr()),
+                                                 lt.gathered.numel() * 4, sp), "d2h")
 
         run_e2e(args.warmup)
         barrier()
@@ -1333,7 +1323,7 @@ def run_gpu_tp(args, metric=None):
                                     "direction makes that term small next to HBM)"},
                 "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                         "h2d_bytes_per_step": h_x.numel() * 4,
-                        "d2h_bytes_per_step": (GA.numel() if as_list else h_o.numel()) * 4,
+                        "d2h_bytes_per_step": (lts[0].gathered.numel() if as_list else h_o.numel()) * 4,
                         "how": ("every step: one sg_memcpy_h2d of all activations from pinned host, "
                                 "sg_q8k_images, sg_matvec_list_q8k on the rank's shards, the NCCL all-gather, one "
                                 "sg_memcpy_d2h of the gathered outputs") if as_list else

@@ -154,6 +154,75 @@ def matvec_tp(shard, xs, grp, buf, stream=None):
     return out
 
 
+def gather_layout(rows, n_ranks):
+    """Where every rank's shard outputs sit in a row-split list's all-gather
+    (matvec_list_tp): each rank's block holds matrix j's shard rows at
+    offset off[j], with room for the largest shard of j over the ranks, so
+    that all blocks have the same size, chunk floats (a multiple of 64).
+    rows: the matrices' full row counts.  Returns (off, chunk)."""
+    maxrows = [max(b - a for a, b in (shard_rows(r, n_ranks, q) for q in range(n_ranks))) for r in rows]
+    off = [sum(maxrows[:j]) for j in range(len(rows))]
+    return off, -(-sum(maxrows) // 64) * 64
+
+
+def split_gathered(gathered, rows, n_ranks, off, chunk):
+    """Matrix j's whole output, rows in order, from the all-gathered blocks
+    of a row-split list (rank q's block at q * chunk): one tensor per matrix."""
+    outs = []
+    for j, r in enumerate(rows):
+        parts = []
+        for q in range(n_ranks):
+            a, b = shard_rows(r, n_ranks, q)
+            parts.append(gathered[q * chunk + off[j]:q * chunk + off[j] + (b - a)])
+        outs.append(torch.cat(parts))
+    return outs
+
+
+class ListTp:
+    """A row-split list of independent matvecs: this rank's shards
+    (ShardedMatrix, up to SG_LIST_MAX of them), one local block of their
+    outputs and the buffer the blocks are all-gathered into (layout of
+    gather_layout)."""
+
+    def __init__(self, shards, n_ranks, device):
+        self.shards, self.n_ranks = list(shards), n_ranks
+        self.rows = [sh.rows for sh in self.shards]
+        self.off, self.chunk = gather_layout(self.rows, n_ranks)
+        self.local = torch.zeros(self.chunk, dtype=torch.float32, device=device)
+        self.gathered = torch.empty(n_ranks * self.chunk, dtype=torch.float32, device=device)
+        self.outs = [self.local[o:o + sh.r1 - sh.r0] for o, sh in zip(self.off, self.shards)]
+
+    def gather(self, group=None):
+        """The NCCL all-gather of the ranks' blocks (on torch's current stream)."""
+        import torch.distributed as dist
+        if _dist_on():
+            dist.all_gather_into_tensor(self.gathered, self.local, group=group)
+        else:
+            self.gathered.copy_(self.local)
+
+    def outputs(self):
+        """Every matrix's whole output (copies taken from the gathered buffer)."""
+        return split_gathered(self.gathered, self.rows, self.n_ranks, self.off, self.chunk)
+
+
+def matvec_list_tp(lt, imgs, group=None, stream=None, gather=True):
+    """Row-split matvecs of a list on every rank: sg_matvec_list_q8k over this
+    rank's shards (imgs: the vectors' Q8_K images, sg.q8k_images, the same on
+    every rank) into lt.local, then (gather=True) one all-gather of the
+    blocks: afterwards lt.gathered holds every matrix's whole output on every
+    rank (lt.outputs() for them in row order).  The rows are bit for bit
+    those of matvec_tp and of one-GPU sg_matvec."""
+    from . import matvec_list_q8k
+    matvec_list_q8k([(sh.w, sh.m, im) for sh, im in zip(lt.shards, imgs)], lt.outs, stream=stream)
+    if gather:
+        if stream is None:
+            lt.gather(group)
+        else:
+            with torch.cuda.stream(stream):
+                lt.gather(group)
+    return lt.gathered
+
+
 class EpMoe:
     """This rank's part of an expert-parallel MoE layer (sg_moe_forward_batch_ep).
 

@@ -1,5 +1,6 @@
 """Host logic of the row-split tensor parallelism (spindle_b200.tp) on CPU:
-the shard split and the rank-ordered exchange, over gloo with two ranks."""
+the shard split, the rank-ordered exchange and the gather layout of the
+row-split list (gather_layout / split_gathered), over gloo with two ranks."""
 import os
 import socket
 import sys

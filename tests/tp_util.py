@@ -22,7 +22,8 @@ def init(rank, world, port, backend):
 
 
 def cpu_rank(rank, world, port, out):
-    # host logic only: the shard split and the rank-ordered exchange
+    # host logic only: the shard split, the rank-ordered exchange and the
+    # row-split list's gather layout
     import torch.distributed as dist
     from spindle_b200.tp import exchange, shard_rows
     init(rank, world, port, "gloo")
@@ -33,6 +34,23 @@ def cpu_rank(rank, world, port, out):
             parts = exchange(shard_rows(rows, world, rank), None)
             assert parts[0][0] == 0 and parts[-1][1] == rows
             assert all(parts[q][1] == parts[q + 1][0] for q in range(world - 1))
+        # the row-split list's gather layout: blocks of equal size, each
+        # matrix's shard at its offset, reassembled in row order
+        import torch
+        from spindle_b200.tp import gather_layout, split_gathered
+        rows = [1, 7, 16, 1000, 4096, 151936, 33]
+        off, chunk = gather_layout(rows, world)
+        assert chunk % 64 == 0 and chunk >= off[-1] + max(b - a for a, b in
+                                                          (shard_rows(rows[-1], world, q) for q in range(world)))
+        local = torch.full((chunk,), -1.0)
+        for j, r in enumerate(rows):
+            a, b = shard_rows(r, world, rank)
+            local[off[j]:off[j] + b - a] = torch.arange(a, b, dtype=torch.float32) + 1e6 * j
+        blocks = [torch.empty(chunk) for _ in range(world)]
+        dist.all_gather(blocks, local)
+        outs = split_gathered(torch.cat(blocks), rows, world, off, chunk)
+        for j, r in enumerate(rows):
+            assert torch.equal(outs[j], torch.arange(r, dtype=torch.float32) + 1e6 * j), j
         out.put((rank, "ok"))
     except Exception as e:  # reported to the parent
         out.put((rank, repr(e)))
