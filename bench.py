@@ -1134,7 +1134,7 @@ def run_gpu_tp(args, metric=None):
     # One vector: the list form, as on one GPU: the activations' Q8_K images
     # (every rank, all of x) and one gemv_list_kernel launch over this rank's
     # seven shards into one local buffer, then one NCCL all-gather of those
-    # buffers (north_star's "row split with an NCCL all-gather"): every rank
+    # buffers (the benchmark's row split followed by an all-gather): every rank
     # ends with every matrix's whole output, as rank-major shard blocks.  The
     # fused form (one sg_matvec_tp per matrix, the gather done by peer stores
     # in the GEMV kernel) is timed beside it.
