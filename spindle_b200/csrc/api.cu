@@ -315,12 +315,22 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
     // the cheap chain steps over the other slots' blocks.  Pick the S with the
     // shortest such path.
     uint32_t S = 1;
+    // The kernel's S warps of a tile meet at named barriers 1 + group and
+    // 1 + G + group (G = warps / S groups), the second only where a group has
+    // a second tile; with 16 warps and S = 2 that would be barrier 16, past
+    // the hardware's 0..15, so that S is taken only where no group gets a
+    // second tile (ntiles <= SMs * G, in the GEMV and the MoE layouts alike).
+    auto s_ok = [&](uint32_t s) {
+        return !(s > 1 && 2 * (warps / s) + 1 > 16 && (uint64_t)ntiles > (uint64_t)di->sms * (warps / s));
+    };
     const int forced = env_int("SG_TILED_S", 0);
-    if ((forced == 1 || forced == 2 || forced == 4 || forced == 8 || forced == 16) && (uint32_t)forced <= warps) {
+    if ((forced == 1 || forced == 2 || forced == 4 || forced == 8 || forced == 16) && (uint32_t)forced <= warps &&
+        s_ok((uint32_t)forced)) {
         S = (uint32_t)forced;
     } else {
         double best = 1e30;
         for (uint32_t s = 1; s <= warps && s <= nb; s *= 2) {
+            if (!s_ok(s)) continue;
             const uint64_t groups = warp_slots / s;
             const uint64_t tiles = (ntiles + groups - 1) / groups;
             const double per_tile = (double)((nb + s - 1) / s) + 0.06 * (double)(nb - nb / s) + (s > 1 ? 0.5 : 0.0);
@@ -361,6 +371,7 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
         double best = 1e30;
         uint32_t bestS = 0;
         for (uint32_t s = 1; s <= warps && s <= nb; s *= 2) {
+            if (!s_ok(s)) continue;
             const uint32_t sbk = (nb + s - 1) / s;
             bool fits = false;
             for (uint32_t b = bc < sbk ? bc : sbk; b >= 1 && !fits; b--)
@@ -392,7 +403,7 @@ sg_status tiled_plan(int dt, uint32_t nb, uint32_t ntiles, int nv, int mode, uin
         else if (bc > 1)
             bc--;
         else if (S > 1)
-            S /= 2;
+            S = s_ok(S / 2) ? S / 2 : 1;
         else
             return SG_ERR_SHAPE;
     }

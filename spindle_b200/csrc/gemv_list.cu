@@ -238,7 +238,8 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_list_kernel(const __
               m.S != (1u << m.s_log2) || m.S > nwarps || (nwarps & (m.S - 1u)) || m.S > m.nb || m.bc == 0 ||
               m.bc * cb > a.stage_bytes || m.slot_blocks * m.S < m.nb ||
               list_chain_floats(nwarps, m.S, m.slot_blocks) > a.chain_floats ||
-              (m.S > 1u && 2u * (nwarps >> m.s_log2) + 1u > 16u && m.tiles_q > 0u) ||
+              (m.S > 1u && 2u * (nwarps >> m.s_log2) + 1u > 16u &&
+               (m.tiles_q > 1u || (m.tiles_q == 1u && m.tiles_r > 0u))) ||
               m.rot >= gridDim.x * (nwarps >> m.s_log2) || (uint64_t)m.ntiles * TILE_ROWS < m.rows || !m.w ||
               !m.out || ((uintptr_t)m.w & 15u) ||
               (m.img ? ((uintptr_t)m.img & 15u) != 0 : (!m.x || ((uintptr_t)m.x & 15u)));

@@ -58,6 +58,10 @@ __global__ void __launch_bounds__(TGEMV_WARPS * 32, 1) gemv_tiled_kernel(const _
             dynamic_smem_size() ||
         a.bc == 0 || a.stage_bytes < a.bc * CB || a.S == 0 || a.S != (1u << a.s_log2) || a.S > nwarps ||
         (nwarps & (a.S - 1)) || (blockDim.x & 31) ||
+        // a group with a second tile needs named barrier 1 + 2G (past 15 for G = 8)
+        (a.S > 1 && 2u * (nwarps >> a.s_log2) + 1u > 16u &&
+         (MOE ? (a.ntiles + gridDim.x - 1) / gridDim.x > (nwarps >> a.s_log2)
+              : a.tiles_q > 1u || (a.tiles_q == 1u && a.tiles_r > 0u))) ||
         a.nstages * nwarps * 8 > ((MOE || a.qx_image) ? MOE_QX_BAR_OFF : TGEMV_BAR_BYTES) ||
         (MODE == IN_Q8K && a.qx_image && a.nvec != 1) ||
         (MOE && a.swiglu && (MODE != IN_MOE_X || (a.nvec != 1 && !JOBS))) ||
